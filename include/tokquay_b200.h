@@ -1,0 +1,170 @@
+/*
+ * tokquay_b200.h -- C ABI of the B200 (sm_100a) paged-attention hot path for
+ * Tokquay's paged forward.
+ *
+ * Every entry point takes plain pointers, sizes and a CUDA stream handle
+ * (`void* stream`, a cudaStream_t; NULL = the legacy default stream), returns
+ * TQ_OK (0) or a nonzero TQ_ERR_* status, and never throws.  After a nonzero
+ * status tq_last_error() holds a message for the calling thread.
+ *
+ * Device pointers point to fp32 / int32 device memory; "host" marks host
+ * memory.  Counts that kernels read on the device (d_num_*) let a launch be
+ * captured once in a CUDA graph and replayed for steps of different sizes up
+ * to the capacity (max_*) the launch was sized for.
+ *
+ * Reference interfaces replaced (paths inside the Tokquay project):
+ *   tq_plan_step               PagedBatch.__init__           tokquay/kv_cache.py:174-226
+ *   tq_kv_write                PagedBatch.write              tokquay/kv_cache.py:228-232
+ *   tq_paged_attention         PagedBatch.gather + scores/mask/softmax/@v
+ *                                                            tokquay/kv_cache.py:234-242,
+ *                                                            tokquay/model.py:94-96
+ *   tq_embed_layernorm         wte(ids) + wpe(pos), then ln_1 of layer 0
+ *                                                            tokquay/model.py:163,172,122
+ *   tq_bias_residual_layernorm x + (y + b), then the next LayerNorm
+ *                                                            tokquay/model.py:99,122-123
+ *   tq_layernorm_rows          x[arange(B), last_idx] then ln_f
+ *                                                            tokquay/model.py:179-180
+ *   tq_bias_gelu               F.gelu(c_fc(x), approximate="tanh")
+ *                                                            tokquay/model.py:110
+ *
+ * Pool layout (the reference's, tokquay/kv_cache.py:1-14, :51-53):
+ *   pool[num_blocks][n_layer][2 (K,V)][n_head][block_size][head_dim], fp32,
+ *   16-byte aligned.  head_dim must be 64; block_size a power of two <= 256.
+ */
+#ifndef TOKQUAY_B200_H
+#define TOKQUAY_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TQ_API __attribute__((visibility("default")))
+#else
+#define TQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TQ_ABI_VERSION 1
+
+enum tq_status {
+  TQ_OK = 0,
+  TQ_ERR_INVALID = 1,     /* bad argument or batch (the reference raises ValueError) */
+  TQ_ERR_UNSUPPORTED = 2, /* shape this build does not handle (head_dim != 64, ...) */
+  TQ_ERR_CUDA = 3,        /* a CUDA runtime call or launch failed */
+  TQ_ERR_CAPACITY = 4,    /* output buffer too small; the needed size is reported */
+  TQ_ERR_DEVICE = 5       /* a kernel flagged an error (see tq_device_status) */
+};
+
+/* Layout of a plan (tq_plan_step): layout[] indices. */
+enum tq_plan_layout {
+  TQ_PLAN_NUM_TOKENS = 0,    /* N = sum of q_len */
+  TQ_PLAN_NUM_SEQS = 1,      /* B */
+  TQ_PLAN_NUM_ITEMS = 2,     /* attention work items */
+  TQ_PLAN_NUM_COMBINE = 3,   /* rows whose keys were split (combine entries) */
+  TQ_PLAN_NUM_PARTIALS = 4,  /* split-K partial slots needed (x head_dim floats of scratch each) */
+  TQ_PLAN_TABLE_STRIDE = 5,  /* int32 per row of the packed block tables */
+  TQ_PLAN_MAX_CTX = 6,       /* longest sequence after this step */
+  TQ_PLAN_SPLIT_CHUNKS = 7,  /* 32-key chunks per split-K item */
+  TQ_PLAN_TOTAL_INTS = 8,    /* int32 the plan occupies */
+  TQ_PLAN_OFF_COUNTS = 9,    /* [4]: N, num_items, num_combine, B (the d_num_* pointers) */
+  TQ_PLAN_OFF_SEQ_INFO = 10, /* [B][4]: first row, q_len, start, ctx */
+  TQ_PLAN_OFF_TABLES = 11,   /* [B][table_stride] block ids */
+  TQ_PLAN_OFF_SLOTS = 12,    /* [N] slot = block * block_size + offset */
+  TQ_PLAN_OFF_POSITIONS = 13,/* [N] absolute positions */
+  TQ_PLAN_OFF_TOKEN_IDS = 14,/* [N] token ids (copied from token_ids, or 0) */
+  TQ_PLAN_OFF_LAST_ROWS = 15,/* [B] row of each sequence's last new token */
+  TQ_PLAN_OFF_ITEMS = 16,    /* [num_items][8] attention work items */
+  TQ_PLAN_OFF_COMBINE = 17,  /* [num_combine][4] combine entries */
+  TQ_PLAN_LAYOUT_LEN = 18
+};
+
+TQ_API int tq_abi_version(void);
+
+/* Message for the last nonzero status returned on this thread. */
+TQ_API const char* tq_last_error(void);
+
+/* Reads (and with clear != 0 resets) the device error word of the current
+ * device: bit 1 = a bounded wait timed out, 2 = a block id outside the pool,
+ * 4 = a slot outside the pool, 8 = a token id outside the vocabulary.
+ * Synchronises the device.  *bits receives the word. */
+TQ_API int tq_device_status(int clear, int32_t* bits);
+
+/* Host-side step planner (replaces PagedBatch.__init__, tokquay/kv_cache.py:174-226).
+ * Validates the batch as the reference does (same conditions: non-empty,
+ * every q_len >= 1, each block table long enough for start+q_len tokens) plus
+ * block ids inside the pool and token ids inside the vocabulary, then writes
+ * into the host buffer `out` every index array one step needs (see
+ * tq_plan_layout), ready for a single host-to-device copy.  Sequence b feeds
+ * q_len[b] tokens at positions start[b] .. start[b]+q_len[b]-1; its block
+ * table is table_data[table_offsets[b] .. table_offsets[b+1]).
+ * token_ids (host, [N], may be NULL) are copied into the plan.
+ * target_units: attention (item, head) units to aim for when choosing the
+ * split-K size; min_split_chunks: smallest split, in 32-key chunks.
+ * Returns TQ_ERR_CAPACITY (layout[TQ_PLAN_TOTAL_INTS] = ints needed) if
+ * out_capacity is too small. */
+TQ_API int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_t* q_len,
+                 const int32_t* table_offsets, const int32_t* table_data,
+                 const int32_t* token_ids, int32_t block_size, int64_t num_blocks,
+                 int32_t n_head, int32_t vocab_size, int32_t target_units,
+                 int32_t min_split_chunks, int32_t* out, int64_t out_capacity,
+                 int32_t* layout);
+
+/* KV write (replaces PagedBatch.write, tokquay/kv_cache.py:228-232).
+ * For each of the *d_num_tokens new tokens n: pool[slot/bs][layer][0][h][slot%bs][:]
+ * = qkv[n*qkv_row_stride + k_col + h*head_dim ...] and likewise V from v_col.
+ * max_tokens sizes the grid (>= *d_num_tokens). */
+TQ_API int tq_kv_write(float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
+                int32_t block_size, int32_t head_dim, int32_t layer, const float* qkv,
+                int64_t qkv_row_stride, int64_t k_col, int64_t v_col,
+                const int32_t* slot_mapping, const int32_t* d_num_tokens, int32_t max_tokens,
+                void* stream);
+
+/* Paged attention, decode and causal prefill rows mixed in one launch
+ * (replaces PagedBatch.gather + the masked softmax attention,
+ * tokquay/kv_cache.py:234-242, tokquay/model.py:94-96).
+ * Row r of the plan (a new token at position p of sequence b) attends to the
+ * keys at positions 0..p of sequence b:
+ *   out[r*out_row_stride + h*64 + i] = softmax_j(q_r.k_j * scale) v_j[i].
+ * q rows: q[r*q_row_stride + h*64 ...].  work_items / combine_list /
+ * block_tables come from tq_plan_step.  partial_ml ([P][2] floats) and
+ * partial_acc ([P][64] floats), P = TQ_PLAN_NUM_PARTIALS, are caller-owned
+ * split-K scratch (may be NULL when P == 0).  max_items / max_combine size
+ * the grids.  Launches the attention kernel and, if max_combine > 0, the
+ * combine kernel, on `stream`. */
+TQ_API int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64_t q_row_stride,
+                       const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
+                       int32_t block_size, int32_t head_dim, int32_t layer,
+                       const int32_t* block_tables, int32_t table_stride,
+                       const int32_t* work_items, const int32_t* d_num_items, int32_t max_items,
+                       float* partial_ml, float* partial_acc, const int32_t* combine_list,
+                       const int32_t* d_num_combine, int32_t max_combine, float scale,
+                       void* stream);
+
+/* x[r] = wte[ids[r]] + wpe[pos[r]];  xa[r] = LayerNorm(x[r]; ln_w, ln_b, eps).
+ * n_embd must be a multiple of 128 and at most 1024. */
+TQ_API int tq_embed_layernorm(float* x, float* xa, const int32_t* ids, const int32_t* pos,
+                       const float* wte, const float* wpe, int32_t vocab_size,
+                       int32_t n_positions, const float* ln_w, const float* ln_b, float eps,
+                       int32_t n_embd, const int32_t* d_num_rows, int32_t max_rows, void* stream);
+
+/* x[r] += y[r] + bias;  then, if ln_w != NULL, xa[r] = LayerNorm(x[r]). */
+TQ_API int tq_bias_residual_layernorm(float* x, float* xa, const float* y, const float* bias,
+                               const float* ln_w, const float* ln_b, float eps, int32_t n_embd,
+                               const int32_t* d_num_rows, int32_t max_rows, void* stream);
+
+/* out[i] = LayerNorm(x[rows[i]]) (rows == NULL: x[i]). */
+TQ_API int tq_layernorm_rows(float* out, const float* x, const int32_t* rows, const float* ln_w,
+                      const float* ln_b, float eps, int32_t n_embd, const int32_t* d_num_rows,
+                      int32_t max_rows, void* stream);
+
+/* h[r][c] = gelu_tanh(h[r][c] + bias[c]) in place; n_cols a multiple of 4. */
+TQ_API int tq_bias_gelu(float* h, const float* bias, int32_t n_cols, const int32_t* d_num_rows,
+                 int32_t max_rows, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TOKQUAY_B200_H */

@@ -1,0 +1,325 @@
+"""Generate the golden fixtures from the unmodified reference implementation.
+
+    PYTHONPATH=<tokquay checkout> python tests/golden/make_golden.py [--ref PATH]
+
+Runs the reference Tokquay code (pure Python + torch on the CPU) on seeded
+inputs built by ``tokquay_b200.workloads`` and records what it produced:
+logits, greedy token streams, block tables, free lists and the K/V rows it
+wrote.  The reference is only needed here, once; the fixtures
+(``golden.json`` + ``golden.npz``) are committed and every test reads those.
+Weights and pool contents are not stored: they are rebuilt from the seeds.
+
+Cases (reference test each one re-hosts, paths inside the Tokquay project):
+  mini_decode   prefill 6, decode to 40 across bs=4 block boundaries, f64 + f32,
+                plus the full-sequence forward (tests/test_phase3_paged.py:87-106)
+  mini_batch8   8 prompts of lengths 1..48 greedy-decoded together, 20 tokens,
+                vs each alone on the contiguous cache (tests/test_phase3_paged.py:109-129)
+  mini_mixed    one step mixing a decode and a whole-prompt prefill, f64 + f32
+                (tests/test_phase3_paged.py:143-164)
+  cfg1          BASELINE config 1: GPT-2 124M, 8 decodes, bs 16, 1,024 blocks
+  cfg3_bs16/32  BASELINE config 3: 4 prefills + 60 decodes in one step
+  cfg2          BASELINE config 2 (first 3 of its 100 greedy steps), 2,048 blocks
+  alloc_trace   random allocate / grow / free on a tiny allocator
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import random
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path.insert(0, str(ROOT))
+
+from tokquay_b200 import workloads as W  # noqa: E402
+
+LOGIT_STRIDE_FULL = 8     # columns kept from GPT-2 124M logits (config 1)
+LOGIT_STRIDE_LARGE = 32   # columns kept for the 64-sequence configs
+
+
+def summarize_logits(x: torch.Tensor, stride: int) -> dict[str, np.ndarray]:
+    x = x.detach().to(torch.float32).cpu()
+    top = torch.topk(x, 2, dim=-1)
+    return {
+        "cols": x[:, ::stride].numpy().copy(),
+        "argmax": top.indices[:, 0].numpy().astype(np.int64),
+        "top2": top.values.numpy().copy(),
+        "absmax": x.abs().amax(-1).numpy().copy(),
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference", help="path of the reference checkout")
+    ap.add_argument("--only", default=None, help="comma-separated case names")
+    args = ap.parse_args()
+    sys.path.insert(0, args.ref)
+    from tokquay.generate import greedy_generate, paged_forward  # the reference
+    from tokquay.kv_cache import BlockAllocator, OutOfBlocksError
+    from tokquay.model import GPT2, GPT2Config
+    from tokquay.sequence import Sequence
+
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    only = set(args.only.split(",")) if args.only else None
+    meta: dict = {"generator": "tests/golden/make_golden.py", "torch": torch.__version__,
+                  "numpy": np.__version__, "cases": {}}  # fmt: skip
+    arrays: dict[str, np.ndarray] = {}
+    json_path, npz_path = HERE / "golden.json", HERE / "golden.npz"
+    if only and json_path.exists():
+        meta = json.loads(json_path.read_text())
+        with np.load(npz_path) as z:
+            arrays = {k: z[k] for k in z.files if k.split("/")[0] not in only}
+        for k in list(meta["cases"]):
+            if k in only:
+                del meta["cases"][k]
+
+    def want(name):
+        return only is None or name in only
+
+    def model_for(cfg_kw, seed, init, dtype):
+        cfg = GPT2Config(**cfg_kw)
+        m = GPT2(cfg)
+        W.load_weights(m, W.random_weights(cfg, seed, init), dtype)
+        return m.to(dtype).eval()
+
+    def garbage_alloc(cfg, num_blocks, bs, dtype, pool_seed, free_seed, cls=BlockAllocator):
+        a = cls(cfg, num_blocks, bs, device="cpu", dtype=dtype)
+        W.fill_pool_blocks(a.pool, range(num_blocks), pool_seed, scale=50.0)
+        W.shuffle_free_list(a, free_seed)
+        return a
+
+    # ---------------------------------------------------------------- mini_decode
+    if want("mini_decode"):
+        t0 = time.time()
+        ids = [random.Random(7).randrange(W.MINI["vocab_size"]) for _ in range(40)]
+        case = {"cfg": W.MINI, "weights_seed": 11, "init": "gpt2", "block_size": 4, "num_blocks": 32,
+                "pool_seed": 100, "pool_scale": 50.0, "free_seed": 0, "ids": ids, "prefill": 6}  # fmt: skip
+        for dt, tag in ((torch.float64, "f64"), (torch.float32, "f32")):
+            m = model_for(W.MINI, 11, "gpt2", dt)
+            a = garbage_alloc(m.cfg, 32, 4, dt, 100, 0)
+            s = Sequence(0, ids[:6])
+            a.allocate(s)
+            got = [paged_forward(m, a, [s])[0]]
+            for t in range(6, len(ids)):
+                s.append_token(ids[t])
+                a.append_slot(s)
+                got.append(paged_forward(m, a, [s])[0])
+            arrays[f"mini_decode/logits_{tag}"] = torch.stack(got).numpy()
+            if dt == torch.float64:
+                with torch.no_grad():
+                    arrays["mini_decode/full_f64"] = m(torch.tensor([ids]))[0].numpy()
+                case["block_table"] = list(s.block_table)
+                case["free_after"] = list(a._free)
+        meta["cases"]["mini_decode"] = case
+        print(f"mini_decode {time.time() - t0:.1f}s")
+
+    # ---------------------------------------------------------------- mini_batch8
+    if want("mini_batch8"):
+        t0 = time.time()
+
+        class Recording(BlockAllocator):
+            def __init__(self, *a, **kw):
+                super().__init__(*a, **kw)
+                self.ever_taken: set[int] = set()
+
+            def _take(self, n):
+                blocks = super()._take(n)
+                self.ever_taken.update(blocks)
+                return blocks
+
+        text = [random.Random(8).randrange(W.MINI["vocab_size"]) for _ in range(200)]
+        lengths = [1, 3, 7, 12, 16, 17, 33, 48]
+        prompts = [text[3 * i:3 * i + n] for i, n in enumerate(lengths)]
+        n_new = 20
+        m = model_for(W.MINI, 12, "gpt2", torch.float32)
+        a = garbage_alloc(m.cfg, 128, 16, torch.float32, 101, 1, cls=Recording)
+        before = a.pool.clone()
+        seqs = [Sequence(i, list(p)) for i, p in enumerate(prompts)]
+        for s in seqs:
+            a.allocate(s)
+        running, steps, step_logits = seqs, [], []
+        while running:
+            tables = [list(s.block_table) for s in running]
+            logits = paged_forward(m, a, running)
+            nxt = logits.argmax(-1).tolist()
+            steps.append({"seq_ids": [s.seq_id for s in running], "tables": tables, "next": nxt})
+            step_logits.append(logits.numpy())
+            still = []
+            for s, t in zip(running, nxt):
+                s.append_token(t)
+                if len(s.output_token_ids) >= n_new:
+                    a.free(s)
+                else:
+                    a.append_slot(s)
+                    still.append(s)
+            running = still
+        alone = [greedy_generate(m, torch.tensor([p]), n_new, use_cache=True) for p in prompts]
+        changed = sorted(b for b in range(a.num_blocks) if not torch.equal(a.pool[b], before[b]))
+        arrays["mini_batch8/logits"] = np.concatenate(step_logits)
+        meta["cases"]["mini_batch8"] = {
+            "cfg": W.MINI, "weights_seed": 12, "init": "gpt2", "block_size": 16, "num_blocks": 128,
+            "pool_seed": 101, "pool_scale": 50.0, "free_seed": 1, "prompts": prompts, "n_new": n_new,
+            "tokens": [s.output_token_ids for s in seqs], "alone": alone, "steps": steps,
+            "ever_taken": sorted(a.ever_taken), "changed_blocks": changed, "free_after": list(a._free),
+        }  # fmt: skip
+        print(f"mini_batch8 {time.time() - t0:.1f}s")
+
+    # ---------------------------------------------------------------- mini_mixed
+    if want("mini_mixed"):
+        t0 = time.time()
+        rng = random.Random(9)
+        a_ids = [rng.randrange(W.MINI["vocab_size"]) for _ in range(12)]
+        b_ids = [rng.randrange(W.MINI["vocab_size"]) for _ in range(9)]
+        case = {"cfg": W.MINI, "weights_seed": 13, "init": "gpt2", "block_size": 4, "num_blocks": 64,
+                "pool_seed": 102, "pool_scale": 50.0, "free_seed": 3, "a_ids": a_ids, "b_ids": b_ids}  # fmt: skip
+        for dt, tag in ((torch.float64, "f64"), (torch.float32, "f32")):
+            m = model_for(W.MINI, 13, "gpt2", dt)
+            al = garbage_alloc(m.cfg, 64, 4, dt, 102, 3)
+            sa = Sequence(0, a_ids[:-1])
+            al.allocate(sa)
+            paged_forward(m, al, [sa])
+            sa.append_token(a_ids[-1])
+            al.append_slot(sa)
+            sb = Sequence(1, b_ids)
+            al.allocate(sb)
+            case[f"tables_{tag}"] = [list(sa.block_table), list(sb.block_table)]
+            arrays[f"mini_mixed/logits_{tag}"] = paged_forward(m, al, [sa, sb]).numpy()
+            if dt == torch.float64:
+                with torch.no_grad():
+                    arrays["mini_mixed/full_a_f64"] = m(torch.tensor([a_ids]))[0, -1].numpy()
+                    arrays["mini_mixed/full_b_f64"] = m(torch.tensor([b_ids]))[0, -1].numpy()
+        meta["cases"]["mini_mixed"] = case
+        print(f"mini_mixed {time.time() - t0:.1f}s")
+
+    # ---------------------------------------------------------------- GPT-2 124M configs
+    big = None
+
+    def gpt2_model():
+        nonlocal big
+        if big is None:
+            big = model_for(W.GPT2_SMALL, 0, "normal", torch.float32)
+        return big
+
+    if want("cfg1"):
+        t0 = time.time()
+        m = gpt2_model()
+        c = W.CONFIGS[1]
+        a = BlockAllocator(m.cfg, c["num_blocks"], c["block_size"], device="cpu")
+        case = W.decode_case(Sequence, a, c["n_seqs"], c["ctx_range"], m.cfg.vocab_size, seed=0)
+        W.fill_pool_blocks(a.pool, W.used_blocks(case), seed=0)
+        tables = case.block_tables
+        logits = paged_forward(m, a, case.seqs)
+        for k, v in summarize_logits(logits, LOGIT_STRIDE_FULL).items():
+            arrays[f"cfg1/{k}"] = v
+        # The K/V rows this step wrote (the last position of each sequence), layers 0 and 11.
+        rows = []
+        for s, ctx in zip(case.seqs, case.meta["ctx"]):
+            p = ctx - 1
+            blk, off = s.block_table[p // c["block_size"]], p % c["block_size"]
+            rows.append(a.pool[blk, [0, 11], :, :, off].numpy())  # [2 layers, 2 kv, H, d]
+        arrays["cfg1/written_kv"] = np.stack(rows)
+        meta["cases"]["cfg1"] = {"seed": 0, "weights_seed": 0, "init": "normal", **{k: c[k] for k in c},
+                                 "ctx": case.meta["ctx"], "tables": tables, "free_after": list(a._free),
+                                 "logit_stride": LOGIT_STRIDE_FULL}  # fmt: skip
+        print(f"cfg1 {time.time() - t0:.1f}s")
+
+    for bs in (16, 32):
+        name = f"cfg3_bs{bs}"
+        if not want(name):
+            continue
+        t0 = time.time()
+        m = gpt2_model()
+        c = W.CONFIGS[3]
+        a = BlockAllocator(m.cfg, c["num_blocks"], bs, device="cpu")
+        case = W.mixed_case(Sequence, a, c["n_prefill"], c["n_decode"], c["len_range"], m.cfg.vocab_size, seed=3)
+        W.fill_pool_blocks(a.pool, W.used_blocks(case), seed=3)
+        tables = case.block_tables
+        logits = paged_forward(m, a, case.seqs, case.new_lens)
+        for k, v in summarize_logits(logits, LOGIT_STRIDE_LARGE).items():
+            arrays[f"{name}/{k}"] = v
+        meta["cases"][name] = {"seed": 3, "weights_seed": 0, "init": "normal", "block_size": bs,
+                               "num_blocks": c["num_blocks"], "n_prefill": c["n_prefill"],
+                               "n_decode": c["n_decode"], "len_range": c["len_range"],
+                               "kinds": case.meta["kinds"], "lens": case.meta["lens"], "new_lens": case.new_lens,
+                               "tables": tables, "logit_stride": LOGIT_STRIDE_LARGE}  # fmt: skip
+        print(f"{name} {time.time() - t0:.1f}s")
+
+    if want("cfg2"):
+        t0 = time.time()
+        m = gpt2_model()
+        c = W.CONFIGS[2]
+        a = BlockAllocator(m.cfg, c["num_blocks"], c["block_size"], device="cpu")
+        case = W.decode_case(Sequence, a, c["n_seqs"], c["ctx_range"], m.cfg.vocab_size, seed=2)
+        W.fill_pool_blocks(a.pool, W.used_blocks(case), seed=2)
+        steps = []
+        n_steps = 3
+        for k in range(n_steps):
+            tables = [list(s.block_table) for s in case.seqs]
+            logits = paged_forward(m, a, case.seqs)
+            summ = summarize_logits(logits, LOGIT_STRIDE_LARGE)
+            for key, v in summ.items():
+                arrays[f"cfg2/step{k}_{key}"] = v
+            nxt = summ["argmax"].tolist()
+            steps.append({"tables": tables, "next": nxt})
+            for s, t in zip(case.seqs, nxt):
+                s.append_token(t)
+                a.append_slot(s)
+        meta["cases"]["cfg2"] = {"seed": 2, "weights_seed": 0, "init": "normal", **{k: c[k] for k in c},
+                                 "ctx": case.meta["ctx"], "steps": steps, "n_steps": n_steps,
+                                 "free_after": list(a._free), "logit_stride": LOGIT_STRIDE_LARGE}  # fmt: skip
+        print(f"cfg2 {time.time() - t0:.1f}s")
+
+    # ---------------------------------------------------------------- allocator trace
+    if want("alloc_trace"):
+        tiny = GPT2Config(vocab_size=8, n_positions=64, n_embd=4, n_layer=1, n_head=1)
+        a = BlockAllocator(tiny, 24, 4, device="cpu")
+        rng = random.Random(5)
+        live: dict[int, Sequence] = {}
+        ops, nid = [], 0
+        for _ in range(400):
+            r = rng.random()
+            if r < 0.4 or not live:
+                n = rng.randint(1, 30)
+                s = Sequence(nid, [0] * n)
+                nid += 1
+                try:
+                    a.allocate(s)
+                    live[s.seq_id] = s
+                    res = "ok"
+                except OutOfBlocksError:
+                    res = "oob"
+                ops.append({"op": "allocate", "id": s.seq_id, "n": n, "res": res})
+            elif r < 0.8:
+                sid = rng.choice(sorted(live))
+                s = live[sid]
+                s.append_token(0)
+                try:
+                    grabbed = a.append_slot(s)
+                    res = "grabbed" if grabbed else "same"
+                except OutOfBlocksError:
+                    s.output_token_ids.pop()
+                    res = "oob"
+                ops.append({"op": "append", "id": sid, "res": res})
+            else:
+                sid = rng.choice(sorted(live))
+                a.free(live.pop(sid))
+                ops.append({"op": "free", "id": sid, "res": "ok"})
+            ops[-1]["free"] = list(a._free)
+            ops[-1]["tables"] = {str(k): list(v.block_table) for k, v in live.items()}
+            ops[-1]["ref_counts"] = list(a.ref_counts)
+        meta["cases"]["alloc_trace"] = {"num_blocks": 24, "block_size": 4, "ops": ops}
+
+    json_path.write_text(json.dumps(meta, separators=(",", ":")))
+    np.savez_compressed(npz_path, **arrays)
+    print(f"wrote {json_path} ({json_path.stat().st_size} B), {npz_path} ({npz_path.stat().st_size} B)")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,39 @@
+"""B200-native (sm_100a) paged-attention hot path for Tokquay's paged forward.
+
+Public surface, mirroring the reference's modules:
+
+* ``GPT2Config``, ``GPT2``                       (tokquay/model.py)
+* ``BlockAllocator``, ``BatchedKV``, ``OutOfBlocksError``, ``DevicePagedBatch``
+                                                  (tokquay/kv_cache.py)
+* ``Sequence``, ``SamplingParams``, ``SequenceStatus``   (tokquay/sequence.py)
+* ``paged_forward``, ``paged_greedy_generate``   (tokquay/generate.py)
+
+The CUDA kernels live in ``libtokquay_b200.so`` (C ABI: include/tokquay_b200.h),
+built in-tree by ``python -m tokquay_b200.build``.
+"""
+
+from tokquay_b200.sequence import SamplingParams, Sequence, SequenceStatus  # noqa: F401
+from tokquay_b200.kv_cache import (  # noqa: F401
+    BatchedKV,
+    BlockAllocator,
+    DevicePagedBatch,
+    OutOfBlocksError,
+    cdiv,
+)
+from tokquay_b200.model import GPT2, GPT2Config  # noqa: F401
+from tokquay_b200.generate import paged_forward, paged_greedy_generate  # noqa: F401
+
+__all__ = [
+    "BatchedKV",
+    "BlockAllocator",
+    "DevicePagedBatch",
+    "GPT2",
+    "GPT2Config",
+    "OutOfBlocksError",
+    "SamplingParams",
+    "Sequence",
+    "SequenceStatus",
+    "cdiv",
+    "paged_forward",
+    "paged_greedy_generate",
+]

@@ -1,0 +1,366 @@
+// extern "C" entry points of libtokquay_b200.so (declared in include/tokquay_b200.h).
+//
+// The whole device side is this one translation unit: it includes every
+// kernel header, validates arguments on the host (the kernels assume them),
+// sizes persistent grids from the device's SM count and launches on the
+// caller's stream.  No entry point allocates device memory.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <mutex>
+
+#include "../../include/tokquay_b200.h"
+#include "common.cuh"
+#include "elementwise.cuh"
+#include "host_error.h"
+#include "kv_write.cuh"
+#include "paged_attention.cuh"
+
+namespace tq {
+
+char* error_buffer() {
+  static thread_local char buf[kErrorBufferLen] = {0};
+  return buf;
+}
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  int sm_count = 0;
+  bool ready = false;
+};
+
+DeviceInfo g_devices[kMaxDevices];
+std::mutex g_devices_mu;
+
+// SM count of the current device; on first use per device also raises the
+// attention kernel's dynamic shared-memory limit.
+int device_setup(int* sm_count) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(TQ_ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lock(g_devices_mu);
+  DeviceInfo& d = g_devices[dev];
+  if (!d.ready) {
+    e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess)
+      return set_error(TQ_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+    e = cudaFuncSetAttribute(paged_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kAttnSmemBytes);
+    if (e != cudaSuccess)
+      return set_error(TQ_ERR_CUDA, "cudaFuncSetAttribute(paged_attention): %s",
+                       cudaGetErrorString(e));
+    d.ready = true;
+  }
+  *sm_count = d.sm_count;
+  return TQ_OK;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  return TQ_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int log2_exact(int v) {
+  int l = 0;
+  while ((1 << l) < v) ++l;
+  return l;
+}
+
+int check_pool(const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
+               int32_t block_size, int32_t head_dim, int32_t layer) {
+  if (pool == nullptr) return set_error(TQ_ERR_INVALID, "pool must not be NULL");
+  if (!aligned(pool, 16)) return set_error(TQ_ERR_INVALID, "pool must be 16-byte aligned");
+  if (head_dim != kHeadDim)
+    return set_error(TQ_ERR_UNSUPPORTED, "head_dim must be %d, got %d", kHeadDim, head_dim);
+  if (block_size < 1 || block_size > 256 || (block_size & (block_size - 1)) != 0)
+    return set_error(TQ_ERR_UNSUPPORTED, "block_size must be a power of two in [1, 256], got %d",
+                     block_size);
+  if (num_blocks < 1 || num_blocks * (int64_t)block_size > INT32_MAX)
+    return set_error(TQ_ERR_UNSUPPORTED, "num_blocks * block_size must be in [1, 2^31)");
+  if (n_head < 1 || n_layer < 1 || layer < 0 || layer >= n_layer)
+    return set_error(TQ_ERR_INVALID, "layer %d outside [0, %d) or n_head %d < 1", layer, n_layer,
+                     n_head);
+  return TQ_OK;
+}
+
+// Instantiates a row kernel template for C = 128 * VPL, VPL in 1..8.
+#define TQ_ROW_LAUNCH(KERNEL, VPL_RT, GRID, BLOCK, STREAM, PARAMS)     \
+  do {                                                                 \
+    switch (VPL_RT) {                                                  \
+      case 1: KERNEL<1><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
+      case 2: KERNEL<2><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
+      case 3: KERNEL<3><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
+      case 4: KERNEL<4><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
+      case 5: KERNEL<5><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
+      case 6: KERNEL<6><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
+      case 7: KERNEL<7><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
+      case 8: KERNEL<8><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
+    }                                                                  \
+  } while (0)
+
+int check_embd(int32_t n_embd) {
+  if (n_embd < 128 || n_embd > 1024 || n_embd % 128 != 0)
+    return set_error(TQ_ERR_UNSUPPORTED, "n_embd must be a multiple of 128 in [128, 1024], got %d",
+                     n_embd);
+  return TQ_OK;
+}
+
+// Grid for `warps` independent warps of 8 per 256-thread block, capped at 8
+// blocks per SM (the kernels grid-stride beyond that).
+int warp_grid(int64_t warps, int sm_count) {
+  const int64_t blocks = (warps + 7) / 8;
+  return (int)std::min<int64_t>(std::max<int64_t>(blocks, 1), (int64_t)sm_count * 8);
+}
+
+}  // namespace
+}  // namespace tq
+
+using namespace tq;
+
+extern "C" {
+
+int tq_abi_version(void) { return TQ_ABI_VERSION; }
+
+const char* tq_last_error(void) { return error_buffer(); }
+
+int tq_device_status(int clear, int32_t* bits) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "cudaDeviceSynchronize: %s", cudaGetErrorString(e));
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
+  if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "read device error word: %s", cudaGetErrorString(e));
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess)
+      return set_error(TQ_ERR_CUDA, "clear device error word: %s", cudaGetErrorString(e));
+  }
+  if (bits) *bits = v;
+  return TQ_OK;
+}
+
+int tq_kv_write(float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
+                int32_t block_size, int32_t head_dim, int32_t layer, const float* qkv,
+                int64_t qkv_row_stride, int64_t k_col, int64_t v_col,
+                const int32_t* slot_mapping, const int32_t* d_num_tokens, int32_t max_tokens,
+                void* stream) {
+  int st = check_pool(pool, num_blocks, n_layer, n_head, block_size, head_dim, layer);
+  if (st) return st;
+  if (max_tokens < 0) return set_error(TQ_ERR_INVALID, "max_tokens must be >= 0");
+  if (max_tokens == 0) return TQ_OK;
+  if (!qkv || !slot_mapping || !d_num_tokens)
+    return set_error(TQ_ERR_INVALID, "qkv, slot_mapping and d_num_tokens must not be NULL");
+  if (!aligned(qkv, 16) || qkv_row_stride % 4 || k_col % 4 || v_col % 4)
+    return set_error(TQ_ERR_INVALID, "qkv rows and the K/V columns must be 16-byte aligned");
+  int sms = 0;
+  if ((st = device_setup(&sms))) return st;
+  KvWriteParams p;
+  p.pool = pool;
+  p.num_blocks = num_blocks;
+  p.n_layer = n_layer;
+  p.n_head = n_head;
+  p.block_size = block_size;
+  p.log2_bs = log2_exact(block_size);
+  p.layer = layer;
+  p.qkv = qkv;
+  p.qkv_stride = qkv_row_stride;
+  p.k_col = k_col;
+  p.v_col = v_col;
+  p.slots = slot_mapping;
+  p.n_tokens = d_num_tokens;
+  kv_write_kernel<<<warp_grid(2LL * max_tokens, sms), 256, 0, (cudaStream_t)stream>>>(p);
+  return check_launch("kv_write");
+}
+
+int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64_t q_row_stride,
+                       const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
+                       int32_t block_size, int32_t head_dim, int32_t layer,
+                       const int32_t* block_tables, int32_t table_stride,
+                       const int32_t* work_items, const int32_t* d_num_items, int32_t max_items,
+                       float* partial_ml, float* partial_acc, const int32_t* combine_list,
+                       const int32_t* d_num_combine, int32_t max_combine, float scale,
+                       void* stream) {
+  int st = check_pool(pool, num_blocks, n_layer, n_head, block_size, head_dim, layer);
+  if (st) return st;
+  if (max_items < 0 || max_combine < 0) return set_error(TQ_ERR_INVALID, "negative capacity");
+  if (max_items == 0) return TQ_OK;
+  if (!out || !q || !block_tables || !work_items || !d_num_items)
+    return set_error(TQ_ERR_INVALID, "out, q, block_tables and work items must not be NULL");
+  if (!aligned(q, 16) || q_row_stride % 4)
+    return set_error(TQ_ERR_INVALID, "q rows must be 16-byte aligned");
+  if (!aligned(out, 8) || out_row_stride % 2)
+    return set_error(TQ_ERR_INVALID, "out rows must be 8-byte aligned");
+  if (!aligned(work_items, 16)) return set_error(TQ_ERR_INVALID, "work items must be 16-byte aligned");
+  if (max_combine > 0) {
+    if (!partial_ml || !partial_acc || !combine_list || !d_num_combine)
+      return set_error(TQ_ERR_INVALID, "split-K scratch and combine list must not be NULL");
+    if (!aligned(partial_acc, 8) || !aligned(partial_ml, 8) || !aligned(combine_list, 16))
+      return set_error(TQ_ERR_INVALID, "split-K scratch misaligned");
+  }
+  if (table_stride < 0) return set_error(TQ_ERR_INVALID, "table_stride must be >= 0");
+  if (!(scale > 0.f) || !std::isfinite(scale)) return set_error(TQ_ERR_INVALID, "bad scale");
+  int sms = 0;
+  if ((st = device_setup(&sms))) return st;
+  const cudaStream_t s = (cudaStream_t)stream;
+
+  AttnParams p;
+  p.out = out;
+  p.out_stride = out_row_stride;
+  p.q = q;
+  p.q_stride = q_row_stride;
+  p.pool = pool;
+  p.num_blocks = num_blocks;
+  p.n_layer = n_layer;
+  p.n_head = n_head;
+  p.block_size = block_size;
+  p.log2_bs = log2_exact(block_size);
+  p.layer = layer;
+  p.tables = block_tables;
+  p.table_stride = table_stride;
+  p.items = reinterpret_cast<const WorkItem*>(work_items);
+  p.n_items = d_num_items;
+  p.part_ml = partial_ml;
+  p.part_acc = partial_acc;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  const int64_t units = (int64_t)max_items * n_head;
+  const int grid = (int)std::min<int64_t>((units + kAttnWarps - 1) / kAttnWarps, sms);
+  paged_attention_kernel<<<grid, kAttnWarps * 32, kAttnSmemBytes, s>>>(p);
+  if ((st = check_launch("paged_attention"))) return st;
+
+  if (max_combine > 0) {
+    CombineParams c;
+    c.out = out;
+    c.out_stride = out_row_stride;
+    c.part_ml = partial_ml;
+    c.part_acc = partial_acc;
+    c.entries = reinterpret_cast<const int4*>(combine_list);
+    c.n_entries = d_num_combine;
+    c.n_head = n_head;
+    attn_combine_kernel<<<warp_grid((int64_t)max_combine * n_head, sms), 256, 0, s>>>(c);
+    if ((st = check_launch("attn_combine"))) return st;
+  }
+  return TQ_OK;
+}
+
+int tq_embed_layernorm(float* x, float* xa, const int32_t* ids, const int32_t* pos,
+                       const float* wte, const float* wpe, int32_t vocab_size,
+                       int32_t n_positions, const float* ln_w, const float* ln_b, float eps,
+                       int32_t n_embd, const int32_t* d_num_rows, int32_t max_rows, void* stream) {
+  int st = check_embd(n_embd);
+  if (st) return st;
+  if (max_rows < 0) return set_error(TQ_ERR_INVALID, "max_rows must be >= 0");
+  if (max_rows == 0) return TQ_OK;
+  if (!x || !xa || !ids || !pos || !wte || !wpe || !ln_w || !ln_b || !d_num_rows)
+    return set_error(TQ_ERR_INVALID, "embed_layernorm: NULL argument");
+  if (!aligned(x, 16) || !aligned(xa, 16) || !aligned(wte, 16) || !aligned(wpe, 16) ||
+      !aligned(ln_w, 16) || !aligned(ln_b, 16))
+    return set_error(TQ_ERR_INVALID, "embed_layernorm: float arrays must be 16-byte aligned");
+  if (vocab_size < 1 || n_positions < 1) return set_error(TQ_ERR_INVALID, "bad vocab / positions");
+  int sms = 0;
+  if ((st = device_setup(&sms))) return st;
+  RowParams p{};
+  p.x = x;
+  p.xa = xa;
+  p.ids = ids;
+  p.pos = pos;
+  p.wte = wte;
+  p.wpe = wpe;
+  p.ln_w = ln_w;
+  p.ln_b = ln_b;
+  p.n_rows = d_num_rows;
+  p.C = n_embd;
+  p.vocab = vocab_size;
+  p.n_positions = n_positions;
+  p.eps = eps;
+  TQ_ROW_LAUNCH(embed_ln_kernel, n_embd / 128, warp_grid(max_rows, sms), 256, (cudaStream_t)stream, p);
+  return check_launch("embed_layernorm");
+}
+
+int tq_bias_residual_layernorm(float* x, float* xa, const float* y, const float* bias,
+                               const float* ln_w, const float* ln_b, float eps, int32_t n_embd,
+                               const int32_t* d_num_rows, int32_t max_rows, void* stream) {
+  int st = check_embd(n_embd);
+  if (st) return st;
+  if (max_rows < 0) return set_error(TQ_ERR_INVALID, "max_rows must be >= 0");
+  if (max_rows == 0) return TQ_OK;
+  if (!x || !y || !bias || !d_num_rows || (ln_w && (!ln_b || !xa)))
+    return set_error(TQ_ERR_INVALID, "bias_residual_layernorm: NULL argument");
+  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(bias, 16) || (xa && !aligned(xa, 16)) ||
+      (ln_w && (!aligned(ln_w, 16) || !aligned(ln_b, 16))))
+    return set_error(TQ_ERR_INVALID, "bias_residual_layernorm: arrays must be 16-byte aligned");
+  int sms = 0;
+  if ((st = device_setup(&sms))) return st;
+  RowParams p{};
+  p.x = x;
+  p.xa = xa;
+  p.y = y;
+  p.bias = bias;
+  p.ln_w = ln_w;
+  p.ln_b = ln_b;
+  p.n_rows = d_num_rows;
+  p.C = n_embd;
+  p.eps = eps;
+  TQ_ROW_LAUNCH(bias_residual_ln_kernel, n_embd / 128, warp_grid(max_rows, sms), 256,
+                (cudaStream_t)stream, p);
+  return check_launch("bias_residual_layernorm");
+}
+
+int tq_layernorm_rows(float* out, const float* x, const int32_t* rows, const float* ln_w,
+                      const float* ln_b, float eps, int32_t n_embd, const int32_t* d_num_rows,
+                      int32_t max_rows, void* stream) {
+  int st = check_embd(n_embd);
+  if (st) return st;
+  if (max_rows < 0) return set_error(TQ_ERR_INVALID, "max_rows must be >= 0");
+  if (max_rows == 0) return TQ_OK;
+  if (!out || !x || !ln_w || !ln_b || !d_num_rows)
+    return set_error(TQ_ERR_INVALID, "layernorm_rows: NULL argument");
+  if (!aligned(out, 16) || !aligned(x, 16) || !aligned(ln_w, 16) || !aligned(ln_b, 16))
+    return set_error(TQ_ERR_INVALID, "layernorm_rows: arrays must be 16-byte aligned");
+  int sms = 0;
+  if ((st = device_setup(&sms))) return st;
+  RowParams p{};
+  p.xa = out;
+  p.x = const_cast<float*>(x);
+  p.rows = rows;
+  p.ln_w = ln_w;
+  p.ln_b = ln_b;
+  p.n_rows = d_num_rows;
+  p.C = n_embd;
+  p.eps = eps;
+  TQ_ROW_LAUNCH(layernorm_rows_kernel, n_embd / 128, warp_grid(max_rows, sms), 256,
+                (cudaStream_t)stream, p);
+  return check_launch("layernorm_rows");
+}
+
+int tq_bias_gelu(float* h, const float* bias, int32_t n_cols, const int32_t* d_num_rows,
+                 int32_t max_rows, void* stream) {
+  if (max_rows < 0 || n_cols < 4 || n_cols % 4)
+    return set_error(TQ_ERR_INVALID, "bias_gelu: n_cols must be a positive multiple of 4");
+  if (max_rows == 0) return TQ_OK;
+  if (!h || !bias || !d_num_rows) return set_error(TQ_ERR_INVALID, "bias_gelu: NULL argument");
+  if (!aligned(h, 16) || !aligned(bias, 16))
+    return set_error(TQ_ERR_INVALID, "bias_gelu: arrays must be 16-byte aligned");
+  int sms = 0;
+  int st = device_setup(&sms);
+  if (st) return st;
+  GeluParams p;
+  p.h = h;
+  p.bias = bias;
+  p.n_rows = d_num_rows;
+  p.F = n_cols;
+  const int64_t total4 = (int64_t)max_rows * (n_cols / 4);
+  const int grid = (int)std::min<int64_t>(std::max<int64_t>((total4 + 255) / 256, 1), (int64_t)sms * 8);
+  bias_gelu_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
+  return check_launch("bias_gelu");
+}
+
+}  // extern "C"

@@ -1,0 +1,64 @@
+"""Step drivers over the paged cache (tokquay/generate.py:63-120).
+
+``paged_forward`` keeps the reference signature and contract: one batched
+step, next-token logits ``[B, V]`` back, ``num_cached_tokens`` advanced.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from tokquay_b200.kv_cache import BlockAllocator
+from tokquay_b200.model import GPT2
+from tokquay_b200.sequence import Sequence, SequenceStatus
+
+
+@torch.no_grad()
+def paged_forward(
+    model: GPT2,
+    allocator: BlockAllocator,
+    seqs: list[Sequence],
+    new_lens: list[int] | None = None,
+) -> torch.Tensor:
+    """Run one batched step over paged KV and return next-token logits ``[B, vocab]``.
+
+    Sequence ``i`` feeds ``token_ids[num_cached_tokens : num_cached_tokens + n_i]``
+    (``n_i`` defaults to everything uncached), so prefill and decode mix freely.
+    Blocks must already cover the sequences.  Advances ``num_cached_tokens``.
+    """
+    lens = new_lens or [s.num_uncached_tokens for s in seqs]
+    batch = allocator.batch_for(seqs, lens)
+    logits = model.forward_paged(batch, last_only=True)[:, 0]
+    for s, n in zip(seqs, lens):
+        s.num_cached_tokens += n
+    return logits
+
+
+@torch.no_grad()
+def paged_greedy_generate(
+    model: GPT2,
+    allocator: BlockAllocator,
+    prompts: list[list[int]],
+    max_new_tokens: int,
+) -> list[list[int]]:
+    """Greedy-decode several prompts together (tokquay/generate.py:90-120): one
+    prefill batch, then decode steps; a sequence's blocks are freed as soon as
+    it has ``max_new_tokens`` outputs."""
+    seqs = [Sequence(i, list(p)) for i, p in enumerate(prompts)]
+    for s in seqs:
+        allocator.allocate(s)
+        s.status = SequenceStatus.RUNNING
+    running = seqs
+    while running:
+        next_ids = paged_forward(model, allocator, running).argmax(-1).tolist()
+        still_running = []
+        for s, t in zip(running, next_ids):
+            s.append_token(t)
+            if len(s.output_token_ids) >= max_new_tokens:
+                allocator.free(s)
+                s.status = SequenceStatus.FINISHED
+            else:
+                allocator.append_slot(s)
+                still_running.append(s)
+        running = still_running
+    return [s.output_token_ids for s in seqs]

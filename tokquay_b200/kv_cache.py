@@ -1,0 +1,478 @@
+"""Paged KV cache: the block pool, its allocator and the per-step device view.
+
+Pool layout and allocator bookkeeping are the reference's contract
+(tokquay/kv_cache.py:1-14, :38-127) and are kept exactly: the same pool shape
+
+    pool: [num_blocks, n_layer, 2, n_head, block_size, d_head]   (dim 2: 0=K, 1=V)
+
+the same LIFO free list (reversed so block 0 is handed out first), the same ref
+counts and the same errors, so block tables and allocator state match the
+reference's bit for bit and its scheduler / engine run on top unchanged.
+
+What changes is the per-step view.  The reference's ``PagedBatch`` builds
+padded index tensors with Python loops and, per layer, gathers every
+sequence's blocks into a dense copy (kv_cache.py:174-242).  ``DevicePagedBatch``
+plans the step once on the host in C (``tq_plan_step``), ships it to the GPU in
+one copy, and the CUDA kernels scatter new K/V into the pool and read K/V
+blocks in place -- no dense copy, no padded query rows.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import itertools
+import math
+import threading
+from typing import TYPE_CHECKING
+
+import numpy as np
+import torch
+
+from tokquay_b200 import _lib
+from tokquay_b200.sequence import Sequence
+
+if TYPE_CHECKING:
+    from tokquay_b200.model import GPT2Config
+
+# Keys per attention chunk and warps per attention CTA (csrc/paged_attention.cuh).
+ATTN_CHUNK = 32
+ATTN_WARPS_PER_CTA = 4
+# Split-K policy: aim for this many (item, head) units per SM, never cut a
+# split below this many 32-key chunks.
+UNITS_PER_SM = 16
+MIN_SPLIT_CHUNKS = 2
+
+
+def cdiv(a: int, b: int) -> int:
+    return -(-a // b)
+
+
+class OutOfBlocksError(RuntimeError):
+    """Raised (without changing any state) when the free list is too short."""
+
+
+class BlockAllocator:
+    """Owns the pool, the free list and the ref counts (tokquay/kv_cache.py:38-127).
+
+    The pool must be float32 (what the kernels read) and ``block_size`` a power
+    of two no larger than 256.  A CPU pool is allowed for bookkeeping-only use;
+    building a step view needs a CUDA pool.
+    """
+
+    def __init__(
+        self,
+        cfg: "GPT2Config",
+        num_blocks: int,
+        block_size: int = 16,
+        device=None,
+        dtype: torch.dtype = torch.float32,
+    ):
+        if num_blocks < 1 or block_size < 1:
+            raise ValueError("num_blocks and block_size must be positive")
+        if block_size & (block_size - 1) or block_size > 256:
+            raise ValueError(f"block_size must be a power of two <= 256, got {block_size}")
+        if dtype != torch.float32:
+            raise ValueError(f"the paged kernels store K/V in float32, got {dtype}")
+        self.cfg = cfg
+        self.num_blocks = num_blocks
+        self.block_size = block_size
+        self.pool = torch.zeros(
+            num_blocks, cfg.n_layer, 2, cfg.n_head, block_size, cfg.d_head, device=device, dtype=dtype
+        )
+        # LIFO: the end of the list is handed out next, so reversed order gives block 0 first.
+        self._free: list[int] = list(range(num_blocks - 1, -1, -1))
+        self.ref_counts: list[int] = [0] * num_blocks
+
+    # ---- bookkeeping ---------------------------------------------------------------
+    @property
+    def num_free_blocks(self) -> int:
+        return len(self._free)
+
+    @property
+    def num_used_blocks(self) -> int:
+        return self.num_blocks - len(self._free)
+
+    @property
+    def bytes_per_block(self) -> int:
+        return self.pool[0].numel() * self.pool.element_size()
+
+    def blocks_needed(self, num_tokens: int) -> int:
+        return cdiv(num_tokens, self.block_size)
+
+    # ---- allocation ----------------------------------------------------------------
+    def can_allocate(self, num_tokens: int) -> bool:
+        return self.blocks_needed(num_tokens) <= self.num_free_blocks
+
+    def allocate(self, seq: Sequence, num_tokens: int | None = None) -> None:
+        """Give a block-less sequence blocks for ``num_tokens`` positions
+        (default: all of its tokens)."""
+        if seq.block_table:
+            raise ValueError(f"sequence {seq.seq_id} already owns blocks")
+        n = self.blocks_needed(seq.num_tokens if num_tokens is None else num_tokens)
+        seq.block_table = self._take(n)
+
+    def can_append_slot(self, seq: Sequence) -> bool:
+        return self.blocks_needed(seq.num_tokens) - len(seq.block_table) <= self.num_free_blocks
+
+    def append_slot(self, seq: Sequence) -> bool:
+        """Grow the table to cover ``seq.num_tokens`` positions; True if a block
+        was taken.  ``OutOfBlocksError`` leaves everything unchanged."""
+        missing = self.blocks_needed(seq.num_tokens) - len(seq.block_table)
+        if missing <= 0:
+            return False
+        seq.block_table.extend(self._take(missing))
+        return True
+
+    def free(self, seq: Sequence) -> None:
+        """Release the sequence's blocks (ref-counted; a block-less sequence is a no-op)."""
+        for b in seq.block_table:
+            if self.ref_counts[b] <= 0:
+                raise RuntimeError(f"double free of block {b}")
+            self.ref_counts[b] -= 1
+            if self.ref_counts[b] == 0:
+                self._free.append(b)
+        seq.block_table = []
+
+    def _take(self, n: int) -> list[int]:
+        if n > len(self._free):
+            raise OutOfBlocksError(f"need {n} blocks, only {len(self._free)} free")
+        taken = [self._free.pop() for _ in range(n)]
+        for b in taken:
+            self.ref_counts[b] = 1
+        return taken
+
+    # ---- model-facing --------------------------------------------------------------
+    def batch_for(self, seqs: list[Sequence], new_lens: list[int] | None = None) -> "DevicePagedBatch":
+        """Step view for ``seqs``: each feeds ``new_lens[i]`` tokens (default: all
+        uncached ones) from position ``num_cached_tokens`` (tokquay/kv_cache.py:122-127)."""
+        starts = [s.num_cached_tokens for s in seqs]
+        new_lens = new_lens or [s.num_uncached_tokens for s in seqs]
+        ids = list(itertools.chain.from_iterable(
+            s.tokens_slice(st, st + n) for s, st, n in zip(seqs, starts, new_lens)))  # fmt: skip
+        return DevicePagedBatch(self, [s.block_table for s in seqs], starts, new_lens, ids)
+
+
+class BatchedKV:
+    """What a paged model forward needs from a step view (tokquay/kv_cache.py:130-157):
+    ``B``, ``T``, ``max_ctx``, ``positions [B, T]``, ``last_idx [B]``,
+    ``mask [B, 1, T, S]``, ``write(layer, k, v)``, ``gather(layer)``."""
+
+    B: int
+    T: int
+    max_ctx: int
+    positions: torch.Tensor
+    last_idx: torch.Tensor
+    mask: torch.Tensor
+
+    def write(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        raise NotImplementedError
+
+    def gather(self, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
+        raise NotImplementedError
+
+
+# ------------------------------------------------------------------------------ pinned staging
+class _PinnedRing:
+    """A few grow-only pinned host buffers for the per-step plan copies.  A
+    buffer is reused only after the copy that last read it has finished."""
+
+    def __init__(self, n: int = 4):
+        self._bufs: list[torch.Tensor | None] = [None] * n
+        self._events: list[torch.cuda.Event | None] = [None] * n
+        self._i = 0
+        self._lock = threading.Lock()
+
+    def take(self, n_ints: int) -> tuple[int, torch.Tensor]:
+        with self._lock:
+            i = self._i
+            self._i = (i + 1) % len(self._bufs)
+        ev = self._events[i]
+        if ev is not None:
+            ev.synchronize()
+        buf = self._bufs[i]
+        if buf is None or buf.numel() < n_ints:
+            size = max(n_ints, 4096, 0 if buf is None else 2 * buf.numel())
+            buf = torch.empty(size, dtype=torch.int32, pin_memory=True)
+            self._bufs[i] = buf
+        return i, buf
+
+    def mark(self, i: int, stream: torch.cuda.Stream) -> None:
+        ev = self._events[i]
+        if ev is None:
+            ev = self._events[i] = torch.cuda.Event()
+        ev.record(stream)
+
+
+_rings: dict[int, _PinnedRing] = {}
+_sm_counts: dict[int, int] = {}
+
+
+def _ring(device: torch.device) -> _PinnedRing:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    r = _rings.get(idx)
+    if r is None:
+        r = _rings.setdefault(idx, _PinnedRing())
+    return r
+
+
+def sm_count(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    n = _sm_counts.get(idx)
+    if n is None:
+        n = _sm_counts[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return n
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def plan_step_host(
+    block_size: int,
+    num_blocks: int,
+    n_head: int,
+    block_tables: list[list[int]],
+    start: list[int],
+    new_lens: list[int],
+    token_ids: list[int] | None = None,
+    vocab_size: int = 0,
+    target_units: int = 2368,
+    min_split_chunks: int = MIN_SPLIT_CHUNKS,
+    out: torch.Tensor | np.ndarray | None = None,
+) -> tuple[np.ndarray, np.ndarray]:
+    """Run ``tq_plan_step`` on the host: returns ``(plan, layout)`` (int32
+    arrays).  ``out`` (an int32 host buffer) is written in place when it is
+    large enough; otherwise a new array is returned.  Raises ValueError for a
+    batch the reference would reject."""
+    lib = _lib.load()
+    B = len(block_tables)
+    if B == 0 or not (B == len(start) == len(new_lens)):
+        raise ValueError("block_tables, start and new_lens must be non-empty and the same length")
+    st = np.asarray(start, dtype=np.int32)
+    ql = np.asarray(new_lens, dtype=np.int32)
+    lens = np.fromiter((len(t) for t in block_tables), dtype=np.int64, count=B)
+    offs = np.zeros(B + 1, dtype=np.int64)
+    np.cumsum(lens, out=offs[1:])
+    if offs[-1] > np.iinfo(np.int32).max:
+        raise ValueError("block tables too large")
+    offs32 = offs.astype(np.int32)
+    data = np.fromiter(itertools.chain.from_iterable(block_tables), dtype=np.int32, count=int(offs[-1]))
+    ids = None
+    if token_ids is not None:
+        ids = np.asarray(token_ids, dtype=np.int32)
+        if ids.size != int(ql.sum()):
+            raise ValueError(f"{ids.size} token ids for {int(ql.sum())} new tokens")
+    layout = np.zeros(_lib.PLAN_LAYOUT_LEN, dtype=np.int32)
+    ids_ptr = _ptr(ids) if ids is not None else None
+    data_ptr = _ptr(data) if data.size else None
+
+    def call(buf_ptr, cap):
+        return lib.tq_plan_step(B, _ptr(st), _ptr(ql), _ptr(offs32), data_ptr, ids_ptr, block_size,
+                                num_blocks, n_head, vocab_size, target_units, min_split_chunks,
+                                buf_ptr, cap, _ptr(layout))  # fmt: skip
+
+    if out is not None:
+        cap = out.numel() if isinstance(out, torch.Tensor) else out.size
+        buf_ptr = out.data_ptr() if isinstance(out, torch.Tensor) else _ptr(out)
+        status = call(buf_ptr, cap)
+        if status == _lib.TQ_OK:
+            return out, layout
+        if status != _lib.TQ_ERR_CAPACITY:
+            _lib.check(status, "tq_plan_step")
+    status = call(None, 0)
+    if status != _lib.TQ_ERR_CAPACITY:
+        _lib.check(status, "tq_plan_step")
+    plan = np.empty(int(layout[_lib.PLAN_TOTAL_INTS]), dtype=np.int32)
+    _lib.check(call(_ptr(plan), plan.size), "tq_plan_step")
+    return plan, layout
+
+
+class DevicePagedBatch(BatchedKV):
+    """One step over paged KV, resident on the GPU.
+
+    Sequence ``b`` feeds ``new_lens[b]`` tokens at positions
+    ``start[b] .. start[b]+new_lens[b]-1`` (prefill, decode and a mix of both in
+    one batch, as the reference allows).  The step is planned once and reused
+    by every layer.  Rows are ragged: row ``n`` of the flattened ``[N, C]``
+    activations is the n-th real new token in sequence order.
+
+    ``write`` / ``gather`` / ``positions`` / ``mask`` keep the reference's
+    ``BatchedKV`` contract for callers written against it; the model in this
+    package uses ``write_rows`` / ``attend_rows`` and never builds the dense
+    copies or the mask.
+    """
+
+    def __init__(
+        self,
+        allocator: BlockAllocator,
+        block_tables: list[list[int]],
+        start: list[int],
+        new_lens: list[int],
+        token_ids: list[int] | None = None,
+        stream: torch.cuda.Stream | None = None,
+    ):
+        pool = allocator.pool
+        if pool.device.type != "cuda":
+            raise RuntimeError("DevicePagedBatch needs the pool on a CUDA device")
+        if not block_tables or not (len(block_tables) == len(start) == len(new_lens)):
+            raise ValueError("block_tables, start and new_lens must be non-empty and the same length")
+        if min(new_lens) < 1:
+            raise ValueError("every sequence must feed at least one token")
+        bs = allocator.block_size
+        cfg = allocator.cfg
+        self.allocator = allocator
+        self.pool = pool
+        self.block_size = bs
+        self.n_layer, self.n_head, self.d_head = cfg.n_layer, cfg.n_head, cfg.d_head
+        self.B, self.T = len(block_tables), max(new_lens)
+        self.N = int(sum(new_lens))
+        self._start = list(start)
+        self._new_lens = list(new_lens)
+        ctx = [s + n for s, n in zip(start, new_lens)]
+        self.max_ctx = max(ctx)
+        self.num_blocks_gathered = max(cdiv(c, bs) for c in ctx)
+
+        device = pool.device
+        stream = stream or torch.cuda.current_stream(device)
+        ring = _ring(device)
+        slot, host = ring.take(0)
+        target = UNITS_PER_SM * sm_count(device)
+        plan, layout = plan_step_host(bs, allocator.num_blocks, cfg.n_head, block_tables, start, new_lens,
+                                      token_ids, cfg.vocab_size if token_ids is not None else 0,
+                                      target, MIN_SPLIT_CHUNKS, out=host)  # fmt: skip
+        total = int(layout[_lib.PLAN_TOTAL_INTS])
+        if plan is not host:  # the plan did not fit: grow the pinned buffer and stage it there
+            slot, host = ring.take(total)
+            host[:total].copy_(torch.from_numpy(plan[:total]))
+        self.layout = layout
+        dev = torch.empty(total, dtype=torch.int32, device=device)
+        with torch.cuda.stream(stream):
+            dev.copy_(host[:total], non_blocking=True)
+        ring.mark(slot, stream)
+        self.plan = dev
+        L = layout
+        self.num_items = int(L[_lib.PLAN_NUM_ITEMS])
+        self.num_combine = int(L[_lib.PLAN_NUM_COMBINE])
+        self.num_partials = int(L[_lib.PLAN_NUM_PARTIALS])
+        self.table_stride = int(L[_lib.PLAN_TABLE_STRIDE])
+        self.split_chunks = int(L[_lib.PLAN_SPLIT_CHUNKS])
+
+        def view(off_key: int, n: int) -> torch.Tensor:
+            o = int(L[off_key])
+            return dev[o:o + n]
+
+        self.counts = view(_lib.PLAN_OFF_COUNTS, 4)  # N, items, combine, B
+        self.seq_info = view(_lib.PLAN_OFF_SEQ_INFO, 4 * self.B).view(self.B, 4)
+        self.block_tables_i32 = view(_lib.PLAN_OFF_TABLES, self.B * self.table_stride)
+        self.slot_mapping = view(_lib.PLAN_OFF_SLOTS, self.N)
+        self.row_positions = view(_lib.PLAN_OFF_POSITIONS, self.N)
+        self.token_ids = view(_lib.PLAN_OFF_TOKEN_IDS, self.N) if token_ids is not None else None
+        self.last_rows = view(_lib.PLAN_OFF_LAST_ROWS, self.B)
+        self.work_items = view(_lib.PLAN_OFF_ITEMS, 8 * self.num_items)
+        self.combine_list = view(_lib.PLAN_OFF_COMBINE, 4 * self.num_combine)
+        self._dev_ptr = dev.data_ptr()
+        self._off = {k: int(L[k]) * 4 for k in range(_lib.PLAN_OFF_COUNTS, _lib.PLAN_LAYOUT_LEN)}
+        if self.num_partials:
+            self.partial_ml = torch.empty(2 * self.num_partials, dtype=torch.float32, device=device)
+            self.partial_acc = torch.empty(self.num_partials * self.d_head, dtype=torch.float32, device=device)
+        else:
+            self.partial_ml = self.partial_acc = None
+        self._positions = self._last_idx = self._mask = self._flat_bt = None
+
+    # ---- device-resident counts (for the kernels) ------------------------------------
+    def count_ptr(self, which: int) -> int:
+        """Device address of count ``which`` (0 = N, 1 = items, 2 = combine, 3 = B)."""
+        return self._dev_ptr + self._off[_lib.PLAN_OFF_COUNTS] + 4 * which
+
+    # ---- hot path: ragged rows ---------------------------------------------------------
+    def write_rows(self, layer: int, qkv: torch.Tensor, k_col: int, v_col: int, stream: int) -> None:
+        """Scatter K/V of the ``N`` new rows of ``qkv`` (row-major, K head 0 at
+        column ``k_col``, V at ``v_col``) into the pool (tokquay/kv_cache.py:228-232)."""
+        lib = _lib.load()
+        _lib.check(lib.tq_kv_write(self.pool.data_ptr(), self.allocator.num_blocks, self.n_layer,
+                                   self.n_head, self.block_size, self.d_head, layer, qkv.data_ptr(),
+                                   qkv.stride(0), k_col, v_col, self.slot_mapping.data_ptr(),
+                                   self.count_ptr(0), self.N, stream), "tq_kv_write")  # fmt: skip
+
+    def attend_rows(self, layer: int, q: torch.Tensor, out: torch.Tensor, stream: int) -> None:
+        """``out[n, h*d:(h+1)*d] = softmax(q_n,h . K / sqrt(d)) V`` over keys
+        0..position(n) of row n's sequence, read in place from the pool
+        (replaces tokquay/kv_cache.py:234-242 + tokquay/model.py:94-96).
+        ``q`` rows hold head h at columns ``h*d``; row stride is ``q.stride(0)``."""
+        lib = _lib.load()
+        pm = self.partial_ml.data_ptr() if self.partial_ml is not None else None
+        pa = self.partial_acc.data_ptr() if self.partial_acc is not None else None
+        _lib.check(lib.tq_paged_attention(
+            out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), self.pool.data_ptr(),
+            self.allocator.num_blocks, self.n_layer, self.n_head, self.block_size, self.d_head, layer,
+            self.block_tables_i32.data_ptr(), self.table_stride, self.work_items.data_ptr(),
+            self.count_ptr(1), self.num_items, pm, pa,
+            self.combine_list.data_ptr() if self.num_combine else None, self.count_ptr(2),
+            self.num_combine, 1.0 / math.sqrt(self.d_head), stream), "tq_paged_attention")  # fmt: skip
+
+    # ---- reference BatchedKV contract (not used by this package's model) ---------------
+    @property
+    def positions(self) -> torch.Tensor:
+        if self._positions is None:
+            st = torch.tensor(self._start, dtype=torch.long, device=self.pool.device)
+            self._positions = st[:, None] + torch.arange(self.T, device=self.pool.device)[None, :]
+        return self._positions
+
+    @property
+    def last_idx(self) -> torch.Tensor:
+        if self._last_idx is None:
+            self._last_idx = torch.tensor([n - 1 for n in self._new_lens], dtype=torch.long,
+                                          device=self.pool.device)
+        return self._last_idx
+
+    @property
+    def mask(self) -> torch.Tensor:
+        """``[B, 1, T, nb*bs]`` boolean mask of the reference (kv_cache.py:213-214)."""
+        if self._mask is None:
+            dev = self.pool.device
+            ctx = torch.tensor([s + n for s, n in zip(self._start, self._new_lens)], device=dev)
+            k_pos = torch.arange(self.num_blocks_gathered * self.block_size, device=dev)[None, None, :]
+            self._mask = ((k_pos <= self.positions[:, :, None]) & (k_pos < ctx[:, None, None]))[:, None]
+        return self._mask
+
+    def _valid_bt(self) -> tuple[torch.Tensor, torch.Tensor]:
+        if self._flat_bt is None:
+            b = [i for i, n in enumerate(self._new_lens) for _ in range(n)]
+            t = [j for n in self._new_lens for j in range(n)]
+            dev = self.pool.device
+            self._flat_bt = (torch.tensor(b, device=dev), torch.tensor(t, device=dev))
+        return self._flat_bt
+
+    def write(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Reference-shaped write: ``k``, ``v`` are padded ``[B, H, T, d]``;
+        padded slots are never written."""
+        b, t = self._valid_bt()
+        kv = torch.cat([k[b, :, t].reshape(self.N, -1), v[b, :, t].reshape(self.N, -1)], dim=1)
+        kv = kv.to(torch.float32).contiguous()
+        C = self.n_head * self.d_head
+        self.write_rows(layer, kv, 0, C, torch.cuda.current_stream(self.pool.device).cuda_stream)
+
+    def gather(self, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Dense ``[B, H, nb*bs, d]`` copies, for callers of the reference
+        contract only; the CUDA attention never builds them."""
+        nb = self.num_blocks_gathered
+        tbl = self.block_tables_i32.view(self.B, self.table_stride)[:, :nb].long()
+        out = []
+        for kv in (0, 1):
+            g = self.pool[tbl, layer, kv].permute(0, 2, 1, 3, 4)
+            out.append(g.reshape(self.B, g.shape[1], -1, g.shape[-1]))
+        return out[0], out[1]
+
+    def attend(self, layer: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        """Drop-in for the reference's paged attention branch (model.py:73-78 +
+        :94-96): writes the new K/V, attends with the CUDA kernel, returns
+        ``[B, H, T, d]`` (padded query slots are left at zero)."""
+        self.write(layer, k, v)
+        b, t = self._valid_bt()
+        C = self.n_head * self.d_head
+        qf = q[b, :, t].reshape(self.N, C).to(torch.float32).contiguous()
+        of = torch.empty(self.N, C, dtype=torch.float32, device=q.device)
+        self.attend_rows(layer, qf, of, torch.cuda.current_stream(q.device).cuda_stream)
+        out = torch.zeros(self.B, self.T, self.n_head, self.d_head, dtype=q.dtype, device=q.device)
+        out[b, t] = of.view(self.N, self.n_head, self.d_head).to(q.dtype)
+        return out.transpose(1, 2)

@@ -1,0 +1,169 @@
+"""GPT-2 with the paged forward on the B200 kernels.
+
+Parameter names and shapes are the reference's (tokquay/model.py:24-35,
+:59-134), so a ``state_dict`` moves between the two models unchanged.  The
+paged forward (tokquay/model.py:136-181) runs on ragged rows -- only the N
+real new tokens of the step, never the reference's padded ``B x T`` -- with:
+
+* the fp32 linears on torch matmul (cuBLAS SGEMM; TF32 must stay off);
+* ``tq_embed_layernorm``, ``tq_bias_residual_layernorm``, ``tq_bias_gelu`` and
+  ``tq_layernorm_rows`` for everything elementwise around them;
+* ``tq_kv_write`` + ``tq_paged_attention`` for the attention over the pool.
+
+In the last layer only each sequence's last row is carried past attention
+when ``last_only`` is set: the other rows' K/V are already in the pool and
+their outputs would be discarded (model.py:179).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+
+from tokquay_b200 import _lib
+from tokquay_b200.kv_cache import DevicePagedBatch
+
+
+@dataclass
+class GPT2Config:
+    vocab_size: int = 50257
+    n_positions: int = 1024
+    n_embd: int = 768
+    n_layer: int = 12
+    n_head: int = 12
+    layer_norm_eps: float = 1e-5
+
+    @property
+    def d_head(self) -> int:
+        return self.n_embd // self.n_head
+
+
+class Attention(nn.Module):
+    def __init__(self, cfg: GPT2Config):
+        super().__init__()
+        self.c_attn = nn.Linear(cfg.n_embd, 3 * cfg.n_embd)
+        self.c_proj = nn.Linear(cfg.n_embd, cfg.n_embd)
+
+
+class MLP(nn.Module):
+    def __init__(self, cfg: GPT2Config):
+        super().__init__()
+        self.c_fc = nn.Linear(cfg.n_embd, 4 * cfg.n_embd)
+        self.c_proj = nn.Linear(4 * cfg.n_embd, cfg.n_embd)
+
+
+class Block(nn.Module):
+    def __init__(self, cfg: GPT2Config):
+        super().__init__()
+        self.ln_1 = nn.LayerNorm(cfg.n_embd, eps=cfg.layer_norm_eps)
+        self.attn = Attention(cfg)
+        self.ln_2 = nn.LayerNorm(cfg.n_embd, eps=cfg.layer_norm_eps)
+        self.mlp = MLP(cfg)
+
+
+def _tf32_off() -> bool:
+    return not torch.backends.cuda.matmul.allow_tf32 and torch.get_float32_matmul_precision() == "highest"
+
+
+class GPT2(nn.Module):
+    def __init__(self, cfg: GPT2Config | None = None):
+        super().__init__()
+        self.cfg = cfg or GPT2Config()
+        self.wte = nn.Embedding(self.cfg.vocab_size, self.cfg.n_embd)
+        self.wpe = nn.Embedding(self.cfg.n_positions, self.cfg.n_embd)
+        self.h = nn.ModuleList(Block(self.cfg) for _ in range(self.cfg.n_layer))
+        self.ln_f = nn.LayerNorm(self.cfg.n_embd, eps=self.cfg.layer_norm_eps)
+
+    # ---- reference-shaped entry point --------------------------------------------------
+    @torch.no_grad()
+    def forward(self, input_ids: torch.Tensor, cache: DevicePagedBatch, last_only: bool = False) -> torch.Tensor:
+        """``input_ids [B, T]`` (right-padded, as the reference takes them) ->
+        logits ``[B, T, V]`` (or ``[B, 1, V]`` with ``last_only``).  Logits of
+        padded slots are zero.  Only the paged path exists in this package."""
+        if not isinstance(cache, DevicePagedBatch):
+            raise TypeError("this model runs the paged forward only: pass a DevicePagedBatch")
+        B, T = input_ids.shape
+        if (B, T) != (cache.B, cache.T):
+            raise ValueError(f"input_ids {tuple(input_ids.shape)} does not match batch {(cache.B, cache.T)}")
+        b, t = cache._valid_bt()
+        ids = input_ids.to(cache.pool.device)[b, t].to(torch.int32).contiguous()
+        return self.forward_paged(cache, last_only=last_only, ids=ids)
+
+    # ---- hot path ------------------------------------------------------------------------
+    @torch.no_grad()
+    def forward_paged(self, batch: DevicePagedBatch, last_only: bool = True,
+                      ids: torch.Tensor | None = None) -> torch.Tensor:  # fmt: skip
+        """Paged forward over the batch's ragged rows.  ``ids`` (int32 ``[N]``
+        on the device) defaults to the token ids the batch was planned with.
+        Returns ``[B, 1, V]`` (``last_only``) or ``[B, T, V]``."""
+        cfg = self.cfg
+        if batch.max_ctx > cfg.n_positions:  # tokquay/model.py:159-160
+            raise ValueError(f"sequence length {batch.max_ctx} exceeds n_positions={cfg.n_positions}")
+        if not _tf32_off():
+            raise RuntimeError("TF32 matmul is enabled; the fp32 paged forward needs it off "
+                               "(torch.backends.cuda.matmul.allow_tf32 = False, precision 'highest')")
+        if ids is None:
+            ids = batch.token_ids
+            if ids is None:
+                raise ValueError("the batch carries no token ids; pass ids")
+        lib = _lib.load()
+        dev = batch.pool.device
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        C, eps, N, B = cfg.n_embd, cfg.layer_norm_eps, batch.N, batch.B
+        n_ptr, b_ptr = batch.count_ptr(0), batch.count_ptr(3)
+        x = torch.empty(N, C, dtype=torch.float32, device=dev)
+        xa = torch.empty(N, C, dtype=torch.float32, device=dev)
+        h0 = self.h[0].ln_1
+        _lib.check(lib.tq_embed_layernorm(
+            x.data_ptr(), xa.data_ptr(), ids.data_ptr(), batch.row_positions.data_ptr(),
+            self.wte.weight.data_ptr(), self.wpe.weight.data_ptr(), cfg.vocab_size, cfg.n_positions,
+            h0.weight.data_ptr(), h0.bias.data_ptr(), eps, C, n_ptr, N, stream), "tq_embed_layernorm")  # fmt: skip
+
+        rows, rows_ptr = N, n_ptr
+        for i, blk in enumerate(self.h):
+            last = i == cfg.n_layer - 1
+            att = blk.attn
+            qkv = torch.addmm(att.c_attn.bias, xa, att.c_attn.weight.t())  # [N, 3C]
+            batch.write_rows(i, qkv, C, 2 * C, stream)
+            a = torch.empty(N, C, dtype=torch.float32, device=dev)
+            batch.attend_rows(i, qkv, a, stream)
+            if last and last_only and N != B:
+                # Only the last row of each sequence is sampled from (model.py:179).
+                sel = batch.last_rows
+                a, x = a.index_select(0, sel), x.index_select(0, sel)
+                xa = torch.empty(B, C, dtype=torch.float32, device=dev)
+                rows, rows_ptr = B, b_ptr
+            y = torch.mm(a, att.c_proj.weight.t())
+            _lib.check(lib.tq_bias_residual_layernorm(
+                x.data_ptr(), xa.data_ptr(), y.data_ptr(), att.c_proj.bias.data_ptr(),
+                blk.ln_2.weight.data_ptr(), blk.ln_2.bias.data_ptr(), eps, C, rows_ptr, rows, stream),
+                "tq_bias_residual_layernorm")  # fmt: skip
+            hid = torch.mm(xa, blk.mlp.c_fc.weight.t())
+            _lib.check(lib.tq_bias_gelu(hid.data_ptr(), blk.mlp.c_fc.bias.data_ptr(), hid.shape[1],
+                                        rows_ptr, rows, stream), "tq_bias_gelu")  # fmt: skip
+            y = torch.mm(hid, blk.mlp.c_proj.weight.t())
+            nxt = None if last else self.h[i + 1].ln_1
+            _lib.check(lib.tq_bias_residual_layernorm(
+                x.data_ptr(), xa.data_ptr(), y.data_ptr(), blk.mlp.c_proj.bias.data_ptr(),
+                nxt.weight.data_ptr() if nxt is not None else None,
+                nxt.bias.data_ptr() if nxt is not None else None, eps, C, rows_ptr, rows, stream),
+                "tq_bias_residual_layernorm")  # fmt: skip
+
+        if last_only:
+            xf = torch.empty(B, C, dtype=torch.float32, device=dev)
+            sel_ptr = None if rows == B else batch.last_rows.data_ptr()
+            _lib.check(lib.tq_layernorm_rows(xf.data_ptr(), x.data_ptr(), sel_ptr, self.ln_f.weight.data_ptr(),
+                                             self.ln_f.bias.data_ptr(), eps, C, b_ptr, B, stream),
+                       "tq_layernorm_rows")  # fmt: skip
+            return torch.mm(xf, self.wte.weight.t()).unsqueeze(1)  # tied LM head, model.py:181
+        xf = torch.empty(N, C, dtype=torch.float32, device=dev)
+        _lib.check(lib.tq_layernorm_rows(xf.data_ptr(), x.data_ptr(), None, self.ln_f.weight.data_ptr(),
+                                         self.ln_f.bias.data_ptr(), eps, C, n_ptr, N, stream),
+                   "tq_layernorm_rows")  # fmt: skip
+        logits = torch.mm(xf, self.wte.weight.t())
+        out = torch.zeros(B, batch.T, cfg.vocab_size, dtype=torch.float32, device=dev)
+        b, t = batch._valid_bt()
+        out[b, t] = logits
+        return out
