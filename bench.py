@@ -1,0 +1,504 @@
+"""Decode throughput of the B200 paged-attention path (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg2|cfg4|cfg1] [--impl ours|reference]
+
+Workload (default ``cfg2``): GPT-2 124M architecture,
+random-init N(0, 0.02) fp32 weights, 64 sequences with contexts uniform in
+[16, 512], block size 16, fragmented block tables, consecutive greedy decode
+steps.  A *step* is one paged forward over the 64 sequences plus the greedy
+argmax that feeds the next step.  Config 2's pool of 1,024 blocks cannot hold
+its contexts, so it runs on 2,048 blocks (the reference case does the same).
+
+Multi-GPU: one process per GPU (torchrun), each an independent engine replica
+with its own sequences and KV pool; no collective on the data path.  Timing is
+the max over ranks; ``value`` is the tokens of all ranks over that time.
+
+Reported on one JSON line (rank 0):
+  value        device-resident loop: step plans already in HBM, each step's
+               input tokens are the previous step's argmax (CUDA events)
+  e2e          the public API: ``paged_forward`` + argmax + ``.tolist()`` per
+               step, host planning and the pinned host->device plan copy inside
+  roofline     the paged-attention kernel (+ its split-K combine): algorithmic
+               bytes (K/V rows read + q read + output write + split scratch) per
+               launch over its CUDA-event duration, vs the measured HBM copy peak
+  cpu_baseline the numpy oracle (the reference algorithm: dense gather + masked
+               softmax) on the host cores, on a bounded sample of the workload
+
+``--impl reference`` times that CPU implementation as the main line (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_PATH = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 2**20
+
+WORKLOADS = {
+    "cfg2": dict(n_seqs=64, ctx_range=(16, 512), block_size=16, num_blocks=2048, grow=True,
+                 desc="BASELINE config 2: 64 seqs, ctx U[16,512], bs 16, 2048 blocks, consecutive greedy decode steps"),
+    "cfg4": dict(n_seqs=512, ctx_range=(256, 1024), block_size=32, pool_bytes=150e9, grow=False,
+                 desc="BASELINE config 4: 512 seqs, ctx U[256,1024], bs 32, ~150 GB pool, repeated decode step"),
+    "cfg1": dict(n_seqs=8, ctx_range=(16, 256), block_size=16, num_blocks=1024, grow=True,
+                 desc="BASELINE config 1: 8 seqs, ctx U[16,256], bs 16, 1024 blocks, greedy decode steps"),
+}  # fmt: skip
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------------------ distributed
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples the SM clock and throttle reasons through NVML every 10 ms."""
+
+    REASONS = {
+        "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8,
+        "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index: int):
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            try:  # the CUDA device's own GPU, whatever CUDA_VISIBLE_DEVICES remaps
+                uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+                self._h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:  # noqa: BLE001
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001
+            log(f"clock sampling unavailable: {e}")
+            self._nvml = None
+
+    def _run(self):
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM))
+                get = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    n.nvmlDeviceGetCurrentClocksThrottleReasons
+                bits = get(self._h)
+                for name, mask in self.REASONS.items():
+                    if bits & mask:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(0.01)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+        }
+
+
+# ------------------------------------------------------------------------------ setup
+def make_model(device, seed=0):
+    from tokquay_b200 import GPT2, GPT2Config
+    from tokquay_b200 import workloads as W
+
+    cfg = GPT2Config(**W.GPT2_SMALL)
+    with torch.device("meta"):
+        m = GPT2(cfg)
+    m = m.to_empty(device=device)
+    g = torch.Generator(device=device).manual_seed(seed)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.normal_(0.0, 0.02, generator=g)  # BASELINE random init: every parameter N(0, 0.02)
+    return m.eval()
+
+
+def make_allocator(spec, cfg, device):
+    from tokquay_b200 import BlockAllocator
+
+    bs = spec["block_size"]
+    if "num_blocks" in spec:
+        nb = spec["num_blocks"]
+    else:
+        per_block = cfg.n_layer * 2 * cfg.n_head * bs * cfg.d_head * 4
+        free = torch.cuda.mem_get_info(device)[0]
+        nb = int(min(spec["pool_bytes"], free - 8e9) // per_block)
+    a = BlockAllocator(cfg, nb, bs, device=device)
+    g = torch.Generator(device=device).manual_seed(1234)
+    a.pool.normal_(generator=g)  # BASELINE: K/V pool filled N(0, 1)
+    return a
+
+
+def reset_allocator(a):
+    a._free = list(range(a.num_blocks - 1, -1, -1))
+    a.ref_counts = [0] * a.num_blocks
+
+
+def make_case(spec, a, seed):
+    from tokquay_b200 import Sequence
+    from tokquay_b200 import workloads as W
+
+    reset_allocator(a)
+    return W.decode_case(Sequence, a, spec["n_seqs"], spec["ctx_range"], a.cfg.vocab_size, seed=seed)
+
+
+def attn_bytes(ctx_list, n_head, d, num_partials):
+    """Algorithmic bytes of one attention launch (one layer): every sequence's
+    K and V rows of all heads read once, q read, output written, split-K
+    partials written and read back."""
+    kv = sum(ctx_list) * n_head * d * 4 * 2
+    qo = len(ctx_list) * n_head * d * 4 * 2
+    part = num_partials * (d + 2) * 4 * 2
+    return kv + qo + part
+
+
+# ------------------------------------------------------------------------------ our arm
+def run_ours(args, world, rank, local):
+    from tokquay_b200 import paged_forward
+    from tokquay_b200.kv_cache import DevicePagedBatch
+
+    spec = WORKLOADS[args.workload]
+    device = torch.device("cuda", local)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.set_float32_matmul_precision("highest")
+    model = make_model(device)
+    cfg = model.cfg
+    a = make_allocator(spec, cfg, device)
+    seed = 2 + rank  # each replica decodes its own sequences
+    K, Wm = args.steps, args.warmup
+    total_steps = K + Wm
+
+    # ---- device-resident loop: plan every step first (bookkeeping only) -------------
+    case = make_case(spec, a, seed)
+    seqs = case.seqs
+    plans, ctx_per_step = [], []
+    for k in range(total_steps):
+        starts = [s.num_cached_tokens for s in seqs]
+        ids = [s.tokens_slice(st, st + 1)[0] for s, st in zip(seqs, starts)]
+        b = DevicePagedBatch(a, [s.block_table for s in seqs], starts, [1] * len(seqs), ids)
+        plans.append(b)
+        ctx_per_step.append([st + 1 for st in starts])
+        if spec["grow"]:
+            for s in seqs:
+                s.num_cached_tokens += 1
+                s.append_token(0)  # placeholder; the device loop feeds the real argmax
+                a.append_slot(s)
+    torch.cuda.synchronize(device)
+
+    def device_step(k):
+        logits = model.forward_paged(plans[k], last_only=True)[:, 0]
+        tok = logits.argmax(-1)
+        if k + 1 < total_steps:
+            plans[k + 1].token_ids.copy_(tok)
+        return tok
+
+    for k in range(Wm):
+        device_step(k)
+    torch.cuda.synchronize(device)
+    model.attention_events = []
+    launches0 = model.kernel_launches
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for k in range(Wm, total_steps):
+            device_step(k)
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    barrier(world)
+    ms = start.elapsed_time(end)
+    launches = model.kernel_launches - launches0
+    attn_ms = [e0.elapsed_time(e1) for e0, e1 in model.attention_events]
+    model.attention_events = None
+    n_layer = cfg.n_layer
+    bytes_per_launch = [
+        attn_bytes(ctx_per_step[k], cfg.n_head, cfg.d_head, plans[k].num_partials)
+        for k in range(Wm, total_steps) for _ in range(n_layer)
+    ]  # fmt: skip
+    tokens = len(seqs) * K
+    ms_max = max_over_ranks(ms, world)
+    tokens_all = sum_over_ranks(tokens, world)
+    del plans
+
+    # ---- end to end through the public API -----------------------------------------
+    case = make_case(spec, a, seed)
+    seqs = case.seqs
+    h2d = []
+
+    def api_step():
+        logits = paged_forward(model, a, seqs)
+        toks = logits.argmax(-1).tolist()  # the step's device->host read
+        for s, t in zip(seqs, toks):
+            s.append_token(t)
+            if spec["grow"]:
+                a.append_slot(s)
+            else:
+                s.num_cached_tokens -= 1  # repeat the same step
+                s.output_token_ids.pop()
+        return toks
+
+    for _ in range(Wm):
+        api_step()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(K):
+        api_step()
+        h2d.append(model.last_h2d_bytes)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    wall_ms = (time.perf_counter() - t0) * 1e3
+    barrier(world)
+    e2e_ms = max(e0.elapsed_time(e1), 0.0)
+    e2e_ms_max = max_over_ranks(e2e_ms, world)
+    # Bytes copied per step: the packed step plan (host->device, token ids
+    # included) and the B int64 sampled tokens back.
+    h2d_bytes = sum(h2d) / len(h2d)
+    d2h_bytes = len(seqs) * 8
+
+    result = None
+    if rank == 0:
+        peaks = json.loads(PEAKS_PATH.read_text()) if PEAKS_PATH.exists() else {}
+        peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
+        avg_attn_ms = sum(attn_ms) / len(attn_ms)
+        avg_bytes = sum(bytes_per_launch) / len(bytes_per_launch)
+        achieved = avg_bytes / (avg_attn_ms * 1e-3) / 1e9
+        result = {
+            "metric": "decode tok/s",
+            "value": tokens_all / (ms_max * 1e-3),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": K,
+            "warmup": Wm,
+            "ms_per_step": ms_max / K,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic",
+            "config": {
+                "workload": spec["desc"],
+                "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32, TF32 off",
+                "global_batch": len(seqs) * world,
+                "seq_len": f"ctx U{list(spec['ctx_range'])}",
+                "block_size": spec["block_size"],
+                "num_blocks": a.num_blocks,
+                "parallelism": f"replicas{world} (one engine + KV pool per GPU, no collective)",
+                "l2": "inputs larger than L2: each step reads the whole weight set (0.5 GB) and every "
+                      "context's K/V of 12 layers (> 1 GB), so no step finds the previous step's data in L2",
+            },  # fmt: skip
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "paged_attention_kernel (+ attn_combine_kernel when split)",
+                "achieved": achieved,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "traffic": None,
+                "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
+                "algorithmic_bytes_per_launch": avg_bytes,
+                "avg_launch_ms": avg_attn_ms,
+                "attention_share_of_step": sum(attn_ms) / ms,
+            },
+            "e2e": {
+                "value": tokens_all / (e2e_ms_max * 1e-3),
+                "unit": "tok/s",
+                "h2d_bytes_per_step": h2d_bytes,
+                "d2h_bytes_per_step": d2h_bytes,
+                "ms_per_step": e2e_ms_max / K,
+                "wall_ms_per_step_rank0": wall_ms / K,
+            },
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+    return result
+
+
+# ------------------------------------------------------------------------------ CPU oracle
+def cpu_oracle_rate(spec, n_seqs, steps, warmup, seed=2, budget_s=None):
+    """The numpy oracle (reference algorithm) on the host: decode steps over
+    ``n_seqs`` sequences of the workload.  Returns (tok/s, sample description, threads)."""
+    import oracle
+    from tokquay_b200 import BlockAllocator, GPT2Config, Sequence
+    from tokquay_b200 import workloads as W
+
+    cfg = GPT2Config(**W.GPT2_SMALL)
+    rng = np.random.default_rng(0)
+    weights = {n: (rng.standard_normal(s, dtype=np.float32) * np.float32(0.02)) for n, s in W.param_specs(cfg)}
+    bs = spec["block_size"]
+    max_ctx = spec["ctx_range"][1] + steps + warmup + 1
+    nb = n_seqs * (-(-max_ctx // bs)) + 1
+    a = BlockAllocator(cfg, nb, bs, device="cpu")  # bookkeeping only
+    a.pool = torch.empty(0)
+    case = W.decode_case(Sequence, a, n_seqs, spec["ctx_range"], cfg.vocab_size, seed=seed)
+    pool = np.zeros((nb, cfg.n_layer, 2, cfg.n_head, bs, cfg.d_head), np.float32)
+    seqs = case.seqs
+    times = []
+    for k in range(warmup + steps):
+        t0 = time.perf_counter()
+        logits = oracle.paged_forward(weights, cfg, pool, bs, seqs)
+        dt = time.perf_counter() - t0
+        if k >= warmup:
+            times.append(dt)
+        for s, t in zip(seqs, logits.argmax(-1).tolist()):
+            s.append_token(int(t))
+            if spec["grow"]:
+                a.append_slot(s)
+            else:
+                s.num_cached_tokens -= 1
+                s.output_token_ids.pop()
+        if budget_s and sum(times) > budget_s:
+            break
+    try:
+        from threadpoolctl import threadpool_info
+
+        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except Exception:  # noqa: BLE001
+        threads = os.cpu_count()
+    rate = n_seqs * len(times) / sum(times)
+    sample = f"{len(times)} decode steps x {n_seqs} sequences of {spec['desc']} (numpy oracle, float32)"
+    return rate, sample, threads
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    spec = WORKLOADS[args.workload]
+    # Each step is a bounded sample: a decode step over a subset of the sequences.
+    n = min(spec["n_seqs"], 16)
+    t0 = time.perf_counter()
+    rate, sample, threads = cpu_oracle_rate(spec, n, args.steps, args.warmup, budget_s=150)
+    return {
+        "impl": "reference",
+        "metric": "decode tok/s",
+        "value": rate,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": n / rate * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": spec["desc"], "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32"},
+        "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": time.perf_counter() - t0,
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("warmup raised to 3 (timing rule)")
+        args.warmup = 3
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        res = run_reference(args, world, rank)
+    else:
+        res = run_ours(args, world, rank, local)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            rate, sample, threads = cpu_oracle_rate(WORKLOADS[args.workload], 16, 2, 1)
+            res["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
+                                   "sample": sample}  # fmt: skip
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

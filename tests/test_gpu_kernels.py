@@ -1,0 +1,230 @@
+"""Kernel-level parity on the GPU, through the C ABI.
+
+* KV write: bit-exact against a torch scatter of the same rows.
+* Paged attention (decode and causal prefill rows mixed, split-K or not):
+  against a float64 torch reference of softmax(q k^T / sqrt(d)) v over each
+  row's keys 0..position, on a pool whose unused slots hold NaN -- so any
+  read of a slot outside a sequence's causal range poisons the result.
+* Fused LayerNorm / bias / GELU / residual: against torch fp32 ops.
+"""
+
+import math
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from tokquay_b200 import _lib
+from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, cdiv
+from tokquay_b200.model import GPT2Config
+
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device"),
+]
+
+ATTN_RTOL = 2e-5  # fp32 online softmax vs a float64 reference, relative to max |out|
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _mixed_batch(rng, alloc, n_seqs, max_ctx, prefill_frac):
+    """Random sequences: some decode one token after a cached context, some
+    prefill a chunk starting at an arbitrary cached position."""
+    bs = alloc.block_size
+    tables, start, new = [], [], []
+    for _ in range(n_seqs):
+        if rng.random() < prefill_frac:
+            n = rng.randint(2, 70)
+            s = rng.randint(0, max(0, max_ctx - n))
+        else:
+            n = 1
+            s = rng.randint(0, max_ctx - 1)
+        tables.append(alloc._take(cdiv(s + n, bs)))
+        start.append(s)
+        new.append(n)
+    return tables, start, new
+
+
+def _reference_attention(pool, layer, q, tables, start, new, bs):
+    """float64 per-row softmax attention over keys 0..position (the semantics
+    of tokquay/model.py:94-96 with the mask of tokquay/kv_cache.py:213-214)."""
+    H, d = pool.shape[3], pool.shape[5]
+    out = torch.empty(q.shape[0], H * d, dtype=torch.float64, device=q.device)
+    row = 0
+    for tbl, s, n in zip(tables, start, new):
+        ctx = s + n
+        idx = torch.tensor(tbl[:cdiv(ctx, bs)], device=q.device)
+        k = pool[idx, layer, 0].permute(1, 0, 2, 3).reshape(H, -1, d)[:, :ctx].double()
+        v = pool[idx, layer, 1].permute(1, 0, 2, 3).reshape(H, -1, d)[:, :ctx].double()
+        qq = q[row:row + n].view(n, H, d).transpose(0, 1).double()  # [H, n, d]
+        sc = qq @ k.transpose(1, 2) / math.sqrt(d)
+        pos = torch.arange(s, s + n, device=q.device)[:, None]
+        sc = sc.masked_fill(torch.arange(ctx, device=q.device)[None, :] > pos, float("-inf"))
+        out[row:row + n] = (torch.softmax(sc, -1) @ v).transpose(0, 1).reshape(n, H * d)
+        row += n
+    return out
+
+
+@pytest.mark.parametrize("bs", [1, 4, 16, 32, 64, 256])
+@pytest.mark.parametrize("kind", ["decode", "mixed", "prefill"])
+@pytest.mark.parametrize("seed", [0, 1])
+def test_paged_attention_matches_float64_reference(bs, kind, seed):
+    rng = random.Random(seed * 100 + bs)
+    cfg = GPT2Config(vocab_size=64, n_positions=1024, n_embd=256, n_layer=2, n_head=4)
+    max_ctx = 700
+    n_seqs = {"decode": 37, "mixed": 21, "prefill": 6}[kind]
+    frac = {"decode": 0.0, "mixed": 0.3, "prefill": 1.0}[kind]
+    num_blocks = n_seqs * cdiv(max_ctx + 2, bs) + 8
+    alloc = BlockAllocator(cfg, num_blocks, bs, device="cuda")
+    random.Random(seed).shuffle(alloc._free)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    alloc.pool.normal_(generator=g)
+    tables, start, new = _mixed_batch(rng, alloc, n_seqs, max_ctx, frac)
+    # Poison every slot at or beyond each sequence's context: masked keys must never be read.
+    for tbl, s, n in zip(tables, start, new):
+        ctx = s + n
+        for j, blk in enumerate(tbl):
+            lo = max(0, ctx - j * bs)
+            if lo < bs:
+                alloc.pool[blk, :, :, :, lo:] = float("nan")
+    for blk in alloc._free:
+        alloc.pool[blk] = float("nan")
+    batch = DevicePagedBatch(alloc, tables, start, new)
+    C = cfg.n_embd
+    layer = 1
+    # q rows live inside a wider [N, 3C] buffer, as the c_attn output does.
+    qkv = torch.randn(batch.N, 3 * C, device="cuda", generator=g)
+    out = torch.full((batch.N, C), float("nan"), device="cuda")
+    batch.attend_rows(layer, qkv, out, _stream())
+    torch.cuda.synchronize()
+    want = _reference_attention(alloc.pool, layer, qkv[:, :C], tables, start, new, bs)
+    assert torch.isfinite(out).all()
+    err = (out.double() - want).abs().max().item()
+    assert err <= ATTN_RTOL * want.abs().max().item(), (err, batch.split_chunks, batch.num_combine)
+    assert _lib.device_status() == 0
+
+
+def test_paged_attention_split_k_is_exercised():
+    """Few long decodes force split-K + combine; compare with the unsplit run."""
+    cfg = GPT2Config(vocab_size=64, n_positions=1024, n_embd=768, n_layer=1, n_head=12)
+    alloc = BlockAllocator(cfg, 8 * 64 + 4, 16, device="cuda")
+    alloc.pool.normal_()
+    tables = [alloc._take(64) for _ in range(8)]
+    start, new = [1000 + i for i in range(8)], [1] * 8
+    batch = DevicePagedBatch(alloc, tables, start, new)
+    assert batch.num_combine == 8 and batch.split_chunks >= 2
+    qkv = torch.randn(8, 3 * 768, device="cuda")
+    out = torch.empty(8, 768, device="cuda")
+    batch.attend_rows(0, qkv, out, _stream())
+    want = _reference_attention(alloc.pool, 0, qkv[:, :768], tables, start, new, 16)
+    assert (out.double() - want).abs().max().item() <= ATTN_RTOL * want.abs().max().item()
+
+
+@pytest.mark.parametrize("bs", [1, 4, 16, 32, 128])
+def test_kv_write_is_bit_exact(bs):
+    cfg = GPT2Config(vocab_size=64, n_positions=1024, n_embd=768, n_layer=3, n_head=12)
+    rng = random.Random(bs)
+    alloc = BlockAllocator(cfg, 200, bs, device="cuda")
+    random.Random(3).shuffle(alloc._free)
+    alloc.pool.normal_()
+    before = alloc.pool.clone()
+    tables, start, new = [], [], []
+    for _ in range(9):
+        s, n = rng.randint(0, 300), rng.choice([1, 1, 17, 40])
+        if cdiv(s + n, bs) > alloc.num_free_blocks:
+            break
+        tables.append(alloc._take(cdiv(s + n, bs)))
+        start.append(s)
+        new.append(n)
+    batch = DevicePagedBatch(alloc, tables, start, new)
+    qkv = torch.randn(batch.N, 3 * 768, device="cuda")
+    layer = 2
+    batch.write_rows(layer, qkv, 768, 1536, _stream())
+    torch.cuda.synchronize()
+    want = before.clone()
+    row = 0
+    for tbl, s, n in zip(tables, start, new):
+        for t in range(n):
+            p = s + t
+            blk, off = tbl[p // bs], p % bs
+            want[blk, layer, 0, :, off] = qkv[row, 768:1536].view(12, 64)
+            want[blk, layer, 1, :, off] = qkv[row, 1536:].view(12, 64)
+            row += 1
+    assert torch.equal(alloc.pool, want)
+
+
+def _ln(x, w, b, eps):
+    return torch.nn.functional.layer_norm(x, (x.shape[-1],), w, b, eps)
+
+
+@pytest.mark.parametrize("C", [128, 768, 1024])
+def test_fused_row_kernels_match_torch(C):
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(C)
+    N, V, P, eps = 37, 500, 64, 1e-5
+    dev = "cuda"
+    r = lambda *s: torch.randn(*s, device=dev, generator=g)  # noqa: E731
+    wte, wpe, w, b = r(V, C), r(P, C), r(C), r(C)
+    ids = torch.randint(0, V, (N,), device=dev, dtype=torch.int32, generator=g)
+    pos = torch.randint(0, P, (N,), device=dev, dtype=torch.int32, generator=g)
+    n_dev = torch.tensor([N, 0, 0, 0], dtype=torch.int32, device=dev)
+    x, xa = torch.empty(N, C, device=dev), torch.empty(N, C, device=dev)
+    s = _stream()
+    _lib.check(lib.tq_embed_layernorm(x.data_ptr(), xa.data_ptr(), ids.data_ptr(), pos.data_ptr(), wte.data_ptr(),
+                                      wpe.data_ptr(), V, P, w.data_ptr(), b.data_ptr(), eps, C, n_dev.data_ptr(), N,
+                                      s), "embed")  # fmt: skip
+    x_ref = wte[ids.long()] + wpe[pos.long()]
+    torch.testing.assert_close(x, x_ref, rtol=0, atol=0)
+    torch.testing.assert_close(xa, _ln(x_ref, w, b, eps), rtol=1e-5, atol=1e-5)
+
+    y, bias = r(N, C), r(C)
+    x0 = x.clone()
+    _lib.check(lib.tq_bias_residual_layernorm(x.data_ptr(), xa.data_ptr(), y.data_ptr(), bias.data_ptr(),
+                                              w.data_ptr(), b.data_ptr(), eps, C, n_dev.data_ptr(), N, s),
+               "bias_residual_ln")  # fmt: skip
+    x1 = x0 + (y + bias)
+    torch.testing.assert_close(x, x1, rtol=0, atol=0)
+    torch.testing.assert_close(xa, _ln(x1, w, b, eps), rtol=1e-5, atol=1e-5)
+    xa_before = xa.clone()
+    _lib.check(lib.tq_bias_residual_layernorm(x.data_ptr(), None, y.data_ptr(), bias.data_ptr(), None, None, eps, C,
+                                              n_dev.data_ptr(), N, s), "bias_residual")  # fmt: skip
+    torch.testing.assert_close(x, x1 + (y + bias), rtol=0, atol=0)
+    assert torch.equal(xa, xa_before)
+
+    rows = torch.tensor([5, 0, 36, 17], dtype=torch.int32, device=dev)
+    out = torch.empty(4, C, device=dev)
+    n4 = torch.tensor([4], dtype=torch.int32, device=dev)
+    _lib.check(lib.tq_layernorm_rows(out.data_ptr(), x.data_ptr(), rows.data_ptr(), w.data_ptr(), b.data_ptr(), eps, C,
+                                     n4.data_ptr(), 4, s), "layernorm_rows")  # fmt: skip
+    torch.testing.assert_close(out, _ln(x[rows.long()], w, b, eps), rtol=1e-5, atol=1e-5)
+
+
+def test_bias_gelu_matches_torch():
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    h = torch.randn(53, 3072, device="cuda", generator=g) * 3
+    bias = torch.randn(3072, device="cuda", generator=g)
+    want = torch.nn.functional.gelu(h + bias, approximate="tanh")
+    n = torch.tensor([53], dtype=torch.int32, device="cuda")
+    _lib.check(lib.tq_bias_gelu(h.data_ptr(), bias.data_ptr(), 3072, n.data_ptr(), 53, _stream()), "gelu")
+    torch.testing.assert_close(h, want, rtol=1e-5, atol=1e-6)
+
+
+def test_abi_rejects_bad_arguments():
+    """Validation happens on the host and returns a status; nothing launches."""
+    lib = _lib.load()
+    pool = torch.zeros(4, 1, 2, 1, 16, 64, device="cuda")
+    n = torch.tensor([1], dtype=torch.int32, device="cuda")
+    st = lib.tq_kv_write(pool.data_ptr(), 4, 1, 1, 16, 32, 0, pool.data_ptr(), 192, 64, 128, n.data_ptr(),
+                         n.data_ptr(), 1, None)  # head_dim 32: unsupported
+    assert st == _lib.TQ_ERR_UNSUPPORTED and "head_dim" in _lib.last_error()
+    st = lib.tq_kv_write(pool.data_ptr() + 4, 4, 1, 1, 16, 64, 0, pool.data_ptr(), 192, 64, 128, n.data_ptr(),
+                         n.data_ptr(), 1, None)  # misaligned pool
+    assert st == _lib.TQ_ERR_INVALID
+    st = lib.tq_bias_gelu(pool.data_ptr(), pool.data_ptr(), 6, n.data_ptr(), 1, None)
+    assert st == _lib.TQ_ERR_INVALID
+    assert _lib.device_status() == 0

@@ -1,0 +1,304 @@
+"""The paged forward on the GPU against what the reference produced.
+
+Every golden case (tests/golden) is rerun through this package's
+``paged_forward`` -- allocator, planner, kernels and fp32 linears -- and
+compared with the reference's logits (max-abs 1e-4, the north-star bound; the
+measured error is far smaller), greedy tokens (identical) and allocator state
+(bit-exact).  Random mixed batches are checked against the numpy oracle.
+"""
+
+import random
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from helpers import LOGITS_ATOL, build_config_case, cfg_of, weights_of
+from tokquay_b200 import _lib
+from tokquay_b200 import workloads as W
+from tokquay_b200.generate import paged_forward, paged_greedy_generate
+from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, cdiv
+from tokquay_b200.model import GPT2, GPT2Config
+from tokquay_b200.sequence import Sequence
+
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device"),
+]
+
+DEVICE = "cuda"
+
+
+def make_model(cfg, weights):
+    m = GPT2(cfg)
+    W.load_weights(m, weights)
+    return m.to(DEVICE).eval()
+
+
+@pytest.fixture(scope="module")
+def gpt2_model(gpt2_weights):
+    return make_model(GPT2Config(**W.GPT2_SMALL), gpt2_weights)
+
+
+def garbage_alloc(case, cls=BlockAllocator):
+    cfg = cfg_of(case)
+    a = cls(cfg, case["num_blocks"], case["block_size"], device=DEVICE)
+    W.fill_pool_blocks(a.pool, range(case["num_blocks"]), case["pool_seed"], case["pool_scale"])
+    W.shuffle_free_list(a, case["free_seed"])
+    return a
+
+
+def max_err(got, want):
+    return float(np.abs(np.asarray(got, dtype=np.float64) - np.asarray(want, dtype=np.float64)).max())
+
+
+def test_mini_decode_across_block_boundaries(golden):
+    """tests/test_phase3_paged.py:87-106, fp32: every step's logits vs the
+    reference's fp32 and float64 runs."""
+    case = golden.cases["mini_decode"]
+    m = make_model(cfg_of(case), weights_of(case))
+    a = garbage_alloc(case)
+    ids = case["ids"]
+    s = Sequence(0, ids[:case["prefill"]])
+    a.allocate(s)
+    got = [paged_forward(m, a, [s])[0]]
+    for t in range(case["prefill"], len(ids)):
+        s.append_token(ids[t])
+        a.append_slot(s)
+        got.append(paged_forward(m, a, [s])[0])
+    got = torch.stack(got).cpu().numpy()
+    assert s.block_table == case["block_table"] and a._free == case["free_after"]
+    assert max_err(got, golden.arrays["mini_decode/logits_f32"]) < LOGITS_ATOL
+    assert max_err(got, golden.arrays["mini_decode/logits_f64"]) < LOGITS_ATOL
+    assert s.num_cached_tokens == len(ids) and len(s.block_table) == cdiv(len(ids), 4)
+
+
+def test_mini_batch8_matches_reference_and_each_alone(golden):
+    """tests/test_phase3_paged.py:109-129: 8 prompts decoded together give the
+    reference's tokens (which equal each prompt decoded alone), and no block
+    outside those handed out is written."""
+    case = golden.cases["mini_batch8"]
+    m = make_model(cfg_of(case), weights_of(case))
+    taken: set[int] = set()
+
+    class Recording(BlockAllocator):
+        def _take(self, n):
+            blocks = super()._take(n)
+            taken.update(blocks)
+            return blocks
+
+    a = garbage_alloc(case, Recording)
+    before = a.pool.clone()
+    tokens = paged_greedy_generate(m, a, case["prompts"], case["n_new"])
+    assert tokens == case["tokens"] == case["alone"]
+    assert a.num_free_blocks == a.num_blocks and a._free == case["free_after"]
+    changed = {b for b in range(a.num_blocks) if not torch.equal(a.pool[b], before[b])}
+    assert changed == set(case["changed_blocks"]) and changed <= taken
+    assert taken != set(range(a.num_blocks))
+
+
+def test_mini_batch8_step_logits(golden):
+    case = golden.cases["mini_batch8"]
+    m = make_model(cfg_of(case), weights_of(case))
+    a = garbage_alloc(case)
+    seqs = [Sequence(i, list(p)) for i, p in enumerate(case["prompts"])]
+    for s in seqs:
+        a.allocate(s)
+    ref, row, running, worst = golden.arrays["mini_batch8/logits"], 0, seqs, 0.0
+    for step in case["steps"]:
+        assert [s.block_table for s in running] == step["tables"]
+        logits = paged_forward(m, a, running).cpu().numpy()
+        worst = max(worst, max_err(logits, ref[row:row + len(running)]))
+        row += len(running)
+        still = []
+        for s, t in zip(running, step["next"]):
+            s.append_token(t)
+            if len(s.output_token_ids) >= case["n_new"]:
+                a.free(s)
+            else:
+                a.append_slot(s)
+                still.append(s)
+        running = still
+    assert worst < LOGITS_ATOL
+
+
+def test_mini_mixed_prefill_and_decode(golden):
+    """tests/test_phase3_paged.py:143-164 in fp32."""
+    case = golden.cases["mini_mixed"]
+    m = make_model(cfg_of(case), weights_of(case))
+    a = garbage_alloc(case)
+    sa = Sequence(0, case["a_ids"][:-1])
+    a.allocate(sa)
+    paged_forward(m, a, [sa])
+    sa.append_token(case["a_ids"][-1])
+    a.append_slot(sa)
+    sb = Sequence(1, case["b_ids"])
+    a.allocate(sb)
+    assert [sa.block_table, sb.block_table] == case["tables_f32"]
+    logits = paged_forward(m, a, [sa, sb]).cpu().numpy()
+    assert max_err(logits, golden.arrays["mini_mixed/logits_f32"]) < LOGITS_ATOL
+    assert max_err(logits[0], golden.arrays["mini_mixed/full_a_f64"]) < LOGITS_ATOL
+    assert max_err(logits[1], golden.arrays["mini_mixed/full_b_f64"]) < LOGITS_ATOL
+
+
+def _check_cols(logits, golden, key_prefix, stride):
+    cols = golden.arrays[f"{key_prefix}cols"]
+    err = max_err(logits[:, ::stride], cols)
+    assert err < LOGITS_ATOL, err
+    top2 = golden.arrays[f"{key_prefix}top2"]
+    gap = top2[:, 0] - top2[:, 1]
+    am = logits.argmax(-1)
+    ref_am = golden.arrays[f"{key_prefix}argmax"]
+    # Greedy tokens identical, except where the reference's own top-2 gap is
+    # below the measured logit error (a legitimate fp32 near-tie).
+    bad = (am != ref_am) & (gap > 2 * err)
+    assert not bad.any(), np.nonzero(bad)
+    return err
+
+
+def test_config1_decode_step(golden, gpt2_model):
+    case = golden.cases["cfg1"]
+    cfg = gpt2_model.cfg
+    a = BlockAllocator(cfg, case["num_blocks"], case["block_size"], device=DEVICE)
+    seqs, _ = build_config_case("cfg1", golden, alloc=a)
+    assert [s.block_table for s in seqs] == case["tables"]
+    W.fill_pool_blocks(a.pool, {b for s in seqs for b in s.block_table}, case["seed"])
+    logits = paged_forward(gpt2_model, a, seqs).cpu().numpy()
+    _check_cols(logits, golden, "cfg1/", case["logit_stride"])
+    assert a._free == case["free_after"]
+    bs = case["block_size"]
+    kv = torch.stack([a.pool[s.block_table[(c - 1) // bs], [0, 11], :, :, (c - 1) % bs]
+                      for s, c in zip(seqs, case["ctx"])]).cpu().numpy()  # fmt: skip
+    assert max_err(kv, golden.arrays["cfg1/written_kv"]) < 1e-5
+
+
+@pytest.mark.parametrize("bs", [16, 32])
+def test_config3_mixed_step(golden, gpt2_model, bs):
+    name = f"cfg3_bs{bs}"
+    case = golden.cases[name]
+    a = BlockAllocator(gpt2_model.cfg, case["num_blocks"], bs, device=DEVICE)
+    seqs, new_lens = build_config_case(name, golden, alloc=a)
+    assert [s.block_table for s in seqs] == case["tables"] and new_lens == case["new_lens"]
+    W.fill_pool_blocks(a.pool, {b for s in seqs for b in s.block_table}, case["seed"])
+    logits = paged_forward(gpt2_model, a, seqs, new_lens).cpu().numpy()
+    _check_cols(logits, golden, f"{name}/", case["logit_stride"])
+
+
+def test_config2_greedy_steps(golden, gpt2_model):
+    case = golden.cases["cfg2"]
+    a = BlockAllocator(gpt2_model.cfg, case["num_blocks"], case["block_size"], device=DEVICE)
+    seqs, _ = build_config_case("cfg2", golden, alloc=a)
+    W.fill_pool_blocks(a.pool, {b for s in seqs for b in s.block_table}, case["seed"])
+    for k, step in enumerate(case["steps"]):
+        assert [s.block_table for s in seqs] == step["tables"]
+        logits = paged_forward(gpt2_model, a, seqs).cpu().numpy()
+        _check_cols(logits, golden, f"cfg2/step{k}_", case["logit_stride"])
+        for s, t in zip(seqs, step["next"]):
+            s.append_token(t)
+            a.append_slot(s)
+    assert a._free == case["free_after"]
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_random_mixed_batches_match_the_oracle(seed):
+    """Mixed prefill (with cached prefixes) + decode batches on a small model
+    with LayerNorm-1 init: every row's logits vs the numpy oracle."""
+    rng = random.Random(seed)
+    cfg = GPT2Config(**W.MINI)
+    w = W.random_weights(cfg, 100 + seed, "gpt2")
+    m = make_model(cfg, w)
+    bs = [4, 8, 16, 32][seed]
+    a = BlockAllocator(cfg, 256, bs, device=DEVICE)
+    W.shuffle_free_list(a, seed)
+    pool_np = np.zeros(tuple(a.pool.shape), np.float32)
+    W.fill_pool_blocks(pool_np, range(256), 50 + seed, 3.0)
+    a.pool.copy_(torch.from_numpy(pool_np))
+    seqs, lens = [], []
+    for i in range(rng.randint(3, 9)):
+        total = rng.randint(2, 120)
+        s = Sequence(i, [rng.randrange(cfg.vocab_size) for _ in range(total)])
+        a.allocate(s)
+        s.num_cached_tokens = rng.randint(0, total - 1)
+        seqs.append(s)
+        lens.append(rng.randint(1, total - s.num_cached_tokens))
+    clones = [Sequence(s.seq_id, list(s.prompt_token_ids), block_table=list(s.block_table),
+                       num_cached_tokens=s.num_cached_tokens) for s in seqs]  # fmt: skip
+    got = paged_forward(m, a, seqs, lens).cpu().numpy()
+    want = oracle.paged_forward(w, cfg, pool_np, bs, clones, lens)
+    assert max_err(got, want) < 1e-5
+    # The K/V the step wrote equal the oracle's scatter (same values up to fp32 GEMM rounding).
+    np.testing.assert_allclose(a.pool.cpu().numpy(), pool_np, atol=1e-5, rtol=0)
+
+
+def test_forward_with_padded_input_ids_matches_paged_forward(gpt2_model):
+    """The reference-shaped entry point GPT2.forward(input_ids [B, T], batch)."""
+    cfg = gpt2_model.cfg
+    a = BlockAllocator(cfg, 64, 16, device=DEVICE)
+    rng = random.Random(0)
+    seqs = [Sequence(i, [rng.randrange(cfg.vocab_size) for _ in range(n)]) for i, n in enumerate([5, 17, 33])]
+    for s in seqs:
+        a.allocate(s)
+    a.pool.normal_()
+    batch = a.batch_for(seqs)
+    T = batch.T
+    ids = torch.tensor([s.prompt_token_ids + [0] * (T - len(s.prompt_token_ids)) for s in seqs], device=DEVICE)
+    full = gpt2_model(ids, batch, last_only=False)
+    last = gpt2_model.forward_paged(a.batch_for(seqs), last_only=True)[:, 0]
+    for b, s in enumerate(seqs):
+        torch.testing.assert_close(full[b, len(s.prompt_token_ids) - 1], last[b], atol=1e-5, rtol=0)
+    with pytest.raises(ValueError):
+        gpt2_model(ids[:, :-1], batch)
+
+
+def test_padding_positions_beyond_n_positions_are_safe(gpt2_model):
+    """tests/test_phase3_paged.py:167-182: a short sequence next to one ending
+    at position 1022 runs; a sequence longer than n_positions is rejected."""
+    cfg = gpt2_model.cfg
+    a = BlockAllocator(cfg, cdiv(1024, 16) + 4, 16, device=DEVICE)
+    long_seq, short = Sequence(0, [1] * 1023), Sequence(1, [2, 3])
+    a.allocate(long_seq)
+    a.allocate(short)
+    out = paged_forward(gpt2_model, a, [long_seq, short])
+    assert torch.isfinite(out).all()
+    a.free(long_seq)
+    a.free(short)
+    too_long = Sequence(2, [1] * 1025)
+    a.allocate(too_long)
+    with pytest.raises(ValueError):
+        paged_forward(gpt2_model, a, [too_long])
+
+
+def test_batch_rejects_block_tables_that_are_too_short(gpt2_model):
+    """tests/test_phase3_paged.py:185-190."""
+    a = BlockAllocator(gpt2_model.cfg, 8, 4, device=DEVICE)
+    s = Sequence(0, [1] * 9)
+    a.allocate(s, num_tokens=4)
+    with pytest.raises(ValueError):
+        paged_forward(gpt2_model, a, [s])
+
+
+def test_attend_hook_matches_dense_reference_math():
+    """DevicePagedBatch.attend(layer, q, k, v): the drop-in for the reference
+    model's paged branch, on padded [B, H, T, d] tensors."""
+    cfg = GPT2Config(vocab_size=64, n_positions=256, n_embd=128, n_layer=2, n_head=2)
+    a = BlockAllocator(cfg, 40, 4, device=DEVICE)
+    a.pool.normal_()
+    seqs = [Sequence(0, [1] * 9), Sequence(1, [1] * 3)]
+    for s in seqs:
+        a.allocate(s)
+    seqs[0].num_cached_tokens = 8  # decode 1; seq 1 prefills 3
+    batch = a.batch_for(seqs)
+    B, H, T, d = 2, 2, batch.T, 64
+    q, k, v = (torch.randn(B, H, T, d, device=DEVICE) for _ in range(3))
+    out = batch.attend(1, q, k, v)
+    kd, vd = batch.gather(1)
+    sc = (q @ kd.transpose(-2, -1)) / 8.0
+    sc = sc.masked_fill(~batch.mask, float("-inf"))
+    want = torch.softmax(sc, -1) @ vd
+    for b, n in enumerate([1, 3]):
+        torch.testing.assert_close(out[b, :, :n], want[b, :, :n], atol=1e-5, rtol=1e-5)
+
+
+def test_no_device_errors_were_flagged():
+    assert _lib.device_status() == 0

@@ -345,6 +345,7 @@ class DevicePagedBatch(BatchedKV):
             slot, host = ring.take(total)
             host[:total].copy_(torch.from_numpy(plan[:total]))
         self.layout = layout
+        self.h2d_bytes = 4 * total  # the one host->device copy this step makes
         dev = torch.empty(total, dtype=torch.int32, device=device)
         with torch.cuda.stream(stream):
             dev.copy_(host[:total], non_blocking=True)

@@ -70,6 +70,13 @@ def _tf32_off() -> bool:
 class GPT2(nn.Module):
     def __init__(self, cfg: GPT2Config | None = None):
         super().__init__()
+        # Optional measurement hooks: when ``attention_events`` is a list, every
+        # attention launch appends a (start, end) CUDA-event pair recorded on the
+        # launching stream; ``kernel_launches`` counts this package's kernel
+        # launches (GEMMs and other torch ops are not counted).
+        self.attention_events: list | None = None
+        self.kernel_launches = 0
+        self.last_h2d_bytes = 0  # plan bytes the last forward's batch copied to the device
         self.cfg = cfg or GPT2Config()
         self.wte = nn.Embedding(self.cfg.vocab_size, self.cfg.n_embd)
         self.wpe = nn.Embedding(self.cfg.n_positions, self.cfg.n_embd)
@@ -111,6 +118,7 @@ class GPT2(nn.Module):
         lib = _lib.load()
         dev = batch.pool.device
         stream = torch.cuda.current_stream(dev).cuda_stream
+        self.last_h2d_bytes = batch.h2d_bytes
         C, eps, N, B = cfg.n_embd, cfg.layer_norm_eps, batch.N, batch.B
         n_ptr, b_ptr = batch.count_ptr(0), batch.count_ptr(3)
         x = torch.empty(N, C, dtype=torch.float32, device=dev)
@@ -128,7 +136,14 @@ class GPT2(nn.Module):
             qkv = torch.addmm(att.c_attn.bias, xa, att.c_attn.weight.t())  # [N, 3C]
             batch.write_rows(i, qkv, C, 2 * C, stream)
             a = torch.empty(N, C, dtype=torch.float32, device=dev)
-            batch.attend_rows(i, qkv, a, stream)
+            if self.attention_events is not None:
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ev0.record()
+                batch.attend_rows(i, qkv, a, stream)
+                ev1.record()
+                self.attention_events.append((ev0, ev1))
+            else:
+                batch.attend_rows(i, qkv, a, stream)
             if last and last_only and N != B:
                 # Only the last row of each sequence is sampled from (model.py:179).
                 sel = batch.last_rows
@@ -151,6 +166,8 @@ class GPT2(nn.Module):
                 nxt.bias.data_ptr() if nxt is not None else None, eps, C, rows_ptr, rows, stream),
                 "tq_bias_residual_layernorm")  # fmt: skip
 
+        # embed + per layer (kv_write, attention [+ combine], 2x bias_residual, gelu) + final LN
+        self.kernel_launches += 2 + cfg.n_layer * (5 + (1 if batch.num_combine else 0))
         if last_only:
             xf = torch.empty(B, C, dtype=torch.float32, device=dev)
             sel_ptr = None if rows == B else batch.last_rows.data_ptr()
