@@ -46,7 +46,7 @@
 extern "C" {
 #endif
 
-#define TQ_ABI_VERSION 1
+#define TQ_ABI_VERSION 3
 
 enum tq_status {
   TQ_OK = 0,
@@ -82,6 +82,10 @@ enum tq_plan_layout {
 
 TQ_API int tq_abi_version(void);
 
+/* Keys per attention chunk of this build (the split-K granularity of
+ * tq_plan_step work items: TQ_PLAN_SPLIT_CHUNKS counts these). */
+TQ_API int tq_attention_chunk_keys(void);
+
 /* Message for the last nonzero status returned on this thread. */
 TQ_API const char* tq_last_error(void);
 
@@ -102,14 +106,20 @@ TQ_API int tq_device_status(int clear, int32_t* bits);
  * token_ids (host, [N], may be NULL) are copied into the plan.
  * target_units: attention (item, head) units to aim for when choosing the
  * split-K size; min_split_chunks: smallest split, in 32-key chunks.
+ * caps (host, may be NULL): fixed capacities {max_seqs, max_tokens,
+ * table_stride, max_items, max_combine, max_partials}.  With caps every region
+ * has its capacity's size, so the layout (and the table stride) is the same
+ * for every step that fits -- the form a captured CUDA graph needs -- and the
+ * split is coarsened until items and partials fit; a step that still does not
+ * fit returns TQ_ERR_CAPACITY.  Without caps the plan is packed to this step.
  * Returns TQ_ERR_CAPACITY (layout[TQ_PLAN_TOTAL_INTS] = ints needed) if
  * out_capacity is too small. */
 TQ_API int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_t* q_len,
                  const int32_t* table_offsets, const int32_t* table_data,
                  const int32_t* token_ids, int32_t block_size, int64_t num_blocks,
                  int32_t n_head, int32_t vocab_size, int32_t target_units,
-                 int32_t min_split_chunks, int32_t* out, int64_t out_capacity,
-                 int32_t* layout);
+                 int32_t min_split_chunks, const int32_t* caps, int32_t* out,
+                 int64_t out_capacity, int32_t* layout);
 
 /* KV write (replaces PagedBatch.write, tokquay/kv_cache.py:228-232).
  * For each of the *d_num_tokens new tokens n: pool[slot/bs][layer][0][h][slot%bs][:]
@@ -127,20 +137,21 @@ TQ_API int tq_kv_write(float* pool, int64_t num_blocks, int32_t n_layer, int32_t
  * Row r of the plan (a new token at position p of sequence b) attends to the
  * keys at positions 0..p of sequence b:
  *   out[r*out_row_stride + h*64 + i] = softmax_j(q_r.k_j * scale) v_j[i].
- * q rows: q[r*q_row_stride + h*64 ...].  work_items / combine_list /
- * block_tables come from tq_plan_step.  partial_ml ([P][2] floats) and
- * partial_acc ([P][64] floats), P = TQ_PLAN_NUM_PARTIALS, are caller-owned
- * split-K scratch (may be NULL when P == 0).  max_items / max_combine size
- * the grids.  Launches the attention kernel and, if max_combine > 0, the
- * combine kernel, on `stream`. */
+ * q rows: q[r*q_row_stride + h*64 ...]; q, out 16-byte aligned rows.
+ * work_items / block_tables come from tq_plan_step.  Split-K scratch is the
+ * caller's: partial_ml ([P][2] floats), partial_acc ([P][64] floats) and
+ * partial_counters ([P] int32, all zero before the first launch; every launch
+ * that completes leaves them zero again), P >= TQ_PLAN_NUM_PARTIALS of every
+ * plan launched with it (max_partials; NULL scratch is fine when it is 0).
+ * Launches that share scratch must not overlap on the GPU.  max_items sizes
+ * the grid.  One kernel launch on `stream`; the split-K merge is fused. */
 TQ_API int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64_t q_row_stride,
                        const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
                        int32_t block_size, int32_t head_dim, int32_t layer,
                        const int32_t* block_tables, int32_t table_stride,
                        const int32_t* work_items, const int32_t* d_num_items, int32_t max_items,
-                       float* partial_ml, float* partial_acc, const int32_t* combine_list,
-                       const int32_t* d_num_combine, int32_t max_combine, float scale,
-                       void* stream);
+                       float* partial_ml, float* partial_acc, int32_t* partial_counters,
+                       int32_t max_partials, float scale, void* stream);
 
 /* x[r] = wte[ids[r]] + wpe[pos[r]];  xa[r] = LayerNorm(x[r]; ln_w, ln_b, eps).
  * n_embd must be a multiple of 128 and at most 1024. */

@@ -302,3 +302,97 @@ def test_attend_hook_matches_dense_reference_math():
 
 def test_no_device_errors_were_flagged():
     assert _lib.device_status() == 0
+
+
+def _twin_allocators(cfg, num_blocks, bs, seed):
+    pool = torch.randn(num_blocks, cfg.n_layer, 2, cfg.n_head, bs, cfg.d_head,
+                       generator=torch.Generator().manual_seed(seed))  # fmt: skip
+    allocs = []
+    for _ in range(2):
+        a = BlockAllocator(cfg, num_blocks, bs, device=DEVICE)
+        a.pool.copy_(pool)
+        W.shuffle_free_list(a, seed)
+        allocs.append(a)
+    return allocs
+
+
+def test_cuda_graph_decode_matches_eager_across_buckets():
+    """Decode steps replayed from captured graphs (batch sizes below, at and
+    across bucket sizes) give the eager path's logits, tokens and pool writes."""
+    cfg = GPT2Config(**W.MINI)
+    m = make_model(cfg, W.random_weights(cfg, 7, "gpt2"))
+    ag, ae = _twin_allocators(cfg, 200, 16, 0)
+    m.use_cuda_graphs(ag, buckets=(4, 8))
+    rng = random.Random(0)
+    prompts = [[rng.randrange(cfg.vocab_size) for _ in range(rng.randint(3, 60))] for _ in range(7)]
+    sg = [Sequence(i, list(p)) for i, p in enumerate(prompts)]
+    se = [Sequence(i, list(p)) for i, p in enumerate(prompts)]
+    for s1, s2 in zip(sg, se):
+        ag.allocate(s1)
+        ae.allocate(s2)
+        s1.num_cached_tokens = s2.num_cached_tokens = len(s1.prompt_token_ids) - 1
+    worst = 0.0
+    for step, n in enumerate([7, 7, 5, 3, 4, 8 - 1, 2]):
+        g = paged_forward(m, ag, sg[:n])  # graph path (bucket 4 or 8)
+        e = m.forward_paged(ae.batch_for(se[:n]), last_only=True)[:, 0]
+        for s in se[:n]:
+            s.num_cached_tokens += 1
+        worst = max(worst, (g - e).abs().max().item())
+        nxt = e.argmax(-1).tolist()
+        assert g.argmax(-1).tolist() == nxt
+        for s1, s2, t in zip(sg[:n], se[:n], nxt):
+            s1.append_token(t)
+            s2.append_token(t)
+            ag.append_slot(s1)
+            ae.append_slot(s2)
+        for s1, s2 in zip(sg[n:], se[n:]):  # sequences outside this step keep their state
+            assert s1.num_cached_tokens == s2.num_cached_tokens
+    assert worst < 1e-5
+    assert sorted(m.graph_runner._graphs) == [4, 8]
+    torch.testing.assert_close(ag.pool, ae.pool, atol=1e-5, rtol=0)
+    assert _lib.device_status() == 0
+
+
+def test_graph_replay_from_device_resident_plans():
+    """replay_plan: plans prepared in HBM beforehand, token ids fed from the
+    previous replay's argmax on the device (the bench's device-resident loop)."""
+    from tokquay_b200.kv_cache import plan_step_host
+
+    cfg = GPT2Config(**W.MINI)
+    m = make_model(cfg, W.random_weights(cfg, 8, "gpt2"))
+    ag, ae = _twin_allocators(cfg, 100, 8, 1)
+    runner = m.use_cuda_graphs(ag, buckets=(4,))
+    caps = runner.graph(4)[1].caps
+    rng = random.Random(1)
+    seqs = [Sequence(i, [rng.randrange(cfg.vocab_size) for _ in range(rng.randint(2, 30))]) for i in range(4)]
+    twins = [Sequence(s.seq_id, list(s.prompt_token_ids)) for s in seqs]
+    for s, t in zip(seqs, twins):
+        ag.allocate(s)
+        ae.allocate(t)
+        s.num_cached_tokens = t.num_cached_tokens = s.num_tokens - 1
+    plans = []
+    for k in range(5):
+        st = [s.num_cached_tokens for s in seqs]
+        ids = [s.tokens_slice(x, x + 1)[0] for s, x in zip(seqs, st)]
+        plan, _ = plan_step_host(8, 100, cfg.n_head, [list(s.block_table) for s in seqs], st, [1] * 4, ids,
+                                 cfg.vocab_size, 100, 2, caps=caps)  # fmt: skip
+        plans.append(torch.from_numpy(plan.copy()).to(DEVICE))
+        for s in seqs:
+            s.num_cached_tokens += 1
+            s.append_token(0)
+            ag.append_slot(s)
+    prev = None
+    got = []
+    for k in range(5):
+        prev = runner.replay_plan(4, plans[k], ids=None if prev is None else prev[:4])
+        got.append(prev[:4].tolist())
+    want = []
+    for k in range(5):
+        logits = m.forward_paged(ae.batch_for(twins), last_only=True)[:, 0]
+        nxt = logits.argmax(-1).tolist()
+        want.append(nxt)
+        for t, x in zip(twins, nxt):
+            t.num_cached_tokens += 1
+            t.append_token(x)
+            ae.append_slot(t)
+    assert got == want

@@ -41,7 +41,8 @@ def test_abi_version_and_error_channel():
     assert lib.tq_abi_version() == int(m.group(1)) == _lib.EXPECTED_ABI
     # A host-only call that fails sets the thread's message.
     layout = (ctypes.c_int32 * _lib.PLAN_LAYOUT_LEN)()
-    st = lib.tq_plan_step(0, None, None, None, None, None, 16, 8, 1, 0, 1, 1, None, 0, ctypes.addressof(layout))
+    st = lib.tq_plan_step(0, None, None, None, None, None, 16, 8, 1, 0, 1, 1, None, None, 0,
+                          ctypes.addressof(layout))
     assert st == _lib.TQ_ERR_INVALID
     assert "non-empty" in _lib.last_error()
 

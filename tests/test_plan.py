@@ -15,11 +15,11 @@ import pytest
 
 import oracle
 from tokquay_b200 import _lib
-from tokquay_b200.kv_cache import ATTN_CHUNK, MIN_SPLIT_CHUNKS, cdiv, plan_step_host
+from tokquay_b200.kv_cache import MIN_SPLIT_CHUNKS, attention_chunk_keys, cdiv, plan_step_host
 
 N_HEAD = 3
 KMAX_ROWS = 4
-STAGE_ROWS = 32  # K (or V) rows one stage holds
+# K (or V) rows one stage holds: the library's chunk size (checked in simulate_copies)
 
 
 def unpack(plan, layout):
@@ -65,6 +65,7 @@ def simulate_copies(p, bs, num_blocks, n_head):
     """Replay issue_chunk's arithmetic for every (item, head, chunk): every
     copy's source block must be a planned table entry of the sequence and
     every destination inside the stage.  Returns {(row, head): sorted keys}."""
+    ATTN_CHUNK = attention_chunk_keys()
     seen: dict[tuple[int, int], list[int]] = {}
     items = p["items"]
     for it in items:
@@ -87,7 +88,7 @@ def simulate_copies(p, bs, num_blocks, n_head):
                     assert 0 <= blk < num_blocks
                     rows = min(bs, key0 + nkeys - kb * bs)
                     dst = kb * bs - key0
-                    assert 0 <= dst and dst + rows <= STAGE_ROWS
+                    assert 0 <= dst and dst + rows <= ATTN_CHUNK
                     kb += 1
             else:
                 kb = key0 // bs
@@ -182,3 +183,33 @@ def test_capacity_retry_and_in_place_buffer():
     plan2, layout2 = plan_step_host(4, 8, 2, tables, [5, 0], [4, 2], None, 0, 10, 1, out=big)
     assert plan2 is big
     np.testing.assert_array_equal(big[:plan.size], plan)
+
+
+def test_fixed_capacity_layout_is_step_independent():
+    """With caps, every step that fits gets the same offsets and table stride
+    (what a captured CUDA graph needs), and the data matches the packed plan."""
+    caps = np.array([8, 8, 40, 8 * 16, 8, 8 * 3 * 16], dtype=np.int32)
+    rng = random.Random(0)
+    layouts = []
+    for _ in range(5):
+        B = rng.randint(1, 8)
+        tables = [list(range(i * 40, i * 40 + rng.randint(1, 40))) for i in range(B)]
+        start = [rng.randint(0, len(t) * 16 - 1) for t in tables]
+        new = [1] * B
+        plan, layout = plan_step_host(16, 8 * 40, 3, tables, start, new, None, 0, 500, 2, caps=caps)
+        packed, playout = plan_step_host(16, 8 * 40, 3, tables, start, new, None, 0, 500, 2)
+        p, q = unpack(plan, layout), unpack(packed, playout)
+        np.testing.assert_array_equal(p["slots"][:q["N"]], q["slots"])
+        np.testing.assert_array_equal(p["counts"], q["counts"])
+        layouts.append(tuple(int(layout[k]) for k in range(_lib.PLAN_TABLE_STRIDE, _lib.PLAN_LAYOUT_LEN)
+                             if k not in (_lib.PLAN_MAX_CTX, _lib.PLAN_SPLIT_CHUNKS)))
+    assert len(set(layouts)) == 1
+    with pytest.raises(RuntimeError, match="capacities"):
+        plan_step_host(16, 8 * 40, 3, [[0]] * 9, [0] * 9, [1] * 9, None, 0, 500, 2, caps=caps)
+
+
+def test_fixed_capacity_coarsens_the_split_to_fit():
+    caps = np.array([4, 4, 64, 4, 4, 4 * 12 * 2], dtype=np.int32)  # room for 1 item per seq
+    tables = [list(range(i * 64, (i + 1) * 64)) for i in range(4)]
+    plan, layout = plan_step_host(16, 256, 12, tables, [1000] * 4, [1] * 4, None, 0, 10_000, 2, caps=caps)
+    assert layout[_lib.PLAN_NUM_ITEMS] <= 4 and layout[_lib.PLAN_NUM_PARTIALS] <= caps[5]

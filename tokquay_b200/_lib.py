@@ -46,15 +46,16 @@ PLAN_LAYOUT_LEN = 18
 _P = c_void_p
 SIGNATURES: dict[str, tuple] = {
     "tq_abi_version": (c_int, []),
+    "tq_attention_chunk_keys": (c_int, []),
     "tq_last_error": (ctypes.c_char_p, []),
     "tq_device_status": (c_int, [c_int, POINTER(c_int32)]),
     "tq_plan_step": (c_int, [c_int32, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32,
-                             c_int32, c_int32, _P, c_int64, _P]),
+                             c_int32, c_int32, _P, _P, c_int64, _P]),
     "tq_kv_write": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32, _P, c_int64,
                             c_int64, c_int64, _P, _P, c_int32, _P]),
     "tq_paged_attention": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32,
-                                   c_int32, c_int32, _P, c_int32, _P, _P, c_int32, _P, _P, _P, _P,
-                                   c_int32, c_float, _P]),
+                                   c_int32, c_int32, _P, c_int32, _P, _P, c_int32, _P, _P, _P, c_int32,
+                                   c_float, _P]),
     "tq_embed_layernorm": (c_int, [_P, _P, _P, _P, _P, _P, c_int32, c_int32, _P, _P, c_float,
                                    c_int32, _P, c_int32, _P]),
     "tq_bias_residual_layernorm": (c_int, [_P, _P, _P, _P, _P, _P, c_float, c_int32, _P, c_int32, _P]),
@@ -62,7 +63,7 @@ SIGNATURES: dict[str, tuple] = {
     "tq_bias_gelu": (c_int, [_P, _P, c_int32, _P, c_int32, _P]),
 }
 
-EXPECTED_ABI = 1
+EXPECTED_ABI = 3
 
 _lib: ctypes.CDLL | None = None
 _lock = threading.Lock()
@@ -80,7 +81,7 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     with _lock:
         if _lib is not None:
             return _lib
-        p = Path(path) if path else LIB_PATH
+        p = Path(path or os.environ.get("TOKQUAY_B200_LIB") or LIB_PATH)
         if not p.exists():
             raise NativeLibraryMissing(
                 f"{p} is missing: build it with `python -m tokquay_b200.build` (needs nvcc); "

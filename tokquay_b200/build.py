@@ -59,11 +59,15 @@ def is_stale() -> bool:
     return any(p.stat().st_mtime > built for p in _inputs())
 
 
-def build_library(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
-    """Compile the library if it is missing or older than a source; return its path."""
-    if not force and not is_stale():
+def build_library(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None,
+                  out: Path | None = None) -> Path:  # fmt: skip
+    """Compile the library if it is missing or older than a source; return its path.
+    ``out`` builds a variant elsewhere (e.g. with ``-DTQ_ATTN_STAGES=2`` in
+    ``extra_flags``) without touching the in-tree library."""
+    target = Path(out) if out else LIB_PATH
+    if out is None and not force and not is_stale():
         return LIB_PATH
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = target.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, *(extra_flags or []), f"-I{INCLUDE}",
            *map(str, sources()), "-o", str(tmp)]  # fmt: skip
     if verbose:
@@ -73,8 +77,8 @@ def build_library(force: bool = False, verbose: bool = False, extra_flags: list[
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     if verbose and (res.stdout or res.stderr):
         print(res.stdout + res.stderr, file=sys.stderr)
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, target)
+    return target
 
 
 def main() -> None:

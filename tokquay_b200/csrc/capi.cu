@@ -130,6 +130,8 @@ extern "C" {
 
 int tq_abi_version(void) { return TQ_ABI_VERSION; }
 
+int tq_attention_chunk_keys(void) { return kChunk; }
+
 const char* tq_last_error(void) { return error_buffer(); }
 
 int tq_device_status(int clear, int32_t* bits) {
@@ -186,31 +188,29 @@ int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64
                        int32_t block_size, int32_t head_dim, int32_t layer,
                        const int32_t* block_tables, int32_t table_stride,
                        const int32_t* work_items, const int32_t* d_num_items, int32_t max_items,
-                       float* partial_ml, float* partial_acc, const int32_t* combine_list,
-                       const int32_t* d_num_combine, int32_t max_combine, float scale,
-                       void* stream) {
+                       float* partial_ml, float* partial_acc, int32_t* partial_counters,
+                       int32_t max_partials, float scale, void* stream) {
   int st = check_pool(pool, num_blocks, n_layer, n_head, block_size, head_dim, layer);
   if (st) return st;
-  if (max_items < 0 || max_combine < 0) return set_error(TQ_ERR_INVALID, "negative capacity");
+  if (max_items < 0 || max_partials < 0) return set_error(TQ_ERR_INVALID, "negative capacity");
   if (max_items == 0) return TQ_OK;
   if (!out || !q || !block_tables || !work_items || !d_num_items)
     return set_error(TQ_ERR_INVALID, "out, q, block_tables and work items must not be NULL");
   if (!aligned(q, 16) || q_row_stride % 4)
     return set_error(TQ_ERR_INVALID, "q rows must be 16-byte aligned");
-  if (!aligned(out, 8) || out_row_stride % 2)
-    return set_error(TQ_ERR_INVALID, "out rows must be 8-byte aligned");
+  if (!aligned(out, 16) || out_row_stride % 4)
+    return set_error(TQ_ERR_INVALID, "out rows must be 16-byte aligned");
   if (!aligned(work_items, 16)) return set_error(TQ_ERR_INVALID, "work items must be 16-byte aligned");
-  if (max_combine > 0) {
-    if (!partial_ml || !partial_acc || !combine_list || !d_num_combine)
-      return set_error(TQ_ERR_INVALID, "split-K scratch and combine list must not be NULL");
-    if (!aligned(partial_acc, 8) || !aligned(partial_ml, 8) || !aligned(combine_list, 16))
+  if (max_partials > 0) {
+    if (!partial_ml || !partial_acc || !partial_counters)
+      return set_error(TQ_ERR_INVALID, "split-K scratch must not be NULL");
+    if (!aligned(partial_acc, 16) || !aligned(partial_ml, 8) || !aligned(partial_counters, 4))
       return set_error(TQ_ERR_INVALID, "split-K scratch misaligned");
   }
   if (table_stride < 0) return set_error(TQ_ERR_INVALID, "table_stride must be >= 0");
   if (!(scale > 0.f) || !std::isfinite(scale)) return set_error(TQ_ERR_INVALID, "bad scale");
   int sms = 0;
   if ((st = device_setup(&sms))) return st;
-  const cudaStream_t s = (cudaStream_t)stream;
 
   AttnParams p;
   p.out = out;
@@ -230,25 +230,12 @@ int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64
   p.n_items = d_num_items;
   p.part_ml = partial_ml;
   p.part_acc = partial_acc;
+  p.part_cnt = partial_counters;
   p.scale_log2 = scale * 1.4426950408889634f;
   const int64_t units = (int64_t)max_items * n_head;
   const int grid = (int)std::min<int64_t>((units + kAttnWarps - 1) / kAttnWarps, sms);
-  paged_attention_kernel<<<grid, kAttnWarps * 32, kAttnSmemBytes, s>>>(p);
-  if ((st = check_launch("paged_attention"))) return st;
-
-  if (max_combine > 0) {
-    CombineParams c;
-    c.out = out;
-    c.out_stride = out_row_stride;
-    c.part_ml = partial_ml;
-    c.part_acc = partial_acc;
-    c.entries = reinterpret_cast<const int4*>(combine_list);
-    c.n_entries = d_num_combine;
-    c.n_head = n_head;
-    attn_combine_kernel<<<warp_grid((int64_t)max_combine * n_head, sms), 256, 0, s>>>(c);
-    if ((st = check_launch("attn_combine"))) return st;
-  }
-  return TQ_OK;
+  paged_attention_kernel<<<grid, kAttnWarps * 32, kAttnSmemBytes, (cudaStream_t)stream>>>(p);
+  return check_launch("paged_attention");
 }
 
 int tq_embed_layernorm(float* x, float* xa, const int32_t* ids, const int32_t* pos,

@@ -1,5 +1,5 @@
 // Paged attention over the Tokquay block pool, decode and causal prefill rows
-// in one launch, plus the split-K combine.
+// in one launch, split-K merge included.
 //
 // Replaces the dense gather + masked softmax of the reference
 // (tokquay/kv_cache.py:234-242 and tokquay/model.py:94-96): K/V blocks are
@@ -18,31 +18,50 @@
 // of kStages shared-memory stages.  Lane 0 issues TMA bulk copies
 // (cp.async.bulk, global -> shared, mbarrier completion) for the K and V rows
 // of upcoming chunks -- across unit boundaries, so short decode units keep the
-// ring full -- while the warp computes on the oldest stage:
-//   * QK^T: lane j owns key j of the chunk and reads its 256-byte row with a
-//     lane-rotated float4 order (conflict-free), q rows come from shared memory;
-//   * online softmax in the log2 domain, state in registers;
-//   * PV: lane l owns output dims 2l, 2l+1; probabilities are broadcast by
-//     warp shuffles.
+// ring full -- while the warp computes on the oldest stage.  The work metadata
+// travels with the data: block ids are prefetched a chunk ahead, work items a
+// unit ahead, and each stage carries a header, so no global-memory latency sits
+// between two chunks of compute.  Per chunk:
+//   * QK^T and PV with lane = (key group, quarter of the head dims): q rows
+//     and output accumulators live in registers, 4 passes of 8 keys cover
+//     the chunk, shared loads are conflict-free (see attend_chunk);
+//   * online softmax in the log2 domain, state in registers.
 // Finished units write either the normalised output row or (split items) an
-// un-normalised partial (m, l, acc[64]) that attn_combine_kernel merges.
+// un-normalised partial (m, l, acc[64]); the last split of a row merges them
+// (merge_if_last), so no second kernel is launched.
 #pragma once
 
 #include "common.cuh"
 
 namespace tq {
 
+// Pipeline shape (overridable at build time for tuning sweeps).
+#ifndef TQ_ATTN_CHUNK
+#define TQ_ATTN_CHUNK 32
+#endif
+#ifndef TQ_ATTN_MAX_ROWS
+#define TQ_ATTN_MAX_ROWS 2
+#endif
+#ifndef TQ_ATTN_STAGES
+#define TQ_ATTN_STAGES 2
+#endif
+#ifndef TQ_ATTN_WARPS
+#define TQ_ATTN_WARPS 6
+#endif
 constexpr int kHeadDim = 64;
-constexpr int kChunk = 32;    // keys per pipeline stage
-constexpr int kMaxRows = 4;   // query rows per work item
-constexpr int kStages = 3;    // stages per warp
-constexpr int kAttnWarps = 4; // independent warps per CTA
+constexpr int kChunk = TQ_ATTN_CHUNK;        // keys per pipeline stage (16 or 32)
+constexpr int kMaxRows = TQ_ATTN_MAX_ROWS;   // query rows per work item
+constexpr int kStages = TQ_ATTN_STAGES;      // stages per warp
+constexpr int kAttnWarps = TQ_ATTN_WARPS;    // independent warps per CTA
+constexpr int kPasses = kChunk / 8;          // 8 keys per pass (lane = key group x dim quarter)
+static_assert(kChunk == 16 || kChunk == 32, "chunk of 16 or 32 keys");
 
 constexpr int kRowBytes = kHeadDim * 4;                        // 256
 constexpr int kKBytes = kChunk * kRowBytes;                    // 8 KiB
 constexpr int kQBytes = kMaxRows * kRowBytes;                  // 1 KiB
-constexpr int kStageBytes = 2 * kKBytes + kQBytes;             // K | V | Q
-constexpr int kWarpSmemBytes = kStages * kStageBytes + kQBytes + 64;  // + current q + barriers
+constexpr int kHeaderBytes = 64;                               // StageHeader, padded
+constexpr int kStageBytes = 2 * kKBytes + kQBytes + kHeaderBytes;  // K | V | Q | header
+constexpr int kWarpSmemBytes = kStages * kStageBytes + 64;  // + barriers
 constexpr int kAttnSmemBytes = kAttnWarps * kWarpSmemBytes;
 
 // One work item: rows [row0, row0+nrows) of sequence `seq` (absolute
@@ -53,6 +72,14 @@ struct __align__(16) WorkItem {
   int cbeg, cend, part, split_nsplit;  // split | nsplit << 16
 };
 static_assert(sizeof(WorkItem) == 32, "WorkItem is 8 int32");
+
+// Written into each stage by the producer lane together with the copies, so
+// the computing lanes never read work metadata from global memory.
+struct StageHeader {
+  WorkItem it;
+  int h, c, pad0, pad1;
+};
+static_assert(sizeof(StageHeader) <= kHeaderBytes, "header fits its slot");
 
 struct AttnParams {
   float* out;
@@ -68,6 +95,7 @@ struct AttnParams {
   const int* n_items;    // device-resident count
   float* part_ml;        // [P][2]  (m in log2 units, l)
   float* part_acc;       // [P][64]
+  int* part_cnt;         // [P] split counters (zero between launches)
   float scale_log2;      // log2(e) / sqrt(head_dim)
 };
 
@@ -78,64 +106,248 @@ __device__ __forceinline__ size_t pool_tile_offset(const AttnParams& p, long lon
          (size_t)p.block_size * kHeadDim;
 }
 
-// Lane 0 only: arm `bar` and issue the bulk copies of chunk c of unit (it, h)
-// into `stage`.  The q rows ride along with the unit's first chunk.
-__device__ __forceinline__ void issue_chunk(const AttnParams& p, const WorkItem& it, int h, int c,
-                                            unsigned char* stage, uint32_t bar) {
+// Lanes 0..7 hold the 8 ints of a work item; every lane gets the fields.
+__device__ __forceinline__ WorkItem item_from_lanes(int v) {
+  WorkItem w;
+  w.seq = __shfl_sync(kFullMask, v, 0);
+  w.row0 = __shfl_sync(kFullMask, v, 1);
+  w.nrows = __shfl_sync(kFullMask, v, 2);
+  w.pos0 = __shfl_sync(kFullMask, v, 3);
+  w.cbeg = __shfl_sync(kFullMask, v, 4);
+  w.cend = __shfl_sync(kFullMask, v, 5);
+  w.part = __shfl_sync(kFullMask, v, 6);
+  w.split_nsplit = __shfl_sync(kFullMask, v, 7);
+  return w;
+}
+
+__device__ __forceinline__ int item_lane_load(const AttnParams& p, int unit, int n_units, int lane) {
+  return (unit < n_units && lane < 8)
+             ? __ldg(reinterpret_cast<const int*>(p.items) + (size_t)(unit / p.n_head) * 8 + lane)
+             : 0;
+}
+
+// Keys [key0, key0+nkeys) of chunk c, and the blocks [kb0, kb0+nblk) they live in.
+struct ChunkSpan {
+  int key0, nkeys, kb0, nblk;
+};
+
+__device__ __forceinline__ ChunkSpan chunk_span(const AttnParams& p, const WorkItem& it, int c) {
+  ChunkSpan sp;
   const int kend = min(it.pos0 + it.nrows, it.cend * kChunk);  // this item's last key + 1
-  const int key0 = c * kChunk;
-  const int nkeys = min(kChunk, kend - key0);
-  const bool first = (c == it.cbeg);
-  const int* tbl = p.tables + (size_t)it.seq * p.table_stride;
-  const int bs = p.block_size;
+  sp.key0 = c * kChunk;
+  sp.nkeys = min(kChunk, kend - sp.key0);
+  sp.kb0 = sp.key0 >> p.log2_bs;
+  sp.nblk = p.block_size <= kChunk ? ((sp.key0 + sp.nkeys - 1) >> p.log2_bs) - sp.kb0 + 1 : 1;
+  return sp;
+}
 
-  // Pass 1: count the bytes that will really be copied (a block id outside
-  // the pool is flagged and skipped, so expect_tx always matches).
-  uint32_t bytes = first ? (uint32_t)it.nrows * kRowBytes : 0u;
-  if (bs <= kChunk) {
-    for (int kb = key0 >> p.log2_bs; kb * bs < key0 + nkeys; ++kb) {
-      const long long blk = tbl[kb];
-      if (blk < 0 || blk >= p.num_blocks) continue;
-      const int rows = min(bs, key0 + nkeys - kb * bs);
-      bytes += 2u * rows * kRowBytes;
-    }
-  } else {
-    const long long blk = tbl[key0 >> p.log2_bs];
-    if (blk >= 0 && blk < p.num_blocks) bytes += 2u * nkeys * kRowBytes;
-  }
-  mbar_arrive_expect_tx(bar, bytes);
+// Lane layout inside a chunk of kChunk keys: lane = g*4 + qq, with g (0..7)
+// a key group and qq (0..3) a quarter of the 64 head dims.  Pass t
+// (0..kPasses-1) covers key t*8 + g.  A lane keeps its quarter of each q row and of each
+// output accumulator in registers, as 4 float4 "slots": slot i holds float4
+// (i + rot) & 3 of the quarter, rot = (qq >> 1) + 2*(g & 1).  With that
+// rotation the 8 lanes of every quarter-warp read 8 different 16-byte bank
+// groups of a 256-byte K or V row, so the shared loads are conflict-free.
+// Scores need 2 shuffles per pass (sum over quarters); PV needs none (a lane
+// already holds the probabilities of its own keys); the reductions over key
+// groups happen once per unit, in finish_rows().
+__device__ __forceinline__ int lane_rot(int lane) { return ((lane & 3) >> 1) + 2 * ((lane >> 2) & 1); }
 
-  const uint32_t sK = smem_addr(stage);
-  const uint32_t sV = sK + kKBytes;
-  const uint32_t sQ = sK + 2 * kKBytes;
-  if (first) {
-    for (int r = 0; r < it.nrows; ++r)
-      bulk_copy_g2s(sQ + r * kRowBytes, p.q + (size_t)(it.row0 + r) * p.q_stride + h * kHeadDim,
-                    kRowBytes, bar);
-  }
-  const size_t kv_stride = (size_t)p.n_head * bs * kHeadDim;  // K tile -> V tile
-  if (bs <= kChunk) {
-    for (int kb = key0 >> p.log2_bs; kb * bs < key0 + nkeys; ++kb) {
-      const long long blk = tbl[kb];
-      if (blk < 0 || blk >= p.num_blocks) {
-        raise_device_error(TQ_DEVERR_BAD_BLOCK);
-        continue;
+template <int NR>
+__device__ __forceinline__ void attend_chunk(const float* __restrict__ K, const float* __restrict__ V,
+                                             const float4 (&q)[kMaxRows][4], int nrows, int pos0,
+                                             int key0, int nkeys, float scale_log2, int lane,
+                                             float (&m)[kMaxRows], float (&lsum)[kMaxRows],
+                                             float4 (&acc)[kMaxRows][4]) {
+  const int g = lane >> 2, qq = lane & 3, rot = lane_rot(lane);
+  // ---- scores: sc[r][t] = q_r . k_{t*8+g} ------------------------------------
+  float sc[NR][kPasses];
+#pragma unroll
+  for (int t = 0; t < kPasses; ++t) {
+    const float4* krow = reinterpret_cast<const float4*>(K + (t * 8 + g) * kHeadDim + qq * 16);
+    float4 k[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) k[i] = krow[(i + rot) & 3];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      float a = q[r][0].x * k[0].x, b = q[r][0].y * k[0].y;
+      a = fmaf(q[r][0].z, k[0].z, a);
+      b = fmaf(q[r][0].w, k[0].w, b);
+#pragma unroll
+      for (int i = 1; i < 4; ++i) {
+        a = fmaf(q[r][i].x, k[i].x, a);
+        b = fmaf(q[r][i].y, k[i].y, b);
+        a = fmaf(q[r][i].z, k[i].z, a);
+        b = fmaf(q[r][i].w, k[i].w, b);
       }
-      const int rows = min(bs, key0 + nkeys - kb * bs);
-      const float* src = p.pool + pool_tile_offset(p, blk, 0, h);
-      const uint32_t dst_off = (uint32_t)(kb * bs - key0) * kRowBytes;
-      bulk_copy_g2s(sK + dst_off, src, rows * kRowBytes, bar);
-      bulk_copy_g2s(sV + dst_off, src + kv_stride, rows * kRowBytes, bar);
+      sc[r][t] = a + b;
     }
-  } else {
-    const long long blk = tbl[key0 >> p.log2_bs];
-    if (blk < 0 || blk >= p.num_blocks) {
-      raise_device_error(TQ_DEVERR_BAD_BLOCK);
-    } else {
-      const float* src =
-          p.pool + pool_tile_offset(p, blk, 0, h) + (size_t)(key0 & (bs - 1)) * kHeadDim;
-      bulk_copy_g2s(sK, src, nkeys * kRowBytes, bar);
-      bulk_copy_g2s(sV, src + kv_stride, nkeys * kRowBytes, bar);
+  }
+#pragma unroll
+  for (int r = 0; r < NR; ++r)
+#pragma unroll
+    for (int t = 0; t < kPasses; ++t) {
+      sc[r][t] += __shfl_xor_sync(kFullMask, sc[r][t], 1);
+      sc[r][t] += __shfl_xor_sync(kFullMask, sc[r][t], 2);
+    }
+
+  // ---- online softmax update per row (causal: keys <= the row's position) ----
+  float pr[NR][kPasses];
+#pragma unroll
+  for (int r = 0; r < NR; ++r) {
+#pragma unroll
+    for (int t = 0; t < kPasses; ++t) pr[r][t] = 0.f;
+    if (NR == 1 || r < nrows) {
+      const int nvalid = min(kChunk, pos0 + r + 1 - key0);
+      if (nvalid > 0) {
+        float x[kPasses];
+#pragma unroll
+        for (int t = 0; t < kPasses; ++t) x[t] = (t * 8 + g < nvalid) ? sc[r][t] * scale_log2 : -INFINITY;
+        float mx = x[0];
+#pragma unroll
+        for (int t = 1; t < kPasses; ++t) mx = fmaxf(mx, x[t]);
+        mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, 16));
+        const float mn = fmaxf(m[r], mx);
+        const float alpha = exp2f(m[r] - mn);  // 0 while m is still -inf
+        float psum = 0.f;
+#pragma unroll
+        for (int t = 0; t < kPasses; ++t) {
+          pr[r][t] = exp2f(x[t] - mn);
+          psum += pr[r][t];
+        }
+        lsum[r] = fmaf(lsum[r], alpha, psum);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[r][i].x *= alpha;
+          acc[r][i].y *= alpha;
+          acc[r][i].z *= alpha;
+          acc[r][i].w *= alpha;
+        }
+        m[r] = mn;
+      }
+    }
+  }
+
+  // ---- PV over this lane's keys (rows past nkeys were not copied: skip them) --
+#pragma unroll
+  for (int t = 0; t < kPasses; ++t) {
+    if (t * 8 + g < nkeys) {
+      const float4* vrow = reinterpret_cast<const float4*>(V + (t * 8 + g) * kHeadDim + qq * 16);
+      float4 v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = vrow[(i + rot) & 3];
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        const float pp = pr[r][t];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[r][i].x = fmaf(pp, v[i].x, acc[r][i].x);
+          acc[r][i].y = fmaf(pp, v[i].y, acc[r][i].y);
+          acc[r][i].z = fmaf(pp, v[i].z, acc[r][i].z);
+          acc[r][i].w = fmaf(pp, v[i].w, acc[r][i].w);
+        }
+      }
+    }
+  }
+}
+
+// Split-K merge, fused: the warp that writes the last partial of a (row,
+// head) merges all of them into the output row.  Each (row, head) has a
+// counter in part_cnt (at the index of its split 0 partial); every split
+// publishes its partial, fences, and bumps the counter; the one that sees
+// nsplit - 1 reads the partials back through L2 and resets the counter to 0,
+// so the scratch is ready for the next launch without a memset.
+__device__ __forceinline__ void merge_if_last(const AttnParams& p, const WorkItem& it, int r, int h,
+                                              int nsplit, int lane) {
+  const size_t idx0 = (size_t)it.part + ((size_t)r * p.n_head + h) * nsplit;
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    __threadfence();  // this split's partial is visible before the count says so
+    last = atomicAdd(p.part_cnt + idx0, 1) == nsplit - 1;
+  }
+  if (!__shfl_sync(kFullMask, last, 0)) return;
+  __threadfence();  // and every other split's partial is visible to this warp
+  float mmax = -INFINITY;
+  for (int s = lane; s < nsplit; s += 32) mmax = fmaxf(mmax, __ldcg(p.part_ml + 2 * (idx0 + s)));
+  mmax = warp_max(mmax);
+  float l = 0.f;
+  float2 o = make_float2(0.f, 0.f);
+  for (int s = 0; s < nsplit; ++s) {
+    const float w = exp2f(__ldcg(p.part_ml + 2 * (idx0 + s)) - mmax);  // 0 for a split without keys
+    l = fmaf(__ldcg(p.part_ml + 2 * (idx0 + s) + 1), w, l);
+    const float2 a = __ldcg(reinterpret_cast<const float2*>(p.part_acc + (idx0 + s) * kHeadDim) + lane);
+    o.x = fmaf(a.x, w, o.x);
+    o.y = fmaf(a.y, w, o.y);
+  }
+  const float inv = 1.f / l;
+  reinterpret_cast<float2*>(p.out + (size_t)(it.row0 + r) * p.out_stride + h * kHeadDim)[lane] =
+      make_float2(o.x * inv, o.y * inv);
+  if (lane == 0) p.part_cnt[idx0] = 0;
+}
+
+// End of a unit: sum l and the accumulators over the 8 key groups (lanes
+// xor 4, 8, 16; partners across xor 4 hold their slots rotated by 2) and write
+// each row -- normalised output, or a split-K partial.
+__device__ __forceinline__ void finish_rows(const AttnParams& p, const WorkItem& it, int h, int lane,
+                                            const float (&m)[kMaxRows], float (&lsum)[kMaxRows],
+                                            float4 (&acc)[kMaxRows][4]) {
+  const int qq = lane & 3, rot = lane_rot(lane);
+  const int split = it.split_nsplit & 0xffff;
+  const int nsplit = it.split_nsplit >> 16;
+#pragma unroll
+  for (int r = 0; r < kMaxRows; ++r) {
+    if (r < it.nrows) {
+      float l = lsum[r];
+      l += __shfl_xor_sync(kFullMask, l, 4);
+      l += __shfl_xor_sync(kFullMask, l, 8);
+      l += __shfl_xor_sync(kFullMask, l, 16);
+      float4 other[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 a = acc[r][(i + 2) & 3];
+        other[i] = make_float4(__shfl_xor_sync(kFullMask, a.x, 4), __shfl_xor_sync(kFullMask, a.y, 4),
+                               __shfl_xor_sync(kFullMask, a.z, 4), __shfl_xor_sync(kFullMask, a.w, 4));
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float4 a = acc[r][i];
+        a.x += other[i].x;
+        a.y += other[i].y;
+        a.z += other[i].z;
+        a.w += other[i].w;
+#pragma unroll
+        for (int o = 8; o <= 16; o <<= 1) {
+          a.x += __shfl_xor_sync(kFullMask, a.x, o);
+          a.y += __shfl_xor_sync(kFullMask, a.y, o);
+          a.z += __shfl_xor_sync(kFullMask, a.z, o);
+          a.w += __shfl_xor_sync(kFullMask, a.w, o);
+        }
+        acc[r][i] = a;
+      }
+      if (lane < 4) {  // key group 0 writes the row: 4 lanes x 64 bytes
+        if (nsplit == 1) {
+          const float inv = 1.f / l;
+          float4* o = reinterpret_cast<float4*>(p.out + (size_t)(it.row0 + r) * p.out_stride +
+                                                h * kHeadDim + qq * 16);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o[(i + rot) & 3] = make_float4(acc[r][i].x * inv, acc[r][i].y * inv, acc[r][i].z * inv,
+                                           acc[r][i].w * inv);
+        } else {
+          const size_t idx = (size_t)it.part + ((size_t)r * p.n_head + h) * nsplit + split;
+          float4* o = reinterpret_cast<float4*>(p.part_acc + idx * kHeadDim + qq * 16);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) o[(i + rot) & 3] = acc[r][i];
+          if (lane == 0) {
+            p.part_ml[2 * idx] = m[r];
+            p.part_ml[2 * idx + 1] = l;
+          }
+        }
+      }
+      if (nsplit > 1) merge_if_last(p, it, r, h, nsplit, lane);
     }
   }
 }
@@ -145,14 +357,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) paged_attention_kernel(con
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   unsigned char* wsm = smem + warp * kWarpSmemBytes;
-  float* qcur = reinterpret_cast<float*>(wsm + kStages * kStageBytes);
-  const uint32_t bar0 = smem_addr(wsm + kStages * kStageBytes + kQBytes);
+  const uint32_t bar0 = smem_addr(wsm + kStages * kStageBytes);
 
   const int H = p.n_head;
   const int n_units = *p.n_items * H;
   const int TW = gridDim.x * kAttnWarps;
-  int unit = blockIdx.x * kAttnWarps + warp;
-  if (unit >= n_units) return;  // warp-uniform; warps never synchronise with each other
+  const int first_unit = blockIdx.x * kAttnWarps + warp;
+  if (first_unit >= n_units) return;  // warp-uniform; warps never synchronise with each other
 
   if (lane == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(bar0 + 8 * s, 1);
@@ -160,40 +371,118 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) paged_attention_kernel(con
   }
   __syncwarp();
 
-  // Producer cursor (meaningful in lane 0 only).
-  int p_unit = unit;
-  WorkItem p_it = p.items[p_unit / H];
+  // ---- producer cursor: warp-uniform; lane 0 issues the copies ---------------
+  // Block ids of the next chunk to issue are loaded one chunk ahead (lane i
+  // holds block i of the chunk) and the next unit's work item one unit ahead,
+  // so those global loads overlap a chunk of compute instead of stalling it.
+  int p_unit = first_unit;
+  WorkItem p_it = item_from_lanes(item_lane_load(p, p_unit, n_units, lane));
   int p_chunk = p_it.cbeg;
+  int nx_item = item_lane_load(p, p_unit + TW, n_units, lane);
   bool p_live = true;
+  int pf_blk = 0;
+  auto prefetch_blocks = [&]() {
+    const ChunkSpan sp = chunk_span(p, p_it, p_chunk);
+    const int* tbl = p.tables + (size_t)p_it.seq * p.table_stride;
+    pf_blk = lane < sp.nblk ? __ldg(tbl + sp.kb0 + lane) : 0;
+  };
+  prefetch_blocks();
   int issued = 0, consumed = 0;
 
-  auto refill = [&]() {
-    while (p_live && issued < consumed + kStages) {
-      const int s = issued % kStages;
-      if (issued >= kStages) fence_proxy_async_smem();  // stage was read by the warp before
-      issue_chunk(p, p_it, p_unit % H, p_chunk, wsm + s * kStageBytes, bar0 + 8 * s);
-      ++issued;
-      if (++p_chunk == p_it.cend) {
-        p_unit += TW;
-        if (p_unit < n_units) {
-          p_it = p.items[p_unit / H];
-          p_chunk = p_it.cbeg;
+  auto issue = [&]() {
+    const int s = issued % kStages;
+    unsigned char* stage = wsm + s * kStageBytes;
+    const uint32_t bar = bar0 + 8 * s;
+    const ChunkSpan sp = chunk_span(p, p_it, p_chunk);
+    const bool first = (p_chunk == p_it.cbeg);
+    const int bs = p.block_size;
+    uint32_t bytes = first ? (uint32_t)p_it.nrows * kRowBytes : 0u;
+    for (int i = 0; i < sp.nblk; ++i) {
+      const long long blk = __shfl_sync(kFullMask, pf_blk, i);
+      if (blk < 0 || blk >= p.num_blocks) continue;
+      const int rows = bs <= kChunk ? min(bs, sp.key0 + sp.nkeys - (sp.kb0 + i) * bs) : sp.nkeys;
+      bytes += 2u * rows * kRowBytes;
+    }
+    const uint32_t sK = smem_addr(stage);
+    const uint32_t sV = sK + kKBytes;
+    const uint32_t sQ = sK + 2 * kKBytes;
+    if (lane == 0) {
+      if (first) {  // the consumer picks the unit's work item up from here
+        StageHeader* hd = reinterpret_cast<StageHeader*>(stage + 2 * kKBytes + kQBytes);
+        hd->it = p_it;
+        hd->h = p_unit % H;
+        hd->c = p_chunk;
+      }
+      if (issued >= kStages) fence_proxy_async_smem();  // the warp has read this stage before
+      mbar_arrive_expect_tx(bar, bytes);
+      if (first) {
+        for (int r = 0; r < p_it.nrows; ++r)
+          bulk_copy_g2s(sQ + r * kRowBytes,
+                        p.q + (size_t)(p_it.row0 + r) * p.q_stride + (p_unit % H) * kHeadDim, kRowBytes,
+                        bar);
+      }
+    }
+    const size_t kv_stride = (size_t)H * bs * kHeadDim;  // K tile -> V tile
+    for (int i = 0; i < sp.nblk; ++i) {
+      const long long blk = __shfl_sync(kFullMask, pf_blk, i);
+      if (blk < 0 || blk >= p.num_blocks) {
+        if (lane == 0) raise_device_error(TQ_DEVERR_BAD_BLOCK);
+        continue;
+      }
+      if (lane == 0) {
+        if (bs <= kChunk) {
+          const int kb = sp.kb0 + i;
+          const int rows = min(bs, sp.key0 + sp.nkeys - kb * bs);
+          const float* src = p.pool + pool_tile_offset(p, blk, 0, p_unit % H);
+          const uint32_t dst_off = (uint32_t)(kb * bs - sp.key0) * kRowBytes;
+          bulk_copy_g2s(sK + dst_off, src, rows * kRowBytes, bar);
+          bulk_copy_g2s(sV + dst_off, src + kv_stride, rows * kRowBytes, bar);
         } else {
-          p_live = false;
+          const float* src = p.pool + pool_tile_offset(p, blk, 0, p_unit % H) +
+                             (size_t)(sp.key0 & (bs - 1)) * kHeadDim;
+          bulk_copy_g2s(sK, src, sp.nkeys * kRowBytes, bar);
+          bulk_copy_g2s(sV, src + kv_stride, sp.nkeys * kRowBytes, bar);
         }
       }
     }
+    ++issued;
   };
 
-  WorkItem it = p.items[unit / H];
-  int h = unit % H;
-  int c = it.cbeg;
-  float m[kMaxRows], lsum[kMaxRows];
-  float2 acc[kMaxRows];
-  bool failed = false;
+  auto advance = [&]() {
+    if (++p_chunk == p_it.cend) {
+      p_unit += TW;
+      if (p_unit < n_units) {
+        p_it = item_from_lanes(nx_item);
+        p_chunk = p_it.cbeg;
+        nx_item = item_lane_load(p, p_unit + TW, n_units, lane);
+      } else {
+        p_live = false;
+      }
+    }
+    if (p_live) prefetch_blocks();
+  };
 
-  if (lane == 0) refill();
-  while (true) {
+  auto refill = [&]() {
+    while (p_live && issued < consumed + kStages) {
+      issue();
+      advance();
+    }
+  };
+
+  // ---- consumer: everything it needs is in the stage -------------------------
+  // Stages are consumed in issue order, so the consumer tracks the chunk index
+  // itself and reads the work item from a stage header only at a unit start.
+  float m[kMaxRows], lsum[kMaxRows];
+  float4 acc[kMaxRows][4];
+  float4 qr[kMaxRows][4];
+  WorkItem it;
+  int h = 0, c = 0;
+  bool at_unit_start = true;
+  bool failed = false;
+  const int rot = lane_rot(lane);
+
+  refill();
+  while (consumed < issued) {
     const int s = consumed % kStages;
     const uint32_t parity = (uint32_t)(consumed / kStages) & 1u;
     const bool ok = mbar_wait_bounded(bar0 + 8 * s, parity);
@@ -201,114 +490,42 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) paged_attention_kernel(con
       failed = true;
       break;
     }
-    unsigned char* stage = wsm + s * kStageBytes;
-    const float* K = reinterpret_cast<const float*>(stage);
-    const float2* V2 = reinterpret_cast<const float2*>(stage + kKBytes);
-
-    if (c == it.cbeg) {  // first chunk of a unit: take its q rows, reset state
+    const unsigned char* stage = wsm + s * kStageBytes;
+    if (at_unit_start) {  // take the unit's work item and q rows, reset state
+      const StageHeader* hd = reinterpret_cast<const StageHeader*>(stage + 2 * kKBytes + kQBytes);
+      it = hd->it;
+      h = hd->h;
+      c = it.cbeg;
       const float4* qsrc = reinterpret_cast<const float4*>(stage + 2 * kKBytes);
-      float4* qdst = reinterpret_cast<float4*>(qcur);
-      for (int i = lane; i < it.nrows * (kHeadDim / 4); i += 32) qdst[i] = qsrc[i];
 #pragma unroll
       for (int r = 0; r < kMaxRows; ++r) {
         m[r] = -INFINITY;
         lsum[r] = 0.f;
-        acc[r] = make_float2(0.f, 0.f);
-      }
-      __syncwarp();
-    }
-
-    const int key0 = c * kChunk;
-    const int kend = min(it.pos0 + it.nrows, it.cend * kChunk);
-    const int nkeys = min(kChunk, kend - key0);
-
-    // ---- scores: lane j <-> key key0 + j ------------------------------------
-    float sc[kMaxRows];
 #pragma unroll
-    for (int r = 0; r < kMaxRows; ++r) sc[r] = 0.f;
-    const float4* krow = reinterpret_cast<const float4*>(K) + lane * (kHeadDim / 4);
-    const float4* q4 = reinterpret_cast<const float4*>(qcur);
-#pragma unroll
-    for (int i = 0; i < kHeadDim / 4; ++i) {
-      const int ch = (i + lane) & (kHeadDim / 4 - 1);
-      const float4 k = krow[ch];
-#pragma unroll
-      for (int r = 0; r < kMaxRows; ++r) {
-        if (r < it.nrows) {
-          const float4 q = q4[r * (kHeadDim / 4) + ch];
-          sc[r] = fmaf(q.x, k.x, sc[r]);
-          sc[r] = fmaf(q.y, k.y, sc[r]);
-          sc[r] = fmaf(q.z, k.z, sc[r]);
-          sc[r] = fmaf(q.w, k.w, sc[r]);
+        for (int i = 0; i < 4; ++i) {
+          acc[r][i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          qr[r][i] = r < it.nrows ? qsrc[r * (kHeadDim / 4) + (lane & 3) * 4 + ((i + rot) & 3)]
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
+      at_unit_start = false;
     }
 
-    // ---- online softmax update per row --------------------------------------
-    float pr[kMaxRows];
-#pragma unroll
-    for (int r = 0; r < kMaxRows; ++r) {
-      pr[r] = 0.f;
-      if (r < it.nrows) {
-        const int nvalid = min(kChunk, it.pos0 + r + 1 - key0);  // causal: keys <= position
-        if (nvalid > 0) {
-          const float x = (lane < nvalid) ? sc[r] * p.scale_log2 : -INFINITY;
-          const float mn = fmaxf(m[r], warp_max(x));
-          const float alpha = exp2f(m[r] - mn);
-          pr[r] = exp2f(x - mn);
-          lsum[r] = fmaf(lsum[r], alpha, pr[r]);
-          acc[r].x *= alpha;
-          acc[r].y *= alpha;
-          m[r] = mn;
-        }
-      }
-    }
-
-    // ---- PV: lane l owns dims 2l, 2l+1 --------------------------------------
-#pragma unroll 4
-    for (int j = 0; j < nkeys; ++j) {
-      const float2 v = V2[j * (kHeadDim / 2) + lane];
-#pragma unroll
-      for (int r = 0; r < kMaxRows; ++r) {
-        if (r < it.nrows) {
-          const float pj = __shfl_sync(kFullMask, pr[r], j);
-          acc[r].x = fmaf(pj, v.x, acc[r].x);
-          acc[r].y = fmaf(pj, v.y, acc[r].y);
-        }
-      }
-    }
+    const ChunkSpan sp = chunk_span(p, it, c);
+    const float* K = reinterpret_cast<const float*>(stage);
+    const float* V = reinterpret_cast<const float*>(stage + kKBytes);
+    if (it.nrows == 1)
+      attend_chunk<1>(K, V, qr, 1, it.pos0, sp.key0, sp.nkeys, p.scale_log2, lane, m, lsum, acc);
+    else
+      attend_chunk<kMaxRows>(K, V, qr, it.nrows, it.pos0, sp.key0, sp.nkeys, p.scale_log2, lane, m,
+                             lsum, acc);
     __syncwarp();
     ++consumed;
-
-    if (++c == it.cend) {  // unit finished: write its rows
-      const int split = it.split_nsplit & 0xffff;
-      const int nsplit = it.split_nsplit >> 16;
-#pragma unroll
-      for (int r = 0; r < kMaxRows; ++r) {
-        if (r < it.nrows) {
-          const float l = warp_sum(lsum[r]);
-          if (nsplit == 1) {
-            const float inv = 1.f / l;
-            float2* o = reinterpret_cast<float2*>(p.out + (size_t)(it.row0 + r) * p.out_stride +
-                                                  h * kHeadDim);
-            o[lane] = make_float2(acc[r].x * inv, acc[r].y * inv);
-          } else {
-            const size_t idx = (size_t)it.part + ((size_t)r * H + h) * nsplit + split;
-            reinterpret_cast<float2*>(p.part_acc + idx * kHeadDim)[lane] = acc[r];
-            if (lane == 0) {
-              p.part_ml[2 * idx] = m[r];
-              p.part_ml[2 * idx + 1] = l;
-            }
-          }
-        }
-      }
-      unit += TW;
-      if (unit >= n_units) break;
-      it = p.items[unit / H];
-      h = unit % H;
-      c = it.cbeg;
+    if (++c == it.cend) {  // unit finished
+      finish_rows(p, it, h, lane, m, lsum, acc);
+      at_unit_start = true;
     }
-    if (lane == 0) refill();
+    refill();
   }
 
   if (failed) {
@@ -317,44 +534,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) paged_attention_kernel(con
     for (int k = consumed; k < issued; ++k) {
       if (!mbar_wait_bounded(bar0 + 8 * (k % kStages), (uint32_t)(k / kStages) & 1u)) break;
     }
-  }
-}
-
-// Merge split-K partials: one warp per (combine entry, head).
-struct CombineParams {
-  float* out;
-  long long out_stride;
-  const float* part_ml;
-  const float* part_acc;
-  const int4* entries;    // {row, partial base of (row, head 0), nsplit, unused}
-  const int* n_entries;   // device-resident count
-  int n_head;
-};
-
-__global__ void __launch_bounds__(256) attn_combine_kernel(const CombineParams p) {
-  const int lane = threadIdx.x & 31;
-  const int TW = gridDim.x * (blockDim.x >> 5);
-  const int n_units = *p.n_entries * p.n_head;
-  for (int u = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n_units; u += TW) {
-    const int4 e = p.entries[u / p.n_head];
-    const int h = u % p.n_head;
-    const size_t base = (size_t)e.y + (size_t)h * e.z;
-    float mmax = -INFINITY;
-    for (int s = lane; s < e.z; s += 32) mmax = fmaxf(mmax, p.part_ml[2 * (base + s)]);
-    mmax = warp_max(mmax);
-    float l = 0.f;
-    float2 o = make_float2(0.f, 0.f);
-    for (int s = 0; s < e.z; ++s) {
-      const float ms = p.part_ml[2 * (base + s)];
-      const float w = exp2f(ms - mmax);  // 0 for a split that saw no key of this row
-      l = fmaf(p.part_ml[2 * (base + s) + 1], w, l);
-      const float2 a = reinterpret_cast<const float2*>(p.part_acc + (base + s) * kHeadDim)[lane];
-      o.x = fmaf(a.x, w, o.x);
-      o.y = fmaf(a.y, w, o.y);
-    }
-    const float inv = 1.f / l;
-    reinterpret_cast<float2*>(p.out + (size_t)e.x * p.out_stride + h * kHeadDim)[lane] =
-        make_float2(o.x * inv, o.y * inv);
   }
 }
 

@@ -18,14 +18,22 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "../../include/tokquay_b200.h"
 #include "host_error.h"
 
 namespace {
 
-constexpr int kChunk = 32;    // keys per attention chunk (paged_attention.cuh)
-constexpr int kMaxRows = 4;   // query rows per work item
+// Must match the attention kernel's pipeline shape (paged_attention.cuh).
+#ifndef TQ_ATTN_CHUNK
+#define TQ_ATTN_CHUNK 32
+#endif
+#ifndef TQ_ATTN_MAX_ROWS
+#define TQ_ATTN_MAX_ROWS 2
+#endif
+constexpr int kChunk = TQ_ATTN_CHUNK;      // keys per attention chunk
+constexpr int kMaxRows = TQ_ATTN_MAX_ROWS; // query rows per work item
 
 inline int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t align4(int64_t n) { return (n + 3) & ~int64_t(3); }
@@ -36,8 +44,8 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
                             const int32_t* table_offsets, const int32_t* table_data,
                             const int32_t* token_ids, int32_t block_size, int64_t num_blocks,
                             int32_t n_head, int32_t vocab_size, int32_t target_units,
-                            int32_t min_split_chunks, int32_t* out, int64_t out_capacity,
-                            int32_t* layout) {
+                            int32_t min_split_chunks, const int32_t* caps, int32_t* out,
+                            int64_t out_capacity, int32_t* layout) {
   using tq::set_error;
   if (layout == nullptr) return set_error(TQ_ERR_INVALID, "layout must not be NULL");
   std::memset(layout, 0, sizeof(int32_t) * TQ_PLAN_LAYOUT_LEN);
@@ -99,22 +107,49 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   split_chunks = std::max<int64_t>(split_chunks, cdiv64(cdiv64(max_ctx, kChunk), 0x7fff));
 
   int64_t n_items = 0, n_combine = 0, n_partials = 0;
-  for (int b = 0; b < num_seqs; ++b) {
-    for (int64_t g0 = 0; g0 < q_len[b]; g0 += kMaxRows) {
-      const int64_t nrows = std::min<int64_t>(kMaxRows, q_len[b] - g0);
-      const int64_t nc = cdiv64(start[b] + g0 + nrows, kChunk);
-      const int64_t nsplit = cdiv64(nc, split_chunks);
-      n_items += nsplit;
-      if (nsplit > 1) {
-        n_combine += nrows;
-        n_partials += nrows * n_head * nsplit;
+  auto count_items = [&]() {
+    n_items = n_combine = n_partials = 0;
+    for (int b = 0; b < num_seqs; ++b) {
+      for (int64_t g0 = 0; g0 < q_len[b]; g0 += kMaxRows) {
+        const int64_t nrows = std::min<int64_t>(kMaxRows, q_len[b] - g0);
+        const int64_t nc = cdiv64(start[b] + g0 + nrows, kChunk);
+        const int64_t nsplit = cdiv64(nc, split_chunks);
+        n_items += nsplit;
+        if (nsplit > 1) {
+          n_combine += nrows;
+          n_partials += nrows * n_head * nsplit;
+        }
       }
     }
+  };
+  count_items();
+  // With fixed capacities, coarsen the split until the items and partials fit.
+  while (caps && split_chunks < INT32_MAX && (n_items > caps[3] || n_partials > caps[5])) {
+    split_chunks = split_chunks >= (INT32_MAX / 2) ? INT32_MAX : split_chunks * 2;
+    count_items();
   }
   if (n_partials > INT32_MAX || n_items > INT32_MAX / n_head)
     return set_error(TQ_ERR_UNSUPPORTED, "step too large to plan");
 
   const int64_t B = num_seqs;
+  // Region sizes: this step's own, or the fixed capacities (caps) so that the
+  // offsets -- and every pointer a captured CUDA graph holds -- stay put.
+  int64_t dim_B = B, dim_N = N, dim_nb = max_nb, dim_items = n_items, dim_comb = n_combine;
+  if (caps) {
+    if (B > caps[0] || N > caps[1] || max_nb > caps[2] || n_items > caps[3] ||
+        n_combine > caps[4] || n_partials > caps[5])
+      return set_error(TQ_ERR_CAPACITY,
+                       "step (seqs %lld, tokens %lld, blocks/seq %lld, items %lld, combine %lld, "
+                       "partials %lld) exceeds the fixed plan capacities (%d, %d, %d, %d, %d, %d)",
+                       (long long)B, (long long)N, (long long)max_nb, (long long)n_items,
+                       (long long)n_combine, (long long)n_partials, caps[0], caps[1], caps[2],
+                       caps[3], caps[4], caps[5]);
+    dim_B = caps[0];
+    dim_N = caps[1];
+    dim_nb = caps[2];
+    dim_items = caps[3];
+    dim_comb = caps[4];
+  }
   int64_t off = 0;
   auto take = [&](int64_t n) {
     const int64_t o = off;
@@ -122,16 +157,17 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     return o;
   };
   const int64_t o_counts = take(4);
-  const int64_t o_seq = take(B * 4);
-  const int64_t o_tab = take(B * max_nb);
-  const int64_t o_slot = take(N);
-  const int64_t o_pos = take(N);
-  const int64_t o_ids = take(N);
-  const int64_t o_last = take(B);
-  const int64_t o_items = take(n_items * 8);
-  const int64_t o_comb = take(n_combine * 4);
+  const int64_t o_seq = take(dim_B * 4);
+  const int64_t o_tab = take(dim_B * dim_nb);
+  const int64_t o_slot = take(dim_N);
+  const int64_t o_pos = take(dim_N);
+  const int64_t o_ids = take(dim_N);
+  const int64_t o_last = take(dim_B);
+  const int64_t o_items = take(dim_items * 8);
+  const int64_t o_comb = take(dim_comb * 4);
   const int64_t total = off;
   if (total > INT32_MAX) return set_error(TQ_ERR_UNSUPPORTED, "step too large to plan");
+  max_nb = dim_nb;  // row stride of the packed tables
 
   layout[TQ_PLAN_NUM_TOKENS] = (int32_t)N;
   layout[TQ_PLAN_NUM_SEQS] = (int32_t)B;
@@ -157,6 +193,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
 
   // ---- pass 2: write --------------------------------------------------------
   std::memset(out, 0, sizeof(int32_t) * total);
+  std::vector<int32_t> items((size_t)n_items * 8);
   out[o_counts + 0] = (int32_t)N;
   out[o_counts + 1] = (int32_t)n_items;
   out[o_counts + 2] = (int32_t)n_combine;
@@ -184,7 +221,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
       const int64_t nc = cdiv64(s0 + g0 + nrows, kChunk);
       const int64_t nsplit = cdiv64(nc, split_chunks);
       for (int64_t s = 0; s < nsplit; ++s) {
-        int32_t* it = out + o_items + 8 * item++;
+        int32_t* it = items.data() + 8 * item++;
         it[0] = b;
         it[1] = (int32_t)(row + g0);
         it[2] = (int32_t)nrows;
@@ -207,5 +244,15 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     }
     row += n;
   }
+  // Longest items first: the kernel hands unit u to warp u % (warps in the
+  // grid), so every warp then gets one item of each length class and all
+  // warps finish within about one item of each other.
+  std::vector<int32_t> order((size_t)n_items);
+  for (int64_t i = 0; i < n_items; ++i) order[i] = (int32_t)i;
+  std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) {
+    return items[8 * a + 5] - items[8 * a + 4] > items[8 * b + 5] - items[8 * b + 4];
+  });
+  for (int64_t i = 0; i < n_items; ++i)
+    std::memcpy(out + o_items + 8 * i, items.data() + 8 * (size_t)order[i], 8 * sizeof(int32_t));
   return TQ_OK;
 }

@@ -27,8 +27,12 @@ def paged_forward(
     Blocks must already cover the sequences.  Advances ``num_cached_tokens``.
     """
     lens = new_lens or [s.num_uncached_tokens for s in seqs]
-    batch = allocator.batch_for(seqs, lens)
-    logits = model.forward_paged(batch, last_only=True)[:, 0]
+    runner = getattr(model, "graph_runner", None)
+    if runner is not None and runner.accepts(allocator, seqs, lens):
+        logits = runner.run(seqs)  # decode step: replay a captured CUDA graph
+    else:
+        batch = allocator.batch_for(seqs, lens)
+        logits = model.forward_paged(batch, last_only=True)[:, 0]
     for s, n in zip(seqs, lens):
         s.num_cached_tokens += n
     return logits

@@ -1,0 +1,161 @@
+"""CUDA-graph replay of the decode step.
+
+A decode step (one new token per sequence) launches ~75 of this package's
+kernels and ~60 torch ops; issued one by one from Python that costs more host
+time than the GPU spends on a 64-sequence step.  ``DecodeGraphRunner``
+captures the whole step -- paged forward plus the greedy argmax -- once per
+batch-size bucket, over a ``PlanWorkspace`` of that bucket's capacities, and
+replays it: per step the host only plans (``tq_plan_step``, in C), copies the
+plan into the workspace and launches the graph.
+
+A bucket's graph runs any decode batch of up to ``bucket`` sequences: the
+kernels read the step's true token, work-item and combine counts from the
+device plan, and the GEMMs / argmax run over the bucket's rows (the rows past
+the batch hold stale values whose results are never read).
+"""
+
+from __future__ import annotations
+
+import bisect
+
+import torch
+
+from tokquay_b200 import _lib
+from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, PlanWorkspace
+from tokquay_b200.sequence import Sequence
+
+DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256, 512)
+
+
+class DecodeGraphRunner:
+    """Captured decode steps for one model and one allocator (pool).
+
+    ``run(seqs)`` = ``paged_forward`` for a batch where every sequence feeds
+    exactly one token; returns a fresh ``[B, vocab]`` logits tensor (the
+    graph's own output buffer is overwritten by the next replay).
+    """
+
+    def __init__(self, model, allocator: BlockAllocator, buckets=DEFAULT_BUCKETS, max_ctx: int | None = None):
+        if allocator.pool.device.type != "cuda":
+            raise RuntimeError("CUDA graphs need the pool on a CUDA device")
+        self.model = model
+        self.allocator = allocator
+        self.buckets = sorted(set(int(b) for b in buckets))
+        self.max_ctx = max_ctx or model.cfg.n_positions
+        self._graphs: dict[int, tuple] = {}
+        self._pool = None  # one private memory pool shared by every bucket's graph
+
+    @property
+    def max_batch(self) -> int:
+        return self.buckets[-1]
+
+    def bucket_for(self, n: int) -> int | None:
+        i = bisect.bisect_left(self.buckets, n)
+        return self.buckets[i] if i < len(self.buckets) else None
+
+    def accepts(self, allocator, seqs: list[Sequence], new_lens: list[int]) -> bool:
+        return (allocator is self.allocator and 0 < len(seqs) <= self.max_batch
+                and all(n == 1 for n in new_lens)
+                and max(s.num_cached_tokens for s in seqs) < self.max_ctx)  # fmt: skip
+
+    def _capture(self, bucket: int):
+        ws = PlanWorkspace(self.allocator, bucket, bucket, self.max_ctx)
+        # A plan whose counts are all zero: every kernel of the step exits at
+        # once, so the warm-up run below touches neither the pool nor anything else.
+        ws.plan.zero_()
+        view = _CaptureView(ws)
+        dev = self.allocator.pool.device
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):  # warm cuBLAS handles and workspaces outside the capture
+                self.model.forward_paged(view, last_only=True)[:, 0].argmax(-1)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        if self._pool is None:
+            self._pool = torch.cuda.graph_pool_handle()
+        launches = self.model.kernel_launches
+        with torch.cuda.graph(graph, pool=self._pool):
+            logits = self.model.forward_paged(view, last_only=True)[:, 0]
+            tokens = logits.argmax(-1)
+        per_replay = self.model.kernel_launches - launches
+        self.model.kernel_launches = launches
+        entry = (graph, ws, logits, tokens, per_replay)
+        self._graphs[bucket] = entry
+        return entry
+
+    def graph(self, bucket: int):
+        return self._graphs.get(bucket) or self._capture(bucket)
+
+    def run(self, seqs: list[Sequence]) -> torch.Tensor:
+        """Plan the decode step for ``seqs``, replay its bucket's graph, return
+        ``[B, vocab]`` logits (a copy).  Does not advance the sequences."""
+        B = len(seqs)
+        bucket = self.bucket_for(B)
+        if bucket is None:
+            raise ValueError(f"{B} sequences exceed the largest graph bucket {self.max_batch}")
+        graph, ws, logits, _, per_replay = self.graph(bucket)
+        starts = [s.num_cached_tokens for s in seqs]
+        ids = [s.tokens_slice(st, st + 1)[0] for s, st in zip(seqs, starts)]
+        DevicePagedBatch(self.allocator, [s.block_table for s in seqs], starts, [1] * B, ids, workspace=ws)
+        self.model.last_h2d_bytes = ws.total * 4
+        graph.replay()
+        self.model.kernel_launches += per_replay
+        return logits[:B].clone()
+
+    def replay_plan(self, bucket: int, plan: torch.Tensor, ids: torch.Tensor | None = None) -> torch.Tensor:
+        """Replay ``bucket``'s graph on a plan already in device memory (built
+        with that bucket's workspace capacities, ``PlanWorkspace.caps``),
+        optionally overwriting its token ids from a device tensor first.
+        Returns the graph's greedy-token buffer (valid until the next replay)."""
+        graph, ws, _, tokens, per_replay = self.graph(bucket)
+        ws.plan.copy_(plan)
+        if ids is not None:
+            off = int(ws.layout[_lib.PLAN_OFF_TOKEN_IDS])
+            ws.plan[off:off + ids.numel()].copy_(ids)
+        graph.replay()
+        self.model.kernel_launches += per_replay
+        return tokens
+
+
+class _CaptureView(DevicePagedBatch):
+    """A step view over a workspace with no plan of its own: capacities for
+    sizing, the workspace's fixed buffers for every pointer.  Used only to
+    capture a graph; the plan is filled in before each replay."""
+
+    def __init__(self, ws: PlanWorkspace):  # noqa: D107 -- deliberately skips the planner
+        a = ws.allocator
+        cfg = a.cfg
+        L = ws.layout
+        caps = ws.caps
+        self.allocator, self.pool, self.block_size = a, a.pool, a.block_size
+        self.n_layer, self.n_head, self.d_head = cfg.n_layer, cfg.n_head, cfg.d_head
+        self.B = self.N = self.T = 1
+        self.max_ctx = 1
+        self.layout = L
+        self.h2d_bytes = 0
+        self.plan = ws.plan
+        self.table_stride = int(L[_lib.PLAN_TABLE_STRIDE])
+        self.rows_alloc, self.seqs_alloc = int(caps[1]), int(caps[0])
+        self.items_alloc, self.partials_alloc = int(caps[3]), int(caps[5])
+        self.num_items = self.num_combine = self.num_partials = 0
+        dev = ws.plan
+
+        def view(k, n):
+            o = int(L[k])
+            return dev[o:o + int(n)]
+
+        self.counts = view(_lib.PLAN_OFF_COUNTS, 4)
+        self.block_tables_i32 = view(_lib.PLAN_OFF_TABLES, int(caps[0]) * self.table_stride)
+        self.slot_mapping = view(_lib.PLAN_OFF_SLOTS, int(caps[1]))
+        self.row_positions = view(_lib.PLAN_OFF_POSITIONS, int(caps[1]))
+        self.token_ids = view(_lib.PLAN_OFF_TOKEN_IDS, int(caps[1]))
+        self.last_rows = view(_lib.PLAN_OFF_LAST_ROWS, int(caps[0]))
+        self.work_items = view(_lib.PLAN_OFF_ITEMS, 8 * int(caps[3]))
+        self.combine_list = view(_lib.PLAN_OFF_COMBINE, 4 * int(caps[4]))
+        self._dev_ptr = dev.data_ptr()
+        self._off = {k: int(L[k]) * 4 for k in range(_lib.PLAN_OFF_COUNTS, _lib.PLAN_LAYOUT_LEN)}
+        self.partial_ml, self.partial_acc = ws.partial_ml, ws.partial_acc
+        self.partial_counters = ws.partial_counters
+        self._positions = self._last_idx = self._mask = self._flat_bt = None

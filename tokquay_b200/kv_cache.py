@@ -34,9 +34,6 @@ from tokquay_b200.sequence import Sequence
 if TYPE_CHECKING:
     from tokquay_b200.model import GPT2Config
 
-# Keys per attention chunk and warps per attention CTA (csrc/paged_attention.cuh).
-ATTN_CHUNK = 32
-ATTN_WARPS_PER_CTA = 4
 # Split-K policy: aim for this many (item, head) units per SM, never cut a
 # split below this many 32-key chunks.
 UNITS_PER_SM = 16
@@ -45,6 +42,12 @@ MIN_SPLIT_CHUNKS = 2
 
 def cdiv(a: int, b: int) -> int:
     return -(-a // b)
+
+
+def attention_chunk_keys() -> int:
+    """Keys per attention chunk of the loaded library build (the unit of
+    split-K sizes and of the kernel's shared-memory stages)."""
+    return _lib.load().tq_attention_chunk_keys()
 
 
 class OutOfBlocksError(RuntimeError):
@@ -239,11 +242,14 @@ def plan_step_host(
     target_units: int = 2368,
     min_split_chunks: int = MIN_SPLIT_CHUNKS,
     out: torch.Tensor | np.ndarray | None = None,
+    caps: np.ndarray | None = None,
 ) -> tuple[np.ndarray, np.ndarray]:
     """Run ``tq_plan_step`` on the host: returns ``(plan, layout)`` (int32
     arrays).  ``out`` (an int32 host buffer) is written in place when it is
-    large enough; otherwise a new array is returned.  Raises ValueError for a
-    batch the reference would reject."""
+    large enough; otherwise a new array is returned.  ``caps`` (6 int32:
+    max seqs, tokens, table stride, items, combine entries, partials) selects
+    the fixed-capacity layout.  Raises ValueError for a batch the reference
+    would reject, RuntimeError for one beyond ``caps``."""
     lib = _lib.load()
     B = len(block_tables)
     if B == 0 or not (B == len(start) == len(new_lens)):
@@ -265,11 +271,15 @@ def plan_step_host(
     layout = np.zeros(_lib.PLAN_LAYOUT_LEN, dtype=np.int32)
     ids_ptr = _ptr(ids) if ids is not None else None
     data_ptr = _ptr(data) if data.size else None
+    caps_ptr = None
+    if caps is not None:
+        caps = np.ascontiguousarray(caps, dtype=np.int32)
+        caps_ptr = _ptr(caps)
 
     def call(buf_ptr, cap):
         return lib.tq_plan_step(B, _ptr(st), _ptr(ql), _ptr(offs32), data_ptr, ids_ptr, block_size,
                                 num_blocks, n_head, vocab_size, target_units, min_split_chunks,
-                                buf_ptr, cap, _ptr(layout))  # fmt: skip
+                                caps_ptr, buf_ptr, cap, _ptr(layout))  # fmt: skip
 
     if out is not None:
         cap = out.numel() if isinstance(out, torch.Tensor) else out.size
@@ -277,14 +287,66 @@ def plan_step_host(
         status = call(buf_ptr, cap)
         if status == _lib.TQ_OK:
             return out, layout
-        if status != _lib.TQ_ERR_CAPACITY:
+        if status != _lib.TQ_ERR_CAPACITY or layout[_lib.PLAN_TOTAL_INTS] == 0:
             _lib.check(status, "tq_plan_step")
     status = call(None, 0)
-    if status != _lib.TQ_ERR_CAPACITY:
+    if status != _lib.TQ_ERR_CAPACITY or layout[_lib.PLAN_TOTAL_INTS] == 0:
         _lib.check(status, "tq_plan_step")
     plan = np.empty(int(layout[_lib.PLAN_TOTAL_INTS]), dtype=np.int32)
     _lib.check(call(_ptr(plan), plan.size), "tq_plan_step")
     return plan, layout
+
+
+class PlanWorkspace:
+    """A fixed-capacity home for one step plan on the device.
+
+    Plans written here use the planner's fixed layout, so every device pointer
+    a step hands to the kernels -- plan regions, split-K scratch -- is the same
+    for every step that fits the capacities.  That is what lets a decode step
+    be captured once as a CUDA graph and replayed (``DecodeGraphRunner``).
+    One workspace holds one step at a time: planning the next step overwrites
+    the device plan (in stream order, after the previous step's kernels).
+    """
+
+    def __init__(self, allocator: "BlockAllocator", max_seqs: int, max_tokens: int | None = None,
+                 max_ctx: int | None = None):  # fmt: skip
+        cfg = allocator.cfg
+        bs = allocator.block_size
+        max_tokens = max_tokens or max_seqs
+        max_ctx = max_ctx or cfg.n_positions
+        max_split = cdiv(cdiv(max_ctx, attention_chunk_keys()), MIN_SPLIT_CHUNKS)
+        max_groups = max_tokens  # a query-row group holds at least one token
+        self.allocator = allocator
+        self.max_seqs, self.max_tokens, self.max_ctx = max_seqs, max_tokens, max_ctx
+        self.caps = np.array([max_seqs, max_tokens, cdiv(max_ctx, bs), max_groups * max_split,
+                              max_tokens, max_tokens * cfg.n_head * max_split], dtype=np.int32)  # fmt: skip
+        # The layout is fixed by the capacities: get it from a one-token plan.
+        _, layout = plan_step_host(bs, allocator.num_blocks, cfg.n_head, [[0]], [0], [1], caps=self.caps)
+        self.layout = layout
+        self.total = int(layout[_lib.PLAN_TOTAL_INTS])
+        dev = allocator.pool.device
+        self.plan = torch.zeros(self.total, dtype=torch.int32, device=dev)
+        n_part = int(self.caps[5])
+        self.partial_ml = torch.empty(2 * n_part, dtype=torch.float32, device=dev)
+        self.partial_acc = torch.empty(n_part * cfg.d_head, dtype=torch.float32, device=dev)
+        self.partial_counters = torch.zeros(n_part, dtype=torch.int32, device=dev)  # kernels leave them 0
+        self._pinned = [torch.empty(self.total, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self._events: list[torch.cuda.Event | None] = [None, None]
+        self._turn = 0
+
+    def pinned_buffer(self) -> tuple[int, torch.Tensor]:
+        """The next pinned staging buffer, once the copy that last read it is done."""
+        i = self._turn
+        self._turn ^= 1
+        if self._events[i] is not None:
+            self._events[i].synchronize()
+        return i, self._pinned[i]
+
+    def mark_copied(self, i: int, stream: torch.cuda.Stream) -> None:
+        ev = self._events[i]
+        if ev is None:
+            ev = self._events[i] = torch.cuda.Event()
+        ev.record(stream)
 
 
 class DevicePagedBatch(BatchedKV):
@@ -295,6 +357,12 @@ class DevicePagedBatch(BatchedKV):
     one batch, as the reference allows).  The step is planned once and reused
     by every layer.  Rows are ragged: row ``n`` of the flattened ``[N, C]``
     activations is the n-th real new token in sequence order.
+
+    With a ``workspace`` the plan goes to the workspace's fixed device buffer
+    and split-K scratch; ``graph_sizing`` then makes the model size every
+    activation and launch for the workspace's capacities (the shape a CUDA
+    graph is captured with), while the kernels read the step's true counts
+    from the device plan.
 
     ``write`` / ``gather`` / ``positions`` / ``mask`` keep the reference's
     ``BatchedKV`` contract for callers written against it; the model in this
@@ -310,6 +378,8 @@ class DevicePagedBatch(BatchedKV):
         new_lens: list[int],
         token_ids: list[int] | None = None,
         stream: torch.cuda.Stream | None = None,
+        workspace: PlanWorkspace | None = None,
+        graph_sizing: bool = False,
     ):
         pool = allocator.pool
         if pool.device.type != "cuda":
@@ -318,6 +388,8 @@ class DevicePagedBatch(BatchedKV):
             raise ValueError("block_tables, start and new_lens must be non-empty and the same length")
         if min(new_lens) < 1:
             raise ValueError("every sequence must feed at least one token")
+        if graph_sizing and workspace is None:
+            raise ValueError("graph_sizing needs a workspace")
         bs = allocator.block_size
         cfg = allocator.cfg
         self.allocator = allocator
@@ -334,22 +406,36 @@ class DevicePagedBatch(BatchedKV):
 
         device = pool.device
         stream = stream or torch.cuda.current_stream(device)
-        ring = _ring(device)
-        slot, host = ring.take(0)
         target = UNITS_PER_SM * sm_count(device)
-        plan, layout = plan_step_host(bs, allocator.num_blocks, cfg.n_head, block_tables, start, new_lens,
-                                      token_ids, cfg.vocab_size if token_ids is not None else 0,
-                                      target, MIN_SPLIT_CHUNKS, out=host)  # fmt: skip
-        total = int(layout[_lib.PLAN_TOTAL_INTS])
-        if plan is not host:  # the plan did not fit: grow the pinned buffer and stage it there
-            slot, host = ring.take(total)
-            host[:total].copy_(torch.from_numpy(plan[:total]))
+        vocab = cfg.vocab_size if token_ids is not None else 0
+        if workspace is None:
+            ring = _ring(device)
+            slot, host = ring.take(0)
+            plan, layout = plan_step_host(bs, allocator.num_blocks, cfg.n_head, block_tables, start, new_lens,
+                                          token_ids, vocab, target, MIN_SPLIT_CHUNKS, out=host)  # fmt: skip
+            total = int(layout[_lib.PLAN_TOTAL_INTS])
+            if plan is not host:  # the plan did not fit: grow the pinned buffer and stage it there
+                slot, host = ring.take(total)
+                host[:total].copy_(torch.from_numpy(plan[:total]))
+            dev = torch.empty(total, dtype=torch.int32, device=device)
+            with torch.cuda.stream(stream):
+                dev.copy_(host[:total], non_blocking=True)
+            ring.mark(slot, stream)
+        else:
+            if workspace.allocator is not allocator:
+                raise ValueError("the workspace belongs to another allocator")
+            slot, host = workspace.pinned_buffer()
+            plan, layout = plan_step_host(bs, allocator.num_blocks, cfg.n_head, block_tables, start, new_lens,
+                                          token_ids, vocab, target, MIN_SPLIT_CHUNKS, out=host,
+                                          caps=workspace.caps)  # fmt: skip
+            total = int(layout[_lib.PLAN_TOTAL_INTS])
+            assert plan is host and total == workspace.total
+            dev = workspace.plan
+            with torch.cuda.stream(stream):
+                dev.copy_(host, non_blocking=True)
+            workspace.mark_copied(slot, stream)
         self.layout = layout
         self.h2d_bytes = 4 * total  # the one host->device copy this step makes
-        dev = torch.empty(total, dtype=torch.int32, device=device)
-        with torch.cuda.stream(stream):
-            dev.copy_(host[:total], non_blocking=True)
-        ring.mark(slot, stream)
         self.plan = dev
         L = layout
         self.num_items = int(L[_lib.PLAN_NUM_ITEMS])
@@ -357,27 +443,41 @@ class DevicePagedBatch(BatchedKV):
         self.num_partials = int(L[_lib.PLAN_NUM_PARTIALS])
         self.table_stride = int(L[_lib.PLAN_TABLE_STRIDE])
         self.split_chunks = int(L[_lib.PLAN_SPLIT_CHUNKS])
+        # What activations and launches are sized for.
+        if graph_sizing:
+            caps = workspace.caps
+            self.rows_alloc, self.seqs_alloc = int(caps[1]), int(caps[0])
+            self.items_alloc, self.partials_alloc = int(caps[3]), int(caps[5])
+        else:
+            self.rows_alloc, self.seqs_alloc = self.N, self.B
+            self.items_alloc, self.partials_alloc = self.num_items, self.num_partials
+        dims = (workspace.caps if workspace is not None else
+                [self.B, self.N, self.table_stride, self.num_items, self.num_combine, self.num_partials])  # fmt: skip
 
         def view(off_key: int, n: int) -> torch.Tensor:
             o = int(L[off_key])
-            return dev[o:o + n]
+            return dev[o:o + int(n)]
 
         self.counts = view(_lib.PLAN_OFF_COUNTS, 4)  # N, items, combine, B
-        self.seq_info = view(_lib.PLAN_OFF_SEQ_INFO, 4 * self.B).view(self.B, 4)
-        self.block_tables_i32 = view(_lib.PLAN_OFF_TABLES, self.B * self.table_stride)
-        self.slot_mapping = view(_lib.PLAN_OFF_SLOTS, self.N)
-        self.row_positions = view(_lib.PLAN_OFF_POSITIONS, self.N)
-        self.token_ids = view(_lib.PLAN_OFF_TOKEN_IDS, self.N) if token_ids is not None else None
+        self.seq_info = view(_lib.PLAN_OFF_SEQ_INFO, 4 * dims[0]).view(-1, 4)
+        self.block_tables_i32 = view(_lib.PLAN_OFF_TABLES, dims[0] * self.table_stride)
+        self.slot_mapping = view(_lib.PLAN_OFF_SLOTS, dims[1])
+        self.row_positions = view(_lib.PLAN_OFF_POSITIONS, dims[1])
+        self.token_ids = view(_lib.PLAN_OFF_TOKEN_IDS, dims[1]) if token_ids is not None else None
         self.last_rows = view(_lib.PLAN_OFF_LAST_ROWS, self.B)
-        self.work_items = view(_lib.PLAN_OFF_ITEMS, 8 * self.num_items)
-        self.combine_list = view(_lib.PLAN_OFF_COMBINE, 4 * self.num_combine)
+        self.work_items = view(_lib.PLAN_OFF_ITEMS, 8 * dims[3])
+        self.combine_list = view(_lib.PLAN_OFF_COMBINE, 4 * dims[4])
         self._dev_ptr = dev.data_ptr()
         self._off = {k: int(L[k]) * 4 for k in range(_lib.PLAN_OFF_COUNTS, _lib.PLAN_LAYOUT_LEN)}
-        if self.num_partials:
+        if workspace is not None:
+            self.partial_ml, self.partial_acc = workspace.partial_ml, workspace.partial_acc
+            self.partial_counters = workspace.partial_counters
+        elif self.num_partials:
             self.partial_ml = torch.empty(2 * self.num_partials, dtype=torch.float32, device=device)
             self.partial_acc = torch.empty(self.num_partials * self.d_head, dtype=torch.float32, device=device)
+            self.partial_counters = torch.zeros(self.num_partials, dtype=torch.int32, device=device)
         else:
-            self.partial_ml = self.partial_acc = None
+            self.partial_ml = self.partial_acc = self.partial_counters = None
         self._positions = self._last_idx = self._mask = self._flat_bt = None
 
     # ---- device-resident counts (for the kernels) ------------------------------------
@@ -393,23 +493,24 @@ class DevicePagedBatch(BatchedKV):
         _lib.check(lib.tq_kv_write(self.pool.data_ptr(), self.allocator.num_blocks, self.n_layer,
                                    self.n_head, self.block_size, self.d_head, layer, qkv.data_ptr(),
                                    qkv.stride(0), k_col, v_col, self.slot_mapping.data_ptr(),
-                                   self.count_ptr(0), self.N, stream), "tq_kv_write")  # fmt: skip
+                                   self.count_ptr(0), self.rows_alloc, stream), "tq_kv_write")  # fmt: skip
 
     def attend_rows(self, layer: int, q: torch.Tensor, out: torch.Tensor, stream: int) -> None:
         """``out[n, h*d:(h+1)*d] = softmax(q_n,h . K / sqrt(d)) V`` over keys
         0..position(n) of row n's sequence, read in place from the pool
         (replaces tokquay/kv_cache.py:234-242 + tokquay/model.py:94-96).
-        ``q`` rows hold head h at columns ``h*d``; row stride is ``q.stride(0)``."""
+        ``q`` rows hold head h at columns ``h*d``; row stride is ``q.stride(0)``.
+        Long contexts are split over several warps and merged in the same launch."""
         lib = _lib.load()
         pm = self.partial_ml.data_ptr() if self.partial_ml is not None else None
         pa = self.partial_acc.data_ptr() if self.partial_acc is not None else None
+        pc = self.partial_counters.data_ptr() if self.partial_counters is not None else None
         _lib.check(lib.tq_paged_attention(
             out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), self.pool.data_ptr(),
             self.allocator.num_blocks, self.n_layer, self.n_head, self.block_size, self.d_head, layer,
             self.block_tables_i32.data_ptr(), self.table_stride, self.work_items.data_ptr(),
-            self.count_ptr(1), self.num_items, pm, pa,
-            self.combine_list.data_ptr() if self.num_combine else None, self.count_ptr(2),
-            self.num_combine, 1.0 / math.sqrt(self.d_head), stream), "tq_paged_attention")  # fmt: skip
+            self.count_ptr(1), self.items_alloc, pm, pa, pc, self.partials_alloc,
+            1.0 / math.sqrt(self.d_head), stream), "tq_paged_attention")  # fmt: skip
 
     # ---- reference BatchedKV contract (not used by this package's model) ---------------
     @property

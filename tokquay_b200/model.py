@@ -75,13 +75,24 @@ class GPT2(nn.Module):
         # launching stream; ``kernel_launches`` counts this package's kernel
         # launches (GEMMs and other torch ops are not counted).
         self.attention_events: list | None = None
+        self.attention_event_prelude = None  # optional callable run before each start event
         self.kernel_launches = 0
         self.last_h2d_bytes = 0  # plan bytes the last forward's batch copied to the device
+        self.graph_runner = None  # set by use_cuda_graphs()
         self.cfg = cfg or GPT2Config()
         self.wte = nn.Embedding(self.cfg.vocab_size, self.cfg.n_embd)
         self.wpe = nn.Embedding(self.cfg.n_positions, self.cfg.n_embd)
         self.h = nn.ModuleList(Block(self.cfg) for _ in range(self.cfg.n_layer))
         self.ln_f = nn.LayerNorm(self.cfg.n_embd, eps=self.cfg.layer_norm_eps)
+
+    def use_cuda_graphs(self, allocator, buckets=None, max_ctx: int | None = None):
+        """Replay decode steps over ``allocator``'s pool as captured CUDA graphs
+        (``paged_forward`` then uses them for every all-decode batch that fits a
+        bucket).  Returns the runner; graphs are captured on first use."""
+        from tokquay_b200.graphs import DEFAULT_BUCKETS, DecodeGraphRunner
+
+        self.graph_runner = DecodeGraphRunner(self, allocator, buckets or DEFAULT_BUCKETS, max_ctx)
+        return self.graph_runner
 
     # ---- reference-shaped entry point --------------------------------------------------
     @torch.no_grad()
@@ -119,7 +130,12 @@ class GPT2(nn.Module):
         dev = batch.pool.device
         stream = torch.cuda.current_stream(dev).cuda_stream
         self.last_h2d_bytes = batch.h2d_bytes
-        C, eps, N, B = cfg.n_embd, cfg.layer_norm_eps, batch.N, batch.B
+        # Activations and launches are sized for rows_alloc / seqs_alloc: the
+        # step's own N and B, or a workspace's capacities when the step is being
+        # captured as a CUDA graph (the kernels read the true counts on the device).
+        C, eps, N, B = cfg.n_embd, cfg.layer_norm_eps, batch.rows_alloc, batch.seqs_alloc
+        if not last_only and (N, B) != (batch.N, batch.B):
+            raise ValueError("all-position logits need a batch sized to its own rows")
         n_ptr, b_ptr = batch.count_ptr(0), batch.count_ptr(3)
         x = torch.empty(N, C, dtype=torch.float32, device=dev)
         xa = torch.empty(N, C, dtype=torch.float32, device=dev)
@@ -138,6 +154,8 @@ class GPT2(nn.Module):
             a = torch.empty(N, C, dtype=torch.float32, device=dev)
             if self.attention_events is not None:
                 ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                if self.attention_event_prelude is not None:
+                    self.attention_event_prelude()
                 ev0.record()
                 batch.attend_rows(i, qkv, a, stream)
                 ev1.record()
@@ -166,8 +184,8 @@ class GPT2(nn.Module):
                 nxt.bias.data_ptr() if nxt is not None else None, eps, C, rows_ptr, rows, stream),
                 "tq_bias_residual_layernorm")  # fmt: skip
 
-        # embed + per layer (kv_write, attention [+ combine], 2x bias_residual, gelu) + final LN
-        self.kernel_launches += 2 + cfg.n_layer * (5 + (1 if batch.num_combine else 0))
+        # embed + per layer (kv_write, attention, 2x bias_residual, gelu) + final LN
+        self.kernel_launches += 2 + cfg.n_layer * 5
         if last_only:
             xf = torch.empty(B, C, dtype=torch.float32, device=dev)
             sel_ptr = None if rows == B else batch.last_rows.data_ptr()
