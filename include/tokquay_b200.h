@@ -153,6 +153,33 @@ TQ_API int tq_paged_attention(float* out, int64_t out_row_stride, const float* q
                        float* partial_ml, float* partial_acc, int32_t* partial_counters,
                        int32_t max_partials, float scale, void* stream);
 
+/* Split-K partials tq_paged_attention_noalloc can hold.  Its scratch,
+ * TQ_NOALLOC_MAX_PARTIALS * (1 + 2 + 64) * 4 bytes (about 8.6 MB), is a fixed
+ * array inside the library on every GPU that loads it, kept until exit. */
+#define TQ_NOALLOC_MAX_PARTIALS 32768
+
+/* No counterpart in the reference (Tokquay allocates freely through torch).
+ * tq_paged_attention for callers that cannot allocate device memory or hand
+ * over scratch: a host runtime that passes this library only the tensors it
+ * already owns (a serving process held to a fixed memory budget, an embedding
+ * without its own device allocator).  Same arguments and result as
+ * tq_paged_attention, minus the scratch pointers; num_partials is the plan's
+ * TQ_PLAN_NUM_PARTIALS.  The split-K scratch is a library-owned array, so the
+ * call allocates nothing; a plan needing more than TQ_NOALLOC_MAX_PARTIALS
+ * partials is rejected with TQ_ERR_CAPACITY before anything is launched.
+ * The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress): make that first call before any stream capture.
+ * Every call on a device shares the one array and clears the split counters
+ * it uses before its kernel runs, so calls that overlap on the GPU (other
+ * streams, other threads) race: issue them one after another. */
+TQ_API int tq_paged_attention_noalloc(float* out, int64_t out_row_stride, const float* q,
+                                      int64_t q_row_stride, const float* pool, int64_t num_blocks,
+                                      int32_t n_layer, int32_t n_head, int32_t block_size,
+                                      int32_t head_dim, int32_t layer, const int32_t* block_tables,
+                                      int32_t table_stride, const int32_t* work_items,
+                                      const int32_t* d_num_items, int32_t max_items,
+                                      int32_t num_partials, float scale, void* stream);
+
 /* x[r] = wte[ids[r]] + wpe[pos[r]];  xa[r] = LayerNorm(x[r]; ln_w, ln_b, eps).
  * n_embd must be a multiple of 128 and at most 1024. */
 TQ_API int tq_embed_layernorm(float* x, float* xa, const int32_t* ids, const int32_t* pos,

@@ -59,3 +59,8 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     monkeypatch.setattr(_lib, "_lib", None)
     with pytest.raises(_lib.NativeLibraryMissing):
         _lib.load(tmp_path / "nope.so")
+
+
+def test_noalloc_limit_matches_the_header():
+    m = re.search(r"#define TQ_NOALLOC_MAX_PARTIALS (\d+)", HEADER.read_text())
+    assert int(m.group(1)) == _lib.NOALLOC_MAX_PARTIALS

@@ -56,6 +56,9 @@ SIGNATURES: dict[str, tuple] = {
     "tq_paged_attention": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32,
                                    c_int32, c_int32, _P, c_int32, _P, _P, c_int32, _P, _P, _P, c_int32,
                                    c_float, _P]),
+    "tq_paged_attention_noalloc": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32,
+                                           c_int32, c_int32, _P, c_int32, _P, _P, c_int32, c_int32, c_float,
+                                           _P]),
     "tq_embed_layernorm": (c_int, [_P, _P, _P, _P, _P, _P, c_int32, c_int32, _P, _P, c_float,
                                    c_int32, _P, c_int32, _P]),
     "tq_bias_residual_layernorm": (c_int, [_P, _P, _P, _P, _P, _P, c_float, c_int32, _P, c_int32, _P]),
@@ -64,6 +67,10 @@ SIGNATURES: dict[str, tuple] = {
 }
 
 EXPECTED_ABI = 3
+
+# Split-K partials the no-allocation attention entry point can hold
+# (TQ_NOALLOC_MAX_PARTIALS in include/tokquay_b200.h).
+NOALLOC_MAX_PARTIALS = 32768
 
 _lib: ctypes.CDLL | None = None
 _lock = threading.Lock()

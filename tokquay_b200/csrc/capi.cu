@@ -238,6 +238,123 @@ int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64
   return check_launch("paged_attention");
 }
 
+}  // extern "C"
+
+// ---- paged attention whose split-K scratch lives inside this library -------
+//
+// tq_paged_attention needs caller-owned split-K scratch.  Some callers cannot
+// provide it: a host runtime that gives this library only the tensors it
+// already owns and forbids side allocations (a serving process working inside
+// a fixed memory budget, or an embedding that has no device allocator of its
+// own at the point it runs attention).  tq_paged_attention_noalloc serves
+// them: the scratch is the file-scope array below, which every GPU that loads
+// this library holds until the process exits (about 8.6 MB), so the entry
+// point itself never allocates.  Host code must not pass the array's name to
+// a kernel -- on the host that name is only a stand-in for the symbol -- so
+// its device address is looked up once per device with cudaGetSymbolAddress.
+namespace tq {
+namespace {
+
+constexpr int kNoAllocMaxPartials = TQ_NOALLOC_MAX_PARTIALS;
+constexpr size_t kNoAllocCounterBytes = (size_t)kNoAllocMaxPartials * sizeof(int);        // 128 KiB
+constexpr size_t kNoAllocMlBytes = (size_t)kNoAllocMaxPartials * 2 * sizeof(float);       // 256 KiB
+constexpr size_t kNoAllocAccBytes = (size_t)kNoAllocMaxPartials * kHeadDim * sizeof(float);  // 8 MiB
+
+// [counters | (m, l) pairs | accumulators]; each region starts 256-byte aligned.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocCounterBytes + kNoAllocMlBytes +
+                                                                 kNoAllocAccBytes];
+
+unsigned char* g_noalloc_base[kMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+// Device address of g_noalloc_scratch on the current device, looked up on the
+// first call per device.
+int noalloc_scratch(unsigned char** base) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(TQ_ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_base[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || ptr == nullptr)
+      return set_error(TQ_ERR_CUDA, "cudaGetSymbolAddress(split-K scratch): %s", cudaGetErrorString(e));
+    g_noalloc_base[dev] = static_cast<unsigned char*>(ptr);
+  }
+  *base = g_noalloc_base[dev];
+  return TQ_OK;
+}
+
+}  // namespace
+}  // namespace tq
+
+extern "C" {
+
+int tq_paged_attention_noalloc(float* out, int64_t out_row_stride, const float* q,
+                               int64_t q_row_stride, const float* pool, int64_t num_blocks,
+                               int32_t n_layer, int32_t n_head, int32_t block_size,
+                               int32_t head_dim, int32_t layer, const int32_t* block_tables,
+                               int32_t table_stride, const int32_t* work_items,
+                               const int32_t* d_num_items, int32_t max_items,
+                               int32_t num_partials, float scale, void* stream) {
+  int st = check_pool(pool, num_blocks, n_layer, n_head, block_size, head_dim, layer);
+  if (st) return st;
+  if (max_items < 0 || num_partials < 0) return set_error(TQ_ERR_INVALID, "negative capacity");
+  if (num_partials > kNoAllocMaxPartials)
+    return set_error(TQ_ERR_CAPACITY,
+                     "the plan needs %d split-K partials but the no-allocation entry point holds at "
+                     "most %d; plan with fewer splits or use tq_paged_attention with your own scratch",
+                     num_partials, kNoAllocMaxPartials);
+  if (max_items == 0) return TQ_OK;
+  if (!out || !q || !block_tables || !work_items || !d_num_items)
+    return set_error(TQ_ERR_INVALID, "out, q, block_tables and work items must not be NULL");
+  if (!aligned(q, 16) || q_row_stride % 4)
+    return set_error(TQ_ERR_INVALID, "q rows must be 16-byte aligned");
+  if (!aligned(out, 16) || out_row_stride % 4)
+    return set_error(TQ_ERR_INVALID, "out rows must be 16-byte aligned");
+  if (!aligned(work_items, 16)) return set_error(TQ_ERR_INVALID, "work items must be 16-byte aligned");
+  if (table_stride < 0) return set_error(TQ_ERR_INVALID, "table_stride must be >= 0");
+  if (!(scale > 0.f) || !std::isfinite(scale)) return set_error(TQ_ERR_INVALID, "bad scale");
+  int sms = 0;
+  if ((st = device_setup(&sms))) return st;
+  unsigned char* base = nullptr;
+  if ((st = noalloc_scratch(&base))) return st;
+  const cudaStream_t s = (cudaStream_t)stream;
+  // The split counters must start at zero.  A completed launch leaves them at
+  // zero, but one that gave up early (a flagged device error) may not: clear
+  // the ones this plan uses.  The other regions are fully written before read.
+  if (num_partials > 0) {
+    const cudaError_t e = cudaMemsetAsync(base, 0, (size_t)num_partials * sizeof(int), s);
+    if (e != cudaSuccess)
+      return set_error(TQ_ERR_CUDA, "clearing split-K counters: %s", cudaGetErrorString(e));
+  }
+  AttnParams p;
+  p.out = out;
+  p.out_stride = out_row_stride;
+  p.q = q;
+  p.q_stride = q_row_stride;
+  p.pool = pool;
+  p.num_blocks = num_blocks;
+  p.n_layer = n_layer;
+  p.n_head = n_head;
+  p.block_size = block_size;
+  p.log2_bs = log2_exact(block_size);
+  p.layer = layer;
+  p.tables = block_tables;
+  p.table_stride = table_stride;
+  p.items = reinterpret_cast<const WorkItem*>(work_items);
+  p.n_items = d_num_items;
+  p.part_cnt = reinterpret_cast<int*>(base);
+  p.part_ml = reinterpret_cast<float*>(base + kNoAllocCounterBytes);
+  p.part_acc = reinterpret_cast<float*>(base + kNoAllocCounterBytes + kNoAllocMlBytes);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  const int64_t units = (int64_t)max_items * n_head;
+  const int grid = (int)std::min<int64_t>((units + kAttnWarps - 1) / kAttnWarps, sms);
+  paged_attention_kernel<<<grid, kAttnWarps * 32, kAttnSmemBytes, s>>>(p);
+  return check_launch("paged_attention_noalloc");
+}
+
 int tq_embed_layernorm(float* x, float* xa, const int32_t* ids, const int32_t* pos,
                        const float* wte, const float* wpe, int32_t vocab_size,
                        int32_t n_positions, const float* ln_w, const float* ln_b, float eps,
