@@ -175,6 +175,19 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------ setup
+def workload_spec(args) -> dict:
+    """The workload, with the --num-seqs / --pool-gb overrides used for small
+    profiling cases of the same shape (the defaults are the BASELINE configs)."""
+    spec = dict(WORKLOADS[args.workload])
+    if args.num_seqs:
+        spec["n_seqs"] = args.num_seqs
+        spec["desc"] += f" [num_seqs overridden: {args.num_seqs}]"
+    if args.pool_gb:
+        spec["pool_gb"] = args.pool_gb
+        spec["desc"] += f" [pool overridden: {args.pool_gb} GB]"
+    return spec
+
+
 def make_model(device, seed=0):
     from tokquay_b200 import GPT2, GPT2Config
     from tokquay_b200 import workloads as W
@@ -194,7 +207,9 @@ def make_allocator(spec, cfg, device):
     from tokquay_b200 import BlockAllocator
 
     bs = spec["block_size"]
-    if "num_blocks" in spec:
+    if spec.get("pool_gb"):
+        nb = int(spec["pool_gb"] * 1e9 // (cfg.n_layer * 2 * cfg.n_head * bs * cfg.d_head * 4))
+    elif "num_blocks" in spec:
         nb = spec["num_blocks"]
     else:
         per_block = cfg.n_layer * 2 * cfg.n_head * bs * cfg.d_head * 4
@@ -231,10 +246,11 @@ def attn_bytes(ctx_list, n_head, d, num_partials):
 
 # ------------------------------------------------------------------------------ our arm
 def run_ours(args, world, rank, local):
+    from tokquay_b200 import kv_cache as KV
     from tokquay_b200 import paged_forward
     from tokquay_b200.kv_cache import DevicePagedBatch, plan_step_host
 
-    spec = WORKLOADS[args.workload]
+    spec = workload_spec(args)
     device = torch.device("cuda", local)
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.set_float32_matmul_precision("highest")
@@ -260,8 +276,8 @@ def run_ours(args, world, rank, local):
         tables = [list(s.block_table) for s in seqs]
         if runner:
             plan, _ = plan_step_host(a.block_size, a.num_blocks, cfg.n_head, tables, starts, [1] * B, ids,
-                                     cfg.vocab_size, 16 * torch.cuda.get_device_properties(device).multi_processor_count,
-                                     caps=caps)  # fmt: skip
+                                     cfg.vocab_size, KV.UNITS_PER_SM * KV.sm_count(device),
+                                     KV.MIN_SPLIT_CHUNKS, caps=caps)  # fmt: skip
             plans.append(torch.from_numpy(plan).to(device))
         else:
             batches.append(DevicePagedBatch(a, tables, starts, [1] * B, ids))
@@ -486,7 +502,7 @@ def cpu_oracle_rate(spec, n_seqs, steps, warmup, seed=2, budget_s=None):
 def run_reference(args, world, rank):
     if rank != 0:
         return None
-    spec = WORKLOADS[args.workload]
+    spec = workload_spec(args)
     # Each step is a bounded sample: a decode step over a subset of the sequences.
     n = min(spec["n_seqs"], 16)
     t0 = time.perf_counter()
@@ -521,6 +537,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graphs", action="store_true", help="launch every kernel from Python (no CUDA graphs)")
+    ap.add_argument("--num-seqs", type=int, default=0, help="override the workload's sequence count (profiling)")
+    ap.add_argument("--pool-gb", type=float, default=0, help="override the KV pool size in GB (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")
@@ -531,7 +549,7 @@ def main():
     else:
         res = run_ours(args, world, rank, local)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            rate, sample, threads = cpu_oracle_rate(WORKLOADS[args.workload], 16, 2, 1)
+            rate, sample, threads = cpu_oracle_rate(workload_spec(args), 16, 2, 1)
             res["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
                                    "sample": sample}  # fmt: skip
     if rank == 0 and res is not None:

@@ -76,6 +76,8 @@ def simulate_copies(p, bs, num_blocks, n_head):
         need = cdiv(ctx, bs)
         kend = min(pos0 + nrows, cend * ATTN_CHUNK)
         assert kend <= ctx
+        # the kernel holds one item's block ids in two registers per lane
+        assert (kend - 1) // bs - (cbeg * ATTN_CHUNK) // bs + 1 <= 64
         for c in range(cbeg, cend):
             key0 = c * ATTN_CHUNK
             nkeys = min(ATTN_CHUNK, kend - key0)

@@ -355,6 +355,18 @@ int tq_paged_attention_noalloc(float* out, int64_t out_row_stride, const float* 
   return check_launch("paged_attention_noalloc");
 }
 
+#ifdef TQ_ATTN_TRACE
+// Tuning builds only (not part of the ABI): copy the per-warp timeline of the
+// last attention launch to `host` ([n_warps][16] uint64).
+TQ_API int tq_debug_attention_trace(unsigned long long* host, int32_t n_warps) {
+  const int n = std::min<int>(n_warps, kTraceWarps);
+  const cudaError_t e =
+      cudaMemcpyFromSymbol(host, g_attn_trace, (size_t)n * kTraceSlots * sizeof(unsigned long long));
+  if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "trace read: %s", cudaGetErrorString(e));
+  return TQ_OK;
+}
+#endif
+
 int tq_embed_layernorm(float* x, float* xa, const int32_t* ids, const int32_t* pos,
                        const float* wte, const float* wpe, int32_t vocab_size,
                        int32_t n_positions, const float* ln_w, const float* ln_b, float eps,

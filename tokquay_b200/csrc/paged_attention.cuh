@@ -54,7 +54,29 @@ constexpr int kMaxRows = TQ_ATTN_MAX_ROWS;   // query rows per work item
 constexpr int kStages = TQ_ATTN_STAGES;      // stages per warp
 constexpr int kAttnWarps = TQ_ATTN_WARPS;    // independent warps per CTA
 constexpr int kPasses = kChunk / 8;          // 8 keys per pass (lane = key group x dim quarter)
+constexpr int kUnitBlocks = 64;              // most blocks one work item's key range may span
 static_assert(kChunk == 16 || kChunk == 32, "chunk of 16 or 32 keys");
+
+#ifdef TQ_ATTN_TRACE
+// Tuning builds only: per-warp timeline of the last launch, [warp][16] =
+// {start ns, first data ns, end ns, wait, compute, finish, refill, chunks,
+//  issue:block-id wait, issue:copies, advance, finish:reduce+store,
+//  finish:fence+atomic, finish:merge, units, -} (cycles unless noted).
+// Read back with tq_debug_attention_trace.
+constexpr int kTraceWarps = 8192;
+constexpr int kTraceSlots = 16;
+__device__ unsigned long long g_attn_trace[kTraceWarps * kTraceSlots];
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define TQ_TRACE(...) __VA_ARGS__
+#define TQ_TRACE_ARG(x) x
+#else
+#define TQ_TRACE(...)
+#define TQ_TRACE_ARG(x) nullptr
+#endif
 
 constexpr int kRowBytes = kHeadDim * 4;                        // 256
 constexpr int kKBytes = kChunk * kRowBytes;                    // 8 KiB
@@ -260,15 +282,18 @@ __device__ __forceinline__ void attend_chunk(const float* __restrict__ K, const 
 // nsplit - 1 reads the partials back through L2 and resets the counter to 0,
 // so the scratch is ready for the next launch without a memset.
 __device__ __forceinline__ void merge_if_last(const AttnParams& p, const WorkItem& it, int r, int h,
-                                              int nsplit, int lane) {
+                                              int nsplit, int lane, long long* tr_sub) {
   const size_t idx0 = (size_t)it.part + ((size_t)r * p.n_head + h) * nsplit;
   __syncwarp();
+  TQ_TRACE(long long tm0 = clock64();)
   int last = 0;
   if (lane == 0) {
     __threadfence();  // this split's partial is visible before the count says so
     last = atomicAdd(p.part_cnt + idx0, 1) == nsplit - 1;
   }
-  if (!__shfl_sync(kFullMask, last, 0)) return;
+  last = __shfl_sync(kFullMask, last, 0);
+  TQ_TRACE(if (lane == 0) tr_sub[4] += clock64() - tm0; tm0 = clock64();)
+  if (!last) return;
   __threadfence();  // and every other split's partial is visible to this warp
   float mmax = -INFINITY;
   for (int s = lane; s < nsplit; s += 32) mmax = fmaxf(mmax, __ldcg(p.part_ml + 2 * (idx0 + s)));
@@ -286,6 +311,7 @@ __device__ __forceinline__ void merge_if_last(const AttnParams& p, const WorkIte
   reinterpret_cast<float2*>(p.out + (size_t)(it.row0 + r) * p.out_stride + h * kHeadDim)[lane] =
       make_float2(o.x * inv, o.y * inv);
   if (lane == 0) p.part_cnt[idx0] = 0;
+  TQ_TRACE(if (lane == 0) tr_sub[5] += clock64() - tm0;)
 }
 
 // End of a unit: sum l and the accumulators over the 8 key groups (lanes
@@ -293,7 +319,8 @@ __device__ __forceinline__ void merge_if_last(const AttnParams& p, const WorkIte
 // each row -- normalised output, or a split-K partial.
 __device__ __forceinline__ void finish_rows(const AttnParams& p, const WorkItem& it, int h, int lane,
                                             const float (&m)[kMaxRows], float (&lsum)[kMaxRows],
-                                            float4 (&acc)[kMaxRows][4]) {
+                                            float4 (&acc)[kMaxRows][4], long long* tr_sub) {
+  TQ_TRACE(const long long tf0 = clock64(); if (lane == 0) tr_sub[6] += 1;)
   const int qq = lane & 3, rot = lane_rot(lane);
   const int split = it.split_nsplit & 0xffff;
   const int nsplit = it.split_nsplit >> 16;
@@ -347,7 +374,8 @@ __device__ __forceinline__ void finish_rows(const AttnParams& p, const WorkItem&
           }
         }
       }
-      if (nsplit > 1) merge_if_last(p, it, r, h, nsplit, lane);
+      TQ_TRACE(if (lane == 0) tr_sub[3] += clock64() - tf0;)
+      if (nsplit > 1) merge_if_last(p, it, r, h, nsplit, lane, tr_sub);
     }
   }
 }
@@ -362,7 +390,16 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) paged_attention_kernel(con
   const int H = p.n_head;
   const int n_units = *p.n_items * H;
   const int TW = gridDim.x * kAttnWarps;
-  const int first_unit = blockIdx.x * kAttnWarps + warp;
+  // Units are visited in snake order: round r gives this warp unit
+  // r*TW + w on even rounds and r*TW + TW-1-w on odd ones.  The planner sorts
+  // items longest first, so each warp gets a long and a short unit in every
+  // pair of rounds and all warps finish together.
+  const int wslot = blockIdx.x * kAttnWarps + warp;
+  auto unit_of = [&](int round) { return round * TW + ((round & 1) ? TW - 1 - wslot : wslot); };
+  const int first_unit = wslot;
+  TQ_TRACE(const int gw = first_unit; unsigned long long tr_start = global_ns(), tr_first = 0;
+           long long tr_wait = 0, tr_comp = 0, tr_fin = 0, tr_refill = 0, tr_chunks = 0;
+           long long tr_sub[8] = {0, 0, 0, 0, 0, 0, 0, 0};)
   if (first_unit >= n_units) return;  // warp-uniform; warps never synchronise with each other
 
   if (lane == 0) {
@@ -375,20 +412,38 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) paged_attention_kernel(con
   // Block ids of the next chunk to issue are loaded one chunk ahead (lane i
   // holds block i of the chunk) and the next unit's work item one unit ahead,
   // so those global loads overlap a chunk of compute instead of stalling it.
+  // A unit's block ids (at most kUnitBlocks; the planner keeps units that
+  // short) live in two registers per lane: lane i holds blocks kb0+i and
+  // kb0+32+i of the unit's key range.  They are loaded one unit ahead, and
+  // the work item two units ahead, so neither load sits on the path between
+  // two chunks.
+  int p_round = 0;
   int p_unit = first_unit;
   WorkItem p_it = item_from_lanes(item_lane_load(p, p_unit, n_units, lane));
   int p_chunk = p_it.cbeg;
-  int nx_item = item_lane_load(p, p_unit + TW, n_units, lane);
-  bool p_live = true;
-  int pf_blk = 0;
-  auto prefetch_blocks = [&]() {
-    const ChunkSpan sp = chunk_span(p, p_it, p_chunk);
-    const int* tbl = p.tables + (size_t)p_it.seq * p.table_stride;
-    pf_blk = lane < sp.nblk ? __ldg(tbl + sp.kb0 + lane) : 0;
+  int pf_a = 0, pf_b = 0;   // current unit's block ids
+  int nx_a = 0, nx_b = 0;   // next unit's block ids (in flight)
+  auto load_unit_blocks = [&](const WorkItem& w, bool valid, int& a, int& b) {
+    if (!valid) return;
+    const int kb0 = (w.cbeg * kChunk) >> p.log2_bs;
+    const int kend = min(w.pos0 + w.nrows, w.cend * kChunk);
+    const int n = ((kend - 1) >> p.log2_bs) - kb0 + 1;
+    const int* tbl = p.tables + (size_t)w.seq * p.table_stride + kb0;
+    a = lane < n ? __ldg(tbl + lane) : 0;
+    b = lane + 32 < n ? __ldg(tbl + 32 + lane) : 0;
   };
-  prefetch_blocks();
+  load_unit_blocks(p_it, true, pf_a, pf_b);
+  bool nx_valid = unit_of(1) < n_units;
+  WorkItem nx_it = item_from_lanes(item_lane_load(p, unit_of(1), n_units, lane));
+  load_unit_blocks(nx_it, nx_valid, nx_a, nx_b);
+  int nx2_item = item_lane_load(p, unit_of(2), n_units, lane);
+  bool p_live = true;
   int issued = 0, consumed = 0;
 
+  // Issue chunk p_chunk of the current unit into the next stage.  Each lane
+  // describes one copy (K or V rows of one block, or a q row), and the copies
+  // go out as one warp-wide cp.async.bulk: the TMA issue cost is paid per warp
+  // instruction, not per copy.
   auto issue = [&]() {
     const int s = issued % kStages;
     unsigned char* stage = wsm + s * kStageBytes;
@@ -396,70 +451,96 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) paged_attention_kernel(con
     const ChunkSpan sp = chunk_span(p, p_it, p_chunk);
     const bool first = (p_chunk == p_it.cbeg);
     const int bs = p.block_size;
-    uint32_t bytes = first ? (uint32_t)p_it.nrows * kRowBytes : 0u;
-    for (int i = 0; i < sp.nblk; ++i) {
-      const long long blk = __shfl_sync(kFullMask, pf_blk, i);
-      if (blk < 0 || blk >= p.num_blocks) continue;
-      const int rows = bs <= kChunk ? min(bs, sp.key0 + sp.nkeys - (sp.kb0 + i) * bs) : sp.nkeys;
-      bytes += 2u * rows * kRowBytes;
-    }
+    const int h = p_unit % H;
+    const int unit_kb0 = (p_it.cbeg * kChunk) >> p.log2_bs;
+    const int n_kv = 2 * sp.nblk;
+    const int n_desc = n_kv + (first ? p_it.nrows : 0);
     const uint32_t sK = smem_addr(stage);
-    const uint32_t sV = sK + kKBytes;
-    const uint32_t sQ = sK + 2 * kKBytes;
+    const size_t kv_stride = (size_t)H * bs * kHeadDim;  // K tile -> V tile
+    TQ_TRACE(long long ti0 = clock64();)
+    // Descriptor d: copies `bytes` from `src` to shared address `dst`.
+    auto describe = [&](int d, const float*& src, uint32_t& dst, uint32_t& bytes) {
+      // Every lane shuffles (the source lane varies per lane).
+      const int rel = (sp.kb0 - unit_kb0) + min(d, max(n_kv - 1, 0)) / 2;
+      const int a = __shfl_sync(kFullMask, pf_a, rel & 31);
+      const int b = __shfl_sync(kFullMask, pf_b, rel & 31);
+      bytes = 0;
+      if (d < n_kv) {
+        const long long blk = rel < 32 ? a : b;
+        if (blk < 0 || blk >= p.num_blocks) {
+          raise_device_error(TQ_DEVERR_BAD_BLOCK);
+          return;
+        }
+        const int kv = d & 1;
+        if (bs <= kChunk) {
+          const int kb = sp.kb0 + (d >> 1);
+          const int rows = min(bs, sp.key0 + sp.nkeys - kb * bs);
+          src = p.pool + pool_tile_offset(p, blk, 0, h) + kv * kv_stride;
+          dst = sK + kv * kKBytes + (uint32_t)(kb * bs - sp.key0) * kRowBytes;
+          bytes = rows * kRowBytes;
+        } else {
+          src = p.pool + pool_tile_offset(p, blk, 0, h) + kv * kv_stride +
+                (size_t)(sp.key0 & (bs - 1)) * kHeadDim;
+          dst = sK + kv * kKBytes;
+          bytes = sp.nkeys * kRowBytes;
+        }
+      } else if (d < n_desc) {
+        const int r = d - n_kv;
+        src = p.q + (size_t)(p_it.row0 + r) * p.q_stride + h * kHeadDim;
+        dst = sK + 2 * kKBytes + r * kRowBytes;
+        bytes = kRowBytes;
+      }
+    };
+    uint32_t total = 0;
+    for (int base = 0; base < n_desc; base += 32) {
+      const float* src = nullptr;
+      uint32_t dst = 0, bytes = 0;
+      describe(base + lane, src, dst, bytes);
+      total += __reduce_add_sync(kFullMask, bytes);
+    }
+    TQ_TRACE(if (lane == 0) tr_sub[0] += clock64() - ti0; ti0 = clock64();)
     if (lane == 0) {
       if (first) {  // the consumer picks the unit's work item up from here
         StageHeader* hd = reinterpret_cast<StageHeader*>(stage + 2 * kKBytes + kQBytes);
         hd->it = p_it;
-        hd->h = p_unit % H;
+        hd->h = h;
         hd->c = p_chunk;
       }
-      if (issued >= kStages) fence_proxy_async_smem();  // the warp has read this stage before
-      mbar_arrive_expect_tx(bar, bytes);
-      if (first) {
-        for (int r = 0; r < p_it.nrows; ++r)
-          bulk_copy_g2s(sQ + r * kRowBytes,
-                        p.q + (size_t)(p_it.row0 + r) * p.q_stride + (p_unit % H) * kHeadDim, kRowBytes,
-                        bar);
-      }
+      // A reused stage needs no proxy fence: every lane's reads of it fed the
+      // arithmetic that preceded the warp's __syncwarp, so they are complete
+      // before the copies below are issued (the completion-before-reissue
+      // argument TMA pipelines rely on).
+      mbar_arrive_expect_tx(bar, total);
     }
-    const size_t kv_stride = (size_t)H * bs * kHeadDim;  // K tile -> V tile
-    for (int i = 0; i < sp.nblk; ++i) {
-      const long long blk = __shfl_sync(kFullMask, pf_blk, i);
-      if (blk < 0 || blk >= p.num_blocks) {
-        if (lane == 0) raise_device_error(TQ_DEVERR_BAD_BLOCK);
-        continue;
-      }
-      if (lane == 0) {
-        if (bs <= kChunk) {
-          const int kb = sp.kb0 + i;
-          const int rows = min(bs, sp.key0 + sp.nkeys - kb * bs);
-          const float* src = p.pool + pool_tile_offset(p, blk, 0, p_unit % H);
-          const uint32_t dst_off = (uint32_t)(kb * bs - sp.key0) * kRowBytes;
-          bulk_copy_g2s(sK + dst_off, src, rows * kRowBytes, bar);
-          bulk_copy_g2s(sV + dst_off, src + kv_stride, rows * kRowBytes, bar);
-        } else {
-          const float* src = p.pool + pool_tile_offset(p, blk, 0, p_unit % H) +
-                             (size_t)(sp.key0 & (bs - 1)) * kHeadDim;
-          bulk_copy_g2s(sK, src, sp.nkeys * kRowBytes, bar);
-          bulk_copy_g2s(sV, src + kv_stride, sp.nkeys * kRowBytes, bar);
-        }
-      }
+    __syncwarp();
+    for (int base = 0; base < n_desc; base += 32) {
+      const float* src = nullptr;
+      uint32_t dst = 0, bytes = 0;
+      describe(base + lane, src, dst, bytes);
+      if (bytes) bulk_copy_g2s(dst, src, bytes, bar);
     }
+    TQ_TRACE(if (lane == 0) tr_sub[1] += clock64() - ti0;)
     ++issued;
   };
 
   auto advance = [&]() {
+    TQ_TRACE(long long ta0 = clock64();)
     if (++p_chunk == p_it.cend) {
-      p_unit += TW;
+      p_unit = unit_of(++p_round);
       if (p_unit < n_units) {
-        p_it = item_from_lanes(nx_item);
+        p_it = nx_it;
+        pf_a = nx_a;
+        pf_b = nx_b;
         p_chunk = p_it.cbeg;
-        nx_item = item_lane_load(p, p_unit + TW, n_units, lane);
+        nx_valid = unit_of(p_round + 1) < n_units;
+        nx_it = item_from_lanes(nx2_item);
+        load_unit_blocks(nx_it, nx_valid, nx_a, nx_b);
+        nx2_item = item_lane_load(p, unit_of(p_round + 2), n_units, lane);
       } else {
         p_live = false;
       }
     }
-    if (p_live) prefetch_blocks();
+    TQ_TRACE(if (lane == 0) tr_sub[2] += clock64() - ta0;)
   };
 
   auto refill = [&]() {
@@ -481,11 +562,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) paged_attention_kernel(con
   bool failed = false;
   const int rot = lane_rot(lane);
 
+  TQ_TRACE(long long tr0 = clock64();)
   refill();
+  TQ_TRACE(tr_refill += clock64() - tr0;)
   while (consumed < issued) {
     const int s = consumed % kStages;
     const uint32_t parity = (uint32_t)(consumed / kStages) & 1u;
+    TQ_TRACE(tr0 = clock64();)
     const bool ok = mbar_wait_bounded(bar0 + 8 * s, parity);
+    TQ_TRACE(tr_wait += clock64() - tr0; if (tr_first == 0) tr_first = global_ns(); ++tr_chunks;)
     if (!__all_sync(kFullMask, ok)) {
       failed = true;
       break;
@@ -514,19 +599,29 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) paged_attention_kernel(con
     const ChunkSpan sp = chunk_span(p, it, c);
     const float* K = reinterpret_cast<const float*>(stage);
     const float* V = reinterpret_cast<const float*>(stage + kKBytes);
+    TQ_TRACE(tr0 = clock64();)
     if (it.nrows == 1)
       attend_chunk<1>(K, V, qr, 1, it.pos0, sp.key0, sp.nkeys, p.scale_log2, lane, m, lsum, acc);
     else
       attend_chunk<kMaxRows>(K, V, qr, it.nrows, it.pos0, sp.key0, sp.nkeys, p.scale_log2, lane, m,
                              lsum, acc);
     __syncwarp();
+    TQ_TRACE(tr_comp += clock64() - tr0; tr0 = clock64();)
     ++consumed;
     if (++c == it.cend) {  // unit finished
-      finish_rows(p, it, h, lane, m, lsum, acc);
+      finish_rows(p, it, h, lane, m, lsum, acc, TQ_TRACE_ARG(tr_sub));
       at_unit_start = true;
     }
+    TQ_TRACE(tr_fin += clock64() - tr0; tr0 = clock64();)
     refill();
+    TQ_TRACE(tr_refill += clock64() - tr0;)
   }
+  TQ_TRACE(if (lane == 0 && gw < kTraceWarps) {
+    unsigned long long* t = g_attn_trace + (size_t)gw * kTraceSlots;
+    t[0] = tr_start; t[1] = tr_first; t[2] = global_ns(); t[3] = tr_wait; t[4] = tr_comp;
+    t[5] = tr_fin; t[6] = tr_refill; t[7] = tr_chunks;
+    for (int k = 0; k < 8; ++k) t[8 + k] = tr_sub[k];
+  })
 
   if (failed) {
     // Drain: give every copy this warp issued a bounded chance to land before

@@ -34,6 +34,7 @@ namespace {
 #endif
 constexpr int kChunk = TQ_ATTN_CHUNK;      // keys per attention chunk
 constexpr int kMaxRows = TQ_ATTN_MAX_ROWS; // query rows per work item
+constexpr int kUnitBlocks = 64;            // most blocks one work item may span
 
 inline int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t align4(int64_t n) { return (n + 3) & ~int64_t(3); }
@@ -105,6 +106,10 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     split_chunks = std::max<int64_t>(min_split_chunks, cdiv64(total_chunks * n_head, target_units));
   // A work item stores its split index and count in 16 bits each.
   split_chunks = std::max<int64_t>(split_chunks, cdiv64(cdiv64(max_ctx, kChunk), 0x7fff));
+  // The kernel keeps one item's block ids in two registers per lane, so an
+  // item spans at most kUnitBlocks blocks: (split_chunks * kChunk) keys can
+  // straddle one extra block boundary.
+  split_chunks = std::min<int64_t>(split_chunks, std::max<int64_t>(1, (int64_t)(kUnitBlocks - 1) * block_size / kChunk));
 
   int64_t n_items = 0, n_combine = 0, n_partials = 0;
   auto count_items = [&]() {

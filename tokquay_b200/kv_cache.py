@@ -35,9 +35,9 @@ if TYPE_CHECKING:
     from tokquay_b200.model import GPT2Config
 
 # Split-K policy: aim for this many (item, head) units per SM, never cut a
-# split below this many 32-key chunks.
-UNITS_PER_SM = 16
-MIN_SPLIT_CHUNKS = 2
+# split below this many chunks (measured best on B200 for BASELINE config 2).
+UNITS_PER_SM = 32
+MIN_SPLIT_CHUNKS = 4
 
 
 def cdiv(a: int, b: int) -> int:
