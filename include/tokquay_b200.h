@@ -24,8 +24,8 @@
  *                                                            tokquay/model.py:99,122-123
  *   tq_layernorm_rows          x[arange(B), last_idx] then ln_f
  *                                                            tokquay/model.py:179-180
- *   tq_bias_gelu               F.gelu(c_fc(x), approximate="tanh")
- *                                                            tokquay/model.py:110
+ *   tq_bias_gelu               F.gelu(c_fc(x), approximate="tanh"), and the
+ *                              bias of c_attn            tokquay/model.py:110, :69
  *
  * Pool layout (the reference's, tokquay/kv_cache.py:1-14, :51-53):
  *   pool[num_blocks][n_layer][2 (K,V)][n_head][block_size][head_dim], fp32,
@@ -46,7 +46,7 @@
 extern "C" {
 #endif
 
-#define TQ_ABI_VERSION 3
+#define TQ_ABI_VERSION 4
 
 enum tq_status {
   TQ_OK = 0,
@@ -187,9 +187,12 @@ TQ_API int tq_embed_layernorm(float* x, float* xa, const int32_t* ids, const int
                        int32_t n_positions, const float* ln_w, const float* ln_b, float eps,
                        int32_t n_embd, const int32_t* d_num_rows, int32_t max_rows, void* stream);
 
-/* x[r] += y[r] + bias;  then, if ln_w != NULL, xa[r] = LayerNorm(x[r]). */
-TQ_API int tq_bias_residual_layernorm(float* x, float* xa, const float* y, const float* bias,
-                               const float* ln_w, const float* ln_b, float eps, int32_t n_embd,
+/* x[r] += (y_0[r] + ... + y_{n_parts-1}[r]) + bias;  then, if ln_w != NULL,
+ * xa[r] = LayerNorm(x[r]).  y_s = y + s*part_stride: the split-K partial sums
+ * of the linear (n_parts = 1: y is the whole output). */
+TQ_API int tq_bias_residual_layernorm(float* x, float* xa, const float* y, int32_t n_parts,
+                               int64_t part_stride, const float* bias, const float* ln_w,
+                               const float* ln_b, float eps, int32_t n_embd,
                                const int32_t* d_num_rows, int32_t max_rows, void* stream);
 
 /* out[i] = LayerNorm(x[rows[i]]) (rows == NULL: x[i]). */
@@ -197,9 +200,12 @@ TQ_API int tq_layernorm_rows(float* out, const float* x, const int32_t* rows, co
                       const float* ln_b, float eps, int32_t n_embd, const int32_t* d_num_rows,
                       int32_t max_rows, void* stream);
 
-/* h[r][c] = gelu_tanh(h[r][c] + bias[c]) in place; n_cols a multiple of 4. */
-TQ_API int tq_bias_gelu(float* h, const float* bias, int32_t n_cols, const int32_t* d_num_rows,
-                 int32_t max_rows, void* stream);
+/* out[r][c] = gelu_tanh(sum_s h_s[r][c] + bias[c]) (apply_gelu != 0) or the
+ * biased sum alone; h_s = h + s*part_stride are split-K partial sums
+ * (n_parts = 1, out == h: in place).  n_cols a multiple of 4. */
+TQ_API int tq_bias_gelu(float* out, const float* h, int32_t n_parts, int64_t part_stride,
+                 const float* bias, int32_t n_cols, int32_t apply_gelu,
+                 const int32_t* d_num_rows, int32_t max_rows, void* stream);
 
 #ifdef __cplusplus
 }

@@ -183,17 +183,26 @@ def test_fused_row_kernels_match_torch(C):
 
     y, bias = r(N, C), r(C)
     x0 = x.clone()
-    _lib.check(lib.tq_bias_residual_layernorm(x.data_ptr(), xa.data_ptr(), y.data_ptr(), bias.data_ptr(),
+    _lib.check(lib.tq_bias_residual_layernorm(x.data_ptr(), xa.data_ptr(), y.data_ptr(), 1, 0, bias.data_ptr(),
                                               w.data_ptr(), b.data_ptr(), eps, C, n_dev.data_ptr(), N, s),
                "bias_residual_ln")  # fmt: skip
     x1 = x0 + (y + bias)
     torch.testing.assert_close(x, x1, rtol=0, atol=0)
     torch.testing.assert_close(xa, _ln(x1, w, b, eps), rtol=1e-5, atol=1e-5)
     xa_before = xa.clone()
-    _lib.check(lib.tq_bias_residual_layernorm(x.data_ptr(), None, y.data_ptr(), bias.data_ptr(), None, None, eps, C,
-                                              n_dev.data_ptr(), N, s), "bias_residual")  # fmt: skip
+    _lib.check(lib.tq_bias_residual_layernorm(x.data_ptr(), None, y.data_ptr(), 1, 0, bias.data_ptr(), None, None,
+                                              eps, C, n_dev.data_ptr(), N, s), "bias_residual")  # fmt: skip
     torch.testing.assert_close(x, x1 + (y + bias), rtol=0, atol=0)
     assert torch.equal(xa, xa_before)
+    # split-K partial sums of the linear output: x += (y_0 + y_1 + y_2) + bias
+    parts = r(3, N, C)
+    x2 = x.clone()
+    _lib.check(lib.tq_bias_residual_layernorm(x.data_ptr(), xa.data_ptr(), parts.data_ptr(), 3, N * C,
+                                              bias.data_ptr(), w.data_ptr(), b.data_ptr(), eps, C, n_dev.data_ptr(),
+                                              N, s), "bias_residual_ln parts")  # fmt: skip
+    x3 = x2 + (((parts[0] + parts[1]) + parts[2]) + bias)
+    torch.testing.assert_close(x, x3, rtol=0, atol=0)
+    torch.testing.assert_close(xa, _ln(x3, w, b, eps), rtol=1e-5, atol=1e-5)
 
     rows = torch.tensor([5, 0, 36, 17], dtype=torch.int32, device=dev)
     out = torch.empty(4, C, device=dev)
@@ -210,8 +219,17 @@ def test_bias_gelu_matches_torch():
     bias = torch.randn(3072, device="cuda", generator=g)
     want = torch.nn.functional.gelu(h + bias, approximate="tanh")
     n = torch.tensor([53], dtype=torch.int32, device="cuda")
-    _lib.check(lib.tq_bias_gelu(h.data_ptr(), bias.data_ptr(), 3072, n.data_ptr(), 53, _stream()), "gelu")
+    _lib.check(lib.tq_bias_gelu(h.data_ptr(), h.data_ptr(), 1, 0, bias.data_ptr(), 3072, 1, n.data_ptr(), 53,
+                                _stream()), "gelu")  # fmt: skip
     torch.testing.assert_close(h, want, rtol=1e-5, atol=1e-6)
+    # split-K partial sums into a separate output, with and without the GELU
+    parts = torch.randn(4, 53, 3072, device="cuda", generator=g)
+    total = ((parts[0] + parts[1]) + parts[2]) + parts[3]
+    out = torch.empty(53, 3072, device="cuda")
+    for act, ref in ((1, torch.nn.functional.gelu(total + bias, approximate="tanh")), (0, total + bias)):
+        _lib.check(lib.tq_bias_gelu(out.data_ptr(), parts.data_ptr(), 4, 53 * 3072, bias.data_ptr(), 3072, act,
+                                    n.data_ptr(), 53, _stream()), "gelu parts")  # fmt: skip
+        torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-6)
 
 
 def test_abi_rejects_bad_arguments():
@@ -225,6 +243,6 @@ def test_abi_rejects_bad_arguments():
     st = lib.tq_kv_write(pool.data_ptr() + 4, 4, 1, 1, 16, 64, 0, pool.data_ptr(), 192, 64, 128, n.data_ptr(),
                          n.data_ptr(), 1, None)  # misaligned pool
     assert st == _lib.TQ_ERR_INVALID
-    st = lib.tq_bias_gelu(pool.data_ptr(), pool.data_ptr(), 6, n.data_ptr(), 1, None)
+    st = lib.tq_bias_gelu(pool.data_ptr(), pool.data_ptr(), 1, 0, pool.data_ptr(), 6, 1, n.data_ptr(), 1, None)
     assert st == _lib.TQ_ERR_INVALID
     assert _lib.device_status() == 0

@@ -61,12 +61,13 @@ SIGNATURES: dict[str, tuple] = {
                                            _P]),
     "tq_embed_layernorm": (c_int, [_P, _P, _P, _P, _P, _P, c_int32, c_int32, _P, _P, c_float,
                                    c_int32, _P, c_int32, _P]),
-    "tq_bias_residual_layernorm": (c_int, [_P, _P, _P, _P, _P, _P, c_float, c_int32, _P, c_int32, _P]),
+    "tq_bias_residual_layernorm": (c_int, [_P, _P, _P, c_int32, c_int64, _P, _P, _P, c_float, c_int32, _P,
+                                           c_int32, _P]),
     "tq_layernorm_rows": (c_int, [_P, _P, _P, _P, _P, c_float, c_int32, _P, c_int32, _P]),
-    "tq_bias_gelu": (c_int, [_P, _P, c_int32, _P, c_int32, _P]),
+    "tq_bias_gelu": (c_int, [_P, _P, c_int32, c_int64, _P, c_int32, c_int32, _P, c_int32, _P]),
 }
 
-EXPECTED_ABI = 3
+EXPECTED_ABI = 4
 
 # Split-K partials the no-allocation attention entry point can hold
 # (TQ_NOALLOC_MAX_PARTIALS in include/tokquay_b200.h).

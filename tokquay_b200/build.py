@@ -81,6 +81,35 @@ def build_library(force: bool = False, verbose: bool = False, extra_flags: list[
     return target
 
 
+HOSTPACK_SRC = CSRC / "hostpack.c"
+
+
+def hostpack_path() -> Path:
+    import sysconfig
+
+    return PKG / ("_hostpack" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_hostpack(force: bool = False, verbose: bool = False) -> Path:
+    """Compile the ``_hostpack`` CPython extension (plain C, gcc) in-tree."""
+    import sysconfig
+
+    out = hostpack_path()
+    if not force and out.exists() and out.stat().st_mtime >= HOSTPACK_SRC.stat().st_mtime:
+        return out
+    cc = os.environ.get("CC") or shutil.which("gcc") or "cc"
+    tmp = out.with_name(out.name + ".tmp")
+    cmd = [cc, "-O2", "-shared", "-fPIC", "-Wall", f"-I{sysconfig.get_paths()['include']}",
+           str(HOSTPACK_SRC), "-o", str(tmp)]  # fmt: skip
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"{cc} failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, out)
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--force", action="store_true")
@@ -89,6 +118,7 @@ def main() -> None:
     extra = ["-Xptxas", "-v"] if args.ptxas_info else None
     path = build_library(force=args.force or args.ptxas_info, verbose=True, extra_flags=extra)
     print(path)
+    print(build_hostpack(force=args.force, verbose=True))
 
 
 if __name__ == "__main__":

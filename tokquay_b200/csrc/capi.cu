@@ -401,12 +401,15 @@ int tq_embed_layernorm(float* x, float* xa, const int32_t* ids, const int32_t* p
   return check_launch("embed_layernorm");
 }
 
-int tq_bias_residual_layernorm(float* x, float* xa, const float* y, const float* bias,
-                               const float* ln_w, const float* ln_b, float eps, int32_t n_embd,
+int tq_bias_residual_layernorm(float* x, float* xa, const float* y, int32_t n_parts,
+                               int64_t part_stride, const float* bias, const float* ln_w,
+                               const float* ln_b, float eps, int32_t n_embd,
                                const int32_t* d_num_rows, int32_t max_rows, void* stream) {
   int st = check_embd(n_embd);
   if (st) return st;
   if (max_rows < 0) return set_error(TQ_ERR_INVALID, "max_rows must be >= 0");
+  if (n_parts < 1 || (n_parts > 1 && (part_stride < (int64_t)max_rows * n_embd || part_stride % 4)))
+    return set_error(TQ_ERR_INVALID, "bias_residual_layernorm: bad split-K parts");
   if (max_rows == 0) return TQ_OK;
   if (!x || !y || !bias || !d_num_rows || (ln_w && (!ln_b || !xa)))
     return set_error(TQ_ERR_INVALID, "bias_residual_layernorm: NULL argument");
@@ -419,6 +422,8 @@ int tq_bias_residual_layernorm(float* x, float* xa, const float* y, const float*
   p.x = x;
   p.xa = xa;
   p.y = y;
+  p.n_parts = n_parts;
+  p.part_stride = part_stride;
   p.bias = bias;
   p.ln_w = ln_w;
   p.ln_b = ln_b;
@@ -457,22 +462,33 @@ int tq_layernorm_rows(float* out, const float* x, const int32_t* rows, const flo
   return check_launch("layernorm_rows");
 }
 
-int tq_bias_gelu(float* h, const float* bias, int32_t n_cols, const int32_t* d_num_rows,
-                 int32_t max_rows, void* stream) {
+int tq_bias_gelu(float* out, const float* h, int32_t n_parts, int64_t part_stride, const float* bias,
+                 int32_t n_cols, int32_t apply_gelu, const int32_t* d_num_rows, int32_t max_rows,
+                 void* stream) {
   if (max_rows < 0 || n_cols < 4 || n_cols % 4)
     return set_error(TQ_ERR_INVALID, "bias_gelu: n_cols must be a positive multiple of 4");
+  if (n_parts < 1 || (n_parts > 1 && (part_stride < (int64_t)max_rows * n_cols || part_stride % 4)))
+    return set_error(TQ_ERR_INVALID, "bias_gelu: bad split-K parts");
   if (max_rows == 0) return TQ_OK;
-  if (!h || !bias || !d_num_rows) return set_error(TQ_ERR_INVALID, "bias_gelu: NULL argument");
-  if (!aligned(h, 16) || !aligned(bias, 16))
+  if (!out || !h || !bias || !d_num_rows) return set_error(TQ_ERR_INVALID, "bias_gelu: NULL argument");
+  if (!aligned(out, 16) || !aligned(h, 16) || !aligned(bias, 16))
     return set_error(TQ_ERR_INVALID, "bias_gelu: arrays must be 16-byte aligned");
+  if (n_parts > 1 && out != h &&
+      reinterpret_cast<const char*>(out) < reinterpret_cast<const char*>(h + part_stride * n_parts) &&
+      reinterpret_cast<const char*>(h) < reinterpret_cast<const char*>(out + (int64_t)max_rows * n_cols))
+    return set_error(TQ_ERR_INVALID, "bias_gelu: out overlaps the partial sums");
   int sms = 0;
   int st = device_setup(&sms);
   if (st) return st;
   GeluParams p;
+  p.out = out;
   p.h = h;
+  p.n_parts = n_parts;
+  p.part_stride = part_stride;
   p.bias = bias;
   p.n_rows = d_num_rows;
   p.F = n_cols;
+  p.gelu = apply_gelu ? 1 : 0;
   const int64_t total4 = (int64_t)max_rows * (n_cols / 4);
   const int grid = (int)std::min<int64_t>(std::max<int64_t>((total4 + 255) / 256, 1), (int64_t)sms * 8);
   bias_gelu_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);

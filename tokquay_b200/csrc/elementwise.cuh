@@ -7,7 +7,10 @@
 //   embed_ln           x = wte[id] + wpe[pos];  xa = LN(x)             (model.py:172 + ln_1 of layer 0)
 //   bias_residual_ln   x += y + bias;           xa = LN(x) (optional)  (model.py:122-123 + next LN)
 //   layernorm_rows     out[i] = LN(x[rows[i]])                         (model.py:179-180)
-//   bias_gelu          h = gelu_tanh(h + bias)                          (model.py:110)
+//   bias_gelu          out = gelu_tanh(sum of h parts + bias), or the biased
+//                      sum alone                                         (model.py:110, :69)
+// Linear outputs may arrive as split-K partial sums (K-slices computed by one
+// batched fp32 matmul); the kernels add the parts up as they read them.
 // LayerNorm follows nn.LayerNorm: biased variance, eps inside the square root.
 // Row kernels use one warp per row of C = 128*VPL floats held in registers
 // (two-pass mean / variance, no re-read).
@@ -48,7 +51,9 @@ __device__ __forceinline__ void ln_row(const float4 (&v)[VPL], const float4* __r
 struct RowParams {
   float* x;            // residual stream [rows][C] (in/out)
   float* xa;           // LayerNorm output [rows][C] (may be null where noted)
-  const float* y;      // linear output [rows][C] (bias_residual_ln)
+  const float* y;      // linear output [rows][C] (bias_residual_ln), n_parts K-slices of it
+  int n_parts;         // split-K partial sums of the linear output to add up (>= 1)
+  long long part_stride;  // floats between consecutive partial sums
   const float* bias;   // [C]
   const float* ln_w;   // [C] (may be null: skip the LayerNorm)
   const float* ln_b;
@@ -103,7 +108,15 @@ __global__ void __launch_bounds__(256) bias_residual_ln_kernel(const RowParams p
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const int k = lane + 32 * i;
-      const float4 a = xr[k], y = yr[k], b = bias[k];
+      float4 y = yr[k];
+      for (int s = 1; s < p.n_parts; ++s) {  // split-K partial sums of the linear
+        const float4 t = reinterpret_cast<const float4*>(p.y + s * p.part_stride + (size_t)r * p.C)[k];
+        y.x += t.x;
+        y.y += t.y;
+        y.z += t.z;
+        y.w += t.w;
+      }
+      const float4 a = xr[k], b = bias[k];
       // x + (y + b): the linear's bias first, as addmm produces it.
       v[i] = make_float4(a.x + (y.x + b.x), a.y + (y.y + b.y), a.z + (y.z + b.z), a.w + (y.w + b.w));
       xr[k] = v[i];
@@ -138,26 +151,47 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 }
 
 struct GeluParams {
-  float* h;             // [rows][F] in place
+  float* out;           // [rows][F]
+  const float* h;       // [rows][F], n_parts split-K partial sums part_stride floats apart (may be out)
+  int n_parts;
+  long long part_stride;
   const float* bias;    // [F]
   const int* n_rows;    // device-resident row count
   int F;                // multiple of 4
+  int gelu;             // 1: gelu_tanh(sum + bias); 0: sum + bias
 };
 
+// out = gelu_tanh(sum_s h_s + bias)  (or just the biased sum).
 __global__ void __launch_bounds__(256) bias_gelu_kernel(const GeluParams p) {
   const long long f4 = p.F >> 2;
   const long long total = (long long)(*p.n_rows) * f4;
-  float4* h = reinterpret_cast<float4*>(p.h);
+  const float4* h = reinterpret_cast<const float4*>(p.h);
+  float4* out = reinterpret_cast<float4*>(p.out);
   const float4* bias = reinterpret_cast<const float4*>(p.bias);
+  const long long ps4 = p.part_stride >> 2;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     const float4 b = bias[i % f4];
     float4 v = h[i];
-    v.x = gelu_tanh(v.x + b.x);
-    v.y = gelu_tanh(v.y + b.y);
-    v.z = gelu_tanh(v.z + b.z);
-    v.w = gelu_tanh(v.w + b.w);
-    h[i] = v;
+    for (int s = 1; s < p.n_parts; ++s) {
+      const float4 t = h[s * ps4 + i];
+      v.x += t.x;
+      v.y += t.y;
+      v.z += t.z;
+      v.w += t.w;
+    }
+    if (p.gelu) {
+      v.x = gelu_tanh(v.x + b.x);
+      v.y = gelu_tanh(v.y + b.y);
+      v.z = gelu_tanh(v.z + b.z);
+      v.w = gelu_tanh(v.w + b.w);
+    } else {
+      v.x += b.x;
+      v.y += b.y;
+      v.z += b.z;
+      v.w += b.w;
+    }
+    out[i] = v;
   }
 }
 

@@ -21,7 +21,7 @@ import bisect
 import torch
 
 from tokquay_b200 import _lib
-from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, PlanWorkspace
+from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, PackedStep, PlanWorkspace
 from tokquay_b200.sequence import Sequence
 
 DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256, 512)
@@ -96,9 +96,8 @@ class DecodeGraphRunner:
         if bucket is None:
             raise ValueError(f"{B} sequences exceed the largest graph bucket {self.max_batch}")
         graph, ws, logits, _, per_replay = self.graph(bucket)
-        starts = [s.num_cached_tokens for s in seqs]
-        ids = [s.tokens_slice(st, st + 1)[0] for s, st in zip(seqs, starts)]
-        DevicePagedBatch(self.allocator, [s.block_table for s in seqs], starts, [1] * B, ids, workspace=ws)
+        packed = PackedStep.from_sequences(seqs, [1] * B)
+        ws.stage(packed, torch.cuda.current_stream(self.allocator.pool.device), self.model.cfg.vocab_size)
         self.model.last_h2d_bytes = ws.total * 4
         graph.replay()
         self.model.kernel_launches += per_replay

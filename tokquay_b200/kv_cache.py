@@ -31,6 +31,11 @@ import torch
 from tokquay_b200 import _lib
 from tokquay_b200.sequence import Sequence
 
+try:  # native host-side packing (tokquay_b200/csrc/hostpack.c); same results without it
+    from tokquay_b200 import _hostpack
+except ImportError:  # pragma: no cover - the Python packer below is used instead
+    _hostpack = None
+
 if TYPE_CHECKING:
     from tokquay_b200.model import GPT2Config
 
@@ -148,11 +153,7 @@ class BlockAllocator:
     def batch_for(self, seqs: list[Sequence], new_lens: list[int] | None = None) -> "DevicePagedBatch":
         """Step view for ``seqs``: each feeds ``new_lens[i]`` tokens (default: all
         uncached ones) from position ``num_cached_tokens`` (tokquay/kv_cache.py:122-127)."""
-        starts = [s.num_cached_tokens for s in seqs]
-        new_lens = new_lens or [s.num_uncached_tokens for s in seqs]
-        ids = list(itertools.chain.from_iterable(
-            s.tokens_slice(st, st + n) for s, st, n in zip(seqs, starts, new_lens)))  # fmt: skip
-        return DevicePagedBatch(self, [s.block_table for s in seqs], starts, new_lens, ids)
+        return DevicePagedBatch(self, None, None, None, packed=PackedStep.from_sequences(seqs, new_lens))
 
 
 class BatchedKV:
@@ -230,14 +231,57 @@ def _ptr(a: np.ndarray) -> int:
     return a.ctypes.data
 
 
-def plan_step_host(
+class PackedStep:
+    """One step's host metadata as int32 arrays, the planner's input:
+    ``start[B]``, ``lens[B]``, ``offsets[B+1]`` + ``tables`` (block tables,
+    CSR), and ``ids`` (the new tokens, in sequence order) or None."""
+
+    __slots__ = ("start", "lens", "offsets", "tables", "ids")
+
+    def __init__(self, start, lens, offsets, tables, ids):
+        self.start, self.lens, self.offsets, self.tables, self.ids = start, lens, offsets, tables, ids
+
+    @classmethod
+    def from_lists(cls, block_tables, start, new_lens, token_ids=None) -> "PackedStep":
+        B = len(block_tables)
+        if B == 0 or not (B == len(start) == len(new_lens)):
+            raise ValueError("block_tables, start and new_lens must be non-empty and the same length")
+        lens = np.fromiter((len(t) for t in block_tables), dtype=np.int64, count=B)
+        offs = np.zeros(B + 1, dtype=np.int64)
+        np.cumsum(lens, out=offs[1:])
+        if offs[-1] > np.iinfo(np.int32).max:
+            raise ValueError("block tables too large")
+        data = np.fromiter(itertools.chain.from_iterable(block_tables), dtype=np.int32, count=int(offs[-1]))
+        ids = None if token_ids is None else np.asarray(token_ids, dtype=np.int32)
+        return cls(np.asarray(start, dtype=np.int32), np.asarray(new_lens, dtype=np.int32),
+                   offs.astype(np.int32), data, ids)  # fmt: skip
+
+    @classmethod
+    def from_sequences(cls, seqs, new_lens: list[int] | None = None) -> "PackedStep":
+        """Sequence ``i`` feeds ``new_lens[i]`` tokens (default: all uncached)
+        from ``num_cached_tokens``; token ids included.  Uses the native
+        ``_hostpack`` helper when it is built (same result, no per-element
+        Python work)."""
+        if not seqs:
+            raise ValueError("block_tables, start and new_lens must be non-empty and the same length")
+        if _hostpack is not None:
+            st, ln, of, tb, ids = _hostpack.pack_step(seqs, new_lens or None)
+            f = np.frombuffer
+            return cls(f(st, np.int32), f(ln, np.int32), f(of, np.int32), f(tb, np.int32), f(ids, np.int32))
+        starts = [s.num_cached_tokens for s in seqs]
+        lens = new_lens or [s.num_uncached_tokens for s in seqs]
+        if len(lens) != len(seqs):
+            raise ValueError("block_tables, start and new_lens must be non-empty and the same length")
+        ids = list(itertools.chain.from_iterable(
+            s.tokens_slice(st, st + n) for s, st, n in zip(seqs, starts, lens) if n > 0 and st >= 0))  # fmt: skip
+        return cls.from_lists([s.block_table for s in seqs], starts, lens, ids)
+
+
+def plan_packed(
     block_size: int,
     num_blocks: int,
     n_head: int,
-    block_tables: list[list[int]],
-    start: list[int],
-    new_lens: list[int],
-    token_ids: list[int] | None = None,
+    packed: PackedStep,
     vocab_size: int = 0,
     target_units: int = 2368,
     min_split_chunks: int = MIN_SPLIT_CHUNKS,
@@ -251,25 +295,17 @@ def plan_step_host(
     the fixed-capacity layout.  Raises ValueError for a batch the reference
     would reject, RuntimeError for one beyond ``caps``."""
     lib = _lib.load()
-    B = len(block_tables)
-    if B == 0 or not (B == len(start) == len(new_lens)):
+    B = int(packed.start.size)
+    if B == 0 or packed.lens.size != B or packed.offsets.size != B + 1:
         raise ValueError("block_tables, start and new_lens must be non-empty and the same length")
-    st = np.asarray(start, dtype=np.int32)
-    ql = np.asarray(new_lens, dtype=np.int32)
-    lens = np.fromiter((len(t) for t in block_tables), dtype=np.int64, count=B)
-    offs = np.zeros(B + 1, dtype=np.int64)
-    np.cumsum(lens, out=offs[1:])
-    if offs[-1] > np.iinfo(np.int32).max:
-        raise ValueError("block tables too large")
-    offs32 = offs.astype(np.int32)
-    data = np.fromiter(itertools.chain.from_iterable(block_tables), dtype=np.int32, count=int(offs[-1]))
-    ids = None
-    if token_ids is not None:
-        ids = np.asarray(token_ids, dtype=np.int32)
-        if ids.size != int(ql.sum()):
-            raise ValueError(f"{ids.size} token ids for {int(ql.sum())} new tokens")
+    st, ql, offs, data, ids = (np.ascontiguousarray(a, dtype=np.int32) if a is not None else None
+                               for a in (packed.start, packed.lens, packed.offsets, packed.tables, packed.ids))  # fmt: skip
+    if ids is not None and ids.size != int(np.maximum(ql, 0).sum()):
+        raise ValueError(f"{ids.size} token ids for {int(ql.sum())} new tokens")
     layout = np.zeros(_lib.PLAN_LAYOUT_LEN, dtype=np.int32)
-    ids_ptr = _ptr(ids) if ids is not None else None
+    ids_ptr = _ptr(ids) if ids is not None and ids.size else None
+    if ids is not None and ids_ptr is None:
+        ids_ptr = _ptr(np.zeros(1, np.int32))
     data_ptr = _ptr(data) if data.size else None
     caps_ptr = None
     if caps is not None:
@@ -277,7 +313,7 @@ def plan_step_host(
         caps_ptr = _ptr(caps)
 
     def call(buf_ptr, cap):
-        return lib.tq_plan_step(B, _ptr(st), _ptr(ql), _ptr(offs32), data_ptr, ids_ptr, block_size,
+        return lib.tq_plan_step(B, _ptr(st), _ptr(ql), _ptr(offs), data_ptr, ids_ptr, block_size,
                                 num_blocks, n_head, vocab_size, target_units, min_split_chunks,
                                 caps_ptr, buf_ptr, cap, _ptr(layout))  # fmt: skip
 
@@ -295,6 +331,26 @@ def plan_step_host(
     plan = np.empty(int(layout[_lib.PLAN_TOTAL_INTS]), dtype=np.int32)
     _lib.check(call(_ptr(plan), plan.size), "tq_plan_step")
     return plan, layout
+
+
+def plan_step_host(
+    block_size: int,
+    num_blocks: int,
+    n_head: int,
+    block_tables: list[list[int]],
+    start: list[int],
+    new_lens: list[int],
+    token_ids: list[int] | None = None,
+    vocab_size: int = 0,
+    target_units: int = 2368,
+    min_split_chunks: int = MIN_SPLIT_CHUNKS,
+    out: torch.Tensor | np.ndarray | None = None,
+    caps: np.ndarray | None = None,
+) -> tuple[np.ndarray, np.ndarray]:
+    """``plan_packed`` for Python lists (block tables, starts, lengths, ids)."""
+    packed = PackedStep.from_lists(block_tables, start, new_lens, token_ids)
+    return plan_packed(block_size, num_blocks, n_head, packed, vocab_size, target_units, min_split_chunks,
+                       out, caps)  # fmt: skip
 
 
 class PlanWorkspace:
@@ -333,6 +389,22 @@ class PlanWorkspace:
         self._pinned = [torch.empty(self.total, dtype=torch.int32, pin_memory=True) for _ in range(2)]
         self._events: list[torch.cuda.Event | None] = [None, None]
         self._turn = 0
+
+    def stage(self, packed: PackedStep, stream: torch.cuda.Stream, vocab_size: int = 0,
+              target_units: int | None = None) -> np.ndarray:  # fmt: skip
+        """Plan ``packed`` into the next pinned buffer and copy it into the
+        device plan on ``stream``; returns the layout."""
+        a = self.allocator
+        if target_units is None:
+            target_units = UNITS_PER_SM * sm_count(a.pool.device)
+        slot, host = self.pinned_buffer()
+        plan, layout = plan_packed(a.block_size, a.num_blocks, a.cfg.n_head, packed, vocab_size, target_units,
+                                   MIN_SPLIT_CHUNKS, out=host, caps=self.caps)  # fmt: skip
+        assert plan is host and int(layout[_lib.PLAN_TOTAL_INTS]) == self.total
+        with torch.cuda.stream(stream):
+            self.plan.copy_(host, non_blocking=True)
+        self.mark_copied(slot, stream)
+        return layout
 
     def pinned_buffer(self) -> tuple[int, torch.Tensor]:
         """The next pinned staging buffer, once the copy that last read it is done."""
@@ -373,20 +445,26 @@ class DevicePagedBatch(BatchedKV):
     def __init__(
         self,
         allocator: BlockAllocator,
-        block_tables: list[list[int]],
-        start: list[int],
-        new_lens: list[int],
+        block_tables: list[list[int]] | None,
+        start: list[int] | None,
+        new_lens: list[int] | None,
         token_ids: list[int] | None = None,
         stream: torch.cuda.Stream | None = None,
         workspace: PlanWorkspace | None = None,
         graph_sizing: bool = False,
+        packed: PackedStep | None = None,
     ):
         pool = allocator.pool
         if pool.device.type != "cuda":
             raise RuntimeError("DevicePagedBatch needs the pool on a CUDA device")
-        if not block_tables or not (len(block_tables) == len(start) == len(new_lens)):
+        if packed is None:
+            if not block_tables or not (len(block_tables) == len(start) == len(new_lens)):
+                raise ValueError("block_tables, start and new_lens must be non-empty and the same length")
+            packed = PackedStep.from_lists(block_tables, start, new_lens, token_ids)
+        st, ln = packed.start, packed.lens
+        if st.size == 0:
             raise ValueError("block_tables, start and new_lens must be non-empty and the same length")
-        if min(new_lens) < 1:
+        if int(ln.min()) < 1:
             raise ValueError("every sequence must feed at least one token")
         if graph_sizing and workspace is None:
             raise ValueError("graph_sizing needs a workspace")
@@ -396,23 +474,23 @@ class DevicePagedBatch(BatchedKV):
         self.pool = pool
         self.block_size = bs
         self.n_layer, self.n_head, self.d_head = cfg.n_layer, cfg.n_head, cfg.d_head
-        self.B, self.T = len(block_tables), max(new_lens)
-        self.N = int(sum(new_lens))
-        self._start = list(start)
-        self._new_lens = list(new_lens)
-        ctx = [s + n for s, n in zip(start, new_lens)]
-        self.max_ctx = max(ctx)
-        self.num_blocks_gathered = max(cdiv(c, bs) for c in ctx)
+        self.B, self.T = int(st.size), int(ln.max())
+        self.N = int(ln.sum())
+        self._start = st
+        self._new_lens = ln
+        ctx = st.astype(np.int64) + ln
+        self.max_ctx = int(ctx.max())
+        self.num_blocks_gathered = int(-(-ctx.max() // bs))
 
         device = pool.device
         stream = stream or torch.cuda.current_stream(device)
         target = UNITS_PER_SM * sm_count(device)
-        vocab = cfg.vocab_size if token_ids is not None else 0
+        vocab = cfg.vocab_size if packed.ids is not None else 0
         if workspace is None:
             ring = _ring(device)
             slot, host = ring.take(0)
-            plan, layout = plan_step_host(bs, allocator.num_blocks, cfg.n_head, block_tables, start, new_lens,
-                                          token_ids, vocab, target, MIN_SPLIT_CHUNKS, out=host)  # fmt: skip
+            plan, layout = plan_packed(bs, allocator.num_blocks, cfg.n_head, packed, vocab, target,
+                                       MIN_SPLIT_CHUNKS, out=host)  # fmt: skip
             total = int(layout[_lib.PLAN_TOTAL_INTS])
             if plan is not host:  # the plan did not fit: grow the pinned buffer and stage it there
                 slot, host = ring.take(total)
@@ -422,18 +500,9 @@ class DevicePagedBatch(BatchedKV):
                 dev.copy_(host[:total], non_blocking=True)
             ring.mark(slot, stream)
         else:
-            if workspace.allocator is not allocator:
-                raise ValueError("the workspace belongs to another allocator")
-            slot, host = workspace.pinned_buffer()
-            plan, layout = plan_step_host(bs, allocator.num_blocks, cfg.n_head, block_tables, start, new_lens,
-                                          token_ids, vocab, target, MIN_SPLIT_CHUNKS, out=host,
-                                          caps=workspace.caps)  # fmt: skip
-            total = int(layout[_lib.PLAN_TOTAL_INTS])
-            assert plan is host and total == workspace.total
+            layout = workspace.stage(packed, stream, vocab, target)
+            total = workspace.total
             dev = workspace.plan
-            with torch.cuda.stream(stream):
-                dev.copy_(host, non_blocking=True)
-            workspace.mark_copied(slot, stream)
         self.layout = layout
         self.h2d_bytes = 4 * total  # the one host->device copy this step makes
         self.plan = dev
@@ -463,7 +532,7 @@ class DevicePagedBatch(BatchedKV):
         self.block_tables_i32 = view(_lib.PLAN_OFF_TABLES, dims[0] * self.table_stride)
         self.slot_mapping = view(_lib.PLAN_OFF_SLOTS, dims[1])
         self.row_positions = view(_lib.PLAN_OFF_POSITIONS, dims[1])
-        self.token_ids = view(_lib.PLAN_OFF_TOKEN_IDS, dims[1]) if token_ids is not None else None
+        self.token_ids = view(_lib.PLAN_OFF_TOKEN_IDS, dims[1]) if packed.ids is not None else None
         self.last_rows = view(_lib.PLAN_OFF_LAST_ROWS, self.B)
         self.work_items = view(_lib.PLAN_OFF_ITEMS, 8 * dims[3])
         self.combine_list = view(_lib.PLAN_OFF_COMBINE, 4 * dims[4])
@@ -516,15 +585,14 @@ class DevicePagedBatch(BatchedKV):
     @property
     def positions(self) -> torch.Tensor:
         if self._positions is None:
-            st = torch.tensor(self._start, dtype=torch.long, device=self.pool.device)
+            st = torch.from_numpy(self._start.astype(np.int64)).to(self.pool.device)
             self._positions = st[:, None] + torch.arange(self.T, device=self.pool.device)[None, :]
         return self._positions
 
     @property
     def last_idx(self) -> torch.Tensor:
         if self._last_idx is None:
-            self._last_idx = torch.tensor([n - 1 for n in self._new_lens], dtype=torch.long,
-                                          device=self.pool.device)
+            self._last_idx = torch.from_numpy(self._new_lens.astype(np.int64) - 1).to(self.pool.device)
         return self._last_idx
 
     @property
@@ -532,15 +600,15 @@ class DevicePagedBatch(BatchedKV):
         """``[B, 1, T, nb*bs]`` boolean mask of the reference (kv_cache.py:213-214)."""
         if self._mask is None:
             dev = self.pool.device
-            ctx = torch.tensor([s + n for s, n in zip(self._start, self._new_lens)], device=dev)
+            ctx = torch.from_numpy(self._start.astype(np.int64) + self._new_lens).to(dev)
             k_pos = torch.arange(self.num_blocks_gathered * self.block_size, device=dev)[None, None, :]
             self._mask = ((k_pos <= self.positions[:, :, None]) & (k_pos < ctx[:, None, None]))[:, None]
         return self._mask
 
     def _valid_bt(self) -> tuple[torch.Tensor, torch.Tensor]:
         if self._flat_bt is None:
-            b = [i for i, n in enumerate(self._new_lens) for _ in range(n)]
-            t = [j for n in self._new_lens for j in range(n)]
+            b = [i for i, n in enumerate(self._new_lens.tolist()) for _ in range(n)]
+            t = [j for n in self._new_lens.tolist() for j in range(n)]
             dev = self.pool.device
             self._flat_bt = (torch.tensor(b, device=dev), torch.tensor(t, device=dev))
         return self._flat_bt

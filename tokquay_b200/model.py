@@ -5,7 +5,9 @@ Parameter names and shapes are the reference's (tokquay/model.py:24-35,
 paged forward (tokquay/model.py:136-181) runs on ragged rows -- only the N
 real new tokens of the step, never the reference's padded ``B x T`` -- with:
 
-* the fp32 linears on torch matmul (cuBLAS SGEMM; TF32 must stay off);
+* the fp32 linears on torch matmul (cuBLAS SGEMM; TF32 must stay off), split
+  over K-slices at decode batch sizes (``split_k_for``), with the slices'
+  partial sums added by the fused kernel that consumes the linear's output;
 * ``tq_embed_layernorm``, ``tq_bias_residual_layernorm``, ``tq_bias_gelu`` and
   ``tq_layernorm_rows`` for everything elementwise around them;
 * ``tq_kv_write`` + ``tq_paged_attention`` for the attention over the pool.
@@ -67,6 +69,23 @@ def _tf32_off() -> bool:
     return not torch.backends.cuda.matmul.allow_tf32 and torch.get_float32_matmul_precision() == "highest"
 
 
+def split_k_for(rows: int, k: int, n: int) -> int:
+    """How many K-slices an fp32 linear of ``rows x k @ k x n`` is split into.
+
+    At decode batch sizes cuBLAS's fp32 GEMM runs a handful of CTAs down the
+    whole K loop; one batched matmul over K-slices fills the GPU and the
+    slices' partial sums are added by the fused kernel that consumes the
+    output.  Chosen from B200 measurements of torch.mm vs torch.bmm over
+    K-slices for GPT-2's linears (rows 8 / 64 / 512)."""
+    if rows > 128:
+        s = 4 if k >= 2048 else 1
+    else:
+        s = 16 if k >= 2048 else (8 if n <= 1024 else 4)
+    while s > 1 and (k % s or k // s < 64):
+        s //= 2
+    return s
+
+
 class GPT2(nn.Module):
     def __init__(self, cfg: GPT2Config | None = None):
         super().__init__()
@@ -79,6 +98,7 @@ class GPT2(nn.Module):
         self.kernel_launches = 0
         self.last_h2d_bytes = 0  # plan bytes the last forward's batch copied to the device
         self.graph_runner = None  # set by use_cuda_graphs()
+        self._wt: dict[str, tuple] = {}  # name -> (parameter version, contiguous W^T)
         self.cfg = cfg or GPT2Config()
         self.wte = nn.Embedding(self.cfg.vocab_size, self.cfg.n_embd)
         self.wpe = nn.Embedding(self.cfg.n_positions, self.cfg.n_embd)
@@ -93,6 +113,27 @@ class GPT2(nn.Module):
 
         self.graph_runner = DecodeGraphRunner(self, allocator, buckets or DEFAULT_BUCKETS, max_ctx)
         return self.graph_runner
+
+    def _weight_t(self, name: str, w: torch.Tensor) -> torch.Tensor:
+        """Contiguous ``[in, out]`` copy of a linear weight, rebuilt if the
+        parameter was changed in place."""
+        hit = self._wt.get(name)
+        if hit is None or hit[0] != w._version or hit[1].device != w.device:
+            hit = (w._version, w.detach().t().contiguous())
+            self._wt[name] = hit
+        return hit[1]
+
+    @staticmethod
+    def _linear_parts(x: torch.Tensor, wt: torch.Tensor) -> tuple[torch.Tensor, int, int]:
+        """``x @ wt`` as ``n_parts`` split-K partial sums laid out ``part_stride``
+        floats apart (torch fp32 matmul; TF32 stays off)."""
+        rows, k = x.shape
+        n = wt.shape[1]
+        s = split_k_for(rows, k, n)
+        if s == 1:
+            return torch.mm(x, wt), 1, 0
+        parts = torch.bmm(x.view(rows, s, k // s).transpose(0, 1), wt.view(s, k // s, n))  # [s, rows, n]
+        return parts, s, rows * n
 
     # ---- reference-shaped entry point --------------------------------------------------
     @torch.no_grad()
@@ -149,7 +190,11 @@ class GPT2(nn.Module):
         for i, blk in enumerate(self.h):
             last = i == cfg.n_layer - 1
             att = blk.attn
-            qkv = torch.addmm(att.c_attn.bias, xa, att.c_attn.weight.t())  # [N, 3C]
+            p = f"h.{i}."
+            parts, ns, ps = self._linear_parts(xa, self._weight_t(p + "c_attn", att.c_attn.weight))
+            qkv = parts if ns == 1 else torch.empty(N, 3 * C, dtype=torch.float32, device=dev)
+            _lib.check(lib.tq_bias_gelu(qkv.data_ptr(), parts.data_ptr(), ns, ps, att.c_attn.bias.data_ptr(),
+                                        3 * C, 0, rows_ptr, rows, stream), "tq_bias_gelu")  # fmt: skip
             batch.write_rows(i, qkv, C, 2 * C, stream)
             a = torch.empty(N, C, dtype=torch.float32, device=dev)
             if self.attention_events is not None:
@@ -168,36 +213,37 @@ class GPT2(nn.Module):
                 a, x = a.index_select(0, sel), x.index_select(0, sel)
                 xa = torch.empty(B, C, dtype=torch.float32, device=dev)
                 rows, rows_ptr = B, b_ptr
-            y = torch.mm(a, att.c_proj.weight.t())
+            y, ns, ps = self._linear_parts(a, self._weight_t(p + "c_proj", att.c_proj.weight))
             _lib.check(lib.tq_bias_residual_layernorm(
-                x.data_ptr(), xa.data_ptr(), y.data_ptr(), att.c_proj.bias.data_ptr(),
+                x.data_ptr(), xa.data_ptr(), y.data_ptr(), ns, ps, att.c_proj.bias.data_ptr(),
                 blk.ln_2.weight.data_ptr(), blk.ln_2.bias.data_ptr(), eps, C, rows_ptr, rows, stream),
                 "tq_bias_residual_layernorm")  # fmt: skip
-            hid = torch.mm(xa, blk.mlp.c_fc.weight.t())
-            _lib.check(lib.tq_bias_gelu(hid.data_ptr(), blk.mlp.c_fc.bias.data_ptr(), hid.shape[1],
-                                        rows_ptr, rows, stream), "tq_bias_gelu")  # fmt: skip
-            y = torch.mm(hid, blk.mlp.c_proj.weight.t())
+            parts, ns, ps = self._linear_parts(xa, self._weight_t(p + "c_fc", blk.mlp.c_fc.weight))
+            hid = parts if ns == 1 else torch.empty(rows, 4 * C, dtype=torch.float32, device=dev)
+            _lib.check(lib.tq_bias_gelu(hid.data_ptr(), parts.data_ptr(), ns, ps, blk.mlp.c_fc.bias.data_ptr(),
+                                        4 * C, 1, rows_ptr, rows, stream), "tq_bias_gelu")  # fmt: skip
+            y, ns, ps = self._linear_parts(hid, self._weight_t(p + "mlp.c_proj", blk.mlp.c_proj.weight))
             nxt = None if last else self.h[i + 1].ln_1
             _lib.check(lib.tq_bias_residual_layernorm(
-                x.data_ptr(), xa.data_ptr(), y.data_ptr(), blk.mlp.c_proj.bias.data_ptr(),
+                x.data_ptr(), xa.data_ptr(), y.data_ptr(), ns, ps, blk.mlp.c_proj.bias.data_ptr(),
                 nxt.weight.data_ptr() if nxt is not None else None,
                 nxt.bias.data_ptr() if nxt is not None else None, eps, C, rows_ptr, rows, stream),
                 "tq_bias_residual_layernorm")  # fmt: skip
 
-        # embed + per layer (kv_write, attention, 2x bias_residual, gelu) + final LN
-        self.kernel_launches += 2 + cfg.n_layer * 5
+        # embed + per layer (qkv bias, kv_write, attention, 2x bias_residual, gelu) + final LN
+        self.kernel_launches += 2 + cfg.n_layer * 6
         if last_only:
             xf = torch.empty(B, C, dtype=torch.float32, device=dev)
             sel_ptr = None if rows == B else batch.last_rows.data_ptr()
             _lib.check(lib.tq_layernorm_rows(xf.data_ptr(), x.data_ptr(), sel_ptr, self.ln_f.weight.data_ptr(),
                                              self.ln_f.bias.data_ptr(), eps, C, b_ptr, B, stream),
                        "tq_layernorm_rows")  # fmt: skip
-            return torch.mm(xf, self.wte.weight.t()).unsqueeze(1)  # tied LM head, model.py:181
+            return torch.mm(xf, self._weight_t("wte", self.wte.weight)).unsqueeze(1)  # tied LM head, model.py:181
         xf = torch.empty(N, C, dtype=torch.float32, device=dev)
         _lib.check(lib.tq_layernorm_rows(xf.data_ptr(), x.data_ptr(), None, self.ln_f.weight.data_ptr(),
                                          self.ln_f.bias.data_ptr(), eps, C, n_ptr, N, stream),
                    "tq_layernorm_rows")  # fmt: skip
-        logits = torch.mm(xf, self.wte.weight.t())
+        logits = torch.mm(xf, self._weight_t("wte", self.wte.weight))
         out = torch.zeros(B, batch.T, cfg.vocab_size, dtype=torch.float32, device=dev)
         b, t = batch._valid_bt()
         out[b, t] = logits
