@@ -92,21 +92,6 @@ int check_pool(const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n
   return TQ_OK;
 }
 
-// Instantiates a row kernel template for C = 128 * VPL, VPL in 1..8.
-#define TQ_ROW_LAUNCH(KERNEL, VPL_RT, GRID, BLOCK, STREAM, PARAMS)     \
-  do {                                                                 \
-    switch (VPL_RT) {                                                  \
-      case 1: KERNEL<1><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
-      case 2: KERNEL<2><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
-      case 3: KERNEL<3><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
-      case 4: KERNEL<4><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
-      case 5: KERNEL<5><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
-      case 6: KERNEL<6><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
-      case 7: KERNEL<7><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
-      case 8: KERNEL<8><<<GRID, BLOCK, 0, STREAM>>>(PARAMS); break;    \
-    }                                                                  \
-  } while (0)
-
 int check_embd(int32_t n_embd) {
   if (n_embd < 128 || n_embd > 1024 || n_embd % 128 != 0)
     return set_error(TQ_ERR_UNSUPPORTED, "n_embd must be a multiple of 128 in [128, 1024], got %d",
@@ -119,6 +104,12 @@ int check_embd(int32_t n_embd) {
 int warp_grid(int64_t warps, int sm_count) {
   const int64_t blocks = (warps + 7) / 8;
   return (int)std::min<int64_t>(std::max<int64_t>(blocks, 1), (int64_t)sm_count * 8);
+}
+
+// Grid for block-per-row kernels: one block per row, capped at 16 blocks per
+// SM (the kernels grid-stride beyond that).
+int row_grid(int64_t rows, int sm_count) {
+  return (int)std::min<int64_t>(std::max<int64_t>(rows, 1), (int64_t)sm_count * 16);
 }
 
 }  // namespace
@@ -179,7 +170,8 @@ int tq_kv_write(float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head
   p.v_col = v_col;
   p.slots = slot_mapping;
   p.n_tokens = d_num_tokens;
-  kv_write_kernel<<<warp_grid(2LL * max_tokens, sms), 256, 0, (cudaStream_t)stream>>>(p);
+  const int threads = std::min(1024, ((2 * n_head * 16 + 31) / 32) * 32);
+  kv_write_kernel<<<row_grid(max_tokens, sms), threads, 0, (cudaStream_t)stream>>>(p);
   return check_launch("kv_write");
 }
 
@@ -397,7 +389,7 @@ int tq_embed_layernorm(float* x, float* xa, const int32_t* ids, const int32_t* p
   p.vocab = vocab_size;
   p.n_positions = n_positions;
   p.eps = eps;
-  TQ_ROW_LAUNCH(embed_ln_kernel, n_embd / 128, warp_grid(max_rows, sms), 256, (cudaStream_t)stream, p);
+  embed_ln_kernel<<<row_grid(max_rows, sms), n_embd / 4, 0, (cudaStream_t)stream>>>(p);
   return check_launch("embed_layernorm");
 }
 
@@ -430,8 +422,16 @@ int tq_bias_residual_layernorm(float* x, float* xa, const float* y, int32_t n_pa
   p.n_rows = d_num_rows;
   p.C = n_embd;
   p.eps = eps;
-  TQ_ROW_LAUNCH(bias_residual_ln_kernel, n_embd / 128, warp_grid(max_rows, sms), 256,
-                (cudaStream_t)stream, p);
+  const cudaStream_t s = (cudaStream_t)stream;
+  const int grid = row_grid(max_rows, sms), threads = n_embd / 4;
+  switch (n_parts) {  // partial-sum loads unrolled for the split counts the model uses
+    case 1: bias_residual_ln_kernel<1><<<grid, threads, 0, s>>>(p); break;
+    case 2: bias_residual_ln_kernel<2><<<grid, threads, 0, s>>>(p); break;
+    case 4: bias_residual_ln_kernel<4><<<grid, threads, 0, s>>>(p); break;
+    case 8: bias_residual_ln_kernel<8><<<grid, threads, 0, s>>>(p); break;
+    case 16: bias_residual_ln_kernel<16><<<grid, threads, 0, s>>>(p); break;
+    default: bias_residual_ln_kernel<0><<<grid, threads, 0, s>>>(p); break;
+  }
   return check_launch("bias_residual_layernorm");
 }
 
@@ -457,8 +457,7 @@ int tq_layernorm_rows(float* out, const float* x, const int32_t* rows, const flo
   p.n_rows = d_num_rows;
   p.C = n_embd;
   p.eps = eps;
-  TQ_ROW_LAUNCH(layernorm_rows_kernel, n_embd / 128, warp_grid(max_rows, sms), 256,
-                (cudaStream_t)stream, p);
+  layernorm_rows_kernel<<<row_grid(max_rows, sms), n_embd / 4, 0, (cudaStream_t)stream>>>(p);
   return check_launch("layernorm_rows");
 }
 
@@ -491,7 +490,15 @@ int tq_bias_gelu(float* out, const float* h, int32_t n_parts, int64_t part_strid
   p.gelu = apply_gelu ? 1 : 0;
   const int64_t total4 = (int64_t)max_rows * (n_cols / 4);
   const int grid = (int)std::min<int64_t>(std::max<int64_t>((total4 + 255) / 256, 1), (int64_t)sms * 8);
-  bias_gelu_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
+  const cudaStream_t s = (cudaStream_t)stream;
+  switch (n_parts) {  // partial-sum loads unrolled for the split counts the model uses
+    case 1: bias_gelu_kernel<1><<<grid, 256, 0, s>>>(p); break;
+    case 2: bias_gelu_kernel<2><<<grid, 256, 0, s>>>(p); break;
+    case 4: bias_gelu_kernel<4><<<grid, 256, 0, s>>>(p); break;
+    case 8: bias_gelu_kernel<8><<<grid, 256, 0, s>>>(p); break;
+    case 16: bias_gelu_kernel<16><<<grid, 256, 0, s>>>(p); break;
+    default: bias_gelu_kernel<0><<<grid, 256, 0, s>>>(p); break;
+  }
   return check_launch("bias_gelu");
 }
 

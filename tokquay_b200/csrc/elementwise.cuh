@@ -12,40 +12,37 @@
 // Linear outputs may arrive as split-K partial sums (K-slices computed by one
 // batched fp32 matmul); the kernels add the parts up as they read them.
 // LayerNorm follows nn.LayerNorm: biased variance, eps inside the square root.
-// Row kernels use one warp per row of C = 128*VPL floats held in registers
-// (two-pass mean / variance, no re-read).
+// Row kernels use one block per row of C floats, one float4 per thread
+// (two-pass mean / variance over the values held in registers, no re-read).
 #pragma once
 
 #include "common.cuh"
 
 namespace tq {
 
-template <int VPL>
-__device__ __forceinline__ void ln_row(const float4 (&v)[VPL], const float4* __restrict__ w,
-                                       const float4* __restrict__ b, float4* __restrict__ out,
-                                       int lane, int C, float eps) {
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-  const float mean = warp_sum(s) / (float)C;
-  float q = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const float a = v[i].x - mean, bb = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
-    q += (a * a + bb * bb) + (c * c + d * d);
-  }
-  const float rstd = rsqrtf(warp_sum(q) / (float)C + eps);
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int k = lane + 32 * i;
-    const float4 ww = w[k], bv = b[k];
-    float4 o;
-    o.x = (v[i].x - mean) * rstd * ww.x + bv.x;
-    o.y = (v[i].y - mean) * rstd * ww.y + bv.y;
-    o.z = (v[i].z - mean) * rstd * ww.z + bv.z;
-    o.w = (v[i].w - mean) * rstd * ww.w + bv.w;
-    out[k] = o;
-  }
+// Sum over the block (one value per thread, blockDim = C/4 <= 256).
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();  // red may still be read by the previous reduction
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+
+// LayerNorm of one row held one float4 per thread: biased variance, eps
+// inside the root, then * w + b (nn.LayerNorm).
+__device__ __forceinline__ float4 ln_value(const float4 v, const float4* __restrict__ w,
+                                           const float4* __restrict__ b, int C, float eps, float* red) {
+  const int k = threadIdx.x;
+  const float mean = block_sum((v.x + v.y) + (v.z + v.w), red) / (float)C;
+  const float a = v.x - mean, bb = v.y - mean, c = v.z - mean, d = v.w - mean;
+  const float rstd = rsqrtf(block_sum((a * a + bb * bb) + (c * c + d * d), red) / (float)C + eps);
+  const float4 ww = w[k], bv = b[k];
+  return make_float4(a * rstd * ww.x + bv.x, bb * rstd * ww.y + bv.y, c * rstd * ww.z + bv.z,
+                     d * rstd * ww.w + bv.w);
 }
 
 struct RowParams {
@@ -67,79 +64,85 @@ struct RowParams {
   float eps;
 };
 
-template <int VPL>
+// The row kernels run one block per row, one float4 of the row per thread
+// (blockDim = C/4), so every load of a row is in flight at once; rows beyond
+// the grid are taken in a grid-stride loop.
+
 __global__ void __launch_bounds__(256) embed_ln_kernel(const RowParams p) {
-  const int lane = threadIdx.x & 31;
-  const int TW = gridDim.x * (blockDim.x >> 5);
+  __shared__ float red[8];
   const int n = *p.n_rows;
-  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n; r += TW) {
+  const int k = threadIdx.x;
+  for (int r = blockIdx.x; r < n; r += gridDim.x) {
     int id = p.ids[r];
     int ps = p.pos[r];
     if (id < 0 || id >= p.vocab) {
-      if (lane == 0) raise_device_error(TQ_DEVERR_BAD_TOKEN);
+      if (k == 0) raise_device_error(TQ_DEVERR_BAD_TOKEN);
       id = 0;
     }
     ps = min(max(ps, 0), p.n_positions - 1);  // real rows are always in range (model.py:163)
-    const float4* te = reinterpret_cast<const float4*>(p.wte + (size_t)id * p.C);
-    const float4* pe = reinterpret_cast<const float4*>(p.wpe + (size_t)ps * p.C);
-    float4* xo = reinterpret_cast<float4*>(p.x + (size_t)r * p.C);
-    float4 v[VPL];
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const float4 a = te[lane + 32 * i], b = pe[lane + 32 * i];
-      v[i] = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
-      xo[lane + 32 * i] = v[i];
-    }
-    ln_row<VPL>(v, reinterpret_cast<const float4*>(p.ln_w), reinterpret_cast<const float4*>(p.ln_b),
-                reinterpret_cast<float4*>(p.xa + (size_t)r * p.C), lane, p.C, p.eps);
+    const float4 a = reinterpret_cast<const float4*>(p.wte + (size_t)id * p.C)[k];
+    const float4 b = reinterpret_cast<const float4*>(p.wpe + (size_t)ps * p.C)[k];
+    const float4 v = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+    reinterpret_cast<float4*>(p.x + (size_t)r * p.C)[k] = v;
+    reinterpret_cast<float4*>(p.xa + (size_t)r * p.C)[k] =
+        ln_value(v, reinterpret_cast<const float4*>(p.ln_w), reinterpret_cast<const float4*>(p.ln_b), p.C,
+                 p.eps, red);
   }
 }
 
-template <int VPL>
+// NP > 0: exactly NP partial sums, loads unrolled; NP == 0: p.n_parts, looped.
+template <int NP>
 __global__ void __launch_bounds__(256) bias_residual_ln_kernel(const RowParams p) {
-  const int lane = threadIdx.x & 31;
-  const int TW = gridDim.x * (blockDim.x >> 5);
+  __shared__ float red[8];
   const int n = *p.n_rows;
-  const float4* bias = reinterpret_cast<const float4*>(p.bias);
-  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n; r += TW) {
-    float4* xr = reinterpret_cast<float4*>(p.x + (size_t)r * p.C);
-    const float4* yr = reinterpret_cast<const float4*>(p.y + (size_t)r * p.C);
-    float4 v[VPL];
+  const int k = threadIdx.x;
+  const float4 b = reinterpret_cast<const float4*>(p.bias)[k];
+  for (int r = blockIdx.x; r < n; r += gridDim.x) {
+    const float4* yr = reinterpret_cast<const float4*>(p.y + (size_t)r * p.C) + k;
+    const long long ps4 = p.part_stride >> 2;
+    float4 y = yr[0];
+    if (NP > 0) {
+      float4 t[NP > 1 ? NP - 1 : 1];
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int k = lane + 32 * i;
-      float4 y = yr[k];
-      for (int s = 1; s < p.n_parts; ++s) {  // split-K partial sums of the linear
-        const float4 t = reinterpret_cast<const float4*>(p.y + s * p.part_stride + (size_t)r * p.C)[k];
+      for (int s = 1; s < NP; ++s) t[s - 1] = yr[s * ps4];
+#pragma unroll
+      for (int s = 1; s < NP; ++s) {  // same order as the looped form: ((y0 + y1) + y2) + ...
+        y.x += t[s - 1].x;
+        y.y += t[s - 1].y;
+        y.z += t[s - 1].z;
+        y.w += t[s - 1].w;
+      }
+    } else {
+      for (int s = 1; s < p.n_parts; ++s) {
+        const float4 t = yr[s * ps4];
         y.x += t.x;
         y.y += t.y;
         y.z += t.z;
         y.w += t.w;
       }
-      const float4 a = xr[k], b = bias[k];
-      // x + (y + b): the linear's bias first, as addmm produces it.
-      v[i] = make_float4(a.x + (y.x + b.x), a.y + (y.y + b.y), a.z + (y.z + b.z), a.w + (y.w + b.w));
-      xr[k] = v[i];
     }
+    float4* xr = reinterpret_cast<float4*>(p.x + (size_t)r * p.C) + k;
+    const float4 a = *xr;
+    // x + (y + b): the linear's bias first, as addmm produces it.
+    const float4 v = make_float4(a.x + (y.x + b.x), a.y + (y.y + b.y), a.z + (y.z + b.z), a.w + (y.w + b.w));
+    *xr = v;
     if (p.ln_w != nullptr)
-      ln_row<VPL>(v, reinterpret_cast<const float4*>(p.ln_w), reinterpret_cast<const float4*>(p.ln_b),
-                  reinterpret_cast<float4*>(p.xa + (size_t)r * p.C), lane, p.C, p.eps);
+      reinterpret_cast<float4*>(p.xa + (size_t)r * p.C)[k] =
+          ln_value(v, reinterpret_cast<const float4*>(p.ln_w), reinterpret_cast<const float4*>(p.ln_b), p.C,
+                   p.eps, red);
   }
 }
 
-template <int VPL>
 __global__ void __launch_bounds__(256) layernorm_rows_kernel(const RowParams p) {
-  const int lane = threadIdx.x & 31;
-  const int TW = gridDim.x * (blockDim.x >> 5);
+  __shared__ float red[8];
   const int n = *p.n_rows;
-  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n; r += TW) {
+  const int k = threadIdx.x;
+  for (int r = blockIdx.x; r < n; r += gridDim.x) {
     const int src = p.rows ? p.rows[r] : r;
-    const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)src * p.C);
-    float4 v[VPL];
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) v[i] = xr[lane + 32 * i];
-    ln_row<VPL>(v, reinterpret_cast<const float4*>(p.ln_w), reinterpret_cast<const float4*>(p.ln_b),
-                reinterpret_cast<float4*>(p.xa + (size_t)r * p.C), lane, p.C, p.eps);
+    const float4 v = reinterpret_cast<const float4*>(p.x + (size_t)src * p.C)[k];
+    reinterpret_cast<float4*>(p.xa + (size_t)r * p.C)[k] =
+        ln_value(v, reinterpret_cast<const float4*>(p.ln_w), reinterpret_cast<const float4*>(p.ln_b), p.C,
+                 p.eps, red);
   }
 }
 
@@ -161,7 +164,9 @@ struct GeluParams {
   int gelu;             // 1: gelu_tanh(sum + bias); 0: sum + bias
 };
 
-// out = gelu_tanh(sum_s h_s + bias)  (or just the biased sum).
+// out = gelu_tanh(sum_s h_s + bias)  (or just the biased sum).  NP > 0:
+// exactly NP partial sums, loads unrolled; NP == 0: p.n_parts, looped.
+template <int NP>
 __global__ void __launch_bounds__(256) bias_gelu_kernel(const GeluParams p) {
   const long long f4 = p.F >> 2;
   const long long total = (long long)(*p.n_rows) * f4;
@@ -173,12 +178,25 @@ __global__ void __launch_bounds__(256) bias_gelu_kernel(const GeluParams p) {
        i += (long long)gridDim.x * blockDim.x) {
     const float4 b = bias[i % f4];
     float4 v = h[i];
-    for (int s = 1; s < p.n_parts; ++s) {
-      const float4 t = h[s * ps4 + i];
-      v.x += t.x;
-      v.y += t.y;
-      v.z += t.z;
-      v.w += t.w;
+    if (NP > 0) {
+      float4 t[NP > 1 ? NP - 1 : 1];
+#pragma unroll
+      for (int s = 1; s < NP; ++s) t[s - 1] = h[s * ps4 + i];
+#pragma unroll
+      for (int s = 1; s < NP; ++s) {
+        v.x += t[s - 1].x;
+        v.y += t[s - 1].y;
+        v.z += t[s - 1].z;
+        v.w += t[s - 1].w;
+      }
+    } else {
+      for (int s = 1; s < p.n_parts; ++s) {
+        const float4 t = h[s * ps4 + i];
+        v.x += t.x;
+        v.y += t.y;
+        v.z += t.z;
+        v.w += t.w;
+      }
     }
     if (p.gelu) {
       v.x = gelu_tanh(v.x + b.x);

@@ -23,31 +23,32 @@ struct KvWriteParams {
   const int* n_tokens;   // device-resident count
 };
 
-// One warp per (token, K or V): 16-byte loads of the contiguous n_head*64
-// source floats, 16-byte stores into n_head pool rows of 256 bytes each.
-__global__ void __launch_bounds__(256) kv_write_kernel(const KvWriteParams p) {
-  const int lane = threadIdx.x & 31;
-  const int TW = gridDim.x * (blockDim.x >> 5);
-  const int total = *p.n_tokens * 2;
-  const int per_row4 = p.n_head * 16;  // float4 per K (or V) row of one token
+// One block per token: thread t copies float4 t of the token's K and V rows
+// (2 * n_head * 16 float4), 16-byte loads of contiguous source floats and
+// 16-byte stores into 2 * n_head pool rows of 256 bytes each.
+__global__ void __launch_bounds__(1024) kv_write_kernel(const KvWriteParams p) {
+  const int n_tok = *p.n_tokens;
+  const int per_kv4 = p.n_head * 16;  // float4 per K (or V) row of one token
   const long long pool_slots = p.num_blocks << p.log2_bs;
-  for (int u = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < total; u += TW) {
-    const int n = u >> 1;
-    const int kv = u & 1;
+  const size_t head_stride4 = (size_t)p.block_size * 16;
+  for (int n = blockIdx.x; n < n_tok; n += gridDim.x) {
     const long long slot = p.slots[n];
     if (slot < 0 || slot >= pool_slots) {
-      if (lane == 0) raise_device_error(TQ_DEVERR_BAD_SLOT);
+      if (threadIdx.x == 0) raise_device_error(TQ_DEVERR_BAD_SLOT);
       continue;
     }
     const long long blk = slot >> p.log2_bs;
     const int off = (int)(slot & (p.block_size - 1));
-    const float4* src =
-        reinterpret_cast<const float4*>(p.qkv + (size_t)n * p.qkv_stride + (kv ? p.v_col : p.k_col));
-    float4* dst = reinterpret_cast<float4*>(
-        p.pool + ((((size_t)blk * p.n_layer + p.layer) * 2 + kv) * p.n_head) * (size_t)p.block_size * 64 +
-        (size_t)off * 64);
-    const size_t head_stride4 = (size_t)p.block_size * 16;
-    for (int f = lane; f < per_row4; f += 32) dst[(f >> 4) * head_stride4 + (f & 15)] = src[f];
+    for (int f = threadIdx.x; f < 2 * per_kv4; f += blockDim.x) {
+      const int kv = f >= per_kv4;
+      const int g = f - kv * per_kv4;
+      const float4 v = reinterpret_cast<const float4*>(p.qkv + (size_t)n * p.qkv_stride +
+                                                       (kv ? p.v_col : p.k_col))[g];
+      float4* dst = reinterpret_cast<float4*>(
+          p.pool + ((((size_t)blk * p.n_layer + p.layer) * 2 + kv) * p.n_head) * (size_t)p.block_size * 64 +
+          (size_t)off * 64);
+      dst[(g >> 4) * head_stride4 + (g & 15)] = v;
+    }
   }
 }
 
