@@ -45,6 +45,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 PEAKS_PATH = ROOT / "MEASURED_PEAKS.json"
+# ncu captures of the attention kernel on each workload's shape: DRAM traffic
+# (read + write) over algorithmic bytes, scaled here to this run's launches.
+TRAFFIC_PROFILES = {"cfg2": ROOT / "profiles" / "paged_attention_cfg2.md",
+                    "cfg4": ROOT / "profiles" / "paged_attention_cfg4_small.md"}  # fmt: skip
 FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 2**20
 
@@ -172,6 +176,54 @@ class ClockSampler:
             "reasons": sorted(self.reasons),
             "samples": len(self.samples),
         }
+
+
+def traffic_ratio(workload: str) -> float | None:
+    import re
+
+    path = TRAFFIC_PROFILES.get(workload)
+    if path is None or not path.exists():
+        return None
+    m = re.search(r"traffic_over_algorithmic:\s*([0-9.]+)", path.read_text())
+    return float(m.group(1)) if m else None
+
+
+def kernel_table(model, a, seqs, spec, steps: int = 10) -> str:
+    """Per-kernel device time over `steps` public-API decode steps (CUPTI via
+    torch.profiler, kernels back to back as in the run)."""
+    import collections
+
+    from torch.profiler import ProfilerActivity, profile
+
+    from tokquay_b200 import paged_forward
+
+    def step():
+        toks = paged_forward(model, a, seqs).argmax(-1).tolist()
+        for s, t in zip(seqs, toks):
+            s.append_token(t)
+            if spec["grow"]:
+                a.append_slot(s)
+            else:
+                s.num_cached_tokens -= 1
+                s.output_token_ids.pop()
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            step()
+        torch.cuda.synchronize()
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            k = e.name.split("(")[0][:90]
+            agg[k][0] += 1
+            agg[k][1] += getattr(e, "device_time", None) or e.cuda_time
+    tot = sum(v[1] for v in agg.values())
+    lines = [f"device time per step: {tot / steps:.1f} us", "| kernel | us/step | share | launches/step | avg us |",
+             "|---|---|---|---|---|"]  # fmt: skip
+    for k, (n, t) in sorted(agg.items(), key=lambda x: -x[1][1])[:20]:
+        lines.append(f"| {k} | {t / steps:.1f} | {100 * t / tot:.1f}% | {n / steps:.1f} | {t / n:.2f} |")
+    return "\n".join(lines)
 
 
 # ------------------------------------------------------------------------------ setup
@@ -430,7 +482,11 @@ def run_ours(args, world, rank, local):
                 "peak": peak,
                 "unit": "GB/s",
                 "frac": achieved / peak,
-                "traffic": None,
+                "traffic": (traffic_ratio(args.workload) or float("nan")) * avg_bytes
+                if traffic_ratio(args.workload) else None,
+                "traffic_source": f"ncu DRAM read+write / algorithmic bytes = {traffic_ratio(args.workload)} "
+                                  f"on a captured launch ({TRAFFIC_PROFILES.get(args.workload)}), times this "
+                                  "run's average algorithmic bytes per launch" if traffic_ratio(args.workload) else None,
                 "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
                 "algorithmic_bytes_per_launch": avg_bytes,
                 "avg_launch_ms": avg_attn_ms,
@@ -450,6 +506,8 @@ def run_ours(args, world, rank, local):
             "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
+    if args.kernel_table and rank == 0:
+        log(kernel_table(model, a, seqs, spec))
     return result
 
 
@@ -538,6 +596,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graphs", action="store_true", help="launch every kernel from Python (no CUDA graphs)")
     ap.add_argument("--num-seqs", type=int, default=0, help="override the workload's sequence count (profiling)")
+    ap.add_argument("--kernel-table", action="store_true",
+                    help="after the run, print per-kernel device times of 10 more decode steps (stderr)")
     ap.add_argument("--pool-gb", type=float, default=0, help="override the KV pool size in GB (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
