@@ -67,47 +67,10 @@ def log(*a):
 
 
 # ------------------------------------------------------------------------------ distributed
-def dist_setup():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
-    elif torch.cuda.is_available():
-        torch.cuda.set_device(local)
-    return world, rank, local
-
-
-def barrier(world):
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-
-
-def max_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
-
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
-def sum_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
-
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+# One replica per GPU (tokquay_b200.replicas): no collective on the data path,
+# host reductions only for the barrier and the max-over-ranks timing.
+from tokquay_b200.replicas import ReplicaInfo, barrier, max_over_ranks, replica_seed, sum_over_ranks  # noqa: E402
+from tokquay_b200 import replicas as _replicas  # noqa: E402
 
 
 # ------------------------------------------------------------------------------ clocks
@@ -309,7 +272,7 @@ def run_ours(args, world, rank, local):
     model = make_model(device)
     cfg = model.cfg
     a = make_allocator(spec, cfg, device)
-    seed = 2 + rank  # each replica decodes its own sequences
+    seed = replica_seed(2, rank)  # each replica decodes its own sequences
     K, Wm = args.steps, args.warmup
     total_steps = K + Wm
     B = spec["n_seqs"]
@@ -485,7 +448,7 @@ def run_ours(args, world, rank, local):
                 "traffic": (traffic_ratio(args.workload) or float("nan")) * avg_bytes
                 if traffic_ratio(args.workload) else None,
                 "traffic_source": f"ncu DRAM read+write / algorithmic bytes = {traffic_ratio(args.workload)} "
-                                  f"on a captured launch ({TRAFFIC_PROFILES.get(args.workload)}), times this "
+                                  f"on a captured launch ({TRAFFIC_PROFILES[args.workload].relative_to(ROOT)}), times this "
                                   "run's average algorithmic bytes per launch" if traffic_ratio(args.workload) else None,
                 "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
                 "algorithmic_bytes_per_launch": avg_bytes,
@@ -603,21 +566,24 @@ def main():
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")
         args.warmup = 3
-    world, rank, local = dist_setup()
     if args.impl == "reference":
+        # The CPU reference arm runs on rank 0 alone; no process group is needed.
+        info = ReplicaInfo.from_env()
+        world, rank, local = info.world, info.rank, info.local
         res = run_reference(args, world, rank)
-    else:
-        res = run_ours(args, world, rank, local)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            rate, sample, threads = cpu_oracle_rate(workload_spec(args), 16, 2, 1)
-            res["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
-                                   "sample": sample}  # fmt: skip
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    info = _replicas.setup()
+    world, rank, local = info.world, info.rank, info.local
+    res = run_ours(args, world, rank, local)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, sample, threads = cpu_oracle_rate(workload_spec(args), 16, 2, 1)
+        res["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
+                               "sample": sample}  # fmt: skip
     if rank == 0 and res is not None:
         print(json.dumps(res), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
+    _replicas.teardown(info)
 
 
 if __name__ == "__main__":
