@@ -143,8 +143,10 @@ TQ_API int tq_kv_write(float* pool, int64_t num_blocks, int32_t n_layer, int32_t
  * partial_counters ([P] int32, all zero before the first launch; every launch
  * that completes leaves them zero again), P >= TQ_PLAN_NUM_PARTIALS of every
  * plan launched with it (max_partials; NULL scratch is fine when it is 0).
- * Launches that share scratch must not overlap on the GPU.  max_items sizes
- * the grid.  One kernel launch on `stream`; the split-K merge is fused. */
+ * Launches that share scratch must not overlap on the GPU.  max_items is the
+ * capacity of work_items (the kernel may read any of its max_items entries,
+ * and uses the first *d_num_items) and sizes the grid.  One kernel launch on
+ * `stream`; the split-K merge is fused. */
 TQ_API int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64_t q_row_stride,
                        const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
                        int32_t block_size, int32_t head_dim, int32_t layer,

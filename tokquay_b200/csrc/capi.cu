@@ -220,13 +220,14 @@ int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64
   p.table_stride = table_stride;
   p.items = reinterpret_cast<const WorkItem*>(work_items);
   p.n_items = d_num_items;
+  p.max_items = max_items;
   p.part_ml = partial_ml;
   p.part_acc = partial_acc;
   p.part_cnt = partial_counters;
   p.scale_log2 = scale * 1.4426950408889634f;
   const int64_t units = (int64_t)max_items * n_head;
   const int grid = (int)std::min<int64_t>((units + kAttnWarps - 1) / kAttnWarps, sms);
-  paged_attention_kernel<<<grid, kAttnWarps * 32, kAttnSmemBytes, (cudaStream_t)stream>>>(p);
+  paged_attention_kernel<<<grid, kAttnThreads, kAttnSmemBytes, (cudaStream_t)stream>>>(p);
   return check_launch("paged_attention");
 }
 
@@ -337,13 +338,14 @@ int tq_paged_attention_noalloc(float* out, int64_t out_row_stride, const float* 
   p.table_stride = table_stride;
   p.items = reinterpret_cast<const WorkItem*>(work_items);
   p.n_items = d_num_items;
+  p.max_items = max_items;
   p.part_cnt = reinterpret_cast<int*>(base);
   p.part_ml = reinterpret_cast<float*>(base + kNoAllocCounterBytes);
   p.part_acc = reinterpret_cast<float*>(base + kNoAllocCounterBytes + kNoAllocMlBytes);
   p.scale_log2 = scale * 1.4426950408889634f;
   const int64_t units = (int64_t)max_items * n_head;
   const int grid = (int)std::min<int64_t>((units + kAttnWarps - 1) / kAttnWarps, sms);
-  paged_attention_kernel<<<grid, kAttnWarps * 32, kAttnSmemBytes, s>>>(p);
+  paged_attention_kernel<<<grid, kAttnThreads, kAttnSmemBytes, s>>>(p);
   return check_launch("paged_attention_noalloc");
 }
 
@@ -354,6 +356,16 @@ TQ_API int tq_debug_attention_trace(unsigned long long* host, int32_t n_warps) {
   const int n = std::min<int>(n_warps, kTraceWarps);
   const cudaError_t e =
       cudaMemcpyFromSymbol(host, g_attn_trace, (size_t)n * kTraceSlots * sizeof(unsigned long long));
+  if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "trace read: %s", cudaGetErrorString(e));
+  return TQ_OK;
+}
+
+// Per-chunk timeline of the last launch: [n_warps][32][3] uint64 =
+// {issue ns, data-ready ns, bytes}.
+TQ_API int tq_debug_attention_chunks(unsigned long long* host, int32_t n_warps) {
+  const int n = std::min<int>(n_warps, kTraceWarps);
+  const cudaError_t e =
+      cudaMemcpyFromSymbol(host, g_attn_chunks, (size_t)n * kTraceChunks * 3 * sizeof(unsigned long long));
   if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "trace read: %s", cudaGetErrorString(e));
   return TQ_OK;
 }

@@ -48,6 +48,12 @@ namespace tq {
 #ifndef TQ_ATTN_WARPS
 #define TQ_ATTN_WARPS 6
 #endif
+#ifndef TQ_ATTN_EARLY_REFILL
+#define TQ_ATTN_EARLY_REFILL 1
+#endif
+#ifndef TQ_ATTN_SC_FENCE
+#define TQ_ATTN_SC_FENCE 0
+#endif
 constexpr int kHeadDim = 64;
 constexpr int kChunk = TQ_ATTN_CHUNK;        // keys per pipeline stage (16 or 32)
 constexpr int kMaxRows = TQ_ATTN_MAX_ROWS;   // query rows per work item
@@ -66,6 +72,9 @@ static_assert(kChunk == 16 || kChunk == 32, "chunk of 16 or 32 keys");
 constexpr int kTraceWarps = 8192;
 constexpr int kTraceSlots = 16;
 __device__ unsigned long long g_attn_trace[kTraceWarps * kTraceSlots];
+// Per warp, per chunk (first kTraceChunks): {issue ns, data-ready ns, bytes}.
+constexpr int kTraceChunks = 32;
+__device__ unsigned long long g_attn_chunks[kTraceWarps * kTraceChunks * 3];
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -115,6 +124,7 @@ struct AttnParams {
   int table_stride;
   const WorkItem* items;
   const int* n_items;    // device-resident count
+  int max_items;         // capacity of `items` (entries that may be read, valid or not)
   float* part_ml;        // [P][2]  (m in log2 units, l)
   float* part_acc;       // [P][64]
   int* part_cnt;         // [P] split counters (zero between launches)
@@ -142,8 +152,11 @@ __device__ __forceinline__ WorkItem item_from_lanes(int v) {
   return w;
 }
 
-__device__ __forceinline__ int item_lane_load(const AttnParams& p, int unit, int n_units, int lane) {
-  return (unit < n_units && lane < 8)
+// Loads are bounded by the buffer's capacity, not by the device-resident
+// count, so they need not wait for the count; a unit past the count is never
+// used (the consumers check it against n_units).
+__device__ __forceinline__ int item_lane_load(const AttnParams& p, int unit, int lane) {
+  return (unit < p.max_items * p.n_head && lane < 8)
              ? __ldg(reinterpret_cast<const int*>(p.items) + (size_t)(unit / p.n_head) * 8 + lane)
              : 0;
 }
@@ -288,13 +301,26 @@ __device__ __forceinline__ void merge_if_last(const AttnParams& p, const WorkIte
   TQ_TRACE(long long tm0 = clock64();)
   int last = 0;
   if (lane == 0) {
-    __threadfence();  // this split's partial is visible before the count says so
+#if TQ_ATTN_SC_FENCE
+    __threadfence();
     last = atomicAdd(p.part_cnt + idx0, 1) == nsplit - 1;
+#else
+    // Release: the partial this warp stored (lanes 0-3, ordered before lane 0
+    // by the __syncwarp above) is visible before the count says so.  Acquire:
+    // the last split sees every other split's partial.
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.part_cnt + idx0) : "memory");
+    last = old == nsplit - 1;
+#endif
   }
   last = __shfl_sync(kFullMask, last, 0);
   TQ_TRACE(if (lane == 0) tr_sub[4] += clock64() - tm0; tm0 = clock64();)
   if (!last) return;
-  __threadfence();  // and every other split's partial is visible to this warp
+#if TQ_ATTN_SC_FENCE
+  __threadfence();
+#else
+  __syncwarp();  // lane 0's acquire orders the other lanes' reads of the partials below
+#endif
   float mmax = -INFINITY;
   for (int s = lane; s < nsplit; s += 32) mmax = fmaxf(mmax, __ldcg(p.part_ml + 2 * (idx0 + s)));
   mmax = warp_max(mmax);
@@ -380,154 +406,176 @@ __device__ __forceinline__ void finish_rows(const AttnParams& p, const WorkItem&
   }
 }
 
-__global__ void __launch_bounds__(kAttnWarps * 32, 1) paged_attention_kernel(const AttnParams p) {
+// Block layout: warps 0..kAttnWarps-1 are consumers, warps kAttnWarps.. their
+// producers; consumer w and producer kAttnWarps+w share ring w.
+constexpr int kAttnThreads = 2 * kAttnWarps * 32;
+
+__global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const AttnParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  unsigned char* wsm = smem + warp * kWarpSmemBytes;
-  const uint32_t bar0 = smem_addr(wsm + kStages * kStageBytes);
+  const bool producer = warp >= kAttnWarps;
+  const int pair = producer ? warp - kAttnWarps : warp;
+  unsigned char* wsm = smem + pair * kWarpSmemBytes;
+  const uint32_t full0 = smem_addr(wsm + kStages * kStageBytes);  // TMA bytes landed
+  const uint32_t empty0 = full0 + 8 * kStages;                    // consumer done reading
 
   const int H = p.n_head;
+  const int wslot = blockIdx.x * kAttnWarps + pair;
+  const int first_item_word = producer ? item_lane_load(p, wslot, lane) : 0;  // overlaps the count
   const int n_units = *p.n_items * H;
   const int TW = gridDim.x * kAttnWarps;
-  // Units are visited in snake order: round r gives this warp unit
+  // Units are visited in snake order: round r gives this pair unit
   // r*TW + w on even rounds and r*TW + TW-1-w on odd ones.  The planner sorts
-  // items longest first, so each warp gets a long and a short unit in every
-  // pair of rounds and all warps finish together.
-  const int wslot = blockIdx.x * kAttnWarps + warp;
+  // items longest first, so each pair gets a long and a short unit in every
+  // pair of rounds and all pairs finish together.  Producer and consumer walk
+  // the same sequence.
   auto unit_of = [&](int round) { return round * TW + ((round & 1) ? TW - 1 - wslot : wslot); };
-  const int first_unit = wslot;
-  TQ_TRACE(const int gw = first_unit; unsigned long long tr_start = global_ns(), tr_first = 0;
-           long long tr_wait = 0, tr_comp = 0, tr_fin = 0, tr_refill = 0, tr_chunks = 0;
+  TQ_TRACE(const int gw = wslot; unsigned long long* trec = g_attn_trace + (size_t)gw * kTraceSlots;
            long long tr_sub[8] = {0, 0, 0, 0, 0, 0, 0, 0};)
-  if (first_unit >= n_units) return;  // warp-uniform; warps never synchronise with each other
 
-  if (lane == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(bar0 + 8 * s, 1);
+  if (!producer && lane == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full0 + 8 * s, 1);   // the producer's arrive_expect_tx + the copies' bytes
+      mbar_init(empty0 + 8 * s, 1);  // the consumer's arrive
+    }
     mbar_init_fence();
   }
-  __syncwarp();
+  __syncthreads();  // every ring's barriers are initialised before either warp of a pair uses them
+  if (wslot >= n_units) return;  // pair-uniform: producer and consumer leave together
 
-  // ---- producer cursor: warp-uniform; lane 0 issues the copies ---------------
-  // Block ids of the next chunk to issue are loaded one chunk ahead (lane i
-  // holds block i of the chunk) and the next unit's work item one unit ahead,
-  // so those global loads overlap a chunk of compute instead of stalling it.
-  // A unit's block ids (at most kUnitBlocks; the planner keeps units that
-  // short) live in two registers per lane: lane i holds blocks kb0+i and
-  // kb0+32+i of the unit's key range.  They are loaded one unit ahead, and
-  // the work item two units ahead, so neither load sits on the path between
-  // two chunks.
-  int p_round = 0;
-  int p_unit = first_unit;
-  WorkItem p_it = item_from_lanes(item_lane_load(p, p_unit, n_units, lane));
-  int p_chunk = p_it.cbeg;
-  int pf_a = 0, pf_b = 0;   // current unit's block ids
-  int nx_a = 0, nx_b = 0;   // next unit's block ids (in flight)
-  auto load_unit_blocks = [&](const WorkItem& w, bool valid, int& a, int& b) {
-    if (!valid) return;
-    const int kb0 = (w.cbeg * kChunk) >> p.log2_bs;
-    const int kend = min(w.pos0 + w.nrows, w.cend * kChunk);
-    const int n = ((kend - 1) >> p.log2_bs) - kb0 + 1;
-    const int* tbl = p.tables + (size_t)w.seq * p.table_stride + kb0;
-    a = lane < n ? __ldg(tbl + lane) : 0;
-    b = lane + 32 < n ? __ldg(tbl + 32 + lane) : 0;
-  };
-  load_unit_blocks(p_it, true, pf_a, pf_b);
-  bool nx_valid = unit_of(1) < n_units;
-  WorkItem nx_it = item_from_lanes(item_lane_load(p, unit_of(1), n_units, lane));
-  load_unit_blocks(nx_it, nx_valid, nx_a, nx_b);
-  int nx2_item = item_lane_load(p, unit_of(2), n_units, lane);
-  bool p_live = true;
-  int issued = 0, consumed = 0;
-
-  // Issue chunk p_chunk of the current unit into the next stage.  Each lane
-  // describes one copy (K or V rows of one block, or a q row), and the copies
-  // go out as one warp-wide cp.async.bulk: the TMA issue cost is paid per warp
-  // instruction, not per copy.
-  auto issue = [&]() {
-    const int s = issued % kStages;
-    unsigned char* stage = wsm + s * kStageBytes;
-    const uint32_t bar = bar0 + 8 * s;
-    const ChunkSpan sp = chunk_span(p, p_it, p_chunk);
-    const bool first = (p_chunk == p_it.cbeg);
-    const int bs = p.block_size;
-    const int h = p_unit % H;
-    const int unit_kb0 = (p_it.cbeg * kChunk) >> p.log2_bs;
-    const int n_kv = 2 * sp.nblk;
-    const int n_desc = n_kv + (first ? p_it.nrows : 0);
-    const uint32_t sK = smem_addr(stage);
-    const size_t kv_stride = (size_t)H * bs * kHeadDim;  // K tile -> V tile
-    TQ_TRACE(long long ti0 = clock64();)
-    // Descriptor d: copies `bytes` from `src` to shared address `dst`.
-    auto describe = [&](int d, const float*& src, uint32_t& dst, uint32_t& bytes) {
-      // Every lane shuffles (the source lane varies per lane).
-      const int rel = (sp.kb0 - unit_kb0) + min(d, max(n_kv - 1, 0)) / 2;
-      const int a = __shfl_sync(kFullMask, pf_a, rel & 31);
-      const int b = __shfl_sync(kFullMask, pf_b, rel & 31);
-      bytes = 0;
-      if (d < n_kv) {
-        const long long blk = rel < 32 ? a : b;
-        if (blk < 0 || blk >= p.num_blocks) {
-          raise_device_error(TQ_DEVERR_BAD_BLOCK);
-          return;
-        }
-        const int kv = d & 1;
-        if (bs <= kChunk) {
-          const int kb = sp.kb0 + (d >> 1);
-          const int rows = min(bs, sp.key0 + sp.nkeys - kb * bs);
-          src = p.pool + pool_tile_offset(p, blk, 0, h) + kv * kv_stride;
-          dst = sK + kv * kKBytes + (uint32_t)(kb * bs - sp.key0) * kRowBytes;
-          bytes = rows * kRowBytes;
-        } else {
-          src = p.pool + pool_tile_offset(p, blk, 0, h) + kv * kv_stride +
-                (size_t)(sp.key0 & (bs - 1)) * kHeadDim;
-          dst = sK + kv * kKBytes;
-          bytes = sp.nkeys * kRowBytes;
-        }
-      } else if (d < n_desc) {
-        const int r = d - n_kv;
-        src = p.q + (size_t)(p_it.row0 + r) * p.q_stride + h * kHeadDim;
-        dst = sK + 2 * kKBytes + r * kRowBytes;
-        bytes = kRowBytes;
-      }
+  if (producer) {
+    // ---- producer: work metadata and TMA issue, up to kStages chunks ahead ----
+    // Block ids of the current unit's key range (at most kUnitBlocks; the
+    // planner keeps units that short) live in two registers per lane: lane i
+    // holds blocks kb0+i and kb0+32+i.  They are loaded one unit ahead, and
+    // the work item two units ahead, so neither load sits between two issues.
+    TQ_TRACE(long long tr_empty = 0;)
+    int p_round = 0;
+    int p_unit = wslot;
+    WorkItem p_it = item_from_lanes(first_item_word);
+    int p_chunk = p_it.cbeg;
+    int pf_a = 0, pf_b = 0;  // current unit's block ids
+    int nx_a = 0, nx_b = 0;  // next unit's block ids (in flight)
+    auto load_unit_blocks = [&](const WorkItem& w, bool valid, int& a, int& b) {
+      if (!valid) return;
+      const int kb0 = (w.cbeg * kChunk) >> p.log2_bs;
+      const int kend = min(w.pos0 + w.nrows, w.cend * kChunk);
+      const int n = ((kend - 1) >> p.log2_bs) - kb0 + 1;
+      const int* tbl = p.tables + (size_t)w.seq * p.table_stride + kb0;
+      a = lane < n ? __ldg(tbl + lane) : 0;
+      b = lane + 32 < n ? __ldg(tbl + 32 + lane) : 0;
     };
-    uint32_t total = 0;
-    for (int base = 0; base < n_desc; base += 32) {
-      const float* src = nullptr;
-      uint32_t dst = 0, bytes = 0;
-      describe(base + lane, src, dst, bytes);
-      total += __reduce_add_sync(kFullMask, bytes);
-    }
-    TQ_TRACE(if (lane == 0) tr_sub[0] += clock64() - ti0; ti0 = clock64();)
-    if (lane == 0) {
-      if (first) {  // the consumer picks the unit's work item up from here
-        StageHeader* hd = reinterpret_cast<StageHeader*>(stage + 2 * kKBytes + kQBytes);
-        hd->it = p_it;
-        hd->h = h;
-        hd->c = p_chunk;
-      }
-      // A reused stage needs no proxy fence: every lane's reads of it fed the
-      // arithmetic that preceded the warp's __syncwarp, so they are complete
-      // before the copies below are issued (the completion-before-reissue
-      // argument TMA pipelines rely on).
-      mbar_arrive_expect_tx(bar, total);
-    }
-    __syncwarp();
-    for (int base = 0; base < n_desc; base += 32) {
-      const float* src = nullptr;
-      uint32_t dst = 0, bytes = 0;
-      describe(base + lane, src, dst, bytes);
-      if (bytes) bulk_copy_g2s(dst, src, bytes, bar);
-    }
-    TQ_TRACE(if (lane == 0) tr_sub[1] += clock64() - ti0;)
-    ++issued;
-  };
+    load_unit_blocks(p_it, true, pf_a, pf_b);
+    bool nx_valid = unit_of(1) < n_units;
+    WorkItem nx_it = item_from_lanes(item_lane_load(p, unit_of(1), lane));
+    load_unit_blocks(nx_it, nx_valid, nx_a, nx_b);
+    int nx2_item = item_lane_load(p, unit_of(2), lane);
+    int issued = 0;
+    bool ok = true;
 
-  auto advance = [&]() {
-    TQ_TRACE(long long ta0 = clock64();)
-    if (++p_chunk == p_it.cend) {
-      p_unit = unit_of(++p_round);
-      if (p_unit < n_units) {
+    for (;;) {
+      const int s = issued % kStages;
+      if (issued >= kStages) {  // wait for the consumer to release the stage
+        TQ_TRACE(long long te0 = clock64();)
+        ok = mbar_wait_bounded(empty0 + 8 * s, (uint32_t)(issued / kStages - 1) & 1u);
+        TQ_TRACE(tr_empty += clock64() - te0;)
+        if (!__all_sync(kFullMask, ok)) {
+          ok = false;
+          break;
+        }
+      }
+      // Issue chunk p_chunk of the current unit into stage s.  Each lane
+      // describes one copy (K or V rows of one block, or a q row), and the
+      // copies go out as one warp-wide cp.async.bulk.
+      unsigned char* stage = wsm + s * kStageBytes;
+      const uint32_t bar = full0 + 8 * s;
+      const ChunkSpan sp = chunk_span(p, p_it, p_chunk);
+      const bool first = (p_chunk == p_it.cbeg);
+      const int bs = p.block_size;
+      const int h = p_unit % H;
+      const int unit_kb0 = (p_it.cbeg * kChunk) >> p.log2_bs;
+      const int n_kv = 2 * sp.nblk;
+      const int n_desc = n_kv + (first ? p_it.nrows : 0);
+      const uint32_t sK = smem_addr(stage);
+      const size_t kv_stride = (size_t)H * bs * kHeadDim;  // K tile -> V tile
+      TQ_TRACE(long long ti0 = clock64();)
+      auto describe = [&](int d, const float*& src, uint32_t& dst, uint32_t& bytes) {
+        // Every lane shuffles (the source lane varies per lane).
+        const int rel = (sp.kb0 - unit_kb0) + min(d, max(n_kv - 1, 0)) / 2;
+        const int a = __shfl_sync(kFullMask, pf_a, rel & 31);
+        const int b = __shfl_sync(kFullMask, pf_b, rel & 31);
+        bytes = 0;
+        if (d < n_kv) {
+          const long long blk = rel < 32 ? a : b;
+          if (blk < 0 || blk >= p.num_blocks) {
+            raise_device_error(TQ_DEVERR_BAD_BLOCK);
+            return;
+          }
+          const int kv = d & 1;
+          if (bs <= kChunk) {
+            const int kb = sp.kb0 + (d >> 1);
+            const int rows = min(bs, sp.key0 + sp.nkeys - kb * bs);
+            src = p.pool + pool_tile_offset(p, blk, 0, h) + kv * kv_stride;
+            dst = sK + kv * kKBytes + (uint32_t)(kb * bs - sp.key0) * kRowBytes;
+            bytes = rows * kRowBytes;
+          } else {
+            src = p.pool + pool_tile_offset(p, blk, 0, h) + kv * kv_stride +
+                  (size_t)(sp.key0 & (bs - 1)) * kHeadDim;
+            dst = sK + kv * kKBytes;
+            bytes = sp.nkeys * kRowBytes;
+          }
+        } else if (d < n_desc) {
+          const int r = d - n_kv;
+          src = p.q + (size_t)(p_it.row0 + r) * p.q_stride + h * kHeadDim;
+          dst = sK + 2 * kKBytes + r * kRowBytes;
+          bytes = kRowBytes;
+        }
+      };
+      // Descriptors 0..31 stay in registers between the byte count and the
+      // issue; more than 32 (block_size < 16) are described twice.
+      const float* src0 = nullptr;
+      uint32_t dst0 = 0, bytes0 = 0;
+      describe(lane, src0, dst0, bytes0);
+      uint32_t total = __reduce_add_sync(kFullMask, bytes0);
+      for (int base = 32; base < n_desc; base += 32) {
+        const float* src = nullptr;
+        uint32_t dst = 0, bytes = 0;
+        describe(base + lane, src, dst, bytes);
+        total += __reduce_add_sync(kFullMask, bytes);
+      }
+      TQ_TRACE(if (lane == 0) tr_sub[0] += clock64() - ti0; ti0 = clock64();)
+      if (lane == 0) {
+        if (first) {  // the consumer picks the unit's work item up from here
+          StageHeader* hd = reinterpret_cast<StageHeader*>(stage + 2 * kKBytes + kQBytes);
+          hd->it = p_it;
+          hd->h = h;
+          hd->c = p_chunk;
+        }
+        // Releases the header store to the consumer's acquiring wait.  A
+        // reused stage needs no proxy fence: the consumer's reads of it fed
+        // arithmetic that completed before its arrive on the empty barrier.
+        mbar_arrive_expect_tx(bar, total);
+        TQ_TRACE(if (gw < kTraceWarps && issued < kTraceChunks) {
+          g_attn_chunks[((size_t)gw * kTraceChunks + issued) * 3] = global_ns();
+          g_attn_chunks[((size_t)gw * kTraceChunks + issued) * 3 + 2] = total;
+        })
+      }
+      __syncwarp();
+      if (bytes0) bulk_copy_g2s(dst0, src0, bytes0, bar);
+      for (int base = 32; base < n_desc; base += 32) {
+        const float* src = nullptr;
+        uint32_t dst = 0, bytes = 0;
+        describe(base + lane, src, dst, bytes);
+        if (bytes) bulk_copy_g2s(dst, src, bytes, bar);
+      }
+      TQ_TRACE(if (lane == 0) tr_sub[1] += clock64() - ti0; ti0 = clock64();)
+      ++issued;
+
+      // Advance the cursor.
+      if (++p_chunk == p_it.cend) {
+        p_unit = unit_of(++p_round);
+        if (p_unit >= n_units) break;
         p_it = nx_it;
         pf_a = nx_a;
         pf_b = nx_b;
@@ -535,100 +583,99 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) paged_attention_kernel(con
         nx_valid = unit_of(p_round + 1) < n_units;
         nx_it = item_from_lanes(nx2_item);
         load_unit_blocks(nx_it, nx_valid, nx_a, nx_b);
-        nx2_item = item_lane_load(p, unit_of(p_round + 2), n_units, lane);
-      } else {
-        p_live = false;
+        nx2_item = item_lane_load(p, unit_of(p_round + 2), lane);
       }
+      TQ_TRACE(if (lane == 0) tr_sub[2] += clock64() - ti0;)
     }
-    TQ_TRACE(if (lane == 0) tr_sub[2] += clock64() - ta0;)
-  };
-
-  auto refill = [&]() {
-    while (p_live && issued < consumed + kStages) {
-      issue();
-      advance();
+    if (!ok) {
+      // The consumer stopped releasing stages.  Give every copy still in
+      // flight a bounded chance to land before the CTA exits, so no bulk copy
+      // targets the shared memory of a finished CTA.
+      for (int k = max(issued - kStages, 0); k < issued; ++k)
+        if (!mbar_wait_bounded(full0 + 8 * (k % kStages), (uint32_t)(k / kStages) & 1u)) break;
     }
-  };
+    TQ_TRACE(if (lane == 0 && gw < kTraceWarps) {
+      trec[6] = tr_empty; trec[8] = tr_sub[0]; trec[9] = tr_sub[1]; trec[10] = tr_sub[2];
+      trec[15] = global_ns();
+    })
+    return;
+  }
 
-  // ---- consumer: everything it needs is in the stage -------------------------
-  // Stages are consumed in issue order, so the consumer tracks the chunk index
-  // itself and reads the work item from a stage header only at a unit start.
+  // ---- consumer: wait, compute, release; everything it needs is in the stage --
+  TQ_TRACE(unsigned long long tr_start = global_ns(), tr_first = 0;
+           long long tr_wait = 0, tr_comp = 0, tr_fin = 0, tr_chunks = 0;)
   float m[kMaxRows], lsum[kMaxRows];
   float4 acc[kMaxRows][4];
   float4 qr[kMaxRows][4];
-  WorkItem it;
-  int h = 0, c = 0;
-  bool at_unit_start = true;
-  bool failed = false;
   const int rot = lane_rot(lane);
-
-  TQ_TRACE(long long tr0 = clock64();)
-  refill();
-  TQ_TRACE(tr_refill += clock64() - tr0;)
-  while (consumed < issued) {
-    const int s = consumed % kStages;
-    const uint32_t parity = (uint32_t)(consumed / kStages) & 1u;
-    TQ_TRACE(tr0 = clock64();)
-    const bool ok = mbar_wait_bounded(bar0 + 8 * s, parity);
-    TQ_TRACE(tr_wait += clock64() - tr0; if (tr_first == 0) tr_first = global_ns(); ++tr_chunks;)
-    if (!__all_sync(kFullMask, ok)) {
-      failed = true;
-      break;
-    }
-    const unsigned char* stage = wsm + s * kStageBytes;
-    if (at_unit_start) {  // take the unit's work item and q rows, reset state
-      const StageHeader* hd = reinterpret_cast<const StageHeader*>(stage + 2 * kKBytes + kQBytes);
-      it = hd->it;
-      h = hd->h;
-      c = it.cbeg;
-      const float4* qsrc = reinterpret_cast<const float4*>(stage + 2 * kKBytes);
-#pragma unroll
-      for (int r = 0; r < kMaxRows; ++r) {
-        m[r] = -INFINITY;
-        lsum[r] = 0.f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          acc[r][i] = make_float4(0.f, 0.f, 0.f, 0.f);
-          qr[r][i] = r < it.nrows ? qsrc[r * (kHeadDim / 4) + (lane & 3) * 4 + ((i + rot) & 3)]
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+  int consumed = 0;
+  bool failed = false;
+  for (int round = 0; unit_of(round) < n_units; ++round) {
+    WorkItem it;
+    int h = 0, c = 0;
+    bool at_unit_start = true;
+    do {
+      const int s = consumed % kStages;
+      const uint32_t parity = (uint32_t)(consumed / kStages) & 1u;
+      TQ_TRACE(long long tr0 = clock64();)
+      const bool ok = mbar_wait_bounded(full0 + 8 * s, parity);
+      TQ_TRACE(tr_wait += clock64() - tr0; if (tr_first == 0) tr_first = global_ns(); ++tr_chunks;
+               if (lane == 0 && gw < kTraceWarps && consumed < kTraceChunks)
+                 g_attn_chunks[((size_t)gw * kTraceChunks + consumed) * 3 + 1] = global_ns();)
+      if (!__all_sync(kFullMask, ok)) {
+        failed = true;
+        break;
       }
-      at_unit_start = false;
-    }
-
-    const ChunkSpan sp = chunk_span(p, it, c);
-    const float* K = reinterpret_cast<const float*>(stage);
-    const float* V = reinterpret_cast<const float*>(stage + kKBytes);
-    TQ_TRACE(tr0 = clock64();)
-    if (it.nrows == 1)
-      attend_chunk<1>(K, V, qr, 1, it.pos0, sp.key0, sp.nkeys, p.scale_log2, lane, m, lsum, acc);
-    else
-      attend_chunk<kMaxRows>(K, V, qr, it.nrows, it.pos0, sp.key0, sp.nkeys, p.scale_log2, lane, m,
-                             lsum, acc);
-    __syncwarp();
-    TQ_TRACE(tr_comp += clock64() - tr0; tr0 = clock64();)
-    ++consumed;
-    if (++c == it.cend) {  // unit finished
-      finish_rows(p, it, h, lane, m, lsum, acc, TQ_TRACE_ARG(tr_sub));
-      at_unit_start = true;
-    }
-    TQ_TRACE(tr_fin += clock64() - tr0; tr0 = clock64();)
-    refill();
-    TQ_TRACE(tr_refill += clock64() - tr0;)
+      const unsigned char* stage = wsm + s * kStageBytes;
+      if (at_unit_start) {  // take the unit's work item and q rows, reset state
+        const StageHeader* hd = reinterpret_cast<const StageHeader*>(stage + 2 * kKBytes + kQBytes);
+        it = hd->it;
+        h = hd->h;
+        c = it.cbeg;
+        const float4* qsrc = reinterpret_cast<const float4*>(stage + 2 * kKBytes);
+#pragma unroll
+        for (int r = 0; r < kMaxRows; ++r) {
+          m[r] = -INFINITY;
+          lsum[r] = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc[r][i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            qr[r][i] = r < it.nrows ? qsrc[r * (kHeadDim / 4) + (lane & 3) * 4 + ((i + rot) & 3)]
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+        at_unit_start = false;
+      }
+      const ChunkSpan sp = chunk_span(p, it, c);
+      const float* K = reinterpret_cast<const float*>(stage);
+      const float* V = reinterpret_cast<const float*>(stage + kKBytes);
+      TQ_TRACE(tr0 = clock64();)
+      if (it.nrows == 1)
+        attend_chunk<1>(K, V, qr, 1, it.pos0, sp.key0, sp.nkeys, p.scale_log2, lane, m, lsum, acc);
+      else
+        attend_chunk<kMaxRows>(K, V, qr, it.nrows, it.pos0, sp.key0, sp.nkeys, p.scale_log2, lane, m,
+                               lsum, acc);
+      __syncwarp();  // every lane's reads of the stage are done
+      if (lane == 0) mbar_arrive(empty0 + 8 * s);
+      TQ_TRACE(tr_comp += clock64() - tr0;)
+      ++consumed;
+    } while (++c < it.cend);
+    if (failed) break;
+    TQ_TRACE(long long tf0 = clock64();)
+    finish_rows(p, it, h, lane, m, lsum, acc, TQ_TRACE_ARG(tr_sub));
+    TQ_TRACE(tr_fin += clock64() - tf0;)
   }
   TQ_TRACE(if (lane == 0 && gw < kTraceWarps) {
-    unsigned long long* t = g_attn_trace + (size_t)gw * kTraceSlots;
-    t[0] = tr_start; t[1] = tr_first; t[2] = global_ns(); t[3] = tr_wait; t[4] = tr_comp;
-    t[5] = tr_fin; t[6] = tr_refill; t[7] = tr_chunks;
-    for (int k = 0; k < 8; ++k) t[8 + k] = tr_sub[k];
+    trec[0] = tr_start; trec[1] = tr_first; trec[2] = global_ns(); trec[3] = tr_wait; trec[4] = tr_comp;
+    trec[5] = tr_fin; trec[7] = tr_chunks;
+    for (int k = 3; k < 7; ++k) trec[8 + k] = tr_sub[k];
   })
-
   if (failed) {
-    // Drain: give every copy this warp issued a bounded chance to land before
-    // the CTA exits, so no bulk copy targets the shared memory of a dead CTA.
-    for (int k = consumed; k < issued; ++k) {
-      if (!mbar_wait_bounded(bar0 + 8 * (k % kStages), (uint32_t)(k / kStages) & 1u)) break;
-    }
+    // Give the copies the producer may still have in flight (at most the
+    // ring's depth) a bounded chance to land before this warp exits; the
+    // producer, no longer released, times out on its empty barrier and exits.
+    for (int k = consumed; k < consumed + kStages; ++k)
+      if (!mbar_wait_bounded(full0 + 8 * (k % kStages), (uint32_t)(k / kStages) & 1u)) break;
   }
 }
 
