@@ -291,8 +291,8 @@ def run_ours(args, world, rank, local):
         tables = [list(s.block_table) for s in seqs]
         if runner:
             plan, _ = plan_step_host(a.block_size, a.num_blocks, cfg.n_head, tables, starts, [1] * B, ids,
-                                     cfg.vocab_size, KV.UNITS_PER_SM * KV.sm_count(device),
-                                     KV.MIN_SPLIT_CHUNKS, caps=caps)  # fmt: skip
+                                     cfg.vocab_size, KV.sm_count(device), KV.MIN_SPLIT_CHUNKS,
+                                     caps=caps)  # fmt: skip
             plans.append(torch.from_numpy(plan).to(device))
         else:
             batches.append(DevicePagedBatch(a, tables, starts, [1] * B, ids))

@@ -46,7 +46,7 @@
 extern "C" {
 #endif
 
-#define TQ_ABI_VERSION 4
+#define TQ_ABI_VERSION 5
 
 enum tq_status {
   TQ_OK = 0,
@@ -61,12 +61,12 @@ enum tq_status {
 enum tq_plan_layout {
   TQ_PLAN_NUM_TOKENS = 0,    /* N = sum of q_len */
   TQ_PLAN_NUM_SEQS = 1,      /* B */
-  TQ_PLAN_NUM_ITEMS = 2,     /* attention work items */
+  TQ_PLAN_NUM_ITEMS = 2,     /* attention work items (one query-row group, one head, a chunk range) */
   TQ_PLAN_NUM_COMBINE = 3,   /* rows whose keys were split (combine entries) */
   TQ_PLAN_NUM_PARTIALS = 4,  /* split-K partial slots needed (x head_dim floats of scratch each) */
   TQ_PLAN_TABLE_STRIDE = 5,  /* int32 per row of the packed block tables */
   TQ_PLAN_MAX_CTX = 6,       /* longest sequence after this step */
-  TQ_PLAN_SPLIT_CHUNKS = 7,  /* 32-key chunks per split-K item */
+  TQ_PLAN_SPLIT_CHUNKS = 7,  /* longest work item, in 32-key chunks */
   TQ_PLAN_TOTAL_INTS = 8,    /* int32 the plan occupies */
   TQ_PLAN_OFF_COUNTS = 9,    /* [4]: N, num_items, num_combine, B (the d_num_* pointers) */
   TQ_PLAN_OFF_SEQ_INFO = 10, /* [B][4]: first row, q_len, start, ctx */
@@ -75,23 +75,32 @@ enum tq_plan_layout {
   TQ_PLAN_OFF_POSITIONS = 13,/* [N] absolute positions */
   TQ_PLAN_OFF_TOKEN_IDS = 14,/* [N] token ids (copied from token_ids, or 0) */
   TQ_PLAN_OFF_LAST_ROWS = 15,/* [B] row of each sequence's last new token */
-  TQ_PLAN_OFF_ITEMS = 16,    /* [num_items][8] attention work items */
-  TQ_PLAN_OFF_COMBINE = 17,  /* [num_combine][4] combine entries */
-  TQ_PLAN_LAYOUT_LEN = 18
+  TQ_PLAN_OFF_ITEMS = 16,    /* the attention plan (tq_paged_attention's attn_plan), last region:
+                                [W][8] each warp's first work item, [W+1] (padded to 8) offsets of
+                                the other items, then those items [..][8], W = num_ctas * warps */
+  TQ_PLAN_OFF_COMBINE = 17,  /* [num_combine][4] rows whose keys are split across CTAs */
+  TQ_PLAN_NUM_CTAS = 18,     /* CTAs the attention plan is cut for (its launch grid) */
+  TQ_PLAN_USED_INTS = 19,    /* leading int32 of the plan this step uses (what must be copied) */
+  TQ_PLAN_LAYOUT_LEN = 20
 };
 
 TQ_API int tq_abi_version(void);
 
-/* Keys per attention chunk of this build (the split-K granularity of
- * tq_plan_step work items: TQ_PLAN_SPLIT_CHUNKS counts these). */
+/* Keys per attention chunk of this build (the granularity of tq_plan_step
+ * work items: TQ_PLAN_SPLIT_CHUNKS counts these). */
 TQ_API int tq_attention_chunk_keys(void);
+
+/* Computing warps per attention CTA of this build (a plan for n_ctas CTAs
+ * holds n_ctas * this many per-warp work lists). */
+TQ_API int tq_attention_warps(void);
 
 /* Message for the last nonzero status returned on this thread. */
 TQ_API const char* tq_last_error(void);
 
 /* Reads (and with clear != 0 resets) the device error word of the current
  * device: bit 1 = a bounded wait timed out, 2 = a block id outside the pool,
- * 4 = a slot outside the pool, 8 = a token id outside the vocabulary.
+ * 4 = a slot outside the pool, 8 = a token id outside the vocabulary,
+ * 16 = an attention work item whose merge target lies outside its buffer.
  * Synchronises the device.  *bits receives the word. */
 TQ_API int tq_device_status(int clear, int32_t* bits);
 
@@ -104,20 +113,27 @@ TQ_API int tq_device_status(int clear, int32_t* bits);
  * q_len[b] tokens at positions start[b] .. start[b]+q_len[b]-1; its block
  * table is table_data[table_offsets[b] .. table_offsets[b+1]).
  * token_ids (host, [N], may be NULL) are copied into the plan.
- * target_units: attention (item, head) units to aim for when choosing the
- * split-K size; min_split_chunks: smallest split, in 32-key chunks.
+ *
+ * Attention work is cut for a grid of n_ctas CTAs (normally the SM count;
+ * the attention launch must use the same grid): every (query-row group, head)
+ * pair's keys are a run of 32-key chunks; pairs go to CTAs longest first, each
+ * to the least loaded CTA, and each CTA's chunks are cut evenly over its warps.
+ * A pair cut between warps of one CTA is merged through shared memory; a pair
+ * longer than a CTA's share (and longer than 2 * min_split_chunks) is first
+ * split across CTAs into pieces of at least min_split_chunks chunks, merged
+ * through the split-K scratch.  Contexts up to 65535 chunks.
  * caps (host, may be NULL): fixed capacities {max_seqs, max_tokens,
  * table_stride, max_items, max_combine, max_partials}.  With caps every region
  * has its capacity's size, so the layout (and the table stride) is the same
  * for every step that fits -- the form a captured CUDA graph needs -- and the
- * split is coarsened until items and partials fit; a step that still does not
- * fit returns TQ_ERR_CAPACITY.  Without caps the plan is packed to this step.
- * Returns TQ_ERR_CAPACITY (layout[TQ_PLAN_TOTAL_INTS] = ints needed) if
- * out_capacity is too small. */
+ * cross-CTA split is coarsened until items and partials fit; a step that
+ * still does not fit returns TQ_ERR_CAPACITY.  Without caps the plan is packed
+ * to this step.  Returns TQ_ERR_CAPACITY (layout[TQ_PLAN_TOTAL_INTS] = ints
+ * needed) if out_capacity is too small. */
 TQ_API int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_t* q_len,
                  const int32_t* table_offsets, const int32_t* table_data,
                  const int32_t* token_ids, int32_t block_size, int64_t num_blocks,
-                 int32_t n_head, int32_t vocab_size, int32_t target_units,
+                 int32_t n_head, int32_t vocab_size, int32_t n_ctas,
                  int32_t min_split_chunks, const int32_t* caps, int32_t* out,
                  int64_t out_capacity, int32_t* layout);
 
@@ -138,20 +154,20 @@ TQ_API int tq_kv_write(float* pool, int64_t num_blocks, int32_t n_layer, int32_t
  * keys at positions 0..p of sequence b:
  *   out[r*out_row_stride + h*64 + i] = softmax_j(q_r.k_j * scale) v_j[i].
  * q rows: q[r*q_row_stride + h*64 ...]; q, out 16-byte aligned rows.
- * work_items / block_tables come from tq_plan_step.  Split-K scratch is the
+ * attn_plan / block_tables come from tq_plan_step.  Split-K scratch is the
  * caller's: partial_ml ([P][2] floats), partial_acc ([P][64] floats) and
  * partial_counters ([P] int32, all zero before the first launch; every launch
  * that completes leaves them zero again), P >= TQ_PLAN_NUM_PARTIALS of every
  * plan launched with it (max_partials; NULL scratch is fine when it is 0).
- * Launches that share scratch must not overlap on the GPU.  max_items is the
- * capacity of work_items (the kernel may read any of its max_items entries,
- * and uses the first *d_num_items) and sizes the grid.  One kernel launch on
- * `stream`; the split-K merge is fused. */
+ * Launches that share scratch must not overlap on the GPU.  attn_plan is the
+ * plan's attention region (TQ_PLAN_OFF_ITEMS) and n_ctas its TQ_PLAN_NUM_CTAS,
+ * the launch grid.  One kernel launch on `stream`; every merge of split keys
+ * happens inside it. */
 TQ_API int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64_t q_row_stride,
                        const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
                        int32_t block_size, int32_t head_dim, int32_t layer,
                        const int32_t* block_tables, int32_t table_stride,
-                       const int32_t* work_items, const int32_t* d_num_items, int32_t max_items,
+                       const int32_t* attn_plan, int32_t n_ctas,
                        float* partial_ml, float* partial_acc, int32_t* partial_counters,
                        int32_t max_partials, float scale, void* stream);
 
@@ -178,9 +194,9 @@ TQ_API int tq_paged_attention_noalloc(float* out, int64_t out_row_stride, const 
                                       int64_t q_row_stride, const float* pool, int64_t num_blocks,
                                       int32_t n_layer, int32_t n_head, int32_t block_size,
                                       int32_t head_dim, int32_t layer, const int32_t* block_tables,
-                                      int32_t table_stride, const int32_t* work_items,
-                                      const int32_t* d_num_items, int32_t max_items,
-                                      int32_t num_partials, float scale, void* stream);
+                                      int32_t table_stride, const int32_t* attn_plan,
+                                      int32_t n_ctas, int32_t num_partials, float scale,
+                                      void* stream);
 
 /* x[r] = wte[ids[r]] + wpe[pos[r]];  xa[r] = LayerNorm(x[r]; ln_w, ln_b, eps).
  * n_embd must be a multiple of 128 and at most 1024. */

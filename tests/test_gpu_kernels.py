@@ -16,7 +16,7 @@ import pytest
 import torch
 
 from tokquay_b200 import _lib
-from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, cdiv
+from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, attention_warps, cdiv
 from tokquay_b200.model import GPT2Config
 
 pytestmark = [
@@ -122,6 +122,51 @@ def test_paged_attention_split_k_is_exercised():
     batch.attend_rows(0, qkv, out, _stream())
     want = _reference_attention(alloc.pool, 0, qkv[:, :768], tables, start, new, 16)
     assert (out.double() - want).abs().max().item() <= ATTN_RTOL * want.abs().max().item()
+
+
+def _merge_kinds(batch) -> set[int]:
+    """Flags of the plan's work items: 0 whole, 1 cut inside a CTA, 2 split
+    across CTAs, 3 both."""
+    L = batch.layout
+    plan = batch.plan.cpu().numpy()
+    nw = batch.n_ctas * attention_warps()
+    o = int(L[_lib.PLAN_OFF_ITEMS])
+    first = plan[o:o + 8 * nw].reshape(nw, 8)
+    offs = plan[o + 8 * nw:o + 9 * nw + 1]
+    ro = o + 8 * nw + (nw + 8) // 8 * 8
+    rest = plan[ro:ro + 8 * int(offs[-1])].reshape(-1, 8)
+    words = [w[2] for w in first if w[4] != 0] + [w[2] for w in rest]
+    return {int(np.uint32(x)) >> 24 for x in words}
+
+
+@pytest.mark.parametrize("n_ctas", [1, 5, 37, 148, 400])
+def test_paged_attention_any_grid(n_ctas):
+    """Whatever the grid, the cuts -- merged in shared memory inside a CTA,
+    through split-K scratch across CTAs, or both -- give the float64 result."""
+    rng = random.Random(n_ctas)
+    cfg = GPT2Config(vocab_size=64, n_positions=1024, n_embd=768, n_layer=1, n_head=12)
+    alloc = BlockAllocator(cfg, 40 * 64 + 8, 16, device="cuda")
+    random.Random(1).shuffle(alloc._free)
+    alloc.pool.normal_()
+    tables, start, new = [], [], []
+    for i in range(40):
+        s = rng.choice([rng.randint(0, 60), rng.randint(300, 1000)])
+        n = rng.choice([1, 1, 1, 7])
+        tables.append(alloc._take(cdiv(s + n, 16)))
+        start.append(s)
+        new.append(n)
+    batch = DevicePagedBatch(alloc, tables, start, new, n_ctas=n_ctas)
+    kinds = _merge_kinds(batch)
+    if n_ctas >= 37:
+        assert 1 in kinds or 3 in kinds  # some pair is cut between warps of a CTA
+    qkv = torch.randn(batch.N, 3 * 768, device="cuda")
+    out = torch.full((batch.N, 768), float("nan"), device="cuda")
+    batch.attend_rows(0, qkv, out, _stream())
+    torch.cuda.synchronize()
+    want = _reference_attention(alloc.pool, 0, qkv[:, :768], tables, start, new, 16)
+    assert torch.isfinite(out).all()
+    assert (out.double() - want).abs().max().item() <= ATTN_RTOL * want.abs().max().item(), kinds
+    assert _lib.device_status() == 0
 
 
 @pytest.mark.parametrize("bs", [1, 4, 16, 32, 128])

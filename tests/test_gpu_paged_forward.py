@@ -362,7 +362,8 @@ def test_graph_replay_from_device_resident_plans():
     m = make_model(cfg, W.random_weights(cfg, 8, "gpt2"))
     ag, ae = _twin_allocators(cfg, 100, 8, 1)
     runner = m.use_cuda_graphs(ag, buckets=(4,))
-    caps = runner.graph(4)[1].caps
+    ws = runner.graph(4)[1]
+    caps = ws.caps
     rng = random.Random(1)
     seqs = [Sequence(i, [rng.randrange(cfg.vocab_size) for _ in range(rng.randint(2, 30))]) for i in range(4)]
     twins = [Sequence(s.seq_id, list(s.prompt_token_ids)) for s in seqs]
@@ -375,7 +376,7 @@ def test_graph_replay_from_device_resident_plans():
         st = [s.num_cached_tokens for s in seqs]
         ids = [s.tokens_slice(x, x + 1)[0] for s, x in zip(seqs, st)]
         plan, _ = plan_step_host(8, 100, cfg.n_head, [list(s.block_table) for s in seqs], st, [1] * 4, ids,
-                                 cfg.vocab_size, 100, 2, caps=caps)  # fmt: skip
+                                 cfg.vocab_size, ws.n_ctas, 2, caps=caps)  # fmt: skip
         plans.append(torch.from_numpy(plan.copy()).to(DEVICE))
         for s in seqs:
             s.num_cached_tokens += 1

@@ -15,31 +15,63 @@ import pytest
 
 import oracle
 from tokquay_b200 import _lib
-from tokquay_b200.kv_cache import MIN_SPLIT_CHUNKS, attention_chunk_keys, cdiv, plan_step_host
+from tokquay_b200.kv_cache import MIN_SPLIT_CHUNKS, attention_chunk_keys, attention_warps, cdiv, plan_step_host
 
 N_HEAD = 3
 KMAX_ROWS = 4
 # K (or V) rows one stage holds: the library's chunk size (checked in simulate_copies)
 
 
+def _u32(x) -> int:
+    return int(np.uint32(np.int32(x)))
+
+
+def decode_item(w) -> dict:
+    w = [int(x) for x in w]
+    return dict(
+        seq=w[0], row0=w[1], nrows=w[2] & 0xFF, head=(w[2] >> 8) & 0xFFFF, flags=_u32(w[2]) >> 24, pos0=w[3],
+        cbeg=w[4] & 0xFFFF, cend=_u32(w[4]) >> 16, lsplit=w[5] & 0xFF, lcount=(w[5] >> 8) & 0xFF,
+        lslot=_u32(w[5]) >> 16, gbase=w[6], gsplit=w[7] & 0xFFFF, gnsplit=_u32(w[7]) >> 16,
+    )  # fmt: skip
+
+
+def attention_lists(plan, layout) -> list[list[dict]]:
+    """Each warp slot's work items (decoded), from the attention region."""
+    nw = int(layout[_lib.PLAN_NUM_CTAS]) * attention_warps()
+    o = int(layout[_lib.PLAN_OFF_ITEMS])
+    first = np.asarray(plan[o:o + 8 * nw]).reshape(nw, 8)
+    offs = np.asarray(plan[o + 8 * nw:o + 8 * nw + nw + 1])
+    ro = o + 8 * nw + (nw + 1 + 7) // 8 * 8
+    rest = np.asarray(plan[ro:ro + 8 * int(offs[-1])]).reshape(-1, 8)
+    lists = []
+    for w in range(nw):
+        if _u32(first[w][4]) >> 16:
+            lists.append([decode_item(first[w])] + [decode_item(x) for x in rest[offs[w]:offs[w + 1]]])
+        else:
+            assert not first[w].any() and offs[w] == offs[w + 1]
+            lists.append([])
+    return lists
+
+
 def unpack(plan, layout):
     L = layout
     B, N = int(L[_lib.PLAN_NUM_SEQS]), int(L[_lib.PLAN_NUM_TOKENS])
-    ni, nc, stride = int(L[_lib.PLAN_NUM_ITEMS]), int(L[_lib.PLAN_NUM_COMBINE]), int(L[_lib.PLAN_TABLE_STRIDE])
+    nc, stride = int(L[_lib.PLAN_NUM_COMBINE]), int(L[_lib.PLAN_TABLE_STRIDE])
 
     def v(k, n):
         o = int(L[k])
         return np.asarray(plan[o:o + n])
 
+    warps = attention_lists(plan, layout)
     return dict(
         B=B, N=N, stride=stride,
         counts=v(_lib.PLAN_OFF_COUNTS, 4),
         seq=v(_lib.PLAN_OFF_SEQ_INFO, 4 * B).reshape(B, 4),
         tables=v(_lib.PLAN_OFF_TABLES, B * stride).reshape(B, stride),
         slots=v(_lib.PLAN_OFF_SLOTS, N), pos=v(_lib.PLAN_OFF_POSITIONS, N), ids=v(_lib.PLAN_OFF_TOKEN_IDS, N),
-        last=v(_lib.PLAN_OFF_LAST_ROWS, B), items=v(_lib.PLAN_OFF_ITEMS, 8 * ni).reshape(ni, 8),
+        last=v(_lib.PLAN_OFF_LAST_ROWS, B), warps=warps, items=[it for ws in warps for it in ws],
         combine=v(_lib.PLAN_OFF_COMBINE, 4 * nc).reshape(nc, 4),
-        n_partials=int(L[_lib.PLAN_NUM_PARTIALS]),
+        n_partials=int(L[_lib.PLAN_NUM_PARTIALS]), n_ctas=int(L[_lib.PLAN_NUM_CTAS]),
     )  # fmt: skip
 
 
@@ -61,16 +93,14 @@ def random_batch(rng, bs, num_blocks, n_seqs, max_start, max_new):
     return tables, start, new
 
 
-def simulate_copies(p, bs, num_blocks, n_head):
-    """Replay issue_chunk's arithmetic for every (item, head, chunk): every
+def simulate_copies(p, bs, num_blocks):
+    """Replay the producer's copy arithmetic for every (item, chunk): every
     copy's source block must be a planned table entry of the sequence and
     every destination inside the stage.  Returns {(row, head): sorted keys}."""
     ATTN_CHUNK = attention_chunk_keys()
     seen: dict[tuple[int, int], list[int]] = {}
-    items = p["items"]
-    for it in items:
-        seq, row0, nrows, pos0, cbeg, cend, part, sn = (int(x) for x in it)
-        split, nsplit = sn & 0xFFFF, sn >> 16
+    for it in p["items"]:
+        seq, row0, nrows, pos0, cbeg, cend, h = (it[k] for k in ("seq", "row0", "nrows", "pos0", "cbeg", "cend", "head"))
         assert 1 <= nrows <= KMAX_ROWS and cbeg < cend
         ctx = int(p["seq"][seq][3])
         need = cdiv(ctx, bs)
@@ -100,17 +130,60 @@ def simulate_copies(p, bs, num_blocks, n_head):
             for r in range(nrows):
                 pos = pos0 + r
                 nvalid = min(ATTN_CHUNK, pos + 1 - key0)
-                for h in range(n_head):
-                    seen.setdefault((row0 + r, h), []).extend(range(key0, key0 + max(0, nvalid)))
-        if nsplit > 1:
-            assert part >= 0
-            for r in range(nrows):
-                for h in range(n_head):
-                    idx = part + (r * n_head + h) * nsplit + split
-                    assert 0 <= idx < p["n_partials"]
-        else:
-            assert part == -1 and split == 0
+                seen.setdefault((row0 + r, h), []).extend(range(key0, key0 + max(0, nvalid)))
     return seen
+
+
+def check_merges(p):
+    """Every cut is merged exactly once: shared-memory groups inside one CTA
+    (slots in range, disjoint, one merging warp each), split-K groups across
+    CTAs (every split index written once, partial indices in range and
+    disjoint between groups)."""
+    W = attention_warps()
+    max_rows = max([it["nrows"] for it in p["items"]] or [1])
+    local_slots = 2 * (W - 1) * max_rows
+    global_parts: dict[tuple[int, int], dict] = {}
+    used_parts: set[int] = set()
+    for c in range(p["n_ctas"]):
+        groups: dict[int, list[tuple[int, dict]]] = {}
+        for w in range(W):
+            owned = 0
+            for it in p["warps"][c * W + w]:
+                if it["flags"] & 1:
+                    groups.setdefault(it["lslot"], []).append((w, it))
+                    owned += it["lsplit"] == 0
+                else:
+                    assert it["lcount"] == 0 and it["lsplit"] == 0 and it["lslot"] == 0
+            assert owned <= 1  # a warp merges at most one shared-memory group
+        slots_used: set[int] = set()
+        for base, members in groups.items():
+            k = members[0][1]["lcount"]
+            assert k >= 2 and sorted(m[1]["lsplit"] for m in members) == list(range(k))
+            ws = [m[0] for m in sorted(members, key=lambda m: m[1]["lsplit"])]
+            assert ws == sorted(set(ws))  # one piece per warp, in warp order
+            first = members[0][1]
+            for _, it in members:
+                assert all(it[f] == first[f] for f in ("seq", "row0", "nrows", "head", "flags", "gbase", "gsplit"))
+            spans = sorted((it["cbeg"], it["cend"]) for _, it in members)
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(k - 1))  # contiguous keys
+            rng_ = set(range(base, base + k * first["nrows"]))
+            assert max(rng_) < local_slots and not (rng_ & slots_used)
+            slots_used |= rng_
+            if first["flags"] & 2:
+                g = global_parts.setdefault((first["row0"], first["head"]), {"splits": [], "item": first})
+                g["splits"].append(first["gsplit"])
+        for w in range(W):
+            for it in p["warps"][c * W + w]:
+                if it["flags"] == 2:
+                    g = global_parts.setdefault((it["row0"], it["head"]), {"splits": [], "item": it})
+                    g["splits"].append(it["gsplit"])
+    for (row0, h), g in global_parts.items():
+        it = g["item"]
+        n = it["gnsplit"]
+        assert n >= 2 and sorted(g["splits"]) == list(range(n)), (row0, h, g["splits"])
+        idx = {it["gbase"] + r * n + s for r in range(it["nrows"]) for s in range(n)}
+        assert max(idx) < p["n_partials"] and min(idx) >= 0 and not (idx & used_parts)
+        used_parts |= idx
 
 
 @pytest.mark.parametrize("bs", [1, 2, 4, 16, 32, 64, 256])
@@ -120,8 +193,9 @@ def test_plan_matches_oracle_and_covers_every_key_once(bs, seed):
     num_blocks = 12 * cdiv(742, bs) + 50  # room for every sequence of the batch
     tables, start, new = random_batch(rng, bs, num_blocks, rng.randint(1, 12), 700, rng.choice([1, 5, 40]))
     ids = [rng.randrange(1000) for _ in range(sum(new))]
-    target = rng.choice([1, 50, 10_000])
-    plan, layout = plan_step_host(bs, num_blocks, N_HEAD, tables, start, new, ids, 1000, target, MIN_SPLIT_CHUNKS)
+    n_ctas = rng.choice([1, 3, 50, 148])
+    min_split = rng.choice([1, 2, MIN_SPLIT_CHUNKS])
+    plan, layout = plan_step_host(bs, num_blocks, N_HEAD, tables, start, new, ids, 1000, n_ctas, min_split)
     p = unpack(plan, layout)
     ob = oracle.OracleBatch.build(bs, tables, start, new)
     # Same scatter targets and positions as the reference's index arrays.
@@ -136,26 +210,59 @@ def test_plan_matches_oracle_and_covers_every_key_once(bs, seed):
     cu = np.concatenate([[0], np.cumsum(new)])
     np.testing.assert_array_equal(p["last"], cu[1:] - 1)
     np.testing.assert_array_equal(p["counts"], [p["N"], len(p["items"]), len(p["combine"]), p["B"]])
+    assert p["n_ctas"] == n_ctas and len(p["items"]) == layout[_lib.PLAN_NUM_ITEMS]
     # Every (row, head) sees keys 0..position exactly once across its items.
-    seen = simulate_copies(p, bs, num_blocks, N_HEAD)
+    seen = simulate_copies(p, bs, num_blocks)
     for r in range(p["N"]):
         for h in range(N_HEAD):
-            assert seen[(r, h)] == list(range(int(p["pos"][r]) + 1)), (r, h)
-    # Rows with split keys have exactly one combine entry each.
-    split_rows = {int(it[1]) + k for it in p["items"] if (int(it[7]) >> 16) > 1 for k in range(int(it[2]))}
+            assert sorted(seen[(r, h)]) == list(range(int(p["pos"][r]) + 1)), (r, h)
+    check_merges(p)
+    # Rows with keys split across CTAs have exactly one combine entry each.
+    split_rows = {it["row0"] + k for it in p["items"] if it["flags"] & 2 for k in range(it["nrows"])}
     assert sorted(int(e[0]) for e in p["combine"]) == sorted(split_rows)
+    # The used prefix holds everything the step reads.
+    o = int(layout[_lib.PLAN_OFF_ITEMS])
+    nw = n_ctas * attention_warps()
+    n_rest = int(plan[o + 8 * nw + nw])
+    assert layout[_lib.PLAN_USED_INTS] == o + 8 * nw + (nw + 8) // 8 * 8 + 8 * n_rest
+    assert layout[_lib.PLAN_USED_INTS] <= layout[_lib.PLAN_TOTAL_INTS] == plan.size
+
+
+def test_cuts_balance_the_warps_of_a_cta():
+    """Chunks are spread evenly: every warp of a CTA holds within one chunk of
+    the CTA's mean, and CTA loads are within one longest piece of each other."""
+    rng = random.Random(7)
+    tables, start, new = random_batch(rng, 16, 4096, 64, 600, 1)
+    plan, layout = plan_step_host(16, 4096, 12, tables, start, new, None, 0, 148, MIN_SPLIT_CHUNKS)
+    p = unpack(plan, layout)
+    W = attention_warps()
+    loads = []
+    for c in range(148):
+        per = [sum(it["cend"] - it["cbeg"] for it in p["warps"][c * W + w]) for w in range(W)]
+        assert max(per) - min(per) <= 1, per
+        loads.append(sum(per))
+    longest = max(it["cend"] - it["cbeg"] for it in p["items"])
+    assert max(loads) - min(loads) <= W * longest
 
 
 def test_split_policy():
-    # 8 decodes of 4096 keys with 12 heads: 96 units < target, so split.
+    # 8 decodes of 4096 keys with 12 heads: each pair (128 chunks) is longer
+    # than a CTA's share of 148 CTAs, so it is split across CTAs.
     tables = [list(range(i * 256, (i + 1) * 256)) for i in range(8)]
-    plan, layout = plan_step_host(16, 8 * 256, 12, tables, [4095] * 8, [1] * 8, None, 0, 2368, 2)
+    plan, layout = plan_step_host(16, 8 * 256, 12, tables, [4095] * 8, [1] * 8, None, 0, 148, 2)
     p = unpack(plan, layout)
-    assert layout[_lib.PLAN_SPLIT_CHUNKS] >= 2 and len(p["combine"]) == 8
-    # Enough units already: no split.
+    assert len(p["combine"]) == 8 and layout[_lib.PLAN_NUM_PARTIALS] > 0
+    check_merges(p)
+    # Many short sequences: no cross-CTA split, and no global scratch.
     tables = [list(range(i * 2, i * 2 + 2)) for i in range(300)]
-    plan, layout = plan_step_host(16, 600, 12, tables, [20] * 300, [1] * 300, None, 0, 2368, 2)
+    plan, layout = plan_step_host(16, 600, 12, tables, [20] * 300, [1] * 300, None, 0, 148, 2)
     assert layout[_lib.PLAN_NUM_COMBINE] == 0 and layout[_lib.PLAN_NUM_PARTIALS] == 0
+    # BASELINE config 2 shapes (64 decodes up to 512 keys): CTA-local cuts only.
+    rng = random.Random(3)
+    tables, start, new = random_batch(rng, 16, 4096, 64, 511, 1)
+    plan, layout = plan_step_host(16, 4096, 12, tables, start, new, None, 0, 148, MIN_SPLIT_CHUNKS)
+    p = unpack(plan, layout)
+    assert layout[_lib.PLAN_NUM_PARTIALS] == 0 and any(it["flags"] == 1 for it in p["items"])
 
 
 def test_rejections_match_the_reference():
@@ -184,13 +291,14 @@ def test_capacity_retry_and_in_place_buffer():
     big = np.zeros(4096, dtype=np.int32)
     plan2, layout2 = plan_step_host(4, 8, 2, tables, [5, 0], [4, 2], None, 0, 10, 1, out=big)
     assert plan2 is big
-    np.testing.assert_array_equal(big[:plan.size], plan)
+    used = int(layout[_lib.PLAN_USED_INTS])  # past it the buffer is not written
+    np.testing.assert_array_equal(big[:used], plan[:used])
 
 
 def test_fixed_capacity_layout_is_step_independent():
     """With caps, every step that fits gets the same offsets and table stride
     (what a captured CUDA graph needs), and the data matches the packed plan."""
-    caps = np.array([8, 8, 40, 8 * 16, 8, 8 * 3 * 16], dtype=np.int32)
+    caps = np.array([8, 8, 40, 8 * 3 * 16 + 500 * (attention_warps() - 1), 8, 8 * 3 * 16], dtype=np.int32)
     rng = random.Random(0)
     layouts = []
     for _ in range(5):
@@ -204,14 +312,21 @@ def test_fixed_capacity_layout_is_step_independent():
         np.testing.assert_array_equal(p["slots"][:q["N"]], q["slots"])
         np.testing.assert_array_equal(p["counts"], q["counts"])
         layouts.append(tuple(int(layout[k]) for k in range(_lib.PLAN_TABLE_STRIDE, _lib.PLAN_LAYOUT_LEN)
-                             if k not in (_lib.PLAN_MAX_CTX, _lib.PLAN_SPLIT_CHUNKS)))
+                             if k not in (_lib.PLAN_MAX_CTX, _lib.PLAN_SPLIT_CHUNKS, _lib.PLAN_USED_INTS)))
     assert len(set(layouts)) == 1
     with pytest.raises(RuntimeError, match="capacities"):
         plan_step_host(16, 8 * 40, 3, [[0]] * 9, [0] * 9, [1] * 9, None, 0, 500, 2, caps=caps)
 
 
 def test_fixed_capacity_coarsens_the_split_to_fit():
-    caps = np.array([4, 4, 64, 4, 4, 4 * 12 * 2], dtype=np.int32)  # room for 1 item per seq
+    # 4 decodes of 1001 keys, 12 heads, 148 CTAs: unconstrained, every pair is
+    # split across CTAs; with room for only 2 cross-CTA pieces per pair the
+    # planner coarsens the split until items and partials fit.
     tables = [list(range(i * 64, (i + 1) * 64)) for i in range(4)]
-    plan, layout = plan_step_host(16, 256, 12, tables, [1000] * 4, [1] * 4, None, 0, 10_000, 2, caps=caps)
-    assert layout[_lib.PLAN_NUM_ITEMS] <= 4 and layout[_lib.PLAN_NUM_PARTIALS] <= caps[5]
+    _, free = plan_step_host(16, 256, 12, tables, [1000] * 4, [1] * 4, None, 0, 148, 2)
+    assert free[_lib.PLAN_NUM_PARTIALS] > 4 * 12 * 2
+    W = attention_warps()
+    caps = np.array([4, 4, 64, 4 * 12 * 2 + 148 * (W - 1), 4, 4 * 12 * 2], dtype=np.int32)
+    plan, layout = plan_step_host(16, 256, 12, tables, [1000] * 4, [1] * 4, None, 0, 148, 2, caps=caps)
+    assert layout[_lib.PLAN_NUM_ITEMS] <= caps[3] and 0 < layout[_lib.PLAN_NUM_PARTIALS] <= caps[5]
+    check_merges(unpack(plan, layout))

@@ -60,7 +60,7 @@ def _noalloc(batch: DevicePagedBatch, layer: int, q: torch.Tensor, out: torch.Te
     return _lib.load().tq_paged_attention_noalloc(
         out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), a.pool.data_ptr(), a.num_blocks,
         a.cfg.n_layer, a.cfg.n_head, a.block_size, a.cfg.d_head, layer, batch.block_tables_i32.data_ptr(),
-        batch.table_stride, batch.work_items.data_ptr(), batch.count_ptr(1), batch.num_items, num_partials,
+        batch.table_stride, batch.attn_plan.data_ptr(), batch.n_ctas, num_partials,
         1.0 / math.sqrt(a.cfg.d_head), torch.cuda.current_stream().cuda_stream)  # fmt: skip
 
 

@@ -40,13 +40,16 @@ PLAN_OFF_TOKEN_IDS = 14
 PLAN_OFF_LAST_ROWS = 15
 PLAN_OFF_ITEMS = 16
 PLAN_OFF_COMBINE = 17
-PLAN_LAYOUT_LEN = 18
+PLAN_NUM_CTAS = 18
+PLAN_USED_INTS = 19
+PLAN_LAYOUT_LEN = 20
 
 # Symbols the header declares, with (restype, argtypes).
 _P = c_void_p
 SIGNATURES: dict[str, tuple] = {
     "tq_abi_version": (c_int, []),
     "tq_attention_chunk_keys": (c_int, []),
+    "tq_attention_warps": (c_int, []),
     "tq_last_error": (ctypes.c_char_p, []),
     "tq_device_status": (c_int, [c_int, POINTER(c_int32)]),
     "tq_plan_step": (c_int, [c_int32, _P, _P, _P, _P, _P, c_int32, c_int64, c_int32, c_int32,
@@ -54,10 +57,10 @@ SIGNATURES: dict[str, tuple] = {
     "tq_kv_write": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32, _P, c_int64,
                             c_int64, c_int64, _P, _P, c_int32, _P]),
     "tq_paged_attention": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32,
-                                   c_int32, c_int32, _P, c_int32, _P, _P, c_int32, _P, _P, _P, c_int32,
+                                   c_int32, c_int32, _P, c_int32, _P, c_int32, _P, _P, _P, c_int32,
                                    c_float, _P]),
     "tq_paged_attention_noalloc": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32,
-                                           c_int32, c_int32, _P, c_int32, _P, _P, c_int32, c_int32, c_float,
+                                           c_int32, c_int32, _P, c_int32, _P, c_int32, c_int32, c_float,
                                            _P]),
     "tq_embed_layernorm": (c_int, [_P, _P, _P, _P, _P, _P, c_int32, c_int32, _P, _P, c_float,
                                    c_int32, _P, c_int32, _P]),
@@ -67,7 +70,7 @@ SIGNATURES: dict[str, tuple] = {
     "tq_bias_gelu": (c_int, [_P, _P, c_int32, c_int64, _P, c_int32, c_int32, _P, c_int32, _P]),
 }
 
-EXPECTED_ABI = 4
+EXPECTED_ABI = 5
 
 # Split-K partials the no-allocation attention entry point can hold
 # (TQ_NOALLOC_MAX_PARTIALS in include/tokquay_b200.h).

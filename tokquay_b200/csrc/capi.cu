@@ -92,18 +92,55 @@ int check_pool(const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n
   return TQ_OK;
 }
 
+// Checks shared by the attention entry points; fills everything but the
+// split-K scratch.  n_ctas == 0 (an empty plan) launches nothing.
+int attention_params(float* out, int64_t out_row_stride, const float* q, int64_t q_row_stride,
+                     const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
+                     int32_t block_size, int32_t head_dim, int32_t layer, const int32_t* block_tables,
+                     int32_t table_stride, const int32_t* attn_plan, int32_t n_ctas, float scale,
+                     AttnParams* p) {
+  int st = check_pool(pool, num_blocks, n_layer, n_head, block_size, head_dim, layer);
+  if (st) return st;
+  if (n_ctas < 0 || n_ctas > 0xffff) return set_error(TQ_ERR_INVALID, "n_ctas must be in [0, 65535]");
+  if (n_ctas == 0) return TQ_OK;
+  if (!out || !q || !block_tables || !attn_plan)
+    return set_error(TQ_ERR_INVALID, "out, q, block_tables and attn_plan must not be NULL");
+  if (!aligned(q, 16) || q_row_stride % 4)
+    return set_error(TQ_ERR_INVALID, "q rows must be 16-byte aligned");
+  if (!aligned(out, 16) || out_row_stride % 4)
+    return set_error(TQ_ERR_INVALID, "out rows must be 16-byte aligned");
+  if (!aligned(attn_plan, 16)) return set_error(TQ_ERR_INVALID, "attn_plan must be 16-byte aligned");
+  if (table_stride < 0) return set_error(TQ_ERR_INVALID, "table_stride must be >= 0");
+  if (!(scale > 0.f) || !std::isfinite(scale)) return set_error(TQ_ERR_INVALID, "bad scale");
+  int sms = 0;
+  if ((st = device_setup(&sms))) return st;
+  p->out = out;
+  p->out_stride = out_row_stride;
+  p->q = q;
+  p->q_stride = q_row_stride;
+  p->pool = pool;
+  p->num_blocks = num_blocks;
+  p->n_layer = n_layer;
+  p->n_head = n_head;
+  p->block_size = block_size;
+  p->log2_bs = log2_exact(block_size);
+  p->layer = layer;
+  p->tables = block_tables;
+  p->table_stride = table_stride;
+  p->attn = attn_plan;
+  p->n_warps = n_ctas * kAttnWarps;
+  p->part_ml = p->part_acc = nullptr;
+  p->part_cnt = nullptr;
+  p->max_partials = 0;
+  p->scale_log2 = scale * 1.4426950408889634f;
+  return TQ_OK;
+}
+
 int check_embd(int32_t n_embd) {
   if (n_embd < 128 || n_embd > 1024 || n_embd % 128 != 0)
     return set_error(TQ_ERR_UNSUPPORTED, "n_embd must be a multiple of 128 in [128, 1024], got %d",
                      n_embd);
   return TQ_OK;
-}
-
-// Grid for `warps` independent warps of 8 per 256-thread block, capped at 8
-// blocks per SM (the kernels grid-stride beyond that).
-int warp_grid(int64_t warps, int sm_count) {
-  const int64_t blocks = (warps + 7) / 8;
-  return (int)std::min<int64_t>(std::max<int64_t>(blocks, 1), (int64_t)sm_count * 8);
 }
 
 // Grid for block-per-row kernels: one block per row, capped at 16 blocks per
@@ -122,6 +159,8 @@ extern "C" {
 int tq_abi_version(void) { return TQ_ABI_VERSION; }
 
 int tq_attention_chunk_keys(void) { return kChunk; }
+
+int tq_attention_warps(void) { return kAttnWarps; }
 
 const char* tq_last_error(void) { return error_buffer(); }
 
@@ -179,55 +218,26 @@ int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64
                        const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
                        int32_t block_size, int32_t head_dim, int32_t layer,
                        const int32_t* block_tables, int32_t table_stride,
-                       const int32_t* work_items, const int32_t* d_num_items, int32_t max_items,
+                       const int32_t* attn_plan, int32_t n_ctas,
                        float* partial_ml, float* partial_acc, int32_t* partial_counters,
                        int32_t max_partials, float scale, void* stream) {
-  int st = check_pool(pool, num_blocks, n_layer, n_head, block_size, head_dim, layer);
-  if (st) return st;
-  if (max_items < 0 || max_partials < 0) return set_error(TQ_ERR_INVALID, "negative capacity");
-  if (max_items == 0) return TQ_OK;
-  if (!out || !q || !block_tables || !work_items || !d_num_items)
-    return set_error(TQ_ERR_INVALID, "out, q, block_tables and work items must not be NULL");
-  if (!aligned(q, 16) || q_row_stride % 4)
-    return set_error(TQ_ERR_INVALID, "q rows must be 16-byte aligned");
-  if (!aligned(out, 16) || out_row_stride % 4)
-    return set_error(TQ_ERR_INVALID, "out rows must be 16-byte aligned");
-  if (!aligned(work_items, 16)) return set_error(TQ_ERR_INVALID, "work items must be 16-byte aligned");
+  if (max_partials < 0) return set_error(TQ_ERR_INVALID, "negative capacity");
   if (max_partials > 0) {
     if (!partial_ml || !partial_acc || !partial_counters)
       return set_error(TQ_ERR_INVALID, "split-K scratch must not be NULL");
     if (!aligned(partial_acc, 16) || !aligned(partial_ml, 8) || !aligned(partial_counters, 4))
       return set_error(TQ_ERR_INVALID, "split-K scratch misaligned");
   }
-  if (table_stride < 0) return set_error(TQ_ERR_INVALID, "table_stride must be >= 0");
-  if (!(scale > 0.f) || !std::isfinite(scale)) return set_error(TQ_ERR_INVALID, "bad scale");
-  int sms = 0;
-  if ((st = device_setup(&sms))) return st;
-
   AttnParams p;
-  p.out = out;
-  p.out_stride = out_row_stride;
-  p.q = q;
-  p.q_stride = q_row_stride;
-  p.pool = pool;
-  p.num_blocks = num_blocks;
-  p.n_layer = n_layer;
-  p.n_head = n_head;
-  p.block_size = block_size;
-  p.log2_bs = log2_exact(block_size);
-  p.layer = layer;
-  p.tables = block_tables;
-  p.table_stride = table_stride;
-  p.items = reinterpret_cast<const WorkItem*>(work_items);
-  p.n_items = d_num_items;
-  p.max_items = max_items;
+  int st = attention_params(out, out_row_stride, q, q_row_stride, pool, num_blocks, n_layer, n_head,
+                            block_size, head_dim, layer, block_tables, table_stride, attn_plan, n_ctas,
+                            scale, &p);
+  if (st || n_ctas == 0) return st;
   p.part_ml = partial_ml;
   p.part_acc = partial_acc;
   p.part_cnt = partial_counters;
-  p.scale_log2 = scale * 1.4426950408889634f;
-  const int64_t units = (int64_t)max_items * n_head;
-  const int grid = (int)std::min<int64_t>((units + kAttnWarps - 1) / kAttnWarps, sms);
-  paged_attention_kernel<<<grid, kAttnThreads, kAttnSmemBytes, (cudaStream_t)stream>>>(p);
+  p.max_partials = max_partials;
+  paged_attention_kernel<<<n_ctas, kAttnThreads, kAttnSmemBytes, (cudaStream_t)stream>>>(p);
   return check_launch("paged_attention");
 }
 
@@ -288,29 +298,19 @@ int tq_paged_attention_noalloc(float* out, int64_t out_row_stride, const float* 
                                int64_t q_row_stride, const float* pool, int64_t num_blocks,
                                int32_t n_layer, int32_t n_head, int32_t block_size,
                                int32_t head_dim, int32_t layer, const int32_t* block_tables,
-                               int32_t table_stride, const int32_t* work_items,
-                               const int32_t* d_num_items, int32_t max_items,
+                               int32_t table_stride, const int32_t* attn_plan, int32_t n_ctas,
                                int32_t num_partials, float scale, void* stream) {
-  int st = check_pool(pool, num_blocks, n_layer, n_head, block_size, head_dim, layer);
-  if (st) return st;
-  if (max_items < 0 || num_partials < 0) return set_error(TQ_ERR_INVALID, "negative capacity");
+  if (num_partials < 0) return set_error(TQ_ERR_INVALID, "negative capacity");
   if (num_partials > kNoAllocMaxPartials)
     return set_error(TQ_ERR_CAPACITY,
                      "the plan needs %d split-K partials but the no-allocation entry point holds at "
                      "most %d; plan with fewer splits or use tq_paged_attention with your own scratch",
                      num_partials, kNoAllocMaxPartials);
-  if (max_items == 0) return TQ_OK;
-  if (!out || !q || !block_tables || !work_items || !d_num_items)
-    return set_error(TQ_ERR_INVALID, "out, q, block_tables and work items must not be NULL");
-  if (!aligned(q, 16) || q_row_stride % 4)
-    return set_error(TQ_ERR_INVALID, "q rows must be 16-byte aligned");
-  if (!aligned(out, 16) || out_row_stride % 4)
-    return set_error(TQ_ERR_INVALID, "out rows must be 16-byte aligned");
-  if (!aligned(work_items, 16)) return set_error(TQ_ERR_INVALID, "work items must be 16-byte aligned");
-  if (table_stride < 0) return set_error(TQ_ERR_INVALID, "table_stride must be >= 0");
-  if (!(scale > 0.f) || !std::isfinite(scale)) return set_error(TQ_ERR_INVALID, "bad scale");
-  int sms = 0;
-  if ((st = device_setup(&sms))) return st;
+  AttnParams p;
+  int st = attention_params(out, out_row_stride, q, q_row_stride, pool, num_blocks, n_layer, n_head,
+                            block_size, head_dim, layer, block_tables, table_stride, attn_plan, n_ctas,
+                            scale, &p);
+  if (st || n_ctas == 0) return st;
   unsigned char* base = nullptr;
   if ((st = noalloc_scratch(&base))) return st;
   const cudaStream_t s = (cudaStream_t)stream;
@@ -322,30 +322,11 @@ int tq_paged_attention_noalloc(float* out, int64_t out_row_stride, const float* 
     if (e != cudaSuccess)
       return set_error(TQ_ERR_CUDA, "clearing split-K counters: %s", cudaGetErrorString(e));
   }
-  AttnParams p;
-  p.out = out;
-  p.out_stride = out_row_stride;
-  p.q = q;
-  p.q_stride = q_row_stride;
-  p.pool = pool;
-  p.num_blocks = num_blocks;
-  p.n_layer = n_layer;
-  p.n_head = n_head;
-  p.block_size = block_size;
-  p.log2_bs = log2_exact(block_size);
-  p.layer = layer;
-  p.tables = block_tables;
-  p.table_stride = table_stride;
-  p.items = reinterpret_cast<const WorkItem*>(work_items);
-  p.n_items = d_num_items;
-  p.max_items = max_items;
   p.part_cnt = reinterpret_cast<int*>(base);
   p.part_ml = reinterpret_cast<float*>(base + kNoAllocCounterBytes);
   p.part_acc = reinterpret_cast<float*>(base + kNoAllocCounterBytes + kNoAllocMlBytes);
-  p.scale_log2 = scale * 1.4426950408889634f;
-  const int64_t units = (int64_t)max_items * n_head;
-  const int grid = (int)std::min<int64_t>((units + kAttnWarps - 1) / kAttnWarps, sms);
-  paged_attention_kernel<<<grid, kAttnThreads, kAttnSmemBytes, s>>>(p);
+  p.max_partials = num_partials;
+  paged_attention_kernel<<<n_ctas, kAttnThreads, kAttnSmemBytes, s>>>(p);
   return check_launch("paged_attention_noalloc");
 }
 

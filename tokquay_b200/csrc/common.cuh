@@ -23,6 +23,7 @@ enum DeviceError : int {
   TQ_DEVERR_BAD_BLOCK = 2,     // a block id outside [0, num_blocks) reached a kernel
   TQ_DEVERR_BAD_SLOT = 4,      // a slot index outside the pool reached a kernel
   TQ_DEVERR_BAD_TOKEN = 8,     // a token id outside the vocabulary reached a kernel
+  TQ_DEVERR_BAD_PLAN = 16,     // a work item's merge slot or split-K index lies outside its buffer
 };
 
 // The library is one translation unit (capi.cu includes every kernel

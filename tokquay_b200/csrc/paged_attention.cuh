@@ -1,5 +1,5 @@
 // Paged attention over the Tokquay block pool, decode and causal prefill rows
-// in one launch, split-K merge included.
+// in one launch, every merge of split keys included.
 //
 // Replaces the dense gather + masked softmax of the reference
 // (tokquay/kv_cache.py:234-242 and tokquay/model.py:94-96): K/V blocks are
@@ -8,27 +8,31 @@
 // and never copied into a dense [B, H, S, d] tensor.
 //
 // Work decomposition.  The host planner (plan.cpp) cuts every sequence's new
-// query rows into groups of up to kMaxRows consecutive rows and the keys each
-// group may see (positions 0 .. last row's position, the causal rule of
-// kv_cache.py:213-214) into chunks of kChunk keys; a group with many chunks is
-// split into several work items (split-K).  One *unit* = (work item, head)
-// is processed by one warp.  Decode rows are simply groups of one row.
+// query rows into groups of up to kMaxRows consecutive rows; a (row group,
+// head) pair attends to keys 0 .. its last row's position (the causal rule of
+// kv_cache.py:213-214), a run of kChunk-key chunks.  Pairs go to the grid's
+// CTAs longest first (each to the least loaded CTA), and each CTA's chunks are
+// cut evenly over its kAttnWarps computing warps, so a pair may be shared by
+// neighbouring warps.  Those cuts are merged through shared memory once the
+// CTA's warps are done -- no global fence, no atomic.  Only a pair longer than
+// a CTA's share is split across CTAs; those pieces are merged through split-K
+// scratch by the last one to finish (acq_rel counter).  A work item is one
+// warp's share of one pair: rows, head, chunk range, merge target.
 //
-// Pipeline.  Each warp is an independent persistent worker with its own ring
-// of kStages shared-memory stages.  Lane 0 issues TMA bulk copies
-// (cp.async.bulk, global -> shared, mbarrier completion) for the K and V rows
-// of upcoming chunks -- across unit boundaries, so short decode units keep the
-// ring full -- while the warp computes on the oldest stage.  The work metadata
-// travels with the data: block ids are prefetched a chunk ahead, work items a
-// unit ahead, and each stage carries a header, so no global-memory latency sits
-// between two chunks of compute.  Per chunk:
+// Pipeline.  Each computing (consumer) warp has a producer warp and a ring of
+// kStages shared-memory stages.  The producer walks the same work items,
+// prefetches item metadata two items ahead and block ids one item ahead, and
+// issues TMA bulk copies (cp.async.bulk, global -> shared, mbarrier
+// completion) for the K and V rows of upcoming chunks -- one copy per lane,
+// one warp instruction per chunk -- as soon as the consumer releases a stage.
+// Each stage carries a header with the item, so the consumer never reads
+// work metadata from global memory.  Per chunk the consumer does:
 //   * QK^T and PV with lane = (key group, quarter of the head dims): q rows
 //     and output accumulators live in registers, 4 passes of 8 keys cover
 //     the chunk, shared loads are conflict-free (see attend_chunk);
 //   * online softmax in the log2 domain, state in registers.
-// Finished units write either the normalised output row or (split items) an
-// un-normalised partial (m, l, acc[64]); the last split of a row merges them
-// (merge_if_last), so no second kernel is launched.
+// A finished item writes the normalised output row, or an unnormalised
+// partial (m, l, acc[64]) to its shared slot or split-K slot.
 #pragma once
 
 #include "common.cuh"
@@ -47,12 +51,6 @@ namespace tq {
 #endif
 #ifndef TQ_ATTN_WARPS
 #define TQ_ATTN_WARPS 6
-#endif
-#ifndef TQ_ATTN_EARLY_REFILL
-#define TQ_ATTN_EARLY_REFILL 1
-#endif
-#ifndef TQ_ATTN_SC_FENCE
-#define TQ_ATTN_SC_FENCE 0
 #endif
 constexpr int kHeadDim = 64;
 constexpr int kChunk = TQ_ATTN_CHUNK;        // keys per pipeline stage (16 or 32)
@@ -93,22 +91,52 @@ constexpr int kQBytes = kMaxRows * kRowBytes;                  // 1 KiB
 constexpr int kHeaderBytes = 64;                               // StageHeader, padded
 constexpr int kStageBytes = 2 * kKBytes + kQBytes + kHeaderBytes;  // K | V | Q | header
 constexpr int kWarpSmemBytes = kStages * kStageBytes + 64;  // + barriers
-constexpr int kAttnSmemBytes = kAttnWarps * kWarpSmemBytes;
 
-// One work item: rows [row0, row0+nrows) of sequence `seq` (absolute
-// positions pos0 ..), keys of chunks [cbeg, cend).  Split items (nsplit > 1)
-// write partials at part + (r*n_head + h)*nsplit + split.
+// Shared-memory partials of keys cut between warps of one CTA: one slot per
+// (piece, row) = {m, l, -, -, acc[64]} floats.  Each warp boundary cuts at
+// most one (row group, head) pair, so 2 * (warps - 1) * max_rows slots hold
+// every cut (the planner's bound).
+constexpr int kLocalSlots = 2 * (kAttnWarps - 1) * kMaxRows;
+constexpr int kSlotFloats = 4 + kHeadDim;
+constexpr int kLocalBytes = kLocalSlots * kSlotFloats * 4;
+constexpr int kAttnSmemBytes = kAttnWarps * kWarpSmemBytes + kLocalBytes;
+
+// One work item (8 int32, written by the planner): query rows
+// [row0, row0+nrows) of sequence seq (absolute positions pos0 ..), head, the
+// keys of chunks [cbeg, cend).  Keys of one (row group, head) pair cut between
+// warps of a CTA (flag kLocal) go to shared-memory slots lslot + r*lcount +
+// lsplit and are merged by the warp holding lsplit 0 once the CTA's warps are
+// done; pairs split across CTAs (flag kGlobal) go to split-K partials
+// gbase + r*gnsplit + gsplit, merged by the last split to finish.
+//   w[0] seq   w[1] row0   w[2] nrows | head << 8 | flags << 24   w[3] pos0
+//   w[4] cbeg | cend << 16   w[5] lsplit | lcount << 8 | lslot << 16
+//   w[6] gbase   w[7] gsplit | gnsplit << 16
+// An all-zero item (cend == 0) marks a warp without work.
+constexpr int kFlagLocal = 1, kFlagGlobal = 2;
 struct __align__(16) WorkItem {
-  int seq, row0, nrows, pos0;
-  int cbeg, cend, part, split_nsplit;  // split | nsplit << 16
+  int w[8];
+  __device__ __forceinline__ int seq() const { return w[0]; }
+  __device__ __forceinline__ int row0() const { return w[1]; }
+  __device__ __forceinline__ int nrows() const { return w[2] & 0xff; }
+  __device__ __forceinline__ int head() const { return (w[2] >> 8) & 0xffff; }
+  __device__ __forceinline__ int flags() const { return (int)((unsigned)w[2] >> 24); }
+  __device__ __forceinline__ int pos0() const { return w[3]; }
+  __device__ __forceinline__ int cbeg() const { return w[4] & 0xffff; }
+  __device__ __forceinline__ int cend() const { return (int)((unsigned)w[4] >> 16); }
+  __device__ __forceinline__ int lsplit() const { return w[5] & 0xff; }
+  __device__ __forceinline__ int lcount() const { return (w[5] >> 8) & 0xff; }
+  __device__ __forceinline__ int lslot() const { return (int)((unsigned)w[5] >> 16); }
+  __device__ __forceinline__ int gbase() const { return w[6]; }
+  __device__ __forceinline__ int gsplit() const { return w[7] & 0xffff; }
+  __device__ __forceinline__ int gnsplit() const { return (int)((unsigned)w[7] >> 16); }
 };
 static_assert(sizeof(WorkItem) == 32, "WorkItem is 8 int32");
 
-// Written into each stage by the producer lane together with the copies, so
-// the computing lanes never read work metadata from global memory.
+// Written into each stage by the producer together with the copies, so the
+// consumer never reads work metadata from global memory.
 struct StageHeader {
   WorkItem it;
-  int h, c, pad0, pad1;
+  int c, pad0, pad1, pad2;
 };
 static_assert(sizeof(StageHeader) <= kHeaderBytes, "header fits its slot");
 
@@ -122,14 +150,28 @@ struct AttnParams {
   int n_layer, n_head, block_size, log2_bs, layer;
   const int* tables;     // [num_seqs][table_stride] block ids
   int table_stride;
-  const WorkItem* items;
-  const int* n_items;    // device-resident count
-  int max_items;         // capacity of `items` (entries that may be read, valid or not)
+  const int* attn;       // attention plan: [W][8] first items, [W+1] offsets (padded to 8), other items
+  int n_warps;           // W = grid * kAttnWarps
   float* part_ml;        // [P][2]  (m in log2 units, l)
   float* part_acc;       // [P][64]
   int* part_cnt;         // [P] split counters (zero between launches)
+  int max_partials;      // P
   float scale_log2;      // log2(e) / sqrt(head_dim)
 };
+
+// A work item's merge targets lie inside the shared slots and the split-K
+// scratch; one that does not (a corrupted plan) is flagged and not written.
+__device__ __forceinline__ bool merge_targets_ok(const AttnParams& p, const WorkItem& it) {
+  const int f = it.flags();
+  bool ok = true;
+  if (f & kFlagLocal)
+    ok = it.lcount() >= 2 && it.lsplit() < it.lcount() && it.lslot() + it.nrows() * it.lcount() <= kLocalSlots;
+  if (f & kFlagGlobal)
+    ok = ok && it.gbase() >= 0 && it.gsplit() < it.gnsplit() &&
+         (long long)it.gbase() + (long long)it.nrows() * it.gnsplit() <= p.max_partials;
+  if (!ok && (threadIdx.x & 31) == 0) raise_device_error(TQ_DEVERR_BAD_PLAN);
+  return ok;
+}
 
 __device__ __forceinline__ size_t pool_tile_offset(const AttnParams& p, long long blk, int kv,
                                                    int h) {
@@ -138,27 +180,25 @@ __device__ __forceinline__ size_t pool_tile_offset(const AttnParams& p, long lon
          (size_t)p.block_size * kHeadDim;
 }
 
-// Lanes 0..7 hold the 8 ints of a work item; every lane gets the fields.
+// Lanes 0..7 hold the 8 ints of a work item; every lane gets them all.
 __device__ __forceinline__ WorkItem item_from_lanes(int v) {
-  WorkItem w;
-  w.seq = __shfl_sync(kFullMask, v, 0);
-  w.row0 = __shfl_sync(kFullMask, v, 1);
-  w.nrows = __shfl_sync(kFullMask, v, 2);
-  w.pos0 = __shfl_sync(kFullMask, v, 3);
-  w.cbeg = __shfl_sync(kFullMask, v, 4);
-  w.cend = __shfl_sync(kFullMask, v, 5);
-  w.part = __shfl_sync(kFullMask, v, 6);
-  w.split_nsplit = __shfl_sync(kFullMask, v, 7);
-  return w;
+  WorkItem it;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) it.w[i] = __shfl_sync(kFullMask, v, i);
+  return it;
 }
 
-// Loads are bounded by the buffer's capacity, not by the device-resident
-// count, so they need not wait for the count; a unit past the count is never
-// used (the consumers check it against n_units).
-__device__ __forceinline__ int item_lane_load(const AttnParams& p, int unit, int lane) {
-  return (unit < p.max_items * p.n_head && lane < 8)
-             ? __ldg(reinterpret_cast<const int*>(p.items) + (size_t)(unit / p.n_head) * 8 + lane)
-             : 0;
+// Word `lane` (lanes 0..7) of item k of warp slot `ws`: k == 0 is the warp's
+// first item, at a fixed place, so its load needs no offset; items k >= 1
+// follow the warp's offset r0 in the list of the others.
+__device__ __forceinline__ const int* warp_offsets(const AttnParams& p) { return p.attn + 8 * p.n_warps; }
+__device__ __forceinline__ const int* other_items(const AttnParams& p) {
+  return p.attn + 8 * p.n_warps + ((p.n_warps + 1 + 7) & ~7);
+}
+__device__ __forceinline__ int item_lane_load(const AttnParams& p, int ws, int r0, int k, int count, int lane) {
+  if (k >= count || lane >= 8) return 0;
+  const int* src = k == 0 ? p.attn + 8 * (size_t)ws : other_items(p) + 8 * (size_t)(r0 + k - 1);
+  return __ldg(src + lane);
 }
 
 // Keys [key0, key0+nkeys) of chunk c, and the blocks [kb0, kb0+nblk) they live in.
@@ -168,7 +208,7 @@ struct ChunkSpan {
 
 __device__ __forceinline__ ChunkSpan chunk_span(const AttnParams& p, const WorkItem& it, int c) {
   ChunkSpan sp;
-  const int kend = min(it.pos0 + it.nrows, it.cend * kChunk);  // this item's last key + 1
+  const int kend = min(it.pos0() + it.nrows(), it.cend() * kChunk);  // this item's last key + 1
   sp.key0 = c * kChunk;
   sp.nkeys = min(kChunk, kend - sp.key0);
   sp.kb0 = sp.key0 >> p.log2_bs;
@@ -288,71 +328,62 @@ __device__ __forceinline__ void attend_chunk(const float* __restrict__ K, const 
   }
 }
 
-// Split-K merge, fused: the warp that writes the last partial of a (row,
+// Split-K merge across CTAs: the warp that writes the last partial of a (row,
 // head) merges all of them into the output row.  Each (row, head) has a
 // counter in part_cnt (at the index of its split 0 partial); every split
-// publishes its partial, fences, and bumps the counter; the one that sees
-// nsplit - 1 reads the partials back through L2 and resets the counter to 0,
-// so the scratch is ready for the next launch without a memset.
-__device__ __forceinline__ void merge_if_last(const AttnParams& p, const WorkItem& it, int r, int h,
-                                              int nsplit, int lane, long long* tr_sub) {
-  const size_t idx0 = (size_t)it.part + ((size_t)r * p.n_head + h) * nsplit;
-  __syncwarp();
+// publishes its partial, then bumps the counter (release: the partial is
+// visible before the count says so; acquire: the last split sees every other
+// split's partial).  The one that sees nsplit - 1 reads the partials back
+// through L2 and resets the counter to 0, so the scratch is ready for the next
+// launch without a memset.
+__device__ __forceinline__ void merge_global_if_last(const AttnParams& p, size_t idx0, int nsplit, int out_row,
+                                                     int h, int lane, long long* tr_sub) {
+  __syncwarp();  // the lanes' partial stores are ordered before lane 0's release
   TQ_TRACE(long long tm0 = clock64();)
   int last = 0;
   if (lane == 0) {
-#if TQ_ATTN_SC_FENCE
-    __threadfence();
-    last = atomicAdd(p.part_cnt + idx0, 1) == nsplit - 1;
-#else
-    // Release: the partial this warp stored (lanes 0-3, ordered before lane 0
-    // by the __syncwarp above) is visible before the count says so.  Acquire:
-    // the last split sees every other split's partial.
     int old;
     asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.part_cnt + idx0) : "memory");
     last = old == nsplit - 1;
-#endif
   }
   last = __shfl_sync(kFullMask, last, 0);
   TQ_TRACE(if (lane == 0) tr_sub[4] += clock64() - tm0; tm0 = clock64();)
   if (!last) return;
-#if TQ_ATTN_SC_FENCE
-  __threadfence();
-#else
   __syncwarp();  // lane 0's acquire orders the other lanes' reads of the partials below
-#endif
   float mmax = -INFINITY;
   for (int s = lane; s < nsplit; s += 32) mmax = fmaxf(mmax, __ldcg(p.part_ml + 2 * (idx0 + s)));
   mmax = warp_max(mmax);
   float l = 0.f;
   float2 o = make_float2(0.f, 0.f);
   for (int s = 0; s < nsplit; ++s) {
-    const float w = exp2f(__ldcg(p.part_ml + 2 * (idx0 + s)) - mmax);  // 0 for a split without keys
+    const float ms = __ldcg(p.part_ml + 2 * (idx0 + s));
+    const float w = ms == -INFINITY ? 0.f : exp2f(ms - mmax);  // 0 for a split without keys
     l = fmaf(__ldcg(p.part_ml + 2 * (idx0 + s) + 1), w, l);
     const float2 a = __ldcg(reinterpret_cast<const float2*>(p.part_acc + (idx0 + s) * kHeadDim) + lane);
     o.x = fmaf(a.x, w, o.x);
     o.y = fmaf(a.y, w, o.y);
   }
   const float inv = 1.f / l;
-  reinterpret_cast<float2*>(p.out + (size_t)(it.row0 + r) * p.out_stride + h * kHeadDim)[lane] =
+  reinterpret_cast<float2*>(p.out + (size_t)out_row * p.out_stride + h * kHeadDim)[lane] =
       make_float2(o.x * inv, o.y * inv);
   if (lane == 0) p.part_cnt[idx0] = 0;
   TQ_TRACE(if (lane == 0) tr_sub[5] += clock64() - tm0;)
 }
 
-// End of a unit: sum l and the accumulators over the 8 key groups (lanes
+// End of a work item: sum l and the accumulators over the 8 key groups (lanes
 // xor 4, 8, 16; partners across xor 4 hold their slots rotated by 2) and write
-// each row -- normalised output, or a split-K partial.
-__device__ __forceinline__ void finish_rows(const AttnParams& p, const WorkItem& it, int h, int lane,
+// each row: the normalised output, a shared-memory partial (keys cut between
+// this CTA's warps) or a split-K partial (keys split across CTAs).
+__device__ __forceinline__ void finish_rows(const AttnParams& p, const WorkItem& it, int lane,
                                             const float (&m)[kMaxRows], float (&lsum)[kMaxRows],
-                                            float4 (&acc)[kMaxRows][4], long long* tr_sub) {
+                                            float4 (&acc)[kMaxRows][4], float* local, long long* tr_sub) {
   TQ_TRACE(const long long tf0 = clock64(); if (lane == 0) tr_sub[6] += 1;)
   const int qq = lane & 3, rot = lane_rot(lane);
-  const int split = it.split_nsplit & 0xffff;
-  const int nsplit = it.split_nsplit >> 16;
+  const int flags = it.flags(), h = it.head();
+  if (flags != 0 && !merge_targets_ok(p, it)) return;
 #pragma unroll
   for (int r = 0; r < kMaxRows; ++r) {
-    if (r < it.nrows) {
+    if (r < it.nrows()) {
       float l = lsum[r];
       l += __shfl_xor_sync(kFullMask, l, 4);
       l += __shfl_xor_sync(kFullMask, l, 8);
@@ -381,33 +412,82 @@ __device__ __forceinline__ void finish_rows(const AttnParams& p, const WorkItem&
         acc[r][i] = a;
       }
       if (lane < 4) {  // key group 0 writes the row: 4 lanes x 64 bytes
-        if (nsplit == 1) {
+        if (flags == 0) {
           const float inv = 1.f / l;
-          float4* o = reinterpret_cast<float4*>(p.out + (size_t)(it.row0 + r) * p.out_stride +
+          float4* o = reinterpret_cast<float4*>(p.out + (size_t)(it.row0() + r) * p.out_stride +
                                                 h * kHeadDim + qq * 16);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
             o[(i + rot) & 3] = make_float4(acc[r][i].x * inv, acc[r][i].y * inv, acc[r][i].z * inv,
                                            acc[r][i].w * inv);
         } else {
-          const size_t idx = (size_t)it.part + ((size_t)r * p.n_head + h) * nsplit + split;
-          float4* o = reinterpret_cast<float4*>(p.part_acc + idx * kHeadDim + qq * 16);
+          float* ml;
+          float4* o;
+          if (flags & kFlagLocal) {
+            float* sl = local + (size_t)(it.lslot() + r * it.lcount() + it.lsplit()) * kSlotFloats;
+            ml = sl;
+            o = reinterpret_cast<float4*>(sl + 4 + qq * 16);
+          } else {
+            const size_t idx = (size_t)it.gbase() + (size_t)r * it.gnsplit() + it.gsplit();
+            ml = p.part_ml + 2 * idx;
+            o = reinterpret_cast<float4*>(p.part_acc + idx * kHeadDim + qq * 16);
+          }
 #pragma unroll
           for (int i = 0; i < 4; ++i) o[(i + rot) & 3] = acc[r][i];
           if (lane == 0) {
-            p.part_ml[2 * idx] = m[r];
-            p.part_ml[2 * idx + 1] = l;
+            ml[0] = m[r];
+            ml[1] = l;
           }
         }
       }
       TQ_TRACE(if (lane == 0) tr_sub[3] += clock64() - tf0;)
-      if (nsplit > 1) merge_if_last(p, it, r, h, nsplit, lane, tr_sub);
+      if (flags == kFlagGlobal)
+        merge_global_if_last(p, (size_t)it.gbase() + (size_t)r * it.gnsplit(), it.gnsplit(), it.row0() + r, h,
+                             lane, tr_sub);
+    }
+  }
+}
+
+// After every warp of the CTA is done: merge the shared-memory partials of
+// the pair whose lsplit-0 piece this warp ran, into the output row or (keys
+// also split across CTAs) into this CTA's split-K partial.
+__device__ __forceinline__ void merge_local(const AttnParams& p, const WorkItem& it, const float* local,
+                                            int lane, long long* tr_sub) {
+  const int k = it.lcount(), h = it.head();
+  for (int r = 0; r < it.nrows(); ++r) {
+    const float* s0 = local + (size_t)(it.lslot() + r * k) * kSlotFloats;
+    float mmax = -INFINITY;
+    for (int s = 0; s < k; ++s) mmax = fmaxf(mmax, s0[s * kSlotFloats]);
+    float l = 0.f;
+    float2 o = make_float2(0.f, 0.f);
+    for (int s = 0; s < k; ++s) {
+      const float* sl = s0 + s * kSlotFloats;
+      const float w = sl[0] == -INFINITY ? 0.f : exp2f(sl[0] - mmax);  // 0 for a piece without keys
+      l = fmaf(sl[1], w, l);
+      const float2 a = reinterpret_cast<const float2*>(sl + 4)[lane];
+      o.x = fmaf(a.x, w, o.x);
+      o.y = fmaf(a.y, w, o.y);
+    }
+    if (it.flags() & kFlagGlobal) {
+      const size_t idx0 = (size_t)it.gbase() + (size_t)r * it.gnsplit();
+      const size_t idx = idx0 + it.gsplit();
+      reinterpret_cast<float2*>(p.part_acc + idx * kHeadDim)[lane] = o;
+      if (lane == 0) {
+        p.part_ml[2 * idx] = mmax;
+        p.part_ml[2 * idx + 1] = l;
+      }
+      merge_global_if_last(p, idx0, it.gnsplit(), it.row0() + r, h, lane, tr_sub);
+    } else {
+      const float inv = 1.f / l;
+      reinterpret_cast<float2*>(p.out + (size_t)(it.row0() + r) * p.out_stride + h * kHeadDim)[lane] =
+          make_float2(o.x * inv, o.y * inv);
     }
   }
 }
 
 // Block layout: warps 0..kAttnWarps-1 are consumers, warps kAttnWarps.. their
-// producers; consumer w and producer kAttnWarps+w share ring w.
+// producers; consumer w and producer kAttnWarps+w share ring w and walk the
+// same work items (the planner's list for warp slot blockIdx.x*kAttnWarps+w).
 constexpr int kAttnThreads = 2 * kAttnWarps * 32;
 
 __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const AttnParams p) {
@@ -417,21 +497,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
   const bool producer = warp >= kAttnWarps;
   const int pair = producer ? warp - kAttnWarps : warp;
   unsigned char* wsm = smem + pair * kWarpSmemBytes;
+  float* local = reinterpret_cast<float*>(smem + kAttnWarps * kWarpSmemBytes);
   const uint32_t full0 = smem_addr(wsm + kStages * kStageBytes);  // TMA bytes landed
   const uint32_t empty0 = full0 + 8 * kStages;                    // consumer done reading
 
   const int H = p.n_head;
-  const int wslot = blockIdx.x * kAttnWarps + pair;
-  const int first_item_word = producer ? item_lane_load(p, wslot, lane) : 0;  // overlaps the count
-  const int n_units = *p.n_items * H;
-  const int TW = gridDim.x * kAttnWarps;
-  // Units are visited in snake order: round r gives this pair unit
-  // r*TW + w on even rounds and r*TW + TW-1-w on odd ones.  The planner sorts
-  // items longest first, so each pair gets a long and a short unit in every
-  // pair of rounds and all pairs finish together.  Producer and consumer walk
-  // the same sequence.
-  auto unit_of = [&](int round) { return round * TW + ((round & 1) ? TW - 1 - wslot : wslot); };
-  TQ_TRACE(const int gw = wslot; unsigned long long* trec = g_attn_trace + (size_t)gw * kTraceSlots;
+  const int ws = blockIdx.x * kAttnWarps + pair;
+  // The first item sits at a fixed place: its load and the offsets' load go out together.
+  const int first_word = lane < 8 ? __ldg(p.attn + 8 * (size_t)ws + lane) : 0;
+  const int r0 = __ldg(warp_offsets(p) + ws), r1 = __ldg(warp_offsets(p) + ws + 1);
+  const bool has_work = ((unsigned)__shfl_sync(kFullMask, first_word, 4) >> 16) != 0;  // cend != 0
+  const int count = has_work ? 1 + r1 - r0 : 0;
+  TQ_TRACE(const int gw = ws; unsigned long long* trec = g_attn_trace + (size_t)gw * kTraceSlots;
            long long tr_sub[8] = {0, 0, 0, 0, 0, 0, 0, 0};)
 
   if (!producer && lane == 0) {
@@ -442,35 +519,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
     mbar_init_fence();
   }
   __syncthreads();  // every ring's barriers are initialised before either warp of a pair uses them
-  if (wslot >= n_units) return;  // pair-uniform: producer and consumer leave together
 
   if (producer) {
+    if (count == 0) return;
     // ---- producer: work metadata and TMA issue, up to kStages chunks ahead ----
-    // Block ids of the current unit's key range (at most kUnitBlocks; the
-    // planner keeps units that short) live in two registers per lane: lane i
-    // holds blocks kb0+i and kb0+32+i.  They are loaded one unit ahead, and
-    // the work item two units ahead, so neither load sits between two issues.
+    // Block ids of the current item's key range (at most kUnitBlocks; the
+    // planner keeps items that short) live in two registers per lane: lane i
+    // holds blocks kb0+i and kb0+32+i.  They are loaded one item ahead, and
+    // the item itself two ahead, so neither load sits between two issues.
     TQ_TRACE(long long tr_empty = 0;)
-    int p_round = 0;
-    int p_unit = wslot;
-    WorkItem p_it = item_from_lanes(first_item_word);
-    int p_chunk = p_it.cbeg;
-    int pf_a = 0, pf_b = 0;  // current unit's block ids
-    int nx_a = 0, nx_b = 0;  // next unit's block ids (in flight)
-    auto load_unit_blocks = [&](const WorkItem& w, bool valid, int& a, int& b) {
+    int p_k = 0;
+    WorkItem p_it = item_from_lanes(first_word);
+    int p_chunk = p_it.cbeg();
+    int pf_a = 0, pf_b = 0;  // current item's block ids
+    int nx_a = 0, nx_b = 0;  // next item's block ids (in flight)
+    auto load_item_blocks = [&](const WorkItem& w, bool valid, int& a, int& b) {
       if (!valid) return;
-      const int kb0 = (w.cbeg * kChunk) >> p.log2_bs;
-      const int kend = min(w.pos0 + w.nrows, w.cend * kChunk);
+      const int kb0 = (w.cbeg() * kChunk) >> p.log2_bs;
+      const int kend = min(w.pos0() + w.nrows(), w.cend() * kChunk);
       const int n = ((kend - 1) >> p.log2_bs) - kb0 + 1;
-      const int* tbl = p.tables + (size_t)w.seq * p.table_stride + kb0;
+      const int* tbl = p.tables + (size_t)w.seq() * p.table_stride + kb0;
       a = lane < n ? __ldg(tbl + lane) : 0;
       b = lane + 32 < n ? __ldg(tbl + 32 + lane) : 0;
     };
-    load_unit_blocks(p_it, true, pf_a, pf_b);
-    bool nx_valid = unit_of(1) < n_units;
-    WorkItem nx_it = item_from_lanes(item_lane_load(p, unit_of(1), lane));
-    load_unit_blocks(nx_it, nx_valid, nx_a, nx_b);
-    int nx2_item = item_lane_load(p, unit_of(2), lane);
+    load_item_blocks(p_it, true, pf_a, pf_b);
+    WorkItem nx_it = item_from_lanes(item_lane_load(p, ws, r0, 1, count, lane));
+    load_item_blocks(nx_it, 1 < count, nx_a, nx_b);
+    int nx2_word = item_lane_load(p, ws, r0, 2, count, lane);
     int issued = 0;
     bool ok = true;
 
@@ -485,24 +560,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
           break;
         }
       }
-      // Issue chunk p_chunk of the current unit into stage s.  Each lane
+      // Issue chunk p_chunk of the current item into stage s.  Each lane
       // describes one copy (K or V rows of one block, or a q row), and the
       // copies go out as one warp-wide cp.async.bulk.
       unsigned char* stage = wsm + s * kStageBytes;
       const uint32_t bar = full0 + 8 * s;
       const ChunkSpan sp = chunk_span(p, p_it, p_chunk);
-      const bool first = (p_chunk == p_it.cbeg);
+      const bool first = (p_chunk == p_it.cbeg());
       const int bs = p.block_size;
-      const int h = p_unit % H;
-      const int unit_kb0 = (p_it.cbeg * kChunk) >> p.log2_bs;
+      const int h = p_it.head();
+      const int item_kb0 = (p_it.cbeg() * kChunk) >> p.log2_bs;
       const int n_kv = 2 * sp.nblk;
-      const int n_desc = n_kv + (first ? p_it.nrows : 0);
+      const int n_desc = n_kv + (first ? p_it.nrows() : 0);
       const uint32_t sK = smem_addr(stage);
       const size_t kv_stride = (size_t)H * bs * kHeadDim;  // K tile -> V tile
       TQ_TRACE(long long ti0 = clock64();)
       auto describe = [&](int d, const float*& src, uint32_t& dst, uint32_t& bytes) {
         // Every lane shuffles (the source lane varies per lane).
-        const int rel = (sp.kb0 - unit_kb0) + min(d, max(n_kv - 1, 0)) / 2;
+        const int rel = (sp.kb0 - item_kb0) + min(d, max(n_kv - 1, 0)) / 2;
         const int a = __shfl_sync(kFullMask, pf_a, rel & 31);
         const int b = __shfl_sync(kFullMask, pf_b, rel & 31);
         bytes = 0;
@@ -527,7 +602,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
           }
         } else if (d < n_desc) {
           const int r = d - n_kv;
-          src = p.q + (size_t)(p_it.row0 + r) * p.q_stride + h * kHeadDim;
+          src = p.q + (size_t)(p_it.row0() + r) * p.q_stride + h * kHeadDim;
           dst = sK + 2 * kKBytes + r * kRowBytes;
           bytes = kRowBytes;
         }
@@ -546,10 +621,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
       }
       TQ_TRACE(if (lane == 0) tr_sub[0] += clock64() - ti0; ti0 = clock64();)
       if (lane == 0) {
-        if (first) {  // the consumer picks the unit's work item up from here
+        if (first) {  // the consumer picks the item up from here
           StageHeader* hd = reinterpret_cast<StageHeader*>(stage + 2 * kKBytes + kQBytes);
           hd->it = p_it;
-          hd->h = h;
           hd->c = p_chunk;
         }
         // Releases the header store to the consumer's acquiring wait.  A
@@ -573,17 +647,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
       ++issued;
 
       // Advance the cursor.
-      if (++p_chunk == p_it.cend) {
-        p_unit = unit_of(++p_round);
-        if (p_unit >= n_units) break;
+      if (++p_chunk == p_it.cend()) {
+        if (++p_k == count) break;
         p_it = nx_it;
         pf_a = nx_a;
         pf_b = nx_b;
-        p_chunk = p_it.cbeg;
-        nx_valid = unit_of(p_round + 1) < n_units;
-        nx_it = item_from_lanes(nx2_item);
-        load_unit_blocks(nx_it, nx_valid, nx_a, nx_b);
-        nx2_item = item_lane_load(p, unit_of(p_round + 2), lane);
+        p_chunk = p_it.cbeg();
+        nx_it = item_from_lanes(nx2_word);
+        load_item_blocks(nx_it, p_k + 1 < count, nx_a, nx_b);
+        nx2_word = item_lane_load(p, ws, r0, p_k + 2, count, lane);
       }
       TQ_TRACE(if (lane == 0) tr_sub[2] += clock64() - ti0;)
     }
@@ -610,10 +682,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
   const int rot = lane_rot(lane);
   int consumed = 0;
   bool failed = false;
-  for (int round = 0; unit_of(round) < n_units; ++round) {
+  WorkItem owned;  // the cut pair whose shared-memory partials this warp merges
+  bool has_owned = false;
+  for (int k = 0; k < count; ++k) {
     WorkItem it;
-    int h = 0, c = 0;
-    bool at_unit_start = true;
+    int c = 0;
+    bool at_item_start = true;
     do {
       const int s = consumed % kStages;
       const uint32_t parity = (uint32_t)(consumed / kStages) & 1u;
@@ -627,11 +701,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
         break;
       }
       const unsigned char* stage = wsm + s * kStageBytes;
-      if (at_unit_start) {  // take the unit's work item and q rows, reset state
+      if (at_item_start) {  // take the item and its q rows, reset state
         const StageHeader* hd = reinterpret_cast<const StageHeader*>(stage + 2 * kKBytes + kQBytes);
         it = hd->it;
-        h = hd->h;
-        c = it.cbeg;
+        c = it.cbeg();
         const float4* qsrc = reinterpret_cast<const float4*>(stage + 2 * kKBytes);
 #pragma unroll
         for (int r = 0; r < kMaxRows; ++r) {
@@ -640,29 +713,48 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             acc[r][i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            qr[r][i] = r < it.nrows ? qsrc[r * (kHeadDim / 4) + (lane & 3) * 4 + ((i + rot) & 3)]
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            qr[r][i] = r < it.nrows() ? qsrc[r * (kHeadDim / 4) + (lane & 3) * 4 + ((i + rot) & 3)]
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
           }
         }
-        at_unit_start = false;
+        at_item_start = false;
       }
       const ChunkSpan sp = chunk_span(p, it, c);
       const float* K = reinterpret_cast<const float*>(stage);
       const float* V = reinterpret_cast<const float*>(stage + kKBytes);
       TQ_TRACE(tr0 = clock64();)
-      if (it.nrows == 1)
-        attend_chunk<1>(K, V, qr, 1, it.pos0, sp.key0, sp.nkeys, p.scale_log2, lane, m, lsum, acc);
+      if (it.nrows() == 1)
+        attend_chunk<1>(K, V, qr, 1, it.pos0(), sp.key0, sp.nkeys, p.scale_log2, lane, m, lsum, acc);
       else
-        attend_chunk<kMaxRows>(K, V, qr, it.nrows, it.pos0, sp.key0, sp.nkeys, p.scale_log2, lane, m,
+        attend_chunk<kMaxRows>(K, V, qr, it.nrows(), it.pos0(), sp.key0, sp.nkeys, p.scale_log2, lane, m,
                                lsum, acc);
       __syncwarp();  // every lane's reads of the stage are done
       if (lane == 0) mbar_arrive(empty0 + 8 * s);
       TQ_TRACE(tr_comp += clock64() - tr0;)
       ++consumed;
-    } while (++c < it.cend);
+    } while (++c < it.cend());
     if (failed) break;
     TQ_TRACE(long long tf0 = clock64();)
-    finish_rows(p, it, h, lane, m, lsum, acc, TQ_TRACE_ARG(tr_sub));
+    finish_rows(p, it, lane, m, lsum, acc, local, TQ_TRACE_ARG(tr_sub));
+    if ((it.flags() & kFlagLocal) && it.lsplit() == 0 && merge_targets_ok(p, it)) {
+      owned = it;
+      has_owned = true;
+    }
+    TQ_TRACE(tr_fin += clock64() - tf0;)
+  }
+  if (failed) {
+    // Give the copies the producer may still have in flight (at most the
+    // ring's depth) a bounded chance to land before this warp moves on; the
+    // producer, no longer released, times out on its empty barrier and exits.
+    for (int k = consumed; k < consumed + kStages; ++k)
+      if (!mbar_wait_bounded(full0 + 8 * (k % kStages), (uint32_t)(k / kStages) & 1u)) break;
+  }
+  // Every consumer warp of the CTA (with or without work, failed or not)
+  // meets here, so the shared-memory partials are complete and visible.
+  asm volatile("bar.sync 1, %0;" ::"r"(kAttnWarps * 32) : "memory");
+  if (has_owned && !failed) {
+    TQ_TRACE(long long tf0 = clock64();)
+    merge_local(p, owned, local, lane, TQ_TRACE_ARG(tr_sub));
     TQ_TRACE(tr_fin += clock64() - tf0;)
   }
   TQ_TRACE(if (lane == 0 && gw < kTraceWarps) {
@@ -670,13 +762,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
     trec[5] = tr_fin; trec[7] = tr_chunks;
     for (int k = 3; k < 7; ++k) trec[8 + k] = tr_sub[k];
   })
-  if (failed) {
-    // Give the copies the producer may still have in flight (at most the
-    // ring's depth) a bounded chance to land before this warp exits; the
-    // producer, no longer released, times out on its empty barrier and exits.
-    for (int k = consumed; k < consumed + kStages; ++k)
-      if (!mbar_wait_bounded(full0 + 8 * (k % kStages), (uint32_t)(k / kStages) & 1u)) break;
-  }
 }
 
 }  // namespace tq

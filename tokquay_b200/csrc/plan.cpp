@@ -12,6 +12,7 @@
 // Validation keeps the reference's conditions and messages
 // (kv_cache.py:182-191) and adds pool / vocabulary range checks.
 #include <algorithm>
+#include <array>
 #include <climits>
 #include <cstdarg>
 #include <cstdint>
@@ -32,19 +33,40 @@ namespace {
 #ifndef TQ_ATTN_MAX_ROWS
 #define TQ_ATTN_MAX_ROWS 2
 #endif
+#ifndef TQ_ATTN_WARPS
+#define TQ_ATTN_WARPS 6
+#endif
 constexpr int kChunk = TQ_ATTN_CHUNK;      // keys per attention chunk
 constexpr int kMaxRows = TQ_ATTN_MAX_ROWS; // query rows per work item
+constexpr int kWarps = TQ_ATTN_WARPS;      // computing warps per attention CTA
 constexpr int kUnitBlocks = 64;            // most blocks one work item may span
+constexpr int kMaxChunkIndex = 0xffff;     // chunk indices are stored in 16 bits
+// Work item flags (word 2, bits 24..31).
+constexpr int kFlagLocal = 1;   // keys cut between warps of one CTA: merged in shared memory
+constexpr int kFlagGlobal = 2;  // keys split across CTAs: merged through the split-K scratch
+// Shared-memory partial slots one CTA holds (each warp boundary cuts at most
+// one pair, so a CTA needs at most 2 * (kWarps - 1) * kMaxRows).
+constexpr int kLocalSlots = 2 * (kWarps - 1) * kMaxRows;
 
 inline int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t align4(int64_t n) { return (n + 3) & ~int64_t(3); }
+inline int64_t align8(int64_t n) { return (n + 7) & ~int64_t(7); }
+
+struct Group {  // one query-row group of a sequence
+  int32_t seq, row0, nrows, pos0, nc;  // nc: 32-key chunks it attends to
+};
+
+struct Piece {  // a run of chunks of one (group, head) pair, bound for one CTA
+  int32_t group, head, cbeg, cend, gsplit, gnsplit;
+  int64_t gbase;  // split-K partial of (row 0, split 0), or -1
+};
 
 }  // namespace
 
 extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_t* q_len,
                             const int32_t* table_offsets, const int32_t* table_data,
                             const int32_t* token_ids, int32_t block_size, int64_t num_blocks,
-                            int32_t n_head, int32_t vocab_size, int32_t target_units,
+                            int32_t n_head, int32_t vocab_size, int32_t n_ctas,
                             int32_t min_split_chunks, const int32_t* caps, int32_t* out,
                             int64_t out_capacity, int32_t* layout) {
   using tq::set_error;
@@ -61,9 +83,9 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   if (num_blocks < 1 || num_blocks * (int64_t)block_size > INT32_MAX)
     return set_error(TQ_ERR_UNSUPPORTED, "num_blocks * block_size must be in [1, 2^31), got %lld",
                      (long long)num_blocks * block_size);
-  if (n_head < 1) return set_error(TQ_ERR_INVALID, "n_head must be positive");
+  if (n_head < 1 || n_head > 0xffff) return set_error(TQ_ERR_INVALID, "n_head must be in [1, 65535]");
+  if (n_ctas < 1 || n_ctas > 0xffff) return set_error(TQ_ERR_INVALID, "n_ctas must be in [1, 65535]");
   if (min_split_chunks < 1) min_split_chunks = 1;
-  if (target_units < 1) target_units = 1;
 
   // ---- pass 1: validate, size everything -----------------------------------
   int64_t N = 0, max_nb = 0, max_ctx = 0, n_groups = 0, total_chunks = 0;
@@ -99,66 +121,141 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
                          vocab_size);
   }
 
-  // Split-K size: split only when the unsplit grid would have fewer
-  // (item, head) units than target_units.
-  int64_t split_chunks = INT32_MAX;
-  if (n_groups * n_head < target_units)
-    split_chunks = std::max<int64_t>(min_split_chunks, cdiv64(total_chunks * n_head, target_units));
-  // A work item stores its split index and count in 16 bits each.
-  split_chunks = std::max<int64_t>(split_chunks, cdiv64(cdiv64(max_ctx, kChunk), 0x7fff));
-  // The kernel keeps one item's block ids in two registers per lane, so an
-  // item spans at most kUnitBlocks blocks: (split_chunks * kChunk) keys can
-  // straddle one extra block boundary.
-  split_chunks = std::min<int64_t>(split_chunks, std::max<int64_t>(1, (int64_t)(kUnitBlocks - 1) * block_size / kChunk));
+  if (cdiv64(max_ctx, kChunk) > kMaxChunkIndex)
+    return set_error(TQ_ERR_UNSUPPORTED, "a context of %lld tokens exceeds %d chunks of %d keys",
+                     (long long)max_ctx, kMaxChunkIndex, kChunk);
 
-  int64_t n_items = 0, n_combine = 0, n_partials = 0;
-  auto count_items = [&]() {
-    n_items = n_combine = n_partials = 0;
+  // ---- attention work: (group, head) pairs -> pieces -> CTAs -> warps ----------
+  std::vector<Group> groups;
+  groups.reserve((size_t)n_groups);
+  {
+    int64_t row = 0;
     for (int b = 0; b < num_seqs; ++b) {
       for (int64_t g0 = 0; g0 < q_len[b]; g0 += kMaxRows) {
         const int64_t nrows = std::min<int64_t>(kMaxRows, q_len[b] - g0);
-        const int64_t nc = cdiv64(start[b] + g0 + nrows, kChunk);
-        const int64_t nsplit = cdiv64(nc, split_chunks);
-        n_items += nsplit;
-        if (nsplit > 1) {
-          n_combine += nrows;
-          n_partials += nrows * n_head * nsplit;
-        }
+        groups.push_back({b, (int32_t)(row + g0), (int32_t)nrows, (int32_t)(start[b] + g0),
+                          (int32_t)cdiv64(start[b] + g0 + nrows, kChunk)});
+      }
+      row += q_len[b];
+    }
+  }
+  // The kernel keeps one item's block ids in two registers per lane, so an
+  // item spans at most kUnitBlocks blocks: (chunks * kChunk) keys can
+  // straddle one extra block boundary.
+  const int64_t max_piece = std::max<int64_t>(1, (int64_t)(kUnitBlocks - 1) * block_size / kChunk);
+  const int64_t n_warps = (int64_t)n_ctas * kWarps;
+  // A CTA's fair share of chunks: a pair longer than that (and than twice
+  // the smallest cross-CTA piece) is split across CTAs.
+  const int64_t share = std::max<int64_t>(1, cdiv64(total_chunks * n_head, n_ctas));
+  int64_t split_min = min_split_chunks;
+
+  std::vector<Piece> pieces;
+  int64_t n_partials = 0, n_combine = 0, max_items = 0;
+  pieces.reserve((size_t)(n_groups * n_head));
+  auto make_pieces = [&]() {
+    pieces.clear();
+    n_partials = n_combine = 0;
+    for (size_t gi = 0; gi < groups.size(); ++gi) {
+      const Group& g = groups[gi];
+      int64_t gn = 1;
+      if (g.nc > share && g.nc >= 2 * split_min) gn = std::min(cdiv64(g.nc, share), g.nc / split_min);
+      gn = std::min<int64_t>(std::max(gn, cdiv64(g.nc, max_piece)), g.nc);
+      if (gn > 1) n_combine += g.nrows;
+      for (int h = 0; h < n_head; ++h) {
+        const int64_t gbase = gn > 1 ? n_partials : -1;
+        for (int64_t sp = 0; sp < gn; ++sp)
+          pieces.push_back({(int32_t)gi, h, (int32_t)(sp * g.nc / gn), (int32_t)((sp + 1) * g.nc / gn),
+                            (int32_t)sp, (int32_t)gn, gbase});
+        if (gn > 1) n_partials += (int64_t)g.nrows * gn;
       }
     }
+    // Each warp boundary cuts at most one piece in two.
+    max_items = (int64_t)pieces.size() + (int64_t)n_ctas * (kWarps - 1);
   };
-  count_items();
-  // With fixed capacities, coarsen the split until the items and partials fit.
-  while (caps && split_chunks < INT32_MAX && (n_items > caps[3] || n_partials > caps[5])) {
-    split_chunks = split_chunks >= (INT32_MAX / 2) ? INT32_MAX : split_chunks * 2;
-    count_items();
+  make_pieces();
+  // With fixed capacities, coarsen the cross-CTA split until items and partials fit.
+  while (caps && (max_items > caps[3] || n_partials > caps[5]) && split_min < kMaxChunkIndex) {
+    split_min *= 2;
+    make_pieces();
   }
-  if (n_partials > INT32_MAX || n_items > INT32_MAX / n_head)
+  if (n_partials > INT32_MAX || max_items > INT32_MAX / 8)
     return set_error(TQ_ERR_UNSUPPORTED, "step too large to plan");
+
+  // CTAs: longest piece first (a stable counting sort on length), each to the
+  // least loaded CTA.  Loads are whole chunks and only grow, so the least
+  // loaded CTA comes from a bucket queue (one intrusive list per load value,
+  // scanned upward from the lowest non-empty one): O(pieces + largest load).
+  // A CTA that receives a piece had at most the mean load, so no load exceeds
+  // the mean plus the longest piece.
+  int64_t longest_piece = 1, sum_len = 0;
+  for (const Piece& pc : pieces) {
+    longest_piece = std::max<int64_t>(longest_piece, pc.cend - pc.cbeg);
+    sum_len += pc.cend - pc.cbeg;
+  }
+  std::vector<int32_t> order(pieces.size());
+  {
+    std::vector<int32_t> start_of((size_t)longest_piece + 2, 0);
+    for (const Piece& pc : pieces) ++start_of[(size_t)(longest_piece - (pc.cend - pc.cbeg)) + 1];
+    for (size_t i = 1; i < start_of.size(); ++i) start_of[i] += start_of[i - 1];
+    for (size_t i = 0; i < pieces.size(); ++i)
+      order[start_of[(size_t)(longest_piece - (pieces[i].cend - pieces[i].cbeg))]++] = (int32_t)i;
+  }
+  std::vector<int64_t> cta_load((size_t)n_ctas, 0);
+  std::vector<int32_t> cta_count((size_t)n_ctas + 1, 0), cta_of(pieces.size());
+  {
+    const int64_t max_load = sum_len / n_ctas + longest_piece + 1;
+    std::vector<int32_t> head((size_t)max_load + 1, -1), next((size_t)n_ctas, -1);
+    for (int32_t c = n_ctas - 1; c >= 0; --c) {  // bucket 0 lists CTA 0 first
+      next[c] = head[0];
+      head[0] = c;
+    }
+    int64_t lo = 0;
+    for (int32_t i : order) {
+      while (head[(size_t)lo] < 0) ++lo;
+      const int32_t c = head[(size_t)lo];
+      head[(size_t)lo] = next[c];
+      cta_of[i] = c;
+      ++cta_count[(size_t)c + 1];
+      const int64_t l = cta_load[c] += pieces[i].cend - pieces[i].cbeg;
+      if (l > max_load)
+        return set_error(TQ_ERR_UNSUPPORTED, "internal: CTA load %lld above the bound %lld",
+                         (long long)l, (long long)max_load);
+      next[c] = head[(size_t)l];
+      head[(size_t)l] = c;
+    }
+  }
+  for (int32_t c = 0; c < n_ctas; ++c) cta_count[c + 1] += cta_count[c];
+  std::vector<int32_t> by_cta(pieces.size());  // pieces grouped by CTA, in assignment order
+  {
+    std::vector<int32_t> fill(cta_count.begin(), cta_count.end() - 1);
+    for (int32_t i : order) by_cta[fill[cta_of[i]]++] = i;
+  }
 
   const int64_t B = num_seqs;
   // Region sizes: this step's own, or the fixed capacities (caps) so that the
   // offsets -- and every pointer a captured CUDA graph holds -- stay put.
-  int64_t dim_B = B, dim_N = N, dim_nb = max_nb, dim_items = n_items, dim_comb = n_combine;
+  // Without caps the other-items region is sized for the most items the cuts
+  // can make (max_items); the step uses, and copies, only its used prefix.
+  int64_t dim_B = B, dim_N = N, dim_nb = max_nb, dim_rest = max_items, dim_comb = n_combine;
   if (caps) {
-    if (B > caps[0] || N > caps[1] || max_nb > caps[2] || n_items > caps[3] ||
+    if (B > caps[0] || N > caps[1] || max_nb > caps[2] || max_items > caps[3] ||
         n_combine > caps[4] || n_partials > caps[5])
       return set_error(TQ_ERR_CAPACITY,
                        "step (seqs %lld, tokens %lld, blocks/seq %lld, items %lld, combine %lld, "
                        "partials %lld) exceeds the fixed plan capacities (%d, %d, %d, %d, %d, %d)",
-                       (long long)B, (long long)N, (long long)max_nb, (long long)n_items,
+                       (long long)B, (long long)N, (long long)max_nb, (long long)max_items,
                        (long long)n_combine, (long long)n_partials, caps[0], caps[1], caps[2],
                        caps[3], caps[4], caps[5]);
     dim_B = caps[0];
     dim_N = caps[1];
     dim_nb = caps[2];
-    dim_items = caps[3];
+    dim_rest = caps[3];
     dim_comb = caps[4];
   }
   int64_t off = 0;
   auto take = [&](int64_t n) {
     const int64_t o = off;
-    off = align4(off + n);
+    off = align8(off + n);
     return o;
   };
   const int64_t o_counts = take(4);
@@ -168,11 +265,85 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   const int64_t o_pos = take(dim_N);
   const int64_t o_ids = take(dim_N);
   const int64_t o_last = take(dim_B);
-  const int64_t o_items = take(dim_items * 8);
   const int64_t o_comb = take(dim_comb * 4);
-  const int64_t total = off;
+  // The attention plan goes last, so a step copies only its used prefix.
+  const int64_t o_items = off;
+  const int64_t o_ranges = o_items + 8 * n_warps;
+  const int64_t o_rest = o_ranges + align8(n_warps + 1);
+  const int64_t total = o_rest + 8 * dim_rest;
   if (total > INT32_MAX) return set_error(TQ_ERR_UNSUPPORTED, "step too large to plan");
   max_nb = dim_nb;  // row stride of the packed tables
+  std::memset(layout, 0, sizeof(int32_t) * TQ_PLAN_LAYOUT_LEN);
+  layout[TQ_PLAN_TOTAL_INTS] = (int32_t)total;
+  if (out == nullptr || out_capacity < total)
+    return set_error(TQ_ERR_CAPACITY, "plan needs %lld int32, buffer holds %lld", (long long)total,
+                     (long long)out_capacity);
+
+  // ---- pass 2: write --------------------------------------------------------
+  // Attention items.  Each CTA's chunks, in assignment order, are cut into
+  // kWarps runs of equal length; a piece a cut falls in is shared by the
+  // warps on both sides and merged in the CTA's shared memory.  Items come out
+  // warp by warp: a warp's first item to its fixed place, the others to the
+  // list after the offsets.
+  int64_t rest = 0, n_items = 0, longest = 0;
+  int32_t* const first_items = out + o_items;
+  int32_t* const ranges = out + o_ranges;
+  int32_t* const rest_items = out + o_rest;
+  for (int32_t c = 0; c < n_ctas; ++c) {
+    const int64_t L = cta_load[c];
+    int64_t bnd[kWarps + 1];
+    for (int w = 0; w <= kWarps; ++w) bnd[w] = (int64_t)w * L / kWarps;
+    const int64_t wbase = (int64_t)c * kWarps;
+    bool has[kWarps] = {};  // warp has its first item
+    int cur = 0;            // warp of this CTA whose items are being written
+    ranges[wbase] = (int32_t)rest;
+    int32_t slot = 0;
+    int64_t x = 0;
+    int w0 = 0;  // the warp whose run holds chunk position x (x only grows)
+    for (int32_t k = cta_count[c]; k < cta_count[c + 1]; ++k) {
+      const Piece& pc = pieces[by_cta[k]];
+      const Group& g = groups[pc.group];
+      const int64_t len = pc.cend - pc.cbeg;
+      while (w0 + 1 < kWarps && bnd[w0 + 1] <= x) ++w0;
+      int w1 = w0;  // the warp whose run holds the piece's last chunk
+      while (w1 + 1 < kWarps && bnd[w1 + 1] <= x + len - 1) ++w1;
+      int lcount = 0;  // warps with a non-empty share of this piece (runs can be empty)
+      for (int w = w0; w <= w1; ++w) lcount += std::min(x + len, bnd[w + 1]) > std::max(x, bnd[w]);
+      if (lcount > 1 && slot + lcount * g.nrows > kLocalSlots)
+        return set_error(TQ_ERR_UNSUPPORTED, "internal: CTA %d needs more than %d merge slots", c,
+                         kLocalSlots);
+      const int32_t w2 = g.nrows | (pc.head << 8) |
+                         (((lcount > 1 ? kFlagLocal : 0) | (pc.gnsplit > 1 ? kFlagGlobal : 0)) << 24);
+      const int32_t w6 = pc.gnsplit > 1 ? (int32_t)pc.gbase : -1;
+      const int32_t w7 = pc.gsplit | (pc.gnsplit << 16);
+      int lsplit = 0;
+      for (int w = w0; w <= w1; ++w) {
+        const int64_t lo = std::max(x, bnd[w]) - x, hi = std::min(x + len, bnd[w + 1]) - x;
+        if (hi <= lo) continue;
+        while (cur < w) ranges[wbase + (++cur)] = (int32_t)rest;  // entering warp w
+        int32_t* const it = has[w] ? rest_items + 8 * rest++ : first_items + 8 * (wbase + w);
+        has[w] = true;
+        it[0] = g.seq;
+        it[1] = g.row0;
+        it[2] = w2;
+        it[3] = g.pos0;
+        it[4] = (int32_t)(pc.cbeg + lo) | ((int32_t)(pc.cbeg + hi) << 16);
+        it[5] = lcount > 1 ? (lsplit++ | (lcount << 8) | (slot << 16)) : 0;
+        it[6] = w6;
+        it[7] = w7;
+        ++n_items;
+        longest = std::max(longest, hi - lo);
+      }
+      if (lcount > 1) slot += lcount * g.nrows;
+      x += len;
+    }
+    while (cur < kWarps - 1) ranges[wbase + (++cur)] = (int32_t)rest;
+    for (int w = 0; w < kWarps; ++w)  // a warp without work: an all-zero first item
+      if (!has[w]) std::memset(first_items + 8 * (wbase + w), 0, 8 * sizeof(int32_t));
+  }
+  ranges[n_warps] = (int32_t)rest;
+  std::memset(ranges + n_warps + 1, 0, sizeof(int32_t) * (align8(n_warps + 1) - (n_warps + 1)));
+  const int64_t used = o_rest + 8 * rest;
 
   layout[TQ_PLAN_NUM_TOKENS] = (int32_t)N;
   layout[TQ_PLAN_NUM_SEQS] = (int32_t)B;
@@ -181,8 +352,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   layout[TQ_PLAN_NUM_PARTIALS] = (int32_t)n_partials;
   layout[TQ_PLAN_TABLE_STRIDE] = (int32_t)max_nb;
   layout[TQ_PLAN_MAX_CTX] = (int32_t)max_ctx;
-  layout[TQ_PLAN_SPLIT_CHUNKS] = (int32_t)std::min<int64_t>(split_chunks, INT32_MAX);
-  layout[TQ_PLAN_TOTAL_INTS] = (int32_t)total;
+  layout[TQ_PLAN_SPLIT_CHUNKS] = (int32_t)longest;
   layout[TQ_PLAN_OFF_COUNTS] = (int32_t)o_counts;
   layout[TQ_PLAN_OFF_SEQ_INFO] = (int32_t)o_seq;
   layout[TQ_PLAN_OFF_TABLES] = (int32_t)o_tab;
@@ -192,18 +362,16 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   layout[TQ_PLAN_OFF_LAST_ROWS] = (int32_t)o_last;
   layout[TQ_PLAN_OFF_ITEMS] = (int32_t)o_items;
   layout[TQ_PLAN_OFF_COMBINE] = (int32_t)o_comb;
-  if (out == nullptr || out_capacity < total)
-    return set_error(TQ_ERR_CAPACITY, "plan needs %lld int32, buffer holds %lld", (long long)total,
-                     (long long)out_capacity);
+  layout[TQ_PLAN_NUM_CTAS] = n_ctas;
+  layout[TQ_PLAN_USED_INTS] = (int32_t)used;
 
-  // ---- pass 2: write --------------------------------------------------------
-  std::memset(out, 0, sizeof(int32_t) * total);
-  std::vector<int32_t> items((size_t)n_items * 8);
+  // Everything before the attention plan: zeros first (padding, table tails).
+  std::memset(out, 0, sizeof(int32_t) * o_items);
   out[o_counts + 0] = (int32_t)N;
   out[o_counts + 1] = (int32_t)n_items;
   out[o_counts + 2] = (int32_t)n_combine;
   out[o_counts + 3] = (int32_t)B;
-  int64_t row = 0, item = 0, comb = 0, part = 0;
+  int64_t row = 0, comb = 0;
   for (int b = 0; b < num_seqs; ++b) {
     const int32_t* tbl = table_data + table_offsets[b];
     const int64_t s0 = start[b], n = q_len[b], ctx = s0 + n;
@@ -221,43 +389,18 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
       out[o_ids + row + t] = token_ids ? token_ids[row + t] : 0;
     }
     out[o_last + b] = (int32_t)(row + n - 1);
-    for (int64_t g0 = 0; g0 < n; g0 += kMaxRows) {
-      const int64_t nrows = std::min<int64_t>(kMaxRows, n - g0);
-      const int64_t nc = cdiv64(s0 + g0 + nrows, kChunk);
-      const int64_t nsplit = cdiv64(nc, split_chunks);
-      for (int64_t s = 0; s < nsplit; ++s) {
-        int32_t* it = items.data() + 8 * item++;
-        it[0] = b;
-        it[1] = (int32_t)(row + g0);
-        it[2] = (int32_t)nrows;
-        it[3] = (int32_t)(s0 + g0);
-        it[4] = (int32_t)(s * split_chunks);
-        it[5] = (int32_t)std::min(nc, (s + 1) * split_chunks);
-        it[6] = nsplit > 1 ? (int32_t)part : -1;
-        it[7] = (int32_t)(s | (nsplit << 16));
-      }
-      if (nsplit > 1) {
-        for (int64_t r = 0; r < nrows; ++r) {
-          int32_t* e = out + o_comb + 4 * comb++;
-          e[0] = (int32_t)(row + g0 + r);
-          e[1] = (int32_t)(part + r * n_head * nsplit);
-          e[2] = (int32_t)nsplit;
-          e[3] = 0;
-        }
-        part += nrows * n_head * nsplit;
-      }
-    }
     row += n;
   }
-  // Longest items first: the kernel hands unit u to warp u % (warps in the
-  // grid), so every warp then gets one item of each length class and all
-  // warps finish within about one item of each other.
-  std::vector<int32_t> order((size_t)n_items);
-  for (int64_t i = 0; i < n_items; ++i) order[i] = (int32_t)i;
-  std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) {
-    return items[8 * a + 5] - items[8 * a + 4] > items[8 * b + 5] - items[8 * b + 4];
-  });
-  for (int64_t i = 0; i < n_items; ++i)
-    std::memcpy(out + o_items + 8 * i, items.data() + 8 * (size_t)order[i], 8 * sizeof(int32_t));
+  for (const Piece& pc : pieces) {  // one combine entry per row whose keys are split across CTAs
+    if (pc.head != 0 || pc.gsplit != 0 || pc.gnsplit < 2) continue;
+    const Group& g = groups[pc.group];
+    for (int r = 0; r < g.nrows; ++r) {
+      int32_t* e = out + o_comb + 4 * comb++;
+      e[0] = g.row0 + r;
+      e[1] = (int32_t)(pc.gbase + (int64_t)r * pc.gnsplit);
+      e[2] = pc.gnsplit;
+      e[3] = 0;
+    }
+  }
   return TQ_OK;
 }

@@ -97,18 +97,22 @@ class DecodeGraphRunner:
             raise ValueError(f"{B} sequences exceed the largest graph bucket {self.max_batch}")
         graph, ws, logits, _, per_replay = self.graph(bucket)
         packed = PackedStep.from_sequences(seqs, [1] * B)
-        ws.stage(packed, torch.cuda.current_stream(self.allocator.pool.device), self.model.cfg.vocab_size)
-        self.model.last_h2d_bytes = ws.total * 4
+        layout = ws.stage(packed, torch.cuda.current_stream(self.allocator.pool.device), self.model.cfg.vocab_size)
+        self.model.last_h2d_bytes = int(layout[_lib.PLAN_USED_INTS]) * 4
         graph.replay()
         self.model.kernel_launches += per_replay
         return logits[:B].clone()
 
     def replay_plan(self, bucket: int, plan: torch.Tensor, ids: torch.Tensor | None = None) -> torch.Tensor:
         """Replay ``bucket``'s graph on a plan already in device memory (built
-        with that bucket's workspace capacities, ``PlanWorkspace.caps``),
+        with that bucket's workspace capacities and grid, ``PlanWorkspace.caps``
+        and ``.n_ctas``),
         optionally overwriting its token ids from a device tensor first.
         Returns the graph's greedy-token buffer (valid until the next replay)."""
         graph, ws, _, tokens, per_replay = self.graph(bucket)
+        if plan.numel() != ws.total:
+            raise ValueError(f"plan of {plan.numel()} int32 does not fit bucket {bucket}'s workspace "
+                             f"({ws.total}); plan it with that workspace's caps and n_ctas ({ws.n_ctas})")
         ws.plan.copy_(plan)
         if ids is not None:
             off = int(ws.layout[_lib.PLAN_OFF_TOKEN_IDS])
@@ -137,7 +141,8 @@ class _CaptureView(DevicePagedBatch):
         self.plan = ws.plan
         self.table_stride = int(L[_lib.PLAN_TABLE_STRIDE])
         self.rows_alloc, self.seqs_alloc = int(caps[1]), int(caps[0])
-        self.items_alloc, self.partials_alloc = int(caps[3]), int(caps[5])
+        self.partials_alloc = int(caps[5])
+        self.n_ctas = int(L[_lib.PLAN_NUM_CTAS])
         self.num_items = self.num_combine = self.num_partials = 0
         dev = ws.plan
 
@@ -151,7 +156,7 @@ class _CaptureView(DevicePagedBatch):
         self.row_positions = view(_lib.PLAN_OFF_POSITIONS, int(caps[1]))
         self.token_ids = view(_lib.PLAN_OFF_TOKEN_IDS, int(caps[1]))
         self.last_rows = view(_lib.PLAN_OFF_LAST_ROWS, int(caps[0]))
-        self.work_items = view(_lib.PLAN_OFF_ITEMS, 8 * int(caps[3]))
+        self.attn_plan = dev[int(L[_lib.PLAN_OFF_ITEMS]):]
         self.combine_list = view(_lib.PLAN_OFF_COMBINE, 4 * int(caps[4]))
         self._dev_ptr = dev.data_ptr()
         self._off = {k: int(L[k]) * 4 for k in range(_lib.PLAN_OFF_COUNTS, _lib.PLAN_LAYOUT_LEN)}

@@ -39,10 +39,11 @@ except ImportError:  # pragma: no cover - the Python packer below is used instea
 if TYPE_CHECKING:
     from tokquay_b200.model import GPT2Config
 
-# Split-K policy: aim for this many (item, head) units per SM, never cut a
-# split below this many chunks (measured best on B200 for BASELINE config 2).
-UNITS_PER_SM = 32
-MIN_SPLIT_CHUNKS = 4
+# Attention work is cut for one CTA per SM; keys of one (row group, head) pair
+# are split across CTAs only in pieces of at least this many 32-key chunks
+# (cuts between the warps of one CTA have no such floor: they merge in
+# shared memory).
+MIN_SPLIT_CHUNKS = 8
 
 
 def cdiv(a: int, b: int) -> int:
@@ -51,8 +52,13 @@ def cdiv(a: int, b: int) -> int:
 
 def attention_chunk_keys() -> int:
     """Keys per attention chunk of the loaded library build (the unit of
-    split-K sizes and of the kernel's shared-memory stages)."""
+    work-item sizes and of the kernel's shared-memory stages)."""
     return _lib.load().tq_attention_chunk_keys()
+
+
+def attention_warps() -> int:
+    """Computing warps per attention CTA of the loaded library build."""
+    return _lib.load().tq_attention_warps()
 
 
 class OutOfBlocksError(RuntimeError):
@@ -283,7 +289,7 @@ def plan_packed(
     n_head: int,
     packed: PackedStep,
     vocab_size: int = 0,
-    target_units: int = 2368,
+    n_ctas: int = 148,
     min_split_chunks: int = MIN_SPLIT_CHUNKS,
     out: torch.Tensor | np.ndarray | None = None,
     caps: np.ndarray | None = None,
@@ -314,7 +320,7 @@ def plan_packed(
 
     def call(buf_ptr, cap):
         return lib.tq_plan_step(B, _ptr(st), _ptr(ql), _ptr(offs), data_ptr, ids_ptr, block_size,
-                                num_blocks, n_head, vocab_size, target_units, min_split_chunks,
+                                num_blocks, n_head, vocab_size, n_ctas, min_split_chunks,
                                 caps_ptr, buf_ptr, cap, _ptr(layout))  # fmt: skip
 
     if out is not None:
@@ -342,14 +348,14 @@ def plan_step_host(
     new_lens: list[int],
     token_ids: list[int] | None = None,
     vocab_size: int = 0,
-    target_units: int = 2368,
+    n_ctas: int = 148,
     min_split_chunks: int = MIN_SPLIT_CHUNKS,
     out: torch.Tensor | np.ndarray | None = None,
     caps: np.ndarray | None = None,
 ) -> tuple[np.ndarray, np.ndarray]:
     """``plan_packed`` for Python lists (block tables, starts, lengths, ids)."""
     packed = PackedStep.from_lists(block_tables, start, new_lens, token_ids)
-    return plan_packed(block_size, num_blocks, n_head, packed, vocab_size, target_units, min_split_chunks,
+    return plan_packed(block_size, num_blocks, n_head, packed, vocab_size, n_ctas, min_split_chunks,
                        out, caps)  # fmt: skip
 
 
@@ -370,14 +376,21 @@ class PlanWorkspace:
         bs = allocator.block_size
         max_tokens = max_tokens or max_seqs
         max_ctx = max_ctx or cfg.n_positions
-        max_split = cdiv(cdiv(max_ctx, attention_chunk_keys()), MIN_SPLIT_CHUNKS)
+        chunks = cdiv(max_ctx, attention_chunk_keys())
+        # Cross-CTA pieces of a pair: at least MIN_SPLIT_CHUNKS long, or as many
+        # as the kernel's 64-block item span forces.
+        max_piece = max(1, 63 * bs // attention_chunk_keys())
+        max_split = max(1, chunks // MIN_SPLIT_CHUNKS, cdiv(chunks, max_piece))
         max_groups = max_tokens  # a query-row group holds at least one token
+        self.n_ctas = sm_count(allocator.pool.device)
         self.allocator = allocator
         self.max_seqs, self.max_tokens, self.max_ctx = max_seqs, max_tokens, max_ctx
-        self.caps = np.array([max_seqs, max_tokens, cdiv(max_ctx, bs), max_groups * max_split,
+        max_items = max_groups * cfg.n_head * max_split + self.n_ctas * (attention_warps() - 1)
+        self.caps = np.array([max_seqs, max_tokens, cdiv(max_ctx, bs), max_items,
                               max_tokens, max_tokens * cfg.n_head * max_split], dtype=np.int32)  # fmt: skip
         # The layout is fixed by the capacities: get it from a one-token plan.
-        _, layout = plan_step_host(bs, allocator.num_blocks, cfg.n_head, [[0]], [0], [1], caps=self.caps)
+        _, layout = plan_step_host(bs, allocator.num_blocks, cfg.n_head, [[0]], [0], [1], n_ctas=self.n_ctas,
+                                   caps=self.caps)  # fmt: skip
         self.layout = layout
         self.total = int(layout[_lib.PLAN_TOTAL_INTS])
         dev = allocator.pool.device
@@ -390,20 +403,19 @@ class PlanWorkspace:
         self._events: list[torch.cuda.Event | None] = [None, None]
         self._turn = 0
 
-    def stage(self, packed: PackedStep, stream: torch.cuda.Stream, vocab_size: int = 0,
-              target_units: int | None = None) -> np.ndarray:  # fmt: skip
-        """Plan ``packed`` into the next pinned buffer and copy it into the
-        device plan on ``stream``; returns the layout."""
+    def stage(self, packed: PackedStep, stream: torch.cuda.Stream, vocab_size: int = 0) -> np.ndarray:
+        """Plan ``packed`` into the next pinned buffer and copy the part of it
+        the step uses into the device plan on ``stream``; returns the layout."""
         a = self.allocator
-        if target_units is None:
-            target_units = UNITS_PER_SM * sm_count(a.pool.device)
         slot, host = self.pinned_buffer()
-        plan, layout = plan_packed(a.block_size, a.num_blocks, a.cfg.n_head, packed, vocab_size, target_units,
+        plan, layout = plan_packed(a.block_size, a.num_blocks, a.cfg.n_head, packed, vocab_size, self.n_ctas,
                                    MIN_SPLIT_CHUNKS, out=host, caps=self.caps)  # fmt: skip
         assert plan is host and int(layout[_lib.PLAN_TOTAL_INTS]) == self.total
+        used = int(layout[_lib.PLAN_USED_INTS])
         with torch.cuda.stream(stream):
-            self.plan.copy_(host, non_blocking=True)
+            self.plan[:used].copy_(host[:used], non_blocking=True)
         self.mark_copied(slot, stream)
+        self.last_used_ints = used
         return layout
 
     def pinned_buffer(self) -> tuple[int, torch.Tensor]:
@@ -436,6 +448,9 @@ class DevicePagedBatch(BatchedKV):
     graph is captured with), while the kernels read the step's true counts
     from the device plan.
 
+    ``n_ctas`` is the attention grid the plan is cut for (default: the
+    device's SM count; a workspace fixes its own).
+
     ``write`` / ``gather`` / ``positions`` / ``mask`` keep the reference's
     ``BatchedKV`` contract for callers written against it; the model in this
     package uses ``write_rows`` / ``attend_rows`` and never builds the dense
@@ -453,6 +468,7 @@ class DevicePagedBatch(BatchedKV):
         workspace: PlanWorkspace | None = None,
         graph_sizing: bool = False,
         packed: PackedStep | None = None,
+        n_ctas: int | None = None,
     ):
         pool = allocator.pool
         if pool.device.type != "cuda":
@@ -484,14 +500,13 @@ class DevicePagedBatch(BatchedKV):
 
         device = pool.device
         stream = stream or torch.cuda.current_stream(device)
-        target = UNITS_PER_SM * sm_count(device)
         vocab = cfg.vocab_size if packed.ids is not None else 0
         if workspace is None:
             ring = _ring(device)
             slot, host = ring.take(0)
-            plan, layout = plan_packed(bs, allocator.num_blocks, cfg.n_head, packed, vocab, target,
-                                       MIN_SPLIT_CHUNKS, out=host)  # fmt: skip
-            total = int(layout[_lib.PLAN_TOTAL_INTS])
+            plan, layout = plan_packed(bs, allocator.num_blocks, cfg.n_head, packed, vocab,
+                                       n_ctas or sm_count(device), MIN_SPLIT_CHUNKS, out=host)  # fmt: skip
+            total = int(layout[_lib.PLAN_USED_INTS])  # the step reads only this prefix
             if plan is not host:  # the plan did not fit: grow the pinned buffer and stage it there
                 slot, host = ring.take(total)
                 host[:total].copy_(torch.from_numpy(plan[:total]))
@@ -500,8 +515,10 @@ class DevicePagedBatch(BatchedKV):
                 dev.copy_(host[:total], non_blocking=True)
             ring.mark(slot, stream)
         else:
-            layout = workspace.stage(packed, stream, vocab, target)
-            total = workspace.total
+            if n_ctas is not None and n_ctas != workspace.n_ctas:
+                raise ValueError(f"a workspace plans for {workspace.n_ctas} CTAs, not {n_ctas}")
+            layout = workspace.stage(packed, stream, vocab)
+            total = int(layout[_lib.PLAN_USED_INTS])
             dev = workspace.plan
         self.layout = layout
         self.h2d_bytes = 4 * total  # the one host->device copy this step makes
@@ -512,14 +529,15 @@ class DevicePagedBatch(BatchedKV):
         self.num_partials = int(L[_lib.PLAN_NUM_PARTIALS])
         self.table_stride = int(L[_lib.PLAN_TABLE_STRIDE])
         self.split_chunks = int(L[_lib.PLAN_SPLIT_CHUNKS])
+        self.n_ctas = int(L[_lib.PLAN_NUM_CTAS])
         # What activations and launches are sized for.
         if graph_sizing:
             caps = workspace.caps
             self.rows_alloc, self.seqs_alloc = int(caps[1]), int(caps[0])
-            self.items_alloc, self.partials_alloc = int(caps[3]), int(caps[5])
+            self.partials_alloc = int(caps[5])
         else:
             self.rows_alloc, self.seqs_alloc = self.N, self.B
-            self.items_alloc, self.partials_alloc = self.num_items, self.num_partials
+            self.partials_alloc = self.num_partials
         dims = (workspace.caps if workspace is not None else
                 [self.B, self.N, self.table_stride, self.num_items, self.num_combine, self.num_partials])  # fmt: skip
 
@@ -534,7 +552,7 @@ class DevicePagedBatch(BatchedKV):
         self.row_positions = view(_lib.PLAN_OFF_POSITIONS, dims[1])
         self.token_ids = view(_lib.PLAN_OFF_TOKEN_IDS, dims[1]) if packed.ids is not None else None
         self.last_rows = view(_lib.PLAN_OFF_LAST_ROWS, self.B)
-        self.work_items = view(_lib.PLAN_OFF_ITEMS, 8 * dims[3])
+        self.attn_plan = dev[int(L[_lib.PLAN_OFF_ITEMS]):]  # the kernel finds its parts from n_ctas
         self.combine_list = view(_lib.PLAN_OFF_COMBINE, 4 * dims[4])
         self._dev_ptr = dev.data_ptr()
         self._off = {k: int(L[k]) * 4 for k in range(_lib.PLAN_OFF_COUNTS, _lib.PLAN_LAYOUT_LEN)}
@@ -569,7 +587,7 @@ class DevicePagedBatch(BatchedKV):
         0..position(n) of row n's sequence, read in place from the pool
         (replaces tokquay/kv_cache.py:234-242 + tokquay/model.py:94-96).
         ``q`` rows hold head h at columns ``h*d``; row stride is ``q.stride(0)``.
-        Long contexts are split over several warps and merged in the same launch."""
+        Keys cut between warps or CTAs are merged in the same launch."""
         lib = _lib.load()
         pm = self.partial_ml.data_ptr() if self.partial_ml is not None else None
         pa = self.partial_acc.data_ptr() if self.partial_acc is not None else None
@@ -577,8 +595,8 @@ class DevicePagedBatch(BatchedKV):
         _lib.check(lib.tq_paged_attention(
             out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), self.pool.data_ptr(),
             self.allocator.num_blocks, self.n_layer, self.n_head, self.block_size, self.d_head, layer,
-            self.block_tables_i32.data_ptr(), self.table_stride, self.work_items.data_ptr(),
-            self.count_ptr(1), self.items_alloc, pm, pa, pc, self.partials_alloc,
+            self.block_tables_i32.data_ptr(), self.table_stride, self.attn_plan.data_ptr(), self.n_ctas,
+            pm, pa, pc, self.partials_alloc,
             1.0 / math.sqrt(self.d_head), stream), "tq_paged_attention")  # fmt: skip
 
     # ---- reference BatchedKV contract (not used by this package's model) ---------------
