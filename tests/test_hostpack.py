@@ -53,3 +53,42 @@ def test_native_packer_rejects_what_the_planner_must_see():
         PackedStep.from_sequences([s], [5])  # more tokens than the sequence has
     with pytest.raises(ValueError):
         PackedStep.from_sequences([], None)
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_native_pack_and_plan_matches_the_python_path(seed):
+    """plan_sequences (pack in C, then tq_plan_step) writes the plan that
+    from_sequences + plan_packed writes, with and without fixed capacities."""
+    from tokquay_b200 import _lib
+    from tokquay_b200.kv_cache import MIN_SPLIT_CHUNKS, attention_warps, plan_packed
+
+    rng = random.Random(100 + seed)
+    seqs = random_seqs(rng, rng.randint(1, 30))
+    for s in seqs:  # a valid step: tables cover every sequence, block ids in the pool
+        s.block_table = [rng.randrange(4000) for _ in range(-(-s.num_tokens // 16))]
+    new_lens = [rng.randint(1, s.num_uncached_tokens) for s in seqs]
+    n_ctas = rng.choice([1, 7, 148])
+    caps = np.array([64, 4096, 64, 64 * 12 * 16 + n_ctas * attention_warps(), 64, 4096 * 12 * 8], np.int32)
+    for cp in (None, caps):
+        want, wl = plan_packed(16, 4000, 12, PackedStep.from_sequences(seqs, new_lens), 50257, n_ctas,
+                               MIN_SPLIT_CHUNKS, caps=cp)  # fmt: skip
+        out = np.full(int(wl[_lib.PLAN_TOTAL_INTS]), -7, np.int32)
+        layout = np.zeros(_lib.PLAN_LAYOUT_LEN, np.int32)
+        st = hostpack.plan_sequences(_lib.function_address("tq_plan_step"), seqs, new_lens, 16, 4000, 12, 50257,
+                                     n_ctas, MIN_SPLIT_CHUNKS, 0 if cp is None else cp.ctypes.data, out.ctypes.data,
+                                     out.size, layout.ctypes.data)  # fmt: skip
+        assert st == 0
+        np.testing.assert_array_equal(layout, wl)
+        used = int(wl[_lib.PLAN_USED_INTS])
+        np.testing.assert_array_equal(out[:used], want[:used])
+    # a batch the planner rejects comes back as its status, the message in tq_last_error
+    short = Sequence(99, [1, 2, 3, 4, 5])
+    short.block_table = [0]
+    st = hostpack.plan_sequences(_lib.function_address("tq_plan_step"), [short], None, 4, 4000, 12, 50257, 1, 8, 0,
+                                 out.ctypes.data, out.size, layout.ctypes.data)  # fmt: skip
+    assert st == _lib.TQ_ERR_INVALID and "cannot hold 5 tokens" in _lib.last_error()
+    # one the packer rejects raises before the planner runs
+    bad = seqs[0]
+    with pytest.raises(ValueError):
+        hostpack.plan_sequences(_lib.function_address("tq_plan_step"), [bad], [bad.num_uncached_tokens + 5], 16,
+                                4000, 12, 50257, 1, 8, 0, out.ctypes.data, out.size, layout.ctypes.data)  # fmt: skip

@@ -113,6 +113,11 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         return lib
 
 
+def function_address(name: str) -> int:
+    """Address of an exported entry point (for native callers such as _hostpack)."""
+    return ctypes.cast(getattr(load(), name), c_void_p).value
+
+
 def last_error() -> str:
     msg = load().tq_last_error()
     return msg.decode(errors="replace") if msg else ""

@@ -56,9 +56,9 @@ struct Group {  // one query-row group of a sequence
   int32_t seq, row0, nrows, pos0, nc;  // nc: 32-key chunks it attends to
 };
 
-struct Piece {  // a run of chunks of one (group, head) pair, bound for one CTA
-  int32_t group, head, cbeg, cend, gsplit, gnsplit;
-  int64_t gbase;  // split-K partial of (row 0, split 0), or -1
+struct Piece {  // a run of chunks of a group's pairs (one per head), each bound for one CTA
+  int32_t group, cbeg, cend, gsplit, gnsplit;
+  int64_t gbase;  // split-K partial of (head 0, row 0, split 0), or -1; head h adds h * nrows * gnsplit
 };
 
 }  // namespace
@@ -149,9 +149,12 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   const int64_t share = std::max<int64_t>(1, cdiv64(total_chunks * n_head, n_ctas));
   int64_t split_min = min_split_chunks;
 
+  // Pieces: a group's keys, cut across CTAs when longer than a CTA's share.
+  // All heads of a group are alike, so a piece stands for its n_head (group,
+  // head) pairs: pair p of the step is piece p / n_head, head p % n_head.
   std::vector<Piece> pieces;
-  int64_t n_partials = 0, n_combine = 0, max_items = 0;
-  pieces.reserve((size_t)(n_groups * n_head));
+  int64_t n_partials = 0, n_combine = 0, max_items = 0, n_pairs = 0;
+  pieces.reserve((size_t)n_groups);
   auto make_pieces = [&]() {
     pieces.clear();
     n_partials = n_combine = 0;
@@ -160,17 +163,18 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
       int64_t gn = 1;
       if (g.nc > share && g.nc >= 2 * split_min) gn = std::min(cdiv64(g.nc, share), g.nc / split_min);
       gn = std::min<int64_t>(std::max(gn, cdiv64(g.nc, max_piece)), g.nc);
-      if (gn > 1) n_combine += g.nrows;
-      for (int h = 0; h < n_head; ++h) {
-        const int64_t gbase = gn > 1 ? n_partials : -1;
-        for (int64_t sp = 0; sp < gn; ++sp)
-          pieces.push_back({(int32_t)gi, h, (int32_t)(sp * g.nc / gn), (int32_t)((sp + 1) * g.nc / gn),
-                            (int32_t)sp, (int32_t)gn, gbase});
-        if (gn > 1) n_partials += (int64_t)g.nrows * gn;
+      const int64_t gbase = gn > 1 ? n_partials : -1;
+      for (int64_t sp = 0; sp < gn; ++sp)
+        pieces.push_back({(int32_t)gi, (int32_t)(sp * g.nc / gn), (int32_t)((sp + 1) * g.nc / gn), (int32_t)sp,
+                          (int32_t)gn, gbase});
+      if (gn > 1) {
+        n_combine += g.nrows;
+        n_partials += (int64_t)n_head * g.nrows * gn;
       }
     }
-    // Each warp boundary cuts at most one piece in two.
-    max_items = (int64_t)pieces.size() + (int64_t)n_ctas * (kWarps - 1);
+    n_pairs = (int64_t)pieces.size() * n_head;
+    // Each warp boundary cuts at most one pair in two.
+    max_items = n_pairs + (int64_t)n_ctas * (kWarps - 1);
   };
   make_pieces();
   // With fixed capacities, coarsen the cross-CTA split until items and partials fit.
@@ -181,16 +185,16 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   if (n_partials > INT32_MAX || max_items > INT32_MAX / 8)
     return set_error(TQ_ERR_UNSUPPORTED, "step too large to plan");
 
-  // CTAs: longest piece first (a stable counting sort on length), each to the
-  // least loaded CTA.  Loads are whole chunks and only grow, so the least
-  // loaded CTA comes from a bucket queue (one intrusive list per load value,
-  // scanned upward from the lowest non-empty one): O(pieces + largest load).
-  // A CTA that receives a piece had at most the mean load, so no load exceeds
-  // the mean plus the longest piece.
+  // CTAs: longest pair first (a stable counting sort of the pieces on
+  // length), each to the least loaded CTA.  Loads are whole chunks and only
+  // grow, so the least loaded CTA comes from a bucket queue (one intrusive
+  // list per load value, scanned upward from the lowest non-empty one):
+  // O(pairs + largest load).  A CTA that receives a pair had at most the mean
+  // load, so no load exceeds the mean plus the longest pair.
   int64_t longest_piece = 1, sum_len = 0;
   for (const Piece& pc : pieces) {
     longest_piece = std::max<int64_t>(longest_piece, pc.cend - pc.cbeg);
-    sum_len += pc.cend - pc.cbeg;
+    sum_len += (int64_t)(pc.cend - pc.cbeg) * n_head;
   }
   std::vector<int32_t> order(pieces.size());
   {
@@ -201,7 +205,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
       order[start_of[(size_t)(longest_piece - (pieces[i].cend - pieces[i].cbeg))]++] = (int32_t)i;
   }
   std::vector<int64_t> cta_load((size_t)n_ctas, 0);
-  std::vector<int32_t> cta_count((size_t)n_ctas + 1, 0), cta_of(pieces.size());
+  std::vector<int32_t> cta_count((size_t)n_ctas + 1, 0), cta_of((size_t)n_pairs);
   {
     const int64_t max_load = sum_len / n_ctas + longest_piece + 1;
     std::vector<int32_t> head((size_t)max_load + 1, -1), next((size_t)n_ctas, -1);
@@ -211,24 +215,31 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     }
     int64_t lo = 0;
     for (int32_t i : order) {
-      while (head[(size_t)lo] < 0) ++lo;
-      const int32_t c = head[(size_t)lo];
-      head[(size_t)lo] = next[c];
-      cta_of[i] = c;
-      ++cta_count[(size_t)c + 1];
-      const int64_t l = cta_load[c] += pieces[i].cend - pieces[i].cbeg;
-      if (l > max_load)
-        return set_error(TQ_ERR_UNSUPPORTED, "internal: CTA load %lld above the bound %lld",
-                         (long long)l, (long long)max_load);
-      next[c] = head[(size_t)l];
-      head[(size_t)l] = c;
+      const int64_t len = pieces[i].cend - pieces[i].cbeg;
+      for (int h = 0; h < n_head; ++h) {
+        while (head[(size_t)lo] < 0) ++lo;
+        const int32_t c = head[(size_t)lo];
+        head[(size_t)lo] = next[c];
+        cta_of[(size_t)i * n_head + h] = c;
+        ++cta_count[(size_t)c + 1];
+        const int64_t l = cta_load[c] += len;
+        if (l > max_load)
+          return set_error(TQ_ERR_UNSUPPORTED, "internal: CTA load %lld above the bound %lld",
+                           (long long)l, (long long)max_load);
+        next[c] = head[(size_t)l];
+        head[(size_t)l] = c;
+      }
     }
   }
   for (int32_t c = 0; c < n_ctas; ++c) cta_count[c + 1] += cta_count[c];
-  std::vector<int32_t> by_cta(pieces.size());  // pieces grouped by CTA, in assignment order
+  std::vector<int32_t> by_cta((size_t)n_pairs);  // pairs grouped by CTA, in assignment order
   {
     std::vector<int32_t> fill(cta_count.begin(), cta_count.end() - 1);
-    for (int32_t i : order) by_cta[fill[cta_of[i]]++] = i;
+    for (int32_t i : order)
+      for (int h = 0; h < n_head; ++h) {
+        const int32_t pr = i * n_head + h;
+        by_cta[fill[cta_of[pr]]++] = pr;
+      }
   }
 
   const int64_t B = num_seqs;
@@ -301,7 +312,9 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     int64_t x = 0;
     int w0 = 0;  // the warp whose run holds chunk position x (x only grows)
     for (int32_t k = cta_count[c]; k < cta_count[c + 1]; ++k) {
-      const Piece& pc = pieces[by_cta[k]];
+      const int32_t pair = by_cta[k];
+      const Piece& pc = pieces[pair / n_head];
+      const int head = pair - (pair / n_head) * n_head;
       const Group& g = groups[pc.group];
       const int64_t len = pc.cend - pc.cbeg;
       while (w0 + 1 < kWarps && bnd[w0 + 1] <= x) ++w0;
@@ -312,9 +325,10 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
       if (lcount > 1 && slot + lcount * g.nrows > kLocalSlots)
         return set_error(TQ_ERR_UNSUPPORTED, "internal: CTA %d needs more than %d merge slots", c,
                          kLocalSlots);
-      const int32_t w2 = g.nrows | (pc.head << 8) |
+      const int32_t w2 = g.nrows | (head << 8) |
                          (((lcount > 1 ? kFlagLocal : 0) | (pc.gnsplit > 1 ? kFlagGlobal : 0)) << 24);
-      const int32_t w6 = pc.gnsplit > 1 ? (int32_t)pc.gbase : -1;
+      const int32_t w6 =
+          pc.gnsplit > 1 ? (int32_t)(pc.gbase + (int64_t)head * g.nrows * pc.gnsplit) : -1;
       const int32_t w7 = pc.gsplit | (pc.gnsplit << 16);
       int lsplit = 0;
       for (int w = w0; w <= w1; ++w) {
@@ -392,7 +406,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     row += n;
   }
   for (const Piece& pc : pieces) {  // one combine entry per row whose keys are split across CTAs
-    if (pc.head != 0 || pc.gsplit != 0 || pc.gnsplit < 2) continue;
+    if (pc.gsplit != 0 || pc.gnsplit < 2) continue;
     const Group& g = groups[pc.group];
     for (int r = 0; r < g.nrows; ++r) {
       int32_t* e = out + o_comb + 4 * comb++;

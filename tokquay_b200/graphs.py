@@ -21,7 +21,7 @@ import bisect
 import torch
 
 from tokquay_b200 import _lib
-from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, PackedStep, PlanWorkspace
+from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, PlanWorkspace
 from tokquay_b200.sequence import Sequence
 
 DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256, 512)
@@ -96,9 +96,9 @@ class DecodeGraphRunner:
         if bucket is None:
             raise ValueError(f"{B} sequences exceed the largest graph bucket {self.max_batch}")
         graph, ws, logits, _, per_replay = self.graph(bucket)
-        packed = PackedStep.from_sequences(seqs, [1] * B)
-        layout = ws.stage(packed, torch.cuda.current_stream(self.allocator.pool.device), self.model.cfg.vocab_size)
-        self.model.last_h2d_bytes = int(layout[_lib.PLAN_USED_INTS]) * 4
+        ws.stage_sequences(seqs, [1] * B, torch.cuda.current_stream(self.allocator.pool.device),
+                           self.model.cfg.vocab_size)
+        self.model.last_h2d_bytes = ws.last_used_ints * 4
         graph.replay()
         self.model.kernel_launches += per_replay
         return logits[:B].clone()

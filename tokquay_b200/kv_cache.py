@@ -402,6 +402,9 @@ class PlanWorkspace:
         self._pinned = [torch.empty(self.total, dtype=torch.int32, pin_memory=True) for _ in range(2)]
         self._events: list[torch.cuda.Event | None] = [None, None]
         self._turn = 0
+        self._layout = np.zeros(_lib.PLAN_LAYOUT_LEN, dtype=np.int32)
+        self._native = _hostpack is not None and hasattr(_hostpack, "plan_sequences")
+        self._plan_fn = _lib.function_address("tq_plan_step") if self._native else 0
 
     def stage(self, packed: PackedStep, stream: torch.cuda.Stream, vocab_size: int = 0) -> np.ndarray:
         """Plan ``packed`` into the next pinned buffer and copy the part of it
@@ -417,6 +420,28 @@ class PlanWorkspace:
         self.mark_copied(slot, stream)
         self.last_used_ints = used
         return layout
+
+    def stage_sequences(self, seqs, new_lens: list[int] | None, stream: torch.cuda.Stream,
+                        vocab_size: int = 0) -> np.ndarray:  # fmt: skip
+        """``stage`` straight from ``Sequence`` objects: the native packer
+        hands its arrays to the planner, so planning a step makes no Python
+        objects.  Same plan, same errors as ``stage(PackedStep.from_sequences(...))``."""
+        if not self._native:
+            return self.stage(PackedStep.from_sequences(seqs, new_lens), stream, vocab_size)
+        if not seqs:
+            raise ValueError("block_tables, start and new_lens must be non-empty and the same length")
+        a = self.allocator
+        slot, host = self.pinned_buffer()
+        status = _hostpack.plan_sequences(
+            self._plan_fn, seqs, new_lens, a.block_size, a.num_blocks, a.cfg.n_head, vocab_size, self.n_ctas,
+            MIN_SPLIT_CHUNKS, self.caps.ctypes.data, host.data_ptr(), self.total, self._layout.ctypes.data)
+        _lib.check(status, "tq_plan_step")
+        used = int(self._layout[_lib.PLAN_USED_INTS])
+        with torch.cuda.stream(stream):
+            self.plan[:used].copy_(host[:used], non_blocking=True)
+        self.mark_copied(slot, stream)
+        self.last_used_ints = used
+        return self._layout.copy()
 
     def pinned_buffer(self) -> tuple[int, torch.Tensor]:
         """The next pinned staging buffer, once the copy that last read it is done."""
