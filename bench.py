@@ -69,8 +69,9 @@ def log(*a):
 # ------------------------------------------------------------------------------ distributed
 # One replica per GPU (tokquay_b200.replicas): no collective on the data path,
 # host reductions only for the barrier and the max-over-ranks timing.
-from tokquay_b200.replicas import ReplicaInfo, barrier, max_over_ranks, replica_seed, sum_over_ranks  # noqa: E402
+from tokquay_b200 import _lib  # noqa: E402
 from tokquay_b200 import replicas as _replicas  # noqa: E402
+from tokquay_b200.replicas import ReplicaInfo, barrier, max_over_ranks, replica_seed, sum_over_ranks  # noqa: E402
 
 
 # ------------------------------------------------------------------------------ clocks
@@ -176,13 +177,21 @@ def kernel_table(model, a, seqs, spec, steps: int = 10) -> str:
             step()
         torch.cuda.synchronize()
     agg = collections.defaultdict(lambda: [0, 0.0])
+    spans = []
     for e in prof.events():
         if e.device_type == torch.autograd.DeviceType.CUDA:
             k = e.name.split("(")[0][:90]
             agg[k][0] += 1
             agg[k][1] += getattr(e, "device_time", None) or e.cuda_time
+            spans.append((e.time_range.start, e.time_range.end))
     tot = sum(v[1] for v in agg.values())
-    lines = [f"device time per step: {tot / steps:.1f} us", "| kernel | us/step | share | launches/step | avg us |",
+    # Idle device time between consecutive operations of one step (gaps under
+    # 20 us; longer ones are the host's turn between steps).
+    spans.sort()
+    gaps = [b[0] - a[1] for a, b in zip(spans, spans[1:])]
+    idle = sum(g for g in gaps if 0 < g < 20)
+    lines = [f"device time per step: {tot / steps:.1f} us; idle between operations inside a step: "
+             f"{idle / steps:.1f} us", "| kernel | us/step | share | launches/step | avg us |",
              "|---|---|---|---|---|"]  # fmt: skip
     for k, (n, t) in sorted(agg.items(), key=lambda x: -x[1][1])[:20]:
         lines.append(f"| {k} | {t / steps:.1f} | {100 * t / tot:.1f}% | {n / steps:.1f} | {t / n:.2f} |")
@@ -259,6 +268,44 @@ def attn_bytes(ctx_list, n_head, d, num_partials):
     return kv + qo + part
 
 
+# ------------------------------------------------------------------------------ attention timing
+def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> list[float]:
+    """Per-launch attention times (ms) over the same steps, eager."""
+    from tokquay_b200.kv_cache import DevicePagedBatch
+
+    case = make_case(spec, a, seed)
+    seqs = case.seqs
+    B = len(seqs)
+    pairs: list = []
+
+    def timer(layer: int, start: bool) -> None:
+        if start:
+            torch.cuda._sleep(200_000)  # ~0.1 ms of device work: the host gets ahead
+            pairs.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+        pairs[-1][0 if start else 1].record()
+
+    try:
+        for k in range(total_steps):
+            starts = [s.num_cached_tokens for s in seqs]
+            ids = [s.tokens_slice(st, st + 1)[0] for s, st in zip(seqs, starts)]
+            b = DevicePagedBatch(a, [list(s.block_table) for s in seqs], starts, [1] * B, ids)
+            if k == warmup:
+                torch.cuda.synchronize()
+                pairs.clear()
+            model.attention_timer = timer
+            model.forward_paged(b, last_only=True)
+            model.attention_timer = None
+            if spec["grow"]:
+                for s in seqs:
+                    s.num_cached_tokens += 1
+                    s.append_token(0)
+                    a.append_slot(s)
+        torch.cuda.synchronize()
+    finally:
+        model.attention_timer = None
+    return [e0.elapsed_time(e1) for e0, e1 in pairs]
+
+
 # ------------------------------------------------------------------------------ our arm
 def run_ours(args, world, rank, local):
     from tokquay_b200 import kv_cache as KV
@@ -282,7 +329,7 @@ def run_ours(args, world, rank, local):
     # ---- plan every step first (bookkeeping only; the plans go to HBM) ------------
     case = make_case(spec, a, seed)
     seqs = case.seqs
-    plans, batches, ctx_per_step = [], [], []
+    plans, batches, ctx_per_step, nparts_per_step = [], [], [], []
     if runner:
         caps = runner.graph(bucket)[1].caps  # captures the bucket's graph
     for k in range(total_steps):
@@ -290,12 +337,14 @@ def run_ours(args, world, rank, local):
         ids = [s.tokens_slice(st, st + 1)[0] for s, st in zip(seqs, starts)]
         tables = [list(s.block_table) for s in seqs]
         if runner:
-            plan, _ = plan_step_host(a.block_size, a.num_blocks, cfg.n_head, tables, starts, [1] * B, ids,
-                                     cfg.vocab_size, KV.sm_count(device), KV.MIN_SPLIT_CHUNKS,
-                                     caps=caps)  # fmt: skip
+            plan, lay = plan_step_host(a.block_size, a.num_blocks, cfg.n_head, tables, starts, [1] * B, ids,
+                                       cfg.vocab_size, KV.sm_count(device), KV.MIN_SPLIT_CHUNKS,
+                                       caps=caps)  # fmt: skip
             plans.append(torch.from_numpy(plan).to(device))
+            nparts_per_step.append(int(lay[_lib.PLAN_NUM_PARTIALS]))
         else:
             batches.append(DevicePagedBatch(a, tables, starts, [1] * B, ids))
+            nparts_per_step.append(batches[-1].num_partials)
         ctx_per_step.append([st + 1 for st in starts])
         if spec["grow"]:
             for s in seqs:
@@ -336,35 +385,15 @@ def run_ours(args, world, rank, local):
     ms_max = max_over_ranks(ms, world)
     tokens_all = sum_over_ranks(tokens, world)
 
-    # ---- attention kernel timing: the same steps, eager, events around each launch ---
-    # (CUDA events cannot be recorded inside the captured graph.)  A short device
-    # sleep before each bracketed launch keeps host launch latency out of the interval.
-    case = make_case(spec, a, seed)
-    seqs = case.seqs
-    model.attention_events = []
-    model.attention_event_prelude = lambda: torch.cuda._sleep(200_000)  # ~0.1 ms of device work
-    bytes_per_launch = []
-    try:
-        for k in range(total_steps):
-            starts = [s.num_cached_tokens for s in seqs]
-            ids = [s.tokens_slice(st, st + 1)[0] for s, st in zip(seqs, starts)]
-            b = DevicePagedBatch(a, [list(s.block_table) for s in seqs], starts, [1] * B, ids)
-            if k == Wm:
-                torch.cuda.synchronize(device)
-                model.attention_events = []
-            model.forward_paged(b, last_only=True)
-            if k >= Wm:
-                bytes_per_launch += [attn_bytes(ctx_per_step[k], cfg.n_head, cfg.d_head, b.num_partials)] * cfg.n_layer
-            if spec["grow"]:
-                for s in seqs:
-                    s.num_cached_tokens += 1
-                    s.append_token(0)
-                    a.append_slot(s)
-        torch.cuda.synchronize(device)
-    finally:
-        model.attention_event_prelude = None
-    attn_ms = [e0.elapsed_time(e1) for e0, e1 in model.attention_events]
-    model.attention_events = None
+    # ---- attention kernel timing: CUDA events around every attention launch ----------
+    # The same steps eager (events cannot bracket a node of the timed graph
+    # without changing it), a short device sleep before each bracketed launch
+    # keeping host launch latency out of the interval.
+    bytes_per_launch = [attn_bytes(ctx_per_step[k], cfg.n_head, cfg.d_head, nparts_per_step[k])
+                        for k in range(Wm, total_steps) for _ in range(cfg.n_layer)]  # fmt: skip
+    attn_ms, attn_timing = eager_attention_times(model, a, spec, seed, Wm, total_steps), (
+        "CUDA events around each attention launch in an eager pass over the same steps, a device sleep "
+        "before each so host launch latency is not counted (the GPU's own launch and CTA start-up are)")
     del plans, batches
 
     # ---- end to end through the public API -----------------------------------------
@@ -454,8 +483,7 @@ def run_ours(args, world, rank, local):
                 "algorithmic_bytes_per_launch": avg_bytes,
                 "avg_launch_ms": avg_attn_ms,
                 "launches_timed": len(attn_ms),
-                "timing": "CUDA events around each attention launch on its stream, in an eager pass "
-                          "over the same steps (events cannot sit inside the captured graph)",
+                "timing": attn_timing,
                 "attention_ms_per_step": avg_attn_ms * cfg.n_layer,
             },  # fmt: skip
             "e2e": {

@@ -15,6 +15,9 @@
  * Reference interfaces replaced (paths inside the Tokquay project):
  *   tq_plan_step               PagedBatch.__init__           tokquay/kv_cache.py:174-226
  *   tq_kv_write                PagedBatch.write              tokquay/kv_cache.py:228-232
+ *   tq_qkv_bias_kv_write       c_attn bias + PagedBatch.write
+ *                                                            tokquay/model.py:69,
+ *                                                            tokquay/kv_cache.py:228-232
  *   tq_paged_attention         PagedBatch.gather + scores/mask/softmax/@v
  *                                                            tokquay/kv_cache.py:234-242,
  *                                                            tokquay/model.py:94-96
@@ -22,6 +25,8 @@
  *                                                            tokquay/model.py:163,172,122
  *   tq_bias_residual_layernorm x + (y + b), then the next LayerNorm
  *                                                            tokquay/model.py:99,122-123
+ *   tq_argmax_rows             logits.argmax(-1) of greedy sampling
+ *                                                            tokquay/engine.py:189-194
  *   tq_layernorm_rows          x[arange(B), last_idx] then ln_f
  *                                                            tokquay/model.py:179-180
  *   tq_bias_gelu               F.gelu(c_fc(x), approximate="tanh"), and the
@@ -147,6 +152,20 @@ TQ_API int tq_kv_write(float* pool, int64_t num_blocks, int32_t n_layer, int32_t
                 const int32_t* slot_mapping, const int32_t* d_num_tokens, int32_t max_tokens,
                 void* stream);
 
+/* The c_attn epilogue fused with the KV write (replaces the c_attn bias,
+ * tokquay/model.py:69, and PagedBatch.write, tokquay/kv_cache.py:228-232).
+ * For each of the *d_num_rows new tokens r, with
+ *   row = parts_0[r] + ... + parts_{n_parts-1}[r] + bias   (3 * n_head * head_dim floats,
+ *   parts_s = parts + s * part_stride, rows of 3C floats: the split-K partial sums of c_attn):
+ * q_out[r * q_row_stride + i] = row[i] for i < C; the K and V parts of row go
+ * straight to pool[slot/bs][layer][0 / 1][h][slot%bs][:] (slot = slot_mapping[r]).
+ * n_head <= 21 (one thread per 4 columns).  max_rows sizes the grid. */
+TQ_API int tq_qkv_bias_kv_write(float* q_out, int64_t q_row_stride, const float* parts, int32_t n_parts,
+                                int64_t part_stride, const float* bias, float* pool, int64_t num_blocks,
+                                int32_t n_layer, int32_t n_head, int32_t block_size, int32_t head_dim,
+                                int32_t layer, const int32_t* slot_mapping, const int32_t* d_num_rows,
+                                int32_t max_rows, void* stream);
+
 /* Paged attention, decode and causal prefill rows mixed in one launch
  * (replaces PagedBatch.gather + the masked softmax attention,
  * tokquay/kv_cache.py:234-242, tokquay/model.py:94-96).
@@ -212,6 +231,13 @@ TQ_API int tq_bias_residual_layernorm(float* x, float* xa, const float* y, int32
                                int64_t part_stride, const float* bias, const float* ln_w,
                                const float* ln_b, float eps, int32_t n_embd,
                                const int32_t* d_num_rows, int32_t max_rows, void* stream);
+
+/* Greedy sampling (the greedy rows of Engine._sample, tokquay/engine.py:189-194):
+ * out[r] = argmax over c < n_cols of x[r * row_stride + c] for each of the
+ * *d_num_rows rows, as torch.argmax(-1) picks it: NaN counts as the largest
+ * value, the first of equal values wins.  max_rows sizes the grid. */
+TQ_API int tq_argmax_rows(const float* x, int64_t row_stride, int32_t n_cols, int64_t* out,
+                          const int32_t* d_num_rows, int32_t max_rows, void* stream);
 
 /* out[i] = LayerNorm(x[rows[i]]) (rows == NULL: x[i]). */
 TQ_API int tq_layernorm_rows(float* out, const float* x, const int32_t* rows, const float* ln_w,

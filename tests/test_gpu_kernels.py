@@ -202,6 +202,47 @@ def test_kv_write_is_bit_exact(bs):
     assert torch.equal(alloc.pool, want)
 
 
+@pytest.mark.parametrize("n_parts", [1, 3, 4])
+@pytest.mark.parametrize("bs", [4, 16, 32])
+def test_qkv_bias_kv_write_matches_the_unfused_path(n_parts, bs):
+    """c_attn epilogue fused with the KV write == bias_gelu (no GELU) + kv_write,
+    bit for bit: same q rows, same pool, nothing else in the pool touched."""
+    lib = _lib.load()
+    cfg = GPT2Config(vocab_size=64, n_positions=1024, n_embd=768, n_layer=3, n_head=12)
+    rng = random.Random(bs * 10 + n_parts)
+    alloc = BlockAllocator(cfg, 120, bs, device="cuda")
+    random.Random(5).shuffle(alloc._free)
+    alloc.pool.normal_()
+    tables, start, new = [], [], []
+    for _ in range(7):
+        s, n = rng.randint(0, 200), rng.choice([1, 1, 9])
+        if cdiv(s + n, bs) > alloc.num_free_blocks:
+            break
+        tables.append(alloc._take(cdiv(s + n, bs)))
+        start.append(s)
+        new.append(n)
+    batch = DevicePagedBatch(alloc, tables, start, new)
+    N, C = batch.N, 768
+    g = torch.Generator(device="cuda").manual_seed(bs)
+    parts = torch.randn(n_parts, N, 3 * C, device="cuda", generator=g)
+    bias = torch.randn(3 * C, device="cuda", generator=g)
+    st = _stream()
+    # unfused: sum + bias into qkv, then scatter K/V
+    pool0 = alloc.pool.clone()
+    qkv = torch.empty(N, 3 * C, device="cuda")
+    _lib.check(lib.tq_bias_gelu(qkv.data_ptr(), parts.data_ptr(), n_parts, N * 3 * C, bias.data_ptr(), 3 * C, 0,
+                                batch.count_ptr(0), N, st), "tq_bias_gelu")  # fmt: skip
+    batch.write_rows(2, qkv, C, 2 * C, st)
+    want_pool = alloc.pool.clone()
+    alloc.pool.copy_(pool0)
+    q = torch.full((N, C), float("nan"), device="cuda")
+    batch.write_qkv_rows(2, parts, n_parts, N * 3 * C, bias, q, st)
+    torch.cuda.synchronize()
+    assert torch.equal(q, qkv[:, :C])
+    assert torch.equal(alloc.pool, want_pool)
+    assert _lib.device_status() == 0
+
+
 def _ln(x, w, b, eps):
     return torch.nn.functional.layer_norm(x, (x.shape[-1],), w, b, eps)
 
@@ -291,3 +332,28 @@ def test_abi_rejects_bad_arguments():
     st = lib.tq_bias_gelu(pool.data_ptr(), pool.data_ptr(), 1, 0, pool.data_ptr(), 6, 1, n.data_ptr(), 1, None)
     assert st == _lib.TQ_ERR_INVALID
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("V", [1, 3, 31, 1024, 8193, 50257])
+def test_argmax_rows_matches_torch(V):
+    """tq_argmax_rows picks what torch.argmax(-1) picks: first of equal maxima,
+    NaN as the largest value, all -inf rows at index 0."""
+    from tokquay_b200.model import argmax_rows
+
+    g = torch.Generator(device="cuda").manual_seed(V)
+    x = torch.randn(37, V, device="cuda", generator=g)
+    if V > 10:
+        x[3, V // 3] = x[3, V // 2] = 1e9  # a tie: the first index wins
+        x[5, 7] = float("nan")
+        x[5, 9] = float("nan")
+        x[8, 4] = float("inf")
+    x[6] = float("-inf")
+    x[7] = 2.0
+    got = argmax_rows(x)
+    assert torch.equal(got, x.argmax(-1))
+    # a view with a row stride larger than V, rows limited by a device count
+    wide = torch.randn(20, V + 5, device="cuda", generator=g)
+    out = torch.full((20,), -1, dtype=torch.int64, device="cuda")
+    n = torch.tensor([13], dtype=torch.int32, device="cuda")
+    argmax_rows(wide[:, :V], out=out, d_num_rows=n.data_ptr(), max_rows=20)
+    assert torch.equal(out[:13], wide[:13, :V].argmax(-1)) and (out[13:] == -1).all()

@@ -92,3 +92,36 @@ def test_native_pack_and_plan_matches_the_python_path(seed):
     with pytest.raises(ValueError):
         hostpack.plan_sequences(_lib.function_address("tq_plan_step"), [bad], [bad.num_uncached_tokens + 5], 16,
                                 4000, 12, 50257, 1, 8, 0, out.ctypes.data, out.size, layout.ctypes.data)  # fmt: skip
+
+
+def test_decode_only_planning_and_advance():
+    """decode_max_ctx: a step with a prefill row, or a context past the limit,
+    comes back as -2 with nothing planned; a decode step is planned and
+    advance_cached moves every sequence on by its one token."""
+    from tokquay_b200 import _lib
+    from tokquay_b200.kv_cache import MIN_SPLIT_CHUNKS
+
+    fn = _lib.function_address("tq_plan_step")
+    seqs = []
+    for i in range(5):
+        s = Sequence(i, list(range(10 + i)))
+        s.num_cached_tokens = s.num_tokens - 1
+        s.block_table = list(range(i * 4, i * 4 + 4))
+        seqs.append(s)
+    out = np.zeros(1 << 16, np.int32)
+    layout = np.zeros(_lib.PLAN_LAYOUT_LEN, np.int32)
+    args = (16, 64, 12, 0, 3, MIN_SPLIT_CHUNKS, 0, out.ctypes.data, out.size, layout.ctypes.data)
+    assert hostpack.plan_sequences(fn, seqs, None, *args, 64) == 0
+    before = [s.num_cached_tokens for s in seqs]
+    hostpack.advance_cached(seqs)
+    assert [s.num_cached_tokens for s in seqs] == [b + 1 for b in before]
+    with pytest.raises(RuntimeError):
+        hostpack.advance_cached(seqs)  # only once per planned step
+    for s in seqs:  # one more token each: still a decode step
+        s.append_token(7)
+    assert hostpack.plan_sequences(fn, seqs, None, *args, 14) == -2  # context 15 > 14
+    seqs[2].num_cached_tokens -= 3  # a prefill-like row (4 new tokens)
+    assert hostpack.plan_sequences(fn, seqs, None, *args, 64) == -2
+    with pytest.raises(RuntimeError):
+        hostpack.advance_cached(seqs)  # nothing was planned
+    assert hostpack.plan_sequences(fn, seqs, None, *args) == 0  # no decode check: planned

@@ -56,6 +56,8 @@ SIGNATURES: dict[str, tuple] = {
                              c_int32, c_int32, _P, _P, c_int64, _P]),
     "tq_kv_write": (c_int, [_P, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32, _P, c_int64,
                             c_int64, c_int64, _P, _P, c_int32, _P]),
+    "tq_qkv_bias_kv_write": (c_int, [_P, c_int64, _P, c_int32, c_int64, _P, _P, c_int64, c_int32, c_int32,
+                                     c_int32, c_int32, c_int32, _P, _P, c_int32, _P]),
     "tq_paged_attention": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32,
                                    c_int32, c_int32, _P, c_int32, _P, c_int32, _P, _P, _P, c_int32,
                                    c_float, _P]),
@@ -66,6 +68,7 @@ SIGNATURES: dict[str, tuple] = {
                                    c_int32, _P, c_int32, _P]),
     "tq_bias_residual_layernorm": (c_int, [_P, _P, _P, c_int32, c_int64, _P, _P, _P, c_float, c_int32, _P,
                                            c_int32, _P]),
+    "tq_argmax_rows": (c_int, [_P, c_int64, c_int32, _P, _P, c_int32, _P]),
     "tq_layernorm_rows": (c_int, [_P, _P, _P, _P, _P, c_float, c_int32, _P, c_int32, _P]),
     "tq_bias_gelu": (c_int, [_P, _P, c_int32, c_int64, _P, c_int32, c_int32, _P, c_int32, _P]),
 }

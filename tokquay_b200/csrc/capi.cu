@@ -214,6 +214,58 @@ int tq_kv_write(float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head
   return check_launch("kv_write");
 }
 
+int tq_qkv_bias_kv_write(float* q_out, int64_t q_row_stride, const float* parts, int32_t n_parts,
+                         int64_t part_stride, const float* bias, float* pool, int64_t num_blocks,
+                         int32_t n_layer, int32_t n_head, int32_t block_size, int32_t head_dim,
+                         int32_t layer, const int32_t* slot_mapping, const int32_t* d_num_rows,
+                         int32_t max_rows, void* stream) {
+  int st = check_pool(pool, num_blocks, n_layer, n_head, block_size, head_dim, layer);
+  if (st) return st;
+  if (max_rows < 0) return set_error(TQ_ERR_INVALID, "max_rows must be >= 0");
+  if (n_head > 21) return set_error(TQ_ERR_UNSUPPORTED, "qkv_bias_kv_write: n_head must be at most 21");
+  const int64_t cols = 3LL * n_head * head_dim;
+  if (n_parts < 1 || (n_parts > 1 && (part_stride < (int64_t)max_rows * cols || part_stride % 4)))
+    return set_error(TQ_ERR_INVALID, "qkv_bias_kv_write: bad split-K parts");
+  if (max_rows == 0) return TQ_OK;
+  if (!q_out || !parts || !bias || !slot_mapping || !d_num_rows)
+    return set_error(TQ_ERR_INVALID, "qkv_bias_kv_write: NULL argument");
+  if (!aligned(q_out, 16) || q_row_stride % 4 || !aligned(parts, 16) || !aligned(bias, 16))
+    return set_error(TQ_ERR_INVALID, "qkv_bias_kv_write: arrays must be 16-byte aligned");
+  if (reinterpret_cast<const char*>(q_out) < reinterpret_cast<const char*>(parts + part_stride * (n_parts - 1) +
+                                                                           (int64_t)max_rows * cols) &&
+      reinterpret_cast<const char*>(parts) < reinterpret_cast<const char*>(q_out + (int64_t)max_rows * q_row_stride))
+    return set_error(TQ_ERR_INVALID, "qkv_bias_kv_write: q_out overlaps the partial sums");
+  int sms = 0;
+  if ((st = device_setup(&sms))) return st;
+  QkvWriteParams p;
+  p.q_out = q_out;
+  p.q_stride = q_row_stride;
+  p.parts = parts;
+  p.n_parts = n_parts;
+  p.part_stride = part_stride;
+  p.bias = bias;
+  p.pool = pool;
+  p.num_blocks = num_blocks;
+  p.n_layer = n_layer;
+  p.n_head = n_head;
+  p.block_size = block_size;
+  p.log2_bs = log2_exact(block_size);
+  p.layer = layer;
+  p.slots = slot_mapping;
+  p.n_rows = d_num_rows;
+  const int threads = (int)(cols / 4);
+  const int grid = row_grid(max_rows, sms);
+  const cudaStream_t s = (cudaStream_t)stream;
+  switch (n_parts) {  // partial-sum loads unrolled for the split counts the model uses
+    case 1: qkv_bias_kv_write_kernel<1><<<grid, threads, 0, s>>>(p); break;
+    case 2: qkv_bias_kv_write_kernel<2><<<grid, threads, 0, s>>>(p); break;
+    case 4: qkv_bias_kv_write_kernel<4><<<grid, threads, 0, s>>>(p); break;
+    case 8: qkv_bias_kv_write_kernel<8><<<grid, threads, 0, s>>>(p); break;
+    default: qkv_bias_kv_write_kernel<0><<<grid, threads, 0, s>>>(p); break;
+  }
+  return check_launch("qkv_bias_kv_write");
+}
+
 int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64_t q_row_stride,
                        const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
                        int32_t block_size, int32_t head_dim, int32_t layer,
@@ -423,6 +475,7 @@ int tq_bias_residual_layernorm(float* x, float* xa, const float* y, int32_t n_pa
     case 4: bias_residual_ln_kernel<4><<<grid, threads, 0, s>>>(p); break;
     case 8: bias_residual_ln_kernel<8><<<grid, threads, 0, s>>>(p); break;
     case 16: bias_residual_ln_kernel<16><<<grid, threads, 0, s>>>(p); break;
+    case 32: bias_residual_ln_kernel<32><<<grid, threads, 0, s>>>(p); break;
     default: bias_residual_ln_kernel<0><<<grid, threads, 0, s>>>(p); break;
   }
   return check_launch("bias_residual_layernorm");
@@ -452,6 +505,22 @@ int tq_layernorm_rows(float* out, const float* x, const int32_t* rows, const flo
   p.eps = eps;
   layernorm_rows_kernel<<<row_grid(max_rows, sms), n_embd / 4, 0, (cudaStream_t)stream>>>(p);
   return check_launch("layernorm_rows");
+}
+
+int tq_argmax_rows(const float* x, int64_t row_stride, int32_t n_cols, int64_t* out, const int32_t* d_num_rows,
+                   int32_t max_rows, void* stream) {
+  if (max_rows < 0 || n_cols < 1 || row_stride < n_cols)
+    return set_error(TQ_ERR_INVALID, "argmax_rows: need n_cols >= 1, row_stride >= n_cols, max_rows >= 0");
+  if (max_rows == 0) return TQ_OK;
+  if (!x || !out || !d_num_rows) return set_error(TQ_ERR_INVALID, "argmax_rows: NULL argument");
+  int sms = 0;
+  const int st = device_setup(&sms);
+  if (st) return st;
+  const int threads = n_cols >= 1024 * 8 ? 1024 : 256;
+  argmax_rows_kernel<<<row_grid(max_rows, sms), threads, 0, (cudaStream_t)stream>>>(x, row_stride, n_cols,
+                                                                                     reinterpret_cast<long long*>(out),
+                                                                                     d_num_rows);
+  return check_launch("argmax_rows");
 }
 
 int tq_bias_gelu(float* out, const float* h, int32_t n_parts, int64_t part_stride, const float* bias,

@@ -213,4 +213,70 @@ __global__ void __launch_bounds__(256) bias_gelu_kernel(const GeluParams p) {
   }
 }
 
+// Greedy sampling: out[r] = argmax_c x[r][c], as torch.argmax(-1) picks it
+// (tokquay/engine.py:189-194 samples greedy rows this way): NaN counts as the
+// largest value, and among equal values the first index wins.
+__device__ __forceinline__ void argmax_take(float& v, int& i, float v2, int i2) {
+  const bool nan1 = v != v, nan2 = v2 != v2;
+  const bool take = (nan1 || nan2) ? (nan2 && (!nan1 || i2 < i)) : (v2 > v || (v2 == v && i2 < i));
+  if (take) {
+    v = v2;
+    i = i2;
+  }
+}
+
+// One block per row, threads striding over the columns (coalesced loads;
+// rows of odd length are not 16-byte aligned), then warp and block reductions.
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restrict__ x, long long stride, int n_cols,
+                                                           long long* __restrict__ out, const int* n_rows) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int n = *n_rows;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int r = blockIdx.x; r < n; r += gridDim.x) {
+    const float* row = x + (size_t)r * stride;
+    float v = -INFINITY;
+    int i = 0x7fffffff;
+    // kArgmaxUnroll loads in flight per thread before the comparisons; a
+    // thread's columns still come in increasing order, so ties keep the first.
+    constexpr int kArgmaxUnroll = 8;
+    for (int c0 = threadIdx.x; c0 < n_cols; c0 += kArgmaxUnroll * blockDim.x) {
+      float u[kArgmaxUnroll];
+#pragma unroll
+      for (int k = 0; k < kArgmaxUnroll; ++k) {
+        const int c = c0 + k * blockDim.x;
+        u[k] = c < n_cols ? __ldg(row + c) : -INFINITY;
+      }
+#pragma unroll
+      for (int k = 0; k < kArgmaxUnroll; ++k) {
+        const int c = c0 + k * blockDim.x;
+        if (c < n_cols) argmax_take(v, i, u[k], c);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float v2 = __shfl_xor_sync(kFullMask, v, o);
+      const int i2 = __shfl_xor_sync(kFullMask, i, o);
+      argmax_take(v, i, v2, i2);
+    }
+    if (lane == 0) {
+      sv[w] = v;
+      si[w] = i;
+    }
+    __syncthreads();
+    if (w == 0) {
+      v = lane < nw ? sv[lane] : -INFINITY;
+      i = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(kFullMask, v, o);
+        const int i2 = __shfl_xor_sync(kFullMask, i, o);
+        argmax_take(v, i, v2, i2);
+      }
+      if (lane == 0) out[r] = i;
+    }
+    __syncthreads();  // sv / si are reused by the next row
+  }
+}
+
 }  // namespace tq

@@ -24,7 +24,14 @@
  * straight to the planner (plan_fn: the address of tq_plan_step; caps, out and
  * layout: addresses of int32 host buffers, caps 0 for none), so one decode
  * step's host planning makes no Python objects at all.  Returns the planner's
- * status (0 = TQ_OK).
+ * status (0 = TQ_OK).  With decode_max_ctx > 0 only a decode step (one new
+ * token per sequence, contexts <= decode_max_ctx) is planned; any other step
+ * returns -2 and plans nothing.
+ *
+ *   advance_cached(seqs)
+ *
+ * adds each sequence's q_len of the step plan_sequences last planned to its
+ * num_cached_tokens (tokquay/generate.py:85-86).
  */
 #define PY_SSIZE_T_CLEAN
 #include <Python.h>
@@ -219,20 +226,27 @@ done:
   return result;
 }
 
+/* plan_sequences' answer for a step that is not a decode step (decode_max_ctx). */
+#define NOT_A_DECODE_STEP (-2)
+
 /* The planner's C signature (include/tokquay_b200.h, tq_plan_step). */
 typedef int (*plan_fn_t)(int32_t, const int32_t*, const int32_t*, const int32_t*, const int32_t*, const int32_t*,
                          int32_t, int64_t, int32_t, int32_t, int32_t, int32_t, const int32_t*, int32_t*, int64_t,
                          int32_t*);
 
+/* q_len of the last step plan_sequences packed (for advance_cached). */
+static Py_ssize_t g_last_B = -1;
+
 static PyObject* plan_sequences(PyObject* self, PyObject* args) {
   (void)self;
   unsigned long long fn, caps, out, layout;
   PyObject *seqs, *new_lens, *seq_fast = NULL, *lens_fast = NULL, *result = NULL;
-  int block_size, n_head, vocab, n_ctas, min_split;
+  int block_size, n_head, vocab, n_ctas, min_split, decode_max_ctx = 0;
   long long num_blocks, out_cap;
-  if (!PyArg_ParseTuple(args, "KOOiLiiiiKKLK", &fn, &seqs, &new_lens, &block_size, &num_blocks, &n_head, &vocab,
-                        &n_ctas, &min_split, &caps, &out, &out_cap, &layout))
+  if (!PyArg_ParseTuple(args, "KOOiLiiiiKKLK|i", &fn, &seqs, &new_lens, &block_size, &num_blocks, &n_head, &vocab,
+                        &n_ctas, &min_split, &caps, &out, &out_cap, &layout, &decode_max_ctx))
     return NULL;
+  g_last_B = -1;
   if (!fn || !out || !layout) {
     PyErr_SetString(PyExc_ValueError, "plan_fn, out and layout must be non-zero addresses");
     return NULL;
@@ -244,10 +258,18 @@ static PyObject* plan_sequences(PyObject* self, PyObject* args) {
   Py_ssize_t n_tab = 0, n_tok = 0;
   if (pack_into(seq_fast, lens_fast, small, small + B, small + 2 * B, &g_tabs, &g_toks, &n_tab, &n_tok) < 0)
     goto done;
+  if (decode_max_ctx > 0) { /* only a decode step (one token each, context <= decode_max_ctx) is planned */
+    for (Py_ssize_t b = 0; b < B; ++b)
+      if (small[B + b] != 1 || small[b] < 0 || small[b] + 1 > decode_max_ctx) {
+        result = PyLong_FromLong(NOT_A_DECODE_STEP);
+        goto done;
+      }
+  }
   const int status = ((plan_fn_t)(uintptr_t)fn)(
       (int32_t)B, small, small + B, small + 2 * B, g_tabs.p, g_toks.p, block_size, num_blocks, n_head, vocab, n_ctas,
       min_split, caps ? (const int32_t*)(uintptr_t)caps : NULL, (int32_t*)(uintptr_t)out, out_cap,
       (int32_t*)(uintptr_t)layout);
+  if (status == 0) g_last_B = B;
   result = PyLong_FromLong(status);
 done:
   Py_XDECREF(lens_fast);
@@ -255,12 +277,43 @@ done:
   return result;
 }
 
+/* advance_cached(seqs): num_cached_tokens += q_len for each sequence of the
+ * step plan_sequences last planned successfully (the same list). */
+static PyObject* advance_cached(PyObject* self, PyObject* args) {
+  (void)self;
+  PyObject* seqs;
+  if (!PyArg_ParseTuple(args, "O", &seqs)) return NULL;
+  PyObject* seq_fast = PySequence_Fast(seqs, "seqs must be a sequence");
+  if (!seq_fast) return NULL;
+  const Py_ssize_t B = PySequence_Fast_GET_SIZE(seq_fast);
+  if (B != g_last_B) {
+    Py_DECREF(seq_fast);
+    PyErr_SetString(PyExc_RuntimeError, "advance_cached: not the step plan_sequences last planned");
+    return NULL;
+  }
+  g_last_B = -1;
+  for (Py_ssize_t b = 0; b < B; ++b) {
+    PyObject* v = PyLong_FromLong((long)g_small.p[b] + g_small.p[B + b]);
+    if (!v || PyObject_SetAttr(PySequence_Fast_GET_ITEM(seq_fast, b), s_cached, v) < 0) {
+      Py_XDECREF(v);
+      Py_DECREF(seq_fast);
+      return NULL;
+    }
+    Py_DECREF(v);
+  }
+  Py_DECREF(seq_fast);
+  Py_RETURN_NONE;
+}
+
 static PyMethodDef methods[] = {
     {"pack_step", pack_step, METH_VARARGS,
      "pack_step(seqs, new_lens or None) -> (starts, lens, offsets, tables, ids) int32 bytearrays"},
     {"plan_sequences", plan_sequences, METH_VARARGS,
      "plan_sequences(plan_fn, seqs, new_lens or None, block_size, num_blocks, n_head, vocab_size, n_ctas, "
-     "min_split_chunks, caps, out, out_capacity, layout) -> status"},
+     "min_split_chunks, caps, out, out_capacity, layout[, decode_max_ctx]) -> status "
+     "(-2: not a decode step within decode_max_ctx, nothing planned)"},
+    {"advance_cached", advance_cached, METH_VARARGS,
+     "advance_cached(seqs): num_cached_tokens += q_len of the step plan_sequences last planned"},
     {NULL, NULL, 0, NULL}};
 
 static struct PyModuleDef module = {PyModuleDef_HEAD_INIT, "_hostpack",

@@ -52,4 +52,77 @@ __global__ void __launch_bounds__(1024) kv_write_kernel(const KvWriteParams p) {
   }
 }
 
+// Fused c_attn epilogue: the qkv row is the sum of the split-K partial sums
+// of the c_attn matmul plus its bias (tokquay/model.py:69); q goes to q_out,
+// K and V straight into their pool slot (tokquay/kv_cache.py:228-232), so the
+// K/V columns are never written anywhere else.
+struct QkvWriteParams {
+  float* q_out;
+  long long q_stride;      // floats between q rows
+  const float* parts;      // [n_parts][rows][3C]
+  int n_parts;
+  long long part_stride;   // floats between partial sums
+  const float* bias;       // [3C]
+  float* pool;
+  long long num_blocks;
+  int n_layer, n_head, block_size, log2_bs, layer;
+  const int* slots;
+  const int* n_rows;       // device-resident count
+};
+
+// One block per row, thread t owns float4 t of the 3C columns (blockDim =
+// 3C/4).  NP > 0: exactly NP partial sums, loads unrolled; NP == 0: looped.
+// Summation order matches the unfused path (bias_gelu_kernel): ((p0 + p1) + ...) + bias.
+template <int NP>
+__global__ void __launch_bounds__(1024) qkv_bias_kv_write_kernel(const QkvWriteParams p) {
+  const int n = *p.n_rows;
+  const int C4 = p.n_head * 16;  // float4 per q (or K, or V) row
+  const int t = threadIdx.x;
+  const long long pool_slots = p.num_blocks << p.log2_bs;
+  const float4 b = reinterpret_cast<const float4*>(p.bias)[t];
+  const long long ps4 = p.part_stride >> 2;
+  for (int r = blockIdx.x; r < n; r += gridDim.x) {
+    const float4* src = reinterpret_cast<const float4*>(p.parts) + (size_t)r * 3 * C4 + t;
+    float4 v = src[0];
+    if (NP > 0) {
+      float4 u[NP > 1 ? NP - 1 : 1];
+#pragma unroll
+      for (int s = 1; s < NP; ++s) u[s - 1] = src[s * ps4];
+#pragma unroll
+      for (int s = 1; s < NP; ++s) {
+        v.x += u[s - 1].x;
+        v.y += u[s - 1].y;
+        v.z += u[s - 1].z;
+        v.w += u[s - 1].w;
+      }
+    } else {
+      for (int s = 1; s < p.n_parts; ++s) {
+        const float4 u = src[s * ps4];
+        v.x += u.x;
+        v.y += u.y;
+        v.z += u.z;
+        v.w += u.w;
+      }
+    }
+    v = make_float4(v.x + b.x, v.y + b.y, v.z + b.z, v.w + b.w);
+    if (t < C4) {
+      reinterpret_cast<float4*>(p.q_out + (size_t)r * p.q_stride)[t] = v;
+      continue;
+    }
+    const long long slot = p.slots[r];
+    if (slot < 0 || slot >= pool_slots) {
+      if (t == C4) raise_device_error(TQ_DEVERR_BAD_SLOT);
+      continue;
+    }
+    const int kv = t >= 2 * C4;
+    const int g = t - C4 - kv * C4;  // float4 within the K (or V) row: head g / 16, dims (g % 16) * 4
+    const long long blk = slot >> p.log2_bs;
+    const int off = (int)(slot & (p.block_size - 1));
+    float4* dst = reinterpret_cast<float4*>(
+        p.pool + (((((size_t)blk * p.n_layer + p.layer) * 2 + kv) * p.n_head + (g >> 4)) * (size_t)p.block_size +
+                  off) * 64);
+    dst[g & 15] = v;
+  }
+}
+
 }  // namespace tq

@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import torch
 
-from tokquay_b200.kv_cache import BlockAllocator
+from tokquay_b200.kv_cache import BlockAllocator, _hostpack
 from tokquay_b200.model import GPT2
 from tokquay_b200.sequence import Sequence, SequenceStatus
 
@@ -26,13 +26,19 @@ def paged_forward(
     (``n_i`` defaults to everything uncached), so prefill and decode mix freely.
     Blocks must already cover the sequences.  Advances ``num_cached_tokens``.
     """
-    lens = new_lens or [s.num_uncached_tokens for s in seqs]
     runner = getattr(model, "graph_runner", None)
-    if runner is not None and runner.accepts(allocator, seqs, lens):
-        logits = runner.run(seqs)  # decode step: replay a captured CUDA graph
-    else:
-        batch = allocator.batch_for(seqs, lens)
-        logits = model.forward_paged(batch, last_only=True)[:, 0]
+    if runner is not None and runner.allocator is allocator:
+        logits = runner.try_run(seqs, new_lens)  # a decode step: replay a captured CUDA graph
+        if logits is not None:
+            if _hostpack is not None and hasattr(_hostpack, "advance_cached"):
+                _hostpack.advance_cached(seqs)  # the native packer kept this step's lengths
+            else:
+                for s in seqs:
+                    s.num_cached_tokens += 1
+            return logits
+    lens = new_lens or [s.num_uncached_tokens for s in seqs]
+    batch = allocator.batch_for(seqs, lens)
+    logits = model.forward_paged(batch, last_only=True)[:, 0]
     for s, n in zip(seqs, lens):
         s.num_cached_tokens += n
     return logits

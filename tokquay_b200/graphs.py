@@ -22,6 +22,7 @@ import torch
 
 from tokquay_b200 import _lib
 from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, PlanWorkspace
+from tokquay_b200.model import argmax_rows
 from tokquay_b200.sequence import Sequence
 
 DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256, 512)
@@ -69,7 +70,8 @@ class DecodeGraphRunner:
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
             for _ in range(2):  # warm cuBLAS handles and workspaces outside the capture
-                self.model.forward_paged(view, last_only=True)[:, 0].argmax(-1)
+                lg = self.model.forward_paged(view, last_only=True)[:, 0]
+                argmax_rows(lg, d_num_rows=view.count_ptr(3), max_rows=bucket)
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
         graph = torch.cuda.CUDAGraph()
@@ -78,8 +80,8 @@ class DecodeGraphRunner:
         launches = self.model.kernel_launches
         with torch.cuda.graph(graph, pool=self._pool):
             logits = self.model.forward_paged(view, last_only=True)[:, 0]
-            tokens = logits.argmax(-1)
-        per_replay = self.model.kernel_launches - launches
+            tokens = argmax_rows(logits, d_num_rows=view.count_ptr(3), max_rows=bucket)  # greedy sampling
+        per_replay = self.model.kernel_launches - launches + 1
         self.model.kernel_launches = launches
         entry = (graph, ws, logits, tokens, per_replay)
         self._graphs[bucket] = entry
@@ -87,6 +89,25 @@ class DecodeGraphRunner:
 
     def graph(self, bucket: int):
         return self._graphs.get(bucket) or self._capture(bucket)
+
+    def try_run(self, seqs: list[Sequence], new_lens: list[int] | None = None) -> torch.Tensor | None:
+        """``run`` for a step that turns out to be a decode step (one new token
+        per sequence, context within the graphs' capacity) that fits a
+        bucket; None, with nothing planned or launched, for any other step.
+        Decides in the native packer, without a Python pass over the sequences."""
+        B = len(seqs)
+        bucket = self.bucket_for(B) if B else None
+        if bucket is None:
+            return None
+        graph, ws, logits, _, per_replay = self.graph(bucket)
+        layout = ws.stage_sequences(seqs, new_lens, torch.cuda.current_stream(self.allocator.pool.device),
+                                    self.model.cfg.vocab_size, decode_max_ctx=self.max_ctx)  # fmt: skip
+        if layout is None:
+            return None
+        self.model.last_h2d_bytes = ws.last_used_ints * 4
+        graph.replay()
+        self.model.kernel_launches += per_replay
+        return logits[:B].clone()
 
     def run(self, seqs: list[Sequence]) -> torch.Tensor:
         """Plan the decode step for ``seqs``, replay its bucket's graph, return

@@ -359,6 +359,9 @@ def plan_step_host(
                        out, caps)  # fmt: skip
 
 
+_NOT_A_DECODE_STEP = -2  # _hostpack.plan_sequences: the step is not a decode step, nothing planned
+
+
 class PlanWorkspace:
     """A fixed-capacity home for one step plan on the device.
 
@@ -422,19 +425,33 @@ class PlanWorkspace:
         return layout
 
     def stage_sequences(self, seqs, new_lens: list[int] | None, stream: torch.cuda.Stream,
-                        vocab_size: int = 0) -> np.ndarray:  # fmt: skip
+                        vocab_size: int = 0, decode_max_ctx: int = 0) -> np.ndarray | None:  # fmt: skip
         """``stage`` straight from ``Sequence`` objects: the native packer
         hands its arrays to the planner, so planning a step makes no Python
-        objects.  Same plan, same errors as ``stage(PackedStep.from_sequences(...))``."""
+        objects.  Same plan, same errors as ``stage(PackedStep.from_sequences(...))``.
+        With ``decode_max_ctx`` > 0, a step that is not a decode step within
+        that context, or does not fit the capacities, returns None (nothing staged)."""
         if not self._native:
-            return self.stage(PackedStep.from_sequences(seqs, new_lens), stream, vocab_size)
+            packed = PackedStep.from_sequences(seqs, new_lens)
+            if decode_max_ctx > 0 and (packed.lens.max() != 1 or packed.lens.min() != 1
+                                       or int(packed.start.max()) + 1 > decode_max_ctx):  # fmt: skip
+                return None
+            try:
+                return self.stage(packed, stream, vocab_size)
+            except RuntimeError:
+                if decode_max_ctx > 0:
+                    return None
+                raise
         if not seqs:
             raise ValueError("block_tables, start and new_lens must be non-empty and the same length")
         a = self.allocator
         slot, host = self.pinned_buffer()
         status = _hostpack.plan_sequences(
             self._plan_fn, seqs, new_lens, a.block_size, a.num_blocks, a.cfg.n_head, vocab_size, self.n_ctas,
-            MIN_SPLIT_CHUNKS, self.caps.ctypes.data, host.data_ptr(), self.total, self._layout.ctypes.data)
+            MIN_SPLIT_CHUNKS, self.caps.ctypes.data, host.data_ptr(), self.total, self._layout.ctypes.data,
+            decode_max_ctx)
+        if decode_max_ctx > 0 and status in (_NOT_A_DECODE_STEP, _lib.TQ_ERR_CAPACITY):
+            return None
         _lib.check(status, "tq_plan_step")
         used = int(self._layout[_lib.PLAN_USED_INTS])
         with torch.cuda.stream(stream):
@@ -606,6 +623,19 @@ class DevicePagedBatch(BatchedKV):
                                    self.n_head, self.block_size, self.d_head, layer, qkv.data_ptr(),
                                    qkv.stride(0), k_col, v_col, self.slot_mapping.data_ptr(),
                                    self.count_ptr(0), self.rows_alloc, stream), "tq_kv_write")  # fmt: skip
+
+    def write_qkv_rows(self, layer: int, parts: torch.Tensor, n_parts: int, part_stride: int, bias: torch.Tensor,
+                       q_out: torch.Tensor, stream: int) -> None:  # fmt: skip
+        """The c_attn epilogue: ``row = sum of the n_parts split-K partial sums
+        of c_attn + bias``; q goes to ``q_out`` (``[N, C]`` rows), K and V into
+        the pool slots of the ``N`` new tokens (tokquay/model.py:69 +
+        tokquay/kv_cache.py:228-232, one kernel)."""
+        lib = _lib.load()
+        _lib.check(lib.tq_qkv_bias_kv_write(
+            q_out.data_ptr(), q_out.stride(0), parts.data_ptr(), n_parts, part_stride, bias.data_ptr(),
+            self.pool.data_ptr(), self.allocator.num_blocks, self.n_layer, self.n_head, self.block_size,
+            self.d_head, layer, self.slot_mapping.data_ptr(), self.count_ptr(0), self.rows_alloc, stream),
+            "tq_qkv_bias_kv_write")  # fmt: skip
 
     def attend_rows(self, layer: int, q: torch.Tensor, out: torch.Tensor, stream: int) -> None:
         """``out[n, h*d:(h+1)*d] = softmax(q_n,h . K / sqrt(d)) V`` over keys

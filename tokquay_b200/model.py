@@ -10,7 +10,8 @@ real new tokens of the step, never the reference's padded ``B x T`` -- with:
   partial sums added by the fused kernel that consumes the linear's output;
 * ``tq_embed_layernorm``, ``tq_bias_residual_layernorm``, ``tq_bias_gelu`` and
   ``tq_layernorm_rows`` for everything elementwise around them;
-* ``tq_kv_write`` + ``tq_paged_attention`` for the attention over the pool.
+* ``tq_qkv_bias_kv_write`` (c_attn bias, q out, K/V straight into the pool)
+  + ``tq_paged_attention`` for the attention over the pool.
 
 In the last layer only each sequence's last row is carried past attention
 when ``last_only`` is set: the other rows' K/V are already in the pool and
@@ -69,6 +70,26 @@ def _tf32_off() -> bool:
     return not torch.backends.cuda.matmul.allow_tf32 and torch.get_float32_matmul_precision() == "highest"
 
 
+def argmax_rows(logits: torch.Tensor, out: torch.Tensor | None = None, d_num_rows: int | None = None,
+                max_rows: int | None = None) -> torch.Tensor:
+    """Greedy tokens ``logits.argmax(-1)`` (int64) of a ``[rows, V]`` fp32
+    tensor in one kernel (``tq_argmax_rows``; ties and NaN as torch picks them).
+    ``d_num_rows`` (a device int32 address) limits the rows, for graph capture."""
+    if logits.dim() != 2 or logits.dtype != torch.float32 or logits.stride(1) != 1:
+        raise ValueError("argmax_rows needs a [rows, V] float32 tensor with unit column stride")
+    rows = logits.shape[0] if max_rows is None else max_rows
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int64, device=logits.device)
+    lib = _lib.load()
+    count = d_num_rows
+    if count is None:
+        count_t = torch.full((1,), rows, dtype=torch.int32, device=logits.device)
+        count = count_t.data_ptr()
+    _lib.check(lib.tq_argmax_rows(logits.data_ptr(), logits.stride(0), logits.shape[1], out.data_ptr(), count, rows,
+                                  torch.cuda.current_stream(logits.device).cuda_stream), "tq_argmax_rows")  # fmt: skip
+    return out
+
+
 def split_k_for(rows: int, k: int, n: int) -> int:
     """How many K-slices an fp32 linear of ``rows x k @ k x n`` is split into.
 
@@ -76,7 +97,10 @@ def split_k_for(rows: int, k: int, n: int) -> int:
     whole K loop; one batched matmul over K-slices fills the GPU and the
     slices' partial sums are added by the fused kernel that consumes the
     output.  Chosen from B200 measurements of torch.mm vs torch.bmm over
-    K-slices for GPT-2's linears (rows 8 / 64 / 512)."""
+    K-slices for GPT-2's linears (rows 8 / 64 / 512) and of whole decode
+    steps: finer splits make a matmul alone faster (c_fc and mlp.c_proj at 64
+    rows by ~1.3 us with 8 / 32 slices), but the consumers' extra partial-sum
+    reads cost more than that in the step."""
     if rows > 128:
         s = 4 if k >= 2048 else 1
     else:
@@ -89,12 +113,12 @@ def split_k_for(rows: int, k: int, n: int) -> int:
 class GPT2(nn.Module):
     def __init__(self, cfg: GPT2Config | None = None):
         super().__init__()
-        # Optional measurement hooks: when ``attention_events`` is a list, every
-        # attention launch appends a (start, end) CUDA-event pair recorded on the
-        # launching stream; ``kernel_launches`` counts this package's kernel
-        # launches (GEMMs and other torch ops are not counted).
-        self.attention_events: list | None = None
-        self.attention_event_prelude = None  # optional callable run before each start event
+        # Optional measurement hooks: ``attention_timer(layer, start)`` is called
+        # right before (start=True) and after (start=False) every attention
+        # launch, on the launching stream, so a caller can record CUDA events
+        # around it (also inside a graph capture); ``kernel_launches`` counts this
+        # package's kernel launches (GEMMs and other torch ops are not counted).
+        self.attention_timer = None
         self.kernel_launches = 0
         self.last_h2d_bytes = 0  # plan bytes the last forward's batch copied to the device
         self.graph_runner = None  # set by use_cuda_graphs()
@@ -192,21 +216,15 @@ class GPT2(nn.Module):
             att = blk.attn
             p = f"h.{i}."
             parts, ns, ps = self._linear_parts(xa, self._weight_t(p + "c_attn", att.c_attn.weight))
-            qkv = parts if ns == 1 else torch.empty(N, 3 * C, dtype=torch.float32, device=dev)
-            _lib.check(lib.tq_bias_gelu(qkv.data_ptr(), parts.data_ptr(), ns, ps, att.c_attn.bias.data_ptr(),
-                                        3 * C, 0, rows_ptr, rows, stream), "tq_bias_gelu")  # fmt: skip
-            batch.write_rows(i, qkv, C, 2 * C, stream)
+            q = torch.empty(N, C, dtype=torch.float32, device=dev)
+            batch.write_qkv_rows(i, parts, ns, ps, att.c_attn.bias, q, stream)  # q out, K/V into the pool
             a = torch.empty(N, C, dtype=torch.float32, device=dev)
-            if self.attention_events is not None:
-                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                if self.attention_event_prelude is not None:
-                    self.attention_event_prelude()
-                ev0.record()
-                batch.attend_rows(i, qkv, a, stream)
-                ev1.record()
-                self.attention_events.append((ev0, ev1))
+            if self.attention_timer is not None:
+                self.attention_timer(i, True)
+                batch.attend_rows(i, q, a, stream)
+                self.attention_timer(i, False)
             else:
-                batch.attend_rows(i, qkv, a, stream)
+                batch.attend_rows(i, q, a, stream)
             if last and last_only and N != B:
                 # Only the last row of each sequence is sampled from (model.py:179).
                 sel = batch.last_rows
@@ -230,8 +248,8 @@ class GPT2(nn.Module):
                 nxt.bias.data_ptr() if nxt is not None else None, eps, C, rows_ptr, rows, stream),
                 "tq_bias_residual_layernorm")  # fmt: skip
 
-        # embed + per layer (qkv bias, kv_write, attention, 2x bias_residual, gelu) + final LN
-        self.kernel_launches += 2 + cfg.n_layer * 6
+        # embed + per layer (qkv bias + kv write, attention, 2x bias_residual, gelu) + final LN
+        self.kernel_launches += 2 + cfg.n_layer * 5
         if last_only:
             xf = torch.empty(B, C, dtype=torch.float32, device=dev)
             sel_ptr = None if rows == B else batch.last_rows.data_ptr()
