@@ -55,6 +55,94 @@ def summarize_logits(x: torch.Tensor, stride: int) -> dict[str, np.ndarray]:
     }
 
 
+# Scheduler scenarios: (name, pool blocks, block size, config, request trace).
+# A trace entry is (arrival step, prompt length, max_tokens); "abort" entries
+# (step, "abort", request index) drop a request between steps.
+SCHED_SCENARIOS = [
+    {"name": "burst_preempt", "num_blocks": 40, "block_size": 8, "free_seed": 4,
+     "config": {"max_num_seqs": 8, "max_num_batched_tokens": 400, "max_model_len": 160, "watermark_blocks": 1},
+     "requests": [[0, 20 + 7 * i % 60, 10 + 13 * i % 50] for i in range(14)]},
+    {"name": "staggered", "num_blocks": 64, "block_size": 16, "free_seed": 5,
+     "config": {"max_num_seqs": 5, "max_num_batched_tokens": 300, "max_model_len": 256, "watermark_blocks": 2},
+     "requests": [[3 * i, 10 + 17 * i % 90, 5 + 11 * i % 70] for i in range(20)], "aborts": [[9, 2], [20, 5], [40, 12]]},
+    {"name": "tight_budget", "num_blocks": 24, "block_size": 4, "free_seed": 6,
+     "config": {"max_num_seqs": 16, "max_num_batched_tokens": 64, "max_model_len": 64, "watermark_blocks": 0},
+     "requests": [[i // 3, 5 + 9 * i % 30, 3 + 5 * i % 25] for i in range(18)]},
+]
+
+
+def fake_token(seq_id: int, n_out: int) -> int:
+    """Tokens of the scheduler traces: any deterministic function will do."""
+    return (seq_id * 7919 + n_out * 104729) % 50000
+
+
+def sched_scenario(BlockAllocator, Scheduler, SchedulerConfig, Sequence, SamplingParams, sc) -> dict:
+    """Drive a scheduler with a model-free step (what paged_forward and the
+    engine do to the sequences' state) and record every decision."""
+    alloc = BlockAllocator(_MiniCfg(), sc["num_blocks"], sc["block_size"], device="meta")
+    W.shuffle_free_list(alloc, sc["free_seed"])
+    sched = Scheduler(alloc, SchedulerConfig(**sc["config"]))
+    reqs = [Sequence(i, [(i * 31 + j) % 50000 for j in range(n)], sampling=SamplingParams(max_tokens=mt, ignore_eos=True))
+            for i, (_, n, mt) in enumerate(sc["requests"])]  # fmt: skip
+    arrivals = {}
+    for i, (step, _, _) in enumerate(sc["requests"]):
+        arrivals.setdefault(step, []).append(i)
+    aborts = {}
+    for step, idx in sc.get("aborts", []):
+        aborts.setdefault(step, []).append(idx)
+    rejected, out = [], []
+    k = 0
+    while k <= max(arrivals) or sched.has_unfinished():
+        for idx in aborts.get(k, []):
+            sched.abort(reqs[idx])
+        for idx in arrivals.get(k, []):
+            try:
+                sched.add_request(reqs[idx])
+            except ValueError:
+                rejected.append(idx)
+        batch = sched.schedule()
+        rec = {"step": k}
+        if batch is not None:
+            rec.update(seqs=[s.seq_id for s in batch.seqs], prefill=batch.is_prefill,
+                       preempted=[s.seq_id for s in batch.preempted], padded=batch.padded_tokens)  # fmt: skip
+            for s in batch.seqs:  # what paged_forward + sampling do to the sequence
+                s.num_cached_tokens += s.num_uncached_tokens
+                s.append_token(fake_token(s.seq_id, len(s.output_token_ids)))
+                if len(s.output_token_ids) >= s.sampling.max_tokens:
+                    sched.finish(s, "length")
+        rec.update(running=[s.seq_id for s in sched.running], waiting=[s.seq_id for s in sched.waiting],
+                   tables=[list(s.block_table) for s in sched.running], free=list(alloc._free),
+                   preemptions=sched.num_preemptions, discarded=sched.num_discarded_positions)  # fmt: skip
+        out.append(rec)
+        k += 1
+        if k > 5000:
+            raise RuntimeError("scheduler trace did not finish")
+    return {**sc, "rejected": rejected, "trace": out, "outputs": [s.output_token_ids for s in reqs]}
+
+
+class _MiniCfg:  # what BlockAllocator reads from a config
+    n_layer, n_head, n_embd = 2, 2, 128
+    d_head = 64
+
+
+# The engine case: MINI model, a small pool (preemption), greedy requests
+# arriving in waves.
+ENGINE_CASE = {"cfg": W.MINI, "weights_seed": 21, "init": "gpt2", "block_size": 8, "num_blocks": 30,
+               "pool_seed": 103, "pool_scale": 50.0, "free_seed": 7, "trace_seed": 5,
+               "sched": {"max_num_seqs": 6, "max_num_batched_tokens": 256, "max_model_len": 128,
+                         "watermark_blocks": 1}}  # fmt: skip
+
+
+def engine_arrivals(rng) -> list[list[tuple[list[int], int]]]:
+    """Waves of (prompt, max_tokens): one wave is added before each step."""
+    waves = []
+    for w in range(8):
+        n = [4, 0, 2, 0, 3, 1, 0, 2][w]
+        waves.append([([rng.randrange(W.MINI["vocab_size"]) for _ in range(rng.randint(4, 48))],
+                       rng.randint(6, 40)) for _ in range(n)])  # fmt: skip
+    return waves
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference", help="path of the reference checkout")
@@ -315,6 +403,62 @@ def main() -> None:
             ops[-1]["tables"] = {str(k): list(v.block_table) for k, v in live.items()}
             ops[-1]["ref_counts"] = list(a.ref_counts)
         meta["cases"]["alloc_trace"] = {"num_blocks": 24, "block_size": 4, "ops": ops}
+
+    # ---------------------------------------------------------------- scheduler traces
+    if want("sched_trace"):
+        t0 = time.time()
+        from tokquay.scheduler import Scheduler, SchedulerConfig
+        from tokquay.sequence import SamplingParams
+
+        meta["cases"]["sched_trace"] = {"scenarios": [sched_scenario(BlockAllocator, Scheduler, SchedulerConfig,
+                                                                     Sequence, SamplingParams, sc)
+                                                      for sc in SCHED_SCENARIOS]}  # fmt: skip
+        print(f"sched_trace {time.time() - t0:.1f}s")
+
+    # ---------------------------------------------------------------- engine trace
+    if want("mini_engine"):
+        t0 = time.time()
+        from tokquay.engine import Engine
+        from tokquay.scheduler import SchedulerConfig
+        from tokquay.sequence import SamplingParams
+
+        case = dict(ENGINE_CASE)
+        m = model_for(W.MINI, case["weights_seed"], "gpt2", torch.float32)
+        a = garbage_alloc(m.cfg, case["num_blocks"], case["block_size"], torch.float32, case["pool_seed"],
+                          case["free_seed"])  # fmt: skip
+        eng = Engine(m, a, SchedulerConfig(**case["sched"]))
+        orig_sample = eng._sample
+        margins: list[list[float]] = []
+
+        def sample_and_record(seqs, logits):
+            top = torch.topk(logits.float(), 2, dim=-1).values
+            margins.append((top[:, 0] - top[:, 1]).tolist())
+            return orig_sample(seqs, logits)
+
+        eng._sample = sample_and_record
+        steps = []
+        rng = random.Random(case["trace_seed"])
+        arrivals = engine_arrivals(rng)
+        k = 0
+        while arrivals or eng.has_unfinished():
+            for prompt, max_tokens in arrivals.pop(0) if arrivals else []:
+                eng.add_request(prompt, SamplingParams(max_tokens=max_tokens, ignore_eos=True))
+            events = eng.step()
+            last = eng.last_step
+            steps.append({
+                "events": [[e.seq_id, e.token_id, e.finish_reason] for e in events],
+                "is_prefill": bool(last.is_prefill) if last else None,
+                "running": [s.seq_id for s in eng.scheduler.running],
+                "tables": [list(s.block_table) for s in eng.scheduler.running],
+                "waiting": [s.seq_id for s in eng.scheduler.waiting],
+                "free": list(a._free),
+                "preemptions": eng.scheduler.num_preemptions,
+            })
+            k += 1
+        case["steps"] = steps
+        case["margins"] = margins
+        meta["cases"]["mini_engine"] = case
+        print(f"mini_engine {time.time() - t0:.1f}s, {k} steps")
 
     json_path.write_text(json.dumps(meta, separators=(",", ":")))
     np.savez_compressed(npz_path, **arrays)

@@ -1,0 +1,66 @@
+"""The engine (tokquay_b200/engine.py) over the B200 path reproduces the
+reference engine run on the CPU (tests/golden/make_golden.py, case
+``mini_engine``): requests arriving in waves on a pool small enough to force
+preemption by recompute, greedy sampling.  Every step's tokens, finish
+reasons, prefill/decode choice, running and waiting queues, block tables and
+free list must be equal -- with and without CUDA graphs for the decode steps.
+"""
+
+import random
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+from helpers import cfg_of, load_golden
+from tokquay_b200 import workloads as W
+from tokquay_b200.engine import Engine
+from tokquay_b200.kv_cache import BlockAllocator
+from tokquay_b200.model import GPT2
+from tokquay_b200.scheduler import SchedulerConfig
+from tokquay_b200.sequence import SamplingParams
+
+sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+import make_golden  # noqa: E402  (the arrival waves the fixture was recorded with)
+
+pytestmark = pytest.mark.gpu
+GOLDEN = load_golden()
+# A greedy choice whose top-2 logits are closer than this is a coin toss between
+# float orders of summation; the trace is compared up to the first one.
+NEAR_TIE = 2e-5
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+def test_engine_matches_the_reference_engine(graphs):
+    case = GOLDEN.cases["mini_engine"]
+    cfg = cfg_of(case)
+    m = GPT2(cfg)
+    W.load_weights(m, W.random_weights(cfg, case["weights_seed"], case["init"]))
+    m = m.to("cuda").eval()
+    a = BlockAllocator(cfg, case["num_blocks"], case["block_size"], device="cuda")
+    W.fill_pool_blocks(a.pool, range(case["num_blocks"]), case["pool_seed"], case["pool_scale"])
+    W.shuffle_free_list(a, case["free_seed"])
+    if graphs:
+        m.use_cuda_graphs(a)
+    eng = Engine(m, a, SchedulerConfig(**case["sched"]))
+    arrivals = make_golden.engine_arrivals(random.Random(case["trace_seed"]))
+    margins = [min(x) for x in case["margins"]]
+    for k, want in enumerate(case["steps"]):
+        for prompt, max_tokens in arrivals.pop(0) if arrivals else []:
+            eng.add_request(prompt, SamplingParams(max_tokens=max_tokens, ignore_eos=True))
+        events = eng.step()
+        got = {
+            "events": [[e.seq_id, e.token_id, e.finish_reason] for e in events],
+            "is_prefill": bool(eng.last_step.is_prefill) if eng.last_step else None,
+            "running": [s.seq_id for s in eng.scheduler.running],
+            "tables": [list(s.block_table) for s in eng.scheduler.running],
+            "waiting": [s.seq_id for s in eng.scheduler.waiting],
+            "free": list(a._free),
+            "preemptions": eng.scheduler.num_preemptions,
+        }
+        assert got == want, f"step {k}"
+        if k < len(margins) and margins[k] < NEAR_TIE:
+            break  # later tokens may legitimately differ
+    else:
+        assert not eng.has_unfinished() and eng.stats.num_preemptions > 0
