@@ -269,14 +269,26 @@ def attn_bytes(ctx_list, n_head, d, num_partials):
 
 
 # ------------------------------------------------------------------------------ attention timing
-def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> list[float]:
-    """Per-launch attention times (ms) over the same steps, eager."""
+def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> tuple[list[float], list[float]]:
+    """Attention times (ms) over the same steps, eager, two ways:
+
+    * burst: after each step's forward, its 12 attention launches again back to
+      back, an event between consecutive launches (each interval is one
+      launch as a stream of launches runs it: the kernel plus the GPU's gap to
+      the next);
+    * single: events around each attention launch inside the forward itself,
+      each after a device sleep, so the interval also holds the GPU's launch
+      and CTA start-up of a kernel that follows an idle stream."""
     from tokquay_b200.kv_cache import DevicePagedBatch
 
     case = make_case(spec, a, seed)
     seqs = case.seqs
     B = len(seqs)
     pairs: list = []
+    bursts: list = []
+    C = model.cfg.n_embd
+    q = torch.randn(B, C, device=a.pool.device, generator=torch.Generator(a.pool.device).manual_seed(0))
+    out = torch.empty_like(q)
 
     def timer(layer: int, start: bool) -> None:
         if start:
@@ -292,9 +304,17 @@ def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> list[flo
             if k == warmup:
                 torch.cuda.synchronize()
                 pairs.clear()
+                bursts.clear()
             model.attention_timer = timer
             model.forward_paged(b, last_only=True)
             model.attention_timer = None
+            torch.cuda._sleep(200_000)
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(model.cfg.n_layer + 1)]
+            evs[0].record()
+            for layer in range(model.cfg.n_layer):
+                b.attend_rows(layer, q, out, torch.cuda.current_stream().cuda_stream)
+                evs[layer + 1].record()
+            bursts.append(evs)
             if spec["grow"]:
                 for s in seqs:
                     s.num_cached_tokens += 1
@@ -303,7 +323,8 @@ def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> list[flo
         torch.cuda.synchronize()
     finally:
         model.attention_timer = None
-    return [e0.elapsed_time(e1) for e0, e1 in pairs]
+    burst = [e0.elapsed_time(e1) for evs in bursts for e0, e1 in zip(evs, evs[1:])]
+    return burst, [e0.elapsed_time(e1) for e0, e1 in pairs]
 
 
 # ------------------------------------------------------------------------------ our arm
@@ -391,9 +412,10 @@ def run_ours(args, world, rank, local):
     # keeping host launch latency out of the interval.
     bytes_per_launch = [attn_bytes(ctx_per_step[k], cfg.n_head, cfg.d_head, nparts_per_step[k])
                         for k in range(Wm, total_steps) for _ in range(cfg.n_layer)]  # fmt: skip
-    attn_ms, attn_timing = eager_attention_times(model, a, spec, seed, Wm, total_steps), (
-        "CUDA events around each attention launch in an eager pass over the same steps, a device sleep "
-        "before each so host launch latency is not counted (the GPU's own launch and CTA start-up are)")
+    attn_ms, single_ms = eager_attention_times(model, a, spec, seed, Wm, total_steps)
+    attn_timing = ("CUDA events on the launching stream, eager pass over the same steps: after each step's "
+                   "forward its 12 attention launches run again back to back with an event between "
+                   "consecutive launches (the kernel plus the GPU's gap to the next launch)")
     del plans, batches
 
     # ---- end to end through the public API -----------------------------------------
@@ -484,6 +506,11 @@ def run_ours(args, world, rank, local):
                 "avg_launch_ms": avg_attn_ms,
                 "launches_timed": len(attn_ms),
                 "timing": attn_timing,
+                "single_launch_ms": sum(single_ms) / len(single_ms),
+                "single_launch_achieved": avg_bytes / (sum(single_ms) / len(single_ms) * 1e-3) / 1e9,
+                "single_launch_timing": "events around each attention launch inside the forward, each after "
+                                        "a device sleep: adds the GPU's launch and CTA start-up after an idle "
+                                        "stream",
                 "attention_ms_per_step": avg_attn_ms * cfg.n_layer,
             },  # fmt: skip
             "e2e": {
@@ -548,6 +575,67 @@ def cpu_oracle_rate(spec, n_seqs, steps, warmup, seed=2, budget_s=None):
     return rate, sample, threads
 
 
+# ------------------------------------------------------------------------------ config 5
+def run_serving(args, world, rank, local) -> dict | None:
+    """BASELINE config 5, shortened: the first --trace-requests requests of the
+    serving workload (prompts and outputs U[16,256], Poisson arrivals at
+    --rate req/s, or all at t=0 with --rate inf), round-robined over the
+    replicas, each replica an Engine with 16,384 KV slots (1,024 blocks of 16)
+    and CUDA-graph decode steps, driven open loop in real time."""
+    import math
+
+    from tokquay_b200 import BlockAllocator
+    from tokquay_b200.engine import Engine
+    from tokquay_b200.serving import make_workload, round_robin, run_trace, summarize
+
+    device = torch.device("cuda", local)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.set_float32_matmul_precision("highest")
+    model = make_model(device)
+    a = BlockAllocator(model.cfg, 1024, 16, device=device)
+    runner = model.use_cuda_graphs(a)
+    for b in runner.buckets:  # capture every decode graph the engine can use before the clock starts
+        if b <= 64:
+            runner.graph(b)
+    rate = math.inf if args.rate == "inf" else float(args.rate)
+    workload = make_workload(rate, args.trace_requests, seed=0)
+    mine = round_robin(workload, world, rank)
+    warm = Engine(model, a)
+    for spec in make_workload(math.inf, 8, seed=99, output_len=(4, 8)):  # warm the prefill shapes too
+        warm.add_request(list(spec.prompt_ids))
+    warm.run_until_done()
+    torch.cuda.synchronize(device)
+    eng = Engine(model, a)
+    barrier(world)
+    records, steps, wall = run_trace(eng, mine)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    out = summarize(records, steps)
+    tokens_all = sum_over_ranks(out["output_tokens"], world)
+    dur_max = max_over_ranks(out["duration_s"], world)
+    if rank != 0:
+        return None
+    return {
+        "metric": "serving tok/s (config 5 trace)",
+        "value": tokens_all / dur_max,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "higher_is_better": True,
+        "scaling": "weak" if math.isinf(rate) else "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"BASELINE config 5, first {args.trace_requests} requests at rate {args.rate} req/s "
+                               f"(seed 0), round-robin over {world} replica(s), 1,024 x 16 KV slots each",
+                   "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32, TF32 off",
+                   "parallelism": f"replicas{world}"},  # fmt: skip
+        "rank0": {k: out[k] for k in ("requests", "output_tokens", "duration_s", "throughput_tok_s", "ttft_ms",
+                                      "itl_ms", "latency_ms", "steps", "prefill_steps", "decode_step_ms")},
+        "preemptions_rank0": eng.stats.num_preemptions,
+        "wall_s_rank0": wall,
+    }
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return None
@@ -582,7 +670,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["cfg5"], default="cfg2")
+    ap.add_argument("--trace-requests", type=int, default=400, help="config 5: requests of the trace served")
+    ap.add_argument("--rate", default="64", help="config 5: arrival rate in requests/s, or inf for a burst")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graphs", action="store_true", help="launch every kernel from Python (no CUDA graphs)")
@@ -604,6 +694,12 @@ def main():
         return
     info = _replicas.setup()
     world, rank, local = info.world, info.rank, info.local
+    if args.workload == "cfg5":
+        res = run_serving(args, world, rank, local)
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+        _replicas.teardown(info)
+        return
     res = run_ours(args, world, rank, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, sample, threads = cpu_oracle_rate(workload_spec(args), 16, 2, 1)

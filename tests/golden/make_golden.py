@@ -20,6 +20,12 @@ Cases (reference test each one re-hosts, paths inside the Tokquay project):
   cfg3_bs16/32  BASELINE config 3: 4 prefills + 60 decodes in one step
   cfg2          BASELINE config 2 (first 3 of its 100 greedy steps), 2,048 blocks
   alloc_trace   random allocate / grow / free on a tiny allocator
+  sched_trace   three scheduler scenarios (burst with preemption, staggered
+                arrivals with aborts, a tight step budget) driven without a model
+  mini_engine   the reference Engine on the MINI model, waves of greedy requests
+                on a pool small enough to preempt (tokquay/engine.py)
+  workload      the reference benchmark's serving workload generator
+                (bench/workload.py:24-47) at three rates / seeds
 """
 
 from __future__ import annotations
@@ -459,6 +465,22 @@ def main() -> None:
         case["margins"] = margins
         meta["cases"]["mini_engine"] = case
         print(f"mini_engine {time.time() - t0:.1f}s, {k} steps")
+
+    # ---------------------------------------------------------------- serving workload
+    if want("workload"):
+        sys.path.insert(0, args.ref)
+        from bench.workload import make_workload  # the reference benchmark's generator
+
+        cases = []
+        for rate, n, seed in ((64.0, 60, 0), (float("inf"), 25, 3), (7.5, 40, 11)):
+            specs = make_workload(rate, n, seed)
+            cases.append({"rate": rate if rate != float("inf") else "inf", "n": n, "seed": seed,
+                          "arrivals": [r.arrival for r in specs], "output_lens": [r.output_len for r in specs],
+                          "prompt_lens": [len(r.prompt_ids) for r in specs],
+                          "prompt_heads": [list(r.prompt_ids[:4]) for r in specs],
+                          "prompt_sums": [sum(r.prompt_ids) for r in specs]})  # fmt: skip
+        meta["cases"]["workload"] = {"cases": cases}
+        print("workload done")
 
     json_path.write_text(json.dumps(meta, separators=(",", ":")))
     np.savez_compressed(npz_path, **arrays)
