@@ -54,11 +54,6 @@ class DecodeGraphRunner:
         i = bisect.bisect_left(self.buckets, n)
         return self.buckets[i] if i < len(self.buckets) else None
 
-    def accepts(self, allocator, seqs: list[Sequence], new_lens: list[int]) -> bool:
-        return (allocator is self.allocator and 0 < len(seqs) <= self.max_batch
-                and all(n == 1 for n in new_lens)
-                and max(s.num_cached_tokens for s in seqs) < self.max_ctx)  # fmt: skip
-
     def _capture(self, bucket: int):
         ws = PlanWorkspace(self.allocator, bucket, bucket, self.max_ctx)
         # A plan whose counts are all zero: every kernel of the step exits at
@@ -110,19 +105,13 @@ class DecodeGraphRunner:
         return logits[:B].clone()
 
     def run(self, seqs: list[Sequence]) -> torch.Tensor:
-        """Plan the decode step for ``seqs``, replay its bucket's graph, return
-        ``[B, vocab]`` logits (a copy).  Does not advance the sequences."""
-        B = len(seqs)
-        bucket = self.bucket_for(B)
-        if bucket is None:
-            raise ValueError(f"{B} sequences exceed the largest graph bucket {self.max_batch}")
-        graph, ws, logits, _, per_replay = self.graph(bucket)
-        ws.stage_sequences(seqs, [1] * B, torch.cuda.current_stream(self.allocator.pool.device),
-                           self.model.cfg.vocab_size)
-        self.model.last_h2d_bytes = ws.last_used_ints * 4
-        graph.replay()
-        self.model.kernel_launches += per_replay
-        return logits[:B].clone()
+        """``try_run`` for a step known to be a decode step that fits: ``[B, vocab]``
+        logits (a copy); ValueError otherwise.  Does not advance the sequences."""
+        logits = self.try_run(seqs)
+        if logits is None:
+            raise ValueError(f"not a decode step of at most {self.max_batch} sequences within "
+                             f"{self.max_ctx} positions")
+        return logits
 
     def replay_plan(self, bucket: int, plan: torch.Tensor, ids: torch.Tensor | None = None) -> torch.Tensor:
         """Replay ``bucket``'s graph on a plan already in device memory (built
