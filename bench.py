@@ -532,7 +532,20 @@ def run_ours(args, world, rank, local):
 # ------------------------------------------------------------------------------ CPU oracle
 def cpu_oracle_rate(spec, n_seqs, steps, warmup, seed=2, budget_s=None):
     """The numpy oracle (reference algorithm) on the host: decode steps over
-    ``n_seqs`` sequences of the workload.  Returns (tok/s, sample description, threads)."""
+    ``n_seqs`` sequences of the workload, with every host core (torchrun sets
+    OMP_NUM_THREADS=1 per rank; the reference arm runs on rank 0 alone).
+    Returns (tok/s, sample description, threads)."""
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:  # pragma: no cover
+        threadpool_limits = None
+    if threadpool_limits is not None:
+        with threadpool_limits(limits=os.cpu_count()):
+            return _cpu_oracle_rate(spec, n_seqs, steps, warmup, seed, budget_s)
+    return _cpu_oracle_rate(spec, n_seqs, steps, warmup, seed, budget_s)
+
+
+def _cpu_oracle_rate(spec, n_seqs, steps, warmup, seed, budget_s):
     import oracle
     from tokquay_b200 import BlockAllocator, GPT2Config, Sequence
     from tokquay_b200 import workloads as W
@@ -665,7 +678,22 @@ def run_reference(args, world, rank):
     }
 
 
+def _emit(res: dict) -> None:
+    """The one JSON line, on the process's real stdout (everything else --
+    library banners included -- goes to stderr)."""
+    os.write(_STDOUT_FD, (json.dumps(res) + "\n").encode())
+
+
+_STDOUT_FD = 1
+
+
 def main():
+    global _STDOUT_FD
+    # Keep stdout for the result line alone: NCCL and other libraries may
+    # print banners there during setup.
+    sys.stdout.flush()
+    _STDOUT_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
@@ -690,14 +718,14 @@ def main():
         world, rank, local = info.world, info.rank, info.local
         res = run_reference(args, world, rank)
         if rank == 0 and res is not None:
-            print(json.dumps(res), flush=True)
+            _emit(res)
         return
     info = _replicas.setup()
     world, rank, local = info.world, info.rank, info.local
     if args.workload == "cfg5":
         res = run_serving(args, world, rank, local)
         if rank == 0 and res is not None:
-            print(json.dumps(res), flush=True)
+            _emit(res)
         _replicas.teardown(info)
         return
     res = run_ours(args, world, rank, local)
@@ -706,7 +734,7 @@ def main():
         res["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
                                "sample": sample}  # fmt: skip
     if rank == 0 and res is not None:
-        print(json.dumps(res), flush=True)
+        _emit(res)
     _replicas.teardown(info)
 
 
