@@ -81,8 +81,9 @@ enum tq_plan_layout {
   TQ_PLAN_OFF_TOKEN_IDS = 14,/* [N] token ids (copied from token_ids, or 0) */
   TQ_PLAN_OFF_LAST_ROWS = 15,/* [B] row of each sequence's last new token */
   TQ_PLAN_OFF_ITEMS = 16,    /* the attention plan (tq_paged_attention's attn_plan), last region:
-                                [W][8] each warp's first work item, [W+1] (padded to 8) offsets of
-                                the other items, then those items [..][8], W = num_ctas * warps */
+                                [W][16] each warp's first work item and the block ids of its first
+                                chunk (-1 past them), [W+1] (padded to 8) offsets of the other
+                                items, then those items [..][8], W = num_ctas * warps */
   TQ_PLAN_OFF_COMBINE = 17,  /* [num_combine][4] rows whose keys are split across CTAs */
   TQ_PLAN_NUM_CTAS = 18,     /* CTAs the attention plan is cut for (its launch grid) */
   TQ_PLAN_USED_INTS = 19,    /* leading int32 of the plan this step uses (what must be copied) */

@@ -131,9 +131,9 @@ def _merge_kinds(batch) -> set[int]:
     plan = batch.plan.cpu().numpy()
     nw = batch.n_ctas * attention_warps()
     o = int(L[_lib.PLAN_OFF_ITEMS])
-    first = plan[o:o + 8 * nw].reshape(nw, 8)
-    offs = plan[o + 8 * nw:o + 9 * nw + 1]
-    ro = o + 8 * nw + (nw + 8) // 8 * 8
+    first = plan[o:o + 16 * nw].reshape(nw, 16)[:, :8]  # first items: 8 words + 8 block ids
+    offs = plan[o + 16 * nw:o + 17 * nw + 1]
+    ro = o + 16 * nw + (nw + 8) // 8 * 8
     rest = plan[ro:ro + 8 * int(offs[-1])].reshape(-1, 8)
     words = [w[2] for w in first if w[4] != 0] + [w[2] for w in rest]
     return {int(np.uint32(x)) >> 24 for x in words}

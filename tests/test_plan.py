@@ -18,6 +18,7 @@ from tokquay_b200 import _lib
 from tokquay_b200.kv_cache import MIN_SPLIT_CHUNKS, attention_chunk_keys, attention_warps, cdiv, plan_step_host
 
 N_HEAD = 3
+FIRST_WORDS = 16  # a warp's first item: 8 item words + the block ids of its first chunk
 KMAX_ROWS = 4
 # K (or V) rows one stage holds: the library's chunk size (checked in simulate_copies)
 
@@ -39,14 +40,16 @@ def attention_lists(plan, layout) -> list[list[dict]]:
     """Each warp slot's work items (decoded), from the attention region."""
     nw = int(layout[_lib.PLAN_NUM_CTAS]) * attention_warps()
     o = int(layout[_lib.PLAN_OFF_ITEMS])
-    first = np.asarray(plan[o:o + 8 * nw]).reshape(nw, 8)
-    offs = np.asarray(plan[o + 8 * nw:o + 8 * nw + nw + 1])
-    ro = o + 8 * nw + (nw + 1 + 7) // 8 * 8
+    first = np.asarray(plan[o:o + FIRST_WORDS * nw]).reshape(nw, FIRST_WORDS)
+    offs = np.asarray(plan[o + FIRST_WORDS * nw:o + FIRST_WORDS * nw + nw + 1])
+    ro = o + FIRST_WORDS * nw + (nw + 1 + 7) // 8 * 8
     rest = np.asarray(plan[ro:ro + 8 * int(offs[-1])]).reshape(-1, 8)
     lists = []
     for w in range(nw):
         if _u32(first[w][4]) >> 16:
-            lists.append([decode_item(first[w])] + [decode_item(x) for x in rest[offs[w]:offs[w + 1]]])
+            it = decode_item(first[w][:8])
+            it["first_blocks"] = [int(x) for x in first[w][8:]]
+            lists.append([it] + [decode_item(x) for x in rest[offs[w]:offs[w + 1]]])
         else:
             assert not first[w].any() and offs[w] == offs[w + 1]
             lists.append([])
@@ -101,6 +104,11 @@ def simulate_copies(p, bs, num_blocks):
     seen: dict[tuple[int, int], list[int]] = {}
     for it in p["items"]:
         seq, row0, nrows, pos0, cbeg, cend, h = (it[k] for k in ("seq", "row0", "nrows", "pos0", "cbeg", "cend", "head"))
+        if "first_blocks" in it:  # the first chunk's block ids travel with a warp's first item
+            key0, key_end = cbeg * ATTN_CHUNK, min(cbeg * ATTN_CHUNK + ATTN_CHUNK, pos0 + nrows)
+            kb = list(range(key0 // bs, (key_end - 1) // bs + 1))
+            want = [int(p["tables"][seq][b]) for b in kb][:FIRST_WORDS - 8]
+            assert it["first_blocks"] == want + [-1] * (FIRST_WORDS - 8 - len(want))
         assert 1 <= nrows <= KMAX_ROWS and cbeg < cend
         ctx = int(p["seq"][seq][3])
         need = cdiv(ctx, bs)
@@ -223,8 +231,8 @@ def test_plan_matches_oracle_and_covers_every_key_once(bs, seed):
     # The used prefix holds everything the step reads.
     o = int(layout[_lib.PLAN_OFF_ITEMS])
     nw = n_ctas * attention_warps()
-    n_rest = int(plan[o + 8 * nw + nw])
-    assert layout[_lib.PLAN_USED_INTS] == o + 8 * nw + (nw + 8) // 8 * 8 + 8 * n_rest
+    n_rest = int(plan[o + FIRST_WORDS * nw + nw])
+    assert layout[_lib.PLAN_USED_INTS] == o + FIRST_WORDS * nw + (nw + 8) // 8 * 8 + 8 * n_rest
     assert layout[_lib.PLAN_USED_INTS] <= layout[_lib.PLAN_TOTAL_INTS] == plan.size
 
 

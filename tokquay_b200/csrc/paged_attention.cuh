@@ -189,15 +189,18 @@ __device__ __forceinline__ WorkItem item_from_lanes(int v) {
 }
 
 // Word `lane` (lanes 0..7) of item k of warp slot `ws`: k == 0 is the warp's
-// first item, at a fixed place, so its load needs no offset; items k >= 1
-// follow the warp's offset r0 in the list of the others.
-__device__ __forceinline__ const int* warp_offsets(const AttnParams& p) { return p.attn + 8 * p.n_warps; }
+// first item, at a fixed place (kFirstWords words: the item, then the block
+// ids of its first chunk), so its load needs no offset; items k >= 1 follow
+// the warp's offset r0 in the list of the others.
+constexpr int kFirstWords = 16;
+constexpr int kFirstBlocks = kFirstWords - 8;
+__device__ __forceinline__ const int* warp_offsets(const AttnParams& p) { return p.attn + kFirstWords * p.n_warps; }
 __device__ __forceinline__ const int* other_items(const AttnParams& p) {
-  return p.attn + 8 * p.n_warps + ((p.n_warps + 1 + 7) & ~7);
+  return p.attn + kFirstWords * p.n_warps + ((p.n_warps + 1 + 7) & ~7);
 }
 __device__ __forceinline__ int item_lane_load(const AttnParams& p, int ws, int r0, int k, int count, int lane) {
   if (k >= count || lane >= 8) return 0;
-  const int* src = k == 0 ? p.attn + 8 * (size_t)ws : other_items(p) + 8 * (size_t)(r0 + k - 1);
+  const int* src = k == 0 ? p.attn + kFirstWords * (size_t)ws : other_items(p) + 8 * (size_t)(r0 + k - 1);
   return __ldg(src + lane);
 }
 
@@ -504,7 +507,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
   const int H = p.n_head;
   const int ws = blockIdx.x * kAttnWarps + pair;
   // The first item sits at a fixed place: its load and the offsets' load go out together.
-  const int first_word = lane < 8 ? __ldg(p.attn + 8 * (size_t)ws + lane) : 0;
+  const int first_word = lane < kFirstWords ? __ldg(p.attn + kFirstWords * (size_t)ws + lane) : 0;
   const int r0 = __ldg(warp_offsets(p) + ws), r1 = __ldg(warp_offsets(p) + ws + 1);
   const bool has_work = ((unsigned)__shfl_sync(kFullMask, first_word, 4) >> 16) != 0;  // cend != 0
   const int count = has_work ? 1 + r1 - r0 : 0;
@@ -533,6 +536,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
     int p_chunk = p_it.cbeg();
     int pf_a = 0, pf_b = 0;  // current item's block ids
     int nx_a = 0, nx_b = 0;  // next item's block ids (in flight)
+    // The first chunk's block ids came with the item (lane j: block j), so
+    // its copies go out now; the item's whole list loads meanwhile.
+    const int first_ids = __shfl_sync(kFullMask, first_word, 8 + (lane & (kFirstBlocks - 1)));
+    int full_a = 0, full_b = 0;
     auto load_item_blocks = [&](const WorkItem& w, bool valid, int& a, int& b) {
       if (!valid) return;
       const int kb0 = (w.cbeg() * kChunk) >> p.log2_bs;
@@ -542,7 +549,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
       a = lane < n ? __ldg(tbl + lane) : 0;
       b = lane + 32 < n ? __ldg(tbl + 32 + lane) : 0;
     };
-    load_item_blocks(p_it, true, pf_a, pf_b);
+    load_item_blocks(p_it, true, full_a, full_b);
+    const bool inline_first = chunk_span(p, p_it, p_chunk).nblk <= kFirstBlocks;  // warp-uniform
+    if (inline_first) {
+      pf_a = lane < kFirstBlocks ? first_ids : 0;
+    } else {
+      pf_a = full_a;
+      pf_b = full_b;
+    }
     WorkItem nx_it = item_from_lanes(item_lane_load(p, ws, r0, 1, count, lane));
     load_item_blocks(nx_it, 1 < count, nx_a, nx_b);
     int nx2_word = item_lane_load(p, ws, r0, 2, count, lane);
@@ -644,7 +658,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
         if (bytes) bulk_copy_g2s(dst, src, bytes, bar);
       }
       TQ_TRACE(if (lane == 0) tr_sub[1] += clock64() - ti0; ti0 = clock64();)
-      ++issued;
+      if (++issued == 1 && inline_first) {  // from the second chunk on: the loaded list
+        pf_a = full_a;
+        pf_b = full_b;
+      }
 
       // Advance the cursor.
       if (++p_chunk == p_it.cend()) {

@@ -47,6 +47,10 @@ constexpr int kFlagGlobal = 2;  // keys split across CTAs: merged through the sp
 // Shared-memory partial slots one CTA holds (each warp boundary cuts at most
 // one pair, so a CTA needs at most 2 * (kWarps - 1) * kMaxRows).
 constexpr int kLocalSlots = 2 * (kWarps - 1) * kMaxRows;
+// A warp's first work item (at a fixed place in the plan) carries the block
+// ids of its first chunk, so the kernel's first copies need no table lookup.
+constexpr int kFirstWords = 16;   // 8 item words + up to kFirstBlocks block ids
+constexpr int kFirstBlocks = kFirstWords - 8;
 
 inline int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t align4(int64_t n) { return (n + 3) & ~int64_t(3); }
@@ -279,7 +283,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   const int64_t o_comb = take(dim_comb * 4);
   // The attention plan goes last, so a step copies only its used prefix.
   const int64_t o_items = off;
-  const int64_t o_ranges = o_items + 8 * n_warps;
+  const int64_t o_ranges = o_items + kFirstWords * n_warps;
   const int64_t o_rest = o_ranges + align8(n_warps + 1);
   const int64_t total = o_rest + 8 * dim_rest;
   if (total > INT32_MAX) return set_error(TQ_ERR_UNSUPPORTED, "step too large to plan");
@@ -335,7 +339,14 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
         const int64_t lo = std::max(x, bnd[w]) - x, hi = std::min(x + len, bnd[w + 1]) - x;
         if (hi <= lo) continue;
         while (cur < w) ranges[wbase + (++cur)] = (int32_t)rest;  // entering warp w
-        int32_t* const it = has[w] ? rest_items + 8 * rest++ : first_items + 8 * (wbase + w);
+        int32_t* const it = has[w] ? rest_items + 8 * rest++ : first_items + kFirstWords * (wbase + w);
+        if (!has[w]) {  // block ids of the first chunk, -1 past them
+          const int64_t key0 = (pc.cbeg + lo) * kChunk;
+          const int64_t key_end = std::min<int64_t>(key0 + kChunk, g.pos0 + g.nrows);
+          const int64_t kb0 = key0 / block_size, kb_end = (key_end - 1) / block_size + 1;
+          const int32_t* tbl = table_data + table_offsets[g.seq];
+          for (int j = 0; j < kFirstBlocks; ++j) it[8 + j] = kb0 + j < kb_end ? tbl[kb0 + j] : -1;
+        }
         has[w] = true;
         it[0] = g.seq;
         it[1] = g.row0;
@@ -353,7 +364,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     }
     while (cur < kWarps - 1) ranges[wbase + (++cur)] = (int32_t)rest;
     for (int w = 0; w < kWarps; ++w)  // a warp without work: an all-zero first item
-      if (!has[w]) std::memset(first_items + 8 * (wbase + w), 0, 8 * sizeof(int32_t));
+      if (!has[w]) std::memset(first_items + kFirstWords * (wbase + w), 0, kFirstWords * sizeof(int32_t));
   }
   ranges[n_warps] = (int32_t)rest;
   std::memset(ranges + n_warps + 1, 0, sizeof(int32_t) * (align8(n_warps + 1) - (n_warps + 1)));
