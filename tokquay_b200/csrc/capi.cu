@@ -136,6 +136,23 @@ int attention_params(float* out, int64_t out_row_stride, const float* q, int64_t
   return TQ_OK;
 }
 
+// The attention launch, as a programmatic dependent of the kernel before it
+// in the stream: its CTAs may start (barriers, work items, block ids) while
+// that kernel finishes; its producers wait for it before the first copy.
+cudaError_t launch_attention(const AttnParams& p, int n_ctas, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_ctas);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = kAttnSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, paged_attention_kernel, p);
+}
+
 int check_embd(int32_t n_embd) {
   if (n_embd < 128 || n_embd > 1024 || n_embd % 128 != 0)
     return set_error(TQ_ERR_UNSUPPORTED, "n_embd must be a multiple of 128 in [128, 1024], got %d",
@@ -289,7 +306,8 @@ int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64
   p.part_acc = partial_acc;
   p.part_cnt = partial_counters;
   p.max_partials = max_partials;
-  paged_attention_kernel<<<n_ctas, kAttnThreads, kAttnSmemBytes, (cudaStream_t)stream>>>(p);
+  const cudaError_t e = launch_attention(p, n_ctas, (cudaStream_t)stream);
+  if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "paged_attention launch: %s", cudaGetErrorString(e));
   return check_launch("paged_attention");
 }
 
@@ -378,7 +396,8 @@ int tq_paged_attention_noalloc(float* out, int64_t out_row_stride, const float* 
   p.part_ml = reinterpret_cast<float*>(base + kNoAllocCounterBytes);
   p.part_acc = reinterpret_cast<float*>(base + kNoAllocCounterBytes + kNoAllocMlBytes);
   p.max_partials = num_partials;
-  paged_attention_kernel<<<n_ctas, kAttnThreads, kAttnSmemBytes, s>>>(p);
+  const cudaError_t e = launch_attention(p, n_ctas, s);
+  if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "paged_attention launch: %s", cudaGetErrorString(e));
   return check_launch("paged_attention_noalloc");
 }
 
@@ -516,10 +535,10 @@ int tq_argmax_rows(const float* x, int64_t row_stride, int32_t n_cols, int64_t* 
   int sms = 0;
   const int st = device_setup(&sms);
   if (st) return st;
-  const int threads = n_cols >= 1024 * 8 ? 1024 : 256;
-  argmax_rows_kernel<<<row_grid(max_rows, sms), threads, 0, (cudaStream_t)stream>>>(x, row_stride, n_cols,
-                                                                                     reinterpret_cast<long long*>(out),
-                                                                                     d_num_rows);
+  if ((int64_t)max_rows * kArgmaxSlices > INT32_MAX)
+    return set_error(TQ_ERR_UNSUPPORTED, "argmax_rows: too many rows");
+  argmax_rows_kernel<<<max_rows * kArgmaxSlices, kArgmaxThreads, 0, (cudaStream_t)stream>>>(
+      x, row_stride, n_cols, reinterpret_cast<long long*>(out), d_num_rows);
   return check_launch("argmax_rows");
 }
 

@@ -94,6 +94,14 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
       : "memory");
 }
 
+// Programmatic dependent launch.  launch_dependents: the next kernel in the
+// stream, if launched with programmatic stream serialization, may start its
+// CTAs (as resources free up) before this grid finishes.  wait: block until
+// the preceding grid has completed and its memory is visible (returns at once
+// when this kernel was not launched as a programmatic dependent).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Orders this thread's earlier generic-proxy shared-memory accesses before
 // later async-proxy (TMA) accesses to the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -16,6 +16,8 @@
 // (two-pass mean / variance over the values held in registers, no re-read).
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace tq {
@@ -225,58 +227,85 @@ __device__ __forceinline__ void argmax_take(float& v, int& i, float v2, int i2) 
   }
 }
 
-// One block per row, threads striding over the columns (coalesced loads;
-// rows of odd length are not 16-byte aligned), then warp and block reductions.
-__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restrict__ x, long long stride, int n_cols,
-                                                           long long* __restrict__ out, const int* n_rows) {
-  __shared__ float sv[32];
-  __shared__ int si[32];
-  const int n = *n_rows;
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int r = blockIdx.x; r < n; r += gridDim.x) {
+// A cluster of kArgmaxSlices CTAs per row: CTA k scans slice k of the
+// columns (coalesced loads, kArgmaxUnroll in flight per thread; rows of odd
+// length are not 16-byte aligned), reduces it over its warps, and CTA 0 of the
+// cluster combines the slices' results through distributed shared memory.
+// Slices are in column order and every reduction keeps the first of equal
+// values, so ties resolve as a left-to-right scan would.
+constexpr int kArgmaxSlices = 8;
+constexpr int kArgmaxThreads = 1024;
+constexpr int kArgmaxUnroll = 8;
+
+__device__ __forceinline__ void argmax_warp(float& v, int& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v2 = __shfl_xor_sync(kFullMask, v, o);
+    const int i2 = __shfl_xor_sync(kFullMask, i, o);
+    argmax_take(v, i, v2, i2);
+  }
+}
+
+__global__ void __cluster_dims__(kArgmaxSlices, 1, 1) __launch_bounds__(kArgmaxThreads)
+    argmax_rows_kernel(const float* __restrict__ x, long long stride, int n_cols, long long* __restrict__ out,
+                       const int* n_rows) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ float sv[kArgmaxThreads / 32];
+  __shared__ int si[kArgmaxThreads / 32];
+  __shared__ float slice_v;
+  __shared__ int slice_i;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int r = blockIdx.x / kArgmaxSlices;  // cluster-uniform
+  const int k = (int)cluster.block_rank();
+  const bool live = r < *n_rows;
+  if (live) {
+    const int per = (n_cols + kArgmaxSlices - 1) / kArgmaxSlices;
+    const int c_lo = k * per, c_hi = min(n_cols, c_lo + per);
     const float* row = x + (size_t)r * stride;
     float v = -INFINITY;
     int i = 0x7fffffff;
-    // kArgmaxUnroll loads in flight per thread before the comparisons; a
-    // thread's columns still come in increasing order, so ties keep the first.
-    constexpr int kArgmaxUnroll = 8;
-    for (int c0 = threadIdx.x; c0 < n_cols; c0 += kArgmaxUnroll * blockDim.x) {
+    for (int c0 = c_lo + (int)threadIdx.x; c0 < c_hi; c0 += kArgmaxUnroll * kArgmaxThreads) {
       float u[kArgmaxUnroll];
 #pragma unroll
-      for (int k = 0; k < kArgmaxUnroll; ++k) {
-        const int c = c0 + k * blockDim.x;
-        u[k] = c < n_cols ? __ldg(row + c) : -INFINITY;
+      for (int j = 0; j < kArgmaxUnroll; ++j) {
+        const int c = c0 + j * kArgmaxThreads;
+        u[j] = c < c_hi ? __ldg(row + c) : -INFINITY;
       }
 #pragma unroll
-      for (int k = 0; k < kArgmaxUnroll; ++k) {
-        const int c = c0 + k * blockDim.x;
-        if (c < n_cols) argmax_take(v, i, u[k], c);
+      for (int j = 0; j < kArgmaxUnroll; ++j) {
+        const int c = c0 + j * kArgmaxThreads;
+        if (c < c_hi) argmax_take(v, i, u[j], c);
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float v2 = __shfl_xor_sync(kFullMask, v, o);
-      const int i2 = __shfl_xor_sync(kFullMask, i, o);
-      argmax_take(v, i, v2, i2);
-    }
+    argmax_warp(v, i);
     if (lane == 0) {
       sv[w] = v;
       si[w] = i;
     }
     __syncthreads();
     if (w == 0) {
-      v = lane < nw ? sv[lane] : -INFINITY;
-      i = lane < nw ? si[lane] : 0x7fffffff;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float v2 = __shfl_xor_sync(kFullMask, v, o);
-        const int i2 = __shfl_xor_sync(kFullMask, i, o);
-        argmax_take(v, i, v2, i2);
+      v = lane < kArgmaxThreads / 32 ? sv[lane] : -INFINITY;
+      i = lane < kArgmaxThreads / 32 ? si[lane] : 0x7fffffff;
+      argmax_warp(v, i);
+      if (lane == 0) {
+        slice_v = v;
+        slice_i = i;
       }
-      if (lane == 0) out[r] = i;
     }
-    __syncthreads();  // sv / si are reused by the next row
   }
+  cluster.sync();  // every slice's result is in its CTA's shared memory
+  if (live && k == 0 && w == 0) {
+    float v = -INFINITY;
+    int i = 0x7fffffff;
+    if (lane < kArgmaxSlices) {
+      v = *cluster.map_shared_rank(&slice_v, lane);
+      i = *cluster.map_shared_rank(&slice_i, lane);
+    }
+    argmax_warp(v, i);
+    if (lane == 0) out[r] = i;
+  }
+  cluster.sync();  // no CTA leaves while CTA 0 may still read its shared memory
 }
 
 }  // namespace tq

@@ -75,6 +75,7 @@ struct QkvWriteParams {
 // Summation order matches the unfused path (bias_gelu_kernel): ((p0 + p1) + ...) + bias.
 template <int NP>
 __global__ void __launch_bounds__(1024) qkv_bias_kv_write_kernel(const QkvWriteParams p) {
+  pdl_launch_dependents();  // the attention that follows may start its prologue now
   const int n = *p.n_rows;
   const int C4 = p.n_head * 16;  // float4 per q (or K, or V) row
   const int t = threadIdx.x;

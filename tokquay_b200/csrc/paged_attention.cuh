@@ -514,6 +514,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
   TQ_TRACE(const int gw = ws; unsigned long long* trec = g_attn_trace + (size_t)gw * kTraceSlots;
            long long tr_sub[8] = {0, 0, 0, 0, 0, 0, 0, 0};)
 
+  pdl_launch_dependents();  // a following dependent launch may stage its own prologue
+
   if (!producer && lane == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(full0 + 8 * s, 1);   // the producer's arrive_expect_tx + the copies' bytes
@@ -562,6 +564,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
     int nx2_word = item_lane_load(p, ws, r0, 2, count, lane);
     int issued = 0;
     bool ok = true;
+    // Launched as a programmatic dependent (after the kernel that wrote q and
+    // this step's K/V), everything above overlapped that kernel; the copies
+    // wait for it.  Consumers read only what these copies bring.
+    pdl_wait();
 
     for (;;) {
       const int s = issued % kStages;
