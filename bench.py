@@ -269,13 +269,16 @@ def attn_bytes(ctx_list, n_head, d, num_partials):
 
 
 # ------------------------------------------------------------------------------ attention timing
-def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> tuple[list[float], list[float]]:
-    """Attention times (ms) over the same steps, eager, two ways:
+def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> tuple[list[float], list[float], list[float]]:
+    """Attention times (ms per launch) over the same steps, eager, three ways:
 
-    * burst: after each step's forward, its 12 attention launches again back to
-      back, an event between consecutive launches (each interval is one
-      launch as a stream of launches runs it: the kernel plus the GPU's gap to
-      the next);
+    * stream: after each step's forward, its 12 attention launches (one per
+      layer) again back to back, one event before the first and one after the
+      last; the interval / 12 is one launch as a stream of launches runs it
+      (the kernel plus the GPU's gap to the next launch);
+    * evented: the same 12 launches with an event between consecutive launches
+      (each interval one launch; a timing event between two launches also
+      keeps the GPU from starting the next launch before it is recorded);
     * single: events around each attention launch inside the forward itself,
       each after a device sleep, so the interval also holds the GPU's launch
       and CTA start-up of a kernel that follows an idle stream."""
@@ -286,6 +289,7 @@ def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> tuple[li
     B = len(seqs)
     pairs: list = []
     bursts: list = []
+    streams: list = []
     C = model.cfg.n_embd
     q = torch.randn(B, C, device=a.pool.device, generator=torch.Generator(a.pool.device).manual_seed(0))
     out = torch.empty_like(q)
@@ -305,14 +309,24 @@ def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> tuple[li
                 torch.cuda.synchronize()
                 pairs.clear()
                 bursts.clear()
+                streams.clear()
             model.attention_timer = timer
             model.forward_paged(b, last_only=True)
             model.attention_timer = None
+            L = model.cfg.n_layer
+            sid = torch.cuda.current_stream().cuda_stream
+            torch.cuda._sleep(1_000_000)  # ~0.5 ms: the host queues all 12 launches before the first runs
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record()
+            for layer in range(L):
+                b.attend_rows(layer, q, out, sid)
+            g1.record()
+            streams.append((g0, g1, L))
             torch.cuda._sleep(200_000)
-            evs = [torch.cuda.Event(enable_timing=True) for _ in range(model.cfg.n_layer + 1)]
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(L + 1)]
             evs[0].record()
-            for layer in range(model.cfg.n_layer):
-                b.attend_rows(layer, q, out, torch.cuda.current_stream().cuda_stream)
+            for layer in range(L):
+                b.attend_rows(layer, q, out, sid)
                 evs[layer + 1].record()
             bursts.append(evs)
             if spec["grow"]:
@@ -323,8 +337,9 @@ def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> tuple[li
         torch.cuda.synchronize()
     finally:
         model.attention_timer = None
-    burst = [e0.elapsed_time(e1) for evs in bursts for e0, e1 in zip(evs, evs[1:])]
-    return burst, [e0.elapsed_time(e1) for e0, e1 in pairs]
+    stream_ms = [g0.elapsed_time(g1) / n for g0, g1, n in streams for _ in range(n)]
+    evented = [e0.elapsed_time(e1) for evs in bursts for e0, e1 in zip(evs, evs[1:])]
+    return stream_ms, evented, [e0.elapsed_time(e1) for e0, e1 in pairs]
 
 
 # ------------------------------------------------------------------------------ our arm
@@ -412,10 +427,11 @@ def run_ours(args, world, rank, local):
     # keeping host launch latency out of the interval.
     bytes_per_launch = [attn_bytes(ctx_per_step[k], cfg.n_head, cfg.d_head, nparts_per_step[k])
                         for k in range(Wm, total_steps) for _ in range(cfg.n_layer)]  # fmt: skip
-    attn_ms, single_ms = eager_attention_times(model, a, spec, seed, Wm, total_steps)
+    attn_ms, evented_ms, single_ms = eager_attention_times(model, a, spec, seed, Wm, total_steps)
     attn_timing = ("CUDA events on the launching stream, eager pass over the same steps: after each step's "
-                   "forward its 12 attention launches run again back to back with an event between "
-                   "consecutive launches (the kernel plus the GPU's gap to the next launch)")
+                   "forward its 12 attention launches (one per layer) run again back to back between two "
+                   "events; average launch = the interval / 12 (the kernel plus the GPU's gap to the next "
+                   "launch)")
     del plans, batches
 
     # ---- end to end through the public API -----------------------------------------
@@ -506,6 +522,10 @@ def run_ours(args, world, rank, local):
                 "avg_launch_ms": avg_attn_ms,
                 "launches_timed": len(attn_ms),
                 "timing": attn_timing,
+                "evented_launch_ms": sum(evented_ms) / len(evented_ms),
+                "evented_launch_achieved": avg_bytes / (sum(evented_ms) / len(evented_ms) * 1e-3) / 1e9,
+                "evented_launch_timing": "the same launches with an event between consecutive ones: each "
+                                         "event also holds back the next launch until it is recorded",
                 "single_launch_ms": sum(single_ms) / len(single_ms),
                 "single_launch_achieved": avg_bytes / (sum(single_ms) / len(single_ms) * 1e-3) / 1e9,
                 "single_launch_timing": "events around each attention launch inside the forward, each after "
@@ -588,6 +608,206 @@ def _cpu_oracle_rate(spec, n_seqs, steps, warmup, seed, budget_s):
     return rate, sample, threads
 
 
+# ------------------------------------------------------------------------------ config 3
+def mixed_case(a, seed):
+    """BASELINE config 3 on allocator ``a``: 4 fresh prompts (U[16,256], start 0)
+    and 60 decoding sequences (contexts U[16,256]) in a seeded interleaved order."""
+    from tokquay_b200 import Sequence
+    from tokquay_b200 import workloads as W
+
+    c = W.CONFIGS[3]
+    reset_allocator(a)
+    return W.mixed_case(Sequence, a, c["n_prefill"], c["n_decode"], c["len_range"], a.cfg.vocab_size, seed=seed)
+
+
+def run_mixed(args, world, rank, local) -> dict | None:
+    """one mixed step -- 4 prompts prefilled from position 0
+    next to 60 decode rows -- through the paged forward, one attention launch
+    per layer covering the causal prefill rows and the decode rows together.
+    A step is that forward (+ greedy argmax) over the same batch again: every
+    sequence's cached count goes back, so each step writes the same K/V rows
+    and reads the same contexts.  ``value`` is the query rows (prompt tokens +
+    decode tokens) processed per second."""
+    from tokquay_b200 import BlockAllocator, paged_forward
+    from tokquay_b200.kv_cache import DevicePagedBatch
+    from tokquay_b200.model import argmax_rows
+
+    device = torch.device("cuda", local)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.set_float32_matmul_precision("highest")
+    model = make_model(device)
+    cfg = model.cfg
+    bs = args.block_size or 16
+    a = BlockAllocator(cfg, 1024, bs, device=device)
+    a.pool.normal_(generator=torch.Generator(device=device).manual_seed(1234))  # BASELINE: pool N(0, 1)
+    seed = replica_seed(3, rank)
+    case = mixed_case(a, seed)
+    seqs, new_lens = case.seqs, case.new_lens
+    starts = [s.num_cached_tokens for s in seqs]
+    ids = [t for s, st, n in zip(seqs, starts, new_lens) for t in s.tokens_slice(st, st + n)]
+    batch = DevicePagedBatch(a, [list(s.block_table) for s in seqs], starts, new_lens, ids)
+    N, B = batch.N, batch.B
+    K, Wm = args.steps, args.warmup
+
+    def device_step():
+        logits = model.forward_paged(batch, last_only=True)[:, 0]
+        return argmax_rows(logits)
+
+    for _ in range(Wm):
+        device_step()
+    torch.cuda.synchronize(device)
+    launches0 = model.kernel_launches
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(K):
+            device_step()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    launches = model.kernel_launches - launches0 + K  # + one argmax per step
+    ms_max = max_over_ranks(ms, world)
+    rows_all = sum_over_ranks(N * K, world)
+
+    # Attention alone: each timed step's 12 launches again, back to back between two events.
+    q = torch.randn(N, cfg.n_embd, device=device, generator=torch.Generator(device).manual_seed(0))
+    out = torch.empty_like(q)
+    sid = stream.cuda_stream
+    groups = []
+    for k in range(Wm + K):
+        torch.cuda._sleep(1_000_000)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for layer in range(cfg.n_layer):
+            batch.attend_rows(layer, q, out, sid)
+        g1.record(stream)
+        if k >= Wm:
+            groups.append((g0, g1))
+    torch.cuda.synchronize(device)
+    attn_ms = sum(g0.elapsed_time(g1) for g0, g1 in groups) / (len(groups) * cfg.n_layer)
+    ctx = [st + n for st, n in zip(starts, new_lens)]
+    abytes = attn_bytes(ctx, cfg.n_head, cfg.d_head, batch.num_partials) + (N - B) * cfg.n_head * cfg.d_head * 4 * 2
+
+    # End to end: the public API with host planning and the plan copy inside.
+    def api_step():
+        toks = argmax_rows(paged_forward(model, a, seqs, new_lens)).tolist()
+        for s, st in zip(seqs, starts):
+            s.num_cached_tokens = st
+        return toks
+
+    for _ in range(Wm):
+        api_step()
+    torch.cuda.synchronize(device)
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    h0.record(stream)
+    for _ in range(K):
+        api_step()
+    h1.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    e2e_ms_max = max_over_ranks(h0.elapsed_time(h1), world)
+    h2d_bytes = model.last_h2d_bytes
+    if rank != 0:
+        return None
+    peaks = json.loads(PEAKS_PATH.read_text()) if PEAKS_PATH.exists() else {}
+    peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
+    achieved = abytes / (attn_ms * 1e-3) / 1e9
+    n_prefill = sum(1 for n in new_lens if n > 1)
+    return {
+        "metric": "mixed prefill+decode step rows/s",
+        "value": rows_all / (ms_max * 1e-3),
+        "unit": "rows/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": Wm,
+        "ms_per_step": ms_max / K,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {
+            "workload": f"BASELINE config 3: {n_prefill} prompts U[16,256] prefilled + {B - n_prefill} decodes, "
+                        f"ctx U[16,256], bs {bs}, 1024 blocks, one mixed paged forward per step",
+            "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32, TF32 off",
+            "rows_per_step": N,
+            "sequences": B,
+            "block_size": bs,
+            "parallelism": f"replicas{world} (one engine + KV pool per GPU, no collective)",
+            "cuda_graphs": False,
+            "l2": "each step reads the whole weight set (0.5 GB, larger than L2)",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "paged_attention_kernel (causal prefill + decode rows, one launch per layer)",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": None,
+            "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
+            "algorithmic_bytes_per_launch": abytes,
+            "avg_launch_ms": attn_ms,
+            "timing": "CUDA events on the launching stream: each timed step's 12 attention launches back to back "
+                      "between two events, average launch = the interval / 12; algorithmic bytes = every "
+                      "sequence's K/V rows read once + q read + output written",
+        },
+        "e2e": {
+            "value": rows_all / (e2e_ms_max * 1e-3),
+            "unit": "rows/s",
+            "h2d_bytes_per_step": h2d_bytes,
+            "d2h_bytes_per_step": B * 8,
+            "ms_per_step": e2e_ms_max / K,
+        },
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+    }
+
+
+def cpu_oracle_mixed_rate(bs: int, reps: int, seed: int) -> tuple[float, str, int]:
+    """The numpy oracle on config 3's mixed step (every host core)."""
+    import oracle
+    from tokquay_b200 import BlockAllocator, GPT2Config
+    from tokquay_b200 import workloads as W
+
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+    except ImportError:  # pragma: no cover
+        threadpool_limits = threadpool_info = None
+    cfg = GPT2Config(**W.GPT2_SMALL)
+    rng = np.random.default_rng(0)
+    weights = {n: (rng.standard_normal(s, dtype=np.float32) * np.float32(0.02)) for n, s in W.param_specs(cfg)}
+    a = BlockAllocator(cfg, 1024, bs, device="cpu")  # bookkeeping only
+    a.pool = torch.empty(0)
+    case = mixed_case(a, seed)
+    pool = np.zeros((1024, cfg.n_layer, 2, cfg.n_head, bs, cfg.d_head), np.float32)
+    starts = [s.num_cached_tokens for s in case.seqs]
+    times = []
+    ctx = threadpool_limits(limits=os.cpu_count()) if threadpool_limits else None
+    if ctx:
+        ctx.__enter__()
+    try:
+        for _ in range(reps):  # ~20-40 s per step: the oracle pads every row to the longest prompt
+            t0 = time.perf_counter()
+            oracle.paged_forward(weights, cfg, pool, bs, case.seqs, case.new_lens)
+            times.append(time.perf_counter() - t0)
+            for s, st in zip(case.seqs, starts):
+                s.num_cached_tokens = st
+        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=1) if threadpool_info else 1
+    finally:
+        if ctx:
+            ctx.__exit__(None, None, None)
+    rows = sum(case.new_lens)
+    sample = f"{len(times)} mixed steps of BASELINE config 3 ({rows} rows, bs {bs}; numpy oracle, float32)"
+    return rows * len(times) / sum(times), sample, threads
+
+
 # ------------------------------------------------------------------------------ config 5
 def run_serving(args, world, rank, local) -> dict | None:
     """BASELINE config 5, shortened: the first --trace-requests requests of the
@@ -652,6 +872,21 @@ def run_serving(args, world, rank, local) -> dict | None:
 def run_reference(args, world, rank):
     if rank != 0:
         return None
+    if args.workload == "cfg3":
+        bs = args.block_size or 16
+        t0 = time.perf_counter()
+        rate, sample, threads = cpu_oracle_mixed_rate(bs, max(1, min(args.steps, 3)), replica_seed(3, 0))
+        return {"impl": "reference", "metric": "mixed prefill+decode step rows/s", "value": rate, "unit": "rows/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": f"BASELINE config 3 mixed step, bs {bs}",
+                           "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32"},
+                "cpu_baseline": {"value": rate, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample},
+                "e2e": {"value": rate, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "wall_s": time.perf_counter() - t0}  # fmt: skip
+    if args.workload == "cfg5":
+        return {"impl": "reference", "unavailable": "config 5 serves a live trace through an engine; the CPU "
+                                                    "reference arm times decode and mixed steps only"}  # fmt: skip
     spec = workload_spec(args)
     # Each step is a bounded sample: a decode step over a subset of the sequences.
     n = min(spec["n_seqs"], 16)
@@ -698,7 +933,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["cfg5"], default="cfg2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["cfg3", "cfg5"], default="cfg2")
+    ap.add_argument("--block-size", type=int, default=0, help="config 3: block size (16 or 32; default 16)")
     ap.add_argument("--trace-requests", type=int, default=400, help="config 5: requests of the trace served")
     ap.add_argument("--rate", default="64", help="config 5: arrival rate in requests/s, or inf for a burst")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -724,6 +960,16 @@ def main():
     world, rank, local = info.world, info.rank, info.local
     if args.workload == "cfg5":
         res = run_serving(args, world, rank, local)
+        if rank == 0 and res is not None:
+            _emit(res)
+        _replicas.teardown(info)
+        return
+    if args.workload == "cfg3":
+        res = run_mixed(args, world, rank, local)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline and res is not None:
+            rate, sample, threads = cpu_oracle_mixed_rate(args.block_size or 16, 1, replica_seed(3, 0))
+            res["cpu_baseline"] = {"value": rate, "unit": "rows/s", "cores": threads, "kind": "port",
+                                   "sample": sample}  # fmt: skip
         if rank == 0 and res is not None:
             _emit(res)
         _replicas.teardown(info)
