@@ -16,8 +16,9 @@ the max over ranks; ``value`` is the tokens of all ranks over that time.
 Reported on one JSON line (rank 0):
   value        device-resident loop: step plans already in HBM, each step's
                input tokens are the previous step's argmax (CUDA events)
-  e2e          the public API: ``paged_forward`` + argmax + ``.tolist()`` per
-               step, host planning and the pinned host->device plan copy inside
+  e2e          the public API: ``paged_greedy_step`` per step (host planning,
+               the pinned host->device plan copy, the graph replay, the greedy
+               tokens back to the host)
   roofline     the paged-attention kernel (+ its split-K combine): algorithmic
                bytes (K/V rows read + q read + output write + split scratch) per
                launch over its CUDA-event duration, vs the measured HBM copy peak
@@ -159,10 +160,10 @@ def kernel_table(model, a, seqs, spec, steps: int = 10) -> str:
 
     from torch.profiler import ProfilerActivity, profile
 
-    from tokquay_b200 import paged_forward
+    from tokquay_b200 import paged_greedy_step
 
     def step():
-        toks = paged_forward(model, a, seqs).argmax(-1).tolist()
+        toks = paged_greedy_step(model, a, seqs)
         for s, t in zip(seqs, toks):
             s.append_token(t)
             if spec["grow"]:
@@ -345,7 +346,7 @@ def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> tuple[li
 # ------------------------------------------------------------------------------ our arm
 def run_ours(args, world, rank, local):
     from tokquay_b200 import kv_cache as KV
-    from tokquay_b200 import paged_forward
+    from tokquay_b200 import paged_greedy_step
     from tokquay_b200.kv_cache import DevicePagedBatch, plan_step_host
 
     spec = workload_spec(args)
@@ -440,8 +441,9 @@ def run_ours(args, world, rank, local):
     h2d = []
 
     def api_step():
-        logits = paged_forward(model, a, seqs)  # plans on the host, copies the plan, replays the graph
-        toks = logits.argmax(-1).tolist()  # the step's device->host read
+        # Plans on the host, copies the plan, replays the graph; the step's greedy
+        # tokens (the graph's own argmax) are its one device->host read.
+        toks = paged_greedy_step(model, a, seqs)
         for s, t in zip(seqs, toks):
             s.append_token(t)
             if spec["grow"]:
@@ -628,7 +630,7 @@ def run_mixed(args, world, rank, local) -> dict | None:
     sequence's cached count goes back, so each step writes the same K/V rows
     and reads the same contexts.  ``value`` is the query rows (prompt tokens +
     decode tokens) processed per second."""
-    from tokquay_b200 import BlockAllocator, paged_forward
+    from tokquay_b200 import BlockAllocator, paged_greedy_step
     from tokquay_b200.kv_cache import DevicePagedBatch
     from tokquay_b200.model import argmax_rows
 
@@ -694,7 +696,7 @@ def run_mixed(args, world, rank, local) -> dict | None:
 
     # End to end: the public API with host planning and the plan copy inside.
     def api_step():
-        toks = argmax_rows(paged_forward(model, a, seqs, new_lens)).tolist()
+        toks = paged_greedy_step(model, a, seqs, new_lens)
         for s, st in zip(seqs, starts):
             s.num_cached_tokens = st
         return toks

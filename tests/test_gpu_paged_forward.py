@@ -17,7 +17,7 @@ import oracle
 from helpers import LOGITS_ATOL, build_config_case, cfg_of, weights_of
 from tokquay_b200 import _lib
 from tokquay_b200 import workloads as W
-from tokquay_b200.generate import paged_forward, paged_greedy_generate
+from tokquay_b200.generate import paged_forward, paged_greedy_generate, paged_greedy_step
 from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, cdiv
 from tokquay_b200.model import GPT2, GPT2Config
 from tokquay_b200.sequence import Sequence
@@ -350,6 +350,34 @@ def test_cuda_graph_decode_matches_eager_across_buckets():
     assert worst < 1e-5
     assert sorted(m.graph_runner._graphs) == [4, 8]
     torch.testing.assert_close(ag.pool, ae.pool, atol=1e-5, rtol=0)
+    assert _lib.device_status() == 0
+
+
+def test_greedy_step_tokens_match_paged_forward_argmax():
+    """paged_greedy_step = paged_forward(...).argmax(-1).tolist(): through the
+    graph's own argmax on decode steps (no logits copy) and through the eager
+    path on a prefill step, with the same num_cached_tokens bookkeeping."""
+    cfg = GPT2Config(**W.MINI)
+    m = make_model(cfg, W.random_weights(cfg, 9, "gpt2"))
+    ag, ae = _twin_allocators(cfg, 120, 8, 2)
+    m.use_cuda_graphs(ag, buckets=(8,))
+    rng = random.Random(2)
+    sg = [Sequence(i, [rng.randrange(cfg.vocab_size) for _ in range(rng.randint(3, 40))]) for i in range(6)]
+    se = [Sequence(s.seq_id, list(s.prompt_token_ids)) for s in sg]
+    for s1, s2 in zip(sg, se):
+        ag.allocate(s1)
+        ae.allocate(s2)
+    for step in range(4):  # step 0 prefills every prompt (eager), then decode steps (graph)
+        got = paged_greedy_step(m, ag, sg)
+        want = paged_forward(m, ae, se).argmax(-1).tolist()
+        assert got == want, step
+        assert [s.num_cached_tokens for s in sg] == [s.num_cached_tokens for s in se]
+        for s1, s2, t in zip(sg, se, want):
+            s1.append_token(t)
+            s2.append_token(t)
+            ag.append_slot(s1)
+            ae.append_slot(s2)
+    assert sorted(m.graph_runner._graphs) == [8]
     assert _lib.device_status() == 0
 
 

@@ -6,7 +6,8 @@ Public surface, mirroring the reference's modules:
 * ``BlockAllocator``, ``BatchedKV``, ``OutOfBlocksError``, ``DevicePagedBatch``
                                                   (tokquay/kv_cache.py)
 * ``Sequence``, ``SamplingParams``, ``SequenceStatus``   (tokquay/sequence.py)
-* ``paged_forward``, ``paged_greedy_generate``   (tokquay/generate.py)
+* ``paged_forward``, ``paged_greedy_generate``   (tokquay/generate.py),
+  ``paged_greedy_step`` (one step + greedy tokens)
 
 The CUDA kernels live in ``libtokquay_b200.so`` (C ABI: include/tokquay_b200.h),
 built in-tree by ``python -m tokquay_b200.build``.
@@ -21,7 +22,7 @@ from tokquay_b200.kv_cache import (  # noqa: F401
     cdiv,
 )
 from tokquay_b200.model import GPT2, GPT2Config  # noqa: F401
-from tokquay_b200.generate import paged_forward, paged_greedy_generate  # noqa: F401
+from tokquay_b200.generate import paged_forward, paged_greedy_generate, paged_greedy_step  # noqa: F401
 
 __all__ = [
     "BatchedKV",
@@ -35,5 +36,6 @@ __all__ = [
     "SequenceStatus",
     "cdiv",
     "paged_forward",
+    "paged_greedy_step",
     "paged_greedy_generate",
 ]

@@ -16,7 +16,7 @@ from dataclasses import dataclass
 
 import torch
 
-from tokquay_b200.generate import paged_forward
+from tokquay_b200.generate import paged_forward, paged_greedy_step
 from tokquay_b200.kv_cache import BlockAllocator
 from tokquay_b200.model import GPT2, argmax_rows
 from tokquay_b200.scheduler import Scheduler, SchedulerConfig
@@ -147,10 +147,13 @@ class Engine:
         st.positions_computed += sum(s.num_uncached_tokens for s in batch.seqs)  # before the forward
         st.positions_padded += batch.padded_tokens
 
-        logits = paged_forward(self.model, self.allocator, batch.seqs)  # [B, vocab]
+        if all(s.sampling.temperature <= 0 for s in batch.seqs):  # greedy rows only: tokens straight back
+            tokens = paged_greedy_step(self.model, self.allocator, batch.seqs)
+        else:
+            tokens = self._sample(batch.seqs, paged_forward(self.model, self.allocator, batch.seqs))
         self.last_step = StepInfo(batch.is_prefill, len(batch.seqs), batch.padded_tokens, self.kv_snapshot())
         events = []
-        for seq, tok in zip(batch.seqs, self._sample(batch.seqs, logits)):
+        for seq, tok in zip(batch.seqs, tokens):
             seq.append_token(tok)
             why = finish_reason_for(seq, tok, self.eos_token_id)
             if why:

@@ -9,7 +9,7 @@ from __future__ import annotations
 import torch
 
 from tokquay_b200.kv_cache import BlockAllocator, _hostpack
-from tokquay_b200.model import GPT2
+from tokquay_b200.model import GPT2, argmax_rows
 from tokquay_b200.sequence import Sequence, SequenceStatus
 
 
@@ -30,18 +30,49 @@ def paged_forward(
     if runner is not None and runner.allocator is allocator:
         logits = runner.try_run(seqs, new_lens)  # a decode step: replay a captured CUDA graph
         if logits is not None:
-            if _hostpack is not None and hasattr(_hostpack, "advance_cached"):
-                _hostpack.advance_cached(seqs)  # the native packer kept this step's lengths
-            else:
-                for s in seqs:
-                    s.num_cached_tokens += 1
+            _advance_after_replay(seqs)
             return logits
+    return _eager_forward(model, allocator, seqs, new_lens)
+
+
+def _eager_forward(model: GPT2, allocator: BlockAllocator, seqs: list[Sequence],
+                   new_lens: list[int] | None) -> torch.Tensor:  # fmt: skip
     lens = new_lens or [s.num_uncached_tokens for s in seqs]
     batch = allocator.batch_for(seqs, lens)
     logits = model.forward_paged(batch, last_only=True)[:, 0]
     for s, n in zip(seqs, lens):
         s.num_cached_tokens += n
     return logits
+
+
+def _advance_after_replay(seqs: list[Sequence]) -> None:
+    if _hostpack is not None and hasattr(_hostpack, "advance_cached"):
+        _hostpack.advance_cached(seqs)  # the native packer kept this step's lengths
+    else:
+        for s in seqs:
+            s.num_cached_tokens += 1
+
+
+@torch.no_grad()
+def paged_greedy_step(
+    model: GPT2,
+    allocator: BlockAllocator,
+    seqs: list[Sequence],
+    new_lens: list[int] | None = None,
+) -> list[int]:
+    """One batched step with greedy sampling: each sequence's next token,
+    ``paged_forward(...).argmax(-1).tolist()`` (the greedy rows of
+    tokquay/engine.py:189-194), advancing ``num_cached_tokens`` the same way.
+    A decode step that a captured CUDA graph covers returns the graph's own
+    argmax: no ``[B, vocab]`` logits copy and no second argmax launch, one
+    ``B x 8``-byte device-to-host read."""
+    runner = getattr(model, "graph_runner", None)
+    if runner is not None and runner.allocator is allocator:
+        tokens = runner.try_run_greedy(seqs, new_lens)
+        if tokens is not None:
+            _advance_after_replay(seqs)
+            return tokens.tolist()
+    return argmax_rows(_eager_forward(model, allocator, seqs, new_lens)).tolist()
 
 
 @torch.no_grad()
@@ -60,7 +91,7 @@ def paged_greedy_generate(
         s.status = SequenceStatus.RUNNING
     running = seqs
     while running:
-        next_ids = paged_forward(model, allocator, running).argmax(-1).tolist()
+        next_ids = paged_greedy_step(model, allocator, running)
         still_running = []
         for s, t in zip(running, next_ids):
             s.append_token(t)

@@ -85,16 +85,13 @@ class DecodeGraphRunner:
     def graph(self, bucket: int):
         return self._graphs.get(bucket) or self._capture(bucket)
 
-    def try_run(self, seqs: list[Sequence], new_lens: list[int] | None = None) -> torch.Tensor | None:
-        """``run`` for a step that turns out to be a decode step (one new token
-        per sequence, context within the graphs' capacity) that fits a
-        bucket; None, with nothing planned or launched, for any other step.
-        Decides in the native packer, without a Python pass over the sequences."""
+    def _replay_step(self, seqs: list[Sequence], new_lens: list[int] | None) -> tuple | None:
         B = len(seqs)
         bucket = self.bucket_for(B) if B else None
         if bucket is None:
             return None
-        graph, ws, logits, _, per_replay = self.graph(bucket)
+        entry = self.graph(bucket)
+        graph, ws, _, _, per_replay = entry
         layout = ws.stage_sequences(seqs, new_lens, torch.cuda.current_stream(self.allocator.pool.device),
                                     self.model.cfg.vocab_size, decode_max_ctx=self.max_ctx)  # fmt: skip
         if layout is None:
@@ -102,7 +99,23 @@ class DecodeGraphRunner:
         self.model.last_h2d_bytes = ws.last_used_ints * 4
         graph.replay()
         self.model.kernel_launches += per_replay
-        return logits[:B].clone()
+        return entry
+
+    def try_run(self, seqs: list[Sequence], new_lens: list[int] | None = None) -> torch.Tensor | None:
+        """``run`` for a step that turns out to be a decode step (one new token
+        per sequence, context within the graphs' capacity) that fits a
+        bucket; None, with nothing planned or launched, for any other step.
+        Decides in the native packer, without a Python pass over the sequences."""
+        entry = self._replay_step(seqs, new_lens)
+        return None if entry is None else entry[2][:len(seqs)].clone()
+
+    def try_run_greedy(self, seqs: list[Sequence], new_lens: list[int] | None = None) -> torch.Tensor | None:
+        """``try_run`` returning the step's greedy tokens instead of its logits:
+        the ``[B]`` int64 argmax the graph computed (a copy), so a greedy
+        decode loop neither copies the ``[B, vocab]`` logits nor runs a second
+        argmax; None, with nothing planned or launched, for any other step."""
+        entry = self._replay_step(seqs, new_lens)
+        return None if entry is None else entry[3][:len(seqs)].clone()
 
     def run(self, seqs: list[Sequence]) -> torch.Tensor:
         """``try_run`` for a step known to be a decode step that fits: ``[B, vocab]``
