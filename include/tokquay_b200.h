@@ -182,7 +182,12 @@ TQ_API int tq_qkv_bias_kv_write(float* q_out, int64_t q_row_stride, const float*
  * Launches that share scratch must not overlap on the GPU.  attn_plan is the
  * plan's attention region (TQ_PLAN_OFF_ITEMS) and n_ctas its TQ_PLAN_NUM_CTAS,
  * the launch grid.  One kernel launch on `stream`; every merge of split keys
- * happens inside it. */
+ * happens inside it.  The launch is a programmatic dependent of the kernel
+ * before it on `stream`: for a sequence that feeds one token this step, the
+ * pool rows of its earlier positions (0 .. position-1) may be read before
+ * that kernel has finished, so that kernel may write this step's new K/V
+ * rows (tq_kv_write, tq_qkv_bias_kv_write) and q, but no other pool row;
+ * everything else is read, and every output written, after it completes. */
 TQ_API int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64_t q_row_stride,
                        const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
                        int32_t block_size, int32_t head_dim, int32_t layer,

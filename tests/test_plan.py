@@ -30,7 +30,8 @@ def _u32(x) -> int:
 def decode_item(w) -> dict:
     w = [int(x) for x in w]
     return dict(
-        seq=w[0], row0=w[1], nrows=w[2] & 0xFF, head=(w[2] >> 8) & 0xFFFF, flags=_u32(w[2]) >> 24, pos0=w[3],
+        seq=w[0], row0=w[1], nrows=w[2] & 0xFF, head=(w[2] >> 8) & 0xFFFF, flags=(_u32(w[2]) >> 24) & 3,
+        decode=bool((_u32(w[2]) >> 24) & 4), pos0=w[3],
         cbeg=w[4] & 0xFFFF, cend=_u32(w[4]) >> 16, lsplit=w[5] & 0xFF, lcount=(w[5] >> 8) & 0xFF,
         lslot=_u32(w[5]) >> 16, gbase=w[6], gsplit=w[7] & 0xFFFF, gnsplit=_u32(w[7]) >> 16,
     )  # fmt: skip
@@ -225,6 +226,11 @@ def test_plan_matches_oracle_and_covers_every_key_once(bs, seed):
         for h in range(N_HEAD):
             assert sorted(seen[(r, h)]) == list(range(int(p["pos"][r]) + 1)), (r, h)
     check_merges(p)
+    # The decode flag (the kernel's licence to read the keys before pos0 ahead
+    # of the preceding kernel) marks exactly the items of one-token sequences.
+    for it in p["items"]:
+        assert it["decode"] == (new[it["seq"]] == 1), it
+        assert not it["decode"] or (it["nrows"] == 1 and it["pos0"] == start[it["seq"]])
     # Rows with keys split across CTAs have exactly one combine entry each.
     split_rows = {it["row0"] + k for it in p["items"] if it["flags"] & 2 for k in range(it["nrows"])}
     assert sorted(int(e[0]) for e in p["combine"]) == sorted(split_rows)

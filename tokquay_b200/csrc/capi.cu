@@ -137,8 +137,9 @@ int attention_params(float* out, int64_t out_row_stride, const float* q, int64_t
 }
 
 // The attention launch, as a programmatic dependent of the kernel before it
-// in the stream: its CTAs may start (barriers, work items, block ids) while
-// that kernel finishes; its producers wait for it before the first copy.
+// in the stream: its CTAs may start (barriers, work items, block ids, and for
+// decode items the K/V rows before the new key) while that kernel finishes;
+// everything else waits for it.
 cudaError_t launch_attention(const AttnParams& p, int n_ctas, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(n_ctas);

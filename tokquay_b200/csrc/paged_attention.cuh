@@ -113,6 +113,9 @@ constexpr int kAttnSmemBytes = kAttnWarps * kWarpSmemBytes + kLocalBytes;
 //   w[6] gbase   w[7] gsplit | gnsplit << 16
 // An all-zero item (cend == 0) marks a warp without work.
 constexpr int kFlagLocal = 1, kFlagGlobal = 2;
+// The item's sequence feeds one token this step: pos0 is its only new key.
+constexpr int kFlagDecode = 4;
+constexpr int kMergeFlags = kFlagLocal | kFlagGlobal;
 struct __align__(16) WorkItem {
   int w[8];
   __device__ __forceinline__ int seq() const { return w[0]; }
@@ -162,7 +165,7 @@ struct AttnParams {
 // A work item's merge targets lie inside the shared slots and the split-K
 // scratch; one that does not (a corrupted plan) is flagged and not written.
 __device__ __forceinline__ bool merge_targets_ok(const AttnParams& p, const WorkItem& it) {
-  const int f = it.flags();
+  const int f = it.flags() & kMergeFlags;
   bool ok = true;
   if (f & kFlagLocal)
     ok = it.lcount() >= 2 && it.lsplit() < it.lcount() && it.lslot() + it.nrows() * it.lcount() <= kLocalSlots;
@@ -382,7 +385,7 @@ __device__ __forceinline__ void finish_rows(const AttnParams& p, const WorkItem&
                                             float4 (&acc)[kMaxRows][4], float* local, long long* tr_sub) {
   TQ_TRACE(const long long tf0 = clock64(); if (lane == 0) tr_sub[6] += 1;)
   const int qq = lane & 3, rot = lane_rot(lane);
-  const int flags = it.flags(), h = it.head();
+  const int flags = it.flags() & kMergeFlags, h = it.head();
   if (flags != 0 && !merge_targets_ok(p, it)) return;
 #pragma unroll
   for (int r = 0; r < kMaxRows; ++r) {
@@ -564,12 +567,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
     int nx2_word = item_lane_load(p, ws, r0, 2, count, lane);
     int issued = 0;
     bool ok = true;
-    // Launched as a programmatic dependent (after the kernel that wrote q and
-    // this step's K/V), everything above overlapped that kernel; the copies
-    // wait for it.  Consumers read only what these copies bring.
-    pdl_wait();
-
-    for (;;) {
+    bool more = true;  // the cursor still holds a chunk to issue
+    // Issue chunk p_chunk of the current item into the next stage (waiting
+    // for the consumer to release it), then advance the cursor.  defer_q
+    // leaves the item's q rows out: their bytes are in the stage's count, and
+    // their copies go out later.
+    auto issue_next = [&](bool defer_q) {
       const int s = issued % kStages;
       if (issued >= kStages) {  // wait for the consumer to release the stage
         TQ_TRACE(long long te0 = clock64();)
@@ -577,7 +580,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
         TQ_TRACE(tr_empty += clock64() - te0;)
         if (!__all_sync(kFullMask, ok)) {
           ok = false;
-          break;
+          return;
         }
       }
       // Issue chunk p_chunk of the current item into stage s.  Each lane
@@ -656,12 +659,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
         })
       }
       __syncwarp();
-      if (bytes0) bulk_copy_g2s(dst0, src0, bytes0, bar);
+      // With defer_q the q rows (descriptors n_kv ..) stay out; their bytes are counted above.
+      if (bytes0 && !(defer_q && lane >= n_kv)) bulk_copy_g2s(dst0, src0, bytes0, bar);
       for (int base = 32; base < n_desc; base += 32) {
         const float* src = nullptr;
         uint32_t dst = 0, bytes = 0;
         describe(base + lane, src, dst, bytes);
-        if (bytes) bulk_copy_g2s(dst, src, bytes, bar);
+        if (bytes && !(defer_q && base + lane >= n_kv)) bulk_copy_g2s(dst, src, bytes, bar);
       }
       TQ_TRACE(if (lane == 0) tr_sub[1] += clock64() - ti0; ti0 = clock64();)
       if (++issued == 1 && inline_first) {  // from the second chunk on: the loaded list
@@ -671,7 +675,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
 
       // Advance the cursor.
       if (++p_chunk == p_it.cend()) {
-        if (++p_k == count) break;
+        if (++p_k == count) {
+          more = false;
+          return;
+        }
         p_it = nx_it;
         pf_a = nx_a;
         pf_b = nx_b;
@@ -681,7 +688,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
         nx2_word = item_lane_load(p, ws, r0, p_k + 2, count, lane);
       }
       TQ_TRACE(if (lane == 0) tr_sub[2] += clock64() - ti0;)
+    };
+    // Early copies.  This launch is a programmatic dependent of the kernel
+    // before it (this step's KV write), which may still be running: only the
+    // K/V rows it cannot be writing are read before the wait -- for a decode
+    // item (the sequence's one new key is at pos0), the chunks of the first
+    // item whose keys all lie before pos0 -- at most the ring's kStages
+    // chunks, and never the q rows.  The consumer computes nothing before the
+    // stage's q rows land, and those go out after the wait, so every store of
+    // this launch still follows the preceding kernel.
+    const WorkItem first_it = p_it;
+    int early = 0;
+    if (first_it.flags() & kFlagDecode) {
+      while (ok && more && p_k == 0 && early < kStages) {
+        const ChunkSpan sp = chunk_span(p, p_it, p_chunk);
+        if (sp.key0 + sp.nkeys > p_it.pos0()) break;  // holds the new key
+        issue_next(true);
+        ++early;
+      }
     }
+    pdl_wait();
+    if (early > 0 && lane < first_it.nrows())  // the first chunk's q rows, into stage 0
+      bulk_copy_g2s(smem_addr(wsm) + 2 * kKBytes + lane * kRowBytes,
+                    p.q + (size_t)(first_it.row0() + lane) * p.q_stride + first_it.head() * kHeadDim, kRowBytes,
+                    full0);
+    while (ok && more) issue_next(false);
     if (!ok) {
       // The consumer stopped releasing stages.  Give every copy still in
       // flight a bounded chance to land before the CTA exits, so no bulk copy

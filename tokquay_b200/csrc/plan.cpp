@@ -44,6 +44,7 @@ constexpr int kMaxChunkIndex = 0xffff;     // chunk indices are stored in 16 bit
 // Work item flags (word 2, bits 24..31).
 constexpr int kFlagLocal = 1;   // keys cut between warps of one CTA: merged in shared memory
 constexpr int kFlagGlobal = 2;  // keys split across CTAs: merged through the split-K scratch
+constexpr int kFlagDecode = 4;  // the sequence feeds one token: pos0 is its only new key
 // Shared-memory partial slots one CTA holds (each warp boundary cuts at most
 // one pair, so a CTA needs at most 2 * (kWarps - 1) * kMaxRows).
 constexpr int kLocalSlots = 2 * (kWarps - 1) * kMaxRows;
@@ -330,7 +331,8 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
         return set_error(TQ_ERR_UNSUPPORTED, "internal: CTA %d needs more than %d merge slots", c,
                          kLocalSlots);
       const int32_t w2 = g.nrows | (head << 8) |
-                         (((lcount > 1 ? kFlagLocal : 0) | (pc.gnsplit > 1 ? kFlagGlobal : 0)) << 24);
+                         (((lcount > 1 ? kFlagLocal : 0) | (pc.gnsplit > 1 ? kFlagGlobal : 0) |
+                           (q_len[g.seq] == 1 ? kFlagDecode : 0)) << 24);
       const int32_t w6 =
           pc.gnsplit > 1 ? (int32_t)(pc.gbase + (int64_t)head * g.nrows * pc.gnsplit) : -1;
       const int32_t w7 = pc.gsplit | (pc.gnsplit << 16);
