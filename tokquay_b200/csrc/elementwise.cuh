@@ -233,9 +233,15 @@ __device__ __forceinline__ void argmax_take(float& v, int& i, float v2, int i2) 
 // cluster combines the slices' results through distributed shared memory.
 // Slices are in column order and every reduction keeps the first of equal
 // values, so ties resolve as a left-to-right scan would.
+#ifndef TQ_ARGMAX_THREADS
+#define TQ_ARGMAX_THREADS 512
+#endif
+#ifndef TQ_ARGMAX_UNROLL
+#define TQ_ARGMAX_UNROLL 8
+#endif
 constexpr int kArgmaxSlices = 8;
-constexpr int kArgmaxThreads = 1024;
-constexpr int kArgmaxUnroll = 8;
+constexpr int kArgmaxThreads = TQ_ARGMAX_THREADS;
+constexpr int kArgmaxUnroll = TQ_ARGMAX_UNROLL;
 
 __device__ __forceinline__ void argmax_warp(float& v, int& i) {
 #pragma unroll
