@@ -67,6 +67,25 @@ int check_launch(const char* what) {
   return TQ_OK;
 }
 
+// Launches `kernel` as a programmatic dependent of the kernel before it on
+// `s`: its CTAs may be placed while that kernel drains.  Every kernel
+// launched this way calls pdl_wait() before it reads or writes anything the
+// kernels before it may touch.  A launch error is left for check_launch().
+template <typename... KArgs, typename... Args>
+void launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  (void)cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 int log2_exact(int v) {
@@ -228,7 +247,7 @@ int tq_kv_write(float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head
   p.slots = slot_mapping;
   p.n_tokens = d_num_tokens;
   const int threads = std::min(1024, ((2 * n_head * 16 + 31) / 32) * 32);
-  kv_write_kernel<<<row_grid(max_tokens, sms), threads, 0, (cudaStream_t)stream>>>(p);
+  launch_dependent(kv_write_kernel, row_grid(max_tokens, sms), threads, (cudaStream_t)stream, p);
   return check_launch("kv_write");
 }
 
@@ -275,11 +294,11 @@ int tq_qkv_bias_kv_write(float* q_out, int64_t q_row_stride, const float* parts,
   const int grid = row_grid(max_rows, sms);
   const cudaStream_t s = (cudaStream_t)stream;
   switch (n_parts) {  // partial-sum loads unrolled for the split counts the model uses
-    case 1: qkv_bias_kv_write_kernel<1><<<grid, threads, 0, s>>>(p); break;
-    case 2: qkv_bias_kv_write_kernel<2><<<grid, threads, 0, s>>>(p); break;
-    case 4: qkv_bias_kv_write_kernel<4><<<grid, threads, 0, s>>>(p); break;
-    case 8: qkv_bias_kv_write_kernel<8><<<grid, threads, 0, s>>>(p); break;
-    default: qkv_bias_kv_write_kernel<0><<<grid, threads, 0, s>>>(p); break;
+    case 1: launch_dependent(qkv_bias_kv_write_kernel<1>, grid, threads, s, p); break;
+    case 2: launch_dependent(qkv_bias_kv_write_kernel<2>, grid, threads, s, p); break;
+    case 4: launch_dependent(qkv_bias_kv_write_kernel<4>, grid, threads, s, p); break;
+    case 8: launch_dependent(qkv_bias_kv_write_kernel<8>, grid, threads, s, p); break;
+    default: launch_dependent(qkv_bias_kv_write_kernel<0>, grid, threads, s, p); break;
   }
   return check_launch("qkv_bias_kv_write");
 }
@@ -454,7 +473,7 @@ int tq_embed_layernorm(float* x, float* xa, const int32_t* ids, const int32_t* p
   p.vocab = vocab_size;
   p.n_positions = n_positions;
   p.eps = eps;
-  embed_ln_kernel<<<row_grid(max_rows, sms), n_embd / 4, 0, (cudaStream_t)stream>>>(p);
+  launch_dependent(embed_ln_kernel, row_grid(max_rows, sms), n_embd / 4, (cudaStream_t)stream, p);
   return check_launch("embed_layernorm");
 }
 
@@ -490,13 +509,13 @@ int tq_bias_residual_layernorm(float* x, float* xa, const float* y, int32_t n_pa
   const cudaStream_t s = (cudaStream_t)stream;
   const int grid = row_grid(max_rows, sms), threads = n_embd / 4;
   switch (n_parts) {  // partial-sum loads unrolled for the split counts the model uses
-    case 1: bias_residual_ln_kernel<1><<<grid, threads, 0, s>>>(p); break;
-    case 2: bias_residual_ln_kernel<2><<<grid, threads, 0, s>>>(p); break;
-    case 4: bias_residual_ln_kernel<4><<<grid, threads, 0, s>>>(p); break;
-    case 8: bias_residual_ln_kernel<8><<<grid, threads, 0, s>>>(p); break;
-    case 16: bias_residual_ln_kernel<16><<<grid, threads, 0, s>>>(p); break;
-    case 32: bias_residual_ln_kernel<32><<<grid, threads, 0, s>>>(p); break;
-    default: bias_residual_ln_kernel<0><<<grid, threads, 0, s>>>(p); break;
+    case 1: launch_dependent(bias_residual_ln_kernel<1>, grid, threads, s, p); break;
+    case 2: launch_dependent(bias_residual_ln_kernel<2>, grid, threads, s, p); break;
+    case 4: launch_dependent(bias_residual_ln_kernel<4>, grid, threads, s, p); break;
+    case 8: launch_dependent(bias_residual_ln_kernel<8>, grid, threads, s, p); break;
+    case 16: launch_dependent(bias_residual_ln_kernel<16>, grid, threads, s, p); break;
+    case 32: launch_dependent(bias_residual_ln_kernel<32>, grid, threads, s, p); break;
+    default: launch_dependent(bias_residual_ln_kernel<0>, grid, threads, s, p); break;
   }
   return check_launch("bias_residual_layernorm");
 }
@@ -523,7 +542,7 @@ int tq_layernorm_rows(float* out, const float* x, const int32_t* rows, const flo
   p.n_rows = d_num_rows;
   p.C = n_embd;
   p.eps = eps;
-  layernorm_rows_kernel<<<row_grid(max_rows, sms), n_embd / 4, 0, (cudaStream_t)stream>>>(p);
+  launch_dependent(layernorm_rows_kernel, row_grid(max_rows, sms), n_embd / 4, (cudaStream_t)stream, p);
   return check_launch("layernorm_rows");
 }
 
@@ -538,7 +557,7 @@ int tq_argmax_rows(const float* x, int64_t row_stride, int32_t n_cols, int64_t* 
   if (st) return st;
   if ((int64_t)max_rows * kArgmaxSlices > INT32_MAX)
     return set_error(TQ_ERR_UNSUPPORTED, "argmax_rows: too many rows");
-  argmax_rows_kernel<<<max_rows * kArgmaxSlices, kArgmaxThreads, 0, (cudaStream_t)stream>>>(
+  launch_dependent(argmax_rows_kernel, max_rows * kArgmaxSlices, kArgmaxThreads, (cudaStream_t)stream, 
       x, row_stride, n_cols, reinterpret_cast<long long*>(out), d_num_rows);
   return check_launch("argmax_rows");
 }
@@ -574,12 +593,12 @@ int tq_bias_gelu(float* out, const float* h, int32_t n_parts, int64_t part_strid
   const int grid = (int)std::min<int64_t>(std::max<int64_t>((total4 + 255) / 256, 1), (int64_t)sms * 8);
   const cudaStream_t s = (cudaStream_t)stream;
   switch (n_parts) {  // partial-sum loads unrolled for the split counts the model uses
-    case 1: bias_gelu_kernel<1><<<grid, 256, 0, s>>>(p); break;
-    case 2: bias_gelu_kernel<2><<<grid, 256, 0, s>>>(p); break;
-    case 4: bias_gelu_kernel<4><<<grid, 256, 0, s>>>(p); break;
-    case 8: bias_gelu_kernel<8><<<grid, 256, 0, s>>>(p); break;
-    case 16: bias_gelu_kernel<16><<<grid, 256, 0, s>>>(p); break;
-    default: bias_gelu_kernel<0><<<grid, 256, 0, s>>>(p); break;
+    case 1: launch_dependent(bias_gelu_kernel<1>, grid, 256, s, p); break;
+    case 2: launch_dependent(bias_gelu_kernel<2>, grid, 256, s, p); break;
+    case 4: launch_dependent(bias_gelu_kernel<4>, grid, 256, s, p); break;
+    case 8: launch_dependent(bias_gelu_kernel<8>, grid, 256, s, p); break;
+    case 16: launch_dependent(bias_gelu_kernel<16>, grid, 256, s, p); break;
+    default: launch_dependent(bias_gelu_kernel<0>, grid, 256, s, p); break;
   }
   return check_launch("bias_gelu");
 }

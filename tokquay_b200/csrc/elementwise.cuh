@@ -14,6 +14,9 @@
 // LayerNorm follows nn.LayerNorm: biased variance, eps inside the square root.
 // Row kernels use one block per row of C floats, one float4 per thread
 // (two-pass mean / variance over the values held in registers, no re-read).
+// Every kernel here is launched as a programmatic dependent of the kernel
+// before it (its CTAs may be placed while that kernel drains) and waits for
+// that kernel (griddepcontrol.wait) before its first load.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -72,6 +75,8 @@ struct RowParams {
 
 __global__ void __launch_bounds__(256) embed_ln_kernel(const RowParams p) {
   __shared__ float red[8];
+  pdl_launch_dependents();
+  pdl_wait();
   const int n = *p.n_rows;
   const int k = threadIdx.x;
   for (int r = blockIdx.x; r < n; r += gridDim.x) {
@@ -96,6 +101,8 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(const RowParams p) {
 template <int NP>
 __global__ void __launch_bounds__(256) bias_residual_ln_kernel(const RowParams p) {
   __shared__ float red[8];
+  pdl_launch_dependents();
+  pdl_wait();
   const int n = *p.n_rows;
   const int k = threadIdx.x;
   const float4 b = reinterpret_cast<const float4*>(p.bias)[k];
@@ -137,6 +144,8 @@ __global__ void __launch_bounds__(256) bias_residual_ln_kernel(const RowParams p
 
 __global__ void __launch_bounds__(256) layernorm_rows_kernel(const RowParams p) {
   __shared__ float red[8];
+  pdl_launch_dependents();
+  pdl_wait();
   const int n = *p.n_rows;
   const int k = threadIdx.x;
   for (int r = blockIdx.x; r < n; r += gridDim.x) {
@@ -170,6 +179,8 @@ struct GeluParams {
 // exactly NP partial sums, loads unrolled; NP == 0: p.n_parts, looped.
 template <int NP>
 __global__ void __launch_bounds__(256) bias_gelu_kernel(const GeluParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   const long long f4 = p.F >> 2;
   const long long total = (long long)(*p.n_rows) * f4;
   const float4* h = reinterpret_cast<const float4*>(p.h);
@@ -261,6 +272,8 @@ __global__ void __cluster_dims__(kArgmaxSlices, 1, 1) __launch_bounds__(kArgmaxT
   __shared__ int si[kArgmaxThreads / 32];
   __shared__ float slice_v;
   __shared__ int slice_i;
+  pdl_launch_dependents();
+  pdl_wait();
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int r = blockIdx.x / kArgmaxSlices;  // cluster-uniform
   const int k = (int)cluster.block_rank();

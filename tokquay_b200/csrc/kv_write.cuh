@@ -27,6 +27,8 @@ struct KvWriteParams {
 // (2 * n_head * 16 float4), 16-byte loads of contiguous source floats and
 // 16-byte stores into 2 * n_head pool rows of 256 bytes each.
 __global__ void __launch_bounds__(1024) kv_write_kernel(const KvWriteParams p) {
+  pdl_launch_dependents();  // the attention that follows may start its prologue now
+  pdl_wait();               // the kernel that wrote the K/V rows is complete
   const int n_tok = *p.n_tokens;
   const int per_kv4 = p.n_head * 16;  // float4 per K (or V) row of one token
   const long long pool_slots = p.num_blocks << p.log2_bs;
@@ -76,6 +78,7 @@ struct QkvWriteParams {
 template <int NP>
 __global__ void __launch_bounds__(1024) qkv_bias_kv_write_kernel(const QkvWriteParams p) {
   pdl_launch_dependents();  // the attention that follows may start its prologue now
+  pdl_wait();               // the c_attn matmul before it is complete
   const int n = *p.n_rows;
   const int C4 = p.n_head * 16;  // float4 per q (or K, or V) row
   const int t = threadIdx.x;
