@@ -108,6 +108,49 @@ def test_paged_attention_matches_float64_reference(bs, kind, seed):
     assert _lib.device_status() == 0
 
 
+def test_paged_attention_config4_full_size():
+    """BASELINE config 4 at its full shape -- 512 decoding sequences, contexts
+    U[256, 1024], block size 32, GPT-2 124M's 12 layers x 12 heads -- on a pool
+    sized to the batch (~25 GB, every other slot NaN), one launch per tested
+    layer on the grid the bench uses; every row of every head against the
+    float64 reference."""
+    rng = random.Random(4)
+    cfg = GPT2Config(vocab_size=64, n_positions=1024, n_embd=768, n_layer=12, n_head=12)
+    bs, n_seqs = 32, 512
+    ctx = [rng.randint(256, 1024) for _ in range(n_seqs)]
+    alloc = BlockAllocator(cfg, sum(cdiv(c, bs) for c in ctx) + 16, bs, device="cuda")
+    random.Random(5).shuffle(alloc._free)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    alloc.pool.normal_(generator=g)
+    tables = [alloc._take(cdiv(c, bs)) for c in ctx]
+    start, new = [c - 1 for c in ctx], [1] * n_seqs
+    for tbl, c in zip(tables, ctx):  # slots past each context
+        if c % bs:
+            alloc.pool[tbl[-1], :, :, :, c % bs:] = float("nan")
+    if alloc._free:
+        alloc.pool[torch.tensor(alloc._free, device="cuda")] = float("nan")
+    batch = DevicePagedBatch(alloc, tables, start, new)
+    C = cfg.n_embd
+    try:
+        for layer in (0, 11):
+            q = torch.randn(n_seqs, C, device="cuda", generator=g)
+            out = torch.full((n_seqs, C), float("nan"), device="cuda")
+            batch.attend_rows(layer, q, out, _stream())
+            torch.cuda.synchronize()
+            assert torch.isfinite(out).all(), layer
+            worst, scale = 0.0, 0.0
+            for b0 in range(0, n_seqs, 64):  # the reference in slices of 64 sequences
+                sl = slice(b0, b0 + 64)
+                want = _reference_attention(alloc.pool, layer, q[sl], tables[sl], start[sl], new[sl], bs)
+                worst = max(worst, (out[sl].double() - want).abs().max().item())
+                scale = max(scale, want.abs().max().item())
+            assert worst <= ATTN_RTOL * scale, (layer, worst, scale)
+        assert _lib.device_status() == 0
+    finally:
+        del batch, alloc
+        torch.cuda.empty_cache()
+
+
 def test_paged_attention_split_k_is_exercised():
     """Few long decodes force split-K + combine; compare with the unsplit run."""
     cfg = GPT2Config(vocab_size=64, n_positions=1024, n_embd=768, n_layer=1, n_head=12)
