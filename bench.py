@@ -56,7 +56,7 @@ L2_BYTES = 126 * 2**20
 WORKLOADS = {
     "cfg2": dict(n_seqs=64, ctx_range=(16, 512), block_size=16, num_blocks=2048, grow=True,
                  desc="BASELINE config 2: 64 seqs, ctx U[16,512], bs 16, 2048 blocks, consecutive greedy decode steps"),
-    "cfg4": dict(n_seqs=512, ctx_range=(256, 1024), block_size=32, pool_bytes=150e9, grow=False,
+    "cfg4": dict(n_seqs=512, ctx_range=(256, 1024), block_size=32, pool_bytes=150e9, grow=False, strong=True,
                  desc="BASELINE config 4: 512 seqs, ctx U[256,1024], bs 32, ~150 GB pool, repeated decode step"),
     "cfg1": dict(n_seqs=8, ctx_range=(16, 256), block_size=16, num_blocks=1024, grow=True,
                  desc="BASELINE config 1: 8 seqs, ctx U[16,256], bs 16, 1024 blocks, greedy decode steps"),
@@ -251,12 +251,16 @@ def reset_allocator(a):
     a.ref_counts = [0] * a.num_blocks
 
 
-def make_case(spec, a, seed):
+def make_case(spec, a, seed, rank=0, world=1):
+    """The workload's decode batch on this replica: a copy of the whole batch
+    (weak scaling), or with ``strong`` its share of one batch of ``n_seqs``
+    sequences split by sequence over the replicas (config 4)."""
     from tokquay_b200 import Sequence
     from tokquay_b200 import workloads as W
 
     reset_allocator(a)
-    return W.decode_case(Sequence, a, spec["n_seqs"], spec["ctx_range"], a.cfg.vocab_size, seed=seed)
+    shard = (rank, world) if spec.get("strong") else (0, 1)
+    return W.decode_case(Sequence, a, spec["n_seqs"], spec["ctx_range"], a.cfg.vocab_size, seed=seed, shard=shard)
 
 
 def attn_bytes(ctx_list, n_head, d, num_partials):
@@ -270,7 +274,8 @@ def attn_bytes(ctx_list, n_head, d, num_partials):
 
 
 # ------------------------------------------------------------------------------ attention timing
-def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> tuple[list[float], list[float], list[float]]:
+def eager_attention_times(model, a, spec, seed, warmup, total_steps, rank=0,
+                          world=1) -> tuple[list[float], list[float], list[float]]:  # fmt: skip
     """Attention times (ms per launch) over the same steps, eager, three ways:
 
     * stream: after each step's forward, its 12 attention launches (one per
@@ -285,7 +290,7 @@ def eager_attention_times(model, a, spec, seed, warmup, total_steps) -> tuple[li
       and CTA start-up of a kernel that follows an idle stream."""
     from tokquay_b200.kv_cache import DevicePagedBatch
 
-    case = make_case(spec, a, seed)
+    case = make_case(spec, a, seed, rank, world)
     seqs = case.seqs
     B = len(seqs)
     pairs: list = []
@@ -359,15 +364,18 @@ def run_ours(args, world, rank, local):
     # Every replica decodes its own copy of the same batch (own sequence objects,
     # own pool): per-GPU work is identical as N grows (weak scaling), so the
     # max over ranks measures the replicas, not the spread of random contexts.
+    # Config 4 instead splits its one batch of 512 sequences over the replicas
+    # by sequence (strong scaling).
     seed = 2
     K, Wm = args.steps, args.warmup
     total_steps = K + Wm
-    B = spec["n_seqs"]
+    strong = bool(spec.get("strong"))
+    B = len(range(rank, spec["n_seqs"], world)) if strong else spec["n_seqs"]
     runner = None if args.no_graphs else model.use_cuda_graphs(a)
     bucket = runner.bucket_for(B) if runner else None
 
     # ---- plan every step first (bookkeeping only; the plans go to HBM) ------------
-    case = make_case(spec, a, seed)
+    case = make_case(spec, a, seed, rank, world)
     seqs = case.seqs
     plans, batches, ctx_per_step, nparts_per_step = [], [], [], []
     if runner:
@@ -431,7 +439,7 @@ def run_ours(args, world, rank, local):
     # keeping host launch latency out of the interval.
     bytes_per_launch = [attn_bytes(ctx_per_step[k], cfg.n_head, cfg.d_head, nparts_per_step[k])
                         for k in range(Wm, total_steps) for _ in range(cfg.n_layer)]  # fmt: skip
-    attn_ms, evented_ms, single_ms = eager_attention_times(model, a, spec, seed, Wm, total_steps)
+    attn_ms, evented_ms, single_ms = eager_attention_times(model, a, spec, seed, Wm, total_steps, rank, world)
     attn_timing = ("CUDA events on the launching stream, eager pass over the same steps: after each step's "
                    "forward its 12 attention launches (one per layer) run again back to back between two "
                    "events; average launch = the interval / 12 (the kernel plus the GPU's gap to the next "
@@ -439,7 +447,7 @@ def run_ours(args, world, rank, local):
     del plans, batches
 
     # ---- end to end through the public API -----------------------------------------
-    case = make_case(spec, a, seed)
+    case = make_case(spec, a, seed, rank, world)
     seqs = case.seqs
     h2d = []
 
@@ -494,14 +502,14 @@ def run_ours(args, world, rank, local):
             "warmup": Wm,
             "ms_per_step": ms_max / K,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if strong else "weak",
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic",
             "config": {
-                "workload": spec["desc"],
+                "workload": spec["desc"] + (f" [sequences split over {world} replicas]" if strong and world > 1 else ""),
                 "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32, TF32 off",
-                "global_batch": B * world,
+                "global_batch": spec["n_seqs"] if strong else B * world,
                 "seq_len": f"ctx U{list(spec['ctx_range'])}",
                 "block_size": spec["block_size"],
                 "num_blocks": a.num_blocks,

@@ -113,14 +113,17 @@ class StepCase:
 
 
 def decode_case(SequenceCls, alloc, n_seqs: int, ctx_range: tuple[int, int], vocab: int, seed: int,
-                free_seed: int | None = None) -> StepCase:  # fmt: skip
+                free_seed: int | None = None, shard: tuple[int, int] = (0, 1)) -> StepCase:  # fmt: skip
     """Decode step (configs 1, 2, 4): ``n_seqs`` sequences with context lengths
     uniform in ``ctx_range`` and uniform token ids, all from ``random.Random(seed)``;
     each owns blocks for its whole context and has ``ctx-1`` positions cached,
-    so the step feeds its last token."""
+    so the step feeds its last token.  ``shard=(r, n)`` keeps sequences
+    r, r+n, r+2n, ... of that batch (one replica's share, config 4)."""
     rng = random.Random(seed)
     ctx = [rng.randint(*ctx_range) for _ in range(n_seqs)]
     toks = [[rng.randrange(vocab) for _ in range(c)] for c in ctx]
+    r, n = shard
+    ctx, toks = ctx[r::n], toks[r::n]
     shuffle_free_list(alloc, seed if free_seed is None else free_seed)
     seqs = []
     for i, (c, t) in enumerate(zip(ctx, toks)):
@@ -128,7 +131,7 @@ def decode_case(SequenceCls, alloc, n_seqs: int, ctx_range: tuple[int, int], voc
         alloc.allocate(s)
         s.num_cached_tokens = c - 1
         seqs.append(s)
-    return StepCase(seqs, [1] * n_seqs, {"ctx": ctx})
+    return StepCase(seqs, [1] * len(seqs), {"ctx": ctx})
 
 
 def mixed_case(SequenceCls, alloc, n_prefill: int, n_decode: int, len_range: tuple[int, int], vocab: int,
