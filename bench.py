@@ -16,9 +16,10 @@ the max over ranks; ``value`` is the tokens of all ranks over that time.
 Reported on one JSON line (rank 0):
   value        device-resident loop: step plans already in HBM, each step's
                input tokens are the previous step's argmax (CUDA events)
-  e2e          the public API: ``paged_greedy_step`` per step (host planning,
-               the pinned host->device plan copy, the graph replay, the greedy
-               tokens back to the host)
+  e2e          the public API: ``paged_greedy_decode`` over the K steps (configs
+               1, 2: each step's host plan, pinned host->device plan copy,
+               graph replay and greedy tokens back to the host, pipelined one
+               step ahead) or ``paged_greedy_step`` per step (config 4)
   roofline     the paged-attention kernel (+ its split-K combine): algorithmic
                bytes (K/V rows read + q read + output write + split scratch) per
                launch over its CUDA-event duration, vs the measured HBM copy peak
@@ -351,7 +352,7 @@ def eager_attention_times(model, a, spec, seed, warmup, total_steps, rank=0,
 # ------------------------------------------------------------------------------ our arm
 def run_ours(args, world, rank, local):
     from tokquay_b200 import kv_cache as KV
-    from tokquay_b200 import paged_greedy_step
+    from tokquay_b200 import paged_greedy_decode, paged_greedy_step
     from tokquay_b200.kv_cache import DevicePagedBatch, plan_step_host
 
     spec = workload_spec(args)
@@ -464,17 +465,32 @@ def run_ours(args, world, rank, local):
                 s.output_token_ids.pop()
         return toks
 
-    for _ in range(Wm):
-        api_step()
+    # A growing workload (configs 1, 2) runs its K steps as one fixed-batch
+    # greedy decode (paged_greedy_decode: graph steps pipelined one ahead of
+    # the host); a repeated step (config 4) goes step by step.
+    pipelined = spec["grow"] and runner is not None
+    if pipelined:
+        paged_greedy_decode(model, a, seqs, Wm)
+        for s in seqs:
+            a.append_slot(s)
+    else:
+        for _ in range(Wm):
+            api_step()
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize(device)
     t0 = time.perf_counter()
     e0.record(stream)
-    for _ in range(K):
-        api_step()
-        h2d.append(model.last_h2d_bytes)
+    if pipelined:
+        paged_greedy_decode(model, a, seqs, K)
+        h2d = list(runner.step_h2d_bytes) or [model.last_h2d_bytes]
+        for s in seqs:  # blocks for a following step (the kernel table's)
+            a.append_slot(s)
+    else:
+        for _ in range(K):
+            api_step()
+            h2d.append(model.last_h2d_bytes)
     e1.record(stream)
     torch.cuda.synchronize(device)
     wall_ms = (time.perf_counter() - t0) * 1e3

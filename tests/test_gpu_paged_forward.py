@@ -17,7 +17,7 @@ import oracle
 from helpers import LOGITS_ATOL, build_config_case, cfg_of, weights_of
 from tokquay_b200 import _lib
 from tokquay_b200 import workloads as W
-from tokquay_b200.generate import paged_forward, paged_greedy_generate, paged_greedy_step
+from tokquay_b200.generate import paged_forward, paged_greedy_decode, paged_greedy_generate, paged_greedy_step
 from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, cdiv
 from tokquay_b200.model import GPT2, GPT2Config
 from tokquay_b200.sequence import Sequence
@@ -378,6 +378,48 @@ def test_greedy_step_tokens_match_paged_forward_argmax():
             ag.append_slot(s1)
             ae.append_slot(s2)
     assert sorted(m.graph_runner._graphs) == [8]
+    assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("graph_max_ctx", [None, 40])
+def test_pipelined_decode_matches_step_by_step(graph_max_ctx):
+    """paged_greedy_decode (graph steps pipelined one ahead of the host, token
+    ids fed on the device) = the step-by-step loop: same tokens, same
+    sequences, same allocator state.  With graph_max_ctx=40 the contexts
+    outgrow the graphs mid-run and the rest runs eagerly."""
+    cfg = GPT2Config(**W.MINI)
+    m = make_model(cfg, W.random_weights(cfg, 10, "gpt2"))
+    ag, ae = _twin_allocators(cfg, 160, 4, 3)
+    m.use_cuda_graphs(ag, buckets=(8,), max_ctx=graph_max_ctx)
+    rng = random.Random(3)
+    lens = [rng.randint(3, 30) for _ in range(6)] + [32]  # the last one outgrows 40 positions at step 9
+    sg = [Sequence(i, [rng.randrange(cfg.vocab_size) for _ in range(n)]) for i, n in enumerate(lens)]
+    se = [Sequence(s.seq_id, list(s.prompt_token_ids)) for s in sg]
+    for s1, s2 in zip(sg, se):
+        ag.allocate(s1)
+        ae.allocate(s2)
+    # The prefill step first (eager on both sides), then 12 decode steps.
+    assert paged_greedy_decode(m, ag, sg, 1) == [[t] for t in paged_forward(m, ae, se).argmax(-1).tolist()]
+    for s in se:
+        s.append_token(sg[s.seq_id].output_token_ids[-1])
+    for s1, s2 in zip(sg, se):
+        ag.append_slot(s1)
+        ae.append_slot(s2)
+    got = paged_greedy_decode(m, ag, sg, 12)
+    want = [[] for _ in se]
+    for k in range(12):
+        toks = m.forward_paged(ae.batch_for(se), last_only=True)[:, 0].argmax(-1).tolist()
+        for s, w, t in zip(se, want, toks):
+            s.num_cached_tokens += 1
+            s.append_token(t)
+            w.append(t)
+            if k + 1 < 12:
+                ae.append_slot(s)
+    assert got == want
+    for s1, s2 in zip(sg, se):
+        assert s1.output_token_ids == s2.output_token_ids
+        assert s1.num_cached_tokens == s2.num_cached_tokens and s1.block_table == s2.block_table
+    assert ag._free == ae._free and ag.ref_counts == ae.ref_counts
     assert _lib.device_status() == 0
 
 

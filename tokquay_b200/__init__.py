@@ -7,7 +7,8 @@ Public surface, mirroring the reference's modules:
                                                   (tokquay/kv_cache.py)
 * ``Sequence``, ``SamplingParams``, ``SequenceStatus``   (tokquay/sequence.py)
 * ``paged_forward``, ``paged_greedy_generate``   (tokquay/generate.py),
-  ``paged_greedy_step`` (one step + greedy tokens)
+  ``paged_greedy_step`` (one step + greedy tokens), ``paged_greedy_decode``
+  (a fixed batch's greedy steps, pipelined over CUDA graphs)
 
 The CUDA kernels live in ``libtokquay_b200.so`` (C ABI: include/tokquay_b200.h),
 built in-tree by ``python -m tokquay_b200.build``.
@@ -22,7 +23,12 @@ from tokquay_b200.kv_cache import (  # noqa: F401
     cdiv,
 )
 from tokquay_b200.model import GPT2, GPT2Config  # noqa: F401
-from tokquay_b200.generate import paged_forward, paged_greedy_generate, paged_greedy_step  # noqa: F401
+from tokquay_b200.generate import (  # noqa: F401
+    paged_forward,
+    paged_greedy_decode,
+    paged_greedy_generate,
+    paged_greedy_step,
+)
 
 __all__ = [
     "BatchedKV",
@@ -36,6 +42,7 @@ __all__ = [
     "SequenceStatus",
     "cdiv",
     "paged_forward",
+    "paged_greedy_decode",
     "paged_greedy_step",
     "paged_greedy_generate",
 ]

@@ -76,6 +76,39 @@ def paged_greedy_step(
 
 
 @torch.no_grad()
+def paged_greedy_decode(
+    model: GPT2,
+    allocator: BlockAllocator,
+    seqs: list[Sequence],
+    n_steps: int,
+) -> list[list[int]]:
+    """``n_steps`` greedy steps of a fixed batch: after each step every
+    sequence gets its token appended (``append_token``), and every step but
+    the last is followed by ``allocator.append_slot`` -- the loop of
+    tokquay/generate.py:109-119 for a batch that runs ``n_steps`` more tokens.
+    The first step feeds each sequence's uncached tokens, every later step one.
+    Returns the new tokens per sequence.
+
+    With captured CUDA graphs the steps are pipelined one ahead of the host:
+    step k+1 is planned while step k runs and takes step k's tokens from the
+    device, so the GPU does not wait for the host between steps."""
+    runner = getattr(model, "graph_runner", None)
+    if runner is not None and runner.allocator is allocator:
+        out = runner.decode_steps(seqs, n_steps)
+        if out is not None:
+            return out
+    out: list[list[int]] = [[] for _ in seqs]
+    for k in range(n_steps):
+        toks = paged_greedy_step(model, allocator, seqs)
+        for s, o, t in zip(seqs, out, toks):
+            s.append_token(t)
+            o.append(t)
+            if k + 1 < n_steps:
+                allocator.append_slot(s)
+    return out
+
+
+@torch.no_grad()
 def paged_greedy_generate(
     model: GPT2,
     allocator: BlockAllocator,
@@ -89,17 +122,15 @@ def paged_greedy_generate(
     for s in seqs:
         allocator.allocate(s)
         s.status = SequenceStatus.RUNNING
-    running = seqs
-    while running:
-        next_ids = paged_greedy_step(model, allocator, running)
-        still_running = []
-        for s, t in zip(running, next_ids):
-            s.append_token(t)
-            if len(s.output_token_ids) >= max_new_tokens:
-                allocator.free(s)
-                s.status = SequenceStatus.FINISHED
-            else:
-                allocator.append_slot(s)
-                still_running.append(s)
-        running = still_running
+    # Every sequence runs the same number of steps (max_new_tokens, at least
+    # one), so the batch never changes: the prefill step, then the decode
+    # steps as one pipelined run.
+    paged_greedy_decode(model, allocator, seqs, 1)
+    if max_new_tokens > 1:
+        for s in seqs:
+            allocator.append_slot(s)
+        paged_greedy_decode(model, allocator, seqs, max_new_tokens - 1)
+    for s in seqs:
+        allocator.free(s)
+        s.status = SequenceStatus.FINISHED
     return [s.output_token_ids for s in seqs]

@@ -21,7 +21,7 @@ import bisect
 import torch
 
 from tokquay_b200 import _lib
-from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, PlanWorkspace
+from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, PlanWorkspace, _hostpack
 from tokquay_b200.model import argmax_rows
 from tokquay_b200.sequence import Sequence
 
@@ -117,6 +117,99 @@ class DecodeGraphRunner:
         entry = self._replay_step(seqs, new_lens)
         return None if entry is None else entry[3][:len(seqs)].clone()
 
+    def decode_steps(self, seqs: list[Sequence], n_steps: int) -> list[list[int]] | None:
+        """``n_steps`` greedy decode steps of a fixed batch, one step ahead of
+        the host: while step k runs, the host already plans step k+1 (the
+        sequences' lengths and blocks do not depend on the token values) with a
+        placeholder token id, and step k's argmax is copied into step k+1's
+        plan on the device; step k's tokens reach the host (and replace the
+        placeholders) while step k+1 runs.  After each step every sequence has
+        its token appended, and every step but the last is followed by
+        ``allocator.append_slot`` -- the state the one-step-at-a-time loop
+        leaves.  Returns the tokens per sequence, or None (nothing run) when the
+        first step is not a decode step that fits a bucket; a later step that
+        does not fit ends the pipeline, and the remaining steps go one at a
+        time through ``paged_forward``'s eager path."""
+        B = len(seqs)
+        bucket = self.bucket_for(B) if B else None
+        if bucket is None or n_steps < 1:
+            return None
+        graph, ws, _, tokens, per_replay = self.graph(bucket)
+        dev = self.allocator.pool.device
+        stream = torch.cuda.current_stream(dev)
+        vocab = self.model.cfg.vocab_size
+        ids_off = int(ws.layout[_lib.PLAN_OFF_TOKEN_IDS])
+        host = torch.empty((n_steps, B), dtype=torch.int64, pin_memory=True)
+        ready: list[torch.cuda.Event] = []
+        out: list[list[int]] = [[] for _ in seqs]
+
+        self.step_h2d_bytes = []  # host->device plan bytes of each replayed step
+
+        def launch(k: int) -> None:
+            self.model.last_h2d_bytes = ws.last_used_ints * 4
+            self.step_h2d_bytes.append(ws.last_used_ints * 4)
+            if k > 0:  # the previous step's argmax feeds this step, on the device
+                ws.plan[ids_off:ids_off + B].copy_(tokens[:B])
+            graph.replay()
+            self.model.kernel_launches += per_replay
+            _advance(seqs)
+            host[k].copy_(tokens[:B], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            ready.append(ev)
+
+        def settle(k: int, appended: bool) -> None:
+            """Step k's tokens into the sequences (over the placeholders if appended)."""
+            ready[k].synchronize()
+            toks = host[k].tolist()
+            for s, o, t in zip(seqs, out, toks):
+                if appended:
+                    s.output_token_ids[-1] = t
+                else:
+                    s.append_token(t)
+                o.append(t)
+
+        if ws.stage_sequences(seqs, None, stream, vocab, decode_max_ctx=self.max_ctx) is None:
+            return None
+        launch(0)
+        done = 1
+        while done < n_steps:
+            n_placed = 0
+            try:
+                for s in seqs:  # step done-1's token, not known yet: a placeholder
+                    s.append_token(0)
+                    n_placed += 1
+                    self.allocator.append_slot(s)
+            except BaseException:  # e.g. OutOfBlocksError: leave the real tokens behind
+                ready[done - 1].synchronize()
+                for i, (s, o, t) in enumerate(zip(seqs, out, host[done - 1].tolist())):
+                    if i < n_placed:
+                        s.output_token_ids[-1] = t
+                    else:
+                        s.append_token(t)
+                    o.append(t)
+                raise
+            if ws.stage_sequences(seqs, None, stream, vocab, decode_max_ctx=self.max_ctx) is None:
+                settle(done - 1, True)
+                break
+            launch(done)
+            settle(done - 1, True)
+            done += 1
+        else:
+            settle(n_steps - 1, False)
+            return out
+        from tokquay_b200.generate import _eager_forward
+        from tokquay_b200.model import argmax_rows
+
+        for k in range(done, n_steps):  # the rest one at a time, eagerly
+            toks = argmax_rows(_eager_forward(self.model, self.allocator, seqs, None)).tolist()
+            for s, o, t in zip(seqs, out, toks):
+                s.append_token(t)
+                o.append(t)
+                if k + 1 < n_steps:
+                    self.allocator.append_slot(s)
+        return out
+
     def run(self, seqs: list[Sequence]) -> torch.Tensor:
         """``try_run`` for a step known to be a decode step that fits: ``[B, vocab]``
         logits (a copy); ValueError otherwise.  Does not advance the sequences."""
@@ -143,6 +236,15 @@ class DecodeGraphRunner:
         graph.replay()
         self.model.kernel_launches += per_replay
         return tokens
+
+
+def _advance(seqs: list[Sequence]) -> None:
+    """num_cached_tokens += 1 for a replayed decode step."""
+    if _hostpack is not None and hasattr(_hostpack, "advance_cached"):
+        _hostpack.advance_cached(seqs)  # the native packer kept this step's lengths
+    else:
+        for s in seqs:
+            s.num_cached_tokens += 1
 
 
 class _CaptureView(DevicePagedBatch):
