@@ -848,6 +848,7 @@ def run_serving(args, world, rank, local) -> dict | None:
 
     from tokquay_b200 import BlockAllocator
     from tokquay_b200.engine import Engine
+    from tokquay_b200.scheduler import SchedulerConfig
     from tokquay_b200.serving import make_workload, round_robin, run_trace, summarize
 
     device = torch.device("cuda", local)
@@ -856,18 +857,24 @@ def run_serving(args, world, rank, local) -> dict | None:
     model = make_model(device)
     a = BlockAllocator(model.cfg, 1024, 16, device=device)
     runner = model.use_cuda_graphs(a)
-    for b in runner.buckets:  # capture every decode graph the engine can use before the clock starts
+    P = args.mixed_tokens
+    if P > 0:  # mixed-step graphs sized for P prompt tokens per step
+        runner.mixed_extra = sorted({max(1, P // 4), max(1, P // 2), P})
+    for b in runner.buckets:  # capture every graph the engine can use before the clock starts
         if b <= 64:
             runner.graph(b)
+            for e in runner.mixed_extra if P > 0 else ():
+                runner.graph((b, b + e))
+    sched_cfg = SchedulerConfig(max_model_len=model.cfg.n_positions, mixed_prefill_tokens=P)
     rate = math.inf if args.rate == "inf" else float(args.rate)
     workload = make_workload(rate, args.trace_requests, seed=0)
     mine = round_robin(workload, world, rank)
-    warm = Engine(model, a)
+    warm = Engine(model, a, sched_cfg)
     for spec in make_workload(math.inf, 8, seed=99, output_len=(4, 8)):  # warm the prefill shapes too
         warm.add_request(list(spec.prompt_ids))
     warm.run_until_done()
     torch.cuda.synchronize(device)
-    eng = Engine(model, a)
+    eng = Engine(model, a, sched_cfg)
     barrier(world)
     records, steps, wall = run_trace(eng, mine)
     torch.cuda.synchronize(device)
@@ -889,11 +896,14 @@ def run_serving(args, world, rank, local) -> dict | None:
         "data": "synthetic",
         "config": {"workload": f"BASELINE config 5, first {args.trace_requests} requests at rate {args.rate} req/s "
                                f"(seed 0), round-robin over {world} replica(s), 1,024 x 16 KV slots each",
+                   "scheduler": ("the reference's (prefill and decode steps alternate)" if P == 0 else
+                                 f"opt-in chunked prefill: decodes + up to {P} prompt tokens per step"),
                    "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32, TF32 off",
                    "parallelism": f"replicas{world}"},  # fmt: skip
         "rank0": {k: out[k] for k in ("requests", "output_tokens", "duration_s", "throughput_tok_s", "ttft_ms",
                                       "itl_ms", "latency_ms", "steps", "prefill_steps", "decode_step_ms")},
         "preemptions_rank0": eng.stats.num_preemptions,
+        "mixed_steps_rank0": eng.stats.mixed_steps,
         "wall_s_rank0": wall,
     }
 
@@ -966,6 +976,8 @@ def main():
     ap.add_argument("--block-size", type=int, default=0, help="config 3: block size (16 or 32; default 16)")
     ap.add_argument("--trace-requests", type=int, default=400, help="config 5: requests of the trace served")
     ap.add_argument("--rate", default="64", help="config 5: arrival rate in requests/s, or inf for a burst")
+    ap.add_argument("--mixed-tokens", type=int, default=0,
+                    help="config 5: opt-in chunked-prefill scheduling with this many prompt tokens per step")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graphs", action="store_true", help="launch every kernel from Python (no CUDA graphs)")

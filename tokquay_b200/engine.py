@@ -49,6 +49,7 @@ class EngineStats:
     positions_computed: int = 0  # real positions fed to the model (prompts, recomputes, decodes)
     positions_padded: int = 0  # batch x longest row per step, as the reference counts it
     positions_discarded: int = 0  # cached positions thrown away by preemption
+    mixed_steps: int = 0  # steps that fed prompt chunks beside decodes (opt-in policy)
 
 
 @dataclass
@@ -144,16 +145,20 @@ class Engine:
         st.peak_used_blocks = max(st.peak_used_blocks, self.allocator.num_used_blocks)
         st.num_preemptions = sched.num_preemptions
         st.positions_discarded = sched.num_discarded_positions
-        st.positions_computed += sum(s.num_uncached_tokens for s in batch.seqs)  # before the forward
+        lens = batch.new_lens
+        st.positions_computed += sum(lens) if lens else sum(s.num_uncached_tokens for s in batch.seqs)
         st.positions_padded += batch.padded_tokens
+        st.mixed_steps += int(bool(lens) and max(lens) > 1)
 
         if all(s.sampling.temperature <= 0 for s in batch.seqs):  # greedy rows only: tokens straight back
-            tokens = paged_greedy_step(self.model, self.allocator, batch.seqs)
+            tokens = paged_greedy_step(self.model, self.allocator, batch.seqs, lens)
         else:
-            tokens = self._sample(batch.seqs, paged_forward(self.model, self.allocator, batch.seqs))
+            tokens = self._sample(batch.seqs, paged_forward(self.model, self.allocator, batch.seqs, lens))
         self.last_step = StepInfo(batch.is_prefill, len(batch.seqs), batch.padded_tokens, self.kv_snapshot())
         events = []
         for seq, tok in zip(batch.seqs, tokens):
+            if seq.num_uncached_tokens > 0:  # a prompt chunk short of the prompt's end: no token yet
+                continue
             seq.append_token(tok)
             why = finish_reason_for(seq, tok, self.eos_token_id)
             if why:
@@ -174,6 +179,6 @@ class Engine:
         step's single device-to-host read (tokquay/engine.py:189-194)."""
         tokens = argmax_rows(logits.contiguous())
         for i, s in enumerate(seqs):
-            if s.sampling.temperature > 0:
+            if s.sampling.temperature > 0 and s.num_uncached_tokens == 0:  # mid-prompt rows draw nothing
                 tokens[i] = sample_token(logits[i], s.sampling, self._rngs[s.seq_id])
         return tokens.tolist()

@@ -26,6 +26,9 @@ from tokquay_b200.model import argmax_rows
 from tokquay_b200.sequence import Sequence
 
 DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256, 512)
+# Row capacities of mixed-step graphs: a bucket of b sequences with up to
+# b + e rows (decode rows plus prompt chunks), e from this list.
+DEFAULT_MIXED_EXTRA = (32, 128, 512)
 
 
 class DecodeGraphRunner:
@@ -36,12 +39,14 @@ class DecodeGraphRunner:
     graph's own output buffer is overwritten by the next replay).
     """
 
-    def __init__(self, model, allocator: BlockAllocator, buckets=DEFAULT_BUCKETS, max_ctx: int | None = None):
+    def __init__(self, model, allocator: BlockAllocator, buckets=DEFAULT_BUCKETS, max_ctx: int | None = None,
+                 mixed_extra=DEFAULT_MIXED_EXTRA):  # fmt: skip
         if allocator.pool.device.type != "cuda":
             raise RuntimeError("CUDA graphs need the pool on a CUDA device")
         self.model = model
         self.allocator = allocator
         self.buckets = sorted(set(int(b) for b in buckets))
+        self.mixed_extra = sorted(set(int(e) for e in mixed_extra))
         self.max_ctx = max_ctx or model.cfg.n_positions
         self._graphs: dict[int, tuple] = {}
         self._pool = None  # one private memory pool shared by every bucket's graph
@@ -54,8 +59,9 @@ class DecodeGraphRunner:
         i = bisect.bisect_left(self.buckets, n)
         return self.buckets[i] if i < len(self.buckets) else None
 
-    def _capture(self, bucket: int):
-        ws = PlanWorkspace(self.allocator, bucket, bucket, self.max_ctx)
+    def _capture(self, key):
+        bucket, rows = (key, key) if isinstance(key, int) else key
+        ws = PlanWorkspace(self.allocator, bucket, rows, self.max_ctx)
         # A plan whose counts are all zero: every kernel of the step exits at
         # once, so the warm-up run below touches neither the pool nor anything else.
         ws.plan.zero_()
@@ -79,23 +85,44 @@ class DecodeGraphRunner:
         per_replay = self.model.kernel_launches - launches + 1
         self.model.kernel_launches = launches
         entry = (graph, ws, logits, tokens, per_replay)
-        self._graphs[bucket] = entry
+        self._graphs[key] = entry
         return entry
 
-    def graph(self, bucket: int):
-        return self._graphs.get(bucket) or self._capture(bucket)
+    def graph(self, key):
+        """The graph of a decode bucket (an int) or of a mixed step's
+        (sequences, rows) capacities; captured on first use."""
+        return self._graphs.get(key) or self._capture(key)
+
+    def mixed_key(self, n_seqs: int, n_rows: int) -> tuple[int, int] | None:
+        b = self.bucket_for(n_seqs)
+        if b is None:
+            return None
+        for e in self.mixed_extra:
+            if n_rows <= b + e:
+                return (b, b + e)
+        return None
 
     def _replay_step(self, seqs: list[Sequence], new_lens: list[int] | None) -> tuple | None:
         B = len(seqs)
         bucket = self.bucket_for(B) if B else None
         if bucket is None:
             return None
-        entry = self.graph(bucket)
-        graph, ws, _, _, per_replay = entry
-        layout = ws.stage_sequences(seqs, new_lens, torch.cuda.current_stream(self.allocator.pool.device),
-                                    self.model.cfg.vocab_size, decode_max_ctx=self.max_ctx)  # fmt: skip
-        if layout is None:
+        stream = torch.cuda.current_stream(self.allocator.pool.device)
+        vocab = self.model.cfg.vocab_size
+        entry = None
+        if new_lens is None or max(new_lens) == 1:  # a decode step
+            entry = self.graph(bucket)
+            if entry[1].stage_sequences(seqs, new_lens, stream, vocab, decode_max_ctx=self.max_ctx) is None:
+                entry = None
+        if entry is None and new_lens is not None and self.mixed_extra:  # prompt chunks beside decodes
+            key = self.mixed_key(B, sum(new_lens))
+            if key is not None:
+                entry = self.graph(key)
+                if entry[1].stage_sequences(seqs, new_lens, stream, vocab, fit_only=True) is None:
+                    entry = None
+        if entry is None:
             return None
+        graph, ws, _, _, per_replay = entry
         self.model.last_h2d_bytes = ws.last_used_ints * 4
         graph.replay()
         self.model.kernel_launches += per_replay

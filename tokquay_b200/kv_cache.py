@@ -425,12 +425,14 @@ class PlanWorkspace:
         return layout
 
     def stage_sequences(self, seqs, new_lens: list[int] | None, stream: torch.cuda.Stream,
-                        vocab_size: int = 0, decode_max_ctx: int = 0) -> np.ndarray | None:  # fmt: skip
+                        vocab_size: int = 0, decode_max_ctx: int = 0,
+                        fit_only: bool = False) -> np.ndarray | None:  # fmt: skip
         """``stage`` straight from ``Sequence`` objects: the native packer
         hands its arrays to the planner, so planning a step makes no Python
         objects.  Same plan, same errors as ``stage(PackedStep.from_sequences(...))``.
         With ``decode_max_ctx`` > 0, a step that is not a decode step within
-        that context, or does not fit the capacities, returns None (nothing staged)."""
+        that context, or does not fit the capacities, returns None (nothing
+        staged); with ``fit_only`` any step that does not fit returns None."""
         if not self._native:
             packed = PackedStep.from_sequences(seqs, new_lens)
             if decode_max_ctx > 0 and (packed.lens.max() != 1 or packed.lens.min() != 1
@@ -439,7 +441,7 @@ class PlanWorkspace:
             try:
                 return self.stage(packed, stream, vocab_size)
             except RuntimeError:
-                if decode_max_ctx > 0:
+                if decode_max_ctx > 0 or fit_only:
                     return None
                 raise
         if not seqs:
@@ -451,6 +453,8 @@ class PlanWorkspace:
             MIN_SPLIT_CHUNKS, self.caps.ctypes.data, host.data_ptr(), self.total, self._layout.ctypes.data,
             decode_max_ctx)
         if decode_max_ctx > 0 and status in (_NOT_A_DECODE_STEP, _lib.TQ_ERR_CAPACITY):
+            return None
+        if fit_only and status == _lib.TQ_ERR_CAPACITY:
             return None
         _lib.check(status, "tq_plan_step")
         used = int(self._layout[_lib.PLAN_USED_INTS])

@@ -20,6 +20,14 @@ streams.  The policy:
 The allocator and sequences are this package's (same contract as the
 reference's), so block tables and allocator state follow the reference's bit
 for bit.
+
+``SchedulerConfig.mixed_prefill_tokens > 0`` switches to an opt-in policy
+that is not the reference's (chunked prefill): each step runs every decoding
+sequence together with up to that many prompt tokens -- the next chunk of
+every running sequence still in its prompt, then newly admitted requests --
+in one mixed launch of the paged path.  Admission (FCFS, no skipping, blocks
+for the whole prompt reserved up front, watermark) and preemption (the newest
+running sequence, by recompute) follow the same rules as above.
 """
 
 from __future__ import annotations
@@ -45,24 +53,33 @@ class SchedulerConfig:
     max_num_batched_tokens: int = 2048  # per step, in padded tokens: rows x longest row
     max_model_len: int = 1024
     watermark_blocks: int = 1
+    # Opt-in, not the reference's policy: > 0 runs every decoding sequence and
+    # up to this many prompt tokens (chunks of prompts) in each step.
+    mixed_prefill_tokens: int = 0
 
     def __post_init__(self) -> None:
         if self.max_num_seqs < 1 or self.max_num_batched_tokens < self.max_num_seqs:
             raise ValueError("need max_num_seqs >= 1 and max_num_batched_tokens >= max_num_seqs")
+        if self.mixed_prefill_tokens < 0:
+            raise ValueError("mixed_prefill_tokens must be >= 0")
 
 
 @dataclass
 class ScheduledBatch:
     """One step's sequences.  ``padded_tokens`` is fixed when the batch is made
-    (the step itself changes the sequences' uncached counts)."""
+    (the step itself changes the sequences' uncached counts).  ``new_lens``:
+    the tokens each sequence feeds (None: all of its uncached tokens, as every
+    step of the reference's policy does)."""
 
     seqs: list[Sequence]
     is_prefill: bool
     preempted: list[Sequence] = field(default_factory=list)
+    new_lens: list[int] | None = None
     padded_tokens: int = field(init=False)
 
     def __post_init__(self) -> None:
-        self.padded_tokens = len(self.seqs) * max(s.num_uncached_tokens for s in self.seqs)
+        widest = max(self.new_lens) if self.new_lens else max(s.num_uncached_tokens for s in self.seqs)
+        self.padded_tokens = len(self.seqs) * widest
 
 
 class Scheduler:
@@ -123,6 +140,8 @@ class Scheduler:
     # ---- one decision ----------------------------------------------------------------
     def schedule(self) -> ScheduledBatch | None:
         """The next step's batch, or None when there is nothing to run."""
+        if self.config.mixed_prefill_tokens > 0:
+            return self._mixed_step()
         if self.waiting:
             fresh = self._admit()
             if fresh:
@@ -172,6 +191,55 @@ class Scheduler:
         # free for it (rejection at add time guarantees it fits).
         assert running, "scheduler evicted every running sequence"
         return ScheduledBatch(list(running), is_prefill=False, preempted=evicted)
+
+    def _mixed_step(self) -> ScheduledBatch | None:
+        """The opt-in chunked-prefill policy: every running sequence gets the
+        slots for its next tokens (evicting the newest running sequence while
+        the pool has none, as a decode step does); decoding sequences feed one
+        token, sequences still in their prompt feed their next chunk out of the
+        step's ``mixed_prefill_tokens`` (admission order), and what is left of
+        that budget admits requests from the head of the queue."""
+        cfg, pool, running = self.config, self.allocator, self.running
+        evicted: list[Sequence] = []
+        k = 0
+        while k < len(running):
+            seq = running[k]
+            if pool.can_append_slot(seq):
+                pool.append_slot(seq)
+                k += 1
+                continue
+            victim = running.pop()
+            self._preempt(victim)
+            evicted.append(victim)
+        budget = cfg.mixed_prefill_tokens
+        seqs: list[Sequence] = []
+        lens: list[int] = []
+        for seq in running:
+            left = seq.num_uncached_tokens
+            n = 1 if left == 1 else min(left, budget)
+            if n <= 0:
+                continue  # still in its prompt, no budget left this step
+            if left > 1:
+                budget -= n
+            seqs.append(seq)
+            lens.append(n)
+        while self.waiting and budget > 0 and len(running) < cfg.max_num_seqs:
+            head = self.waiting[0]
+            rows = head.num_tokens  # nothing of it is cached: prompt, plus outputs after a preemption
+            spare = cfg.watermark_blocks if running else 0
+            if pool.blocks_needed(rows) + spare > pool.num_free_blocks:
+                break
+            self.waiting.popleft()
+            pool.allocate(head)
+            head.status = SequenceStatus.RUNNING
+            running.append(head)
+            n = min(rows, budget)
+            budget -= n
+            seqs.append(head)
+            lens.append(n)
+        if not seqs:
+            return None
+        return ScheduledBatch(seqs, is_prefill=False, preempted=evicted, new_lens=lens)
 
     def _preempt(self, seq: Sequence) -> None:
         self.num_discarded_positions += seq.num_cached_tokens  # recomputed on readmission
