@@ -50,6 +50,7 @@ PEAKS_PATH = ROOT / "MEASURED_PEAKS.json"
 # ncu captures of the attention kernel on each workload's shape: DRAM traffic
 # (read + write) over algorithmic bytes, scaled here to this run's launches.
 TRAFFIC_PROFILES = {"cfg2": ROOT / "profiles" / "paged_attention_cfg2.md",
+                    "cfg3": ROOT / "profiles" / "paged_attention_cfg3.md",
                     "cfg4": ROOT / "profiles" / "paged_attention_cfg4_small.md"}  # fmt: skip
 FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 2**20
@@ -779,7 +780,9 @@ def run_mixed(args, world, rank, local) -> dict | None:
             "peak": peak,
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": None,
+            "traffic": traffic_ratio("cfg3") * abytes if traffic_ratio("cfg3") else None,
+            "traffic_source": f"ncu DRAM read+write / algorithmic bytes = {traffic_ratio('cfg3')} on a captured "
+                              "launch (profiles/paged_attention_cfg3.md), times this run's algorithmic bytes",
             "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
             "algorithmic_bytes_per_launch": abytes,
             "avg_launch_ms": attn_ms,
