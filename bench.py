@@ -51,6 +51,7 @@ PEAKS_PATH = ROOT / "MEASURED_PEAKS.json"
 # (read + write) over algorithmic bytes, scaled here to this run's launches.
 TRAFFIC_PROFILES = {"cfg2": ROOT / "profiles" / "paged_attention_cfg2.md",
                     "cfg3": ROOT / "profiles" / "paged_attention_cfg3.md",
+                    "kvwrite": ROOT / "profiles" / "kv_write_16k_rows.md",
                     "cfg4": ROOT / "profiles" / "paged_attention_cfg4_small.md"}  # fmt: skip
 FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 2**20
@@ -802,6 +803,109 @@ def run_mixed(args, world, rank, local) -> dict | None:
     }
 
 
+def run_kvwrite(args, world, rank, local) -> dict | None:
+    """The KV-write kernels alone at a prefill-sized step: --num-seqs prompts
+    (default 64) of 256 tokens each (16,384 new rows) written into a shuffled
+    pool of 16-token blocks, GPT-2 124M shapes.  Two kernels, each timed as a
+    stream of launches between two CUDA events (12 layers per step, L2 flushed
+    by a 512 MB read before each step):
+      * tq_qkv_bias_kv_write (the model's c_attn epilogue): reads the c_attn
+        output rows [N, 3C], writes q [N, C] and the K/V rows into the pool;
+      * tq_kv_write (the plain scatter): reads K/V from the [N, 3C] rows and
+        writes them into the pool.
+    ``value`` is the fused kernel's algorithmic HBM GB/s."""
+    from tokquay_b200 import BlockAllocator
+    from tokquay_b200.kv_cache import DevicePagedBatch
+
+    from tokquay_b200 import GPT2Config
+    from tokquay_b200 import workloads as W
+
+    device = torch.device("cuda", local)
+    model_cfg = GPT2Config(**W.GPT2_SMALL)
+    C = model_cfg.n_embd
+    n_prompts, plen, bs = (args.num_seqs or 64), 256, 16
+    N = n_prompts * plen
+    a = BlockAllocator(model_cfg, n_prompts * plen // bs + 8, bs, device=device)
+    import random as _random
+
+    _random.Random(7).shuffle(a._free)
+    tables = [a._take(plen // bs) for _ in range(n_prompts)]
+    batch = DevicePagedBatch(a, tables, [0] * n_prompts, [plen] * n_prompts)
+    g = torch.Generator(device=device).manual_seed(0)
+    qkv = torch.randn(N, 3 * C, device=device, generator=g)
+    bias = torch.randn(3 * C, device=device, generator=g)
+    q = torch.empty(N, C, device=device)
+    flush = torch.ones(128 << 20, device=device)
+    sid = torch.cuda.current_stream(device).cuda_stream
+    K, Wm, L = args.steps, args.warmup, model_cfg.n_layer
+
+    def timed(fn):
+        per = []
+        for k in range(Wm + K):
+            flush.sum()
+            torch.cuda._sleep(1_000_000)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for layer in range(L):
+                fn(layer)
+            e1.record()
+            torch.cuda.synchronize(device)
+            if k >= Wm:
+                per.append(e0.elapsed_time(e1) / L)
+        return sum(per) / len(per)
+
+    with ClockSampler(local) as clocks:
+        fused_ms = timed(lambda layer: batch.write_qkv_rows(layer, qkv, 1, 0, bias, q, sid))
+        plain_ms = timed(lambda layer: batch.write_rows(layer, qkv, C, 2 * C, sid))
+    assert _lib.device_status() == 0
+    # Algorithmic bytes: fused -- rows [N, 3C] read, q [N, C] and K/V [N, 2C] written (bias once);
+    # plain -- K/V [N, 2C] read and written.
+    fused_bytes = N * 3 * C * 4 + N * C * 4 + N * 2 * C * 4 + 3 * C * 4
+    plain_bytes = 2 * N * 2 * C * 4
+    peaks = json.loads(PEAKS_PATH.read_text()) if PEAKS_PATH.exists() else {}
+    peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
+    fused = fused_bytes / (fused_ms * 1e-3) / 1e9
+    plain = plain_bytes / (plain_ms * 1e-3) / 1e9
+    if rank != 0:
+        return None
+    traffic = traffic_ratio("kvwrite")
+    return {
+        "metric": "KV-write HBM GB/s (fused c_attn epilogue)",
+        "value": fused,
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": Wm,
+        "ms_per_step": fused_ms * L,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"KV write of {n_prompts} prompts x {plen} tokens ({N} rows), GPT-2 124M shapes, "
+                               f"bs {bs}, shuffled blocks",
+                   "l2": "a 512 MB read before each step's 12 launches; each launch moves > 200 MB"},  # fmt: skip
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "qkv_bias_kv_write_kernel",
+            "achieved": fused,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": fused / peak,
+            "traffic": traffic * fused_bytes if traffic else None,
+            "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
+            "algorithmic_bytes_per_launch": fused_bytes,
+            "avg_launch_ms": fused_ms,
+            "timing": "CUDA events around 12 back-to-back launches (one per layer), interval / 12",
+        },
+        "kv_write_plain": {"kernel": "kv_write_kernel", "achieved": plain, "frac": plain / peak,
+                           "algorithmic_bytes_per_launch": plain_bytes, "avg_launch_ms": plain_ms},
+        "e2e": None,
+        "gpu_launches": 2 * L * (Wm + K),
+        "clocks": clocks.summary(),
+    }
+
+
 def cpu_oracle_mixed_rate(bs: int, reps: int, seed: int) -> tuple[float, str, int]:
     """The numpy oracle on config 3's mixed step (every host core)."""
     import oracle
@@ -975,7 +1079,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["cfg3", "cfg5"], default="cfg2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["cfg3", "cfg5", "kvwrite"], default="cfg2")
     ap.add_argument("--block-size", type=int, default=0, help="config 3: block size (16 or 32; default 16)")
     ap.add_argument("--trace-requests", type=int, default=400, help="config 5: requests of the trace served")
     ap.add_argument("--rate", default="64", help="config 5: arrival rate in requests/s, or inf for a burst")
@@ -1004,6 +1108,12 @@ def main():
     world, rank, local = info.world, info.rank, info.local
     if args.workload == "cfg5":
         res = run_serving(args, world, rank, local)
+        if rank == 0 and res is not None:
+            _emit(res)
+        _replicas.teardown(info)
+        return
+    if args.workload == "kvwrite":
+        res = run_kvwrite(args, world, rank, local)
         if rank == 0 and res is not None:
             _emit(res)
         _replicas.teardown(info)
