@@ -33,23 +33,36 @@ __global__ void __launch_bounds__(1024) kv_write_kernel(const KvWriteParams p) {
   const int per_kv4 = p.n_head * 16;  // float4 per K (or V) row of one token
   const long long pool_slots = p.num_blocks << p.log2_bs;
   const size_t head_stride4 = (size_t)p.block_size * 16;
-  for (int n = blockIdx.x; n < n_tok; n += gridDim.x) {
-    const long long slot = p.slots[n];
-    if (slot < 0 || slot >= pool_slots) {
-      if (threadIdx.x == 0) raise_device_error(TQ_DEVERR_BAD_SLOT);
-      continue;
-    }
+  auto valid = [&](long long slot) {
+    if (slot >= 0 && slot < pool_slots) return true;
+    if (threadIdx.x == 0) raise_device_error(TQ_DEVERR_BAD_SLOT);
+    return false;
+  };
+  auto dst_of = [&](long long slot, int kv, int g) {
     const long long blk = slot >> p.log2_bs;
     const int off = (int)(slot & (p.block_size - 1));
+    return reinterpret_cast<float4*>(
+               p.pool + ((((size_t)blk * p.n_layer + p.layer) * 2 + kv) * p.n_head) * (size_t)p.block_size * 64 +
+               (size_t)off * 64) +
+           (g >> 4) * head_stride4 + (g & 15);
+  };
+  // Two tokens per iteration: both slots, then both tokens' loads, are in
+  // flight before anything is stored.
+  for (int n = blockIdx.x; n < n_tok; n += 2 * gridDim.x) {
+    const int n2 = n + gridDim.x;
+    const bool has2 = n2 < n_tok;
+    const long long slot = p.slots[n];
+    const long long slot2 = has2 ? p.slots[n2] : 0;
+    const bool ok = valid(slot), ok2 = has2 && valid(slot2);
     for (int f = threadIdx.x; f < 2 * per_kv4; f += blockDim.x) {
       const int kv = f >= per_kv4;
       const int g = f - kv * per_kv4;
-      const float4 v = reinterpret_cast<const float4*>(p.qkv + (size_t)n * p.qkv_stride +
-                                                       (kv ? p.v_col : p.k_col))[g];
-      float4* dst = reinterpret_cast<float4*>(
-          p.pool + ((((size_t)blk * p.n_layer + p.layer) * 2 + kv) * p.n_head) * (size_t)p.block_size * 64 +
-          (size_t)off * 64);
-      dst[(g >> 4) * head_stride4 + (g & 15)] = v;
+      const long long col = kv ? p.v_col : p.k_col;
+      float4 v, v2;
+      if (ok) v = reinterpret_cast<const float4*>(p.qkv + (size_t)n * p.qkv_stride + col)[g];
+      if (ok2) v2 = reinterpret_cast<const float4*>(p.qkv + (size_t)n2 * p.qkv_stride + col)[g];
+      if (ok) *dst_of(slot, kv, g) = v;
+      if (ok2) *dst_of(slot2, kv, g) = v2;
     }
   }
 }
@@ -85,9 +98,11 @@ __global__ void __launch_bounds__(1024) qkv_bias_kv_write_kernel(const QkvWriteP
   const long long pool_slots = p.num_blocks << p.log2_bs;
   const float4 b = reinterpret_cast<const float4*>(p.bias)[t];
   const long long ps4 = p.part_stride >> 2;
-  for (int r = blockIdx.x; r < n; r += gridDim.x) {
+  // Row r: the sum of its partial sums plus the bias, and (K/V threads) its slot.
+  auto load_row = [&](int r, float4& v, long long& slot) {
     const float4* src = reinterpret_cast<const float4*>(p.parts) + (size_t)r * 3 * C4 + t;
-    float4 v = src[0];
+    slot = t < C4 ? 0 : p.slots[r];
+    v = src[0];
     if (NP > 0) {
       float4 u[NP > 1 ? NP - 1 : 1];
 #pragma unroll
@@ -109,14 +124,15 @@ __global__ void __launch_bounds__(1024) qkv_bias_kv_write_kernel(const QkvWriteP
       }
     }
     v = make_float4(v.x + b.x, v.y + b.y, v.z + b.z, v.w + b.w);
+  };
+  auto store_row = [&](int r, const float4& v, long long slot) {
     if (t < C4) {
       reinterpret_cast<float4*>(p.q_out + (size_t)r * p.q_stride)[t] = v;
-      continue;
+      return;
     }
-    const long long slot = p.slots[r];
     if (slot < 0 || slot >= pool_slots) {
       if (t == C4) raise_device_error(TQ_DEVERR_BAD_SLOT);
-      continue;
+      return;
     }
     const int kv = t >= 2 * C4;
     const int g = t - C4 - kv * C4;  // float4 within the K (or V) row: head g / 16, dims (g % 16) * 4
@@ -126,6 +142,16 @@ __global__ void __launch_bounds__(1024) qkv_bias_kv_write_kernel(const QkvWriteP
         p.pool + (((((size_t)blk * p.n_layer + p.layer) * 2 + kv) * p.n_head + (g >> 4)) * (size_t)p.block_size +
                   off) * 64);
     dst[g & 15] = v;
+  };
+  // Two rows per iteration, both rows' loads in flight before either is stored.
+  for (int r = blockIdx.x; r < n; r += 2 * gridDim.x) {
+    const int r2 = r + gridDim.x;
+    float4 v, v2;
+    long long slot = 0, slot2 = 0;
+    load_row(r, v, slot);
+    if (r2 < n) load_row(r2, v2, slot2);
+    store_row(r, v, slot);
+    if (r2 < n) store_row(r2, v2, slot2);
   }
 }
 
