@@ -11,7 +11,9 @@ plan into the workspace and launches the graph.
 A bucket's graph runs any decode batch of up to ``bucket`` sequences: the
 kernels read the step's true token, work-item and combine counts from the
 device plan, and the GEMMs / argmax run over the bucket's rows (the rows past
-the batch hold stale values whose results are never read).
+the batch hold stale values whose results are never read).  Steps that feed
+prompt chunks beside decode rows (the opt-in chunked-prefill scheduler) replay
+graphs keyed by (sequence bucket, row capacity) the same way.
 """
 
 from __future__ import annotations
@@ -48,7 +50,9 @@ class DecodeGraphRunner:
         self.buckets = sorted(set(int(b) for b in buckets))
         self.mixed_extra = sorted(set(int(e) for e in mixed_extra))
         self.max_ctx = max_ctx or model.cfg.n_positions
-        self._graphs: dict[int, tuple] = {}
+        # decode bucket (int) or mixed (sequences, rows) capacities -> (graph, workspace,
+        # logits, greedy tokens, launches per replay)
+        self._graphs: dict[int | tuple[int, int], tuple] = {}
         self._pool = None  # one private memory pool shared by every bucket's graph
 
     @property
