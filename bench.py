@@ -1059,6 +1059,112 @@ def run_reference(args, world, rank):
     }
 
 
+def run_reference_gpu(args, world, rank, local) -> dict | None:
+    """The reference's algorithm for this path, on the same B200: the "reference
+    on B200" column of the measurement plan.  The reference itself (Python +
+    torch) cannot travel to the GPU box, so its per-step algorithm is restated
+    here in plain torch: the padded index tensors built in Python from the
+    sequences (tokquay/kv_cache.py:174-226), the scatter of the new K/V rows
+    (:228-232), the dense gather of every sequence's blocks into a
+    [B, H, nb*bs, d] copy (:234-242), masked softmax attention over the padded
+    key axis (tokquay/model.py:94-96), torch LayerNorm / GELU(tanh) / fp32
+    linears with TF32 off (:108-124), last-row LM head (:179-181) and the greedy
+    ``argmax(-1).tolist()`` (tokquay/engine.py:189-194).  Same workload, model
+    weights and pool as this build's arm; one step at a time, no CUDA graphs,
+    as the reference runs."""
+    import math
+
+    import torch.nn.functional as F
+
+    spec = workload_spec(args)
+    device = torch.device("cuda", local)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.set_float32_matmul_precision("highest")
+    model = make_model(device)
+    cfg = model.cfg
+    a = make_allocator(spec, cfg, device)
+    seqs = make_case(spec, a, 2, rank, world).seqs
+    C, H, L, bs = cfg.n_embd, cfg.n_head, cfg.n_layer, a.block_size
+    d, eps = C // H, cfg.layer_norm_eps
+    pool = a.pool
+
+    @torch.no_grad()
+    def step() -> list[int]:
+        B = len(seqs)
+        starts = [s.num_cached_tokens for s in seqs]
+        nb = max(-(-(st + 1) // bs) for st in starts)
+        tables = torch.tensor([s.block_table[:nb] + [0] * (nb - len(s.block_table[:nb])) for s in seqs],
+                              device=device)  # fmt: skip
+        pos = torch.tensor(starts, device=device)
+        mask = (torch.arange(nb * bs, device=device)[None, :] <= pos[:, None])[:, None, None, :]
+        w_blk = torch.tensor([s.block_table[st // bs] for s, st in zip(seqs, starts)], device=device)
+        w_off = torch.tensor([st % bs for st in starts], device=device)
+        ids = torch.tensor([s.tokens_slice(st, st + 1)[0] for s, st in zip(seqs, starts)], device=device)
+        x = (model.wte.weight[ids] + model.wpe.weight[pos.clamp(max=cfg.n_positions - 1)])[:, None]  # [B, 1, C]
+        for i, blk in enumerate(model.h):
+            h = F.layer_norm(x, (C,), blk.ln_1.weight, blk.ln_1.bias, eps)
+            qkv = F.linear(h, blk.attn.c_attn.weight, blk.attn.c_attn.bias)
+            q, k, v = (qkv[..., j * C:(j + 1) * C].view(B, 1, H, d).transpose(1, 2) for j in range(3))
+            pool[w_blk, i, 0, :, w_off] = k[:, :, 0]
+            pool[w_blk, i, 1, :, w_off] = v[:, :, 0]
+            kd = pool[tables, i, 0].permute(0, 2, 1, 3, 4).reshape(B, H, nb * bs, d)
+            vd = pool[tables, i, 1].permute(0, 2, 1, 3, 4).reshape(B, H, nb * bs, d)
+            sc = (q @ kd.transpose(-1, -2)) / math.sqrt(d)
+            att = torch.softmax(sc.masked_fill(~mask, float("-inf")), dim=-1) @ vd
+            x = x + F.linear(att.transpose(1, 2).reshape(B, 1, C), blk.attn.c_proj.weight, blk.attn.c_proj.bias)
+            h = F.layer_norm(x, (C,), blk.ln_2.weight, blk.ln_2.bias, eps)
+            h = F.gelu(F.linear(h, blk.mlp.c_fc.weight, blk.mlp.c_fc.bias), approximate="tanh")
+            x = x + F.linear(h, blk.mlp.c_proj.weight, blk.mlp.c_proj.bias)
+        xf = F.layer_norm(x[:, 0], (C,), model.ln_f.weight, model.ln_f.bias, eps)
+        toks = (xf @ model.wte.weight.t()).argmax(-1).tolist()
+        for s, t in zip(seqs, toks):
+            s.num_cached_tokens += 1
+            s.append_token(t)
+            if spec["grow"]:
+                a.append_slot(s)
+            else:
+                s.num_cached_tokens -= 1
+                s.output_token_ids.pop()
+        return toks
+
+    K, Wm = args.steps, args.warmup
+    for _ in range(Wm):
+        step()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(K):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+    ms_max = max_over_ranks(e0.elapsed_time(e1), world)
+    tokens_all = sum_over_ranks(len(seqs) * K, world)
+    if rank != 0:
+        return None
+    return {
+        "impl": "reference-gpu",
+        "metric": "decode tok/s",
+        "value": tokens_all / (ms_max * 1e-3),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": Wm,
+        "ms_per_step": ms_max / K,
+        "higher_is_better": True,
+        "scaling": "strong" if spec.get("strong") else "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": spec["desc"], "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32, TF32 off",
+                   "algorithm": "the reference's per-step algorithm restated in plain torch on the GPU: dense gather "
+                                "of every sequence's blocks + masked softmax over the padded key axis"},  # fmt: skip
+        "clocks": clocks.summary(),
+    }
+
+
 def _emit(res: dict) -> None:
     """The one JSON line, on the process's real stdout (everything else --
     library banners included -- goes to stderr)."""
@@ -1085,7 +1191,7 @@ def main():
     ap.add_argument("--rate", default="64", help="config 5: arrival rate in requests/s, or inf for a burst")
     ap.add_argument("--mixed-tokens", type=int, default=0,
                     help="config 5: opt-in chunked-prefill scheduling with this many prompt tokens per step")
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graphs", action="store_true", help="launch every kernel from Python (no CUDA graphs)")
     ap.add_argument("--num-seqs", type=int, default=0, help="override the workload's sequence count (profiling)")
@@ -1106,6 +1212,12 @@ def main():
         return
     info = _replicas.setup()
     world, rank, local = info.world, info.rank, info.local
+    if args.impl == "reference-gpu":
+        res = run_reference_gpu(args, world, rank, local)
+        if rank == 0 and res is not None:
+            _emit(res)
+        _replicas.teardown(info)
+        return
     if args.workload == "cfg5":
         res = run_serving(args, world, rank, local)
         if rank == 0 and res is not None:
