@@ -1015,6 +1015,101 @@ def run_serving(args, world, rank, local) -> dict | None:
     }
 
 
+def run_serving_http(args) -> dict:
+    """Config 5 through the serving front end: the same trace as --workload
+    cfg5, sent by an HTTP client (aiohttp, open loop in real time) to
+    ``tokquay_b200.frontend`` (uvicorn, one process) over --gpus N replica
+    processes, one per GPU, round robin.  With streaming (the default) every
+    token arrives as a server-sent event and TTFT / ITL are the client's
+    clock; with --http-json each request gets one JSON body (throughput and
+    end-to-end latency only)."""
+    import asyncio
+    import math
+    import socket
+
+    import aiohttp
+    import uvicorn
+
+    from tokquay_b200.frontend import RandomGPT2Engine, ReplicaRouter, create_app
+    from tokquay_b200.serving import RequestRecord, make_workload, summarize
+
+    n = args.gpus
+    P = args.mixed_tokens
+    rate = math.inf if args.rate == "inf" else float(args.rate)
+    workload = make_workload(rate, args.trace_requests, seed=0)
+    stream = not args.http_json
+    factory = RandomGPT2Engine(num_blocks=1024, block_size=16, mixed_prefill_tokens=P, seed=0, warm=True)
+    router = ReplicaRouter(factory, list(range(n)))
+    app = create_app(router)
+
+    async def one(session, url, spec, t0, rec):
+        await asyncio.sleep(max(0.0, spec.arrival - (time.perf_counter() - t0)))
+        body = {"prompt_token_ids": list(spec.prompt_ids), "max_tokens": spec.output_len, "ignore_eos": True,
+                "stream": stream}  # fmt: skip
+        async with session.post(url, json=body) as resp:
+            if resp.status != 200:
+                raise RuntimeError(f"HTTP {resp.status}: {await resp.text()}")
+            if stream:
+                async for line in resp.content:
+                    if line.startswith(b"data: "):
+                        rec.token_times.append(time.perf_counter() - t0)
+            else:
+                out = await resp.json()
+                rec.token_times.extend([time.perf_counter() - t0] * len(out["token_ids"]))
+
+    async def main():
+        sock = socket.socket()
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+        server = uvicorn.Server(uvicorn.Config(app, log_level="warning", timeout_keep_alive=600))
+        task = asyncio.create_task(server.serve(sockets=[sock]))
+        t_ready = time.perf_counter()
+        while not server.started:  # the replicas are built and warmed in the app's start-up
+            if task.done():
+                task.result()
+                raise RuntimeError("the front end failed to start (its log is above)")
+            await asyncio.sleep(0.1)
+        log(f"front end up with {n} replica(s) in {time.perf_counter() - t_ready:.1f} s")
+        url = f"http://127.0.0.1:{port}/generate"
+        records = [RequestRecord(spec.arrival, len(spec.prompt_ids), spec.output_len) for spec in workload]
+        timeout = aiohttp.ClientTimeout(total=None)
+        async with aiohttp.ClientSession(connector=aiohttp.TCPConnector(limit=0), timeout=timeout) as session:
+            t0 = time.perf_counter()
+            await asyncio.gather(*(one(session, url, sp, t0, r) for sp, r in zip(workload, records)))
+            wall = time.perf_counter() - t0
+        health = router.stats()
+        server.should_exit = True
+        await task
+        return records, wall, health
+
+    records, wall, health = asyncio.run(main())
+    out = summarize(records, [])
+    if not stream:  # one body per request: no per-token times
+        out["ttft_ms"] = out["itl_ms"] = None
+    return {
+        "metric": "serving tok/s over HTTP (config 5 trace)",
+        "value": out["throughput_tok_s"],
+        "unit": "tok/s",
+        "n_gpus": n,
+        "higher_is_better": True,
+        "scaling": "weak" if math.isinf(rate) else "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"BASELINE config 5, first {args.trace_requests} requests at rate {args.rate} "
+                               f"req/s (seed 0), HTTP {'SSE streams' if stream else 'JSON bodies'} to one "
+                               f"front end, round robin over {n} replica process(es), 1,024 x 16 KV slots each",
+                   "scheduler": ("the reference's (prefill and decode steps alternate)" if P == 0 else
+                                 f"opt-in chunked prefill: decodes + up to {P} prompt tokens per step"),
+                   "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32, TF32 off",
+                   "parallelism": f"replicas{n} (processes)"},  # fmt: skip
+        "client": {k: out[k] for k in ("requests", "output_tokens", "duration_s", "ttft_ms", "itl_ms",
+                                       "latency_ms")},
+        "preemptions": health["preemptions"],
+        "wall_s": wall,
+    }
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return None
@@ -1185,12 +1280,14 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["cfg3", "cfg5", "kvwrite"], default="cfg2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["cfg3", "cfg5", "cfg5-http", "kvwrite"], default="cfg2")
     ap.add_argument("--block-size", type=int, default=0, help="config 3: block size (16 or 32; default 16)")
     ap.add_argument("--trace-requests", type=int, default=400, help="config 5: requests of the trace served")
     ap.add_argument("--rate", default="64", help="config 5: arrival rate in requests/s, or inf for a burst")
     ap.add_argument("--mixed-tokens", type=int, default=0,
                     help="config 5: opt-in chunked-prefill scheduling with this many prompt tokens per step")
+    ap.add_argument("--http-json", action="store_true",
+                    help="cfg5-http: one JSON body per request instead of a server-sent event per token")
     ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graphs", action="store_true", help="launch every kernel from Python (no CUDA graphs)")
@@ -1202,6 +1299,14 @@ def main():
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")
         args.warmup = 3
+    if args.workload == "cfg5-http":
+        # One process: the front end spawns its own replica processes (--gpus of them).
+        if args.impl != "ours" or ReplicaInfo.from_env().world > 1:
+            _emit({"impl": args.impl, "unavailable": "cfg5-http runs our front end in one process "
+                                                     "(not under torchrun, no reference arm)"})  # fmt: skip
+            return
+        _emit(run_serving_http(args))
+        return
     if args.impl == "reference":
         # The CPU reference arm runs on rank 0 alone; no process group is needed.
         info = ReplicaInfo.from_env()

@@ -213,7 +213,10 @@ def _replica_main(index: int, device, factory: Callable, inbox, outbox) -> None:
 class RandomGPT2Engine:
     """Picklable engine factory for a replica: GPT-2 124M with every
     parameter drawn from N(0, 0.02) (no pretrained weights travel with this
-    package), its KV pool, CUDA-graph decode steps and a scheduler."""
+    package), its KV pool, CUDA-graph decode steps and a scheduler.  With
+    ``warm``, the decode graphs a batch of up to ``max_num_seqs`` can use are
+    captured, and a few short requests run, before the replica reports ready,
+    so the first requests served pay for neither."""
 
     num_blocks: int = 1024
     block_size: int = 16
@@ -221,6 +224,7 @@ class RandomGPT2Engine:
     max_num_batched_tokens: int = 2048
     mixed_prefill_tokens: int = 0
     seed: int = 0
+    warm: bool = False
 
     def __call__(self, device):
         import torch
@@ -247,6 +251,19 @@ class RandomGPT2Engine:
             runner.mixed_extra = sorted({max(1, P // 4), max(1, P // 2), P})
         sched = SchedulerConfig(max_num_seqs=self.max_num_seqs, max_num_batched_tokens=self.max_num_batched_tokens,
                                 max_model_len=cfg.n_positions, mixed_prefill_tokens=self.mixed_prefill_tokens)  # fmt: skip
+        if self.warm:
+            for b in runner.buckets:
+                if b <= self.max_num_seqs:
+                    runner.graph(b)
+                    for e in runner.mixed_extra if self.mixed_prefill_tokens > 0 else ():
+                        runner.graph((b, b + e))
+            warm = Engine(model, alloc, sched)
+            rng = torch.Generator().manual_seed(99)
+            for n in (16, 64, 200, 256):  # the prefill shapes of short and long prompts
+                ids = torch.randint(0, cfg.vocab_size - 1, (n,), generator=rng).tolist()
+                warm.add_request(ids, SamplingParams(max_tokens=4, ignore_eos=True))
+            warm.run_until_done()
+            torch.cuda.synchronize(dev)
         return Engine(model, alloc, sched)
 
 
