@@ -1019,7 +1019,8 @@ def run_serving_http(args) -> dict:
     """Config 5 through the serving front end: the same trace as --workload
     cfg5, sent by an HTTP client (aiohttp, open loop in real time) to
     ``tokquay_b200.frontend`` (uvicorn, one process) over --gpus N replica
-    processes, one per GPU, round robin.  With streaming (the default) every
+    processes, one per GPU, round robin (--front-ends K: K server processes on
+    one port, each over its share of the replicas).  With streaming (the default) every
     token arrives as a server-sent event and TTFT / ITL are the client's
     clock; with --http-json each request gets one JSON body (throughput and
     end-to-end latency only)."""
@@ -1030,7 +1031,7 @@ def run_serving_http(args) -> dict:
     import aiohttp
     import uvicorn
 
-    from tokquay_b200.frontend import RandomGPT2Engine, ReplicaRouter, create_app
+    from tokquay_b200.frontend import FrontEnds, RandomGPT2Engine, ReplicaRouter, create_app
     from tokquay_b200.serving import RequestRecord, make_workload, summarize
 
     n = args.gpus
@@ -1039,8 +1040,9 @@ def run_serving_http(args) -> dict:
     workload = make_workload(rate, args.trace_requests, seed=0)
     stream = not args.http_json
     factory = RandomGPT2Engine(num_blocks=1024, block_size=16, mixed_prefill_tokens=P, seed=0, warm=True)
-    router = ReplicaRouter(factory, list(range(n)))
-    app = create_app(router)
+    K = args.front_ends
+    router = ReplicaRouter(factory, list(range(n))) if K == 1 else None
+    app = create_app(router) if K == 1 else None
 
     async def one(session, url, spec, t0, rec):
         await asyncio.sleep(max(0.0, spec.arrival - (time.perf_counter() - t0)))
@@ -1057,6 +1059,14 @@ def run_serving_http(args) -> dict:
                 out = await resp.json()
                 rec.token_times.extend([time.perf_counter() - t0] * len(out["token_ids"]))
 
+    async def client(url):
+        records = [RequestRecord(spec.arrival, len(spec.prompt_ids), spec.output_len) for spec in workload]
+        timeout = aiohttp.ClientTimeout(total=None)
+        async with aiohttp.ClientSession(connector=aiohttp.TCPConnector(limit=0), timeout=timeout) as session:
+            t0 = time.perf_counter()
+            await asyncio.gather(*(one(session, url, sp, t0, r) for sp, r in zip(workload, records)))
+            return records, time.perf_counter() - t0
+
     async def main():
         sock = socket.socket()
         sock.bind(("127.0.0.1", 0))
@@ -1071,18 +1081,24 @@ def run_serving_http(args) -> dict:
             await asyncio.sleep(0.1)
         log(f"front end up with {n} replica(s) in {time.perf_counter() - t_ready:.1f} s")
         url = f"http://127.0.0.1:{port}/generate"
-        records = [RequestRecord(spec.arrival, len(spec.prompt_ids), spec.output_len) for spec in workload]
-        timeout = aiohttp.ClientTimeout(total=None)
-        async with aiohttp.ClientSession(connector=aiohttp.TCPConnector(limit=0), timeout=timeout) as session:
-            t0 = time.perf_counter()
-            await asyncio.gather(*(one(session, url, sp, t0, r) for sp, r in zip(workload, records)))
-            wall = time.perf_counter() - t0
+        records, wall = await client(url)
         health = router.stats()
         server.should_exit = True
         await task
         return records, wall, health
 
-    records, wall, health = asyncio.run(main())
+    if K == 1:
+        records, wall, health = asyncio.run(main())
+    else:
+        fe = FrontEnds(factory, list(range(n)), K)
+        t_ready = time.perf_counter()
+        fe.start()
+        log(f"{K} front ends up with {n} replica(s) in {time.perf_counter() - t_ready:.1f} s")
+        try:
+            records, wall = asyncio.run(client(f"http://127.0.0.1:{fe.port}/generate"))
+        finally:
+            fe.stop()
+        health = {"preemptions": None}  # each front end answers for its own replicas only
     out = summarize(records, [])
     if not stream:  # one body per request: no per-token times
         out["ttft_ms"] = out["itl_ms"] = None
@@ -1097,8 +1113,9 @@ def run_serving_http(args) -> dict:
         "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": f"BASELINE config 5, first {args.trace_requests} requests at rate {args.rate} "
-                               f"req/s (seed 0), HTTP {'SSE streams' if stream else 'JSON bodies'} to one "
-                               f"front end, round robin over {n} replica process(es), 1,024 x 16 KV slots each",
+                               f"req/s (seed 0), HTTP {'SSE streams' if stream else 'JSON bodies'} to {K} "
+                               f"server process(es) on one port, round robin over {n} replica process(es), "
+                               f"1,024 x 16 KV slots each",
                    "scheduler": ("the reference's (prefill and decode steps alternate)" if P == 0 else
                                  f"opt-in chunked prefill: decodes + up to {P} prompt tokens per step"),
                    "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32, TF32 off",
@@ -1286,6 +1303,8 @@ def main():
     ap.add_argument("--rate", default="64", help="config 5: arrival rate in requests/s, or inf for a burst")
     ap.add_argument("--mixed-tokens", type=int, default=0,
                     help="config 5: opt-in chunked-prefill scheduling with this many prompt tokens per step")
+    ap.add_argument("--front-ends", type=int, default=1,
+                    help="cfg5-http: server processes sharing the port (each over its share of the replicas)")
     ap.add_argument("--http-json", action="store_true",
                     help="cfg5-http: one JSON body per request instead of a server-sent event per token")
     ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours")

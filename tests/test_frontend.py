@@ -214,3 +214,30 @@ def test_http_health_and_503_once_every_replica_failed():
         assert client.post("/generate", json={"prompt_token_ids": [1]}).status_code == 503
         r = client.post("/generate", json={"prompt_token_ids": [1], "stream": True})
         assert r.status_code == 503
+
+
+def test_front_ends_share_one_port():
+    """Two server processes on one port (SO_REUSEPORT), one stand-in replica
+    each: every request on its own connection gets its tokens, whichever
+    process takes it, and stop() ends every process."""
+    import httpx
+
+    from tokquay_b200.frontend import FrontEnds
+
+    fe = FrontEnds(EchoFactory(), ["r0", "r1"], 2)
+    fe.start(timeout_s=120)
+    try:
+        url = f"http://{fe.host}:{fe.port}"
+        seen = set()
+        for i in range(24):
+            with httpx.Client(timeout=60) as client:  # a new connection per request
+                r = client.post(f"{url}/generate", json={"prompt_token_ids": [i + 1], "max_tokens": 3})
+                assert r.status_code == 200 and r.json()["token_ids"] == expected_tokens([i + 1], 3)
+                h = client.get(f"{url}/health").json()
+                assert h["status"] == "ok" and len(h["replicas"]) == 1  # the process's own replica
+                seen.add(h["replicas"][0]["device"])
+        assert seen <= {"r0", "r1"}
+    finally:
+        procs = list(fe._procs)
+        fe.stop()
+    assert procs and not any(p.is_alive() for p in procs)

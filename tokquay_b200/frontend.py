@@ -64,6 +64,7 @@ __all__ = [
     "RandomGPT2Engine",
     "IncrementalDetokenizer",
     "GenerateRequest",
+    "FrontEnds",
     "create_app",
     "main",
 ]
@@ -661,9 +662,101 @@ def create_app(router: ReplicaRouter, tokenizer=None) -> FastAPI:
     return app
 
 
+# ---- several server processes on one port ---------------------------------------------
+
+
+def _shared_port_socket(host: str, port: int):
+    """A TCP socket bound with SO_REUSEPORT: every server process binds its own
+    on the same port, and the kernel spreads new connections over them."""
+    import socket
+
+    sock = socket.socket(socket.AF_INET, socket.SOCK_STREAM)
+    sock.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEADDR, 1)
+    sock.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEPORT, 1)
+    sock.bind((host, port))
+    return sock
+
+
+def _front_end_main(factory: Callable, devices: list, host: str, port: int, tokenizer_factory, ready) -> None:
+    """One server process: uvicorn on the shared port, its own router over
+    ``devices``; sets ``ready`` once its replicas have started.  SIGTERM stops
+    it gracefully (the router stops its replicas)."""
+    import uvicorn
+
+    tokenizer = tokenizer_factory() if tokenizer_factory is not None else None
+    app = create_app(ReplicaRouter(factory, devices), tokenizer)
+    server = uvicorn.Server(uvicorn.Config(app, log_level="warning", timeout_keep_alive=600))
+
+    async def run():
+        task = asyncio.create_task(server.serve(sockets=[_shared_port_socket(host, port)]))
+        while not server.started:
+            if task.done():
+                return
+            await asyncio.sleep(0.05)
+        ready.set()
+        await task
+
+    asyncio.run(run())
+
+
+class FrontEnds:
+    """``n_front_ends`` server processes sharing one port, front end i
+    serving replicas ``devices[i::n_front_ends]``.
+
+    One Python server process relays a few tens of thousands of token events
+    per second, fewer than two busy replicas produce.  Here the kernel spreads
+    connections over the processes (SO_REUSEPORT), so each process relays
+    only its own replicas' tokens.  Each request goes to one server process
+    and then to its replicas round robin.  ``/health`` answers for the
+    replicas of the process that took the connection."""
+
+    def __init__(self, factory: Callable, devices: list, n_front_ends: int, host: str = "127.0.0.1",
+                 port: int = 0, tokenizer_factory: Callable | None = None):  # fmt: skip
+        if not 1 <= n_front_ends <= len(devices):
+            raise ValueError(f"need 1 <= front ends <= replicas, got {n_front_ends} for {len(devices)}")
+        self._ctx = mp.get_context("spawn")
+        self._groups = [list(devices[i::n_front_ends]) for i in range(n_front_ends)]
+        self._factory, self._tokenizer_factory = factory, tokenizer_factory
+        self.host = host
+        self._hold = _shared_port_socket(host, port)  # keeps the port (not listening: takes no connections)
+        self.port = self._hold.getsockname()[1]
+        self._procs: list = []
+
+    def start(self, timeout_s: float = 600.0) -> None:
+        """Spawn every server process; return once each has its replicas up."""
+        events = []
+        for i, group in enumerate(self._groups):
+            ev = self._ctx.Event()
+            p = self._ctx.Process(target=_front_end_main, name=f"tokquay-front-end-{i}",
+                                  args=(self._factory, group, self.host, self.port, self._tokenizer_factory, ev))  # fmt: skip
+            p.start()
+            self._procs.append(p)
+            events.append(ev)
+        deadline = time.monotonic() + timeout_s
+        for i, (p, ev) in enumerate(zip(self._procs, events)):
+            while not ev.wait(0.2):
+                if not p.is_alive() or time.monotonic() > deadline:
+                    self.stop()
+                    raise EngineError(f"front end {i} did not start" + ("" if p.is_alive() else
+                                      f" (exit code {p.exitcode})"))  # fmt: skip
+
+    def stop(self, timeout_s: float = 60.0) -> None:
+        for p in self._procs:
+            if p.is_alive():
+                p.terminate()  # SIGTERM: uvicorn shuts down and the router stops its replicas
+        for p in self._procs:
+            p.join(timeout_s)
+            if p.is_alive():
+                p.kill()
+                p.join(timeout_s)
+        self._procs = []
+        self._hold.close()
+
+
 def main(argv: list[str] | None = None) -> None:
-    """``python -m tokquay_b200.frontend --replicas N``: serve N random-init
-    GPT-2 replicas, one per GPU (cuda:0 .. cuda:N-1)."""
+    """``python -m tokquay_b200.frontend --replicas N [--front-ends K]``: serve
+    N random-init GPT-2 replicas, one per GPU (cuda:0 .. cuda:N-1), behind K
+    server processes on one port."""
     import argparse
 
     ap = argparse.ArgumentParser(description="Serve GPT-2 replicas (one per GPU) with a paged KV cache.")
@@ -677,13 +770,26 @@ def main(argv: list[str] | None = None) -> None:
     ap.add_argument("--mixed-prefill-tokens", type=int, default=0,
                     help="opt-in chunked prefill: prompt tokens a decode step may carry (0: the reference policy)")
     ap.add_argument("--seed", type=int, default=0, help="seed of the random-init weights")
+    ap.add_argument("--front-ends", type=int, default=1,
+                    help="server processes sharing the port (each relays the tokens of its share of the replicas)")
     args = ap.parse_args(argv)
     import uvicorn
 
     factory = RandomGPT2Engine(args.num_blocks, args.block_size, args.max_num_seqs, args.max_num_batched_tokens,
-                               args.mixed_prefill_tokens, args.seed)  # fmt: skip
-    router = ReplicaRouter(factory, list(range(args.replicas)))
-    uvicorn.run(create_app(router), host=args.host, port=args.port)
+                               args.mixed_prefill_tokens, args.seed, warm=True)  # fmt: skip
+    if args.front_ends == 1:
+        uvicorn.run(create_app(ReplicaRouter(factory, list(range(args.replicas)))), host=args.host, port=args.port)
+        return
+    fe = FrontEnds(factory, list(range(args.replicas)), args.front_ends, args.host, args.port)
+    fe.start()
+    print(f"serving on http://{args.host}:{fe.port} with {args.front_ends} server processes", flush=True)
+    try:
+        while all(p.is_alive() for p in fe._procs):
+            time.sleep(1.0)
+    except KeyboardInterrupt:
+        pass
+    finally:
+        fe.stop()
 
 
 if __name__ == "__main__":
