@@ -241,3 +241,46 @@ def test_front_ends_share_one_port():
         procs = list(fe._procs)
         fe.stop()
     assert procs and not any(p.is_alive() for p in procs)
+
+
+def _orphaning_server(out):
+    """Runs in a spawned process: starts one replica, reports its pid, then
+    exits at once without stopping it (as a killed server process would)."""
+    import multiprocessing as mp
+    import os
+
+    from tokquay_b200.frontend import _replica_main
+
+    ctx = mp.get_context("spawn")
+    inbox, outbox = ctx.Queue(), ctx.Queue()
+    p = ctx.Process(target=_replica_main, args=(0, "r0", EchoFactory(), inbox, outbox), daemon=True)
+    p.start()
+    assert outbox.get(timeout=120)[0] == "ready"
+    out.put(p.pid)
+    out.close()
+    out.join_thread()  # the pid must leave before the abrupt exit below
+    os._exit(0)
+
+
+def _exited(pid: int) -> bool:
+    try:
+        with open(f"/proc/{pid}/stat") as f:
+            return f.read().rsplit(")", 1)[1].split()[0] in ("Z", "X")  # a zombie has exited
+    except FileNotFoundError:
+        return True
+
+
+def test_an_orphaned_replica_ends_itself():
+    import multiprocessing as mp
+    import time
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    server = ctx.Process(target=_orphaning_server, args=(q,))
+    server.start()
+    pid = q.get(timeout=180)
+    server.join(60)
+    deadline = time.monotonic() + 30
+    while not _exited(pid) and time.monotonic() < deadline:
+        time.sleep(0.2)
+    assert _exited(pid)

@@ -43,6 +43,7 @@ import itertools
 import json
 import logging
 import multiprocessing as mp
+import os
 import queue
 import threading
 import time
@@ -157,7 +158,10 @@ def _engine_stats(engine) -> dict:
 def _replica_main(index: int, device, factory: Callable, inbox, outbox) -> None:
     """A replica's whole life: build the engine on ``device``, then the
     engine loop of async_engine.py:133-156 over ``inbox`` commands
-    (``("add", req_id, ids, params)``, ``("abort", req_id)``, ``("stop",)``)."""
+    (``("add", req_id, ids, params)``, ``("abort", req_id)``, ``("stop",)``).
+    An idle replica whose server process has gone (killed, so no "stop" will
+    come) ends itself within a second."""
+    parent = os.getppid()
     try:
         if isinstance(device, int):
             import torch
@@ -169,8 +173,12 @@ def _replica_main(index: int, device, factory: Callable, inbox, outbox) -> None:
         req_of: dict[int, int] = {}  # seq_id -> req_id
         while True:
             commands = []
-            if not engine.has_unfinished():
-                commands.append(inbox.get())  # idle: sleep until something arrives
+            while not engine.has_unfinished() and not commands:
+                try:  # idle: sleep until something arrives
+                    commands.append(inbox.get(timeout=_POLL_S * 5))
+                except queue.Empty:
+                    if os.getppid() != parent:  # the server process is gone: nobody will send "stop"
+                        return
             while True:
                 try:
                     commands.append(inbox.get_nowait())
