@@ -47,12 +47,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 PEAKS_PATH = ROOT / "MEASURED_PEAKS.json"
-# ncu captures of the attention kernel on each workload's shape: DRAM traffic
-# (read + write) over algorithmic bytes, scaled here to this run's launches.
-TRAFFIC_PROFILES = {"cfg2": ROOT / "profiles" / "paged_attention_cfg2.md",
-                    "cfg3": ROOT / "profiles" / "paged_attention_cfg3.md",
-                    "kvwrite": ROOT / "profiles" / "kv_write_16k_rows.md",
-                    "cfg4": ROOT / "profiles" / "paged_attention_cfg4_small.md"}  # fmt: skip
+# ncu captures of the dominant kernel on each workload's shape: DRAM traffic
+# (read + write) over algorithmic bytes, with the capture command of each,
+# scaled here to this run's launches.
+TRAFFIC_PATH = ROOT / "profiles" / "dram_traffic.json"
 FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 2**20
 
@@ -70,12 +68,53 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
-# ------------------------------------------------------------------------------ distributed
-# One replica per GPU (tokquay_b200.replicas): no collective on the data path,
-# host reductions only for the barrier and the max-over-ranks timing.
-from tokquay_b200 import _lib  # noqa: E402
-from tokquay_b200 import replicas as _replicas  # noqa: E402
-from tokquay_b200.replicas import ReplicaInfo, barrier, max_over_ranks, replica_seed, sum_over_ranks  # noqa: E402
+# ------------------------------------------------------------------------------ modules
+def _standalone(name: str, rel: str):
+    """A pure-Python module of this repository loaded from its file, without
+    importing the ``tokquay_b200`` package (so none of its native code loads)."""
+    import importlib.util
+
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, ROOT / rel)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+# One replica per GPU (tokquay_b200/replicas.py, plain torch.distributed): no
+# collective on the data path, host reductions only for the barrier and the
+# max-over-ranks timing.
+_replicas = _standalone("tq_bench_replicas", "tokquay_b200/replicas.py")
+ReplicaInfo, barrier, replica_seed = _replicas.ReplicaInfo, _replicas.barrier, _replicas.replica_seed
+max_over_ranks, sum_over_ranks, all_over_ranks = (_replicas.max_over_ranks, _replicas.sum_over_ranks,
+                                                  _replicas.all_over_ranks)  # fmt: skip
+_lib = None  # tokquay_b200._lib, imported by _load_library() for this build's arms
+
+
+def _load_library():
+    global _lib
+    from tokquay_b200 import _lib as lib
+
+    _lib = lib
+    return lib
+
+
+def reference_package():
+    """The unmodified reference, installed next to this file by
+    baseline/install_ref.sh (importable as ``tokquay``); None if absent."""
+    path = ROOT / "baseline" / "_ref"
+    if (path / "tokquay" / "__init__.py").is_file() and str(path) not in sys.path:
+        sys.path.append(str(path))
+    try:
+        import tokquay.engine  # noqa: F401
+        import tokquay.generate  # noqa: F401
+    except ImportError:
+        return None
+    import tokquay
+
+    return tokquay
 
 
 # ------------------------------------------------------------------------------ clocks
@@ -146,14 +185,20 @@ class ClockSampler:
         }
 
 
-def traffic_ratio(workload: str) -> float | None:
-    import re
-
-    path = TRAFFIC_PROFILES.get(workload)
-    if path is None or not path.exists():
+def traffic_source(workload: str) -> str | None:
+    r = traffic_ratio(workload)
+    if r is None:
         return None
-    m = re.search(r"traffic_over_algorithmic:\s*([0-9.]+)", path.read_text())
-    return float(m.group(1)) if m else None
+    return (f"{TRAFFIC_PATH.relative_to(ROOT)} entry {workload!r}: ncu DRAM read+write / algorithmic bytes = {r} "
+            "on a captured launch, times this run's average algorithmic bytes per launch")
+
+
+def traffic_ratio(workload: str) -> float | None:
+    """ncu DRAM bytes over algorithmic bytes of the workload's dominant kernel."""
+    if not TRAFFIC_PATH.exists():
+        return None
+    entry = json.loads(TRAFFIC_PATH.read_text())["entries"].get(workload)
+    return float(entry["ratio"]) if entry else None
 
 
 def kernel_table(model, a, seqs, spec, steps: int = 10) -> str:
@@ -312,7 +357,7 @@ def eager_attention_times(model, a, spec, seed, warmup, total_steps, rank=0,
     try:
         for k in range(total_steps):
             starts = [s.num_cached_tokens for s in seqs]
-            ids = [s.tokens_slice(st, st + 1)[0] for s, st in zip(seqs, starts)]
+            ids = [s.token_ids[st:st + 1][0] for s, st in zip(seqs, starts)]
             b = DevicePagedBatch(a, [list(s.block_table) for s in seqs], starts, [1] * B, ids)
             if k == warmup:
                 torch.cuda.synchronize()
@@ -385,7 +430,7 @@ def run_ours(args, world, rank, local):
         caps = runner.graph(bucket)[1].caps  # captures the bucket's graph
     for k in range(total_steps):
         starts = [s.num_cached_tokens for s in seqs]
-        ids = [s.tokens_slice(st, st + 1)[0] for s, st in zip(seqs, starts)]
+        ids = [s.token_ids[st:st + 1][0] for s, st in zip(seqs, starts)]
         tables = [list(s.block_table) for s in seqs]
         if runner:
             plan, lay = plan_step_host(a.block_size, a.num_blocks, cfg.n_head, tables, starts, [1] * B, ids,
@@ -545,9 +590,7 @@ def run_ours(args, world, rank, local):
                 "frac": achieved / peak,
                 "traffic": (traffic_ratio(args.workload) or float("nan")) * avg_bytes
                 if traffic_ratio(args.workload) else None,
-                "traffic_source": f"ncu DRAM read+write / algorithmic bytes = {traffic_ratio(args.workload)} "
-                                  f"on a captured launch ({TRAFFIC_PROFILES[args.workload].relative_to(ROOT)}), times this "
-                                  "run's average algorithmic bytes per launch" if traffic_ratio(args.workload) else None,
+                "traffic_source": traffic_source(args.workload),
                 "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
                 "algorithmic_bytes_per_launch": avg_bytes,
                 "avg_launch_ms": avg_attn_ms,
@@ -578,6 +621,84 @@ def run_ours(args, world, rank, local):
     if args.kernel_table and rank == 0:
         log(kernel_table(model, a, seqs, spec))
     return result
+
+
+# ------------------------------------------------------------------------------ the reference itself
+def _reference_case(spec, tq, W, device, seed=2):
+    """The workload's decode batch on the reference's own allocator and
+    sequences (config 4: its 64-sequence subset, every 8th sequence)."""
+    from tokquay.kv_cache import BlockAllocator
+    from tokquay.model import GPT2Config
+    from tokquay.sequence import Sequence
+
+    cfg = GPT2Config(**W.GPT2_SMALL)
+    bs = spec["block_size"]
+    shard, n_seqs, note = (0, 1), spec["n_seqs"], ""
+    if "num_blocks" in spec:
+        nb = spec["num_blocks"]
+    else:  # config 4: the subset the parity fixtures use, on a pool sized to it
+        shard, nb = tuple(W.CFG4_SUBSET["shard"]), W.CFG4_SUBSET["num_blocks"]
+        n_seqs = len(range(0, spec["n_seqs"], shard[1]))
+        note = f" [{n_seqs}-sequence subset: every {shard[1]}th sequence, {nb}-block pool]"
+    a = BlockAllocator(cfg, nb, bs, device=device)
+    a.pool.normal_(generator=torch.Generator(device=device).manual_seed(1234))  # BASELINE: pool N(0, 1)
+    case = W.decode_case(Sequence, a, spec["n_seqs"], spec["ctx_range"], cfg.vocab_size, seed=seed, shard=shard)
+    return cfg, a, case.seqs, note
+
+
+def _reference_model(cfg, device):
+    from tokquay.model import GPT2
+
+    gen = torch.Generator(device=device).manual_seed(0)
+    with torch.device(device):
+        m = GPT2(cfg)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.normal_(0.0, 0.02, generator=gen)  # BASELINE random init: every parameter N(0, 0.02)
+    return m.eval()
+
+
+def reference_rate(spec, steps: int, warmup: int, budget_s: float, device="cpu", threads: int | None = None):
+    """The unmodified reference's own step -- ``tokquay.generate.paged_forward``
+    (tokquay/generate.py:63-87: ``BlockAllocator.batch_for``, the padded ids,
+    ``GPT2.forward`` with its dense gather and masked softmax) and the greedy
+    ``argmax(-1).tolist()`` + append / ``append_slot`` of its decode loop
+    (tokquay/generate.py:109-119) -- over the workload's whole batch, timed
+    step by step after ``warmup`` steps, until ``steps`` steps or ``budget_s``
+    seconds of timed steps.  Returns (tok/s, steps timed, batch size, sample
+    note, threads)."""
+    tq = reference_package()
+    if tq is None:
+        return None
+    from tokquay.generate import paged_forward
+
+    W = _standalone("tq_bench_workloads", "tokquay_b200/workloads.py")
+    if device == "cpu" and threads:
+        torch.set_num_threads(threads)
+    cfg, a, seqs, note = _reference_case(spec, tq, W, device)
+    model = _reference_model(cfg, device)
+    sync = torch.cuda.synchronize if device != "cpu" else (lambda: None)
+    times = []
+    with torch.no_grad():
+        for k in range(warmup + steps):
+            sync()
+            t0 = time.perf_counter()
+            toks = paged_forward(model, a, seqs).argmax(-1).tolist()
+            for s, t in zip(seqs, toks):
+                s.append_token(t)
+                if spec["grow"]:
+                    a.append_slot(s)
+                else:  # config 4 repeats its one step
+                    s.num_cached_tokens -= 1
+                    s.output_token_ids.pop()
+            dt = time.perf_counter() - t0
+            if k >= warmup:
+                times.append(dt)
+                if sum(times) > budget_s:
+                    break
+    del a
+    rate = len(seqs) * len(times) / sum(times)
+    return rate, len(times), len(seqs), note, torch.get_num_threads()
 
 
 # ------------------------------------------------------------------------------ CPU oracle
@@ -675,7 +796,7 @@ def run_mixed(args, world, rank, local) -> dict | None:
     case = mixed_case(a, seed)
     seqs, new_lens = case.seqs, case.new_lens
     starts = [s.num_cached_tokens for s in seqs]
-    ids = [t for s, st, n in zip(seqs, starts, new_lens) for t in s.tokens_slice(st, st + n)]
+    ids = [t for s, st, n in zip(seqs, starts, new_lens) for t in s.token_ids[st:st + n]]
     batch = DevicePagedBatch(a, [list(s.block_table) for s in seqs], starts, new_lens, ids)
     N, B = batch.N, batch.B
     K, Wm = args.steps, args.warmup
@@ -782,8 +903,7 @@ def run_mixed(args, world, rank, local) -> dict | None:
             "unit": "GB/s",
             "frac": achieved / peak,
             "traffic": traffic_ratio("cfg3") * abytes if traffic_ratio("cfg3") else None,
-            "traffic_source": f"ncu DRAM read+write / algorithmic bytes = {traffic_ratio('cfg3')} on a captured "
-                              "launch (profiles/paged_attention_cfg3.md), times this run's algorithmic bytes",
+            "traffic_source": traffic_source("cfg3"),
             "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
             "algorithmic_bytes_per_launch": abytes,
             "avg_launch_ms": attn_ms,
@@ -1010,7 +1130,7 @@ def run_serving(args, world, rank, local) -> dict | None:
         "rank0": {k: out[k] for k in ("requests", "output_tokens", "duration_s", "throughput_tok_s", "ttft_ms",
                                       "itl_ms", "latency_ms", "steps", "prefill_steps", "decode_step_ms")},
         "preemptions_rank0": eng.stats.num_preemptions,
-        "mixed_steps_rank0": eng.stats.mixed_steps,
+        "mixed_steps_rank0": eng.mixed_steps,
         "wall_s_rank0": wall,
     }
 
@@ -1127,133 +1247,105 @@ def run_serving_http(args) -> dict:
     }
 
 
+def cpu_baseline(spec) -> dict:
+    """The reference's own CPU step on the host cores, a bounded sample (about
+    20 s of steps over the whole batch); the numpy port when the reference is
+    not installed."""
+    threads = os.cpu_count()
+    got = reference_rate(spec, 30, 1, budget_s=20.0, threads=threads)
+    if got is None:
+        rate, sample, threads = cpu_oracle_rate(spec, 16, 2, 1)
+        return {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
+    rate, timed, n, note, threads = got
+    return {"value": rate, "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"{timed} decode steps x {n} sequences{note}: the reference's own paged_forward "
+                      f"(baseline/_ref) on the host, float32"}  # fmt: skip
+
+
+def reference_gpu_line(spec, args, local) -> dict | None:
+    """The unmodified reference on this GPU, after this build's arm (N = 1):
+    the "reference on B200" figure beside the main line."""
+    device = torch.device("cuda", local)
+    got = reference_rate(spec, args.steps, args.warmup, budget_s=60.0, device=device)
+    if got is None:
+        return None
+    rate, timed, n, note, _ = got
+    torch.cuda.empty_cache()
+    return {"value": rate, "unit": "tok/s", "ms_per_step": n / rate * 1e3, "steps": timed,
+            "sample": f"{timed} greedy decode steps x {n} sequences{note}: the reference's own GPT2 / "
+                      "BlockAllocator / paged_forward (baseline/_ref) with device='cuda', TF32 off, host clock "
+                      "per step (each step ends with the reference's own .tolist())"}  # fmt: skip
+
+
 def run_reference(args, world, rank):
+    """``--impl reference``: the reference's own CPU path on the host cores,
+    on rank 0 alone, over this build's workload (the whole batch), timed step
+    by step (``reference_rate``).  Nothing of this library is imported: the
+    reference's ``BlockAllocator``, ``Sequence``, ``GPT2`` and ``paged_forward``
+    run as installed in baseline/_ref.  Without that install, the numpy
+    restatement (oracle/) is timed instead and labelled ``kind: "port"``."""
     if rank != 0:
         return None
+    if args.workload in ("cfg5", "kvwrite"):
+        return {"impl": "reference", "unavailable": f"{args.workload}: the CPU reference arm times decode and mixed "
+                                                    "steps of the paged forward only"}  # fmt: skip
+    threads = os.cpu_count()
+    t0 = time.perf_counter()
+    common = {"impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+              "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+              "data": "synthetic"}  # fmt: skip
     if args.workload == "cfg3":
+        _load_library()
         bs = args.block_size or 16
-        t0 = time.perf_counter()
         rate, sample, threads = cpu_oracle_mixed_rate(bs, max(1, min(args.steps, 3)), replica_seed(3, 0))
-        return {"impl": "reference", "metric": "mixed prefill+decode step rows/s", "value": rate, "unit": "rows/s",
-                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        return {**common, "metric": "mixed prefill+decode step rows/s", "value": rate, "unit": "rows/s",
                 "config": {"workload": f"BASELINE config 3 mixed step, bs {bs}",
                            "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32"},
                 "cpu_baseline": {"value": rate, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample},
                 "e2e": {"value": rate, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                 "wall_s": time.perf_counter() - t0}  # fmt: skip
-    if args.workload == "cfg5":
-        return {"impl": "reference", "unavailable": "config 5 serves a live trace through an engine; the CPU "
-                                                    "reference arm times decode and mixed steps only"}  # fmt: skip
     spec = workload_spec(args)
-    # Each step is a bounded sample: a decode step over a subset of the sequences.
-    n = min(spec["n_seqs"], 16)
-    t0 = time.perf_counter()
-    rate, sample, threads = cpu_oracle_rate(spec, n, args.steps, args.warmup, budget_s=150)
-    return {
-        "impl": "reference",
-        "metric": "decode tok/s",
-        "value": rate,
-        "unit": "tok/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": n / rate * 1e3,
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "f32",
-        "data": "synthetic",
-        "config": {"workload": spec["desc"], "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32"},
-        "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
-        "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "wall_s": time.perf_counter() - t0,
-    }
+    got = reference_rate(spec, args.steps, max(1, min(args.warmup, 2)), budget_s=150.0, threads=threads)
+    if got is None:  # the reference is not installed: its numpy restatement
+        _load_library()
+        n = min(spec["n_seqs"], 16)
+        rate, sample, threads = cpu_oracle_rate(spec, n, args.steps, args.warmup, budget_s=150)
+        kind, same = "port", False
+    else:
+        rate, timed, n, note, threads = got
+        kind, same = "reference", not note
+        sample = (f"{timed} decode steps x {n} sequences of {spec['desc']}{note}: the reference's own paged_forward "
+                  f"(baseline/_ref), float32, {threads} threads")  # fmt: skip
+    return {**common, "metric": "decode tok/s", "value": rate, "unit": "tok/s", "ms_per_step": n / rate * 1e3,
+            "config": {"workload": spec["desc"], "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32",
+                       "same_config": same},
+            "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
+            "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": time.perf_counter() - t0}  # fmt: skip
 
 
 def run_reference_gpu(args, world, rank, local) -> dict | None:
-    """The reference's algorithm for this path, on the same B200: the "reference
-    on B200" column of the measurement plan.  The reference itself (Python +
-    torch) cannot travel to the GPU box, so its per-step algorithm is restated
-    here in plain torch: the padded index tensors built in Python from the
-    sequences (tokquay/kv_cache.py:174-226), the scatter of the new K/V rows
-    (:228-232), the dense gather of every sequence's blocks into a
-    [B, H, nb*bs, d] copy (:234-242), masked softmax attention over the padded
-    key axis (tokquay/model.py:94-96), torch LayerNorm / GELU(tanh) / fp32
-    linears with TF32 off (:108-124), last-row LM head (:179-181) and the greedy
-    ``argmax(-1).tolist()`` (tokquay/engine.py:189-194).  Same workload, model
-    weights and pool as this build's arm; one step at a time, no CUDA graphs,
-    as the reference runs."""
-    import math
-
-    import torch.nn.functional as F
-
+    """``--impl reference-gpu``: the unmodified reference on the same B200 (the
+    "reference on B200" column): its own ``GPT2``, ``BlockAllocator`` and
+    ``paged_forward`` with ``device="cuda"`` -- per step Python-built index
+    tensors, the advanced-index scatter of the new K/V, the dense gather of
+    every sequence's blocks and masked softmax over the padded key axis, torch
+    fp32 linears with TF32 off, one step at a time and a ``.tolist()`` per step
+    (tokquay/generate.py:63-120).  Same workload as this build's arm; nothing
+    of this library is imported.  Each step is timed on the host clock: the
+    reference's step ends with its own device-to-host read of the tokens."""
+    if reference_package() is None:
+        return {"impl": "reference-gpu", "unavailable": "the reference is not installed in baseline/_ref"}
     spec = workload_spec(args)
     device = torch.device("cuda", local)
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.set_float32_matmul_precision("highest")
-    model = make_model(device)
-    cfg = model.cfg
-    a = make_allocator(spec, cfg, device)
-    seqs = make_case(spec, a, 2, rank, world).seqs
-    C, H, L, bs = cfg.n_embd, cfg.n_head, cfg.n_layer, a.block_size
-    d, eps = C // H, cfg.layer_norm_eps
-    pool = a.pool
-
-    @torch.no_grad()
-    def step() -> list[int]:
-        B = len(seqs)
-        starts = [s.num_cached_tokens for s in seqs]
-        nb = max(-(-(st + 1) // bs) for st in starts)
-        tables = torch.tensor([s.block_table[:nb] + [0] * (nb - len(s.block_table[:nb])) for s in seqs],
-                              device=device)  # fmt: skip
-        pos = torch.tensor(starts, device=device)
-        mask = (torch.arange(nb * bs, device=device)[None, :] <= pos[:, None])[:, None, None, :]
-        w_blk = torch.tensor([s.block_table[st // bs] for s, st in zip(seqs, starts)], device=device)
-        w_off = torch.tensor([st % bs for st in starts], device=device)
-        ids = torch.tensor([s.tokens_slice(st, st + 1)[0] for s, st in zip(seqs, starts)], device=device)
-        x = (model.wte.weight[ids] + model.wpe.weight[pos.clamp(max=cfg.n_positions - 1)])[:, None]  # [B, 1, C]
-        for i, blk in enumerate(model.h):
-            h = F.layer_norm(x, (C,), blk.ln_1.weight, blk.ln_1.bias, eps)
-            qkv = F.linear(h, blk.attn.c_attn.weight, blk.attn.c_attn.bias)
-            q, k, v = (qkv[..., j * C:(j + 1) * C].view(B, 1, H, d).transpose(1, 2) for j in range(3))
-            pool[w_blk, i, 0, :, w_off] = k[:, :, 0]
-            pool[w_blk, i, 1, :, w_off] = v[:, :, 0]
-            kd = pool[tables, i, 0].permute(0, 2, 1, 3, 4).reshape(B, H, nb * bs, d)
-            vd = pool[tables, i, 1].permute(0, 2, 1, 3, 4).reshape(B, H, nb * bs, d)
-            sc = (q @ kd.transpose(-1, -2)) / math.sqrt(d)
-            att = torch.softmax(sc.masked_fill(~mask, float("-inf")), dim=-1) @ vd
-            x = x + F.linear(att.transpose(1, 2).reshape(B, 1, C), blk.attn.c_proj.weight, blk.attn.c_proj.bias)
-            h = F.layer_norm(x, (C,), blk.ln_2.weight, blk.ln_2.bias, eps)
-            h = F.gelu(F.linear(h, blk.mlp.c_fc.weight, blk.mlp.c_fc.bias), approximate="tanh")
-            x = x + F.linear(h, blk.mlp.c_proj.weight, blk.mlp.c_proj.bias)
-        xf = F.layer_norm(x[:, 0], (C,), model.ln_f.weight, model.ln_f.bias, eps)
-        toks = (xf @ model.wte.weight.t()).argmax(-1).tolist()
-        for s, t in zip(seqs, toks):
-            s.num_cached_tokens += 1
-            s.append_token(t)
-            if spec["grow"]:
-                a.append_slot(s)
-            else:
-                s.num_cached_tokens -= 1
-                s.output_token_ids.pop()
-        return toks
-
-    K, Wm = args.steps, args.warmup
-    for _ in range(Wm):
-        step()
-    torch.cuda.synchronize(device)
     barrier(world)
-    stream = torch.cuda.current_stream(device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
-        e0.record(stream)
-        for _ in range(K):
-            step()
-        e1.record(stream)
-        torch.cuda.synchronize(device)
-    ms_max = max_over_ranks(e0.elapsed_time(e1), world)
-    tokens_all = sum_over_ranks(len(seqs) * K, world)
+        rate, timed, n, note, _ = reference_rate(spec, args.steps, args.warmup, budget_s=120.0, device=device)
+    ms = n / rate * 1e3
+    ms_max = max_over_ranks(ms, world)
+    tokens_all = sum_over_ranks(n, world)
     if rank != 0:
         return None
     return {
@@ -1262,17 +1354,18 @@ def run_reference_gpu(args, world, rank, local) -> dict | None:
         "value": tokens_all / (ms_max * 1e-3),
         "unit": "tok/s",
         "n_gpus": world,
-        "steps": K,
-        "warmup": Wm,
-        "ms_per_step": ms_max / K,
+        "steps": timed,
+        "warmup": args.warmup,
+        "ms_per_step": ms_max,
         "higher_is_better": True,
-        "scaling": "strong" if spec.get("strong") else "weak",
+        "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": spec["desc"], "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32, TF32 off",
-                   "algorithm": "the reference's per-step algorithm restated in plain torch on the GPU: dense gather "
-                                "of every sequence's blocks + masked softmax over the padded key axis"},  # fmt: skip
+        "config": {"workload": spec["desc"] + note,
+                   "model": "GPT-2 124M architecture, random-init N(0,0.02), fp32, TF32 off",
+                   "algorithm": "the reference's own code (baseline/_ref) on the GPU: dense gather of every "
+                                "sequence's blocks + masked softmax over the padded key axis"},  # fmt: skip
         "clocks": clocks.summary(),
     }
 
@@ -1342,6 +1435,7 @@ def main():
             _emit(res)
         _replicas.teardown(info)
         return
+    _load_library()
     if args.workload == "cfg5":
         res = run_serving(args, world, rank, local)
         if rank == 0 and res is not None:
@@ -1366,9 +1460,9 @@ def main():
         return
     res = run_ours(args, world, rank, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, sample, threads = cpu_oracle_rate(workload_spec(args), 16, 2, 1)
-        res["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
-                               "sample": sample}  # fmt: skip
+        res["cpu_baseline"] = cpu_baseline(workload_spec(args))
+        torch.cuda.empty_cache()
+        res["reference_gpu"] = reference_gpu_line(workload_spec(args), args, local)
     if rank == 0 and res is not None:
         _emit(res)
     _replicas.teardown(info)

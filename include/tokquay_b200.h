@@ -197,7 +197,8 @@ TQ_API int tq_paged_attention(float* out, int64_t out_row_stride, const float* q
                        int32_t max_partials, float scale, void* stream);
 
 /* Split-K partials tq_paged_attention_noalloc can hold.  Its scratch,
- * TQ_NOALLOC_MAX_PARTIALS * (1 + 2 + 64) * 4 bytes (about 8.6 MB), is a fixed
+ * TQ_NOALLOC_MAX_PARTIALS * (1 + 2 + 64) * 4 bytes (8,781,824 bytes: 8.78 MB,
+ * 8.4 MiB), is a fixed
  * array inside the library on every GPU that loads it, kept until exit. */
 #define TQ_NOALLOC_MAX_PARTIALS 32768
 
@@ -211,7 +212,10 @@ TQ_API int tq_paged_attention(float* out, int64_t out_row_stride, const float* q
  * call allocates nothing; a plan needing more than TQ_NOALLOC_MAX_PARTIALS
  * partials is rejected with TQ_ERR_CAPACITY before anything is launched.
  * The first call on a device looks the array's address up
- * (cudaGetSymbolAddress): make that first call before any stream capture.
+ * (cudaGetSymbolAddress) and keeps it for the life of the process: make that
+ * first call before any stream capture, and do not use this entry point on a
+ * device after cudaDeviceReset (the kept address belongs to the context the
+ * reset destroyed).
  * Every call on a device shares the one array and clears the split counters
  * it uses before its kernel runs, so calls that overlap on the GPU (other
  * streams, other threads) race: issue them one after another. */

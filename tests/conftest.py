@@ -16,6 +16,11 @@ for p in (str(ROOT), str(TESTS)):
     if p not in sys.path:
         sys.path.insert(0, p)
 
+# The reference package ``tokquay`` (installed next to the checkout by
+# baseline/install_ref.sh): this library plugs into it, and the tests drive
+# its own scheduler and engine.
+import tokquay_b200._host  # noqa: E402,F401
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200)")

@@ -16,8 +16,8 @@ from dataclasses import dataclass
 from types import SimpleNamespace
 
 from tokquay_b200.engine import TokenEvent
-from tokquay_b200.scheduler import RequestRejected, Scheduler, SchedulerConfig
-from tokquay_b200.sequence import Sequence
+from tokquay.scheduler import RequestRejected, Scheduler, SchedulerConfig
+from tokquay.sequence import Sequence
 
 
 def expected_tokens(prompt: list[int], n: int, vocab: int = 1000) -> list[int]:

@@ -1,6 +1,6 @@
 """Generate the golden fixtures from the unmodified reference implementation.
 
-    PYTHONPATH=<tokquay checkout> python tests/golden/make_golden.py [--ref PATH]
+    python tests/golden/make_golden.py --ref <reference checkout> [--only CASE,...]
 
 Runs the reference Tokquay code (pure Python + torch on the CPU) on seeded
 inputs built by ``tokquay_b200.workloads`` and records what it produced:
@@ -18,7 +18,10 @@ Cases (reference test each one re-hosts, paths inside the Tokquay project):
                 (tests/test_phase3_paged.py:143-164)
   cfg1          BASELINE config 1: GPT-2 124M, 8 decodes, bs 16, 1,024 blocks
   cfg3_bs16/32  BASELINE config 3: 4 prefills + 60 decodes in one step
-  cfg2          BASELINE config 2 (first 3 of its 100 greedy steps), 2,048 blocks
+  cfg2          BASELINE config 2, all 100 greedy steps, 2,048 blocks (every step's
+                argmax / top-2 / sparse logit columns; the first 3 steps densely)
+  cfg4_sub      BASELINE config 4's shape (bs 32, ctx U[256,1024]) on a 64-sequence
+                subset of its 512 (every 8th), 4,096-block pool, 3 greedy steps
   alloc_trace   random allocate / grow / free on a tiny allocator
   sched_trace   three scheduler scenarios (burst with preemption, staggered
                 arrivals with aborts, a tight step budget) driven without a model
@@ -48,6 +51,8 @@ from tokquay_b200 import workloads as W  # noqa: E402
 
 LOGIT_STRIDE_FULL = 8     # columns kept from GPT-2 124M logits (config 1)
 LOGIT_STRIDE_LARGE = 32   # columns kept for the 64-sequence configs
+LOGIT_STRIDE_SPARSE = 1024  # columns kept for every step of config 2's 100-step run
+DENSE_STEPS = 3           # config-2 steps also kept at LOGIT_STRIDE_LARGE
 
 
 def summarize_logits(x: torch.Tensor, stride: int) -> dict[str, np.ndarray]:
@@ -151,7 +156,7 @@ def engine_arrivals(rng) -> list[list[tuple[list[int], int]]]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference", help="path of the reference checkout")
+    ap.add_argument("--ref", required=True, help="path of the reference checkout (or its install)")
     ap.add_argument("--only", default=None, help="comma-separated case names")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
@@ -352,23 +357,71 @@ def main() -> None:
         a = BlockAllocator(m.cfg, c["num_blocks"], c["block_size"], device="cpu")
         case = W.decode_case(Sequence, a, c["n_seqs"], c["ctx_range"], m.cfg.vocab_size, seed=2)
         W.fill_pool_blocks(a.pool, W.used_blocks(case), seed=2)
-        steps = []
-        n_steps = 3
+        steps, sparse, argmax, top2, absmax = [], [], [], [], []
+        n_steps = c["steps"]
+        # The greedy loop of tokquay/generate.py:109-119 for a batch that runs
+        # n_steps more tokens: sample, append, grow the table for the next step.
         for k in range(n_steps):
             tables = [list(s.block_table) for s in case.seqs]
             logits = paged_forward(m, a, case.seqs)
-            summ = summarize_logits(logits, LOGIT_STRIDE_LARGE)
-            for key, v in summ.items():
-                arrays[f"cfg2/step{k}_{key}"] = v
+            if k < DENSE_STEPS:
+                for key, v in summarize_logits(logits, LOGIT_STRIDE_LARGE).items():
+                    arrays[f"cfg2/step{k}_{key}"] = v
+                steps.append({"tables": tables})
+            summ = summarize_logits(logits, LOGIT_STRIDE_SPARSE)
+            sparse.append(summ["cols"])
+            argmax.append(summ["argmax"])
+            top2.append(summ["top2"])
+            absmax.append(summ["absmax"])
             nxt = summ["argmax"].tolist()
-            steps.append({"tables": tables, "next": nxt})
+            if k < DENSE_STEPS:
+                steps[-1]["next"] = nxt
             for s, t in zip(case.seqs, nxt):
                 s.append_token(t)
-                a.append_slot(s)
+                if k + 1 < n_steps:
+                    a.append_slot(s)
+            if k % 10 == 9:
+                print(f"  cfg2 step {k + 1}/{n_steps} {time.time() - t0:.0f}s", flush=True)
+        arrays["cfg2/all_cols"] = np.stack(sparse)        # [steps, B, V / stride]
+        arrays["cfg2/all_argmax"] = np.stack(argmax)      # [steps, B]
+        arrays["cfg2/all_top2"] = np.stack(top2)          # [steps, B, 2]
+        arrays["cfg2/all_absmax"] = np.stack(absmax)      # [steps, B]
         meta["cases"]["cfg2"] = {"seed": 2, "weights_seed": 0, "init": "normal", **{k: c[k] for k in c},
                                  "ctx": case.meta["ctx"], "steps": steps, "n_steps": n_steps,
-                                 "free_after": list(a._free), "logit_stride": LOGIT_STRIDE_LARGE}  # fmt: skip
+                                 "dense_steps": DENSE_STEPS, "final_tables": [list(s.block_table) for s in case.seqs],
+                                 "free_after": list(a._free), "logit_stride": LOGIT_STRIDE_LARGE,
+                                 "sparse_stride": LOGIT_STRIDE_SPARSE}  # fmt: skip
         print(f"cfg2 {time.time() - t0:.1f}s")
+
+    if want("cfg4_sub"):
+        t0 = time.time()
+        m = gpt2_model()
+        c = W.CONFIGS[4]
+        sub = W.CFG4_SUBSET
+        a = BlockAllocator(m.cfg, sub["num_blocks"], c["block_size"], device="cpu")
+        case = W.decode_case(Sequence, a, c["n_seqs"], c["ctx_range"], m.cfg.vocab_size, seed=4,
+                             shard=tuple(sub["shard"]))  # fmt: skip
+        W.fill_pool_blocks(a.pool, W.used_blocks(case), seed=4)
+        first_tables = [list(s.block_table) for s in case.seqs]
+        n_steps = sub["steps"]
+        for k in range(n_steps):
+            logits = paged_forward(m, a, case.seqs)
+            summ = summarize_logits(logits, LOGIT_STRIDE_LARGE)
+            for key, v in summ.items():
+                arrays[f"cfg4_sub/step{k}_{key}"] = v
+            for s, t in zip(case.seqs, summ["argmax"].tolist()):
+                s.append_token(t)
+                if k + 1 < n_steps:
+                    a.append_slot(s)
+            print(f"  cfg4_sub step {k + 1}/{n_steps} {time.time() - t0:.0f}s", flush=True)
+        meta["cases"]["cfg4_sub"] = {"seed": 4, "weights_seed": 0, "init": "normal", "n_seqs": c["n_seqs"],
+                                     "ctx_range": c["ctx_range"], "block_size": c["block_size"], **sub,
+                                     "ctx": case.meta["ctx"], "tables": first_tables, "n_steps": n_steps,
+                                     "tokens": [s.output_token_ids for s in case.seqs],
+                                     "final_tables": [list(s.block_table) for s in case.seqs],
+                                     "free_after": list(a._free), "logit_stride": LOGIT_STRIDE_LARGE}  # fmt: skip
+        del a
+        print(f"cfg4_sub {time.time() - t0:.1f}s")
 
     # ---------------------------------------------------------------- allocator trace
     if want("alloc_trace"):

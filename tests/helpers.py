@@ -17,7 +17,7 @@ import numpy as np
 
 from tokquay_b200 import workloads as W
 from tokquay_b200.model import GPT2Config
-from tokquay_b200.sequence import Sequence
+from tokquay.sequence import Sequence
 
 GOLDEN_DIR = Path(__file__).resolve().parent / "golden"
 

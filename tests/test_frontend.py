@@ -17,7 +17,7 @@ import pytest
 from fake_engine import EchoFactory, expected_tokens
 from tokquay_b200.frontend import EngineError, IncrementalDetokenizer, ReplicaRouter, create_app
 from tokquay_b200.scheduler import RequestRejected
-from tokquay_b200.sequence import SamplingParams
+from tokquay.sequence import SamplingParams
 
 
 def run(coro):
@@ -243,19 +243,28 @@ def test_front_ends_share_one_port():
     assert procs and not any(p.is_alive() for p in procs)
 
 
-def _orphaning_server(out):
+def _orphaning_server(out, busy):
     """Runs in a spawned process: starts one replica, reports its pid, then
-    exits at once without stopping it (as a killed server process would)."""
+    exits at once without stopping it (as a killed server process would).
+    With ``busy`` the replica is first given long requests, so it is still
+    stepping -- and sending a message per step that nobody will read, more
+    than a pipe holds -- when the server goes."""
     import multiprocessing as mp
     import os
 
+    from tokquay.sequence import SamplingParams
     from tokquay_b200.frontend import _replica_main
 
     ctx = mp.get_context("spawn")
     inbox, outbox = ctx.Queue(), ctx.Queue()
-    p = ctx.Process(target=_replica_main, args=(0, "r0", EchoFactory(), inbox, outbox), daemon=True)
+    factory = EchoFactory(max_model_len=1024, step_s=0.001 if busy else 0.0)
+    p = ctx.Process(target=_replica_main, args=(0, "r0", factory, inbox, outbox), daemon=True)
     p.start()
     assert outbox.get(timeout=120)[0] == "ready"
+    if busy:
+        for rid in range(8):
+            inbox.put(("add", rid, [1, 2, 3, rid], SamplingParams(max_tokens=1000, ignore_eos=True)))
+        assert outbox.get(timeout=60)[0] == "tokens"  # stepping now
     out.put(p.pid)
     out.close()
     out.join_thread()  # the pid must leave before the abrupt exit below
@@ -270,13 +279,14 @@ def _exited(pid: int) -> bool:
         return True
 
 
-def test_an_orphaned_replica_ends_itself():
+@pytest.mark.parametrize("busy", [False, True], ids=["idle", "busy"])
+def test_an_orphaned_replica_ends_itself(busy):
     import multiprocessing as mp
     import time
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    server = ctx.Process(target=_orphaning_server, args=(q,))
+    server = ctx.Process(target=_orphaning_server, args=(q, busy))
     server.start()
     pid = q.get(timeout=180)
     server.join(60)

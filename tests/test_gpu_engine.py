@@ -1,9 +1,20 @@
-"""The engine (tokquay_b200/engine.py) over the B200 path reproduces the
-reference engine run on the CPU (tests/golden/make_golden.py, case
-``mini_engine``): requests arriving in waves on a pool small enough to force
-preemption by recompute, greedy sampling.  Every step's tokens, finish
-reasons, prefill/decode choice, running and waiting queues, block tables and
-free list must be equal -- with and without CUDA graphs for the decode steps.
+"""Tokquay's own engine over the B200 path reproduces the reference engine
+run on the CPU (tests/golden/make_golden.py, case ``mini_engine``): requests
+arriving in waves on a pool small enough to force preemption by recompute,
+greedy sampling.  Every step's tokens, finish reasons, prefill/decode choice,
+running and waiting queues, block tables and free list must be equal, for all
+82 steps of the trace.
+
+The engine is driven three ways, none of which edits the reference:
+
+* ``tokquay.engine.Engine`` -- the reference's class itself, imported from the
+  reference package -- given this package's ``GPT2`` and ``BlockAllocator``,
+  with and without CUDA graphs for the decode steps;
+* ``tokquay_b200.engine.Engine`` (the same class plus the greedy-token hook);
+* the reference's own *model* (``tokquay.model.GPT2``) over this package's
+  step view: unpatched (its ``write`` / ``gather`` / ``mask`` / ``positions``
+  members) and with the attention hook a maintainer adds to
+  ``Attention.forward`` (``cache.attend``; applied here by monkeypatch).
 """
 
 import random
@@ -14,12 +25,16 @@ import pytest
 import torch
 
 from helpers import cfg_of, load_golden
+from tokquay import engine as ref_engine
+from tokquay import model as ref_model
+from tokquay.scheduler import SchedulerConfig as RefSchedulerConfig
+from tokquay.sequence import SamplingParams
+from tokquay_b200 import _lib
 from tokquay_b200 import workloads as W
 from tokquay_b200.engine import Engine
-from tokquay_b200.kv_cache import BlockAllocator
+from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch
 from tokquay_b200.model import GPT2
 from tokquay_b200.scheduler import SchedulerConfig
-from tokquay_b200.sequence import SamplingParams
 
 sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
 import make_golden  # noqa: E402  (the arrival waves the fixture was recorded with)
@@ -31,21 +46,27 @@ GOLDEN = load_golden()
 NEAR_TIE = 2e-5
 
 
-@pytest.mark.parametrize("graphs", [False, True])
-def test_engine_matches_the_reference_engine(graphs):
-    case = GOLDEN.cases["mini_engine"]
+def _mini_allocator(case):
     cfg = cfg_of(case)
-    m = GPT2(cfg)
-    W.load_weights(m, W.random_weights(cfg, case["weights_seed"], case["init"]))
-    m = m.to("cuda").eval()
     a = BlockAllocator(cfg, case["num_blocks"], case["block_size"], device="cuda")
     W.fill_pool_blocks(a.pool, range(case["num_blocks"]), case["pool_seed"], case["pool_scale"])
     W.shuffle_free_list(a, case["free_seed"])
-    if graphs:
-        m.use_cuda_graphs(a)
-    eng = Engine(m, a, SchedulerConfig(**case["sched"]))
+    return a
+
+
+def _mini_model(case, cls=GPT2):
+    cfg = cfg_of(case)
+    m = cls(cfg)
+    W.load_weights(m, W.random_weights(cfg, case["weights_seed"], case["init"]))
+    return m.to("cuda").eval()
+
+
+def _replay_engine_trace(eng, a, case) -> int:
+    """Drive ``eng`` with the trace's arrival waves and compare every step with
+    the reference's; returns how many steps were compared."""
     arrivals = make_golden.engine_arrivals(random.Random(case["trace_seed"]))
     margins = [min(x) for x in case["margins"]]
+    compared = 0
     for k, want in enumerate(case["steps"]):
         for prompt, max_tokens in arrivals.pop(0) if arrivals else []:
             eng.add_request(prompt, SamplingParams(max_tokens=max_tokens, ignore_eos=True))
@@ -60,10 +81,66 @@ def test_engine_matches_the_reference_engine(graphs):
             "preemptions": eng.scheduler.num_preemptions,
         }
         assert got == want, f"step {k}"
+        compared += 1
         if k < len(margins) and margins[k] < NEAR_TIE:
             break  # later tokens may legitimately differ
     else:
         assert not eng.has_unfinished() and eng.stats.num_preemptions > 0
+    # The trace has no near tie, so every one of its steps must have been compared.
+    first_tie = next((k for k, x in enumerate(margins) if x < NEAR_TIE), len(case["steps"]) - 1)
+    assert compared == min(first_tie + 1, len(case["steps"])) == 82, compared
+    return compared
+
+
+@pytest.mark.parametrize("engine_cls", [ref_engine.Engine, Engine], ids=["reference_class", "b200_subclass"])
+@pytest.mark.parametrize("graphs", [False, True])
+def test_engine_matches_the_reference_engine(engine_cls, graphs):
+    case = GOLDEN.cases["mini_engine"]
+    m, a = _mini_model(case), _mini_allocator(case)
+    if graphs:
+        m.use_cuda_graphs(a)
+    eng = engine_cls(m, a, RefSchedulerConfig(**case["sched"]))
+    _replay_engine_trace(eng, a, case)
+    if graphs:
+        assert m.graph_runner._graphs  # decode steps replayed captured graphs
+    assert _lib.device_status() == 0
+
+
+def _attend_forward(orig):
+    """The two-line change of ``Attention.forward``'s paged branch
+    (tokquay/model.py:73-78) that lets the step view attend in place."""
+
+    def forward(self, x, cache=None, layer=0):
+        if not isinstance(cache, DevicePagedBatch):
+            return orig(self, x, cache, layer)
+        B, T, C = x.shape
+        q, k, v = self.c_attn(x).split(C, dim=-1)
+        q, k, v = (t.view(B, T, self.n_head, self.d_head).transpose(1, 2) for t in (q, k, v))
+        out = cache.attend(layer, q, k, v)  # [B, H, T, d]: tq_kv_write + tq_paged_attention
+        return self.c_proj(out.transpose(1, 2).reshape(B, T, C))
+
+    return forward
+
+
+@pytest.mark.parametrize("hook", [False, True], ids=["unpatched", "attend_hook"])
+def test_reference_model_and_engine_over_the_step_view(monkeypatch, hook):
+    """The reference's model and engine, this package's allocator: without the
+    hook the model runs its own dense attention over ``DevicePagedBatch``'s
+    reference members (K/V written by ``tq_kv_write``, dense ``gather``,
+    ``mask``, ``positions``, ``last_idx``); with it, attention is the CUDA
+    kernel.  Either way the trace equals the reference's."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    case = GOLDEN.cases["mini_engine"]
+    if hook:
+        monkeypatch.setattr(ref_model.Attention, "forward", _attend_forward(ref_model.Attention.forward))
+    m, a = _mini_model(case, ref_model.GPT2), _mini_allocator(case)
+    eng = ref_engine.Engine(m, a, RefSchedulerConfig(**case["sched"]))
+    calls = []
+    real = DevicePagedBatch.attend
+    monkeypatch.setattr(DevicePagedBatch, "attend", lambda self, *args: calls.append(1) or real(self, *args))
+    _replay_engine_trace(eng, a, case)
+    assert bool(calls) == hook
+    assert _lib.device_status() == 0
 
 
 def test_serving_trace_through_the_engine():
@@ -126,7 +203,7 @@ def test_mixed_prefill_policy_gives_the_reference_policy_tokens(graphs):
 
     want, _ = run(0, False)
     got, eng = run(24, graphs)
-    assert eng.stats.mixed_steps > 0
+    assert eng.mixed_steps > 0
     for sid, toks in want.items():
         assert len(got[sid]) == len(toks)
         if got[sid] != toks:  # allowed only after a near tie in the reference run

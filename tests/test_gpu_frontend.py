@@ -7,7 +7,7 @@ import random
 import pytest
 
 from tokquay_b200.frontend import RandomGPT2Engine, ReplicaRouter, create_app
-from tokquay_b200.sequence import SamplingParams
+from tokquay.sequence import SamplingParams
 
 pytestmark = pytest.mark.gpu
 

@@ -9,7 +9,7 @@ import pytest
 
 from tokquay_b200 import kv_cache
 from tokquay_b200.kv_cache import PackedStep
-from tokquay_b200.sequence import Sequence
+from tokquay.sequence import Sequence
 
 hostpack = pytest.importorskip("tokquay_b200._hostpack")
 

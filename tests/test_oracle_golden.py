@@ -17,7 +17,7 @@ from helpers import (
 from tokquay_b200 import workloads as W
 from tokquay_b200.kv_cache import BlockAllocator
 from tokquay_b200.model import GPT2Config
-from tokquay_b200.sequence import Sequence
+from tokquay.sequence import Sequence
 
 
 def _w(case, dtype):
@@ -151,6 +151,7 @@ def test_config3_mixed_step(golden, gpt2_weights, bs):
 
 @pytest.mark.slow
 def test_config2_greedy_steps(golden, gpt2_weights):
+    """The oracle on config 2's first steps (the densely recorded ones)."""
     case = golden.cases["cfg2"]
     cfg = GPT2Config(**W.GPT2_SMALL)
     alloc = BlockAllocator(cfg, case["num_blocks"], case["block_size"], device="cpu")
@@ -163,10 +164,27 @@ def test_config2_greedy_steps(golden, gpt2_weights):
         np.testing.assert_allclose(logits[:, ::case["logit_stride"]], _cols(golden, f"cfg2/step{k}_cols"),
                                    atol=ORACLE_F32_ATOL, rtol=0)  # fmt: skip
         nxt = logits.argmax(-1).tolist()
-        assert nxt == step["next"]
+        assert nxt == step["next"] == golden.arrays["cfg2/all_argmax"][k].tolist()
         for s, t in zip(seqs, nxt):
             s.append_token(t)
             alloc.append_slot(s)
+
+
+def test_config2_allocator_state_over_the_hundred_steps(golden):
+    """Config 2's whole greedy run on the allocator alone (the reference's
+    tokens fed back): block tables and free list equal the reference's after
+    all 100 steps, bit for bit."""
+    case = golden.cases["cfg2"]
+    alloc = BlockAllocator(GPT2Config(**W.GPT2_SMALL), case["num_blocks"], case["block_size"], device="meta")
+    seqs, _ = build_config_case("cfg2", golden, alloc=alloc)
+    tokens = golden.arrays["cfg2/all_argmax"]
+    for k in range(case["n_steps"]):
+        for s, t in zip(seqs, tokens[k].tolist()):
+            s.num_cached_tokens += 1
+            s.append_token(t)
+            if k + 1 < case["n_steps"]:
+                alloc.append_slot(s)
+    assert [s.block_table for s in seqs] == case["final_tables"]
     assert alloc._free == case["free_after"]
 
 

@@ -44,7 +44,7 @@ def _worker(rank, world, port, out_dir):
         case = W.decode_case(Sequence, a, 4, (8, 64), cfg.vocab_size, seed=replicas.replica_seed(2, info.rank))
         seqs = case.seqs
         starts = [s.num_cached_tokens for s in seqs]
-        ids = [s.tokens_slice(st, st + 1)[0] for s, st in zip(seqs, starts)]
+        ids = [s.token_ids[st:st + 1][0] for s, st in zip(seqs, starts)]
         plan, layout = KV.plan_step_host(a.block_size, a.num_blocks, cfg.n_head, [list(s.block_table) for s in seqs],
                                          starts, [1] * len(seqs), ids, cfg.vocab_size, 64, KV.MIN_SPLIT_CHUNKS)  # fmt: skip
         replicas.barrier(info.world)

@@ -1,10 +1,13 @@
-"""The scheduler (tokquay_b200/scheduler.py) makes the reference's decisions.
+"""Scheduling over this package's allocator.
 
-Replays the scheduler traces recorded from the unmodified reference scheduler
-(tests/golden/make_golden.py, case ``sched_trace``): the same requests arrive
-at the same steps, each step advances the sequences as paged_forward and the
-engine do (a model-free token function stands in for sampling), and every
-step's batch, preemptions, queues, block tables and free list must be equal.
+The reference's own scheduler (``tokquay.scheduler.Scheduler``, the default)
+over ``tokquay_b200.BlockAllocator`` replays the traces recorded from the
+reference scheduler over the reference's allocator (tests/golden/make_golden.py,
+case ``sched_trace``): the same requests arrive at the same steps, each step
+advances the sequences as paged_forward and the engine do (a model-free token
+function stands in for sampling), and every step's batch, preemptions, queues,
+block tables and free list must be equal.  The opt-in chunked-prefill policy
+(``tokquay_b200.scheduler.Scheduler``) is checked for its invariants.
 CPU only (the allocator's pool lives on the meta device).
 """
 
@@ -14,9 +17,11 @@ from pathlib import Path
 import pytest
 
 from helpers import load_golden
+from tokquay.scheduler import RequestRejected
+from tokquay.scheduler import Scheduler as RefScheduler
+from tokquay.sequence import SamplingParams, Sequence
 from tokquay_b200.kv_cache import BlockAllocator
-from tokquay_b200.scheduler import RequestRejected, Scheduler, SchedulerConfig
-from tokquay_b200.sequence import SamplingParams, Sequence
+from tokquay_b200.scheduler import Scheduler, SchedulerConfig
 
 sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
 import make_golden  # noqa: E402  (the trace driver the fixtures were recorded with)
@@ -30,7 +35,7 @@ def test_scheduler_matches_the_reference_trace(sc):
     spec = {k: sc[k] for k in ("name", "num_blocks", "block_size", "free_seed", "config", "requests")}
     if "aborts" in sc:
         spec["aborts"] = sc["aborts"]
-    got = make_golden.sched_scenario(BlockAllocator, Scheduler, SchedulerConfig, Sequence, SamplingParams, spec)
+    got = make_golden.sched_scenario(BlockAllocator, RefScheduler, SchedulerConfig, Sequence, SamplingParams, spec)
     assert got["rejected"] == sc["rejected"]
     assert len(got["trace"]) == len(sc["trace"])
     for mine, ref in zip(got["trace"], sc["trace"]):
@@ -38,16 +43,25 @@ def test_scheduler_matches_the_reference_trace(sc):
     assert got["outputs"] == sc["outputs"]
 
 
-def test_rejections_and_config_checks():
+@pytest.mark.parametrize("mixed", [0, 16])
+def test_rejections_and_config_checks(mixed):
+    """The reference's up-front rejections hold for both policies."""
     alloc = BlockAllocator(make_golden._MiniCfg(), 8, 4, device="meta")
-    sched = Scheduler(alloc, SchedulerConfig(max_num_seqs=2, max_num_batched_tokens=40, max_model_len=30))
+    cls = Scheduler if mixed else RefScheduler
+    kw = dict(max_num_seqs=2, mixed_prefill_tokens=mixed)
+    sched = cls(alloc, SchedulerConfig(max_num_batched_tokens=40, max_model_len=30, **kw))
     with pytest.raises(RequestRejected, match="model supports 30"):
         sched.add_request(Sequence(0, [1] * 20, sampling=SamplingParams(max_tokens=12)))
     with pytest.raises(RequestRejected, match="KV blocks"):
-        Scheduler(alloc, SchedulerConfig(max_num_seqs=2, max_num_batched_tokens=200, max_model_len=100)).add_request(
+        cls(alloc, SchedulerConfig(max_num_batched_tokens=200, max_model_len=100, **kw)).add_request(
             Sequence(1, [1] * 40, sampling=SamplingParams(max_tokens=5)))
     with pytest.raises(ValueError):
         SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=2)
+    with pytest.raises(ValueError):
+        SchedulerConfig(mixed_prefill_tokens=-1)
+    if not mixed:
+        with pytest.raises(ValueError, match="mixed_prefill_tokens must be > 0"):
+            Scheduler(alloc, SchedulerConfig())
     assert sched.schedule() is None and not sched.has_unfinished()
 
 
@@ -56,7 +70,7 @@ def _run_model_free(sched, alloc, requests, arrivals, token_of):
     advances every batch sequence by its fed tokens (paged_forward), then each
     sequence at the end of its prompt or decoding gets a token, and finishes
     at max_tokens.  Returns the steps' (seq ids, fed tokens) and the outputs."""
-    from tokquay_b200.sequence import SequenceStatus
+    from tokquay.sequence import SequenceStatus
 
     seqs, steps = {}, []
     pending = sorted(zip(arrivals, range(len(requests))))
@@ -71,7 +85,7 @@ def _run_model_free(sched, alloc, requests, arrivals, token_of):
         step += 1
         if batch is None:
             continue
-        lens = batch.new_lens or [s.num_uncached_tokens for s in batch.seqs]
+        lens = getattr(batch, "new_lens", None) or [s.num_uncached_tokens for s in batch.seqs]
         steps.append(([s.seq_id for s in batch.seqs], list(lens), batch.is_prefill))
         for s, n in zip(batch.seqs, lens):
             assert 1 <= n <= s.num_uncached_tokens
@@ -105,7 +119,7 @@ def test_mixed_prefill_policy(budget, tight):
         alloc = BlockAllocator(make_golden._MiniCfg(), 20 if tight else 400, 4, device="meta")
         cfg = SchedulerConfig(max_num_seqs=8, max_num_batched_tokens=64, max_model_len=64,
                               mixed_prefill_tokens=budget if mixed else 0)  # fmt: skip
-        sched = Scheduler(alloc, cfg)
+        sched = (Scheduler if mixed else RefScheduler)(alloc, cfg)
         steps, out = _run_model_free(sched, alloc, requests, arrivals, token_of)
         assert alloc.num_free_blocks == alloc.num_blocks and sorted(alloc._free) == list(range(alloc.num_blocks))
         return steps, out, sched

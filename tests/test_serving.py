@@ -12,7 +12,7 @@ import pytest
 
 from helpers import load_golden
 from tokquay_b200.engine import StepInfo, KVSnapshot, TokenEvent
-from tokquay_b200.sequence import Sequence
+from tokquay.sequence import Sequence
 from tokquay_b200.serving import make_workload, round_robin, run_trace, summarize
 
 GOLDEN = load_golden()

@@ -341,7 +341,7 @@ int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64
 // a fixed memory budget, or an embedding that has no device allocator of its
 // own at the point it runs attention).  tq_paged_attention_noalloc serves
 // them: the scratch is the file-scope array below, which every GPU that loads
-// this library holds until the process exits (about 8.6 MB), so the entry
+// this library holds until the process exits (8.78 MB), so the entry
 // point itself never allocates.  Host code must not pass the array's name to
 // a kernel -- on the host that name is only a stand-in for the symbol -- so
 // its device address is looked up once per device with cudaGetSymbolAddress.
@@ -361,7 +361,8 @@ unsigned char* g_noalloc_base[kMaxDevices] = {nullptr};
 std::mutex g_noalloc_mu;
 
 // Device address of g_noalloc_scratch on the current device, looked up on the
-// first call per device.
+// first call per device and kept: valid for the device's primary context, so
+// not across a cudaDeviceReset (the header says so).
 int noalloc_scratch(unsigned char** base) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

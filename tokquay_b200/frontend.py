@@ -55,8 +55,12 @@ from fastapi import FastAPI, HTTPException, Request
 from fastapi.responses import JSONResponse, Response, StreamingResponse
 from pydantic import BaseModel, Field, model_validator
 
-from tokquay_b200.scheduler import RequestRejected, Scheduler, SchedulerConfig
-from tokquay_b200.sequence import SamplingParams, Sequence
+from tokquay_b200._host import ref_scheduler, ref_sequence
+from tokquay_b200.scheduler import SchedulerConfig
+
+# The reference's request types and rejection rules (tokquay/scheduler.py:82-104).
+RequestRejected, Scheduler = ref_scheduler.RequestRejected, ref_scheduler.Scheduler
+SamplingParams, Sequence = ref_sequence.SamplingParams, ref_sequence.Sequence
 
 __all__ = [
     "EngineError",
@@ -159,9 +163,21 @@ def _replica_main(index: int, device, factory: Callable, inbox, outbox) -> None:
     """A replica's whole life: build the engine on ``device``, then the
     engine loop of async_engine.py:133-156 over ``inbox`` commands
     (``("add", req_id, ids, params)``, ``("abort", req_id)``, ``("stop",)``).
-    An idle replica whose server process has gone (killed, so no "stop" will
-    come) ends itself within a second."""
+    A replica whose server process has gone (killed, so no "stop" will come
+    and nobody drains its outbox) ends itself: within a second when idle,
+    before its next step when busy."""
     parent = os.getppid()
+
+    def orphaned() -> bool:
+        if os.getppid() == parent:
+            return False
+        # Nobody reads the outbox any more: its feeder thread may be blocked on a
+        # full pipe, and the exit must not wait for it (multiprocessing joins the
+        # feeder threads of its queues at exit).
+        inbox.cancel_join_thread()
+        outbox.cancel_join_thread()
+        return True
+
     try:
         if isinstance(device, int):
             import torch
@@ -177,7 +193,7 @@ def _replica_main(index: int, device, factory: Callable, inbox, outbox) -> None:
                 try:  # idle: sleep until something arrives
                     commands.append(inbox.get(timeout=_POLL_S * 5))
                 except queue.Empty:
-                    if os.getppid() != parent:  # the server process is gone: nobody will send "stop"
+                    if orphaned():
                         return
             while True:
                 try:
@@ -204,6 +220,8 @@ def _replica_main(index: int, device, factory: Callable, inbox, outbox) -> None:
                         req_of.pop(seq.seq_id, None)
                         engine.abort_request(seq)
             if engine.has_unfinished():
+                if orphaned():  # busy, but the tokens would go nowhere
+                    return
                 out = []
                 for ev in engine.step():
                     rid = req_of.get(ev.seq_id)

@@ -8,9 +8,11 @@ from __future__ import annotations
 
 import torch
 
-from tokquay_b200.kv_cache import BlockAllocator, _hostpack
+from tokquay_b200._host import ref_sequence
+from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, PackedStep, _hostpack
 from tokquay_b200.model import GPT2, argmax_rows
-from tokquay_b200.sequence import Sequence, SequenceStatus
+
+Sequence, SequenceStatus = ref_sequence.Sequence, ref_sequence.SequenceStatus
 
 
 @torch.no_grad()
@@ -38,7 +40,7 @@ def paged_forward(
 def _eager_forward(model: GPT2, allocator: BlockAllocator, seqs: list[Sequence],
                    new_lens: list[int] | None) -> torch.Tensor:  # fmt: skip
     lens = new_lens or [s.num_uncached_tokens for s in seqs]
-    batch = allocator.batch_for(seqs, lens)
+    batch = DevicePagedBatch(allocator, None, None, None, packed=PackedStep.from_sequences(seqs, lens))
     logits = model.forward_paged(batch, last_only=True)[:, 0]
     for s, n in zip(seqs, lens):
         s.num_cached_tokens += n

@@ -19,13 +19,13 @@ graphs keyed by (sequence bucket, row capacity) the same way.
 from __future__ import annotations
 
 import bisect
+import weakref
 
 import torch
 
 from tokquay_b200 import _lib
-from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch, PlanWorkspace, _hostpack
+from tokquay_b200.kv_cache import BatchedKV, BlockAllocator, DevicePagedBatch, PlanWorkspace, _hostpack
 from tokquay_b200.model import argmax_rows
-from tokquay_b200.sequence import Sequence
 
 DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256, 512)
 # Row capacities of mixed-step graphs: a bucket of b sequences with up to
@@ -54,6 +54,8 @@ class DecodeGraphRunner:
         # logits, greedy tokens, launches per replay)
         self._graphs: dict[int | tuple[int, int], tuple] = {}
         self._pool = None  # one private memory pool shared by every bucket's graph
+        self._staged = 0  # serial number of the last step staged by stage_step()
+        self._greedy = None  # (weakref to the last replay's logits, rows, the graph's argmax buffer)
 
     @property
     def max_batch(self) -> int:
@@ -106,7 +108,7 @@ class DecodeGraphRunner:
                 return (b, b + e)
         return None
 
-    def _replay_step(self, seqs: list[Sequence], new_lens: list[int] | None) -> tuple | None:
+    def _replay_step(self, seqs: list, new_lens: list[int] | None) -> tuple | None:
         B = len(seqs)
         bucket = self.bucket_for(B) if B else None
         if bucket is None:
@@ -128,11 +130,41 @@ class DecodeGraphRunner:
             return None
         graph, ws, _, _, per_replay = entry
         self.model.last_h2d_bytes = ws.last_used_ints * 4
+        self._greedy = None  # the argmax buffers change under any earlier replay's logits
         graph.replay()
         self.model.kernel_launches += per_replay
         return entry
 
-    def try_run(self, seqs: list[Sequence], new_lens: list[int] | None = None) -> torch.Tensor | None:
+    def stage_step(self, seqs, new_lens: list[int] | None = None) -> "GraphStepBatch | None":
+        """Plan a decode step into its bucket's workspace and return the step
+        view that replays the bucket's graph (``BlockAllocator.batch_for`` with
+        graphs on); None, with nothing staged, for any other step."""
+        B = len(seqs)
+        bucket = self.bucket_for(B) if B else None
+        if bucket is None or (new_lens is not None and max(new_lens) != 1):
+            return None
+        entry = self.graph(bucket)
+        stream = torch.cuda.current_stream(self.allocator.pool.device)
+        layout = entry[1].stage_sequences(seqs, new_lens, stream, self.model.cfg.vocab_size,
+                                          decode_max_ctx=self.max_ctx)  # fmt: skip
+        if layout is None:
+            return None
+        self._staged += 1
+        return GraphStepBatch(self, entry, B, int(layout[_lib.PLAN_MAX_CTX]), self._staged)
+
+    def greedy_tokens_for(self, logits: torch.Tensor) -> torch.Tensor | None:
+        """The greedy tokens the graph computed with ``logits``, when these are
+        (a view of) the logits of the last ``GraphStepBatch`` replay; else None."""
+        g = self._greedy
+        if g is None or logits.dim() != 2:
+            return None
+        ref, rows, tokens = g
+        base = logits._base if logits._base is not None else logits
+        if base is not ref() or logits.shape[0] != rows:
+            return None
+        return tokens[:rows]
+
+    def try_run(self, seqs: list, new_lens: list[int] | None = None) -> torch.Tensor | None:
         """``run`` for a step that turns out to be a decode step (one new token
         per sequence, context within the graphs' capacity) that fits a
         bucket; None, with nothing planned or launched, for any other step.
@@ -140,7 +172,7 @@ class DecodeGraphRunner:
         entry = self._replay_step(seqs, new_lens)
         return None if entry is None else entry[2][:len(seqs)].clone()
 
-    def try_run_greedy(self, seqs: list[Sequence], new_lens: list[int] | None = None) -> torch.Tensor | None:
+    def try_run_greedy(self, seqs: list, new_lens: list[int] | None = None) -> torch.Tensor | None:
         """``try_run`` returning the step's greedy tokens instead of its logits:
         the ``[B]`` int64 argmax the graph computed (a copy), so a greedy
         decode loop neither copies the ``[B, vocab]`` logits nor runs a second
@@ -148,7 +180,7 @@ class DecodeGraphRunner:
         entry = self._replay_step(seqs, new_lens)
         return None if entry is None else entry[3][:len(seqs)].clone()
 
-    def decode_steps(self, seqs: list[Sequence], n_steps: int) -> list[list[int]] | None:
+    def decode_steps(self, seqs: list, n_steps: int) -> list[list[int]] | None:
         """``n_steps`` greedy decode steps of a fixed batch, one step ahead of
         the host: while step k runs, the host already plans step k+1 (the
         sequences' lengths and blocks do not depend on the token values) with a
@@ -181,6 +213,7 @@ class DecodeGraphRunner:
             self.step_h2d_bytes.append(ws.last_used_ints * 4)
             if k > 0:  # the previous step's argmax feeds this step, on the device
                 ws.plan[ids_off:ids_off + B].copy_(tokens[:B])
+            self._greedy = None
             graph.replay()
             self.model.kernel_launches += per_replay
             _advance(seqs)
@@ -241,7 +274,7 @@ class DecodeGraphRunner:
                     self.allocator.append_slot(s)
         return out
 
-    def run(self, seqs: list[Sequence]) -> torch.Tensor:
+    def run(self, seqs: list) -> torch.Tensor:
         """``try_run`` for a step known to be a decode step that fits: ``[B, vocab]``
         logits (a copy); ValueError otherwise.  Does not advance the sequences."""
         logits = self.try_run(seqs)
@@ -264,12 +297,58 @@ class DecodeGraphRunner:
         if ids is not None:
             off = int(ws.layout[_lib.PLAN_OFF_TOKEN_IDS])
             ws.plan[off:off + ids.numel()].copy_(ids)
+        self._greedy = None
         graph.replay()
         self.model.kernel_launches += per_replay
         return tokens
 
 
-def _advance(seqs: list[Sequence]) -> None:
+class GraphStepBatch(BatchedKV):
+    """A decode step staged into a captured graph's workspace: the step view
+    ``BlockAllocator.batch_for`` returns when CUDA graphs are on.  The model's
+    ``forward(input_ids, batch)`` replays the graph with the caller's token ids
+    (``replay``).  ``B``, ``T`` (1) and ``max_ctx`` are the reference's
+    ``BatchedKV`` members; the dense ``positions`` / ``mask`` / ``gather``
+    view is not built for a graph step."""
+
+    def __init__(self, runner: DecodeGraphRunner, entry: tuple, B: int, max_ctx: int, serial: int):
+        self.runner, self.entry, self.serial = runner, entry, serial
+        self.B, self.T, self.max_ctx = B, 1, max_ctx
+        self.allocator = runner.allocator
+
+    def replay(self, input_ids: torch.Tensor) -> torch.Tensor:
+        """Run the step: ``input_ids [B, 1]`` (on any device) -> logits ``[B, 1, V]``
+        (a copy; the greedy tokens of the same replay stay available through
+        ``DecodeGraphRunner.greedy_tokens_for``)."""
+        runner = self.runner
+        if self.serial != runner._staged:
+            raise RuntimeError("another step was staged after this one; build the step view again")
+        graph, ws, logits, tokens, per_replay = self.entry
+        B = self.B
+        off = int(ws.layout[_lib.PLAN_OFF_TOKEN_IDS])
+        ws.plan[off:off + B].copy_(input_ids.reshape(-1).to(ws.plan.device, non_blocking=True))
+        runner.model.last_h2d_bytes = ws.last_used_ints * 4
+        graph.replay()
+        runner.model.kernel_launches += per_replay
+        runner._staged += 1  # a view replays once
+        out = logits[:B].clone()
+        runner._greedy = (weakref.ref(out), B, tokens)
+        return out.unsqueeze(1)
+
+    @property
+    def positions(self):
+        raise TypeError("a CUDA-graph decode step has no dense positions/mask view; "
+                        "use this package's GPT2, or turn graphs off for the reference model")
+
+    last_idx = mask = positions
+
+    def write(self, layer, k, v):
+        raise TypeError("a CUDA-graph decode step runs whole; it has no per-layer write/gather")
+
+    gather = write
+
+
+def _advance(seqs: list) -> None:
     """num_cached_tokens += 1 for a replayed decode step."""
     if _hostpack is not None and hasattr(_hostpack, "advance_cached"):
         _hostpack.advance_cached(seqs)  # the native packer kept this step's lengths

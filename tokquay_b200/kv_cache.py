@@ -1,20 +1,20 @@
 """Paged KV cache: the block pool, its allocator and the per-step device view.
 
 Pool layout and allocator bookkeeping are the reference's contract
-(tokquay/kv_cache.py:1-14, :38-127) and are kept exactly: the same pool shape
+(tokquay/kv_cache.py:1-14, :38-127) and are not restated here:
+``BlockAllocator`` subclasses the reference's, so the pool shape
 
     pool: [num_blocks, n_layer, 2, n_head, block_size, d_head]   (dim 2: 0=K, 1=V)
 
-the same LIFO free list (reversed so block 0 is handed out first), the same ref
-counts and the same errors, so block tables and allocator state match the
-reference's bit for bit and its scheduler / engine run on top unchanged.
+the LIFO free list, the ref counts and ``OutOfBlocksError`` are the
+reference's own code, and its scheduler and engine run on top unchanged.
 
-What changes is the per-step view.  The reference's ``PagedBatch`` builds
-padded index tensors with Python loops and, per layer, gathers every
-sequence's blocks into a dense copy (kv_cache.py:174-242).  ``DevicePagedBatch``
-plans the step once on the host in C (``tq_plan_step``), ships it to the GPU in
-one copy, and the CUDA kernels scatter new K/V into the pool and read K/V
-blocks in place -- no dense copy, no padded query rows.
+What changes is the per-step view ``batch_for`` returns.  The reference's
+``PagedBatch`` builds padded index tensors with Python loops and, per layer,
+gathers every sequence's blocks into a dense copy (kv_cache.py:174-242).
+``DevicePagedBatch`` plans the step once on the host in C (``tq_plan_step``),
+ships it to the GPU in one copy, and the CUDA kernels scatter new K/V into the
+pool and read K/V blocks in place -- no dense copy, no padded query rows.
 """
 
 from __future__ import annotations
@@ -29,7 +29,7 @@ import numpy as np
 import torch
 
 from tokquay_b200 import _lib
-from tokquay_b200.sequence import Sequence
+from tokquay_b200._host import ref_kv_cache
 
 try:  # native host-side packing (tokquay_b200/csrc/hostpack.c); same results without it
     from tokquay_b200 import _hostpack
@@ -39,15 +39,17 @@ except ImportError:  # pragma: no cover - the Python packer below is used instea
 if TYPE_CHECKING:
     from tokquay_b200.model import GPT2Config
 
+# The reference's types, re-exported: the step view is a ``BatchedKV`` for the
+# reference model's ``isinstance`` dispatch (tokquay/model.py:73, :155).
+BatchedKV = ref_kv_cache.BatchedKV
+OutOfBlocksError = ref_kv_cache.OutOfBlocksError
+cdiv = ref_kv_cache.cdiv
+
 # Attention work is cut for one CTA per SM; keys of one (row group, head) pair
 # are split across CTAs only in pieces of at least this many 32-key chunks
 # (cuts between the warps of one CTA have no such floor: they merge in
 # shared memory).
 MIN_SPLIT_CHUNKS = 8
-
-
-def cdiv(a: int, b: int) -> int:
-    return -(-a // b)
 
 
 def attention_chunk_keys() -> int:
@@ -61,124 +63,37 @@ def attention_warps() -> int:
     return _lib.load().tq_attention_warps()
 
 
-class OutOfBlocksError(RuntimeError):
-    """Raised (without changing any state) when the free list is too short."""
-
-
-class BlockAllocator:
-    """Owns the pool, the free list and the ref counts (tokquay/kv_cache.py:38-127).
+class BlockAllocator(ref_kv_cache.BlockAllocator):
+    """The reference's allocator (tokquay/kv_cache.py:38-127), whose step view
+    is the device-resident ``DevicePagedBatch``.
 
     The pool must be float32 (what the kernels read) and ``block_size`` a power
     of two no larger than 256.  A CPU pool is allowed for bookkeeping-only use;
-    building a step view needs a CUDA pool.
+    building a step view needs a CUDA pool.  ``cfg`` is kept (the step view
+    reads the model's shape from it).
     """
 
-    def __init__(
-        self,
-        cfg: "GPT2Config",
-        num_blocks: int,
-        block_size: int = 16,
-        device=None,
-        dtype: torch.dtype = torch.float32,
-    ):
-        if num_blocks < 1 or block_size < 1:
-            raise ValueError("num_blocks and block_size must be positive")
-        if block_size & (block_size - 1) or block_size > 256:
+    def __init__(self, cfg: "GPT2Config", num_blocks: int, block_size: int = 16, device=None,
+                 dtype: torch.dtype = torch.float32):  # fmt: skip
+        if block_size >= 1 and (block_size & (block_size - 1) or block_size > 256):
             raise ValueError(f"block_size must be a power of two <= 256, got {block_size}")
         if dtype != torch.float32:
             raise ValueError(f"the paged kernels store K/V in float32, got {dtype}")
+        super().__init__(cfg, num_blocks, block_size, device, dtype)
         self.cfg = cfg
-        self.num_blocks = num_blocks
-        self.block_size = block_size
-        self.pool = torch.zeros(
-            num_blocks, cfg.n_layer, 2, cfg.n_head, block_size, cfg.d_head, device=device, dtype=dtype
-        )
-        # LIFO: the end of the list is handed out next, so reversed order gives block 0 first.
-        self._free: list[int] = list(range(num_blocks - 1, -1, -1))
-        self.ref_counts: list[int] = [0] * num_blocks
+        self.graph_runner = None  # set by GPT2.use_cuda_graphs(): decode steps then replay a graph
 
-    # ---- bookkeeping ---------------------------------------------------------------
-    @property
-    def num_free_blocks(self) -> int:
-        return len(self._free)
-
-    @property
-    def num_used_blocks(self) -> int:
-        return self.num_blocks - len(self._free)
-
-    @property
-    def bytes_per_block(self) -> int:
-        return self.pool[0].numel() * self.pool.element_size()
-
-    def blocks_needed(self, num_tokens: int) -> int:
-        return cdiv(num_tokens, self.block_size)
-
-    # ---- allocation ----------------------------------------------------------------
-    def can_allocate(self, num_tokens: int) -> bool:
-        return self.blocks_needed(num_tokens) <= self.num_free_blocks
-
-    def allocate(self, seq: Sequence, num_tokens: int | None = None) -> None:
-        """Give a block-less sequence blocks for ``num_tokens`` positions
-        (default: all of its tokens)."""
-        if seq.block_table:
-            raise ValueError(f"sequence {seq.seq_id} already owns blocks")
-        n = self.blocks_needed(seq.num_tokens if num_tokens is None else num_tokens)
-        seq.block_table = self._take(n)
-
-    def can_append_slot(self, seq: Sequence) -> bool:
-        return self.blocks_needed(seq.num_tokens) - len(seq.block_table) <= self.num_free_blocks
-
-    def append_slot(self, seq: Sequence) -> bool:
-        """Grow the table to cover ``seq.num_tokens`` positions; True if a block
-        was taken.  ``OutOfBlocksError`` leaves everything unchanged."""
-        missing = self.blocks_needed(seq.num_tokens) - len(seq.block_table)
-        if missing <= 0:
-            return False
-        seq.block_table.extend(self._take(missing))
-        return True
-
-    def free(self, seq: Sequence) -> None:
-        """Release the sequence's blocks (ref-counted; a block-less sequence is a no-op)."""
-        for b in seq.block_table:
-            if self.ref_counts[b] <= 0:
-                raise RuntimeError(f"double free of block {b}")
-            self.ref_counts[b] -= 1
-            if self.ref_counts[b] == 0:
-                self._free.append(b)
-        seq.block_table = []
-
-    def _take(self, n: int) -> list[int]:
-        if n > len(self._free):
-            raise OutOfBlocksError(f"need {n} blocks, only {len(self._free)} free")
-        taken = [self._free.pop() for _ in range(n)]
-        for b in taken:
-            self.ref_counts[b] = 1
-        return taken
-
-    # ---- model-facing --------------------------------------------------------------
-    def batch_for(self, seqs: list[Sequence], new_lens: list[int] | None = None) -> "DevicePagedBatch":
+    def batch_for(self, seqs, new_lens: list[int] | None = None) -> "DevicePagedBatch":
         """Step view for ``seqs``: each feeds ``new_lens[i]`` tokens (default: all
-        uncached ones) from position ``num_cached_tokens`` (tokquay/kv_cache.py:122-127)."""
+        uncached ones) from position ``num_cached_tokens`` (tokquay/kv_cache.py:122-127).
+        With CUDA graphs on, a decode step that a captured graph covers is
+        staged into that graph's workspace instead (``GraphStepBatch``)."""
+        runner = self.graph_runner
+        if runner is not None:
+            step = runner.stage_step(seqs, new_lens)
+            if step is not None:
+                return step
         return DevicePagedBatch(self, None, None, None, packed=PackedStep.from_sequences(seqs, new_lens))
-
-
-class BatchedKV:
-    """What a paged model forward needs from a step view (tokquay/kv_cache.py:130-157):
-    ``B``, ``T``, ``max_ctx``, ``positions [B, T]``, ``last_idx [B]``,
-    ``mask [B, 1, T, S]``, ``write(layer, k, v)``, ``gather(layer)``."""
-
-    B: int
-    T: int
-    max_ctx: int
-    positions: torch.Tensor
-    last_idx: torch.Tensor
-    mask: torch.Tensor
-
-    def write(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
-        raise NotImplementedError
-
-    def gather(self, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
-        raise NotImplementedError
 
 
 # ------------------------------------------------------------------------------ pinned staging
@@ -279,7 +194,7 @@ class PackedStep:
         if len(lens) != len(seqs):
             raise ValueError("block_tables, start and new_lens must be non-empty and the same length")
         ids = list(itertools.chain.from_iterable(
-            s.tokens_slice(st, st + n) for s, st, n in zip(seqs, starts, lens) if n > 0 and st >= 0))  # fmt: skip
+            s.token_ids[st:st + n] for s, st, n in zip(seqs, starts, lens) if n > 0 and st >= 0))  # fmt: skip
         return cls.from_lists([s.block_table for s in seqs], starts, lens, ids)
 
 

@@ -20,27 +20,14 @@ their outputs would be discarded (model.py:179).
 
 from __future__ import annotations
 
-from dataclasses import dataclass
-
 import torch
 import torch.nn as nn
 
 from tokquay_b200 import _lib
+from tokquay_b200._host import ref_model
 from tokquay_b200.kv_cache import DevicePagedBatch
 
-
-@dataclass
-class GPT2Config:
-    vocab_size: int = 50257
-    n_positions: int = 1024
-    n_embd: int = 768
-    n_layer: int = 12
-    n_head: int = 12
-    layer_norm_eps: float = 1e-5
-
-    @property
-    def d_head(self) -> int:
-        return self.n_embd // self.n_head
+GPT2Config = ref_model.GPT2Config  # the reference's config (tokquay/model.py:24-35)
 
 
 class Attention(nn.Module):
@@ -136,6 +123,7 @@ class GPT2(nn.Module):
         from tokquay_b200.graphs import DEFAULT_BUCKETS, DecodeGraphRunner
 
         self.graph_runner = DecodeGraphRunner(self, allocator, buckets or DEFAULT_BUCKETS, max_ctx)
+        allocator.graph_runner = self.graph_runner  # batch_for stages decode steps for it
         return self.graph_runner
 
     def _weight_t(self, name: str, w: torch.Tensor) -> torch.Tensor:
@@ -163,13 +151,24 @@ class GPT2(nn.Module):
     @torch.no_grad()
     def forward(self, input_ids: torch.Tensor, cache: DevicePagedBatch, last_only: bool = False) -> torch.Tensor:
         """``input_ids [B, T]`` (right-padded, as the reference takes them) ->
-        logits ``[B, T, V]`` (or ``[B, 1, V]`` with ``last_only``).  Logits of
-        padded slots are zero.  Only the paged path exists in this package."""
-        if not isinstance(cache, DevicePagedBatch):
-            raise TypeError("this model runs the paged forward only: pass a DevicePagedBatch")
+        logits ``[B, T, V]`` (or ``[B, 1, V]`` with ``last_only``), the call the
+        reference's ``paged_forward`` makes (tokquay/generate.py:84).  Logits of
+        padded slots are zero.  Only the paged path exists in this package:
+        ``cache`` is the step view ``BlockAllocator.batch_for`` returned (a
+        ``DevicePagedBatch``, or a decode step staged into a CUDA graph)."""
+        from tokquay_b200.graphs import GraphStepBatch
+
+        graph_step = isinstance(cache, GraphStepBatch)
+        if not (graph_step or isinstance(cache, DevicePagedBatch)):
+            raise TypeError("this model runs the paged forward only: pass the step view of "
+                            "tokquay_b200.BlockAllocator.batch_for")
         B, T = input_ids.shape
         if (B, T) != (cache.B, cache.T):
             raise ValueError(f"input_ids {tuple(input_ids.shape)} does not match batch {(cache.B, cache.T)}")
+        if graph_step:
+            if cache.runner.model is not self:
+                raise ValueError("the step was staged for another model's CUDA graphs")
+            return cache.replay(input_ids)
         b, t = cache._valid_bt()
         ids = input_ids.to(cache.pool.device)[b, t].to(torch.int32).contiguous()
         return self.forward_paged(cache, last_only=last_only, ids=ids)

@@ -28,6 +28,7 @@ __all__ = [
     "barrier",
     "max_over_ranks",
     "sum_over_ranks",
+    "all_over_ranks",
     "whole_job_rate",
     "replica_seed",
 ]
@@ -111,6 +112,17 @@ def max_over_ranks(x: float, world: int) -> float:
 
 def sum_over_ranks(x: float, world: int) -> float:
     return _reduce(x, world, _dist().ReduceOp.SUM if world > 1 else None)
+
+
+def all_over_ranks(x: float, world: int) -> list[float]:
+    """Every rank's ``x``, in rank order (the spread behind a max over ranks)."""
+    if world == 1:
+        return [float(x)]
+    dist = _dist()
+    t = torch.zeros(world, dtype=torch.float64, device=_device())
+    t[dist.get_rank()] = float(x)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return [float(v) for v in t.tolist()]
 
 
 def whole_job_rate(units: float, seconds: float, world: int) -> tuple[float, float, float]:

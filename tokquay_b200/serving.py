@@ -27,7 +27,9 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
-from tokquay_b200.sequence import SamplingParams
+from tokquay_b200._host import ref_sequence
+
+SamplingParams = ref_sequence.SamplingParams
 
 __all__ = ["RequestSpec", "make_workload", "round_robin", "run_trace", "summarize"]
 

@@ -171,3 +171,8 @@ CONFIGS = {
     3: dict(n_prefill=4, n_decode=60, len_range=(16, 256), block_sizes=(16, 32), num_blocks=1024),
     4: dict(n_seqs=512, ctx_range=(256, 1024), block_size=32, pool_bytes=150e9),
 }
+
+# Config 4's parity case: every 8th of its 512 sequences (the share of one of
+# eight replicas) on a pool of 4,096 blocks (9.7 GB), a size the reference's
+# dense-gather forward also runs at on a host.
+CFG4_SUBSET = dict(shard=(0, 8), num_blocks=4096, steps=3)
