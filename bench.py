@@ -428,6 +428,7 @@ def run_ours(args, world, rank, local):
     plans, batches, ctx_per_step, nparts_per_step = [], [], [], []
     if runner:
         caps = runner.graph(bucket)[1].caps  # captures the bucket's graph
+    t_plan = time.perf_counter()
     for k in range(total_steps):
         starts = [s.num_cached_tokens for s in seqs]
         ids = [s.token_ids[st:st + 1][0] for s, st in zip(seqs, starts)]
@@ -447,6 +448,7 @@ def run_ours(args, world, rank, local):
                 s.num_cached_tokens += 1
                 s.append_token(0)  # placeholder; the device loop feeds the real argmax
                 a.append_slot(s)
+    plan_ms = (time.perf_counter() - t_plan) * 1e3 / total_steps  # host planning + packing per step
     torch.cuda.synchronize(device)
 
     prev = [None]
@@ -544,6 +546,11 @@ def run_ours(args, world, rank, local):
     barrier(world)
     e2e_ms = max(e0.elapsed_time(e1), 0.0)
     e2e_ms_max = max_over_ranks(e2e_ms, world)
+    # Every rank's own figures: the job's time is the slowest rank's, and the
+    # spread says what limits it (host planning, the launch stream, the GPU).
+    per_rank = {"ms_per_step": [x / K for x in all_over_ranks(ms, world)],
+                "e2e_ms_per_step": [x / K for x in all_over_ranks(e2e_ms, world)],
+                "host_plan_ms_per_step": all_over_ranks(plan_ms, world)}  # fmt: skip
     # Bytes copied per step: the packed step plan (host->device, token ids
     # included) and the B int64 sampled tokens back.
     h2d_bytes = sum(h2d) / len(h2d)
@@ -617,7 +624,14 @@ def run_ours(args, world, rank, local):
             },
             "gpu_launches": launches,
             "clocks": clocks.summary(),
+            "per_rank": {**per_rank, "note": "device-timed step, end-to-end step and host planning time of "
+                                             "each rank (rank order); value uses the slowest rank"},
         }
+        if strong and world > 1:
+            result["config"]["scaling_limit"] = (
+                f"strong scaling: {B} of the batch's {spec['n_seqs']} sequences per replica; the fp32 linears "
+                "(torch SIMT SGEMM, kept by the north star) take about as long at 64 rows as at 512, so the step "
+                "time does not fall in proportion to the sequences per GPU")
     if args.kernel_table and rank == 0:
         log(kernel_table(model, a, seqs, spec))
     return result

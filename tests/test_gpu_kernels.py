@@ -168,8 +168,8 @@ def test_paged_attention_split_k_is_exercised():
 
 
 def _merge_kinds(batch) -> set[int]:
-    """Flags of the plan's work items: 0 whole, 1 cut inside a CTA, 2 split
-    across CTAs, 3 both."""
+    """Merge flags of the plan's work items: 0 whole, 1 cut inside a CTA, 2
+    split across CTAs, 3 both (the decode bit, 4, is left out)."""
     L = batch.layout
     plan = batch.plan.cpu().numpy()
     nw = batch.n_ctas * attention_warps()
@@ -179,7 +179,7 @@ def _merge_kinds(batch) -> set[int]:
     ro = o + 16 * nw + (nw + 8) // 8 * 8
     rest = plan[ro:ro + 8 * int(offs[-1])].reshape(-1, 8)
     words = [w[2] for w in first if w[4] != 0] + [w[2] for w in rest]
-    return {int(np.uint32(x)) >> 24 for x in words}
+    return {(int(np.uint32(x)) >> 24) & 3 for x in words}
 
 
 @pytest.mark.parametrize("n_ctas", [1, 5, 37, 148, 400])
