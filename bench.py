@@ -407,6 +407,7 @@ def run_ours(args, world, rank, local):
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.set_float32_matmul_precision("highest")
     model = make_model(device)
+    model.fused_lm_head = args.fused_lm_head
     cfg = model.cfg
     a = make_allocator(spec, cfg, device)
     # Every replica decodes its own copy of the same batch (own sequence objects,
@@ -585,6 +586,9 @@ def run_ours(args, world, rank, local):
                 "num_blocks": a.num_blocks,
                 "parallelism": f"replicas{world} (one engine + KV pool per GPU, no collective)",
                 "cuda_graphs": runner is not None,
+                "lm_head": ("opt-in fused ln_f + LM head + greedy argmax (tq_lm_head_argmax, fp32 CUDA cores)"
+                            if args.fused_lm_head and B <= _lib.LM_HEAD_MAX_ROWS else
+                            "torch fp32 matmul (TF32 off) + tq_argmax_rows, as the north star keeps it"),
                 "l2": "inputs larger than L2: each step reads the whole weight set (0.5 GB) and every "
                       "context's K/V of 12 layers (> 1 GB), so no step finds the previous step's data in L2",
             },  # fmt: skip
@@ -1417,6 +1421,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graphs", action="store_true", help="launch every kernel from Python (no CUDA graphs)")
+    ap.add_argument("--fused-lm-head", action="store_true",
+                    help="opt-in: greedy steps end in the fused ln_f + LM head + argmax kernel "
+                         "(tq_lm_head_argmax) instead of torch's fp32 matmul + tq_argmax_rows")
     ap.add_argument("--num-seqs", type=int, default=0, help="override the workload's sequence count (profiling)")
     ap.add_argument("--kernel-table", action="store_true",
                     help="after the run, print per-kernel device times of 10 more decode steps (stderr)")

@@ -31,6 +31,10 @@
  *                                                            tokquay/model.py:179-180
  *   tq_bias_gelu               F.gelu(c_fc(x), approximate="tanh"), and the
  *                              bias of c_attn            tokquay/model.py:110, :69
+ *   tq_lm_head_argmax          last-row select, ln_f, the tied LM head and the
+ *                              greedy argmax in one kernel (no logits tensor)
+ *                                                            tokquay/model.py:179-181,
+ *                                                            tokquay/engine.py:189-194
  *
  * Pool layout (the reference's, tokquay/kv_cache.py:1-14, :51-53):
  *   pool[num_blocks][n_layer][2 (K,V)][n_head][block_size][head_dim], fp32,
@@ -51,7 +55,7 @@
 extern "C" {
 #endif
 
-#define TQ_ABI_VERSION 5
+#define TQ_ABI_VERSION 6
 
 enum tq_status {
   TQ_OK = 0,
@@ -260,6 +264,29 @@ TQ_API int tq_layernorm_rows(float* out, const float* x, const int32_t* rows, co
 TQ_API int tq_bias_gelu(float* out, const float* h, int32_t n_parts, int64_t part_stride,
                  const float* bias, int32_t n_cols, int32_t apply_gelu,
                  const int32_t* d_num_rows, int32_t max_rows, void* stream);
+
+/* tq_lm_head_argmax: rows per launch, vocabulary columns per CTA slice, and the
+ * bytes of its scratch (per-row maxima and a counter).  Zero the scratch once;
+ * every launch that completes leaves it zero again. */
+#define TQ_LM_HEAD_MAX_ROWS 64
+#define TQ_LM_HEAD_SLICE 352
+#define TQ_LM_HEAD_SCRATCH_BYTES 520
+
+/* Greedy tokens of a step's last rows in one kernel, without a logits tensor:
+ *   h[r]      = LayerNorm(x[rows[r]]; ln_w, ln_b, eps)      (rows == NULL: x[r])
+ *   tokens[r] = argmax_v sum_c h[r][c] * wte_t[c][v]       (the tied LM head)
+ * with torch.argmax's rules (NaN counts as the largest value, the first index
+ * among equals); max_logit[r] (may be NULL) gets that logit.  fp32 on the CUDA
+ * cores.  wte_t is the embedding matrix transposed, [n_embd][vocab_stride],
+ * 16-byte aligned, with vocab_stride a multiple of 4 and at least
+ * ceil(vocab_size / TQ_LM_HEAD_SLICE) * TQ_LM_HEAD_SLICE, columns past
+ * vocab_size zero.  n_embd a multiple of 32 and at most 768; max_rows at most
+ * TQ_LM_HEAD_MAX_ROWS.  Calls that share `scratch` must not overlap on the GPU. */
+TQ_API int tq_lm_head_argmax(int64_t* tokens, float* max_logit, const float* x, int64_t x_row_stride,
+                             const int32_t* rows, const float* ln_w, const float* ln_b, float eps,
+                             int32_t n_embd, const float* wte_t, int64_t vocab_stride,
+                             int32_t vocab_size, void* scratch, const int32_t* d_num_rows,
+                             int32_t max_rows, void* stream);
 
 #ifdef __cplusplus
 }

@@ -71,9 +71,16 @@ SIGNATURES: dict[str, tuple] = {
     "tq_argmax_rows": (c_int, [_P, c_int64, c_int32, _P, _P, c_int32, _P]),
     "tq_layernorm_rows": (c_int, [_P, _P, _P, _P, _P, c_float, c_int32, _P, c_int32, _P]),
     "tq_bias_gelu": (c_int, [_P, _P, c_int32, c_int64, _P, c_int32, c_int32, _P, c_int32, _P]),
+    "tq_lm_head_argmax": (c_int, [_P, _P, _P, c_int64, _P, _P, _P, c_float, c_int32, _P, c_int64, c_int32,
+                                  _P, _P, c_int32, _P]),
 }
 
-EXPECTED_ABI = 5
+EXPECTED_ABI = 6
+
+# tq_lm_head_argmax limits (TQ_LM_HEAD_* in include/tokquay_b200.h).
+LM_HEAD_MAX_ROWS = 64
+LM_HEAD_SLICE = 352
+LM_HEAD_SCRATCH_BYTES = 520
 
 # Split-K partials the no-allocation attention entry point can hold
 # (TQ_NOALLOC_MAX_PARTIALS in include/tokquay_b200.h).

@@ -16,6 +16,7 @@
 #include "elementwise.cuh"
 #include "host_error.h"
 #include "kv_write.cuh"
+#include "lm_head.cuh"
 #include "paged_attention.cuh"
 
 namespace tq {
@@ -55,6 +56,10 @@ int device_setup(int* sm_count) {
     if (e != cudaSuccess)
       return set_error(TQ_ERR_CUDA, "cudaFuncSetAttribute(paged_attention): %s",
                        cudaGetErrorString(e));
+    e = cudaFuncSetAttribute(lm_head_argmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kLmSmemBytes);
+    if (e != cudaSuccess)
+      return set_error(TQ_ERR_CUDA, "cudaFuncSetAttribute(lm_head_argmax): %s", cudaGetErrorString(e));
     d.ready = true;
   }
   *sm_count = d.sm_count;
@@ -561,6 +566,66 @@ int tq_argmax_rows(const float* x, int64_t row_stride, int32_t n_cols, int64_t* 
   launch_dependent(argmax_rows_kernel, max_rows * kArgmaxSlices, kArgmaxThreads, (cudaStream_t)stream, 
       x, row_stride, n_cols, reinterpret_cast<long long*>(out), d_num_rows);
   return check_launch("argmax_rows");
+}
+
+static_assert(TQ_LM_HEAD_MAX_ROWS == tq::kLmMaxRows && TQ_LM_HEAD_SLICE == tq::kLmWidth &&
+                  TQ_LM_HEAD_SCRATCH_BYTES >= tq::kLmMaxRows * 8 + 4,
+              "tq_lm_head_argmax limits in the header match the kernel");
+
+int tq_lm_head_argmax(int64_t* tokens, float* max_logit, const float* x, int64_t x_row_stride,
+                      const int32_t* rows, const float* ln_w, const float* ln_b, float eps, int32_t n_embd,
+                      const float* wte_t, int64_t vocab_stride, int32_t vocab_size, void* scratch,
+                      const int32_t* d_num_rows, int32_t max_rows, void* stream) {
+  if (max_rows < 0 || max_rows > kLmMaxRows)
+    return set_error(TQ_ERR_UNSUPPORTED, "lm_head_argmax: max_rows must be in [0, %d]", kLmMaxRows);
+  if (n_embd < 32 || n_embd > kLmMaxEmbd || n_embd % 32 || n_embd % kLmKTile)
+    return set_error(TQ_ERR_UNSUPPORTED, "lm_head_argmax: n_embd must be a multiple of 32 in [32, %d]",
+                     kLmMaxEmbd);
+  if (vocab_size < 1) return set_error(TQ_ERR_INVALID, "lm_head_argmax: vocab_size must be >= 1");
+  const int64_t slices = ((int64_t)vocab_size + kLmWidth - 1) / kLmWidth;
+  if (vocab_stride < slices * kLmWidth || vocab_stride % 4)
+    return set_error(TQ_ERR_INVALID,
+                     "lm_head_argmax: vocab_stride must be a multiple of 4 and >= %lld (slices of %d columns)",
+                     (long long)(slices * kLmWidth), kLmWidth);
+  if (x_row_stride < n_embd) return set_error(TQ_ERR_INVALID, "lm_head_argmax: x_row_stride < n_embd");
+  if (max_rows == 0) return TQ_OK;
+  if (!tokens || !x || !ln_w || !ln_b || !wte_t || !scratch || !d_num_rows)
+    return set_error(TQ_ERR_INVALID, "lm_head_argmax: NULL argument");
+  if (!aligned(wte_t, 16) || !aligned(scratch, 8))
+    return set_error(TQ_ERR_INVALID, "lm_head_argmax: wte_t must be 16-byte and scratch 8-byte aligned");
+  int sms = 0;
+  const int st = device_setup(&sms);
+  if (st) return st;
+  LmHeadParams p;
+  p.x = x;
+  p.x_stride = x_row_stride;
+  p.sel = rows;
+  p.ln_w = ln_w;
+  p.ln_b = ln_b;
+  p.eps = eps;
+  p.C = n_embd;
+  p.wt = wte_t;
+  p.vstride = vocab_stride;
+  p.V = vocab_size;
+  p.tokens = reinterpret_cast<long long*>(tokens);
+  p.max_logit = max_logit;
+  p.best = reinterpret_cast<unsigned long long*>(scratch);
+  p.done = reinterpret_cast<unsigned int*>(reinterpret_cast<char*>(scratch) + kLmMaxRows * 8);
+  p.n_rows = d_num_rows;
+  p.max_rows = max_rows;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)slices);
+  cfg.blockDim = dim3(kLmThreads);
+  cfg.dynamicSmemBytes = kLmSmemBytes;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, lm_head_argmax_kernel, p);
+  if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "lm_head_argmax launch: %s", cudaGetErrorString(e));
+  return check_launch("lm_head_argmax");
 }
 
 int tq_bias_gelu(float* out, const float* h, int32_t n_parts, int64_t part_stride, const float* bias,

@@ -47,6 +47,24 @@ def _eager_forward(model: GPT2, allocator: BlockAllocator, seqs: list[Sequence],
     return logits
 
 
+def _eager_greedy(model: GPT2, allocator: BlockAllocator, seqs: list[Sequence],
+                  new_lens: list[int] | None) -> torch.Tensor:  # fmt: skip
+    """Greedy tokens of one eager step (int64 ``[B]`` on the device): the fused
+    LM head when the model has it on and the batch fits it, else the logits'
+    ``tq_argmax_rows``.  Advances ``num_cached_tokens``."""
+    from tokquay_b200 import _lib
+
+    if not (model.fused_lm_head and len(seqs) <= _lib.LM_HEAD_MAX_ROWS):
+        return argmax_rows(_eager_forward(model, allocator, seqs, new_lens))
+    lens = new_lens or [s.num_uncached_tokens for s in seqs]
+    batch = DevicePagedBatch(allocator, None, None, None, packed=PackedStep.from_sequences(seqs, lens))
+    tokens = torch.empty(batch.B, dtype=torch.int64, device=allocator.pool.device)
+    model.forward_paged(batch, last_only=True, greedy_out=tokens)
+    for s, n in zip(seqs, lens):
+        s.num_cached_tokens += n
+    return tokens
+
+
 def _advance_after_replay(seqs: list[Sequence]) -> None:
     if _hostpack is not None and hasattr(_hostpack, "advance_cached"):
         _hostpack.advance_cached(seqs)  # the native packer kept this step's lengths
@@ -74,7 +92,7 @@ def paged_greedy_step(
         if tokens is not None:
             _advance_after_replay(seqs)
             return tokens.tolist()
-    return argmax_rows(_eager_forward(model, allocator, seqs, new_lens)).tolist()
+    return _eager_greedy(model, allocator, seqs, new_lens).tolist()
 
 
 @torch.no_grad()

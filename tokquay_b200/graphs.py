@@ -66,7 +66,13 @@ class DecodeGraphRunner:
         return self.buckets[i] if i < len(self.buckets) else None
 
     def _capture(self, key):
-        bucket, rows = (key, key) if isinstance(key, int) else key
+        # int: a decode bucket; (sequences, rows): a mixed step; ("greedy", bucket):
+        # a decode bucket that ends in the fused LM head + argmax (no logits).
+        greedy = isinstance(key, tuple) and key[0] == "greedy"
+        if greedy:
+            bucket = rows = key[1]
+        else:
+            bucket, rows = (key, key) if isinstance(key, int) else key
         ws = PlanWorkspace(self.allocator, bucket, rows, self.max_ctx)
         # A plan whose counts are all zero: every kernel of the step exits at
         # once, so the warm-up run below touches neither the pool nor anything else.
@@ -77,8 +83,12 @@ class DecodeGraphRunner:
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
             for _ in range(2):  # warm cuBLAS handles and workspaces outside the capture
-                lg = self.model.forward_paged(view, last_only=True)[:, 0]
-                argmax_rows(lg, d_num_rows=view.count_ptr(3), max_rows=bucket)
+                if greedy:
+                    self.model.forward_paged(view, last_only=True,
+                                             greedy_out=torch.empty(bucket, dtype=torch.int64, device=dev))
+                else:
+                    lg = self.model.forward_paged(view, last_only=True)[:, 0]
+                    argmax_rows(lg, d_num_rows=view.count_ptr(3), max_rows=bucket)
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
         graph = torch.cuda.CUDAGraph()
@@ -86,17 +96,23 @@ class DecodeGraphRunner:
             self._pool = torch.cuda.graph_pool_handle()
         launches = self.model.kernel_launches
         with torch.cuda.graph(graph, pool=self._pool):
-            logits = self.model.forward_paged(view, last_only=True)[:, 0]
-            tokens = argmax_rows(logits, d_num_rows=view.count_ptr(3), max_rows=bucket)  # greedy sampling
-        per_replay = self.model.kernel_launches - launches + 1
+            if greedy:
+                tokens = torch.empty(bucket, dtype=torch.int64, device=dev)
+                self.model.forward_paged(view, last_only=True, greedy_out=tokens)
+                logits = None
+            else:
+                logits = self.model.forward_paged(view, last_only=True)[:, 0]
+                tokens = argmax_rows(logits, d_num_rows=view.count_ptr(3), max_rows=bucket)  # greedy sampling
+        per_replay = self.model.kernel_launches - launches + (0 if greedy else 1)
         self.model.kernel_launches = launches
         entry = (graph, ws, logits, tokens, per_replay)
         self._graphs[key] = entry
         return entry
 
     def graph(self, key):
-        """The graph of a decode bucket (an int) or of a mixed step's
-        (sequences, rows) capacities; captured on first use."""
+        """The graph of a decode bucket (an int), of a mixed step's (sequences,
+        rows) capacities, or of a decode bucket ending in the fused LM head
+        (("greedy", bucket)); captured on first use."""
         return self._graphs.get(key) or self._capture(key)
 
     def mixed_key(self, n_seqs: int, n_rows: int) -> tuple[int, int] | None:
@@ -108,7 +124,14 @@ class DecodeGraphRunner:
                 return (b, b + e)
         return None
 
-    def _replay_step(self, seqs: list, new_lens: list[int] | None) -> tuple | None:
+    def greedy_key(self, bucket: int):
+        """The graph key of a decode bucket whose tokens alone are wanted: the
+        fused-head variant when the model has it on and the bucket fits it."""
+        if self.model.fused_lm_head and bucket <= _lib.LM_HEAD_MAX_ROWS:
+            return ("greedy", bucket)
+        return bucket
+
+    def _replay_step(self, seqs: list, new_lens: list[int] | None, greedy: bool = False) -> tuple | None:
         B = len(seqs)
         bucket = self.bucket_for(B) if B else None
         if bucket is None:
@@ -117,7 +140,7 @@ class DecodeGraphRunner:
         vocab = self.model.cfg.vocab_size
         entry = None
         if new_lens is None or max(new_lens) == 1:  # a decode step
-            entry = self.graph(bucket)
+            entry = self.graph(self.greedy_key(bucket) if greedy else bucket)
             if entry[1].stage_sequences(seqs, new_lens, stream, vocab, decode_max_ctx=self.max_ctx) is None:
                 entry = None
         if entry is None and new_lens is not None and self.mixed_extra:  # prompt chunks beside decodes
@@ -177,7 +200,7 @@ class DecodeGraphRunner:
         the ``[B]`` int64 argmax the graph computed (a copy), so a greedy
         decode loop neither copies the ``[B, vocab]`` logits nor runs a second
         argmax; None, with nothing planned or launched, for any other step."""
-        entry = self._replay_step(seqs, new_lens)
+        entry = self._replay_step(seqs, new_lens, greedy=True)
         return None if entry is None else entry[3][:len(seqs)].clone()
 
     def decode_steps(self, seqs: list, n_steps: int) -> list[list[int]] | None:
@@ -197,7 +220,7 @@ class DecodeGraphRunner:
         bucket = self.bucket_for(B) if B else None
         if bucket is None or n_steps < 1:
             return None
-        graph, ws, _, tokens, per_replay = self.graph(bucket)
+        graph, ws, _, tokens, per_replay = self.graph(self.greedy_key(bucket))
         dev = self.allocator.pool.device
         stream = torch.cuda.current_stream(dev)
         vocab = self.model.cfg.vocab_size
@@ -262,11 +285,10 @@ class DecodeGraphRunner:
         else:
             settle(n_steps - 1, False)
             return out
-        from tokquay_b200.generate import _eager_forward
-        from tokquay_b200.model import argmax_rows
+        from tokquay_b200.generate import _eager_greedy
 
         for k in range(done, n_steps):  # the rest one at a time, eagerly
-            toks = argmax_rows(_eager_forward(self.model, self.allocator, seqs, None)).tolist()
+            toks = _eager_greedy(self.model, self.allocator, seqs, None).tolist()
             for s, o, t in zip(seqs, out, toks):
                 s.append_token(t)
                 o.append(t)
@@ -289,7 +311,7 @@ class DecodeGraphRunner:
         and ``.n_ctas``),
         optionally overwriting its token ids from a device tensor first.
         Returns the graph's greedy-token buffer (valid until the next replay)."""
-        graph, ws, _, tokens, per_replay = self.graph(bucket)
+        graph, ws, _, tokens, per_replay = self.graph(self.greedy_key(bucket))
         if plan.numel() != ws.total:
             raise ValueError(f"plan of {plan.numel()} int32 does not fit bucket {bucket}'s workspace "
                              f"({ws.total}); plan it with that workspace's caps and n_ctas ({ws.n_ctas})")

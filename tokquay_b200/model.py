@@ -109,6 +109,12 @@ class GPT2(nn.Module):
         self.kernel_launches = 0
         self.last_h2d_bytes = 0  # plan bytes the last forward's batch copied to the device
         self.graph_runner = None  # set by use_cuda_graphs()
+        # Opt-in, not the reference's LM head: greedy-token steps run ln_f, the
+        # tied LM head and the argmax as one fp32 CUDA-core kernel
+        # (tq_lm_head_argmax) instead of torch's fp32 matmul + tq_argmax_rows,
+        # for batches of up to 64 sequences.
+        self.fused_lm_head = False
+        self._lm_scratch: torch.Tensor | None = None
         self._wt: dict[str, tuple] = {}  # name -> (parameter version, contiguous W^T)
         self.cfg = cfg or GPT2Config()
         self.wte = nn.Embedding(self.cfg.vocab_size, self.cfg.n_embd)
@@ -134,6 +140,37 @@ class GPT2(nn.Module):
             hit = (w._version, w.detach().t().contiguous())
             self._wt[name] = hit
         return hit[1]
+
+    def _wte_t_padded(self) -> tuple[torch.Tensor, int]:
+        """``wte`` transposed to ``[C, vstride]`` with zero columns past the
+        vocabulary, vstride a whole number of the fused head's column slices;
+        rebuilt if the embedding changes."""
+        w = self.wte.weight
+        hit = self._wt.get("wte_pad")
+        if hit is None or hit[0] != w._version or hit[1].device != w.device:
+            V, C = w.shape
+            slice_ = _lib.LM_HEAD_SLICE
+            vstride = -(-V // slice_) * slice_
+            wt = torch.zeros(C, vstride, dtype=torch.float32, device=w.device)
+            wt[:, :V] = w.detach().t()
+            hit = (w._version, wt)
+            self._wt["wte_pad"] = hit
+        return hit[1], hit[1].shape[1]
+
+    def lm_head_greedy(self, x: torch.Tensor, rows_ptr: int | None, n_rows_ptr: int, max_rows: int,
+                       tokens: torch.Tensor, stream: int) -> None:
+        """``tokens[r] = argmax((ln_f(x[rows[r]])) @ wte.T)`` for the device's
+        row count (``n_rows_ptr``), up to ``max_rows`` <= 64: one kernel, no
+        logits tensor (tokquay/model.py:179-181 + tokquay/engine.py:189-194)."""
+        lib = _lib.load()
+        wt, vstride = self._wte_t_padded()
+        if self._lm_scratch is None or self._lm_scratch.device != x.device:
+            self._lm_scratch = torch.zeros(_lib.LM_HEAD_SCRATCH_BYTES, dtype=torch.uint8, device=x.device)
+        cfg = self.cfg
+        _lib.check(lib.tq_lm_head_argmax(
+            tokens.data_ptr(), None, x.data_ptr(), x.stride(0), rows_ptr, self.ln_f.weight.data_ptr(),
+            self.ln_f.bias.data_ptr(), cfg.layer_norm_eps, cfg.n_embd, wt.data_ptr(), vstride, cfg.vocab_size,
+            self._lm_scratch.data_ptr(), n_rows_ptr, max_rows, stream), "tq_lm_head_argmax")  # fmt: skip
 
     @staticmethod
     def _linear_parts(x: torch.Tensor, wt: torch.Tensor) -> tuple[torch.Tensor, int, int]:
@@ -176,10 +213,12 @@ class GPT2(nn.Module):
     # ---- hot path ------------------------------------------------------------------------
     @torch.no_grad()
     def forward_paged(self, batch: DevicePagedBatch, last_only: bool = True,
-                      ids: torch.Tensor | None = None) -> torch.Tensor:  # fmt: skip
+                      ids: torch.Tensor | None = None, greedy_out: torch.Tensor | None = None) -> torch.Tensor | None:  # fmt: skip
         """Paged forward over the batch's ragged rows.  ``ids`` (int32 ``[N]``
         on the device) defaults to the token ids the batch was planned with.
-        Returns ``[B, 1, V]`` (``last_only``) or ``[B, T, V]``."""
+        Returns ``[B, 1, V]`` (``last_only``) or ``[B, T, V]``.  With
+        ``greedy_out`` (int64 ``[B]``), ``fused_lm_head`` on and at most 64
+        sequences, the greedy tokens go there instead and None is returned."""
         cfg = self.cfg
         if batch.max_ctx > cfg.n_positions:  # tokquay/model.py:159-160
             raise ValueError(f"sequence length {batch.max_ctx} exceeds n_positions={cfg.n_positions}")
@@ -249,6 +288,10 @@ class GPT2(nn.Module):
 
         # embed + per layer (qkv bias + kv write, attention, 2x bias_residual, gelu) + final LN
         self.kernel_launches += 2 + cfg.n_layer * 5
+        if last_only and greedy_out is not None and self.fused_lm_head and B <= _lib.LM_HEAD_MAX_ROWS:
+            sel_ptr = None if rows == B else batch.last_rows.data_ptr()
+            self.lm_head_greedy(x, sel_ptr, b_ptr, B, greedy_out, stream)  # in place of the final LN's count
+            return None
         if last_only:
             xf = torch.empty(B, C, dtype=torch.float32, device=dev)
             sel_ptr = None if rows == B else batch.last_rows.data_ptr()
