@@ -27,6 +27,8 @@ Cases (reference test each one re-hosts, paths inside the Tokquay project):
                 arrivals with aborts, a tight step budget) driven without a model
   mini_engine   the reference Engine on the MINI model, waves of greedy requests
                 on a pool small enough to preempt (tokquay/engine.py)
+  gpt2_engine   the reference Engine on GPT-2 124M with the first 24 requests of the
+                config-5 workload (outputs capped at 24 tokens), 72-block pool
   workload      the reference benchmark's serving workload generator
                 (bench/workload.py:24-47) at three rates / seeds
 """
@@ -142,6 +144,16 @@ ENGINE_CASE = {"cfg": W.MINI, "weights_seed": 21, "init": "gpt2", "block_size": 
                "pool_seed": 103, "pool_scale": 50.0, "free_seed": 7, "trace_seed": 5,
                "sched": {"max_num_seqs": 6, "max_num_batched_tokens": 256, "max_model_len": 128,
                          "watermark_blocks": 1}}  # fmt: skip
+
+
+# The engine on GPT-2 124M with config-5 requests: the first 24 requests of the
+# reference benchmark's workload (burst, seed 7) in three waves, output lengths
+# capped at 24 tokens (CPU time), on a 72-block pool (preemption by recompute).
+GPT2_ENGINE_CASE = {"weights_seed": 0, "init": "normal", "block_size": 16, "num_blocks": 72, "pool_seed": 104,
+                    "free_seed": 9, "workload_seed": 7, "n_requests": 24, "max_tokens_cap": 24,
+                    "waves": [[0, 0, 8], [4, 8, 16], [10, 16, 24]],
+                    "sched": {"max_num_seqs": 64, "max_num_batched_tokens": 2048, "max_model_len": 1024,
+                              "watermark_blocks": 1}}  # fmt: skip
 
 
 def engine_arrivals(rng) -> list[list[tuple[list[int], int]]]:
@@ -518,6 +530,53 @@ def main() -> None:
         case["margins"] = margins
         meta["cases"]["mini_engine"] = case
         print(f"mini_engine {time.time() - t0:.1f}s, {k} steps")
+
+    if want("gpt2_engine"):
+        t0 = time.time()
+        sys.path.insert(0, args.ref)
+        from bench.workload import make_workload  # the reference benchmark's generator
+        from tokquay.engine import Engine
+        from tokquay.scheduler import SchedulerConfig
+        from tokquay.sequence import SamplingParams
+
+        case = dict(GPT2_ENGINE_CASE)
+        m = gpt2_model()
+        a = BlockAllocator(m.cfg, case["num_blocks"], case["block_size"], device="cpu")
+        W.fill_pool_blocks(a.pool, range(case["num_blocks"]), case["pool_seed"])
+        W.shuffle_free_list(a, case["free_seed"])
+        eng = Engine(m, a, SchedulerConfig(**case["sched"]))
+        orig_sample = eng._sample
+        margins: list[list[float]] = []
+
+        def sample_and_record(seqs, logits):
+            top = torch.topk(logits.float(), 2, dim=-1).values
+            margins.append((top[:, 0] - top[:, 1]).tolist())
+            return orig_sample(seqs, logits)
+
+        eng._sample = sample_and_record
+        specs = make_workload(float("inf"), case["n_requests"], case["workload_seed"])
+        waves = {step: specs[lo:hi] for step, lo, hi in case["waves"]}
+        steps, k = [], 0
+        while k <= max(waves) or eng.has_unfinished():
+            for spec in waves.get(k, []):
+                eng.add_request(list(spec.prompt_ids), SamplingParams(max_tokens=min(spec.output_len,
+                                case["max_tokens_cap"]), ignore_eos=True))  # fmt: skip
+            events = eng.step()
+            last = eng.last_step
+            steps.append({
+                "events": [[e.seq_id, e.token_id, e.finish_reason] for e in events],
+                "is_prefill": bool(last.is_prefill) if last else None,
+                "running": [s.seq_id for s in eng.scheduler.running],
+                "tables": [list(s.block_table) for s in eng.scheduler.running],
+                "waiting": [s.seq_id for s in eng.scheduler.waiting],
+                "free": list(a._free),
+                "preemptions": eng.scheduler.num_preemptions,
+            })
+            k += 1
+        case["steps"] = steps
+        case["margins"] = margins
+        meta["cases"]["gpt2_engine"] = case
+        print(f"gpt2_engine {time.time() - t0:.1f}s, {k} steps, {eng.scheduler.num_preemptions} preemptions")
 
     # ---------------------------------------------------------------- serving workload
     if want("workload"):

@@ -33,7 +33,7 @@ from tokquay_b200 import _lib
 from tokquay_b200 import workloads as W
 from tokquay_b200.engine import Engine
 from tokquay_b200.kv_cache import BlockAllocator, DevicePagedBatch
-from tokquay_b200.model import GPT2
+from tokquay_b200.model import GPT2, GPT2Config
 from tokquay_b200.scheduler import SchedulerConfig
 
 sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
@@ -61,15 +61,34 @@ def _mini_model(case, cls=GPT2):
     return m.to("cuda").eval()
 
 
-def _replay_engine_trace(eng, a, case) -> int:
-    """Drive ``eng`` with the trace's arrival waves and compare every step with
-    the reference's; returns how many steps were compared."""
-    arrivals = make_golden.engine_arrivals(random.Random(case["trace_seed"]))
+def _mini_arrivals(case):
+    waves = make_golden.engine_arrivals(random.Random(case["trace_seed"]))
+    return lambda k: [(p, SamplingParams(max_tokens=mt, ignore_eos=True)) for p, mt in (waves[k] if k < len(waves) else [])]
+
+
+def _gpt2_arrivals(case):
+    """The config-5 requests of the gpt2_engine case (this package's workload
+    generator gives the reference benchmark's requests: tests/test_serving.py)."""
+    from tokquay_b200.serving import make_workload
+
+    specs = make_workload(float("inf"), case["n_requests"], case["workload_seed"])
+    waves = {step: specs[lo:hi] for step, lo, hi in case["waves"]}
+    cap = case["max_tokens_cap"]
+    return lambda k: [(list(r.prompt_ids), SamplingParams(max_tokens=min(r.output_len, cap), ignore_eos=True))
+                      for r in waves.get(k, [])]  # fmt: skip
+
+
+def _replay_engine_trace(eng, a, case, arrivals=None) -> int:
+    """Drive ``eng`` with the trace's arrivals and compare every step with the
+    reference's; returns how many steps were compared.  The comparison stops
+    after a step whose greedy choice was a near tie in the reference run; a
+    trace without one is compared to its last step."""
+    arrivals = arrivals or _mini_arrivals(case)
     margins = [min(x) for x in case["margins"]]
     compared = 0
     for k, want in enumerate(case["steps"]):
-        for prompt, max_tokens in arrivals.pop(0) if arrivals else []:
-            eng.add_request(prompt, SamplingParams(max_tokens=max_tokens, ignore_eos=True))
+        for prompt, params in arrivals(k):
+            eng.add_request(prompt, params)
         events = eng.step()
         got = {
             "events": [[e.seq_id, e.token_id, e.finish_reason] for e in events],
@@ -86,9 +105,8 @@ def _replay_engine_trace(eng, a, case) -> int:
             break  # later tokens may legitimately differ
     else:
         assert not eng.has_unfinished() and eng.stats.num_preemptions > 0
-    # The trace has no near tie, so every one of its steps must have been compared.
     first_tie = next((k for k, x in enumerate(margins) if x < NEAR_TIE), len(case["steps"]) - 1)
-    assert compared == min(first_tie + 1, len(case["steps"])) == 82, compared
+    assert compared == min(first_tie + 1, len(case["steps"])), compared
     return compared
 
 
@@ -100,9 +118,30 @@ def test_engine_matches_the_reference_engine(engine_cls, graphs):
     if graphs:
         m.use_cuda_graphs(a)
     eng = engine_cls(m, a, RefSchedulerConfig(**case["sched"]))
-    _replay_engine_trace(eng, a, case)
+    assert _replay_engine_trace(eng, a, case) == 82  # the MINI trace has no near tie: every step compared
     if graphs:
         assert m.graph_runner._graphs  # decode steps replayed captured graphs
+    assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+def test_reference_engine_on_gpt2_with_config5_requests(graphs, gpt2_weights):
+    """The reference's Engine class on GPT-2 124M over this package's model and
+    allocator, with the first 24 requests of config 5's workload on a pool
+    small enough to preempt: every step equal to the reference's CPU run."""
+    case = GOLDEN.cases["gpt2_engine"]
+    m = GPT2(GPT2Config(**W.GPT2_SMALL))
+    W.load_weights(m, gpt2_weights)
+    m = m.to("cuda").eval()
+    a = BlockAllocator(m.cfg, case["num_blocks"], case["block_size"], device="cuda")
+    W.fill_pool_blocks(a.pool, range(case["num_blocks"]), case["pool_seed"])
+    W.shuffle_free_list(a, case["free_seed"])
+    if graphs:
+        m.use_cuda_graphs(a)
+    eng = ref_engine.Engine(m, a, RefSchedulerConfig(**case["sched"]))
+    compared = _replay_engine_trace(eng, a, case, _gpt2_arrivals(case))
+    print(f"gpt2 engine trace: {compared} of {len(case['steps'])} steps compared")
+    assert compared == len(case["steps"]) == 96  # no near tie in this trace: every step compared
     assert _lib.device_status() == 0
 
 
