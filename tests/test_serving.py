@@ -83,3 +83,58 @@ def test_open_loop_driver_and_summary():
     assert out["ttft_ms"]["p50"] == pytest.approx(10.0)  # every request's first token after one step
     assert out["itl_ms"]["p99"] == pytest.approx(10.0)
     assert out["throughput_tok_s"] == pytest.approx(out["output_tokens"] / (max(r.output_len for r in w) * 0.010))
+
+
+def _reference_harness():
+    """The reference benchmark's bench/harness.py (installed beside tokquay).
+    Its package is named ``bench``, as is this repository's bench.py, so it is
+    loaded under that name only for the import."""
+    import importlib.util
+    import sys
+    from pathlib import Path
+
+    import tokquay
+
+    pkg_dir = Path(tokquay.__file__).resolve().parents[1] / "bench"
+    saved = {k: sys.modules.pop(k) for k in [m for m in sys.modules if m == "bench" or m.startswith("bench.")]}
+    try:
+        spec = importlib.util.spec_from_file_location("bench", pkg_dir / "__init__.py",
+                                                      submodule_search_locations=[str(pkg_dir)])  # fmt: skip
+        pkg = importlib.util.module_from_spec(spec)
+        sys.modules["bench"] = pkg
+        spec.loader.exec_module(pkg)
+        import bench.harness as harness  # noqa: PLC0415
+
+        return harness
+    finally:
+        for k in [m for m in sys.modules if m == "bench" or m.startswith("bench.")]:
+            del sys.modules[k]
+        sys.modules.update(saved)
+
+
+def test_summarize_matches_the_reference_harness():
+    """Throughput, TTFT, inter-token latency and end-to-end latency as the
+    reference's bench/harness.py:149-177 computes them, on one synthetic run."""
+    import random
+
+    from tokquay_b200.serving import RequestRecord, StepRecord
+
+    h = _reference_harness()
+    rng = random.Random(3)
+    mine, theirs, t = [], [], 0.0
+    for i in range(40):
+        arrival = rng.uniform(0, 2)
+        times = sorted(arrival + rng.uniform(0.001, 3) for _ in range(rng.randint(0 if i == 7 else 1, 30)))
+        mine.append(RequestRecord(arrival, 10, len(times), list(times)))
+        theirs.append(h.RequestRecord(arrival, 10, len(times), list(times)))
+    steps = [StepRecord(0.1 * k, 0.1 * k + 0.05, k % 5 == 0, 4, 16) for k in range(30)]
+    ref_steps = [h.StepRecord(s.t_start, s.t_end, s.is_prefill, 4, 16, 64, 40, 4) for s in steps]
+    got = summarize(mine, steps)
+    want = h.summarize(h.RunResult(theirs, ref_steps, {}, 5.0), 73728)
+    for key in ("requests", "output_tokens"):
+        assert got[key] == want[key]
+    for key in ("duration_s", "throughput_tok_s"):
+        assert got[key] == pytest.approx(want[key], rel=1e-12)
+    for key in ("ttft_ms", "itl_ms", "latency_ms"):
+        for q in ("p50", "p99", "mean"):
+            assert got[key][q] == pytest.approx(want[key][q], rel=1e-9), (key, q)
