@@ -55,7 +55,7 @@
 extern "C" {
 #endif
 
-#define TQ_ABI_VERSION 6
+#define TQ_ABI_VERSION 7
 
 enum tq_status {
   TQ_OK = 0,
@@ -140,6 +140,19 @@ TQ_API int tq_device_status(int clear, int32_t* bits);
  * still does not fit returns TQ_ERR_CAPACITY.  Without caps the plan is packed
  * to this step.  Returns TQ_ERR_CAPACITY (layout[TQ_PLAN_TOTAL_INTS] = ints
  * needed) if out_capacity is too small. */
+/* Prompt tiles (no reference counterpart: a planning knob of this path).
+ * tq_plan_step sends every sequence that feeds at least min_rows tokens this
+ * step to tensor-core tiles: its rows are cut evenly into tiles of at most 128
+ * rows, and each (tile, head) is one work item run by a whole CTA (QK^T and PV
+ * as tcgen05 MMAs, fp32-accurate by splitting every operand into two TF32
+ * halves).  Tile items run on the last CTAs of the grid; how many is set by
+ * the estimated loads: a tile item costs chunk_cost_pct percent of a warp-path
+ * 32-key chunk per chunk, plus item_cost_pct.  min_rows 0 turns tiles off.
+ * Arguments below 0 (chunk_cost_pct: <= 0) keep the current value.  The
+ * setting is process-wide and read by each tq_plan_step call; defaults 16,
+ * 600, 200.  Returns the previous min_rows. */
+TQ_API int tq_plan_prompt_tiles(int32_t min_rows, int32_t chunk_cost_pct, int32_t item_cost_pct);
+
 TQ_API int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_t* q_len,
                  const int32_t* table_offsets, const int32_t* table_data,
                  const int32_t* token_ids, int32_t block_size, int64_t num_blocks,

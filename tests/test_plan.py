@@ -18,6 +18,9 @@ from tokquay_b200 import _lib
 from tokquay_b200.kv_cache import MIN_SPLIT_CHUNKS, attention_chunk_keys, attention_warps, cdiv, plan_step_host
 
 N_HEAD = 3
+TILE_FLAG = 8  # a prompt-tile item (or, alone in a first item, the marker of a tile CTA's other warps)
+TILE_ROWS = 128
+TILE_MAX_ITEMS = 96
 FIRST_WORDS = 16  # a warp's first item: 8 item words + the block ids of its first chunk
 KMAX_ROWS = 4
 # K (or V) rows one stage holds: the library's chunk size (checked in simulate_copies)
@@ -31,7 +34,7 @@ def decode_item(w) -> dict:
     w = [int(x) for x in w]
     return dict(
         seq=w[0], row0=w[1], nrows=w[2] & 0xFF, head=(w[2] >> 8) & 0xFFFF, flags=(_u32(w[2]) >> 24) & 3,
-        decode=bool((_u32(w[2]) >> 24) & 4), pos0=w[3],
+        decode=bool((_u32(w[2]) >> 24) & 4), tile=bool((_u32(w[2]) >> 24) & TILE_FLAG), pos0=w[3],
         cbeg=w[4] & 0xFFFF, cend=_u32(w[4]) >> 16, lsplit=w[5] & 0xFF, lcount=(w[5] >> 8) & 0xFF,
         lslot=_u32(w[5]) >> 16, gbase=w[6], gsplit=w[7] & 0xFFFF, gnsplit=_u32(w[7]) >> 16,
     )  # fmt: skip
@@ -45,12 +48,21 @@ def attention_lists(plan, layout) -> list[list[dict]]:
     offs = np.asarray(plan[o + FIRST_WORDS * nw:o + FIRST_WORDS * nw + nw + 1])
     ro = o + FIRST_WORDS * nw + (nw + 1 + 7) // 8 * 8
     rest = np.asarray(plan[ro:ro + 8 * int(offs[-1])]).reshape(-1, 8)
+    W = attention_warps()
     lists = []
     for w in range(nw):
         if _u32(first[w][4]) >> 16:
             it = decode_item(first[w][:8])
-            it["first_blocks"] = [int(x) for x in first[w][8:]]
+            if it["tile"]:  # a tile CTA's list: warp 0 only, no block ids
+                assert w % W == 0 and not first[w][8:].any()
+            else:
+                it["first_blocks"] = [int(x) for x in first[w][8:]]
             lists.append([it] + [decode_item(x) for x in rest[offs[w]:offs[w + 1]]])
+            assert all(x["tile"] == it["tile"] for x in lists[-1])
+        elif _u32(first[w][2]) >> 24 == TILE_FLAG:  # marker: this warp runs its CTA's tile items
+            assert w % W != 0 and lists[w - w % W] and lists[w - w % W][0]["tile"]
+            assert not np.delete(first[w], 2).any() and offs[w] == offs[w + 1]
+            lists.append([])
         else:
             assert not first[w].any() and offs[w] == offs[w + 1]
             lists.append([])
@@ -110,18 +122,26 @@ def simulate_copies(p, bs, num_blocks):
             kb = list(range(key0 // bs, (key_end - 1) // bs + 1))
             want = [int(p["tables"][seq][b]) for b in kb][:FIRST_WORDS - 8]
             assert it["first_blocks"] == want + [-1] * (FIRST_WORDS - 8 - len(want))
-        assert 1 <= nrows <= KMAX_ROWS and cbeg < cend
         ctx = int(p["seq"][seq][3])
         need = cdiv(ctx, bs)
         kend = min(pos0 + nrows, cend * ATTN_CHUNK)
         assert kend <= ctx
-        # the kernel holds one item's block ids in two registers per lane
-        assert (kend - 1) // bs - (cbeg * ATTN_CHUNK) // bs + 1 <= 64
+        if it["tile"]:  # whole key range, one block id per key (prompt_tile.cuh's K/V copies)
+            assert 1 <= nrows <= TILE_ROWS and cbeg == 0 and cend == cdiv(pos0 + nrows, ATTN_CHUNK)
+            assert it["flags"] == 0 and not it["decode"]
+        else:
+            assert 1 <= nrows <= KMAX_ROWS and cbeg < cend
+            # the kernel holds one item's block ids in two registers per lane
+            assert (kend - 1) // bs - (cbeg * ATTN_CHUNK) // bs + 1 <= 64
         for c in range(cbeg, cend):
             key0 = c * ATTN_CHUNK
             nkeys = min(ATTN_CHUNK, kend - key0)
             assert nkeys >= 1
-            if bs <= ATTN_CHUNK:
+            if it["tile"]:
+                for key in range(key0, key0 + nkeys):
+                    assert key // bs < need <= p["stride"]
+                    assert 0 <= int(p["tables"][seq][key // bs]) < num_blocks
+            elif bs <= ATTN_CHUNK:
                 kb = key0 // bs
                 while kb * bs < key0 + nkeys:
                     assert kb < need <= p["stride"]
@@ -344,3 +364,74 @@ def test_fixed_capacity_coarsens_the_split_to_fit():
     plan, layout = plan_step_host(16, 256, 12, tables, [1000] * 4, [1] * 4, None, 0, 148, 2, caps=caps)
     assert layout[_lib.PLAN_NUM_ITEMS] <= caps[3] and 0 < layout[_lib.PLAN_NUM_PARTIALS] <= caps[5]
     check_merges(unpack(plan, layout))
+
+
+@pytest.fixture
+def tile_knobs():
+    """Restores the planner's process-wide prompt-tile settings after a test."""
+    prev = _lib.prompt_tiles()
+    yield _lib.prompt_tiles
+    _lib.prompt_tiles(prev, 600, 200)
+
+
+def test_long_prompt_rows_go_to_tile_ctas_at_the_end_of_the_grid(tile_knobs):
+    """Config-3-like mix: 4 prompts of 16..256 rows become (tile, head) items
+    on CTAs of their own, the last of the grid; decodes keep the warp path."""
+    tile_knobs(16, 600, 200)
+    rng = random.Random(11)
+    bs, num_blocks = 16, 2048
+    free = list(range(num_blocks))
+    rng.shuffle(free)
+    tables, start, new = [], [], []
+    for n in (16, 100, 200, 256):
+        tables.append([free.pop() for _ in range(cdiv(n, bs))])
+        start.append(0)
+        new.append(n)
+    for _ in range(60):
+        c = rng.randint(16, 256)
+        tables.append([free.pop() for _ in range(cdiv(c, bs))])
+        start.append(c - 1)
+        new.append(1)
+    plan, layout = plan_step_host(bs, num_blocks, 12, tables, start, new, None, 0, 148, MIN_SPLIT_CHUNKS)
+    p = unpack(plan, layout)
+    W = attention_warps()
+    tile_ctas = [c for c in range(148) if p["warps"][c * W] and p["warps"][c * W][0]["tile"]]
+    assert tile_ctas and tile_ctas == list(range(148 - len(tile_ctas), 148))
+    for c in tile_ctas:
+        assert len(p["warps"][c * W]) <= TILE_MAX_ITEMS
+        assert all(not p["warps"][c * W + w] for w in range(1, W))
+    tiles = [it for it in p["items"] if it["tile"]]
+    # 16 -> 1 tile, 100 -> 1, 200 -> 2 of 100, 256 -> 2 of 128: 6 tiles x 12 heads
+    assert len(tiles) == 6 * 12
+    assert sorted({(it["row0"], it["nrows"]) for it in tiles}) == [
+        (0, 16), (16, 100), (116, 100), (216, 100), (316, 128), (444, 128)]
+    assert all(it["decode"] for it in p["items"] if not it["tile"])
+    seen = simulate_copies(p, bs, num_blocks)
+    for r in range(p["N"]):
+        for h in range(12):
+            assert sorted(seen[(r, h)]) == list(range(int(p["pos"][r]) + 1)), (r, h)
+    check_merges(p)
+
+
+@pytest.mark.parametrize("n_ctas", [1, 2, 5, 148])
+def test_tiles_on_any_grid_and_off(tile_knobs, n_ctas):
+    """Tiles on any grid (a one-CTA grid beside warp work runs everything on
+    the warp path), and with tiles off every row is a warp item."""
+    rng = random.Random(n_ctas)
+    bs, num_blocks = 4, 4096
+    tables, start, new = random_batch(rng, bs, num_blocks, 9, 300, 150)
+    for min_rows in (0, 1, 16):
+        tile_knobs(min_rows, 600, 200)
+        plan, layout = plan_step_host(bs, num_blocks, N_HEAD, tables, start, new, None, 0, n_ctas, 2)
+        p = unpack(plan, layout)
+        n_tile = sum(it["tile"] for it in p["items"])
+        if min_rows == 0:
+            assert n_tile == 0
+        elif n_ctas > 1:
+            assert n_tile > 0
+        seen = simulate_copies(p, bs, num_blocks)
+        for r in range(p["N"]):
+            for h in range(N_HEAD):
+                assert sorted(seen[(r, h)]) == list(range(int(p["pos"][r]) + 1)), (min_rows, r, h)
+        check_merges(p)
+        assert len(p["items"]) == layout[_lib.PLAN_NUM_ITEMS]

@@ -200,6 +200,14 @@ extern "C" {
 
 int tq_abi_version(void) { return TQ_ABI_VERSION; }
 
+#ifdef TQ_TILE_DEBUG
+extern "C" TQ_API int tq_debug_tile_trace(long long* host) {
+  cudaDeviceSynchronize();
+  cudaError_t e = cudaMemcpyFromSymbol(host, tq::g_tile_trace, sizeof(tq::g_tile_trace));
+  return e == cudaSuccess ? TQ_OK : TQ_ERR_CUDA;
+}
+#endif
+
 int tq_attention_chunk_keys(void) { return kChunk; }
 
 int tq_attention_warps(void) { return kAttnWarps; }

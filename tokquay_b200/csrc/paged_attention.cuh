@@ -491,6 +491,12 @@ __device__ __forceinline__ void merge_local(const AttnParams& p, const WorkItem&
   }
 }
 
+}  // namespace tq
+
+#include "prompt_tile.cuh"
+
+namespace tq {
+
 // Block layout: warps 0..kAttnWarps-1 are consumers, warps kAttnWarps.. their
 // producers; consumer w and producer kAttnWarps+w share ring w and walk the
 // same work items (the planner's list for warp slot blockIdx.x*kAttnWarps+w).
@@ -518,6 +524,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
            long long tr_sub[8] = {0, 0, 0, 0, 0, 0, 0, 0};)
 
   pdl_launch_dependents();  // a following dependent launch may stage its own prologue
+  // Every warp slot of a prompt-tile CTA carries the tile flag: the whole CTA
+  // runs its tile items on the tensor cores (prompt_tile.cuh).
+  if (((unsigned)__shfl_sync(kFullMask, first_word, 2) >> 24) & kFlagTile) {
+    prompt_tile_cta(p, smem);
+    return;
+  }
 
   if (!producer && lane == 0) {
     for (int s = 0; s < kStages; ++s) {

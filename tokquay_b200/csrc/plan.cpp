@@ -13,6 +13,7 @@
 // (kv_cache.py:182-191) and adds pool / vocabulary range checks.
 #include <algorithm>
 #include <array>
+#include <atomic>
 #include <climits>
 #include <cstdarg>
 #include <cstdint>
@@ -52,6 +53,19 @@ constexpr int kLocalSlots = 2 * (kWarps - 1) * kMaxRows;
 // ids of its first chunk, so the kernel's first copies need no table lookup.
 constexpr int kFirstWords = 16;   // 8 item words + up to kFirstBlocks block ids
 constexpr int kFirstBlocks = kFirstWords - 8;
+// Prompt tiles: a sequence that feeds many rows this step goes to whole-CTA
+// tiles of up to kTileRows rows x one head, run on the tensor cores
+// (paged_attention.cuh, prompt-tile CTAs) instead of 2-row warp items.
+constexpr int kFlagTile = 8;       // item of a prompt-tile CTA (word 2, bits 24..31)
+constexpr int kTileRows = 128;     // query rows of one tile (the MMA's M)
+constexpr int kTileMaxItems = 96;  // tile items one CTA holds (its shared-memory list)
+
+// Tile planning knobs (tq_plan_prompt_tiles): the least q_len that is tiled
+// (0: never), and a tile item's cost against a warp-path chunk, in percent:
+// chunk_cost per 32-key chunk plus item_cost per item.
+std::atomic<int> g_tile_min_rows{16};
+std::atomic<int> g_tile_chunk_cost{600};
+std::atomic<int> g_tile_item_cost{200};
 
 inline int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t align4(int64_t n) { return (n + 3) & ~int64_t(3); }
@@ -61,12 +75,24 @@ struct Group {  // one query-row group of a sequence
   int32_t seq, row0, nrows, pos0, nc;  // nc: 32-key chunks it attends to
 };
 
+struct Tile {  // a run of one sequence's query rows, run as one MMA tile per head
+  int32_t seq, row0, nrows, pos0, nc;  // nc: 32-key chunks its last row attends to
+};
+
 struct Piece {  // a run of chunks of a group's pairs (one per head), each bound for one CTA
   int32_t group, cbeg, cend, gsplit, gnsplit;
   int64_t gbase;  // split-K partial of (head 0, row 0, split 0), or -1; head h adds h * nrows * gnsplit
 };
 
 }  // namespace
+
+extern "C" int tq_plan_prompt_tiles(int32_t min_rows, int32_t chunk_cost_pct, int32_t item_cost_pct) {
+  const int prev = g_tile_min_rows.load();
+  if (min_rows >= 0) g_tile_min_rows.store(min_rows);
+  if (chunk_cost_pct > 0) g_tile_chunk_cost.store(chunk_cost_pct);
+  if (item_cost_pct >= 0) g_tile_item_cost.store(item_cost_pct);
+  return prev;
+}
 
 extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_t* q_len,
                             const int32_t* table_offsets, const int32_t* table_data,
@@ -94,6 +120,11 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
 
   // ---- pass 1: validate, size everything -----------------------------------
   int64_t N = 0, max_nb = 0, max_ctx = 0, n_groups = 0, total_chunks = 0;
+  const int tile_min = g_tile_min_rows.load(std::memory_order_relaxed);
+  const int64_t tile_chunk_cost = g_tile_chunk_cost.load(std::memory_order_relaxed);
+  const int64_t tile_item_cost = g_tile_item_cost.load(std::memory_order_relaxed);
+  std::vector<Tile> tiles;
+  std::vector<char> tiled((size_t)num_seqs, 0);
   for (int b = 0; b < num_seqs; ++b) {
     if (q_len[b] < 1) return set_error(TQ_ERR_INVALID, "every sequence must feed at least one token");
     if (start[b] < 0) return set_error(TQ_ERR_INVALID, "sequence %d: negative start %d", b, start[b]);
@@ -112,6 +143,17 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     N += q_len[b];
     max_nb = std::max(max_nb, need);
     max_ctx = std::max(max_ctx, ctx);
+    if (tile_min > 0 && q_len[b] >= tile_min) {
+      tiled[b] = 1;
+      // Rows cut evenly into the fewest tiles of at most kTileRows.
+      const int64_t nt = cdiv64(q_len[b], kTileRows), per = cdiv64(q_len[b], nt);
+      for (int64_t t0 = 0; t0 < q_len[b]; t0 += per) {
+        const int64_t nrows = std::min<int64_t>(per, q_len[b] - t0);
+        tiles.push_back({b, (int32_t)(N - q_len[b] + t0), (int32_t)nrows, (int32_t)(start[b] + t0),
+                         (int32_t)cdiv64(start[b] + t0 + nrows, kChunk)});
+      }
+      continue;
+    }
     for (int64_t g0 = 0; g0 < q_len[b]; g0 += kMaxRows) {
       const int64_t nrows = std::min<int64_t>(kMaxRows, q_len[b] - g0);
       total_chunks += cdiv64(start[b] + g0 + nrows, kChunk);
@@ -130,12 +172,78 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     return set_error(TQ_ERR_UNSUPPORTED, "a context of %lld tokens exceeds %d chunks of %d keys",
                      (long long)max_ctx, kMaxChunkIndex, kChunk);
 
+  // ---- prompt tiles -> tile CTAs ---------------------------------------------
+  // Tile items (one per tile and head) run on CTAs of their own, the last
+  // n_tctas of the grid; the warp path below gets the first n_wctas.  The
+  // split follows the estimated loads -- a warp-path CTA's load is its chunks
+  // (x 100); a tile item costs tile_chunk_cost per chunk plus tile_item_cost
+  // -- and the tile items go longest first to the least loaded tile CTA.  A
+  // step whose tiles do not fit (a one-CTA grid beside warp work, or more
+  // than kTileMaxItems on a CTA) runs every row on the warp path.
+  int32_t n_tctas = 0;
+  std::vector<std::vector<int32_t>> tile_lists;  // per tile CTA: items (tile * n_head + head)
+  if (!tiles.empty()) {
+    const int64_t n_titems = (int64_t)tiles.size() * n_head;
+    std::vector<int64_t> cost(tiles.size());
+    int64_t tile_load = 0;
+    for (size_t i = 0; i < tiles.size(); ++i) {
+      cost[i] = tiles[i].nc * tile_chunk_cost + tile_item_cost;
+      tile_load += cost[i] * n_head;
+    }
+    const int64_t warp_load = total_chunks * n_head * 100;
+    const int64_t max_tctas = n_groups == 0 ? n_ctas : n_ctas - 1;
+    int64_t nt = std::min<int64_t>(max_tctas, n_titems);
+    if (n_groups > 0)
+      nt = std::min<int64_t>(nt, std::max<int64_t>(1, (int64_t)((double)n_ctas * tile_load /
+                                                                  (double)(tile_load + warp_load) + 0.5)));
+    nt = std::max(nt, cdiv64(n_titems, kTileMaxItems));
+    bool fits = nt >= 1 && nt <= max_tctas;
+    if (fits) {
+      std::vector<int32_t> ord(tiles.size());
+      for (size_t i = 0; i < ord.size(); ++i) ord[i] = (int32_t)i;
+      std::stable_sort(ord.begin(), ord.end(), [&](int32_t a, int32_t b) { return cost[a] > cost[b]; });
+      std::vector<int64_t> load((size_t)nt, 0);
+      tile_lists.assign((size_t)nt, {});
+      for (int32_t i : ord)
+        for (int h = 0; h < n_head && fits; ++h) {
+          size_t c = 0;
+          for (size_t j = 1; j < load.size(); ++j)
+            if (load[j] < load[c]) c = j;
+          tile_lists[c].push_back(i * n_head + h);
+          load[c] += cost[i];
+          fits = tile_lists[c].size() <= (size_t)kTileMaxItems;
+        }
+    }
+    if (fits) {
+      n_tctas = (int32_t)nt;
+    } else {  // back to the warp path
+      tile_lists.clear();
+      tiles.clear();
+      for (int b = 0; b < num_seqs; ++b) {
+        if (!tiled[b]) continue;
+        tiled[b] = 0;
+        for (int64_t g0 = 0; g0 < q_len[b]; g0 += kMaxRows) {
+          const int64_t nrows = std::min<int64_t>(kMaxRows, q_len[b] - g0);
+          total_chunks += cdiv64(start[b] + g0 + nrows, kChunk);
+          ++n_groups;
+        }
+      }
+    }
+  }
+  const int32_t n_wctas = n_ctas - n_tctas;  // CTAs of the warp path: 0 .. n_wctas-1
+  int64_t n_tile_items = 0;
+  for (const auto& l : tile_lists) n_tile_items += (int64_t)l.size();
+
   // ---- attention work: (group, head) pairs -> pieces -> CTAs -> warps ----------
   std::vector<Group> groups;
   groups.reserve((size_t)n_groups);
   {
     int64_t row = 0;
     for (int b = 0; b < num_seqs; ++b) {
+      if (tiled[b]) {
+        row += q_len[b];
+        continue;
+      }
       for (int64_t g0 = 0; g0 < q_len[b]; g0 += kMaxRows) {
         const int64_t nrows = std::min<int64_t>(kMaxRows, q_len[b] - g0);
         groups.push_back({b, (int32_t)(row + g0), (int32_t)nrows, (int32_t)(start[b] + g0),
@@ -151,7 +259,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   const int64_t n_warps = (int64_t)n_ctas * kWarps;
   // A CTA's fair share of chunks: a pair longer than that (and than twice
   // the smallest cross-CTA piece) is split across CTAs.
-  const int64_t share = std::max<int64_t>(1, cdiv64(total_chunks * n_head, n_ctas));
+  const int64_t share = std::max<int64_t>(1, cdiv64(total_chunks * n_head, std::max<int32_t>(n_wctas, 1)));
   int64_t split_min = min_split_chunks;
 
   // Pieces: a group's keys, cut across CTAs when longer than a CTA's share.
@@ -178,8 +286,8 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
       }
     }
     n_pairs = (int64_t)pieces.size() * n_head;
-    // Each warp boundary cuts at most one pair in two.
-    max_items = n_pairs + (int64_t)n_ctas * (kWarps - 1);
+    // Each warp boundary cuts at most one pair in two; tile items are one each.
+    max_items = n_pairs + (int64_t)n_wctas * (kWarps - 1) + n_tile_items;
   };
   make_pieces();
   // With fixed capacities, coarsen the cross-CTA split until items and partials fit.
@@ -209,12 +317,12 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     for (size_t i = 0; i < pieces.size(); ++i)
       order[start_of[(size_t)(longest_piece - (pieces[i].cend - pieces[i].cbeg))]++] = (int32_t)i;
   }
-  std::vector<int64_t> cta_load((size_t)n_ctas, 0);
-  std::vector<int32_t> cta_count((size_t)n_ctas + 1, 0), cta_of((size_t)n_pairs);
-  {
-    const int64_t max_load = sum_len / n_ctas + longest_piece + 1;
-    std::vector<int32_t> head((size_t)max_load + 1, -1), next((size_t)n_ctas, -1);
-    for (int32_t c = n_ctas - 1; c >= 0; --c) {  // bucket 0 lists CTA 0 first
+  std::vector<int64_t> cta_load((size_t)n_wctas, 0);
+  std::vector<int32_t> cta_count((size_t)n_wctas + 1, 0), cta_of((size_t)n_pairs);
+  if (n_pairs > 0) {
+    const int64_t max_load = sum_len / n_wctas + longest_piece + 1;
+    std::vector<int32_t> head((size_t)max_load + 1, -1), next((size_t)n_wctas, -1);
+    for (int32_t c = n_wctas - 1; c >= 0; --c) {  // bucket 0 lists CTA 0 first
       next[c] = head[0];
       head[0] = c;
     }
@@ -236,7 +344,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
       }
     }
   }
-  for (int32_t c = 0; c < n_ctas; ++c) cta_count[c + 1] += cta_count[c];
+  for (int32_t c = 0; c < n_wctas; ++c) cta_count[c + 1] += cta_count[c];
   std::vector<int32_t> by_cta((size_t)n_pairs);  // pairs grouped by CTA, in assignment order
   {
     std::vector<int32_t> fill(cta_count.begin(), cta_count.end() - 1);
@@ -305,7 +413,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   int32_t* const first_items = out + o_items;
   int32_t* const ranges = out + o_ranges;
   int32_t* const rest_items = out + o_rest;
-  for (int32_t c = 0; c < n_ctas; ++c) {
+  for (int32_t c = 0; c < n_wctas; ++c) {
     const int64_t L = cta_load[c];
     int64_t bnd[kWarps + 1];
     for (int w = 0; w <= kWarps; ++w) bnd[w] = (int64_t)w * L / kWarps;
@@ -367,6 +475,36 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     while (cur < kWarps - 1) ranges[wbase + (++cur)] = (int32_t)rest;
     for (int w = 0; w < kWarps; ++w)  // a warp without work: an all-zero first item
       if (!has[w]) std::memset(first_items + kFirstWords * (wbase + w), 0, kFirstWords * sizeof(int32_t));
+  }
+  // Tile CTAs: warp 0 holds the CTA's tile items (the first at its fixed
+  // place, the others in its list); warps 1.. hold a marker (the tile flag
+  // alone) that sends them to the CTA's tile code too.
+  for (int32_t t = 0; t < n_tctas; ++t) {
+    const int64_t wbase = (int64_t)(n_wctas + t) * kWarps;
+    const std::vector<int32_t>& list = tile_lists[(size_t)t];
+    ranges[wbase] = (int32_t)rest;
+    for (size_t k = 0; k < list.size(); ++k) {
+      const Tile& tl = tiles[(size_t)(list[k] / n_head)];
+      const int head = list[k] % n_head;
+      int32_t* const it = k == 0 ? first_items + kFirstWords * wbase : rest_items + 8 * rest++;
+      if (k == 0) std::memset(it, 0, kFirstWords * sizeof(int32_t));
+      it[0] = tl.seq;
+      it[1] = tl.row0;
+      it[2] = tl.nrows | (head << 8) | (kFlagTile << 24);
+      it[3] = tl.pos0;
+      it[4] = 0 | (tl.nc << 16);
+      it[5] = 0;
+      it[6] = -1;
+      it[7] = 0;
+      ++n_items;
+      longest = std::max<int64_t>(longest, tl.nc);
+    }
+    for (int w = 1; w < kWarps; ++w) {
+      ranges[wbase + w] = (int32_t)rest;
+      int32_t* const it = first_items + kFirstWords * (wbase + w);
+      std::memset(it, 0, kFirstWords * sizeof(int32_t));
+      it[2] = kFlagTile << 24;
+    }
   }
   ranges[n_warps] = (int32_t)rest;
   std::memset(ranges + n_warps + 1, 0, sizeof(int32_t) * (align8(n_warps + 1) - (n_warps + 1)));
