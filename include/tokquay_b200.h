@@ -150,7 +150,7 @@ TQ_API int tq_device_status(int clear, int32_t* bits);
  * 32-key chunk per chunk, plus item_cost_pct.  min_rows 0 turns tiles off.
  * Arguments below 0 (chunk_cost_pct: <= 0) keep the current value.  The
  * setting is process-wide and read by each tq_plan_step call; defaults 16,
- * 600, 200.  Returns the previous min_rows. */
+ * 1500, 200.  Returns the previous min_rows. */
 TQ_API int tq_plan_prompt_tiles(int32_t min_rows, int32_t chunk_cost_pct, int32_t item_cost_pct);
 
 TQ_API int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_t* q_len,

@@ -400,3 +400,80 @@ def test_argmax_rows_matches_torch(V):
     n = torch.tensor([13], dtype=torch.int32, device="cuda")
     argmax_rows(wide[:, :V], out=out, d_num_rows=n.data_ptr(), max_rows=20)
     assert torch.equal(out[:13], wide[:13, :V].argmax(-1)) and (out[13:] == -1).all()
+
+
+def _item_flags(batch) -> list[int]:
+    """Flag byte of every work item of the batch's plan (first items included)."""
+    L = batch.layout
+    plan = batch.plan.cpu().numpy()
+    nw = batch.n_ctas * attention_warps()
+    o = int(L[_lib.PLAN_OFF_ITEMS])
+    first = plan[o:o + 16 * nw].reshape(nw, 16)[:, :8]
+    offs = plan[o + 16 * nw:o + 17 * nw + 1]
+    ro = o + 16 * nw + (nw + 8) // 8 * 8
+    rest = plan[ro:ro + 8 * int(offs[-1])].reshape(-1, 8)
+    words = [w[2] for w in first if w[4] != 0] + [w[2] for w in rest]
+    return [(int(np.uint32(x)) >> 24) for x in words]
+
+
+@pytest.fixture
+def tile_knobs():
+    prev = _lib.prompt_tiles()
+    yield _lib.prompt_tiles
+    _lib.prompt_tiles(prev, 1500, 200)
+
+
+@pytest.mark.parametrize("bs", [4, 16, 64])
+@pytest.mark.parametrize("shape", ["prefill_split", "beside_decode", "tiles_off"])
+def test_prompt_tiles_match_float64_reference(bs, shape, tile_knobs):
+    """Long prompt chunks (cached prefixes of 0-600 keys, 100-256 rows) on the
+    tensor-core tiles: prompt rows alone (long tiles cut into pieces merged
+    through the split-K scratch), the same beside a decode row (whole tiles),
+    and with tiles off (2-row warp items) -- every row against float64, with
+    NaN in every slot past each context."""
+    tile_knobs(0 if shape == "tiles_off" else 16, 1500, 200)
+    rng = random.Random(bs)
+    cfg = GPT2Config(vocab_size=64, n_positions=1024, n_embd=768, n_layer=1, n_head=12)
+    alloc = BlockAllocator(cfg, 4 * cdiv(1024, bs) + 8, bs, device="cuda")
+    random.Random(2).shuffle(alloc._free)
+    g = torch.Generator(device="cuda").manual_seed(bs)
+    alloc.pool.normal_(generator=g)
+    tables, start, new = [], [], []
+    for s, n in ((0, 256), (rng.randint(100, 600), rng.randint(100, 200)), (rng.randint(0, 300), 128)):
+        tables.append(alloc._take(cdiv(s + n, bs)))
+        start.append(s)
+        new.append(n)
+    if shape == "beside_decode":
+        c = rng.randint(100, 700)
+        tables.append(alloc._take(cdiv(c, bs)))
+        start.append(c - 1)
+        new.append(1)
+    for tbl, s, n in zip(tables, start, new):
+        ctx = s + n
+        for j, blk in enumerate(tbl):
+            lo = max(0, ctx - j * bs)
+            if lo < bs:
+                alloc.pool[blk, :, :, :, lo:] = float("nan")
+    if alloc._free:
+        alloc.pool[torch.tensor(alloc._free, device="cuda")] = float("nan")
+    batch = DevicePagedBatch(alloc, tables, start, new)
+    flags = _item_flags(batch)
+    n_tile = sum(f & 8 != 0 for f in flags)
+    n_split = sum(f & 8 != 0 and f & 2 != 0 for f in flags)
+    if shape == "tiles_off":
+        assert n_tile == 0
+    elif shape == "beside_decode":
+        assert n_tile > 0 and n_split == 0
+    else:
+        assert n_split > 0
+    C = cfg.n_embd
+    qkv = torch.randn(batch.N, 3 * C, device="cuda", generator=g)
+    out = torch.full((batch.N, C), float("nan"), device="cuda")
+    for _ in range(2):  # twice: the split-K counters are left at zero for the next launch
+        batch.attend_rows(0, qkv, out, _stream())
+        torch.cuda.synchronize()
+        want = _reference_attention(alloc.pool, 0, qkv[:, :C], tables, start, new, bs)
+        assert torch.isfinite(out).all()
+        err = (out.double() - want).abs().max().item()
+        assert err <= ATTN_RTOL * want.abs().max().item(), (shape, err)
+    assert _lib.device_status() == 0

@@ -53,10 +53,9 @@ def attention_lists(plan, layout) -> list[list[dict]]:
     for w in range(nw):
         if _u32(first[w][4]) >> 16:
             it = decode_item(first[w][:8])
-            if it["tile"]:  # a tile CTA's list: warp 0 only, no block ids
-                assert w % W == 0 and not first[w][8:].any()
-            else:
-                it["first_blocks"] = [int(x) for x in first[w][8:]]
+            if it["tile"]:  # a tile CTA's list: warp 0 only
+                assert w % W == 0
+            it["first_blocks"] = [int(x) for x in first[w][8:]]
             lists.append([it] + [decode_item(x) for x in rest[offs[w]:offs[w + 1]]])
             assert all(x["tile"] == it["tile"] for x in lists[-1])
         elif _u32(first[w][2]) >> 24 == TILE_FLAG:  # marker: this warp runs its CTA's tile items
@@ -126,9 +125,10 @@ def simulate_copies(p, bs, num_blocks):
         need = cdiv(ctx, bs)
         kend = min(pos0 + nrows, cend * ATTN_CHUNK)
         assert kend <= ctx
-        if it["tile"]:  # whole key range, one block id per key (prompt_tile.cuh's K/V copies)
-            assert 1 <= nrows <= TILE_ROWS and cbeg == 0 and cend == cdiv(pos0 + nrows, ATTN_CHUNK)
-            assert it["flags"] == 0 and not it["decode"]
+        if it["tile"]:  # a run of the tile's chunks (all of them, or a piece merged across CTAs)
+            assert 1 <= nrows <= TILE_ROWS and cbeg < cend <= cdiv(pos0 + nrows, ATTN_CHUNK)
+            assert it["flags"] in (0, 2) and not it["decode"]
+            assert it["flags"] == 2 or (cbeg == 0 and cend == cdiv(pos0 + nrows, ATTN_CHUNK))
         else:
             assert 1 <= nrows <= KMAX_ROWS and cbeg < cend
             # the kernel holds one item's block ids in two registers per lane
@@ -371,7 +371,7 @@ def tile_knobs():
     """Restores the planner's process-wide prompt-tile settings after a test."""
     prev = _lib.prompt_tiles()
     yield _lib.prompt_tiles
-    _lib.prompt_tiles(prev, 600, 200)
+    _lib.prompt_tiles(prev, 1500, 200)
 
 
 def test_long_prompt_rows_go_to_tile_ctas_at_the_end_of_the_grid(tile_knobs):
@@ -401,8 +401,9 @@ def test_long_prompt_rows_go_to_tile_ctas_at_the_end_of_the_grid(tile_knobs):
         assert len(p["warps"][c * W]) <= TILE_MAX_ITEMS
         assert all(not p["warps"][c * W + w] for w in range(1, W))
     tiles = [it for it in p["items"] if it["tile"]]
-    # 16 -> 1 tile, 100 -> 1, 200 -> 2 of 100, 256 -> 2 of 128: 6 tiles x 12 heads
-    assert len(tiles) == 6 * 12
+    # 16 -> 1 tile, 100 -> 1, 200 -> 2 of 100, 256 -> 2 of 128: 6 tiles x 12 heads,
+    # the longest cut into pieces no costlier than a CTA's balanced load
+    assert len(tiles) == 6 * 12 and all(it["flags"] == 0 for it in tiles)  # beside decodes: not split
     assert sorted({(it["row0"], it["nrows"]) for it in tiles}) == [
         (0, 16), (16, 100), (116, 100), (216, 100), (316, 128), (444, 128)]
     assert all(it["decode"] for it in p["items"] if not it["tile"])
@@ -435,3 +436,22 @@ def test_tiles_on_any_grid_and_off(tile_knobs, n_ctas):
                 assert sorted(seen[(r, h)]) == list(range(int(p["pos"][r]) + 1)), (min_rows, r, h)
         check_merges(p)
         assert len(p["items"]) == layout[_lib.PLAN_NUM_ITEMS]
+
+
+def test_prefill_only_steps_split_long_tiles_over_the_grid(tile_knobs):
+    """A step of prompt rows alone spreads long tiles over the grid: tiles are
+    cut over their keys into pieces of at least two chunks, every piece of a
+    (tile, head) merged through the split-K scratch."""
+    tile_knobs(16, 600, 200)
+    tables = [list(range(64))]
+    plan, layout = plan_step_host(16, 64, 12, tables, [0], [1024], None, 0, 148, MIN_SPLIT_CHUNKS)
+    p = unpack(plan, layout)
+    tiles = [it for it in p["items"] if it["tile"]]
+    assert len(tiles) > 8 * 12 and any(it["flags"] == 2 for it in tiles)
+    assert all(it["cend"] - it["cbeg"] >= 2 for it in tiles)
+    assert layout[_lib.PLAN_NUM_PARTIALS] > 0 and len(p["combine"]) > 0
+    seen = simulate_copies(p, 16, 64)
+    for r in range(p["N"]):
+        for h in range(12):
+            assert sorted(seen[(r, h)]) == list(range(int(p["pos"][r]) + 1)), (r, h)
+    check_merges(p)

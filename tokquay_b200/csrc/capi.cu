@@ -201,6 +201,13 @@ extern "C" {
 int tq_abi_version(void) { return TQ_ABI_VERSION; }
 
 #ifdef TQ_TILE_DEBUG
+extern "C" TQ_API int tq_debug_cta_times(unsigned long long* host) {
+  cudaDeviceSynchronize();
+  cudaError_t e = cudaMemcpyFromSymbol(host, tq::g_cta_time, sizeof(tq::g_cta_time));
+  unsigned long long zero[3 * 1024] = {};
+  cudaMemcpyToSymbol(tq::g_cta_time, zero, sizeof(zero));
+  return e == cudaSuccess ? TQ_OK : TQ_ERR_CUDA;
+}
 extern "C" TQ_API int tq_debug_tile_trace(long long* host) {
   cudaDeviceSynchronize();
   cudaError_t e = cudaMemcpyFromSymbol(host, tq::g_tile_trace, sizeof(tq::g_tile_trace));

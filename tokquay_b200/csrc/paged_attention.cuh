@@ -526,8 +526,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
   pdl_launch_dependents();  // a following dependent launch may stage its own prologue
   // Every warp slot of a prompt-tile CTA carries the tile flag: the whole CTA
   // runs its tile items on the tensor cores (prompt_tile.cuh).
-  if (((unsigned)__shfl_sync(kFullMask, first_word, 2) >> 24) & kFlagTile) {
-    prompt_tile_cta(p, smem);
+  const bool tile_cta = ((unsigned)__shfl_sync(kFullMask, first_word, 2) >> 24) & kFlagTile;
+#ifdef TQ_TILE_DEBUG
+  if (threadIdx.x == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    g_cta_time[3 * blockIdx.x] = t;
+    g_cta_time[3 * blockIdx.x + 2] = tile_cta ? 1 : 0;
+  }
+#define TQ_CTA_END()                                               \
+  do {                                                             \
+    unsigned long long t_;                                         \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));         \
+    if ((threadIdx.x & 31) == 0) atomicMax(&g_cta_time[3 * blockIdx.x + 1], t_); \
+  } while (0)
+#else
+#define TQ_CTA_END() do { } while (0)
+#endif
+  if (tile_cta) {
+    // The tile code reads the parameters from shared memory: passed by
+    // reference, the kernel's would be copied to (slow, under load) local memory.
+    AttnParams* const sp = reinterpret_cast<AttnParams*>(smem + kTileOffParams);
+    if (threadIdx.x == 0) *sp = p;
+    __syncthreads();
+    prompt_tile_cta(*sp, smem);
+    TQ_CTA_END();
     return;
   }
 
@@ -828,6 +851,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
     trec[5] = tr_fin; trec[7] = tr_chunks;
     for (int k = 3; k < 7; ++k) trec[8 + k] = tr_sub[k];
   })
+  TQ_CTA_END();
 }
 
 }  // namespace tq

@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <array>
 #include <atomic>
+#include <cmath>
 #include <climits>
 #include <cstdarg>
 #include <cstdint>
@@ -64,7 +65,7 @@ constexpr int kTileMaxItems = 96;  // tile items one CTA holds (its shared-memor
 // (0: never), and a tile item's cost against a warp-path chunk, in percent:
 // chunk_cost per 32-key chunk plus item_cost per item.
 std::atomic<int> g_tile_min_rows{16};
-std::atomic<int> g_tile_chunk_cost{600};
+std::atomic<int> g_tile_chunk_cost{1500};
 std::atomic<int> g_tile_item_cost{200};
 
 inline int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -77,6 +78,11 @@ struct Group {  // one query-row group of a sequence
 
 struct Tile {  // a run of one sequence's query rows, run as one MMA tile per head
   int32_t seq, row0, nrows, pos0, nc;  // nc: 32-key chunks its last row attends to
+};
+
+struct TilePiece {  // a run of a tile's chunks, bound for one CTA (per head)
+  int32_t tile, cbeg, cend, gsplit, gnsplit;
+  int64_t gbase;  // split-K partial of (head 0, row 0, split 0), or -1; head h adds h * nrows * gnsplit
 };
 
 struct Piece {  // a run of chunks of a group's pairs (one per head), each bound for one CTA
@@ -173,24 +179,49 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
                      (long long)max_ctx, kMaxChunkIndex, kChunk);
 
   // ---- prompt tiles -> tile CTAs ---------------------------------------------
-  // Tile items (one per tile and head) run on CTAs of their own, the last
-  // n_tctas of the grid; the warp path below gets the first n_wctas.  The
-  // split follows the estimated loads -- a warp-path CTA's load is its chunks
-  // (x 100); a tile item costs tile_chunk_cost per chunk plus tile_item_cost
-  // -- and the tile items go longest first to the least loaded tile CTA.  A
-  // step whose tiles do not fit (a one-CTA grid beside warp work, or more
-  // than kTileMaxItems on a CTA) runs every row on the warp path.
+  // Tile items (one per tile piece and head) run on CTAs of their own, the
+  // last n_tctas of the grid; the warp path below gets the first n_wctas.
+  // The split follows the estimated loads -- a warp-path CTA's load is its
+  // chunks (x 100); a tile item costs tile_chunk_cost per chunk plus
+  // tile_item_cost.  In a step of prompt rows alone, a tile whose item would
+  // cost more than the balanced load of a CTA is cut over its keys into pieces
+  // of at least two chunks, merged through the split-K scratch by the last
+  // piece to finish (not in plans of fixed capacity: the merge's fences and
+  // counter cost more than they save beside decode work, measured on B200).
+  // The items go longest first to the least loaded tile
+  // CTA.  A step whose tiles do not fit (a one-CTA grid beside warp work, or
+  // more than kTileMaxItems on a CTA) runs every row on the warp path.
   int32_t n_tctas = 0;
-  std::vector<std::vector<int32_t>> tile_lists;  // per tile CTA: items (tile * n_head + head)
+  std::vector<TilePiece> tpieces;
+  std::vector<std::vector<int32_t>> tile_lists;  // per tile CTA: items (piece * n_head + head)
+  int64_t tile_partials = 0, tile_combine = 0;
   if (!tiles.empty()) {
-    const int64_t n_titems = (int64_t)tiles.size() * n_head;
-    std::vector<int64_t> cost(tiles.size());
     int64_t tile_load = 0;
+    for (const Tile& t : tiles) tile_load += (t.nc * tile_chunk_cost + tile_item_cost) * n_head;
+    const int64_t warp_load = total_chunks * n_head * 100;
+    const double balanced = (double)(tile_load + warp_load) / n_ctas;
     for (size_t i = 0; i < tiles.size(); ++i) {
-      cost[i] = tiles[i].nc * tile_chunk_cost + tile_item_cost;
+      const Tile& t = tiles[i];
+      int64_t gn = 1;
+      if (!caps && n_groups == 0) {
+        gn = (int64_t)std::ceil((double)(t.nc * tile_chunk_cost + tile_item_cost) / std::max(balanced, 1.0));
+        gn = std::max<int64_t>(1, std::min<int64_t>(gn, t.nc / 2));
+      }
+      for (int64_t sp = 0; sp < gn; ++sp)
+        tpieces.push_back({(int32_t)i, (int32_t)(sp * t.nc / gn), (int32_t)((sp + 1) * t.nc / gn), (int32_t)sp,
+                           (int32_t)gn, gn > 1 ? tile_partials : -1});
+      if (gn > 1) {
+        tile_partials += (int64_t)n_head * t.nrows * gn;
+        tile_combine += t.nrows;
+      }
+    }
+    std::vector<int64_t> cost(tpieces.size());
+    tile_load = 0;
+    for (size_t i = 0; i < tpieces.size(); ++i) {
+      cost[i] = (tpieces[i].cend - tpieces[i].cbeg) * tile_chunk_cost + tile_item_cost;
       tile_load += cost[i] * n_head;
     }
-    const int64_t warp_load = total_chunks * n_head * 100;
+    const int64_t n_titems = (int64_t)tpieces.size() * n_head;
     const int64_t max_tctas = n_groups == 0 ? n_ctas : n_ctas - 1;
     int64_t nt = std::min<int64_t>(max_tctas, n_titems);
     if (n_groups > 0)
@@ -199,7 +230,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     nt = std::max(nt, cdiv64(n_titems, kTileMaxItems));
     bool fits = nt >= 1 && nt <= max_tctas;
     if (fits) {
-      std::vector<int32_t> ord(tiles.size());
+      std::vector<int32_t> ord(tpieces.size());
       for (size_t i = 0; i < ord.size(); ++i) ord[i] = (int32_t)i;
       std::stable_sort(ord.begin(), ord.end(), [&](int32_t a, int32_t b) { return cost[a] > cost[b]; });
       std::vector<int64_t> load((size_t)nt, 0);
@@ -219,6 +250,8 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     } else {  // back to the warp path
       tile_lists.clear();
       tiles.clear();
+      tpieces.clear();
+      tile_partials = tile_combine = 0;
       for (int b = 0; b < num_seqs; ++b) {
         if (!tiled[b]) continue;
         tiled[b] = 0;
@@ -295,6 +328,11 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     split_min *= 2;
     make_pieces();
   }
+  // Split tiles' partials follow the warp path's.
+  for (TilePiece& tp : tpieces)
+    if (tp.gbase >= 0) tp.gbase += n_partials;
+  n_partials += tile_partials;
+  n_combine += tile_combine;
   if (n_partials > INT32_MAX || max_items > INT32_MAX / 8)
     return set_error(TQ_ERR_UNSUPPORTED, "step too large to plan");
 
@@ -484,20 +522,27 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     const std::vector<int32_t>& list = tile_lists[(size_t)t];
     ranges[wbase] = (int32_t)rest;
     for (size_t k = 0; k < list.size(); ++k) {
-      const Tile& tl = tiles[(size_t)(list[k] / n_head)];
+      const TilePiece& tp = tpieces[(size_t)(list[k] / n_head)];
+      const Tile& tl = tiles[(size_t)tp.tile];
       const int head = list[k] % n_head;
       int32_t* const it = k == 0 ? first_items + kFirstWords * wbase : rest_items + 8 * rest++;
-      if (k == 0) std::memset(it, 0, kFirstWords * sizeof(int32_t));
+      if (k == 0) {  // the block ids of the first chunk ride along (-1 past them), as for warp items
+        const int64_t key0 = (int64_t)tp.cbeg * kChunk;
+        const int64_t key_end = std::min<int64_t>(key0 + kChunk, (int64_t)tl.pos0 + tl.nrows);
+        const int64_t kb0 = key0 / block_size, kb_end = (key_end - 1) / block_size + 1;
+        const int32_t* tbl = table_data + table_offsets[tl.seq];
+        for (int j = 0; j < kFirstBlocks; ++j) it[8 + j] = kb0 + j < kb_end ? tbl[kb0 + j] : -1;
+      }
       it[0] = tl.seq;
       it[1] = tl.row0;
-      it[2] = tl.nrows | (head << 8) | (kFlagTile << 24);
+      it[2] = tl.nrows | (head << 8) | ((kFlagTile | (tp.gnsplit > 1 ? kFlagGlobal : 0)) << 24);
       it[3] = tl.pos0;
-      it[4] = 0 | (tl.nc << 16);
+      it[4] = tp.cbeg | (tp.cend << 16);
       it[5] = 0;
-      it[6] = -1;
-      it[7] = 0;
+      it[6] = tp.gnsplit > 1 ? (int32_t)(tp.gbase + (int64_t)head * tl.nrows * tp.gnsplit) : -1;
+      it[7] = tp.gsplit | (tp.gnsplit << 16);
       ++n_items;
-      longest = std::max<int64_t>(longest, tl.nc);
+      longest = std::max<int64_t>(longest, tp.cend - tp.cbeg);
     }
     for (int w = 1; w < kWarps; ++w) {
       ranges[wbase + w] = (int32_t)rest;
@@ -555,6 +600,17 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
     }
     out[o_last + b] = (int32_t)(row + n - 1);
     row += n;
+  }
+  for (const TilePiece& tp : tpieces) {  // split tiles' rows, likewise
+    if (tp.gsplit != 0 || tp.gnsplit < 2) continue;
+    const Tile& tl = tiles[(size_t)tp.tile];
+    for (int r = 0; r < tl.nrows; ++r) {
+      int32_t* e = out + o_comb + 4 * comb++;
+      e[0] = tl.row0 + r;
+      e[1] = (int32_t)(tp.gbase + (int64_t)r * tp.gnsplit);
+      e[2] = tp.gnsplit;
+      e[3] = 0;
+    }
   }
   for (const Piece& pc : pieces) {  // one combine entry per row whose keys are split across CTAs
     if (pc.gsplit != 0 || pc.gnsplit < 2) continue;

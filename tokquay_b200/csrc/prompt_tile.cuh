@@ -11,7 +11,7 @@
 // keys [0, last row's position] in 32-key chunks.  Per chunk:
 //   S = Q K^T      (M = 128 rows, N = 32 keys, K = 64 dims)
 //   P = exp2(S * scale_log2 - m)  (online softmax, one row per thread)
-//   O += P V       (M = 128 rows, N = 64 dims, K = 32 keys)
+//   O += P V       (M = 128 rows, N = 64 dims, K = 32 keys, accumulated in TMEM)
 // Both products run as tcgen05.mma kind::tf32 with fp32 accumulation in
 // tensor memory.  fp32 accuracy comes from splitting every operand x into
 // hi = x with its low 13 mantissa bits cleared (exact in TF32) and lo = x - hi,
@@ -21,21 +21,23 @@
 // Roles (12 warps):
 //   warps 0-3   row threads: thread t owns query row t = TMEM lane t.  They
 //               write Q (hi | lo) into TMEM, read S back, run the softmax,
-//               write P (hi | lo) into TMEM over S, fold each chunk's PV into
-//               registers and store the normalised output rows.
-//   warp 4      MMA issuer (the whole warp walks the loop, one elected lane
-//               issues): QK^T of chunk g+1 is issued before PV of chunk g, so
-//               the tensor core works while the softmax runs.
+//               write P (hi | lo) into TMEM over S, rescale the item's PV
+//               accumulator when a row's maximum jumps, and store the
+//               normalised output rows.
+//   warp 4      QK^T issuer and warp 11 PV issuer (each: the whole warp walks
+//               the loop, one elected lane issues); two issuing threads keep
+//               the tensor core busy while the softmax runs (one thread's
+//               tcgen05.mma stream is issue-bound, measured on B200).
 //   warp 5      producer: TMA bulk copies of each chunk's K and V rows from the
 //               pool (through the block table) into a raw ring, one per block.
-//   warps 6-11  converters: the hi/lo split of each raw chunk into the MMA
+//   warps 6-10  converters: the hi/lo split of each raw chunk into the MMA
 //               operand layouts (V transposed), up to kTileKVBufs chunks ahead
 //               of the MMAs.
 //
-// Tensor memory (512 columns): Q buffers (hi 64 | lo 64) at 0 and 128, one per
-// item parity (the next item's Q is written while the current one runs); S/P
-// buffers at 256 and 320 (S in 32 columns, then P hi over them, P lo at +32);
-// O buffers at 384 and 448.
+// Tensor memory (512 columns): Q (hi 64 | lo 64) at 0 (the next item's Q is
+// written once the current item's last S is out); three S/P buffers at 128,
+// 192 and 256 (S in 32 columns, then P hi over them, P lo at +32); PV
+// accumulators at 320 and 384, one per item parity.
 //
 // Shared-memory operand layout (K-major, no swizzle): element (r, k) of an
 // operand with R rows and k along the reduction dimension sits at
@@ -61,7 +63,8 @@ constexpr int kTileRowWarps = 4;
 constexpr int kTileMmaWarp = 4;
 constexpr int kTileProducerWarp = 5;  // TMA copies of the K/V rows
 constexpr int kTileCvtWarp0 = 6;      // converters: hi/lo split into the MMA layout
-constexpr int kTileCvtWarps = 2 * kAttnWarps - kTileCvtWarp0;  // 6
+constexpr int kTilePvWarp = 2 * kAttnWarps - 1;  // PV issuer (warp 11)
+constexpr int kTileCvtWarps = kTilePvWarp - kTileCvtWarp0;  // 5
 constexpr int kTileUnits = 32;  // per chunk: {K, V} x 4 groups of 8 keys x 4 blocks of 16 dims
 constexpr int kTileUnitsPerThread = (kTileUnits + kTileCvtWarps - 1) / kTileCvtWarps;
 constexpr int kTileOpBytes = 32 * kHeadDim * 4;  // one hi or lo half of a K chunk
@@ -80,18 +83,29 @@ constexpr int kTileQStride = kHeadDim * 4 + 16;  // padded q rows: thread t's ro
 constexpr int kTileOffQStage = kTileOffRaw + kTileRawStages * kTileRawStageBytes;
 constexpr int kTileOffItems = kTileOffQStage + kTileRows * kTileQStride;
 constexpr int kTileOffBars = kTileOffItems + kTileMaxItems * 32;
-// kv_ready[3] kv_free[3] s_full[2] p_full[2] o_full[2] q_ready[2] done raw_full[R] raw_empty[R]
-constexpr int kTileBarKvReady = 0, kTileBarKvFree = 3, kTileBarSFull = 6, kTileBarPFull = 8,
-              kTileBarOFull = 10, kTileBarQReady = 12, kTileBarDone = 14, kTileBarRawFull = 15,
-              kTileBarRawEmpty = 15 + kTileRawStages, kTileNumBars = 15 + 2 * kTileRawStages;
-constexpr int kTileOffMisc = kTileOffBars + kTileNumBars * 8;  // [0] TMEM base, [1] abort flag
-constexpr int kTileSmemBytes = kTileOffMisc + 16;
+// kv_ready[3] kv_free[3] s_full[3] p_full[3] o_full[3] q_ready done raw_full[R] raw_empty[R]
+// rows_done merge_go (split items: the row warps' partials are out / the merge decision is in)
+constexpr int kTileSP = 3;  // S/P buffers in TMEM (chunk g uses g % kTileSP)
+constexpr int kTileBarKvReady = 0, kTileBarKvFree = 3, kTileBarSFull = 6, kTileBarPFull = 9,
+              kTileBarOFull = 12, kTileBarQReady = 15, kTileBarDone = 16, kTileBarRawFull = 17,
+              kTileBarRawEmpty = kTileBarRawFull + kTileRawStages, kTileBarRowsDone = kTileBarRawEmpty + kTileRawStages,
+              kTileBarMergeGo = kTileBarRowsDone + 1, kTileNumBars = kTileBarMergeGo + 1;
+// [0] TMEM base, [1] abort flag, [2] this CTA wrote the last partial of a split item
+static_assert(kTileBarRawFull == kTileBarDone + 1 && kTileBarDone == kTileBarQReady + 1 &&
+                  kTileBarQReady == kTileBarOFull + kTileSP && kTileBarOFull == kTileBarPFull + kTileSP &&
+                  kTileBarPFull == kTileBarSFull + kTileSP && kTileBarSFull == kTileBarKvFree + kTileKVBufs &&
+                  kTileBarKvFree == kTileBarKvReady + kTileKVBufs,
+              "tile barriers do not overlap");
+constexpr int kTileOffMisc = kTileOffBars + kTileNumBars * 8;
+constexpr int kTileOffParams = kTileOffMisc + 16;  // the launch's AttnParams, copied here
+constexpr int kTileSmemBytes = kTileOffParams + (int)((sizeof(AttnParams) + 15) / 16 * 16);
 static_assert(kChunk == 32, "prompt tiles take 32-key chunks");
 static_assert(kTileSmemBytes <= kAttnSmemBytes, "a tile CTA fits the launch's shared memory");
 static_assert(2 * kAttnWarps * 32 == 384, "tile roles assume 12 warps");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemQ = 0, kTmemS = 256, kTmemO = 384;
+constexpr uint32_t kTmemQ = 0, kTmemS = 128, kTmemO = 320;
 constexpr uint32_t kTmemP = kTmemS;  // P hi (+32: P lo) over S of the same buffer
+constexpr float kTileRescale = 8.f;  // log2 units a row's maximum may pass its reference by
 
 // Instruction descriptors (kind::tf32, fp32 accumulator, M = 128, both
 // operands K-major): bits 4-5 D format (1 = f32), 7-9 A format (2 = tf32),
@@ -176,6 +190,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
       "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+}
+
+// TMA bulk store of `bytes` from this CTA's shared memory to global memory,
+// in this thread's bulk group; wait_read: until the sources have been read.
+__device__ __forceinline__ void bulk_store_s2g(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 // 16-byte global -> shared copy; src_bytes 0 writes zeros and reads nothing.
@@ -283,16 +308,48 @@ __device__ __forceinline__ void tile_q_to_tmem(uint32_t taddr, uint32_t qrow) {
   }
 }
 
-// o = alpha * o + (chunk's PV, 64 columns of this thread's TMEM lane at
-// taddr); the first fold of an item takes the PV alone.
-__device__ __forceinline__ void tile_fold(uint32_t taddr, float (&o)[64], float alpha, bool first) {
+// The 64 accumulator columns of this thread's TMEM lane at taddr, times
+// factor (whole warp: the loads and stores are .sync.aligned).
+__device__ __forceinline__ void tile_scale_o(uint32_t taddr, float factor) {
   uint32_t v[32];
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     tmem_ld32(taddr + 32 * half, v);
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      o[32 * half + i] = first ? __uint_as_float(v[i]) : fmaf(o[32 * half + i], alpha, __uint_as_float(v[i]));
+    for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * factor);
+    tmem_st32(taddr + 32 * half, v);
+  }
+}
+
+// S of chunk g (buffer g % kTileSP) = Q x K^T (shared-memory
+// buffer g % kTileKVBufs): 8 k-steps of 8 dims, hi*hi + hi*lo + lo*hi each.
+__device__ __forceinline__ void tile_issue_qk(uint32_t tmem, uint32_t kv0, int g) {
+  const uint32_t d = tmem + kTmemS + 64 * (g % kTileSP);
+  const uint32_t a = tmem + kTmemQ;
+  const uint32_t kb = kv0 + (uint32_t)((g % kTileKVBufs) * kTileBufBytes);
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    const uint64_t bhi = umma_smem_desc(kb + 1024 * s, 512, 128);
+    const uint64_t blo = umma_smem_desc(kb + kTileOpBytes + 1024 * s, 512, 128);
+    umma_tf32_ts(d, a + 8 * s, bhi, kIdescQK, s > 0);
+    umma_tf32_ts(d, a + 8 * s, blo, kIdescQK, 1);
+    umma_tf32_ts(d, a + 64 + 8 * s, bhi, kIdescQK, 1);
+  }
+}
+
+// Item k's accumulator (+)= P of chunk g x V (transposed in the shared-memory
+// buffer g % kTileKVBufs): 4 k-steps of 8 keys; `first` starts the sum.
+__device__ __forceinline__ void tile_issue_pv(uint32_t tmem, uint32_t kv0, int g, int k, bool first) {
+  const uint32_t d = tmem + kTmemO + 64 * (k & 1);
+  const uint32_t a = tmem + kTmemP + 64 * (g % kTileSP);
+  const uint32_t vb = kv0 + (uint32_t)((g % kTileKVBufs) * kTileBufBytes + kTileOffVt);
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const uint64_t bhi = umma_smem_desc(vb + 2 * kTileVtLbo * s, kTileVtLbo, kTileVtSbo);
+    const uint64_t blo = umma_smem_desc(vb + kTileVtBytes + 2 * kTileVtLbo * s, kTileVtLbo, kTileVtSbo);
+    umma_tf32_ts(d, a + 8 * s, bhi, kIdescPV, !first || s > 0);
+    umma_tf32_ts(d, a + 8 * s, blo, kIdescPV, 1);
+    umma_tf32_ts(d, a + 32 + 8 * s, bhi, kIdescPV, 1);
   }
 }
 
@@ -313,10 +370,12 @@ __device__ __forceinline__ void tile_advance(TileCursor& cur, const WorkItem* it
 // 2 K/V ready, 3 MMA saw kv_ready, 4 MMA saw p_full, 5 PV issued, 6 row saw
 // S, 7 row P written, 8 row saw O (fold).
 constexpr int kTrEv = 20, kTrCh = 48;
-__device__ long long g_tile_trace[4 * kTrEv * kTrCh];
+// Per CTA of the last launch: globaltimer at entry, latest warp exit, tile CTA (1) or not.
+__device__ unsigned long long g_cta_time[3 * 1024];
+__device__ long long g_tile_trace[160 * kTrEv * kTrCh];
 #define TQ_TILE_TR(ev, ch) \
-  do { if (blockIdx.x >= gridDim.x - 4 && (ch) < kTrCh) \
-    g_tile_trace[((blockIdx.x - (gridDim.x - 4)) * kTrEv + (ev)) * kTrCh + (ch)] = clock64() - tr_t0; } while (0)
+  do { if (blockIdx.x < 160 && (ch) < kTrCh) \
+    g_tile_trace[(blockIdx.x * kTrEv + (ev)) * kTrCh + (ch)] = clock64() - tr_t0; } while (0)
 #else
 #define TQ_TILE_TR(ev, ch) do { } while (0)
 #endif
@@ -334,6 +393,8 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
 
   // ---- the CTA's items (warp slot 0's list) and set-up ----------------------
   const int ws0 = blockIdx.x * kAttnWarps;
+  // The producer's first copies use the block ids that ride with the first item.
+  const int first_blk = warp == kTileProducerWarp ? __ldg(p.attn + kFirstWords * (size_t)ws0 + 8 + ((lane >> 1) & 7)) : -1;
   const int r0 = __ldg(warp_offsets(p) + ws0), r1 = __ldg(warp_offsets(p) + ws0 + 1);
   const int count = 1 + r1 - r0;
   if (count > kTileMaxItems) {  // the planner never writes such a list
@@ -355,13 +416,15 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
       mbar_init(bar(kTileBarKvReady + i), kTileCvtWarps);
       mbar_init(bar(kTileBarKvFree + i), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kTileSP; ++i) {
       mbar_init(bar(kTileBarSFull + i), 1);
       mbar_init(bar(kTileBarPFull + i), kTileRowWarps);
       mbar_init(bar(kTileBarOFull + i), 1);
-      mbar_init(bar(kTileBarQReady + i), kTileRowWarps);
     }
-    mbar_init(bar(kTileBarDone), 1);
+    mbar_init(bar(kTileBarQReady), kTileRowWarps);
+    mbar_init(bar(kTileBarDone), 2);  // both MMA issuers' work has completed
+    mbar_init(bar(kTileBarRowsDone), kTileRowWarps);
+    mbar_init(bar(kTileBarMergeGo), 1);
     misc[1] = 0;
     mbar_init_fence();
   }
@@ -373,13 +436,17 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = misc[0];
+  if (threadIdx.x == 0) TQ_TILE_TR(18, 0);
   // Items are checked once, here: rows within a tile, keys within the sequence's
   // table (the K/V role also checks each block id against the pool).
   bool bad = false;
   for (int k = 0; k < count; ++k) {
     const WorkItem& it = items[k];
+    const int f = it.flags() & ~kFlagTile;
     bad |= it.nrows() < 1 || it.nrows() > kTileRows || it.head() >= p.n_head || it.cbeg() >= it.cend() ||
-           (it.pos0() + it.nrows() + kChunk - 1) / kChunk != it.cend() || it.cbeg() != 0;
+           it.cend() > (it.pos0() + it.nrows() + kChunk - 1) / kChunk || (f != 0 && f != kFlagGlobal) ||
+           (f == kFlagGlobal && (it.gbase() < 0 || it.gsplit() >= it.gnsplit() ||
+                                 (long long)it.gbase() + (long long)it.nrows() * it.gnsplit() > p.max_partials));
   }
   if (bad && threadIdx.x == 0) raise_device_error(TQ_DEVERR_BAD_PLAN);
   pdl_wait();  // q rows and this step's K/V rows come from the kernels before this one
@@ -393,60 +460,62 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
     cp_async_wait<0>();
     tile_q_to_tmem(lane_base + kTmemQ, qrow);
     warp_arrive_after_tmem_st(bar(kTileBarQReady));
-    int g = 0;
+    int g = 0, splits_done = 0;
     bool ok = true;
     for (int k = 0; k < count && ok; ++k) {
       const WorkItem it = items[k];
       const bool has_next = k + 1 < count;
-      if (has_next) tile_issue_q(p, items[k + 1], t, qrow);  // lands while the first chunk's S is computed
+      if (has_next) {  // lands while the first chunk's S is computed
+        bulk_store_wait_read();  // the previous item's output has left the staging row
+        tile_issue_q(p, items[k + 1], t, qrow);
+      }
       const int kend = it.pos0() + it.nrows();
       const int lim_abs = min(it.pos0() + t, kend - 1);  // this row's last key
-      float o[64];
-      float m = -INFINITY, l = 0.f, alpha_pend = 1.f;
+      const uint32_t o_col = lane_base + kTmemO + 64 * (k & 1);  // this item's PV accumulator
+      // m: the reference the item's P is taken against (log2 units); l: the
+      // sum of P.  The PVs of the item accumulate in TMEM against m, which
+      // moves only when a chunk's maximum passes it by more than
+      // kTileRescale (P stays below 2^kTileRescale); then the accumulator is
+      // rescaled in place before that chunk's PV is issued.
+      float m = -INFINITY, l = 0.f;
       for (int c = it.cbeg(); c < it.cend() && ok; ++c, ++g) {
-        const int b = g & 1;
-        ok = tile_wait_warp(bar(kTileBarSFull + b), (uint32_t)(g >> 1) & 1u, abort_flag);
+        const int b = g % kTileSP;
+        ok = tile_wait_warp(bar(kTileBarSFull + b), (uint32_t)(g / kTileSP) & 1u, abort_flag);
         if (!ok) break;
         if (t == 0) TQ_TILE_TR(6, g);
         tc_fence_after();
-        if (c == it.cbeg() && has_next) {  // the next item's Q, into the other buffer
+        if (c + 1 == it.cend() && has_next) {  // every QK^T of this item is done: the next item's Q
           cp_async_wait<0>();
-          tile_q_to_tmem(lane_base + kTmemQ + 128 * ((k + 1) & 1), qrow);
-          warp_arrive_after_tmem_st(bar(kTileBarQReady + ((k + 1) & 1)));
+          tile_q_to_tmem(lane_base + kTmemQ, qrow);
+          warp_arrive_after_tmem_st(bar(kTileBarQReady));
         }
         uint32_t s[32];
         tmem_ld32(lane_base + kTmemS + 64 * b, s);
         const int lim = lim_abs - c * kChunk;  // keys j <= lim of this chunk are valid
         float mx = -INFINITY;
-        if (lim >= kChunk - 1) {  // every key of the chunk is valid for this row
+        if (lim < kChunk - 1) {  // the causal diagonal: keys past the row's position
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float x = __uint_as_float(s[j]) * p.scale_log2;
-            s[j] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float x = j <= lim ? __uint_as_float(s[j]) * p.scale_log2 : -INFINITY;
-            s[j] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
-          }
+          for (int j = 0; j < 32; ++j)
+            if (j > lim) s[j] = __float_as_uint(-INFINITY);
         }
-        // Scores are finite (fp32 products of finite q and k), so mn is -inf
-        // only while no key of the row has been seen; exp2(-inf) = 0 masks.
-        const float mn = fmaxf(m, mx);
-        const float alpha = mn == -INFINITY ? 1.f : fast_exp2(m - mn);
-        const float mref = mn == -INFINITY ? 0.f : mn;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, __uint_as_float(s[j]));
+        // Scores are finite (fp32 products of finite q and k): mx is -inf only
+        // for a row without a key in this chunk, whose P is all zero.
+        const float mxs = mx * p.scale_log2;
+        const bool bump = mxs > m + kTileRescale;  // always at the item's first chunk
+        const float mnew = bump ? mxs : m;
+        const float mref = mnew == -INFINITY ? 0.f : mnew;
         float psum = 0.f;
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float pj = fast_exp2(__uint_as_float(s[j]) - mref);
+          const float pj = fast_exp2(fmaf(__uint_as_float(s[j]), p.scale_log2, -mref));  // exp2(-inf) = 0
           psum += pj;
           s[j] = __float_as_uint(pj);
         }
-        l = fmaf(l, alpha, psum);
-        m = mn;
+        const float factor = bump ? fast_exp2(m - mnew) : 1.f;  // 0 while m is -inf
+        l = fmaf(l, factor, psum);
+        m = mnew;
         uint32_t hi[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -455,104 +524,167 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
         }
         tmem_st32(lane_base + kTmemP + 64 * b, hi);
         tmem_st32(lane_base + kTmemP + 64 * b + 32, s);
+        bool waited = c == it.cbeg();  // the item's first PV overwrites the accumulator
+        if (!waited && __any_sync(kFullMask, bump)) {
+          // Rescale the accumulator (every PV issued so far has completed)
+          // before this chunk's PV adds to it.
+          const int pg = g - 1;
+          if (!(ok = tile_wait_warp(bar(kTileBarOFull + pg % kTileSP), (uint32_t)(pg / kTileSP) & 1u, abort_flag))) break;
+          tc_fence_after();
+          tile_scale_o(o_col, factor);
+          waited = true;
+        }
         warp_arrive_after_tmem_st(bar(kTileBarPFull + b));
         if (t == 0) TQ_TILE_TR(7, g);
-        if (c > it.cbeg()) {  // chunk g-1's PV, into the registers
+        if (!waited) {  // chunk g-1's PV: consumed, so the barrier's phases stay in step
           const int pg = g - 1;
-          if (!(ok = tile_wait_warp(bar(kTileBarOFull + (pg & 1)), (uint32_t)(pg >> 1) & 1u, abort_flag))) break;
+          if (!(ok = tile_wait_warp(bar(kTileBarOFull + pg % kTileSP), (uint32_t)(pg / kTileSP) & 1u, abort_flag))) break;
           if (t == 0) TQ_TILE_TR(8, pg);
-          tc_fence_after();
-          tile_fold(lane_base + kTmemO + 64 * (pg & 1), o, alpha_pend, c == it.cbeg() + 1);
         }
-        alpha_pend = alpha;
       }
       if (!ok) break;
-      {  // the last chunk's PV
+      {  // the last chunk's PV completes the accumulator
         const int pg = g - 1;
-        if (!(ok = tile_wait_warp(bar(kTileBarOFull + (pg & 1)), (uint32_t)(pg >> 1) & 1u, abort_flag))) break;
-        if (t == 0) TQ_TILE_TR(8, pg);
+        if (!(ok = tile_wait_warp(bar(kTileBarOFull + pg % kTileSP), (uint32_t)(pg / kTileSP) & 1u, abort_flag))) break;
+        if (t == 0) TQ_TILE_TR(13, k);
         tc_fence_after();
-        tile_fold(lane_base + kTmemO + 64 * (pg & 1), o, alpha_pend, it.cend() - it.cbeg() == 1);
       }
-      if (t < it.nrows()) {
+      float* const orow = p.out + (size_t)(it.row0() + t) * p.out_stride + it.head() * kHeadDim;
+      if (!(it.flags() & kFlagGlobal)) {
+        // The whole key range: the normalised row, staged in this thread's q
+        // row (its q has been consumed; the next q copy waits for this store
+        // to have read it) and written by one 256-byte bulk store.
         const float inv = 1.f / l;
-        float4* dst = reinterpret_cast<float4*>(p.out + (size_t)(it.row0() + t) * p.out_stride + it.head() * kHeadDim);
+        uint32_t v[32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          tmem_ld32(o_col + 32 * half, v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(qrow + 128 * half + 16 * i),
+                         "f"(__uint_as_float(v[4 * i]) * inv), "f"(__uint_as_float(v[4 * i + 1]) * inv),
+                         "f"(__uint_as_float(v[4 * i + 2]) * inv), "f"(__uint_as_float(v[4 * i + 3]) * inv)
+                         : "memory");
+        }
+        if (t < it.nrows()) {
+          fence_proxy_async_smem();
+          bulk_store_s2g(orow, qrow, kRowBytes);
+        }
+        if (t == 0) TQ_TILE_TR(14, k);
+        continue;
+      }
+      // A piece of a split tile: this piece's partial (m, l, unnormalised
+      // accumulator) per row into the split-K scratch; the piece that
+      // completes the count merges every row of the tile (rows without a key
+      // in a piece carry m = -inf and weigh nothing) and leaves the counter 0.
+      const size_t idx0 = (size_t)it.gbase() + (size_t)t * it.gnsplit();  // row t's split 0
+      {
+        uint32_t v[32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          tmem_ld32(o_col + 32 * half, v);
+          if (t < it.nrows()) {
+            float4* dst = reinterpret_cast<float4*>(p.part_acc + (idx0 + it.gsplit()) * kHeadDim + 32 * half);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                   __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+          }
+        }
+        if (t < it.nrows()) *reinterpret_cast<float2*>(p.part_ml + 2 * (idx0 + it.gsplit())) = make_float2(m, l);
+      }
+      __threadfence();  // this row's partial is visible before the count says so
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kTileBarRowsDone));
+      if (t == 0) {
+        const bool seen = tile_wait(bar(kTileBarRowsDone), (uint32_t)splits_done & 1u, abort_flag);
+        int old = 0;
+        if (seen)
+          asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.part_cnt + it.gbase()) : "memory");
+        misc[2] = seen && old == it.gnsplit() - 1;
+        mbar_arrive(bar(kTileBarMergeGo));
+      }
+      if (!(ok = tile_wait_warp(bar(kTileBarMergeGo), (uint32_t)splits_done & 1u, abort_flag))) break;
+      ++splits_done;
+      if (!misc[2]) continue;
+      __threadfence();
+      if (t < it.nrows()) {
+        float mmax = -INFINITY;
+        for (int sp = 0; sp < it.gnsplit(); ++sp) mmax = fmaxf(mmax, __ldcg(p.part_ml + 2 * (idx0 + sp)));
+        float lt = 0.f;
+        float4 acc[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int sp = 0; sp < it.gnsplit(); ++sp) {
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + 2 * (idx0 + sp)));
+          const float w = ml.x == -INFINITY ? 0.f : fast_exp2(ml.x - mmax);
+          lt = fmaf(ml.y, w, lt);
+          const float4* src = reinterpret_cast<const float4*>(p.part_acc + (idx0 + sp) * kHeadDim);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float4 a = __ldcg(src + i);
+            acc[i] = make_float4(fmaf(a.x, w, acc[i].x), fmaf(a.y, w, acc[i].y), fmaf(a.z, w, acc[i].z),
+                                 fmaf(a.w, w, acc[i].w));
+          }
+        }
+        const float inv = 1.f / lt;
+        float4* dst = reinterpret_cast<float4*>(orow);
 #pragma unroll
         for (int i = 0; i < 16; ++i)
-          dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+          dst[i] = make_float4(acc[i].x * inv, acc[i].y * inv, acc[i].z * inv, acc[i].w * inv);
       }
+      if (t == 0) p.part_cnt[it.gbase()] = 0;  // ready for the next launch
     }
-    cp_async_wait<0>();  // no copy of a q row may land after the CTA is gone
+    cp_async_wait<0>();     // no copy of a q row may land after the CTA is gone
+    bulk_store_wait_read();  // nor an output store read its shared memory
   } else if (!bad && warp == kTileMmaWarp) {
-    // ---- MMA issuer: the whole warp walks the loop, one lane issues ---------
-    {
-      const uint32_t kv0 = smem_addr(smem);
-      auto issue_qk = [&](int g, int qbuf) {
-        TQ_TILE_TR(9, g);
-        const uint32_t d = tmem + kTmemS + 64 * (g & 1);
-        const uint32_t a = tmem + kTmemQ + 128 * qbuf;
-        const uint32_t kb = kv0 + (uint32_t)((g % kTileKVBufs) * kTileBufBytes);
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {  // 8 dims per MMA
-          const uint64_t bhi = umma_smem_desc(kb + 1024 * s, 512, 128);
-          const uint64_t blo = umma_smem_desc(kb + kTileOpBytes + 1024 * s, 512, 128);
-          umma_tf32_ts(d, a + 8 * s, bhi, kIdescQK, s > 0);
-          umma_tf32_ts(d, a + 8 * s, blo, kIdescQK, 1);
-          umma_tf32_ts(d, a + 64 + 8 * s, bhi, kIdescQK, 1);
-        }
-      };
-      auto issue_pv = [&](int g) {
-        const uint32_t d = tmem + kTmemO + 64 * (g & 1);
-        const uint32_t a = tmem + kTmemP + 64 * (g & 1);
-        const uint32_t vb = kv0 + (uint32_t)((g % kTileKVBufs) * kTileBufBytes + kTileOffVt);
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {  // 8 keys per MMA
-          const uint64_t bhi = umma_smem_desc(vb + 2 * kTileVtLbo * s, kTileVtLbo, kTileVtSbo);
-          const uint64_t blo = umma_smem_desc(vb + kTileVtBytes + 2 * kTileVtLbo * s, kTileVtLbo, kTileVtSbo);
-          umma_tf32_ts(d, a + 8 * s, bhi, kIdescPV, s > 0);
-          umma_tf32_ts(d, a + 8 * s, blo, kIdescPV, 1);
-          umma_tf32_ts(d, a + 32 + 8 * s, bhi, kIdescPV, 1);
-        }
-      };
-      auto kv_ready = [&](int g) {
-        if (!tile_wait_warp(bar(kTileBarKvReady + g % kTileKVBufs), (uint32_t)(g / kTileKVBufs) & 1u, abort_flag))
-          return false;
+    // ---- QK^T issuer: the whole warp walks the loop, one lane issues ------
+    // S buffer g % kTileSP last held chunk g-kTileSP's P: QK^T of chunk g
+    // waits for that chunk's PV (issued by the PV warp) to complete.
+    const uint32_t kv0 = smem_addr(smem);
+    int g = 0;
+    bool ok = true;
+    for (int k = 0; k < count && ok; ++k) {
+      const WorkItem& it = items[k];
+      if (!(ok = tile_wait_warp(bar(kTileBarQReady), (uint32_t)k & 1u, abort_flag))) break;
+      for (int c = it.cbeg(); c < it.cend(); ++c, ++g) {
+        if (!(ok = tile_wait_warp(bar(kTileBarKvReady + g % kTileKVBufs), (uint32_t)(g / kTileKVBufs) & 1u,
+                                  abort_flag)))
+          break;
         TQ_TILE_TR(3, g);
+        if (g >= kTileSP &&
+            !(ok = tile_wait_warp(bar(kTileBarOFull + g % kTileSP), (uint32_t)(g / kTileSP - 1) & 1u, abort_flag)))
+          break;
         tc_fence_after();
-        return true;
-      };
-      int g = 0;
-      bool ok = true;
-      for (int k = 0; k < count && ok; ++k) {
-        const WorkItem& it = items[k];
-        const int n = it.cend() - it.cbeg();
-        ok = tile_wait_warp(bar(kTileBarQReady + (k & 1)), (uint32_t)(k >> 1) & 1u, abort_flag);
-        if (!ok) break;
-        tc_fence_after();
-        if (!(ok = kv_ready(g))) break;
-        issue_qk(g, k & 1);
-        umma_commit(bar(kTileBarSFull + (g & 1)));
+        TQ_TILE_TR(9, g);
+        tile_issue_qk(tmem, kv0, g);
+        umma_commit(bar(kTileBarSFull + g % kTileSP));
         TQ_TILE_TR(10, g);
-        for (int j = 0; j < n; ++j, ++g) {
-          if (j + 1 < n) {
-            if (!(ok = kv_ready(g + 1))) break;
-            issue_qk(g + 1, k & 1);
-            umma_commit(bar(kTileBarSFull + ((g + 1) & 1)));
-            TQ_TILE_TR(10, g + 1);
-          }
-          if (!(ok = tile_wait_warp(bar(kTileBarPFull + (g & 1)), (uint32_t)(g >> 1) & 1u, abort_flag))) break;
-          TQ_TILE_TR(4, g);
-          tc_fence_after();
-          issue_pv(g);
-          umma_commit(bar(kTileBarOFull + (g & 1)));
-          umma_commit(bar(kTileBarKvFree + g % kTileKVBufs));
-          TQ_TILE_TR(5, g);
-        }
       }
-      // Every MMA issued has completed before the CTA may free TMEM or exit.
-      umma_commit(bar(kTileBarDone));
-      mbar_wait_bounded(bar(kTileBarDone), 0);
     }
+    // Every MMA issued has completed before the CTA may free TMEM or exit.
+    umma_commit(bar(kTileBarDone));
+    mbar_wait_bounded(bar(kTileBarDone), 0);
+    if (lane == 0) TQ_TILE_TR(16, 0);
+  } else if (!bad && warp == kTilePvWarp) {
+    // ---- PV issuer ------------------------------------------------------------
+    const uint32_t kv0 = smem_addr(smem);
+    int g = 0;
+    bool ok = true;
+    for (int k = 0; k < count && ok; ++k) {
+      const WorkItem& it = items[k];
+      for (int c = it.cbeg(); c < it.cend(); ++c, ++g) {
+        if (!(ok = tile_wait_warp(bar(kTileBarPFull + g % kTileSP), (uint32_t)(g / kTileSP) & 1u, abort_flag))) break;
+        TQ_TILE_TR(4, g);
+        tc_fence_after();
+        tile_issue_pv(tmem, kv0, g, k, c == it.cbeg());
+        umma_commit(bar(kTileBarOFull + g % kTileSP));
+        umma_commit(bar(kTileBarKvFree + g % kTileKVBufs));
+        TQ_TILE_TR(5, g);
+      }
+    }
+    umma_commit(bar(kTileBarDone));
+    mbar_wait_bounded(bar(kTileBarDone), 0);
   } else if (!bad && warp == kTileProducerWarp) {
     // ---- producer: each chunk's K and V rows, a bulk copy per block --------
     // Copy d of a chunk (d < 2 * its blocks) is the K (d even) or V (d odd)
@@ -582,7 +714,12 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
     TileCursor cur{0, items[0].cbeg()}, nxt = cur;
     tile_advance(nxt, items, count);
     int ba, bb, na, nb2;
-    load_blocks(cur, ba, bb);
+    if (bs >= kChunk / kFirstBlocks) {  // the first chunk spans at most kFirstBlocks blocks
+      ba = lane < 2 * nblocks(cur) ? first_blk : -1;
+      bb = -1;
+    } else {
+      load_blocks(cur, ba, bb);
+    }
     load_blocks(nxt, na, nb2);
     for (int g = 0; g < total; ++g) {
       const int st = g % kTileRawStages;
@@ -625,10 +762,11 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
       tile_advance(nxt, items, count);
       load_blocks(nxt, na, nb2);
     }
+    if (lane == 0) TQ_TILE_TR(17, 0);
     // Copies still in flight land before the CTA may exit (bounded).
     for (int g = max(total - kTileRawStages, 0); g < total; ++g)
       if (!mbar_wait_bounded(bar(kTileBarRawFull + g % kTileRawStages), (uint32_t)(g / kTileRawStages) & 1u)) break;
-  } else if (!bad && warp >= kTileCvtWarp0) {
+  } else if (!bad && warp >= kTileCvtWarp0 && warp < kTilePvWarp) {
     // ---- converters: raw rows -> hi/lo halves in the MMA layout ------------
     const int cw = warp - kTileCvtWarp0;
     const int f4 = lane >> 3, kk = lane & 7;
@@ -713,6 +851,7 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
   // ---- every role done: free the tensor memory --------------------------------
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) TQ_TILE_TR(15, 0);
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
