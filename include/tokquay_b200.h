@@ -91,7 +91,8 @@ enum tq_plan_layout {
   TQ_PLAN_OFF_COMBINE = 17,  /* [num_combine][4] rows whose keys are split across CTAs */
   TQ_PLAN_NUM_CTAS = 18,     /* CTAs the attention plan is cut for (its launch grid) */
   TQ_PLAN_USED_INTS = 19,    /* leading int32 of the plan this step uses (what must be copied) */
-  TQ_PLAN_LAYOUT_LEN = 20
+  TQ_PLAN_NUM_TILE_CTAS = 20,/* CTAs of the grid that run prompt tiles (tq_plan_prompt_tiles) */
+  TQ_PLAN_LAYOUT_LEN = 21
 };
 
 TQ_API int tq_abi_version(void);
@@ -198,7 +199,11 @@ TQ_API int tq_qkv_bias_kv_write(float* q_out, int64_t q_row_stride, const float*
  * plan launched with it (max_partials; NULL scratch is fine when it is 0).
  * Launches that share scratch must not overlap on the GPU.  attn_plan is the
  * plan's attention region (TQ_PLAN_OFF_ITEMS) and n_ctas its TQ_PLAN_NUM_CTAS,
- * the launch grid.  One kernel launch on `stream`; every merge of split keys
+ * the launch grid.  with_tiles must be nonzero when the plan may hold prompt
+ * tiles (TQ_PLAN_NUM_TILE_CTAS > 0; for a launch captured once and replayed
+ * over plans of fixed capacities: when any of them may) -- it selects the
+ * kernel that carries the tile role; 0 selects the leaner one, which flags
+ * (device error 16) and skips any tile item it is given.  One kernel launch on `stream`; every merge of split keys
  * happens inside it.  The launch is a programmatic dependent of the kernel
  * before it on `stream`: for a sequence that feeds one token this step, the
  * pool rows of its earlier positions (0 .. position-1) may be read before
@@ -209,7 +214,7 @@ TQ_API int tq_paged_attention(float* out, int64_t out_row_stride, const float* q
                        const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
                        int32_t block_size, int32_t head_dim, int32_t layer,
                        const int32_t* block_tables, int32_t table_stride,
-                       const int32_t* attn_plan, int32_t n_ctas,
+                       const int32_t* attn_plan, int32_t n_ctas, int32_t with_tiles,
                        float* partial_ml, float* partial_acc, int32_t* partial_counters,
                        int32_t max_partials, float scale, void* stream);
 

@@ -42,7 +42,8 @@ PLAN_OFF_ITEMS = 16
 PLAN_OFF_COMBINE = 17
 PLAN_NUM_CTAS = 18
 PLAN_USED_INTS = 19
-PLAN_LAYOUT_LEN = 20
+PLAN_NUM_TILE_CTAS = 20
+PLAN_LAYOUT_LEN = 21
 
 # Symbols the header declares, with (restype, argtypes).
 _P = c_void_p
@@ -60,7 +61,7 @@ SIGNATURES: dict[str, tuple] = {
                                      c_int32, c_int32, c_int32, _P, _P, c_int32, _P]),
     "tq_plan_prompt_tiles": (c_int, [c_int32, c_int32, c_int32]),
     "tq_paged_attention": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32,
-                                   c_int32, c_int32, _P, c_int32, _P, c_int32, _P, _P, _P, c_int32,
+                                   c_int32, c_int32, _P, c_int32, _P, c_int32, c_int32, _P, _P, _P, c_int32,
                                    c_float, _P]),
     "tq_paged_attention_noalloc": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32,
                                            c_int32, c_int32, _P, c_int32, _P, c_int32, c_int32, c_float,

@@ -51,8 +51,11 @@ int device_setup(int* sm_count) {
     e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess)
       return set_error(TQ_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
-    e = cudaFuncSetAttribute(paged_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(paged_attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kAttnSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(paged_attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kAttnSmemBytes);
     if (e != cudaSuccess)
       return set_error(TQ_ERR_CUDA, "cudaFuncSetAttribute(paged_attention): %s",
                        cudaGetErrorString(e));
@@ -164,7 +167,7 @@ int attention_params(float* out, int64_t out_row_stride, const float* q, int64_t
 // in the stream: its CTAs may start (barriers, work items, block ids, and for
 // decode items the K/V rows before the new key) while that kernel finishes;
 // everything else waits for it.
-cudaError_t launch_attention(const AttnParams& p, int n_ctas, cudaStream_t stream) {
+cudaError_t launch_attention(const AttnParams& p, int n_ctas, bool with_tiles, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(n_ctas);
   cfg.blockDim = dim3(kAttnThreads);
@@ -175,7 +178,8 @@ cudaError_t launch_attention(const AttnParams& p, int n_ctas, cudaStream_t strea
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, paged_attention_kernel, p);
+  return with_tiles ? cudaLaunchKernelEx(&cfg, paged_attention_kernel<true>, p)
+                    : cudaLaunchKernelEx(&cfg, paged_attention_kernel<false>, p);
 }
 
 int check_embd(int32_t n_embd) {
@@ -327,7 +331,7 @@ int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64
                        const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
                        int32_t block_size, int32_t head_dim, int32_t layer,
                        const int32_t* block_tables, int32_t table_stride,
-                       const int32_t* attn_plan, int32_t n_ctas,
+                       const int32_t* attn_plan, int32_t n_ctas, int32_t with_tiles,
                        float* partial_ml, float* partial_acc, int32_t* partial_counters,
                        int32_t max_partials, float scale, void* stream) {
   if (max_partials < 0) return set_error(TQ_ERR_INVALID, "negative capacity");
@@ -346,7 +350,7 @@ int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64
   p.part_acc = partial_acc;
   p.part_cnt = partial_counters;
   p.max_partials = max_partials;
-  const cudaError_t e = launch_attention(p, n_ctas, (cudaStream_t)stream);
+  const cudaError_t e = launch_attention(p, n_ctas, with_tiles != 0, (cudaStream_t)stream);
   if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "paged_attention launch: %s", cudaGetErrorString(e));
   return check_launch("paged_attention");
 }
@@ -437,7 +441,7 @@ int tq_paged_attention_noalloc(float* out, int64_t out_row_stride, const float* 
   p.part_ml = reinterpret_cast<float*>(base + kNoAllocCounterBytes);
   p.part_acc = reinterpret_cast<float*>(base + kNoAllocCounterBytes + kNoAllocMlBytes);
   p.max_partials = num_partials;
-  const cudaError_t e = launch_attention(p, n_ctas, s);
+  const cudaError_t e = launch_attention(p, n_ctas, true, s);  // any plan: the variant with tiles
   if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "paged_attention launch: %s", cudaGetErrorString(e));
   return check_launch("paged_attention_noalloc");
 }

@@ -502,6 +502,11 @@ namespace tq {
 // same work items (the planner's list for warp slot blockIdx.x*kAttnWarps+w).
 constexpr int kAttnThreads = 2 * kAttnWarps * 32;
 
+// kTiles: the kernel also carries the prompt-tile role (prompt_tile.cuh).
+// The variant without it serves plans without tile CTAs (every decode step):
+// the tile code's register and call overhead would cost its launches ~1.5 %
+// (measured on config 2: 21.9 vs 21.6 us).
+template <bool kTiles>
 __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const AttnParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5;
@@ -543,7 +548,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
 #else
 #define TQ_CTA_END() do { } while (0)
 #endif
-  if (tile_cta) {
+  if constexpr (!kTiles) {
+    if (tile_cta) {  // a plan with tile CTAs, launched on the variant without them
+      if (threadIdx.x == 0) raise_device_error(TQ_DEVERR_BAD_PLAN);
+      return;
+    }
+  } else if (tile_cta) {
     // The tile code reads the parameters from shared memory: passed by
     // reference, the kernel's would be copied to (slow, under load) local memory.
     AttnParams* const sp = reinterpret_cast<AttnParams*>(smem + kTileOffParams);

@@ -574,6 +574,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   layout[TQ_PLAN_OFF_COMBINE] = (int32_t)o_comb;
   layout[TQ_PLAN_NUM_CTAS] = n_ctas;
   layout[TQ_PLAN_USED_INTS] = (int32_t)used;
+  layout[TQ_PLAN_NUM_TILE_CTAS] = n_tctas;
 
   // Everything before the attention plan: zeros first (padding, table tails).
   std::memset(out, 0, sizeof(int32_t) * o_items);

@@ -400,6 +400,8 @@ class _CaptureView(DevicePagedBatch):
         self.rows_alloc, self.seqs_alloc = int(caps[1]), int(caps[0])
         self.partials_alloc = int(caps[5])
         self.n_ctas = int(L[_lib.PLAN_NUM_CTAS])
+        # Replays of a mixed-step capacity may hold prompt tiles: capture the kernel with them.
+        self.with_tiles = ws.max_tokens > ws.max_seqs
         self.num_items = self.num_combine = self.num_partials = 0
         dev = ws.plan
 

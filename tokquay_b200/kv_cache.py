@@ -491,6 +491,12 @@ class DevicePagedBatch(BatchedKV):
         self.table_stride = int(L[_lib.PLAN_TABLE_STRIDE])
         self.split_chunks = int(L[_lib.PLAN_SPLIT_CHUNKS])
         self.n_ctas = int(L[_lib.PLAN_NUM_CTAS])
+        # The attention kernel that carries the prompt-tile role: for a plan
+        # with tile CTAs, and for launches sized for a workspace (captured once,
+        # replayed over its steps) whenever a step of its capacity may feed
+        # several tokens of one sequence.
+        self.with_tiles = int(L[_lib.PLAN_NUM_TILE_CTAS]) > 0 or (
+            graph_sizing and workspace.max_tokens > workspace.max_seqs)
         # What activations and launches are sized for.
         if graph_sizing:
             caps = workspace.caps
@@ -570,7 +576,7 @@ class DevicePagedBatch(BatchedKV):
             out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), self.pool.data_ptr(),
             self.allocator.num_blocks, self.n_layer, self.n_head, self.block_size, self.d_head, layer,
             self.block_tables_i32.data_ptr(), self.table_stride, self.attn_plan.data_ptr(), self.n_ctas,
-            pm, pa, pc, self.partials_alloc,
+            int(self.with_tiles), pm, pa, pc, self.partials_alloc,
             1.0 / math.sqrt(self.d_head), stream), "tq_paged_attention")  # fmt: skip
 
     # ---- reference BatchedKV contract (not used by this package's model) ---------------
