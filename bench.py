@@ -1428,6 +1428,9 @@ def main():
     ap.add_argument("--kernel-table", action="store_true",
                     help="after the run, print per-kernel device times of 10 more decode steps (stderr)")
     ap.add_argument("--pool-gb", type=float, default=0, help="override the KV pool size in GB (profiling)")
+    ap.add_argument("--prompt-tile-rows", type=int, default=-1,
+                    help="least prompt chunk (rows) run as tensor-core tiles; 0 = every prompt row on warp "
+                         "items; default: the library's")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")
@@ -1457,8 +1460,17 @@ def main():
         _replicas.teardown(info)
         return
     _load_library()
+    if args.prompt_tile_rows >= 0:
+        _lib.prompt_tiles(args.prompt_tile_rows)
+    tile_rows = _lib.prompt_tiles()  # (reads the setting)
+
+    def tagged(res):  # the line names the prompt-tile setting it ran with
+        if res is not None and isinstance(res.get("config"), dict):
+            res["config"]["prompt_tile_min_rows"] = tile_rows
+        return res
+
     if args.workload == "cfg5":
-        res = run_serving(args, world, rank, local)
+        res = tagged(run_serving(args, world, rank, local))
         if rank == 0 and res is not None:
             _emit(res)
         _replicas.teardown(info)
@@ -1470,7 +1482,7 @@ def main():
         _replicas.teardown(info)
         return
     if args.workload == "cfg3":
-        res = run_mixed(args, world, rank, local)
+        res = tagged(run_mixed(args, world, rank, local))
         if rank == 0 and world == 1 and not args.no_cpu_baseline and res is not None:
             rate, sample, threads = cpu_oracle_mixed_rate(args.block_size or 16, 1, replica_seed(3, 0))
             res["cpu_baseline"] = {"value": rate, "unit": "rows/s", "cores": threads, "kind": "port",

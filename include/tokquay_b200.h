@@ -149,10 +149,14 @@ TQ_API int tq_device_status(int clear, int32_t* bits);
  * halves).  Tile items run on the last CTAs of the grid; how many is set by
  * the estimated loads: a tile item costs chunk_cost_pct percent of a warp-path
  * 32-key chunk per chunk, plus item_cost_pct.  min_rows 0 turns tiles off.
- * Arguments below 0 (chunk_cost_pct: <= 0) keep the current value.  The
- * setting is process-wide and read by each tq_plan_step call; defaults 16,
- * 1500, 200.  Returns the previous min_rows. */
-TQ_API int tq_plan_prompt_tiles(int32_t min_rows, int32_t chunk_cost_pct, int32_t item_cost_pct);
+ * max_pieces > 1 lets a step of prompt rows alone cut a long tile over its keys
+ * into up to that many pieces on different CTAs, merged through the split-K
+ * scratch (slower than whole tiles on B200: off by default).  Arguments below
+ * 0 (chunk_cost_pct, max_pieces: <= 0) keep the current value.  The setting is
+ * process-wide and read by each tq_plan_step call; defaults 16, 1500, 200, 1.
+ * Returns the previous min_rows. */
+TQ_API int tq_plan_prompt_tiles(int32_t min_rows, int32_t chunk_cost_pct, int32_t item_cost_pct,
+                                int32_t max_pieces);
 
 TQ_API int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_t* q_len,
                  const int32_t* table_offsets, const int32_t* table_data,

@@ -420,7 +420,7 @@ def _item_flags(batch) -> list[int]:
 def tile_knobs():
     prev = _lib.prompt_tiles()
     yield _lib.prompt_tiles
-    _lib.prompt_tiles(prev, 1500, 200)
+    _lib.prompt_tiles(prev, 1500, 200, 1)
 
 
 @pytest.mark.parametrize("bs", [4, 16, 64])
@@ -430,8 +430,9 @@ def test_prompt_tiles_match_float64_reference(bs, shape, tile_knobs):
     tensor-core tiles: prompt rows alone (long tiles cut into pieces merged
     through the split-K scratch), the same beside a decode row (whole tiles),
     and with tiles off (2-row warp items) -- every row against float64, with
+    pieces allowed for the first shape (off by default),
     NaN in every slot past each context."""
-    tile_knobs(0 if shape == "tiles_off" else 16, 1500, 200)
+    tile_knobs(0 if shape == "tiles_off" else 16, 1500, 200, 8 if shape == "prefill_split" else 1)
     rng = random.Random(bs)
     cfg = GPT2Config(vocab_size=64, n_positions=1024, n_embd=768, n_layer=1, n_head=12)
     alloc = BlockAllocator(cfg, 4 * cdiv(1024, bs) + 8, bs, device="cuda")

@@ -371,7 +371,7 @@ def tile_knobs():
     """Restores the planner's process-wide prompt-tile settings after a test."""
     prev = _lib.prompt_tiles()
     yield _lib.prompt_tiles
-    _lib.prompt_tiles(prev, 1500, 200)
+    _lib.prompt_tiles(prev, 1500, 200, 1)
 
 
 def test_long_prompt_rows_go_to_tile_ctas_at_the_end_of_the_grid(tile_knobs):
@@ -439,10 +439,10 @@ def test_tiles_on_any_grid_and_off(tile_knobs, n_ctas):
 
 
 def test_prefill_only_steps_split_long_tiles_over_the_grid(tile_knobs):
-    """A step of prompt rows alone spreads long tiles over the grid: tiles are
+    """With pieces allowed, a step of prompt rows alone spreads long tiles over the grid: tiles are
     cut over their keys into pieces of at least two chunks, every piece of a
     (tile, head) merged through the split-K scratch."""
-    tile_knobs(16, 600, 200)
+    tile_knobs(16, 600, 200, 8)
     tables = [list(range(64))]
     plan, layout = plan_step_host(16, 64, 12, tables, [0], [1024], None, 0, 148, MIN_SPLIT_CHUNKS)
     p = unpack(plan, layout)

@@ -59,7 +59,7 @@ SIGNATURES: dict[str, tuple] = {
                             c_int64, c_int64, _P, _P, c_int32, _P]),
     "tq_qkv_bias_kv_write": (c_int, [_P, c_int64, _P, c_int32, c_int64, _P, _P, c_int64, c_int32, c_int32,
                                      c_int32, c_int32, c_int32, _P, _P, c_int32, _P]),
-    "tq_plan_prompt_tiles": (c_int, [c_int32, c_int32, c_int32]),
+    "tq_plan_prompt_tiles": (c_int, [c_int32, c_int32, c_int32, c_int32]),
     "tq_paged_attention": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int32, c_int32, c_int32,
                                    c_int32, c_int32, _P, c_int32, _P, c_int32, c_int32, _P, _P, _P, c_int32,
                                    c_float, _P]),
@@ -146,11 +146,14 @@ def check(status: int, what: str) -> None:
     raise RuntimeError(f"{what} failed (status {status}): {msg}")
 
 
-def prompt_tiles(min_rows: int = -1, chunk_cost_pct: int = -1, item_cost_pct: int = -1) -> int:
+def prompt_tiles(min_rows: int = -1, chunk_cost_pct: int = -1, item_cost_pct: int = -1,
+                 max_pieces: int = -1) -> int:
     """Set the planner's prompt-tile knobs (tq_plan_prompt_tiles: sequences
     feeding at least ``min_rows`` tokens go to tensor-core tiles, 0 = never;
-    negative arguments keep the current value); returns the previous min_rows."""
-    return int(load().tq_plan_prompt_tiles(int(min_rows), int(chunk_cost_pct), int(item_cost_pct)))
+    a tile is cut into at most ``max_pieces`` pieces; negative arguments keep
+    the current value); returns the previous min_rows."""
+    return int(load().tq_plan_prompt_tiles(int(min_rows), int(chunk_cost_pct), int(item_cost_pct),
+                                           int(max_pieces)))
 
 
 def device_status(clear: bool = True) -> int:

@@ -67,6 +67,7 @@ constexpr int kTileMaxItems = 96;  // tile items one CTA holds (its shared-memor
 std::atomic<int> g_tile_min_rows{16};
 std::atomic<int> g_tile_chunk_cost{1500};
 std::atomic<int> g_tile_item_cost{200};
+std::atomic<int> g_tile_max_pieces{1};  // most pieces a tile is cut into (1: never cut)
 
 inline int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t align4(int64_t n) { return (n + 3) & ~int64_t(3); }
@@ -92,11 +93,13 @@ struct Piece {  // a run of chunks of a group's pairs (one per head), each bound
 
 }  // namespace
 
-extern "C" int tq_plan_prompt_tiles(int32_t min_rows, int32_t chunk_cost_pct, int32_t item_cost_pct) {
+extern "C" int tq_plan_prompt_tiles(int32_t min_rows, int32_t chunk_cost_pct, int32_t item_cost_pct,
+                                    int32_t max_pieces) {
   const int prev = g_tile_min_rows.load();
   if (min_rows >= 0) g_tile_min_rows.store(min_rows);
   if (chunk_cost_pct > 0) g_tile_chunk_cost.store(chunk_cost_pct);
   if (item_cost_pct >= 0) g_tile_item_cost.store(item_cost_pct);
+  if (max_pieces > 0) g_tile_max_pieces.store(max_pieces);
   return prev;
 }
 
@@ -129,6 +132,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   const int tile_min = g_tile_min_rows.load(std::memory_order_relaxed);
   const int64_t tile_chunk_cost = g_tile_chunk_cost.load(std::memory_order_relaxed);
   const int64_t tile_item_cost = g_tile_item_cost.load(std::memory_order_relaxed);
+  const int64_t tile_max_pieces = g_tile_max_pieces.load(std::memory_order_relaxed);
   std::vector<Tile> tiles;
   std::vector<char> tiled((size_t)num_seqs, 0);
   for (int b = 0; b < num_seqs; ++b) {
@@ -183,11 +187,13 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   // last n_tctas of the grid; the warp path below gets the first n_wctas.
   // The split follows the estimated loads -- a warp-path CTA's load is its
   // chunks (x 100); a tile item costs tile_chunk_cost per chunk plus
-  // tile_item_cost.  In a step of prompt rows alone, a tile whose item would
-  // cost more than the balanced load of a CTA is cut over its keys into pieces
-  // of at least two chunks, merged through the split-K scratch by the last
-  // piece to finish (not in plans of fixed capacity: the merge's fences and
-  // counter cost more than they save beside decode work, measured on B200).
+  // tile_item_cost.  With max_pieces > 1 (opt-in), in a step of prompt rows
+  // alone, a tile whose item would cost more than the balanced load of a CTA
+  // is cut over its keys into up to max_pieces pieces of at least two chunks,
+  // merged through the split-K scratch by the last piece to finish (never in
+  // plans of fixed capacity).  Off by default: each piece pays the item's
+  // start-up and the merge's fences and counter, which cost more than they
+  // save (four 256-row prompts: 14.6 us whole, 31-42 us cut, measured on B200).
   // The items go longest first to the least loaded tile
   // CTA.  A step whose tiles do not fit (a one-CTA grid beside warp work, or
   // more than kTileMaxItems on a CTA) runs every row on the warp path.
@@ -205,7 +211,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
       int64_t gn = 1;
       if (!caps && n_groups == 0) {
         gn = (int64_t)std::ceil((double)(t.nc * tile_chunk_cost + tile_item_cost) / std::max(balanced, 1.0));
-        gn = std::max<int64_t>(1, std::min<int64_t>(gn, t.nc / 2));
+        gn = std::max<int64_t>(1, std::min<int64_t>({gn, t.nc / 2, tile_max_pieces}));
       }
       for (int64_t sp = 0; sp < gn; ++sp)
         tpieces.push_back({(int32_t)i, (int32_t)(sp * t.nc / gn), (int32_t)((sp + 1) * t.nc / gn), (int32_t)sp,
