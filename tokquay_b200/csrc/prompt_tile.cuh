@@ -105,7 +105,11 @@ static_assert(2 * kAttnWarps * 32 == 384, "tile roles assume 12 warps");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemQ = 0, kTmemS = 128, kTmemO = 320;
 constexpr uint32_t kTmemP = kTmemS;  // P hi (+32: P lo) over S of the same buffer
-constexpr float kTileRescale = 8.f;  // log2 units a row's maximum may pass its reference by
+constexpr float kTileRescale = 8.f;
+#ifndef TQ_TILE_FAST_WAIT_SLEEP
+#define TQ_TILE_FAST_WAIT_SLEEP 0
+#endif
+constexpr bool kTileFastWaitSleep = TQ_TILE_FAST_WAIT_SLEEP;  // row threads' and MMA issuers' waits  // log2 units a row's maximum may pass its reference by
 
 // Instruction descriptors (kind::tf32, fp32 accumulator, M = 128, both
 // operands K-major): bits 4-5 D format (1 = f32), 7-9 A format (2 = tf32),
@@ -232,7 +236,8 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 
 // tile_wait for a whole (converged) warp: the outcome is the same in every
 // lane, so the warp leaves its loops together.
-__device__ __forceinline__ bool tile_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag);
+__device__ __forceinline__ bool tile_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                               bool sleep = true);
 
 // One arrival for the whole warp, once every lane's earlier tcgen05 stores
 // (waited for) are ordered before it.
@@ -249,10 +254,15 @@ __device__ __forceinline__ float fast_exp2(float x) {  // ex2.approx.ftz: exp2(-
 }
 
 // Bounded wait that also gives up once another role has aborted the CTA.
-__device__ __forceinline__ bool tile_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait_sleep(bar, parity)) return true;
+// sleep: let the thread sleep until the phase completes (warps whose wake-up
+// latency does not sit on the chunk's critical path: producer, converters);
+// otherwise poll (row threads, MMA issuers).
+__device__ __forceinline__ bool tile_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          bool sleep = true) {
+  auto probe = [&]() { return sleep ? mbar_try_wait_sleep(bar, parity) : mbar_try_wait(bar, parity); };
+  if (probe()) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait_sleep(bar, parity)) {
+  while (!probe()) {
     if (*abort_flag) return false;
     if (clock64() - t0 > kWaitLimitCycles) {
       raise_device_error(TQ_DEVERR_WAIT_TIMEOUT);
@@ -263,8 +273,9 @@ __device__ __forceinline__ bool tile_wait(uint32_t bar, uint32_t parity, volatil
   return true;
 }
 
-__device__ __forceinline__ bool tile_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-  return __all_sync(kFullMask, tile_wait(bar, parity, abort_flag));
+__device__ __forceinline__ bool tile_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                               bool sleep) {
+  return __all_sync(kFullMask, tile_wait(bar, parity, abort_flag, sleep));
 }
 
 // Row t's q row of head h (zeros for rows past the item), copied into the
@@ -480,7 +491,7 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
       float m = -INFINITY, l = 0.f;
       for (int c = it.cbeg(); c < it.cend() && ok; ++c, ++g) {
         const int b = g % kTileSP;
-        ok = tile_wait_warp(bar(kTileBarSFull + b), (uint32_t)(g / kTileSP) & 1u, abort_flag);
+        ok = tile_wait_warp(bar(kTileBarSFull + b), (uint32_t)(g / kTileSP) & 1u, abort_flag, kTileFastWaitSleep);
         if (!ok) break;
         if (t == 0) TQ_TILE_TR(6, g);
         tc_fence_after();
@@ -529,7 +540,7 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
           // Rescale the accumulator (every PV issued so far has completed)
           // before this chunk's PV adds to it.
           const int pg = g - 1;
-          if (!(ok = tile_wait_warp(bar(kTileBarOFull + pg % kTileSP), (uint32_t)(pg / kTileSP) & 1u, abort_flag))) break;
+          if (!(ok = tile_wait_warp(bar(kTileBarOFull + pg % kTileSP), (uint32_t)(pg / kTileSP) & 1u, abort_flag, kTileFastWaitSleep))) break;
           tc_fence_after();
           tile_scale_o(o_col, factor);
           waited = true;
@@ -538,14 +549,14 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
         if (t == 0) TQ_TILE_TR(7, g);
         if (!waited) {  // chunk g-1's PV: consumed, so the barrier's phases stay in step
           const int pg = g - 1;
-          if (!(ok = tile_wait_warp(bar(kTileBarOFull + pg % kTileSP), (uint32_t)(pg / kTileSP) & 1u, abort_flag))) break;
+          if (!(ok = tile_wait_warp(bar(kTileBarOFull + pg % kTileSP), (uint32_t)(pg / kTileSP) & 1u, abort_flag, kTileFastWaitSleep))) break;
           if (t == 0) TQ_TILE_TR(8, pg);
         }
       }
       if (!ok) break;
       {  // the last chunk's PV completes the accumulator
         const int pg = g - 1;
-        if (!(ok = tile_wait_warp(bar(kTileBarOFull + pg % kTileSP), (uint32_t)(pg / kTileSP) & 1u, abort_flag))) break;
+        if (!(ok = tile_wait_warp(bar(kTileBarOFull + pg % kTileSP), (uint32_t)(pg / kTileSP) & 1u, abort_flag, kTileFastWaitSleep))) break;
         if (t == 0) TQ_TILE_TR(13, k);
         tc_fence_after();
       }
@@ -597,14 +608,14 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kTileBarRowsDone));
       if (t == 0) {
-        const bool seen = tile_wait(bar(kTileBarRowsDone), (uint32_t)splits_done & 1u, abort_flag);
+        const bool seen = tile_wait(bar(kTileBarRowsDone), (uint32_t)splits_done & 1u, abort_flag, kTileFastWaitSleep);
         int old = 0;
         if (seen)
           asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.part_cnt + it.gbase()) : "memory");
         misc[2] = seen && old == it.gnsplit() - 1;
         mbar_arrive(bar(kTileBarMergeGo));
       }
-      if (!(ok = tile_wait_warp(bar(kTileBarMergeGo), (uint32_t)splits_done & 1u, abort_flag))) break;
+      if (!(ok = tile_wait_warp(bar(kTileBarMergeGo), (uint32_t)splits_done & 1u, abort_flag, kTileFastWaitSleep))) break;
       ++splits_done;
       if (!misc[2]) continue;
       __threadfence();
@@ -646,14 +657,14 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
     bool ok = true;
     for (int k = 0; k < count && ok; ++k) {
       const WorkItem& it = items[k];
-      if (!(ok = tile_wait_warp(bar(kTileBarQReady), (uint32_t)k & 1u, abort_flag))) break;
+      if (!(ok = tile_wait_warp(bar(kTileBarQReady), (uint32_t)k & 1u, abort_flag, kTileFastWaitSleep))) break;
       for (int c = it.cbeg(); c < it.cend(); ++c, ++g) {
         if (!(ok = tile_wait_warp(bar(kTileBarKvReady + g % kTileKVBufs), (uint32_t)(g / kTileKVBufs) & 1u,
                                   abort_flag)))
           break;
         TQ_TILE_TR(3, g);
         if (g >= kTileSP &&
-            !(ok = tile_wait_warp(bar(kTileBarOFull + g % kTileSP), (uint32_t)(g / kTileSP - 1) & 1u, abort_flag)))
+            !(ok = tile_wait_warp(bar(kTileBarOFull + g % kTileSP), (uint32_t)(g / kTileSP - 1) & 1u, abort_flag, kTileFastWaitSleep)))
           break;
         tc_fence_after();
         TQ_TILE_TR(9, g);
@@ -674,7 +685,7 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
     for (int k = 0; k < count && ok; ++k) {
       const WorkItem& it = items[k];
       for (int c = it.cbeg(); c < it.cend(); ++c, ++g) {
-        if (!(ok = tile_wait_warp(bar(kTileBarPFull + g % kTileSP), (uint32_t)(g / kTileSP) & 1u, abort_flag))) break;
+        if (!(ok = tile_wait_warp(bar(kTileBarPFull + g % kTileSP), (uint32_t)(g / kTileSP) & 1u, abort_flag, kTileFastWaitSleep))) break;
         TQ_TILE_TR(4, g);
         tc_fence_after();
         tile_issue_pv(tmem, kv0, g, k, c == it.cbeg());
@@ -804,6 +815,10 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
                        : "=f"(x[i].x), "=f"(x[i].y), "=f"(x[i].z), "=f"(x[i].w)
                        : "r"(rs + (uint32_t)((u >> 4) * kTileOpBytes + j * kRowBytes + m * 16)));
       }
+      // The raw stage is read (the arrive's release orders the loads before
+      // it): the producer may refill it while this chunk is split.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kTileBarRawEmpty + st));
 #pragma unroll
       for (int i = 0; i < kTileUnitsPerThread; ++i) {
         const int u = cw + kTileCvtWarps * i;
@@ -839,10 +854,7 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
       fence_proxy_async_smem();  // the split halves are read by the tensor core
       if (kk == 0 && f4 == 0 && cw == 0) TQ_TILE_TR(12, g);
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(bar(kTileBarKvReady + b));
-        mbar_arrive(bar(kTileBarRawEmpty + st));
-      }
+      if (lane == 0) mbar_arrive(bar(kTileBarKvReady + b));
       if (kk == 0 && f4 == 0 && cw == 0) TQ_TILE_TR(2, g);
       tile_advance(cur, items, count);
     }
