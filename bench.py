@@ -1431,6 +1431,9 @@ def main():
     ap.add_argument("--prompt-tile-rows", type=int, default=-1,
                     help="least prompt chunk (rows) run as tensor-core tiles; 0 = every prompt row on warp "
                          "items; default: the library's")
+    ap.add_argument("--prompt-tile-pieces", type=int, default=-1,
+                    help="most pieces a costly prompt tile is cut into over its keys (merged by a second "
+                         "kernel after the attention grid); 1 = never cut; default: the library's")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")
@@ -1462,11 +1465,15 @@ def main():
     _load_library()
     if args.prompt_tile_rows >= 0:
         _lib.prompt_tiles(args.prompt_tile_rows)
+    if args.prompt_tile_pieces > 0:
+        _lib.prompt_tiles(-1, -1, -1, args.prompt_tile_pieces)
     tile_rows = _lib.prompt_tiles()  # (reads the setting)
 
     def tagged(res):  # the line names the prompt-tile setting it ran with
         if res is not None and isinstance(res.get("config"), dict):
             res["config"]["prompt_tile_min_rows"] = tile_rows
+            if args.prompt_tile_pieces > 0:
+                res["config"]["prompt_tile_max_pieces"] = args.prompt_tile_pieces
         return res
 
     if args.workload == "cfg5":

@@ -55,7 +55,7 @@
 extern "C" {
 #endif
 
-#define TQ_ABI_VERSION 7
+#define TQ_ABI_VERSION 8
 
 enum tq_status {
   TQ_OK = 0,
@@ -87,12 +87,17 @@ enum tq_plan_layout {
   TQ_PLAN_OFF_ITEMS = 16,    /* the attention plan (tq_paged_attention's attn_plan), last region:
                                 [W][16] each warp's first work item and the block ids of its first
                                 chunk (-1 past them), [W+1] (padded to 8) offsets of the other
-                                items, then those items [..][8], W = num_ctas * warps */
+                                items, then those items [..][8], W = num_ctas * warps, then
+                                the tile-merge trailer: [8] (word 0: TQ_PLAN_NUM_TILE_MERGES),
+                                [num_tile_merges][4] {row, partial of head 0, pieces, partials
+                                between heads} */
   TQ_PLAN_OFF_COMBINE = 17,  /* [num_combine][4] rows whose keys are split across CTAs */
   TQ_PLAN_NUM_CTAS = 18,     /* CTAs the attention plan is cut for (its launch grid) */
   TQ_PLAN_USED_INTS = 19,    /* leading int32 of the plan this step uses (what must be copied) */
   TQ_PLAN_NUM_TILE_CTAS = 20,/* CTAs of the grid that run prompt tiles (tq_plan_prompt_tiles) */
-  TQ_PLAN_LAYOUT_LEN = 21
+  TQ_PLAN_NUM_TILE_MERGES = 21,/* rows of prompt tiles cut over their keys: merged after the
+                                attention grid (tq_paged_attention with TQ_ATTN_TILE_MERGE) */
+  TQ_PLAN_LAYOUT_LEN = 22
 };
 
 TQ_API int tq_abi_version(void);
@@ -149,10 +154,12 @@ TQ_API int tq_device_status(int clear, int32_t* bits);
  * halves).  Tile items run on the last CTAs of the grid; how many is set by
  * the estimated loads: a tile item costs chunk_cost_pct percent of a warp-path
  * 32-key chunk per chunk, plus item_cost_pct.  min_rows 0 turns tiles off.
- * max_pieces > 1 lets a step of prompt rows alone cut a long tile over its keys
- * into up to that many pieces on different CTAs, merged through the split-K
- * scratch (slower than whole tiles on B200: off by default).  Arguments below
- * 0 (chunk_cost_pct, max_pieces: <= 0) keep the current value.  The setting is
+ * max_pieces > 1 lets a plan without fixed capacities cut a tile whose item
+ * would cost more than a CTA's balanced load over its keys, into up to that
+ * many pieces of at least two chunks on different CTAs; each piece leaves its
+ * partials in the split-K scratch and a merge kernel after the attention grid
+ * combines them (TQ_PLAN_NUM_TILE_MERGES rows).  Arguments below 0
+ * (chunk_cost_pct, max_pieces: <= 0) keep the current value.  The setting is
  * process-wide and read by each tq_plan_step call; defaults 16, 1500, 200, 1.
  * Returns the previous min_rows. */
 TQ_API int tq_plan_prompt_tiles(int32_t min_rows, int32_t chunk_cost_pct, int32_t item_cost_pct,
@@ -203,17 +210,21 @@ TQ_API int tq_qkv_bias_kv_write(float* q_out, int64_t q_row_stride, const float*
  * plan launched with it (max_partials; NULL scratch is fine when it is 0).
  * Launches that share scratch must not overlap on the GPU.  attn_plan is the
  * plan's attention region (TQ_PLAN_OFF_ITEMS) and n_ctas its TQ_PLAN_NUM_CTAS,
- * the launch grid.  with_tiles must be nonzero when the plan may hold prompt
- * tiles (TQ_PLAN_NUM_TILE_CTAS > 0; for a launch captured once and replayed
- * over plans of fixed capacities: when any of them may) -- it selects the
- * kernel that carries the tile role; 0 selects the leaner one, which flags
- * (device error 16) and skips any tile item it is given.  One kernel launch on `stream`; every merge of split keys
- * happens inside it.  The launch is a programmatic dependent of the kernel
+ * the launch grid.  with_tiles must hold TQ_ATTN_TILES when the plan may hold
+ * prompt tiles (TQ_PLAN_NUM_TILE_CTAS > 0; for a launch captured once and
+ * replayed over plans of fixed capacities: when any of them may) -- it selects
+ * the kernel that carries the tile role; 0 selects the leaner one, which flags
+ * (device error 16) and skips any tile item it is given.  TQ_ATTN_TILES |
+ * TQ_ATTN_TILE_MERGE when the plan also cuts tiles over their keys
+ * (TQ_PLAN_NUM_TILE_MERGES > 0): a second kernel then merges their pieces,
+ * as a programmatic dependent of the first.  Otherwise one kernel launch on
+ * `stream`, and every merge of split keys happens inside it.  The launch is a programmatic dependent of the kernel
  * before it on `stream`: for a sequence that feeds one token this step, the
  * pool rows of its earlier positions (0 .. position-1) may be read before
  * that kernel has finished, so that kernel may write this step's new K/V
  * rows (tq_kv_write, tq_qkv_bias_kv_write) and q, but no other pool row;
  * everything else is read, and every output written, after it completes. */
+enum tq_attn_tiles { TQ_ATTN_TILES = 1, TQ_ATTN_TILE_MERGE = 2 };
 TQ_API int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64_t q_row_stride,
                        const float* pool, int64_t num_blocks, int32_t n_layer, int32_t n_head,
                        int32_t block_size, int32_t head_dim, int32_t layer,
@@ -233,8 +244,9 @@ TQ_API int tq_paged_attention(float* out, int64_t out_row_stride, const float* q
  * over scratch: a host runtime that passes this library only the tensors it
  * already owns (a serving process held to a fixed memory budget, an embedding
  * without its own device allocator).  Same arguments and result as
- * tq_paged_attention, minus the scratch pointers; num_partials is the plan's
- * TQ_PLAN_NUM_PARTIALS.  The split-K scratch is a library-owned array, so the
+ * tq_paged_attention, minus the scratch pointers and with_tiles (it launches
+ * the tile-capable kernel and the tile merge for any plan); num_partials is
+ * the plan's TQ_PLAN_NUM_PARTIALS.  The split-K scratch is a library-owned array, so the
  * call allocates nothing; a plan needing more than TQ_NOALLOC_MAX_PARTIALS
  * partials is rejected with TQ_ERR_CAPACITY before anything is launched.
  * The first call on a device looks the array's address up

@@ -424,15 +424,16 @@ def tile_knobs():
 
 
 @pytest.mark.parametrize("bs", [4, 16, 64])
-@pytest.mark.parametrize("shape", ["prefill_split", "beside_decode", "tiles_off"])
+@pytest.mark.parametrize("shape", ["prefill_split", "beside_decode", "decode_split", "tiles_off"])
 def test_prompt_tiles_match_float64_reference(bs, shape, tile_knobs):
     """Long prompt chunks (cached prefixes of 0-600 keys, 100-256 rows) on the
-    tensor-core tiles: prompt rows alone (long tiles cut into pieces merged
-    through the split-K scratch), the same beside a decode row (whole tiles),
-    and with tiles off (2-row warp items) -- every row against float64, with
-    pieces allowed for the first shape (off by default),
-    NaN in every slot past each context."""
-    tile_knobs(0 if shape == "tiles_off" else 16, 1500, 200, 8 if shape == "prefill_split" else 1)
+    tensor-core tiles: prompt rows alone (long tiles cut into pieces whose
+    partials the merge kernel combines after the grid), the same beside a
+    decode row (whole tiles, and cut into pieces), and with tiles off (2-row
+    warp items) -- every row against float64, NaN in every slot past each
+    context."""
+    pieces = {"prefill_split": 8, "decode_split": 4}.get(shape, 1)
+    tile_knobs(0 if shape == "tiles_off" else 16, 1500, 200, pieces)
     rng = random.Random(bs)
     cfg = GPT2Config(vocab_size=64, n_positions=1024, n_embd=768, n_layer=1, n_head=12)
     alloc = BlockAllocator(cfg, 4 * cdiv(1024, bs) + 8, bs, device="cuda")
@@ -444,7 +445,7 @@ def test_prompt_tiles_match_float64_reference(bs, shape, tile_knobs):
         tables.append(alloc._take(cdiv(s + n, bs)))
         start.append(s)
         new.append(n)
-    if shape == "beside_decode":
+    if shape in ("beside_decode", "decode_split"):
         c = rng.randint(100, 700)
         tables.append(alloc._take(cdiv(c, bs)))
         start.append(c - 1)
@@ -464,13 +465,13 @@ def test_prompt_tiles_match_float64_reference(bs, shape, tile_knobs):
     if shape == "tiles_off":
         assert n_tile == 0
     elif shape == "beside_decode":
-        assert n_tile > 0 and n_split == 0
+        assert n_tile > 0 and n_split == 0 and batch.tile_merges == 0
     else:
-        assert n_split > 0
+        assert n_split > 0 and batch.tile_merges > 0
     C = cfg.n_embd
     qkv = torch.randn(batch.N, 3 * C, device="cuda", generator=g)
     out = torch.full((batch.N, C), float("nan"), device="cuda")
-    for _ in range(2):  # twice: the split-K counters are left at zero for the next launch
+    for _ in range(2):  # twice: the scratch (counters at zero) serves the next launch
         batch.attend_rows(0, qkv, out, _stream())
         torch.cuda.synchronize()
         want = _reference_attention(alloc.pool, 0, qkv[:, :C], tables, start, new, bs)

@@ -78,7 +78,14 @@ def unpack(plan, layout):
         return np.asarray(plan[o:o + n])
 
     warps = attention_lists(plan, layout)
+    # The tile-merge trailer after the attention items: [8] (word 0: rows), then [rows][4].
+    nw = int(L[_lib.PLAN_NUM_CTAS]) * attention_warps()
+    o = int(L[_lib.PLAN_OFF_ITEMS])
+    t0 = o + FIRST_WORDS * nw + (nw + 1 + 7) // 8 * 8 + 8 * int(plan[o + FIRST_WORDS * nw + nw])
+    n_merges = int(plan[t0])
+    assert n_merges == L[_lib.PLAN_NUM_TILE_MERGES] and not np.asarray(plan[t0 + 1:t0 + 8]).any()
     return dict(
+        merges=np.asarray(plan[t0 + 8:t0 + 8 + 4 * n_merges]).reshape(n_merges, 4),
         B=B, N=N, stride=stride,
         counts=v(_lib.PLAN_OFF_COUNTS, 4),
         seq=v(_lib.PLAN_OFF_SEQ_INFO, 4 * B).reshape(B, 4),
@@ -213,6 +220,21 @@ def check_merges(p):
         idx = {it["gbase"] + r * n + s for r in range(it["nrows"]) for s in range(n)}
         assert max(idx) < p["n_partials"] and min(idx) >= 0 and not (idx & used_parts)
         used_parts |= idx
+    # Split tiles are merged after the grid: one trailer entry per row, whose
+    # partials (head h at + h * its head stride) are the pieces' of that row.
+    merges = {int(e[0]): e for e in p["merges"]}
+    assert len(merges) == len(p["merges"])
+    tile_rows = set()
+    for (row0, h), g in global_parts.items():
+        it = g["item"]
+        if not it["tile"]:
+            continue
+        n = it["gnsplit"]
+        for r in range(it["nrows"]):
+            e = merges[row0 + r]
+            tile_rows.add(row0 + r)
+            assert e[2] == n and e[3] == it["nrows"] * n and e[1] + h * e[3] == it["gbase"] + r * n, (row0, r, h)
+    assert tile_rows == set(merges)
 
 
 @pytest.mark.parametrize("bs", [1, 2, 4, 16, 32, 64, 256])
@@ -258,7 +280,8 @@ def test_plan_matches_oracle_and_covers_every_key_once(bs, seed):
     o = int(layout[_lib.PLAN_OFF_ITEMS])
     nw = n_ctas * attention_warps()
     n_rest = int(plan[o + FIRST_WORDS * nw + nw])
-    assert layout[_lib.PLAN_USED_INTS] == o + FIRST_WORDS * nw + (nw + 8) // 8 * 8 + 8 * n_rest
+    trailer = 8 + (4 * len(p["merges"]) + 7) // 8 * 8
+    assert layout[_lib.PLAN_USED_INTS] == o + FIRST_WORDS * nw + (nw + 8) // 8 * 8 + 8 * n_rest + trailer
     assert layout[_lib.PLAN_USED_INTS] <= layout[_lib.PLAN_TOTAL_INTS] == plan.size
 
 
@@ -449,9 +472,48 @@ def test_prefill_only_steps_split_long_tiles_over_the_grid(tile_knobs):
     tiles = [it for it in p["items"] if it["tile"]]
     assert len(tiles) > 8 * 12 and any(it["flags"] == 2 for it in tiles)
     assert all(it["cend"] - it["cbeg"] >= 2 for it in tiles)
-    assert layout[_lib.PLAN_NUM_PARTIALS] > 0 and len(p["combine"]) > 0
+    assert layout[_lib.PLAN_NUM_PARTIALS] > 0 and len(p["combine"]) > 0 and len(p["merges"]) > 0
     seen = simulate_copies(p, 16, 64)
     for r in range(p["N"]):
         for h in range(12):
             assert sorted(seen[(r, h)]) == list(range(int(p["pos"][r]) + 1)), (r, h)
+    check_merges(p)
+
+
+def test_long_tiles_beside_decodes_split_with_a_merge_after_the_grid(tile_knobs):
+    """With pieces allowed, a mixed step cuts its costliest tiles over their
+    keys beside the decode items; the trailer lists every row of a cut tile
+    once, and plans of fixed capacities never cut a tile."""
+    tile_knobs(16, 1500, 200, 4)
+    rng = random.Random(3)
+    bs, num_blocks = 16, 2048
+    free = list(range(num_blocks))
+    rng.shuffle(free)
+    tables, start, new = [], [], []
+    for n in (75, 236, 32, 170):
+        tables.append([free.pop() for _ in range(cdiv(n, bs))])
+        start.append(0)
+        new.append(n)
+    for _ in range(60):
+        c = rng.randint(16, 256)
+        tables.append([free.pop() for _ in range(cdiv(c, bs))])
+        start.append(c - 1)
+        new.append(1)
+    plan, layout = plan_step_host(bs, num_blocks, 12, tables, start, new, None, 0, 148, MIN_SPLIT_CHUNKS)
+    p = unpack(plan, layout)
+    tiles = [it for it in p["items"] if it["tile"]]
+    cut = [it for it in tiles if it["flags"] == 2]
+    assert cut and all(it["cend"] - it["cbeg"] >= 2 for it in cut)
+    assert max(it["cend"] - it["cbeg"] for it in tiles) < 8  # the 8-chunk tile is cut
+    assert len(p["merges"]) == layout[_lib.PLAN_NUM_TILE_MERGES] > 0
+    seen = simulate_copies(p, bs, num_blocks)
+    for r in range(p["N"]):
+        for h in range(12):
+            assert sorted(seen[(r, h)]) == list(range(int(p["pos"][r]) + 1)), (r, h)
+    check_merges(p)
+    # The same step planned for fixed capacities keeps its tiles whole.
+    caps = np.array([64, 1024, 64, 20000, 4096, 20000], np.int32)
+    plan, layout = plan_step_host(bs, num_blocks, 12, tables, start, new, None, 0, 148, MIN_SPLIT_CHUNKS, caps=caps)
+    p = unpack(plan, layout)
+    assert layout[_lib.PLAN_NUM_TILE_MERGES] == 0 and not [it for it in p["items"] if it["tile"] and it["flags"]]
     check_merges(p)

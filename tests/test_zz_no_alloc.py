@@ -92,3 +92,38 @@ def test_noalloc_refuses_a_plan_beyond_its_scratch():
     torch.cuda.synchronize()
     assert torch.count_nonzero(out) == 0  # refused before anything ran
     assert _lib.device_status() == 0
+
+
+def test_noalloc_merges_split_prompt_tiles():
+    """A plan whose prompt tiles are cut over their keys: the no-allocation
+    entry point merges their pieces after the grid, as the allocating one does."""
+    prev = _lib.prompt_tiles()
+    try:
+        _lib.prompt_tiles(16, 1500, 200, 4)
+        cfg = GPT2Config(vocab_size=64, n_positions=1024, n_embd=768, n_layer=1, n_head=12)
+        bs = 16
+        rng = random.Random(5)
+        alloc = BlockAllocator(cfg, 6 * 64, bs, device="cuda")
+        random.Random(5).shuffle(alloc._free)
+        alloc.pool.normal_(generator=torch.Generator(device="cuda").manual_seed(5))
+        tables, start, new = [], [], []
+        for s, n in ((0, 236), (rng.randint(100, 400), 170)) + tuple((rng.randint(16, 500), 1) for _ in range(8)):
+            tables.append(alloc._take(cdiv(s + n, bs)))
+            start.append(s)
+            new.append(n)
+        batch = DevicePagedBatch(alloc, tables, start, new)
+        assert batch.tile_merges > 0 and 0 < batch.num_partials <= _lib.NOALLOC_MAX_PARTIALS
+        C = cfg.n_embd
+        stream = torch.cuda.current_stream().cuda_stream
+        qkv = torch.randn(batch.N, 3 * C, device="cuda", generator=torch.Generator(device="cuda").manual_seed(6))
+        want = torch.full((batch.N, C), float("nan"), device="cuda")
+        batch.attend_rows(0, qkv, want, stream)
+        got = torch.full((batch.N, C), float("nan"), device="cuda")
+        _lib.check(_noalloc(batch, 0, qkv, got, batch.num_partials), "tq_paged_attention_noalloc")
+        torch.cuda.synchronize()
+        assert torch.isfinite(want).all() and torch.isfinite(got).all()
+        err = (got - want).abs().max().item()
+        assert err <= ATTN_RTOL * want.abs().max().item(), err
+        assert _lib.device_status() == 0
+    finally:
+        _lib.prompt_tiles(prev, 1500, 200, 1)

@@ -43,7 +43,12 @@ PLAN_OFF_COMBINE = 17
 PLAN_NUM_CTAS = 18
 PLAN_USED_INTS = 19
 PLAN_NUM_TILE_CTAS = 20
-PLAN_LAYOUT_LEN = 21
+PLAN_NUM_TILE_MERGES = 21
+PLAN_LAYOUT_LEN = 22
+
+# tq_paged_attention's with_tiles bits (enum tq_attn_tiles).
+ATTN_TILES = 1
+ATTN_TILE_MERGE = 2
 
 # Symbols the header declares, with (restype, argtypes).
 _P = c_void_p
@@ -77,7 +82,7 @@ SIGNATURES: dict[str, tuple] = {
                                   _P, _P, c_int32, _P]),
 }
 
-EXPECTED_ABI = 7
+EXPECTED_ABI = 8
 
 # tq_lm_head_argmax limits (TQ_LM_HEAD_* in include/tokquay_b200.h).
 LM_HEAD_MAX_ROWS = 64

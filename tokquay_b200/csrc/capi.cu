@@ -55,7 +55,7 @@ int device_setup(int* sm_count) {
                              kAttnSmemBytes);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(paged_attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kAttnSmemBytes);
+                               kTileLaunchSmemBytes);
     if (e != cudaSuccess)
       return set_error(TQ_ERR_CUDA, "cudaFuncSetAttribute(paged_attention): %s",
                        cudaGetErrorString(e));
@@ -167,19 +167,29 @@ int attention_params(float* out, int64_t out_row_stride, const float* q, int64_t
 // in the stream: its CTAs may start (barriers, work items, block ids, and for
 // decode items the K/V rows before the new key) while that kernel finishes;
 // everything else waits for it.
-cudaError_t launch_attention(const AttnParams& p, int n_ctas, bool with_tiles, cudaStream_t stream) {
+cudaError_t launch_attention(const AttnParams& p, int n_ctas, bool with_tiles, bool tile_merge,
+                             cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(n_ctas);
   cfg.blockDim = dim3(kAttnThreads);
-  cfg.dynamicSmemBytes = kAttnSmemBytes;
+  cfg.dynamicSmemBytes = with_tiles ? kTileLaunchSmemBytes : kAttnSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return with_tiles ? cudaLaunchKernelEx(&cfg, paged_attention_kernel<true>, p)
-                    : cudaLaunchKernelEx(&cfg, paged_attention_kernel<false>, p);
+  cudaError_t e = with_tiles ? cudaLaunchKernelEx(&cfg, paged_attention_kernel<true>, p)
+                             : cudaLaunchKernelEx(&cfg, paged_attention_kernel<false>, p);
+  if (e != cudaSuccess || !tile_merge) return e;
+  // The pieces of split prompt tiles, merged once the attention grid is done
+  // (the merge kernel's CTAs may be placed while it drains).
+  int sms = 0;
+  if (device_setup(&sms) != TQ_OK) return cudaErrorUnknown;
+  cfg.gridDim = dim3(sms);
+  cfg.blockDim = dim3(kMergeThreads);
+  cfg.dynamicSmemBytes = 0;
+  return cudaLaunchKernelEx(&cfg, tile_merge_kernel, p);
 }
 
 int check_embd(int32_t n_embd) {
@@ -350,7 +360,10 @@ int tq_paged_attention(float* out, int64_t out_row_stride, const float* q, int64
   p.part_acc = partial_acc;
   p.part_cnt = partial_counters;
   p.max_partials = max_partials;
-  const cudaError_t e = launch_attention(p, n_ctas, with_tiles != 0, (cudaStream_t)stream);
+  if (with_tiles & ~(TQ_ATTN_TILES | TQ_ATTN_TILE_MERGE) || (with_tiles & TQ_ATTN_TILE_MERGE && !(with_tiles & TQ_ATTN_TILES)))
+    return set_error(TQ_ERR_INVALID, "with_tiles must be 0, TQ_ATTN_TILES or TQ_ATTN_TILES | TQ_ATTN_TILE_MERGE");
+  const cudaError_t e = launch_attention(p, n_ctas, with_tiles & TQ_ATTN_TILES,
+                                         (with_tiles & TQ_ATTN_TILE_MERGE) != 0, (cudaStream_t)stream);
   if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "paged_attention launch: %s", cudaGetErrorString(e));
   return check_launch("paged_attention");
 }
@@ -441,7 +454,9 @@ int tq_paged_attention_noalloc(float* out, int64_t out_row_stride, const float* 
   p.part_ml = reinterpret_cast<float*>(base + kNoAllocCounterBytes);
   p.part_acc = reinterpret_cast<float*>(base + kNoAllocCounterBytes + kNoAllocMlBytes);
   p.max_partials = num_partials;
-  const cudaError_t e = launch_attention(p, n_ctas, true, s);  // any plan: the variant with tiles
+  // Any plan: the variant with tiles, and the merge of split tiles (a plan
+  // without split tiles gives it no work).
+  const cudaError_t e = launch_attention(p, n_ctas, true, true, s);
   if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "paged_attention launch: %s", cudaGetErrorString(e));
   return check_launch("paged_attention_noalloc");
 }

@@ -187,13 +187,12 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   // last n_tctas of the grid; the warp path below gets the first n_wctas.
   // The split follows the estimated loads -- a warp-path CTA's load is its
   // chunks (x 100); a tile item costs tile_chunk_cost per chunk plus
-  // tile_item_cost.  With max_pieces > 1 (opt-in), in a step of prompt rows
-  // alone, a tile whose item would cost more than the balanced load of a CTA
-  // is cut over its keys into up to max_pieces pieces of at least two chunks,
-  // merged through the split-K scratch by the last piece to finish (never in
-  // plans of fixed capacity).  Off by default: each piece pays the item's
-  // start-up and the merge's fences and counter, which cost more than they
-  // save (four 256-row prompts: 14.6 us whole, 31-42 us cut, measured on B200).
+  // tile_item_cost.  With max_pieces > 1, a tile whose item would cost more
+  // than the balanced load of a CTA is cut over its keys into up to
+  // max_pieces pieces of at least two chunks (never in plans of fixed
+  // capacity).  Each piece leaves its partials in the split-K scratch, and
+  // the merge kernel after the attention grid combines them (the entries of
+  // the tile-merge trailer).
   // The items go longest first to the least loaded tile
   // CTA.  A step whose tiles do not fit (a one-CTA grid beside warp work, or
   // more than kTileMaxItems on a CTA) runs every row on the warp path.
@@ -202,17 +201,43 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   std::vector<std::vector<int32_t>> tile_lists;  // per tile CTA: items (piece * n_head + head)
   int64_t tile_partials = 0, tile_combine = 0;
   if (!tiles.empty()) {
-    int64_t tile_load = 0;
-    for (const Tile& t : tiles) tile_load += (t.nc * tile_chunk_cost + tile_item_cost) * n_head;
     const int64_t warp_load = total_chunks * n_head * 100;
-    const double balanced = (double)(tile_load + warp_load) / n_ctas;
+    const int64_t max_tctas0 = n_groups == 0 ? n_ctas : n_ctas - 1;
+    // Tile CTAs for a given tile load: the grid's share of the estimated work.
+    auto tile_ctas_for = [&](int64_t tile_load) {
+      if (n_groups == 0) return max_tctas0;
+      return std::min<int64_t>(max_tctas0, std::max<int64_t>(1, (int64_t)((double)n_ctas * tile_load /
+                                                                            (double)(tile_load + warp_load) + 0.5)));
+    };
+    // Pieces per tile: one, then (plans without fixed capacities) one more for
+    // the tile with the costliest piece, while that piece costs more than a
+    // CTA's balanced load and every tile item still gets a CTA of its own.
+    std::vector<int64_t> gns(tiles.size(), 1);
+    for (;;) {
+      int64_t tile_load = 0, n_pieces = 0;
+      for (size_t i = 0; i < tiles.size(); ++i) {
+        tile_load += (tiles[i].nc * tile_chunk_cost + gns[i] * tile_item_cost) * n_head;
+        n_pieces += gns[i];
+      }
+      if (caps || tile_max_pieces < 2) break;
+      const double balanced = (double)(tile_load + warp_load) / n_ctas;
+      int64_t best = -1;
+      double best_cost = 0.0;
+      for (size_t i = 0; i < tiles.size(); ++i) {
+        const double c = (double)cdiv64(tiles[i].nc, gns[i]) * tile_chunk_cost + tile_item_cost;
+        if (gns[i] < std::min<int64_t>(tile_max_pieces, tiles[i].nc / 2) && c > best_cost) {
+          best = (int64_t)i;
+          best_cost = c;
+        }
+      }
+      if (best < 0 || best_cost <= balanced) break;
+      const int64_t more = tile_load + (tile_item_cost * n_head);
+      if ((n_pieces + 1) * n_head > tile_ctas_for(more)) break;
+      ++gns[(size_t)best];
+    }
     for (size_t i = 0; i < tiles.size(); ++i) {
       const Tile& t = tiles[i];
-      int64_t gn = 1;
-      if (!caps && n_groups == 0) {
-        gn = (int64_t)std::ceil((double)(t.nc * tile_chunk_cost + tile_item_cost) / std::max(balanced, 1.0));
-        gn = std::max<int64_t>(1, std::min<int64_t>({gn, t.nc / 2, tile_max_pieces}));
-      }
+      const int64_t gn = gns[i];
       for (int64_t sp = 0; sp < gn; ++sp)
         tpieces.push_back({(int32_t)i, (int32_t)(sp * t.nc / gn), (int32_t)((sp + 1) * t.nc / gn), (int32_t)sp,
                            (int32_t)gn, gn > 1 ? tile_partials : -1});
@@ -222,17 +247,14 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
       }
     }
     std::vector<int64_t> cost(tpieces.size());
-    tile_load = 0;
+    int64_t tile_load = 0;
     for (size_t i = 0; i < tpieces.size(); ++i) {
       cost[i] = (tpieces[i].cend - tpieces[i].cbeg) * tile_chunk_cost + tile_item_cost;
       tile_load += cost[i] * n_head;
     }
     const int64_t n_titems = (int64_t)tpieces.size() * n_head;
-    const int64_t max_tctas = n_groups == 0 ? n_ctas : n_ctas - 1;
-    int64_t nt = std::min<int64_t>(max_tctas, n_titems);
-    if (n_groups > 0)
-      nt = std::min<int64_t>(nt, std::max<int64_t>(1, (int64_t)((double)n_ctas * tile_load /
-                                                                  (double)(tile_load + warp_load) + 0.5)));
+    const int64_t max_tctas = max_tctas0;
+    int64_t nt = std::min<int64_t>({max_tctas, n_titems, tile_ctas_for(tile_load)});
     nt = std::max(nt, cdiv64(n_titems, kTileMaxItems));
     bool fits = nt >= 1 && nt <= max_tctas;
     if (fits) {
@@ -438,7 +460,11 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   const int64_t o_items = off;
   const int64_t o_ranges = o_items + kFirstWords * n_warps;
   const int64_t o_rest = o_ranges + align8(n_warps + 1);
-  const int64_t total = o_rest + 8 * dim_rest;
+  // The tile-merge trailer follows the items actually written: a count word
+  // (padded to 8) and one entry of 4 per row of a split tile.
+  const int64_t n_tile_merges = tile_combine;
+  const int64_t trailer_ints = 8 + align8(4 * n_tile_merges);
+  const int64_t total = o_rest + 8 * dim_rest + trailer_ints;
   if (total > INT32_MAX) return set_error(TQ_ERR_UNSUPPORTED, "step too large to plan");
   max_nb = dim_nb;  // row stride of the packed tables
   std::memset(layout, 0, sizeof(int32_t) * TQ_PLAN_LAYOUT_LEN);
@@ -559,7 +585,23 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   }
   ranges[n_warps] = (int32_t)rest;
   std::memset(ranges + n_warps + 1, 0, sizeof(int32_t) * (align8(n_warps + 1) - (n_warps + 1)));
-  const int64_t used = o_rest + 8 * rest;
+  {  // the tile-merge trailer
+    int32_t* const trailer = rest_items + 8 * rest;
+    std::memset(trailer, 0, sizeof(int32_t) * trailer_ints);
+    trailer[0] = (int32_t)n_tile_merges;
+    int32_t* e = trailer + 8;
+    for (const TilePiece& tp : tpieces) {
+      if (tp.gsplit != 0 || tp.gnsplit < 2) continue;
+      const Tile& tl = tiles[(size_t)tp.tile];
+      for (int r = 0; r < tl.nrows; ++r, e += 4) {
+        e[0] = tl.row0 + r;
+        e[1] = (int32_t)(tp.gbase + (int64_t)r * tp.gnsplit);
+        e[2] = tp.gnsplit;
+        e[3] = tl.nrows * tp.gnsplit;
+      }
+    }
+  }
+  const int64_t used = o_rest + 8 * rest + trailer_ints;
 
   layout[TQ_PLAN_NUM_TOKENS] = (int32_t)N;
   layout[TQ_PLAN_NUM_SEQS] = (int32_t)B;
@@ -581,6 +623,7 @@ extern "C" int tq_plan_step(int32_t num_seqs, const int32_t* start, const int32_
   layout[TQ_PLAN_NUM_CTAS] = n_ctas;
   layout[TQ_PLAN_USED_INTS] = (int32_t)used;
   layout[TQ_PLAN_NUM_TILE_CTAS] = n_tctas;
+  layout[TQ_PLAN_NUM_TILE_MERGES] = (int32_t)n_tile_merges;
 
   // Everything before the attention plan: zeros first (padding, table tails).
   std::memset(out, 0, sizeof(int32_t) * o_items);

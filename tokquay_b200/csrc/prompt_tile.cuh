@@ -57,8 +57,14 @@ namespace tq {
 constexpr int kFlagTile = 8;          // work-item flag: a prompt-tile item / CTA marker
 constexpr int kTileRows = 128;        // query rows per tile (the MMA's M)
 constexpr int kTileMaxItems = 96;     // tile items one CTA holds
-constexpr int kTileKVBufs = 3;        // converted K/V chunks (hi | lo) in shared memory
-constexpr int kTileRawStages = 4;     // raw K/V chunks in flight (the producer's ring)
+#ifndef TQ_TILE_KV_BUFS
+#define TQ_TILE_KV_BUFS 3
+#endif
+#ifndef TQ_TILE_RAW_STAGES
+#define TQ_TILE_RAW_STAGES 4
+#endif
+constexpr int kTileKVBufs = TQ_TILE_KV_BUFS;        // converted K/V chunks (hi | lo) in shared memory
+constexpr int kTileRawStages = TQ_TILE_RAW_STAGES;  // raw K/V chunks in flight (the producer's ring)
 constexpr int kTileRowWarps = 4;
 constexpr int kTileMmaWarp = 4;
 constexpr int kTileProducerWarp = 5;  // TMA copies of the K/V rows
@@ -83,14 +89,17 @@ constexpr int kTileQStride = kHeadDim * 4 + 16;  // padded q rows: thread t's ro
 constexpr int kTileOffQStage = kTileOffRaw + kTileRawStages * kTileRawStageBytes;
 constexpr int kTileOffItems = kTileOffQStage + kTileRows * kTileQStride;
 constexpr int kTileOffBars = kTileOffItems + kTileMaxItems * 32;
-// kv_ready[3] kv_free[3] s_full[3] p_full[3] o_full[3] q_ready done raw_full[R] raw_empty[R]
-// rows_done merge_go (split items: the row warps' partials are out / the merge decision is in)
-constexpr int kTileSP = 3;  // S/P buffers in TMEM (chunk g uses g % kTileSP)
-constexpr int kTileBarKvReady = 0, kTileBarKvFree = 3, kTileBarSFull = 6, kTileBarPFull = 9,
-              kTileBarOFull = 12, kTileBarQReady = 15, kTileBarDone = 16, kTileBarRawFull = 17,
-              kTileBarRawEmpty = kTileBarRawFull + kTileRawStages, kTileBarRowsDone = kTileBarRawEmpty + kTileRawStages,
-              kTileBarMergeGo = kTileBarRowsDone + 1, kTileNumBars = kTileBarMergeGo + 1;
-// [0] TMEM base, [1] abort flag, [2] this CTA wrote the last partial of a split item
+// kv_ready[B] kv_free[B] s_full[SP] p_full[SP] o_full[SP] q_ready done raw_full[R] raw_empty[R]
+#ifndef TQ_TILE_SP
+#define TQ_TILE_SP 3
+#endif
+constexpr int kTileSP = TQ_TILE_SP;  // S/P buffers in TMEM (chunk g uses g % kTileSP)
+constexpr int kTileBarKvReady = 0, kTileBarKvFree = kTileKVBufs, kTileBarSFull = 2 * kTileKVBufs,
+              kTileBarPFull = kTileBarSFull + kTileSP, kTileBarOFull = kTileBarPFull + kTileSP,
+              kTileBarQReady = kTileBarOFull + kTileSP, kTileBarDone = kTileBarQReady + 1,
+              kTileBarRawFull = kTileBarDone + 1,
+              kTileBarRawEmpty = kTileBarRawFull + kTileRawStages, kTileNumBars = kTileBarRawEmpty + kTileRawStages;
+// [0] TMEM base, [1] abort flag
 static_assert(kTileBarRawFull == kTileBarDone + 1 && kTileBarDone == kTileBarQReady + 1 &&
                   kTileBarQReady == kTileBarOFull + kTileSP && kTileBarOFull == kTileBarPFull + kTileSP &&
                   kTileBarPFull == kTileBarSFull + kTileSP && kTileBarSFull == kTileBarKvFree + kTileKVBufs &&
@@ -100,10 +109,13 @@ constexpr int kTileOffMisc = kTileOffBars + kTileNumBars * 8;
 constexpr int kTileOffParams = kTileOffMisc + 16;  // the launch's AttnParams, copied here
 constexpr int kTileSmemBytes = kTileOffParams + (int)((sizeof(AttnParams) + 15) / 16 * 16);
 static_assert(kChunk == 32, "prompt tiles take 32-key chunks");
-static_assert(kTileSmemBytes <= kAttnSmemBytes, "a tile CTA fits the launch's shared memory");
+// A launch that may hold tile CTAs asks for the larger of the two layouts.
+constexpr int kTileLaunchSmemBytes = kTileSmemBytes > kAttnSmemBytes ? kTileSmemBytes : kAttnSmemBytes;
+static_assert(kTileLaunchSmemBytes <= 232448, "a tile CTA fits an SM's shared memory");
 static_assert(2 * kAttnWarps * 32 == 384, "tile roles assume 12 warps");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemQ = 0, kTmemS = 128, kTmemO = 320;
+constexpr uint32_t kTmemQ = 0, kTmemS = 128, kTmemO = kTmemS + 64 * kTileSP;
+static_assert(kTmemO + 128 <= kTmemCols, "Q, the S/P buffers and two PV accumulators fit the tensor memory");
 constexpr uint32_t kTmemP = kTmemS;  // P hi (+32: P lo) over S of the same buffer
 constexpr float kTileRescale = 8.f;
 #ifndef TQ_TILE_FAST_WAIT_SLEEP
@@ -375,6 +387,37 @@ __device__ __forceinline__ void tile_advance(TileCursor& cur, const WorkItem* it
   }
 }
 
+// Bulk L2 prefetch of every K and V row the CTA's items read (one warp, at
+// the start).  The producer's raw ring holds kTileRawStages chunks; with the
+// DRAM latency seen beside a decode launch's full-bandwidth traffic (~3.5 us
+// per copy on B200) that ring alone delivers a chunk every ~0.9 us.  With the
+// rows already on their way to L2, each refill waits for L2, not DRAM.  Block
+// ids outside the pool are skipped here (the producer reports them).
+#ifndef TQ_TILE_PREFETCH_L2
+#define TQ_TILE_PREFETCH_L2 1
+#endif
+constexpr bool kTilePrefetchL2 = TQ_TILE_PREFETCH_L2;
+__device__ __forceinline__ void tile_prefetch_l2(const AttnParams& p, const WorkItem* items, int count, int lane) {
+  const int bs = p.block_size;
+  const size_t kv_stride = (size_t)p.n_head * bs * kHeadDim;  // K tile -> V tile
+  for (int k = 0; k < count; ++k) {
+    const WorkItem& it = items[k];
+    const int key_lo = it.cbeg() * kChunk, key_hi = min(it.pos0() + it.nrows(), it.cend() * kChunk);
+    const int kb0 = key_lo >> p.log2_bs, nb = ((key_hi - 1) >> p.log2_bs) - kb0 + 1;
+    const int* tbl = p.tables + (size_t)it.seq() * p.table_stride + kb0;
+    for (int j = lane; j < nb; j += 32) {
+      const int blk = __ldg(tbl + j);
+      if (blk < 0 || blk >= p.num_blocks) continue;
+      const int kb = kb0 + j;
+      const int r0 = max(key_lo - kb * bs, 0), r1 = min(key_hi - kb * bs, bs);  // rows of this block
+      const float* src = p.pool + pool_tile_offset(p, blk, 0, it.head()) + (size_t)r0 * kHeadDim;
+      const uint32_t bytes = (uint32_t)(r1 - r0) * kRowBytes;
+      bulk_prefetch_l2(src, bytes);
+      bulk_prefetch_l2(src + kv_stride, bytes);
+    }
+  }
+}
+
 #ifdef TQ_TILE_DEBUG
 // Per-chunk event clocks (SM cycles since the role started) of the last 4
 // CTAs: [cta][event][chunk], events: 0 K/V data landed, 1 K/V buffer free,
@@ -423,7 +466,7 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
       mbar_init(bar(kTileBarRawFull + i), 1);                 // the producer's expect_tx + the bytes
       mbar_init(bar(kTileBarRawEmpty + i), kTileCvtWarps);    // every converter warp has read it
     }
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < kTileKVBufs; ++i) {
       mbar_init(bar(kTileBarKvReady + i), kTileCvtWarps);
       mbar_init(bar(kTileBarKvFree + i), 1);
     }
@@ -434,8 +477,6 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
     }
     mbar_init(bar(kTileBarQReady), kTileRowWarps);
     mbar_init(bar(kTileBarDone), 2);  // both MMA issuers' work has completed
-    mbar_init(bar(kTileBarRowsDone), kTileRowWarps);
-    mbar_init(bar(kTileBarMergeGo), 1);
     misc[1] = 0;
     mbar_init_fence();
   }
@@ -471,7 +512,7 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
     cp_async_wait<0>();
     tile_q_to_tmem(lane_base + kTmemQ, qrow);
     warp_arrive_after_tmem_st(bar(kTileBarQReady));
-    int g = 0, splits_done = 0;
+    int g = 0;
     bool ok = true;
     for (int k = 0; k < count && ok; ++k) {
       const WorkItem it = items[k];
@@ -585,66 +626,25 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
         continue;
       }
       // A piece of a split tile: this piece's partial (m, l, unnormalised
-      // accumulator) per row into the split-K scratch; the piece that
-      // completes the count merges every row of the tile (rows without a key
-      // in a piece carry m = -inf and weigh nothing) and leaves the counter 0.
-      const size_t idx0 = (size_t)it.gbase() + (size_t)t * it.gnsplit();  // row t's split 0
-      {
-        uint32_t v[32];
+      // accumulator) per row into the split-K scratch, and on to the next
+      // item.  tile_merge_kernel, the launch's programmatic dependent, merges
+      // the pieces of every row (rows without a key in a piece carry m = -inf
+      // and weigh nothing): no fence, counter or round trip on this CTA's path.
+      const size_t idx = (size_t)it.gbase() + (size_t)t * it.gnsplit() + it.gsplit();
+      uint32_t v[32];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          tmem_ld32(o_col + 32 * half, v);
-          if (t < it.nrows()) {
-            float4* dst = reinterpret_cast<float4*>(p.part_acc + (idx0 + it.gsplit()) * kHeadDim + 32 * half);
+      for (int half = 0; half < 2; ++half) {
+        tmem_ld32(o_col + 32 * half, v);
+        if (t < it.nrows()) {
+          float4* dst = reinterpret_cast<float4*>(p.part_acc + idx * kHeadDim + 32 * half);
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                   __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-          }
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                 __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
         }
-        if (t < it.nrows()) *reinterpret_cast<float2*>(p.part_ml + 2 * (idx0 + it.gsplit())) = make_float2(m, l);
       }
-      __threadfence();  // this row's partial is visible before the count says so
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kTileBarRowsDone));
-      if (t == 0) {
-        const bool seen = tile_wait(bar(kTileBarRowsDone), (uint32_t)splits_done & 1u, abort_flag, kTileFastWaitSleep);
-        int old = 0;
-        if (seen)
-          asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.part_cnt + it.gbase()) : "memory");
-        misc[2] = seen && old == it.gnsplit() - 1;
-        mbar_arrive(bar(kTileBarMergeGo));
-      }
-      if (!(ok = tile_wait_warp(bar(kTileBarMergeGo), (uint32_t)splits_done & 1u, abort_flag, kTileFastWaitSleep))) break;
-      ++splits_done;
-      if (!misc[2]) continue;
-      __threadfence();
-      if (t < it.nrows()) {
-        float mmax = -INFINITY;
-        for (int sp = 0; sp < it.gnsplit(); ++sp) mmax = fmaxf(mmax, __ldcg(p.part_ml + 2 * (idx0 + sp)));
-        float lt = 0.f;
-        float4 acc[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int sp = 0; sp < it.gnsplit(); ++sp) {
-          const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + 2 * (idx0 + sp)));
-          const float w = ml.x == -INFINITY ? 0.f : fast_exp2(ml.x - mmax);
-          lt = fmaf(ml.y, w, lt);
-          const float4* src = reinterpret_cast<const float4*>(p.part_acc + (idx0 + sp) * kHeadDim);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float4 a = __ldcg(src + i);
-            acc[i] = make_float4(fmaf(a.x, w, acc[i].x), fmaf(a.y, w, acc[i].y), fmaf(a.z, w, acc[i].z),
-                                 fmaf(a.w, w, acc[i].w));
-          }
-        }
-        const float inv = 1.f / lt;
-        float4* dst = reinterpret_cast<float4*>(orow);
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          dst[i] = make_float4(acc[i].x * inv, acc[i].y * inv, acc[i].z * inv, acc[i].w * inv);
-      }
-      if (t == 0) p.part_cnt[it.gbase()] = 0;  // ready for the next launch
+      if (t < it.nrows()) *reinterpret_cast<float2*>(p.part_ml + 2 * idx) = make_float2(m, l);
+      if (t == 0) TQ_TILE_TR(14, k);
     }
     cp_async_wait<0>();     // no copy of a q row may land after the CTA is gone
     bulk_store_wait_read();  // nor an output store read its shared memory
@@ -783,6 +783,7 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
     const int f4 = lane >> 3, kk = lane & 7;
     const uint32_t raw0 = smem_addr(smem + kTileOffRaw);
     const uint32_t kv0 = smem_addr(smem);
+    if (kTilePrefetchL2 && cw == kTileCvtWarps - 1) tile_prefetch_l2(p, items, count, lane);
     TileCursor cur{0, items[0].cbeg()};
     int total = 0;
     for (int k = 0; k < count; ++k) total += items[k].cend() - items[k].cbeg();
@@ -867,6 +868,54 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---- merge of split prompt tiles ---------------------------------------------
+// The plan's attention region ends with a trailer after the other items: word
+// 0 the number E of rows of split tiles, then (after 8 words) E entries
+// {output row, partial of (head 0, split 0), splits, partials between heads}.
+// One warp per (entry, head) merges that row's per-piece partials
+//   O = sum_s exp2(m_s - M) acc_s / sum_s exp2(m_s - M) l_s,  M = max_s m_s,
+// lane i holding dims 2i and 2i+1.  Launched as a programmatic dependent of
+// the attention launch that wrote the partials: it waits for that grid.
+constexpr int kMergeThreads = 256;
+__device__ __forceinline__ const int* tile_merge_trailer(const AttnParams& p) {
+  return other_items(p) + 8 * (size_t)__ldg(warp_offsets(p) + p.n_warps);
+}
+__global__ void __launch_bounds__(kMergeThreads) tile_merge_kernel(const AttnParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int* trailer = tile_merge_trailer(p);
+  const int E = __ldg(trailer);
+  const int* ent = trailer + 8;
+  const int lane = threadIdx.x & 31;
+  const long long tasks = (long long)E * p.n_head;
+  const long long step = (long long)gridDim.x * (kMergeThreads / 32);
+  for (long long task = (long long)blockIdx.x * (kMergeThreads / 32) + (threadIdx.x >> 5); task < tasks;
+       task += step) {
+    const int e = (int)(task / p.n_head), h = (int)(task - (long long)e * p.n_head);
+    const int row = __ldg(ent + 4 * e), base = __ldg(ent + 4 * e + 1), ns = __ldg(ent + 4 * e + 2),
+              hstride = __ldg(ent + 4 * e + 3);
+    const long long idx0 = (long long)base + (long long)h * hstride;
+    if (row < 0 || ns < 2 || hstride < 0 || idx0 < 0 || idx0 + ns > p.max_partials) {  // a corrupted plan
+      if (lane == 0) raise_device_error(TQ_DEVERR_BAD_PLAN);
+      continue;
+    }
+    float mmax = -INFINITY;
+    for (int sp = 0; sp < ns; ++sp) mmax = fmaxf(mmax, __ldg(p.part_ml + 2 * (idx0 + sp)));
+    float lt = 0.f;
+    float2 acc = make_float2(0.f, 0.f);
+    for (int sp = 0; sp < ns; ++sp) {
+      const float2 ml = __ldg(reinterpret_cast<const float2*>(p.part_ml + 2 * (idx0 + sp)));
+      const float w = ml.x == -INFINITY ? 0.f : fast_exp2(ml.x - mmax);
+      lt = fmaf(ml.y, w, lt);
+      const float2 a = __ldg(reinterpret_cast<const float2*>(p.part_acc + (idx0 + sp) * kHeadDim) + lane);
+      acc = make_float2(fmaf(a.x, w, acc.x), fmaf(a.y, w, acc.y));
+    }
+    const float inv = 1.f / lt;
+    reinterpret_cast<float2*>(p.out + (size_t)row * p.out_stride + h * kHeadDim)[lane] =
+        make_float2(acc.x * inv, acc.y * inv);
   }
 }
 

@@ -402,6 +402,7 @@ class _CaptureView(DevicePagedBatch):
         self.n_ctas = int(L[_lib.PLAN_NUM_CTAS])
         # Replays of a mixed-step capacity may hold prompt tiles: capture the kernel with them.
         self.with_tiles = ws.max_tokens > ws.max_seqs
+        self.tile_merges = 0  # plans of fixed capacities never cut a tile
         self.num_items = self.num_combine = self.num_partials = 0
         dev = ws.plan
 

@@ -497,6 +497,9 @@ class DevicePagedBatch(BatchedKV):
         # several tokens of one sequence.
         self.with_tiles = int(L[_lib.PLAN_NUM_TILE_CTAS]) > 0 or (
             graph_sizing and workspace.max_tokens > workspace.max_seqs)
+        # Rows of tiles cut over their keys (plans without fixed capacities):
+        # a merge kernel after the attention grid combines their pieces.
+        self.tile_merges = int(L[_lib.PLAN_NUM_TILE_MERGES])
         # What activations and launches are sized for.
         if graph_sizing:
             caps = workspace.caps
@@ -576,7 +579,8 @@ class DevicePagedBatch(BatchedKV):
             out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), self.pool.data_ptr(),
             self.allocator.num_blocks, self.n_layer, self.n_head, self.block_size, self.d_head, layer,
             self.block_tables_i32.data_ptr(), self.table_stride, self.attn_plan.data_ptr(), self.n_ctas,
-            int(self.with_tiles), pm, pa, pc, self.partials_alloc,
+            (_lib.ATTN_TILES if self.with_tiles else 0) | (_lib.ATTN_TILE_MERGE if self.tile_merges else 0),
+            pm, pa, pc, self.partials_alloc,
             1.0 / math.sqrt(self.d_head), stream), "tq_paged_attention")  # fmt: skip
 
     # ---- reference BatchedKV contract (not used by this package's model) ---------------
