@@ -94,12 +94,6 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
       : "memory");
 }
 
-// Bulk prefetch of global memory into L2 (no completion, no destination):
-// src 16-byte aligned, bytes a multiple of 16.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // Programmatic dependent launch.  launch_dependents: the next kernel in the
 // stream, if launched with programmatic stream serialization, may start its
 // CTAs (as resources free up) before this grid finishes.  wait: block until

@@ -387,37 +387,6 @@ __device__ __forceinline__ void tile_advance(TileCursor& cur, const WorkItem* it
   }
 }
 
-// Bulk L2 prefetch of every K and V row the CTA's items read (one warp, at
-// the start).  The producer's raw ring holds kTileRawStages chunks; with the
-// DRAM latency seen beside a decode launch's full-bandwidth traffic (~3.5 us
-// per copy on B200) that ring alone delivers a chunk every ~0.9 us.  With the
-// rows already on their way to L2, each refill waits for L2, not DRAM.  Block
-// ids outside the pool are skipped here (the producer reports them).
-#ifndef TQ_TILE_PREFETCH_L2
-#define TQ_TILE_PREFETCH_L2 1
-#endif
-constexpr bool kTilePrefetchL2 = TQ_TILE_PREFETCH_L2;
-__device__ __forceinline__ void tile_prefetch_l2(const AttnParams& p, const WorkItem* items, int count, int lane) {
-  const int bs = p.block_size;
-  const size_t kv_stride = (size_t)p.n_head * bs * kHeadDim;  // K tile -> V tile
-  for (int k = 0; k < count; ++k) {
-    const WorkItem& it = items[k];
-    const int key_lo = it.cbeg() * kChunk, key_hi = min(it.pos0() + it.nrows(), it.cend() * kChunk);
-    const int kb0 = key_lo >> p.log2_bs, nb = ((key_hi - 1) >> p.log2_bs) - kb0 + 1;
-    const int* tbl = p.tables + (size_t)it.seq() * p.table_stride + kb0;
-    for (int j = lane; j < nb; j += 32) {
-      const int blk = __ldg(tbl + j);
-      if (blk < 0 || blk >= p.num_blocks) continue;
-      const int kb = kb0 + j;
-      const int r0 = max(key_lo - kb * bs, 0), r1 = min(key_hi - kb * bs, bs);  // rows of this block
-      const float* src = p.pool + pool_tile_offset(p, blk, 0, it.head()) + (size_t)r0 * kHeadDim;
-      const uint32_t bytes = (uint32_t)(r1 - r0) * kRowBytes;
-      bulk_prefetch_l2(src, bytes);
-      bulk_prefetch_l2(src + kv_stride, bytes);
-    }
-  }
-}
-
 #ifdef TQ_TILE_DEBUG
 // Per-chunk event clocks (SM cycles since the role started) of the last 4
 // CTAs: [cta][event][chunk], events: 0 K/V data landed, 1 K/V buffer free,
@@ -783,7 +752,6 @@ __device__ __noinline__ void prompt_tile_cta(const AttnParams& p, unsigned char*
     const int f4 = lane >> 3, kk = lane & 7;
     const uint32_t raw0 = smem_addr(smem + kTileOffRaw);
     const uint32_t kv0 = smem_addr(smem);
-    if (kTilePrefetchL2 && cw == kTileCvtWarps - 1) tile_prefetch_l2(p, items, count, lane);
     TileCursor cur{0, items[0].cbeg()};
     int total = 0;
     for (int k = 0; k < count; ++k) total += items[k].cend() - items[k].cbeg();
