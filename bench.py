@@ -210,6 +210,10 @@ def kernel_table(model, a, seqs, spec, steps: int = 10) -> str:
 
     from tokquay_b200 import paged_greedy_step
 
+    # Algorithmic bytes of the table's attention launches: contexts grow by one per step.
+    ctx0 = [s.num_cached_tokens + 1 for s in seqs]
+    bytes_per_launch = sum(attn_bytes([c + (k if spec["grow"] else 0) for c in ctx0], model.cfg.n_head,
+                                      model.cfg.n_embd // model.cfg.n_head, 0) for k in range(steps)) / steps
     def step():
         toks = paged_greedy_step(model, a, seqs)
         for s, t in zip(seqs, toks):
@@ -232,15 +236,30 @@ def kernel_table(model, a, seqs, spec, steps: int = 10) -> str:
             k = e.name.split("(")[0][:90]
             agg[k][0] += 1
             agg[k][1] += getattr(e, "device_time", None) or e.cuda_time
-            spans.append((e.time_range.start, e.time_range.end))
+            spans.append((e.time_range.start, e.time_range.end, k))
     tot = sum(v[1] for v in agg.values())
+    # The attention launch's exposed time: from the later of its own start and
+    # the end of the operation before it to its end.  A programmatic dependent
+    # starts its CTAs during the kernel before it, so its own duration counts
+    # time that kernel also spends; the exposed time is what the step pays.
+    spans.sort()
+    exposed, n_attn, prev_end = 0.0, 0, None
+    for t0, t1, k in spans:
+        if "paged_attention_kernel" in k and prev_end is not None:
+            exposed += t1 - max(t0, prev_end)
+            n_attn += 1
+        prev_end = t1 if prev_end is None else max(prev_end, t1)
     # Idle device time between consecutive operations of one step (gaps under
     # 20 us; longer ones are the host's turn between steps).
-    spans.sort()
     gaps = [b[0] - a[1] for a, b in zip(spans, spans[1:])]
     idle = sum(g for g in gaps if 0 < g < 20)
     lines = [f"device time per step: {tot / steps:.1f} us; idle between operations inside a step: "
-             f"{idle / steps:.1f} us", "| kernel | us/step | share | launches/step | avg us |",
+             f"{idle / steps:.1f} us",
+             f"attention exposed (end - max(own start, previous operation's end)): "
+             f"{exposed / max(n_attn, 1):.2f} us per launch over {n_attn} launches, "
+             f"{bytes_per_launch / 1e6:.1f} MB algorithmic per launch = "
+             f"{bytes_per_launch / (exposed / max(n_attn, 1)) / 1e3:.0f} GB/s exposed",
+             "| kernel | us/step | share | launches/step | avg us |",
              "|---|---|---|---|---|"]  # fmt: skip
     for k, (n, t) in sorted(agg.items(), key=lambda x: -x[1][1])[:20]:
         lines.append(f"| {k} | {t / steps:.1f} | {100 * t / tot:.1f}% | {n / steps:.1f} | {t / n:.2f} |")
