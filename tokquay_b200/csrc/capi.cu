@@ -462,6 +462,25 @@ int tq_paged_attention_noalloc(float* out, int64_t out_row_stride, const float* 
 }
 
 #ifdef TQ_ATTN_TRACE
+// Tuning builds only (not part of the ABI): the latest CTA end (globaltimer
+// ns) of any qkv_bias_kv_write launch so far.
+TQ_API int tq_debug_qkv_times(unsigned long long* host, int32_t reset) {  // [64][3]
+  cudaError_t e = cudaMemcpyFromSymbol(host, g_qkv_times, sizeof(g_qkv_times));
+  if (e == cudaSuccess && reset) {
+    static unsigned long long init[64][3];
+    for (int l = 0; l < 64; ++l) init[l][0] = init[l][1] = ~0ull, init[l][2] = 0;
+    e = cudaMemcpyToSymbol(g_qkv_times, init, sizeof(init));
+  }
+  if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "trace read: %s", cudaGetErrorString(e));
+  return TQ_OK;
+}
+
+TQ_API int tq_debug_qkv_write_end(unsigned long long* host) {
+  const cudaError_t e = cudaMemcpyFromSymbol(host, g_qkv_write_end, sizeof(unsigned long long));
+  if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "trace read: %s", cudaGetErrorString(e));
+  return TQ_OK;
+}
+
 // Tuning builds only (not part of the ABI): copy the per-warp timeline of the
 // last attention launch to `host` ([n_warps][16] uint64).
 TQ_API int tq_debug_attention_trace(unsigned long long* host, int32_t n_warps) {

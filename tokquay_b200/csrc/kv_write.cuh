@@ -88,10 +88,27 @@ struct QkvWriteParams {
 // One block per row, thread t owns float4 t of the 3C columns (blockDim =
 // 3C/4).  NP > 0: exactly NP partial sums, loads unrolled; NP == 0: looped.
 // Summation order matches the unfused path (bias_gelu_kernel): ((p0 + p1) + ...) + bias.
+#ifdef TQ_ATTN_TRACE
+__device__ unsigned long long g_qkv_write_end;
+// Per layer: {first CTA entry, first return from the wait, last CTA end} (ns).
+__device__ unsigned long long g_qkv_times[64][3];
+#endif
 template <int NP>
 __global__ void __launch_bounds__(1024) qkv_bias_kv_write_kernel(const QkvWriteParams p) {
+#ifdef TQ_ATTN_TRACE
+  unsigned long long tq_t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tq_t0));
+#endif
   pdl_launch_dependents();  // the attention that follows may start its prologue now
   pdl_wait();               // the c_attn matmul before it is complete
+#ifdef TQ_ATTN_TRACE
+  if (threadIdx.x == 0 && p.layer < 64) {
+    unsigned long long t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    atomicMin(&g_qkv_times[p.layer][0], tq_t0);
+    atomicMin(&g_qkv_times[p.layer][1], t1);
+  }
+#endif
   const int n = *p.n_rows;
   const int C4 = p.n_head * 16;  // float4 per q (or K, or V) row
   const int t = threadIdx.x;
@@ -153,6 +170,14 @@ __global__ void __launch_bounds__(1024) qkv_bias_kv_write_kernel(const QkvWriteP
     store_row(r, v, slot);
     if (r2 < n) store_row(r2, v2, slot2);
   }
+#ifdef TQ_ATTN_TRACE
+  if (threadIdx.x == 0) {  // tuning builds: the latest end of any CTA of this kernel
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    atomicMax(&g_qkv_write_end, t);
+    if (p.layer < 64) atomicMax(&g_qkv_times[p.layer][2], t);
+  }
+#endif
 }
 
 }  // namespace tq

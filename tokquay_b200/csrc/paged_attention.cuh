@@ -65,7 +65,8 @@ static_assert(kChunk == 16 || kChunk == 32, "chunk of 16 or 32 keys");
 // Tuning builds only: per-warp timeline of the last launch, [warp][16] =
 // {start ns, first data ns, end ns, wait, compute, finish, refill, chunks,
 //  issue:block-id wait, issue:copies, advance, finish:reduce+store,
-//  finish:fence+atomic, finish:merge, units, -} (cycles unless noted).
+//  finish:fence+atomic, finish:merge, producer entry ns, producer end ns}
+// (cycles unless noted).
 // Read back with tq_debug_attention_trace.
 constexpr int kTraceWarps = 8192;
 constexpr int kTraceSlots = 16;
@@ -508,6 +509,7 @@ constexpr int kAttnThreads = 2 * kAttnWarps * 32;
 // (measured on config 2: 21.9 vs 21.6 us).
 template <bool kTiles>
 __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const AttnParams p) {
+  TQ_TRACE(const unsigned long long tr_entry = global_ns();)
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -766,7 +768,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
         if (!mbar_wait_bounded(full0 + 8 * (k % kStages), (uint32_t)(k / kStages) & 1u)) break;
     }
     TQ_TRACE(if (lane == 0 && gw < kTraceWarps) {
-      trec[6] = tr_empty; trec[8] = tr_sub[0]; trec[9] = tr_sub[1]; trec[10] = tr_sub[2];
+      trec[6] = tr_empty; trec[8] = tr_sub[0]; trec[9] = tr_sub[1]; trec[10] = tr_sub[2]; trec[14] = tr_entry;
       trec[15] = global_ns();
     })
     return;
@@ -859,7 +861,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
   TQ_TRACE(if (lane == 0 && gw < kTraceWarps) {
     trec[0] = tr_start; trec[1] = tr_first; trec[2] = global_ns(); trec[3] = tr_wait; trec[4] = tr_comp;
     trec[5] = tr_fin; trec[7] = tr_chunks;
-    for (int k = 3; k < 7; ++k) trec[8 + k] = tr_sub[k];
+    for (int k = 3; k < 6; ++k) trec[8 + k] = tr_sub[k];  // slot 14: the producer's entry stamp
   })
   TQ_CTA_END();
 }
