@@ -464,13 +464,18 @@ int tq_paged_attention_noalloc(float* out, int64_t out_row_stride, const float* 
 #ifdef TQ_ATTN_TRACE
 // Tuning builds only (not part of the ABI): the latest CTA end (globaltimer
 // ns) of any qkv_bias_kv_write launch so far.
-TQ_API int tq_debug_qkv_times(unsigned long long* host, int32_t reset) {  // [64][3]
+TQ_API int tq_debug_qkv_times(unsigned long long* host, int32_t reset) {  // [64][3] + [64] attention entries
   cudaError_t e = cudaMemcpyFromSymbol(host, g_qkv_times, sizeof(g_qkv_times));
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(host + 192, g_attn_entry, sizeof(g_attn_entry));
   if (e == cudaSuccess && reset) {
     static unsigned long long init[64][3];
     for (int l = 0; l < 64; ++l) init[l][0] = init[l][1] = ~0ull, init[l][2] = 0;
     e = cudaMemcpyToSymbol(g_qkv_times, init, sizeof(init));
+    static unsigned long long first[64];
+    for (int l = 0; l < 64; ++l) first[l] = ~0ull;
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_attn_entry, first, sizeof(first));
   }
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(host + 192, g_attn_entry, sizeof(g_attn_entry));
   if (e != cudaSuccess) return set_error(TQ_ERR_CUDA, "trace read: %s", cudaGetErrorString(e));
   return TQ_OK;
 }

@@ -69,6 +69,8 @@ static_assert(kChunk == 16 || kChunk == 32, "chunk of 16 or 32 keys");
 // (cycles unless noted).
 // Read back with tq_debug_attention_trace.
 constexpr int kTraceWarps = 8192;
+// Per layer: the first CTA entry (ns) of the latest launches (reset by the host).
+__device__ unsigned long long g_attn_entry[64];
 constexpr int kTraceSlots = 16;
 __device__ unsigned long long g_attn_trace[kTraceWarps * kTraceSlots];
 // Per warp, per chunk (first kTraceChunks): {issue ns, data-ready ns, bytes}.
@@ -509,7 +511,8 @@ constexpr int kAttnThreads = 2 * kAttnWarps * 32;
 // (measured on config 2: 21.9 vs 21.6 us).
 template <bool kTiles>
 __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const AttnParams p) {
-  TQ_TRACE(const unsigned long long tr_entry = global_ns();)
+  TQ_TRACE(const unsigned long long tr_entry = global_ns();
+           if (threadIdx.x == 0 && p.layer < 64) atomicMin(&g_attn_entry[p.layer], tr_entry);)
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
