@@ -63,7 +63,7 @@ static_assert(kChunk == 16 || kChunk == 32, "chunk of 16 or 32 keys");
 
 #ifdef TQ_ATTN_TRACE
 // Tuning builds only: per-warp timeline of the last launch, [warp][16] =
-// {start ns, first data ns, end ns, wait, compute, finish, refill, chunks,
+// {start ns, first data ns, end ns, wait, compute, finish, SM id, chunks,
 //  issue:block-id wait, issue:copies, advance, finish:reduce+store,
 //  finish:fence+atomic, finish:merge, producer entry ns, producer end ns}
 // (cycles unless noted).
@@ -585,7 +585,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
     // planner keeps items that short) live in two registers per lane: lane i
     // holds blocks kb0+i and kb0+32+i.  They are loaded one item ahead, and
     // the item itself two ahead, so neither load sits between two issues.
-    TQ_TRACE(long long tr_empty = 0;)
     int p_k = 0;
     WorkItem p_it = item_from_lanes(first_word);
     int p_chunk = p_it.cbeg();
@@ -625,9 +624,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
     auto issue_next = [&](bool defer_q) {
       const int s = issued % kStages;
       if (issued >= kStages) {  // wait for the consumer to release the stage
-        TQ_TRACE(long long te0 = clock64();)
         ok = mbar_wait_bounded(empty0 + 8 * s, (uint32_t)(issued / kStages - 1) & 1u);
-        TQ_TRACE(tr_empty += clock64() - te0;)
         if (!__all_sync(kFullMask, ok)) {
           ok = false;
           return;
@@ -771,7 +768,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) paged_attention_kernel(const 
         if (!mbar_wait_bounded(full0 + 8 * (k % kStages), (uint32_t)(k / kStages) & 1u)) break;
     }
     TQ_TRACE(if (lane == 0 && gw < kTraceWarps) {
-      trec[6] = tr_empty; trec[8] = tr_sub[0]; trec[9] = tr_sub[1]; trec[10] = tr_sub[2]; trec[14] = tr_entry;
+      unsigned smid_;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid_));
+      trec[6] = smid_; trec[8] = tr_sub[0]; trec[9] = tr_sub[1]; trec[10] = tr_sub[2]; trec[14] = tr_entry;
       trec[15] = global_ns();
     })
     return;
